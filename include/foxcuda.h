@@ -1,0 +1,197 @@
+/*
+ * libfoxcuda -- the B200 (sm_100a) token loop behind RustFox's fox.h API.
+ *
+ * A C ABI of plain pointers and sizes. Every entry point returns a status with
+ * the numbering of upstream's fox_status (include/fox/fox.h:17-26) and, on
+ * failure, leaves a message for foxcuda_last_error() (thread-local, like
+ * upstream's fox_last_error, src/log.c:40-57). Nothing aborts.
+ *
+ * Kernel-level entry points take DEVICE pointers and an optional CUDA stream
+ * (cudaStream_t passed as void*, NULL = legacy default stream); they enqueue
+ * work and return without synchronising. Model-level entry points take HOST
+ * buffers and synchronise before returning, as upstream's calls do.
+ *
+ * Each declaration names the upstream interface it replaces (file:line in the
+ * RustFox tree).
+ */
+#ifndef FOXCUDA_H
+#define FOXCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int foxcuda_status;
+enum {
+    FOXCUDA_OK = 0,
+    FOXCUDA_ERR_ARG,
+    FOXCUDA_ERR_IO,
+    FOXCUDA_ERR_NOMEM,
+    FOXCUDA_ERR_FORMAT,
+    FOXCUDA_ERR_UNSUPPORTED,
+    FOXCUDA_ERR_NOTFOUND,
+    FOXCUDA_ERR_INTERNAL
+};
+
+/* ggml type ids used here (upstream include/fox/fox.h:203-213) */
+enum {
+    FOXCUDA_F32 = 0, FOXCUDA_F16 = 1, FOXCUDA_Q8_0 = 8, FOXCUDA_Q4_K = 12,
+    FOXCUDA_Q6_K = 14, FOXCUDA_TQ1_0 = 34, FOXCUDA_TQ2_0 = 35
+};
+
+/* replaces fox_last_error (include/fox/fox.h:30, src/log.c:40-57) */
+const char *foxcuda_last_error(void);
+/* replaces fox_version (include/fox/fox.h:15) */
+const char *foxcuda_version(void);
+/* Selects and checks the device (compute capability 10.x). */
+foxcuda_status foxcuda_init(int device);
+
+/* ---- kernel level (device pointers) ------------------------------------ */
+
+/* replaces fox_quantize_activations_i8 (include/fox/fox.h:342-343,
+ * src/gemv.c:11-42): one absmax scale for the n-vector; *scale is device. */
+foxcuda_status foxcuda_quantize_activations_i8(const float *x, size_t n, int8_t *q,
+                                               float *scale, void *stream);
+
+/* replaces fox_gemv_tq1_i8 / fox_gemv_tq2_i8 (include/fox/fox.h:350-355,
+ * src/gemv.c:155-192). Weights in GGUF layout; act_scale is a device float. */
+foxcuda_status foxcuda_gemv_tq1_i8(const int8_t *q, const float *act_scale,
+                                   const void *weights, size_t n_rows, size_t n_cols,
+                                   float *out, void *stream);
+foxcuda_status foxcuda_gemv_tq2_i8(const int8_t *q, const float *act_scale,
+                                   const void *weights, size_t n_rows, size_t n_cols,
+                                   float *out, void *stream);
+
+/* replaces fox_gemv (include/fox/fox.h:363-365, src/kernels.c:809-872) for
+ * TQ1_0, TQ2_0, Q4_K, Q6_K and Q8_0 weights in GGUF layout. Repacks the
+ * weights into stream-ordered scratch memory, then runs the packed kernel. */
+foxcuda_status foxcuda_gemv(int ggml_type, const float *x, const void *weights,
+                            size_t n_rows, size_t n_cols, float *out, void *stream);
+
+/* replaces fox_dequant_row (include/fox/fox.h:367-368, src/kernels.c:874-941)
+ * for F32, F16, Q8_0, Q4_K and Q6_K. */
+foxcuda_status foxcuda_dequant_row(int ggml_type, const void *row, size_t n, float *out,
+                                   void *stream);
+
+/* Integer partial sums exactly as upstream forms them, for bit-exact checks
+ * (no single upstream entry point; the sums inside src/ternary.c:158-173,
+ * 253-287 and src/kernels.c:465-569):
+ *   TQ1_0/TQ2_0  n_rows*(n_cols/256)      block sums of q . (trit)
+ *   Q4_K         n_rows*(n_cols/256)*16   per sub-block: dot(nibble, q), sum(q)
+ *   Q6_K         n_rows*(n_cols/256)*4    per (half, sub) scaled group dot
+ * q is the int8 activation vector (per-vector or per-256 quantised). */
+foxcuda_status foxcuda_block_partials(int ggml_type, const int8_t *q, const void *weights,
+                                      size_t n_rows, size_t n_cols, int32_t *out,
+                                      void *stream);
+
+/* The HBM weight layout: GGUF blocks regrouped into 16-byte planes per unit
+ * of rows (a byte permutation). */
+size_t         foxcuda_packed_bytes(int ggml_type, size_t n_rows, size_t n_cols);
+foxcuda_status foxcuda_pack(int ggml_type, const void *gguf_rows, size_t n_rows,
+                            size_t n_cols, void *packed, void *stream);
+/* fox_gemv on already packed weights: no scratch memory. */
+foxcuda_status foxcuda_gemv_packed(int ggml_type, const float *x, const void *packed,
+                                   size_t n_rows, size_t n_cols, float *out, void *stream);
+
+/* ---- model level (host buffers) ---------------------------------------- */
+
+typedef struct foxcuda_model   foxcuda_model;
+typedef struct foxcuda_context foxcuda_context;
+typedef struct foxcuda_sampler foxcuda_sampler;
+
+/* the shape fields of upstream fox_model_info (include/fox/fox.h:404-419) */
+typedef struct {
+    uint32_t n_layer, n_embd, n_head, n_head_kv, n_ff, head_dim, n_vocab;
+    float    rms_eps, rope_freq_base;
+} foxcuda_model_info;
+
+/* tensor roles: the tensors upstream's loader resolves (src/model.c:51-83,
+ * 243-252) */
+enum {
+    FOXCUDA_TOKEN_EMBD = 0, FOXCUDA_OUTPUT_NORM, FOXCUDA_OUTPUT,
+    FOXCUDA_ATTN_NORM, FOXCUDA_ATTN_Q, FOXCUDA_ATTN_K, FOXCUDA_ATTN_V,
+    FOXCUDA_ATTN_OUT, FOXCUDA_FFN_NORM, FOXCUDA_FFN_GATE, FOXCUDA_FFN_UP,
+    FOXCUDA_FFN_DOWN, FOXCUDA_N_ROLES
+};
+
+/* replaces fox_model_open (include/fox/fox.h:425-426, src/model.c:146-303):
+ * the caller parses GGUF and hands every tensor over with
+ * foxcuda_model_upload; OUTPUT may be omitted (tied to TOKEN_EMBD,
+ * src/model.c:248-252). Weights stay resident in HBM. */
+foxcuda_status foxcuda_model_create(const foxcuda_model_info *info, int device,
+                                    foxcuda_model **out);
+foxcuda_status foxcuda_model_upload(foxcuda_model *m, int role, uint32_t layer,
+                                    int ggml_type, uint64_t ne0, uint64_t ne1,
+                                    const void *host_data, size_t bytes);
+foxcuda_status foxcuda_model_finalize(foxcuda_model *m);
+void           foxcuda_model_destroy(foxcuda_model *m);
+uint64_t       foxcuda_model_device_bytes(const foxcuda_model *m);
+
+/* KV cache element type */
+enum { FOXCUDA_KV_F16 = 0, FOXCUDA_KV_F32 = 1 };
+
+typedef struct {
+    uint32_t n_ctx;      /* positions held per sequence */
+    int      kv_type;    /* FOXCUDA_KV_F16 (default) or FOXCUDA_KV_F32 */
+    int      attn_exact; /* 1: attention in upstream's serial operation order
+                            (bit-exact parity mode, slow); 0: split-K decode */
+} foxcuda_context_config;
+
+/* replaces fox_context_create / destroy / reset / position /
+ * last_eval_seconds (include/fox/fox.h:433-450, src/forward.c:56-165) */
+foxcuda_status foxcuda_context_create(foxcuda_model *m, const foxcuda_context_config *cfg,
+                                      foxcuda_context **out);
+void           foxcuda_context_destroy(foxcuda_context *c);
+void           foxcuda_context_reset(foxcuda_context *c);
+uint32_t       foxcuda_context_position(const foxcuda_context *c);
+double         foxcuda_context_last_eval_seconds(const foxcuda_context *c);
+
+/* replaces fox_eval (include/fox/fox.h:446-447, src/forward.c:411-438):
+ * evaluates n tokens from host memory; when logits_out is not NULL the last
+ * token's n_vocab logits are copied to it (host). */
+foxcuda_status foxcuda_eval(foxcuda_context *c, const uint32_t *tokens, size_t n,
+                            float *logits_out);
+
+/* Residual stream of the last evaluated token after layer `layer` (0 = the
+ * embedding, n_layer = after the last layer), n_embd floats to host. Valid
+ * after foxcuda_eval with foxcuda_context_set_trace(c, 1). */
+foxcuda_status foxcuda_context_set_trace(foxcuda_context *c, int on);
+foxcuda_status foxcuda_context_hidden(const foxcuda_context *c, uint32_t layer, float *out);
+
+/* replaces fox_sampler_config (include/fox/fox.h:453-460) */
+typedef struct {
+    float    temperature;
+    int      top_k;
+    float    top_p;
+    float    repeat_penalty;
+    uint32_t repeat_last_n;
+    uint64_t seed;
+} foxcuda_sampler_config;
+
+/* replaces fox_sampler_create / destroy / accept / pick (include/fox/fox.h:
+ * 462-469, src/sample.c:47-195), on the device: pick reads the context's
+ * current logits (the last foxcuda_eval). repeat_last_n <= 1024. */
+foxcuda_status foxcuda_sampler_create(foxcuda_context *c, const foxcuda_sampler_config *cfg,
+                                      foxcuda_sampler **out);
+void           foxcuda_sampler_destroy(foxcuda_sampler *s);
+foxcuda_status foxcuda_sampler_accept(foxcuda_sampler *s, uint32_t token);
+foxcuda_status foxcuda_sampler_pick(foxcuda_sampler *s, uint32_t *out);
+
+/* One decode step of upstream's `fox run` loop (src/cli.c:340-361) as one
+ * CUDA graph: eval `token`, pick the next token, accept it into the sampler
+ * history; the pick is returned in *next (host). */
+foxcuda_status foxcuda_decode(foxcuda_context *c, foxcuda_sampler *s, uint32_t token,
+                              uint32_t *next);
+
+/* n decode steps with the picked token fed back on the device (no host round
+ * trip between steps); out receives the n picks (host). */
+foxcuda_status foxcuda_generate(foxcuda_context *c, foxcuda_sampler *s, uint32_t token,
+                                size_t n, uint32_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,14 @@
+"""rustfox_b200: RustFox's per-token forward pass on B200 (sm_100a).
+
+The compute lives in libfoxcuda.so (C ABI, include/foxcuda.h); this package
+is its Python host side, mirroring upstream RustFox's fox.h API, plus the GGUF
+and synthetic-model helpers.
+"""
+from . import formats, synth  # noqa: F401
+from .api import (FoxError, Model, Context, Sampler, lib, last_error,  # noqa: F401
+                  quantize_activations_i8, gemv, gemv_tq1_i8, gemv_tq2_i8, dequant_row,
+                  block_partials, pack, gemv_packed, greedy_generate)
+
+__all__ = ["formats", "synth", "FoxError", "Model", "Context", "Sampler", "lib", "last_error",
+           "quantize_activations_i8", "gemv", "gemv_tq1_i8", "gemv_tq2_i8", "dequant_row",
+           "block_partials", "pack", "gemv_packed", "greedy_generate"]

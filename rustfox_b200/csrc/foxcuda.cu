@@ -1,0 +1,1041 @@
+// libfoxcuda: the C ABI (include/foxcuda.h), the HBM weight store, the decode
+// context and its CUDA graphs.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/foxcuda.h"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "ops.cuh"
+#include "pack.cuh"
+
+using namespace fox;
+
+// ---------------------------------------------------------------------------
+// errors: thread-local message, status codes of upstream fox_status
+
+static thread_local char g_err[512];
+
+static foxcuda_status fail(foxcuda_status st, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+static foxcuda_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? FOXCUDA_ERR_NOMEM : FOXCUDA_ERR_INTERNAL,
+              "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call, what)                                   \
+  do {                                                   \
+    cudaError_t e_ = (call);                             \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what);   \
+  } while (0)
+
+extern "C" const char* foxcuda_last_error(void) { return g_err[0] ? g_err : "no error recorded"; }
+extern "C" const char* foxcuda_version(void) { return "foxcuda 0.1.0 (sm_100a)"; }
+
+static int sm_count(int dev) {
+  static int cached[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+static int current_sms() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return sm_count(d);
+}
+
+extern "C" foxcuda_status foxcuda_init(int device) {
+  int n = 0;
+  CK(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return fail(FOXCUDA_ERR_ARG, "init: device %d of %d", device, n);
+  CK(cudaSetDevice(device), "cudaSetDevice");
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "init: %s is sm_%d%d; this build is sm_100a only",
+                prop.name, prop.major, prop.minor);
+  return FOXCUDA_OK;
+}
+
+static bool type_gemv_ok(int t) {
+  return t == T_TQ1_0 || t == T_TQ2_0 || t == T_Q4_K || t == T_Q6_K || t == T_Q8_0;
+}
+
+static size_t row_bytes(int t, size_t n_cols) {
+  const int be = block_elems(t);
+  if (n_cols % be) return 0;
+  return n_cols / be * block_bytes(t);
+}
+
+// ---------------------------------------------------------------------------
+// GEMV launch
+
+template <int T, int PRO, int EPI>
+static cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
+  auto kern = gemv_kernel<T, PRO, EPI>;
+  const int threads = (p.U * p.nb + 31) / 32 * 32;
+  const size_t smem = gemv_smem_bytes(T, PRO, p.K, p.U, p.nb);
+  static size_t attr_set = 0;  // per instantiation
+  if (smem > 48 * 1024 && smem > attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = smem;
+  }
+  int occ = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (occ < 1) return cudaErrorInvalidConfiguration;
+  const int units = (p.n_rows + p.U - 1) / p.U;
+  const int grid = std::min(units, occ * current_sms());
+  kern<<<grid, threads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <int T>
+static cudaError_t launch_gemv_pe(int pro, int epi, const GemvParams& p, cudaStream_t s) {
+  if (pro == PRO_VEC && epi == EPI_STORE) return launch_gemv_t<T, PRO_VEC, EPI_STORE>(p, s);
+  if (pro == PRO_VEC && epi == EPI_ADD) return launch_gemv_t<T, PRO_VEC, EPI_ADD>(p, s);
+  if (pro == PRO_NORM && epi == EPI_STORE) return launch_gemv_t<T, PRO_NORM, EPI_STORE>(p, s);
+  if (pro == PRO_NORM && epi == EPI_QKV) return launch_gemv_t<T, PRO_NORM, EPI_QKV>(p, s);
+  if (pro == PRO_NORM && epi == EPI_SWIGLU) return launch_gemv_t<T, PRO_NORM, EPI_SWIGLU>(p, s);
+  if constexpr (T != T_Q8_0)
+    if (pro == PRO_PREQ && epi == EPI_STORE) return launch_gemv_t<T, PRO_PREQ, EPI_STORE>(p, s);
+  return cudaErrorInvalidValue;
+}
+
+static cudaError_t launch_gemv(int type, int pro, int epi, const GemvParams& p, cudaStream_t s) {
+  switch (type) {
+    case T_TQ1_0: return launch_gemv_pe<T_TQ1_0>(pro, epi, p, s);
+    case T_TQ2_0: return launch_gemv_pe<T_TQ2_0>(pro, epi, p, s);
+    case T_Q4_K: return launch_gemv_pe<T_Q4_K>(pro, epi, p, s);
+    case T_Q6_K: return launch_gemv_pe<T_Q6_K>(pro, epi, p, s);
+    case T_Q8_0: return launch_gemv_pe<T_Q8_0>(pro, epi, p, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// kernel-level entry points
+
+__global__ void quantize_vec_kernel(const float* __restrict__ x, int n, int8_t* __restrict__ q,
+                                    float* __restrict__ scale) {
+  __shared__ float red[32];
+  float am = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) am = absmax_acc(am, x[i]);
+  const float amax = block_reduce<float>(am, red, OpMax(), 0.0f);
+  const bool nz = amax > 0.0f;
+  const float inv = nz ? __fdiv_rn(127.0f, amax) : 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) q[i] = (int8_t)quant1(x[i], inv);
+  if (threadIdx.x == 0) *scale = nz ? __fdiv_rn(amax, 127.0f) : 0.0f;
+}
+
+extern "C" foxcuda_status foxcuda_quantize_activations_i8(const float* x, size_t n, int8_t* q,
+                                                          float* scale, void* stream) {
+  if (!x || !q || !scale || n == 0) return fail(FOXCUDA_ERR_ARG, "quantize: null or empty");
+  if (n > (size_t)INT32_MAX) return fail(FOXCUDA_ERR_ARG, "quantize: vector too long");
+  quantize_vec_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(x, (int)n, q, scale);
+  CK(cudaGetLastError(), "quantize launch");
+  return FOXCUDA_OK;
+}
+
+static foxcuda_status check_gemv_args(int type, const void* a, const void* w, size_t n_rows,
+                                      size_t n_cols, const void* out, int* nb, int* U) {
+  if (!a || !w || !out) return fail(FOXCUDA_ERR_ARG, "gemv: null pointer");
+  if (n_rows == 0 || n_cols == 0) return fail(FOXCUDA_ERR_ARG, "gemv: empty matrix");
+  if (!type_gemv_ok(type))
+    return fail(FOXCUDA_ERR_UNSUPPORTED,
+                "gemv: no kernel for ggml type %d; this build handles TQ1_0, TQ2_0, Q4_K, "
+                "Q6_K and Q8_0", type);
+  const int be = block_elems(type);
+  if (n_cols % be)
+    return fail(FOXCUDA_ERR_ARG, "gemv: %zu columns is not a multiple of the %d-element block",
+                n_cols, be);
+  if (type != T_Q8_0 && n_cols % 256)
+    return fail(FOXCUDA_ERR_ARG, "gemv: %zu columns is not a multiple of 256", n_cols);
+  if (n_rows > (size_t)INT32_MAX || n_cols > (1u << 20))
+    return fail(FOXCUDA_ERR_ARG, "gemv: %zu x %zu is beyond this build's limits", n_rows, n_cols);
+  *nb = (int)(n_cols / be);
+  *U = unit_rows(type, *nb);
+  if (*U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemv: %zu columns has no unit layout", n_cols);
+  return FOXCUDA_OK;
+}
+
+extern "C" size_t foxcuda_packed_bytes(int type, size_t n_rows, size_t n_cols) {
+  if (!type_gemv_ok(type)) return 0;
+  return n_rows * row_bytes(type, n_cols);
+}
+
+static cudaError_t pack_rows(int type, const void* src, size_t n_rows, int nb, int U, void* dst,
+                             cudaStream_t s) {
+  const long total = (long)n_rows * nb;
+  const int grid = (int)std::min<long>((total + 255) / 256, 4096);
+  pack_kernel<<<grid, 256, 0, s>>>(type, (const uint8_t*)src, (int)n_rows, nb, U, (uint8_t*)dst);
+  return cudaGetLastError();
+}
+
+extern "C" foxcuda_status foxcuda_pack(int type, const void* src, size_t n_rows, size_t n_cols,
+                                       void* packed, void* stream) {
+  int nb, U;
+  foxcuda_status st = check_gemv_args(type, src, src, n_rows, n_cols, packed, &nb, &U);
+  if (st) return st;
+  CK(pack_rows(type, src, n_rows, nb, U, packed, (cudaStream_t)stream), "pack launch");
+  return FOXCUDA_OK;
+}
+
+static GemvParams gemv_base(int type, const void* packed, size_t n_rows, size_t n_cols, int nb, int U) {
+  GemvParams p;
+  memset(&p, 0, sizeof p);
+  p.w = (const uint8_t*)packed;
+  p.n_rows = (int)n_rows;
+  p.K = (int)n_cols;
+  p.nb = nb;
+  p.U = U;
+  return p;
+}
+
+extern "C" foxcuda_status foxcuda_gemv_packed(int type, const float* x, const void* packed,
+                                              size_t n_rows, size_t n_cols, float* out,
+                                              void* stream) {
+  int nb, U;
+  foxcuda_status st = check_gemv_args(type, x, packed, n_rows, n_cols, out, &nb, &U);
+  if (st) return st;
+  GemvParams p = gemv_base(type, packed, n_rows, n_cols, nb, U);
+  p.x = x;
+  p.out = out;
+  CK(launch_gemv(type, PRO_VEC, EPI_STORE, p, (cudaStream_t)stream), "gemv launch");
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_gemv(int type, const float* x, const void* w, size_t n_rows,
+                                       size_t n_cols, float* out, void* stream) {
+  int nb, U;
+  foxcuda_status st = check_gemv_args(type, x, w, n_rows, n_cols, out, &nb, &U);
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  void* scratch = nullptr;
+  CK(cudaMallocAsync(&scratch, n_rows * row_bytes(type, n_cols), s), "gemv scratch");
+  cudaError_t e = pack_rows(type, w, n_rows, nb, U, scratch, s);
+  if (e == cudaSuccess) {
+    GemvParams p = gemv_base(type, scratch, n_rows, n_cols, nb, U);
+    p.x = x;
+    p.out = out;
+    e = launch_gemv(type, PRO_VEC, EPI_STORE, p, s);
+  }
+  cudaError_t e2 = cudaFreeAsync(scratch, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gemv");
+  CK(e2, "gemv scratch free");
+  return FOXCUDA_OK;
+}
+
+static foxcuda_status gemv_tq_i8(int type, const int8_t* q, const float* act_scale, const void* w,
+                                 size_t n_rows, size_t n_cols, float* out, void* stream) {
+  int nb, U;
+  foxcuda_status st = check_gemv_args(type, q, w, n_rows, n_cols, out, &nb, &U);
+  if (st) return st;
+  if (!act_scale) return fail(FOXCUDA_ERR_ARG, "gemv: null activation scale");
+  cudaStream_t s = (cudaStream_t)stream;
+  void* scratch = nullptr;
+  CK(cudaMallocAsync(&scratch, n_rows * row_bytes(type, n_cols), s), "gemv scratch");
+  cudaError_t e = pack_rows(type, w, n_rows, nb, U, scratch, s);
+  if (e == cudaSuccess) {
+    GemvParams p = gemv_base(type, scratch, n_rows, n_cols, nb, U);
+    p.xq = q;
+    p.xq_scale = act_scale;
+    p.out = out;
+    e = launch_gemv(type, PRO_PREQ, EPI_STORE, p, s);
+  }
+  cudaError_t e2 = cudaFreeAsync(scratch, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gemv");
+  CK(e2, "gemv scratch free");
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_gemv_tq1_i8(const int8_t* q, const float* act_scale,
+                                              const void* w, size_t n_rows, size_t n_cols,
+                                              float* out, void* stream) {
+  return gemv_tq_i8(T_TQ1_0, q, act_scale, w, n_rows, n_cols, out, stream);
+}
+extern "C" foxcuda_status foxcuda_gemv_tq2_i8(const int8_t* q, const float* act_scale,
+                                              const void* w, size_t n_rows, size_t n_cols,
+                                              float* out, void* stream) {
+  return gemv_tq_i8(T_TQ2_0, q, act_scale, w, n_rows, n_cols, out, stream);
+}
+
+extern "C" foxcuda_status foxcuda_dequant_row(int type, const void* row, size_t n, float* out,
+                                              void* stream) {
+  if (!row || !out || n == 0) return fail(FOXCUDA_ERR_ARG, "dequant: null or empty");
+  if (!(type == T_F32 || type == T_F16 || type == T_Q8_0 || type == T_Q4_K || type == T_Q6_K))
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "dequant: ggml type %d is not implemented", type);
+  if (n % block_elems(type))
+    return fail(FOXCUDA_ERR_ARG, "dequant: %zu elements is not a whole number of blocks", n);
+  const int grid = (int)std::min<size_t>((n + 255) / 256, 1024);
+  dequant_row_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(type, (const uint8_t*)row, (int)n, out);
+  CK(cudaGetLastError(), "dequant launch");
+  return FOXCUDA_OK;
+}
+
+// Integer partials straight from GGUF-layout blocks, through the same block
+// decoders the GEMV kernels use (the block bytes are regrouped in registers
+// into the plane order the decoders read).
+template <int T>
+__global__ void partials_kernel(const int8_t* __restrict__ q, const uint8_t* __restrict__ w,
+                                int n_rows, int nb, int32_t* __restrict__ out) {
+  const long g = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (g >= (long)n_rows * nb) return;
+  const int b = (int)(g % nb);
+  typename W<T>::R r;
+  unsigned char* rb = reinterpret_cast<unsigned char*>(&r);
+  memset(rb, 0, sizeof r);
+  const SegTable tab = seg_table(T);
+  const uint8_t* blk = w + g * block_bytes(T);
+  int off = 0;
+  for (int p = 0; p < tab.n; ++p) {
+    for (int i = 0; i < tab.s[p].size; ++i) rb[off + i] = blk[tab.s[p].src + i];
+    off += tab.s[p].size;
+  }
+  uint32_t xw[64];
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(q + (long)b * 256);
+  for (int i = 0; i < 64; ++i) xw[i] = src[i];
+  int sx = 0;
+  for (int i = 0; i < 64; ++i) sx = dp4a(0x01010101u, xw[i], sx);
+  if constexpr (T == T_TQ1_0 || T == T_TQ2_0) {
+    out[g] = W<T>::isum(r, xw, sx);
+  } else if constexpr (T == T_Q4_K) {
+    W<T>::ipart(r, xw, out + g * 16);
+  } else if constexpr (T == T_Q6_K) {
+    W<T>::ipart(r, xw, out + g * 4);
+  }
+}
+
+extern "C" foxcuda_status foxcuda_block_partials(int type, const int8_t* q, const void* w,
+                                                 size_t n_rows, size_t n_cols, int32_t* out,
+                                                 void* stream) {
+  if (!q || !w || !out || n_rows == 0 || n_cols == 0)
+    return fail(FOXCUDA_ERR_ARG, "partials: null pointer or empty matrix");
+  if (n_cols % 256) return fail(FOXCUDA_ERR_ARG, "partials: columns not a multiple of 256");
+  const int nb = (int)(n_cols / 256);
+  const long total = (long)n_rows * nb;
+  const int grid = (int)((total + 127) / 128);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (type) {
+    case T_TQ1_0: partials_kernel<T_TQ1_0><<<grid, 128, 0, s>>>(q, (const uint8_t*)w, (int)n_rows, nb, out); break;
+    case T_TQ2_0: partials_kernel<T_TQ2_0><<<grid, 128, 0, s>>>(q, (const uint8_t*)w, (int)n_rows, nb, out); break;
+    case T_Q4_K: partials_kernel<T_Q4_K><<<grid, 128, 0, s>>>(q, (const uint8_t*)w, (int)n_rows, nb, out); break;
+    case T_Q6_K: partials_kernel<T_Q6_K><<<grid, 128, 0, s>>>(q, (const uint8_t*)w, (int)n_rows, nb, out); break;
+    default: return fail(FOXCUDA_ERR_UNSUPPORTED, "partials: ggml type %d has none", type);
+  }
+  CK(cudaGetLastError(), "partials launch");
+  return FOXCUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// HBM weight store
+
+struct PackedMat {
+  int type = -1;
+  int n_rows = 0, K = 0, nb = 0, U = 0;
+  uint8_t* dev = nullptr;
+};
+
+struct RawTensor {
+  int type = -1;
+  uint64_t ne0 = 0, ne1 = 0;
+  uint8_t* dev = nullptr;
+  size_t bytes = 0;
+};
+
+struct LayerW {
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  PackedMat qkv[3];  // [q|k|v] split into runs of one type; count in n_qkv
+  int qkv_base[3] = {0, 0, 0};
+  int n_qkv = 0;
+  PackedMat o, gateup, down;
+};
+
+struct foxcuda_model {
+  foxcuda_model_info info;
+  int device = 0;
+  bool finalized = false;
+  std::vector<RawTensor> raw;  // [role * (n_layer+1) + layer] staging until finalize
+  RawTensor embd;              // GGUF layout, row gather
+  float* out_norm = nullptr;
+  PackedMat output;
+  std::vector<LayerW> layers;
+  uint64_t device_bytes = 0;
+  std::vector<void*> allocs;
+  RawTensor& slot(int role, uint32_t layer) { return raw[(size_t)role * (info.n_layer + 1) + layer]; }
+};
+
+static cudaError_t dev_alloc(foxcuda_model* m, size_t bytes, void** p) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e == cudaSuccess) { m->allocs.push_back(*p); m->device_bytes += bytes; }
+  return e;
+}
+
+extern "C" foxcuda_status foxcuda_model_create(const foxcuda_model_info* info, int device,
+                                               foxcuda_model** out) {
+  if (!info || !out) return fail(FOXCUDA_ERR_ARG, "model: null argument");
+  *out = nullptr;
+  const foxcuda_model_info& mi = *info;
+  if (!mi.n_layer || !mi.n_embd || !mi.n_head || !mi.n_head_kv || !mi.n_ff || !mi.n_vocab ||
+      !mi.head_dim)
+    return fail(FOXCUDA_ERR_FORMAT, "model: architecture metadata is incomplete");
+  if (mi.head_dim % 2) return fail(FOXCUDA_ERR_UNSUPPORTED, "model: odd head dimension %u", mi.head_dim);
+  if (mi.n_head % mi.n_head_kv)
+    return fail(FOXCUDA_ERR_FORMAT, "model: %u query heads do not divide into %u kv heads",
+                mi.n_head, mi.n_head_kv);
+  if (mi.n_head / mi.n_head_kv > ATTN_MAX_GQA || mi.head_dim > 32 * ATTN_MAX_DPL ||
+      mi.head_dim % 32)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "model: head_dim %u / gqa %u not covered by the "
+                "attention kernel (head_dim a multiple of 32 up to 256, gqa <= 8)",
+                mi.head_dim, mi.n_head / mi.n_head_kv);
+  if (mi.n_embd % 256 || mi.n_ff % 256 || (mi.n_head * mi.head_dim) % 256)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "model: widths must be multiples of 256");
+  foxcuda_status st = foxcuda_init(device);
+  if (st) return st;
+  foxcuda_model* m = new foxcuda_model();
+  m->info = mi;
+  m->device = device;
+  m->raw.resize((size_t)FOXCUDA_N_ROLES * (mi.n_layer + 1));
+  m->layers.resize(mi.n_layer);
+  *out = m;
+  return FOXCUDA_OK;
+}
+
+extern "C" void foxcuda_model_destroy(foxcuda_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  for (void* p : m->allocs) cudaFree(p);
+  for (RawTensor& r : m->raw) if (r.dev) cudaFree(r.dev);
+  delete m;
+}
+
+extern "C" uint64_t foxcuda_model_device_bytes(const foxcuda_model* m) { return m ? m->device_bytes : 0; }
+
+static bool role_per_layer(int role) { return role >= FOXCUDA_ATTN_NORM && role < FOXCUDA_N_ROLES; }
+
+extern "C" foxcuda_status foxcuda_model_upload(foxcuda_model* m, int role, uint32_t layer,
+                                               int type, uint64_t ne0, uint64_t ne1,
+                                               const void* host, size_t bytes) {
+  if (!m || !host) return fail(FOXCUDA_ERR_ARG, "upload: null argument");
+  if (m->finalized) return fail(FOXCUDA_ERR_ARG, "upload: model already finalized");
+  if (role < 0 || role >= FOXCUDA_N_ROLES) return fail(FOXCUDA_ERR_ARG, "upload: bad role %d", role);
+  if (role_per_layer(role) ? layer >= m->info.n_layer : layer != 0)
+    return fail(FOXCUDA_ERR_ARG, "upload: bad layer %u for role %d", layer, role);
+  if (ne1 == 0) ne1 = 1;
+  const size_t want = row_bytes(type, ne0) * ne1;
+  if (!(type == T_F32 || type == T_F16 || type_gemv_ok(type)) || row_bytes(type, ne0) == 0)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "upload: ggml type %d with %llu columns", type,
+                (unsigned long long)ne0);
+  if (bytes != want)
+    return fail(FOXCUDA_ERR_FORMAT, "upload: %zu bytes, the shape wants %zu", bytes, want);
+  cudaSetDevice(m->device);
+  RawTensor& r = m->slot(role, layer);
+  if (r.dev) cudaFree(r.dev);
+  r = RawTensor();
+  CK(cudaMalloc(&r.dev, bytes), "upload alloc");
+  r.type = type; r.ne0 = ne0; r.ne1 = ne1; r.bytes = bytes;
+  CK(cudaMemcpy(r.dev, host, bytes, cudaMemcpyHostToDevice), "upload copy");
+  return FOXCUDA_OK;
+}
+
+static foxcuda_status pack_into(foxcuda_model* m, int type, const void* src_dev, int n_rows, int K,
+                                PackedMat* out) {
+  const int nb = K / block_elems(type);
+  const int U = unit_rows(type, nb);
+  if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "pack: %d columns has no unit layout", K);
+  void* dst = nullptr;
+  CK(dev_alloc(m, (size_t)n_rows * row_bytes(type, K), &dst), "weight alloc");
+  CK(pack_rows(type, src_dev, n_rows, nb, U, dst, 0), "pack");
+  out->type = type; out->n_rows = n_rows; out->K = K; out->nb = nb; out->U = U;
+  out->dev = (uint8_t*)dst;
+  return FOXCUDA_OK;
+}
+
+static foxcuda_status norm_vec(foxcuda_model* m, const RawTensor& r, float** out) {
+  const uint32_t n = m->info.n_embd;
+  if (r.ne0 != n || r.ne1 != 1) return fail(FOXCUDA_ERR_FORMAT, "model: norm weight is not %u wide", n);
+  if (r.type != T_F32 && r.type != T_F16)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "model: norm weights must be F32 or F16");
+  void* d = nullptr;
+  CK(dev_alloc(m, n * 4, &d), "norm alloc");
+  dequant_row_kernel<<<(n + 255) / 256, 256>>>(r.type, r.dev, (int)n, (float*)d);
+  CK(cudaGetLastError(), "norm convert");
+  *out = (float*)d;
+  return FOXCUDA_OK;
+}
+
+static void free_raw(RawTensor& r) {
+  if (r.dev) cudaFree(r.dev);
+  r = RawTensor();
+}
+
+extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
+  if (!m) return fail(FOXCUDA_ERR_ARG, "finalize: null model");
+  if (m->finalized) return FOXCUDA_OK;
+  cudaSetDevice(m->device);
+  const foxcuda_model_info& mi = m->info;
+  const int nq = mi.n_head * mi.head_dim, nkv = mi.n_head_kv * mi.head_dim;
+  const int E = mi.n_embd, Fd = mi.n_ff;
+  static const char* names[] = {"token_embd", "output_norm", "output", "attn_norm", "attn_q",
+                                "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate",
+                                "ffn_up", "ffn_down"};
+  struct Want { int role; uint64_t ne0, ne1; };
+  const Want per_layer[] = {{FOXCUDA_ATTN_NORM, (uint64_t)E, 1}, {FOXCUDA_ATTN_Q, (uint64_t)E, (uint64_t)nq},
+                            {FOXCUDA_ATTN_K, (uint64_t)E, (uint64_t)nkv}, {FOXCUDA_ATTN_V, (uint64_t)E, (uint64_t)nkv},
+                            {FOXCUDA_ATTN_OUT, (uint64_t)nq, (uint64_t)E}, {FOXCUDA_FFN_NORM, (uint64_t)E, 1},
+                            {FOXCUDA_FFN_GATE, (uint64_t)E, (uint64_t)Fd}, {FOXCUDA_FFN_UP, (uint64_t)E, (uint64_t)Fd},
+                            {FOXCUDA_FFN_DOWN, (uint64_t)Fd, (uint64_t)E}};
+  for (uint32_t l = 0; l < mi.n_layer; ++l)
+    for (const Want& w : per_layer) {
+      const RawTensor& r = m->slot(w.role, l);
+      if (!r.dev) return fail(FOXCUDA_ERR_NOTFOUND, "model: tensor 'blk.%u.%s.weight' is missing", l, names[w.role]);
+      if (r.ne0 != w.ne0 || r.ne1 != w.ne1)
+        return fail(FOXCUDA_ERR_FORMAT, "model: 'blk.%u.%s.weight' is %llux%llu, expected %llux%llu", l,
+                    names[w.role], (unsigned long long)r.ne0, (unsigned long long)r.ne1,
+                    (unsigned long long)w.ne0, (unsigned long long)w.ne1);
+      if (w.ne1 > 1 && !type_gemv_ok(r.type))
+        return fail(FOXCUDA_ERR_UNSUPPORTED, "model: 'blk.%u.%s.weight' has ggml type %d, which has no "
+                    "kernel here", l, names[w.role], r.type);
+    }
+  RawTensor& emb = m->slot(FOXCUDA_TOKEN_EMBD, 0);
+  if (!emb.dev) return fail(FOXCUDA_ERR_NOTFOUND, "model: tensor 'token_embd.weight' is missing");
+  if (emb.ne0 != (uint64_t)E || emb.ne1 != mi.n_vocab)
+    return fail(FOXCUDA_ERR_FORMAT, "model: token_embd is %llux%llu, expected %ux%u",
+                (unsigned long long)emb.ne0, (unsigned long long)emb.ne1, E, mi.n_vocab);
+  if (!(emb.type == T_F32 || emb.type == T_F16 || emb.type == T_Q8_0 || emb.type == T_Q4_K ||
+        emb.type == T_Q6_K))
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "model: token_embd type %d cannot be dequantised "
+                "(upstream src/kernels.c:886-940)", emb.type);
+  if (!m->slot(FOXCUDA_OUTPUT_NORM, 0).dev)
+    return fail(FOXCUDA_ERR_NOTFOUND, "model: tensor 'output_norm.weight' is missing");
+  RawTensor& outw = m->slot(FOXCUDA_OUTPUT, 0);
+  const RawTensor& head = outw.dev ? outw : emb;  // tied output (upstream src/model.c:248-252)
+  if (head.ne0 != (uint64_t)E || head.ne1 != mi.n_vocab)
+    return fail(FOXCUDA_ERR_FORMAT, "model: output head is not %ux%u", E, mi.n_vocab);
+  if (!type_gemv_ok(head.type))
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "model: output head type %d has no kernel here", head.type);
+
+  foxcuda_status st;
+  for (uint32_t l = 0; l < mi.n_layer; ++l) {
+    LayerW& L = m->layers[l];
+    if ((st = norm_vec(m, m->slot(FOXCUDA_ATTN_NORM, l), &L.attn_norm))) return st;
+    if ((st = norm_vec(m, m->slot(FOXCUDA_FFN_NORM, l), &L.ffn_norm))) return st;
+    // q|k|v: rows concatenated; consecutive tensors of one type share a matrix
+    const RawTensor* qkv[3] = {&m->slot(FOXCUDA_ATTN_Q, l), &m->slot(FOXCUDA_ATTN_K, l),
+                               &m->slot(FOXCUDA_ATTN_V, l)};
+    const int rows[3] = {nq, nkv, nkv};
+    int i = 0, base = 0;
+    L.n_qkv = 0;
+    while (i < 3) {
+      int j = i, nrow = 0;
+      size_t bytes = 0;
+      while (j < 3 && qkv[j]->type == qkv[i]->type) { nrow += rows[j]; bytes += qkv[j]->bytes; ++j; }
+      void* cat = nullptr;
+      CK(cudaMalloc(&cat, bytes), "staging alloc");
+      size_t off = 0;
+      for (int k = i; k < j; ++k) {
+        cudaMemcpy((uint8_t*)cat + off, qkv[k]->dev, qkv[k]->bytes, cudaMemcpyDeviceToDevice);
+        off += qkv[k]->bytes;
+      }
+      st = pack_into(m, qkv[i]->type, cat, nrow, E, &L.qkv[L.n_qkv]);
+      cudaDeviceSynchronize();
+      cudaFree(cat);
+      if (st) return st;
+      if (L.qkv[L.n_qkv].U > 0 && ((rows[i] % L.qkv[L.n_qkv].U) || (mi.head_dim % 2)))
+        return fail(FOXCUDA_ERR_UNSUPPORTED, "model: q/k/v rows do not align to %d-row units",
+                    L.qkv[L.n_qkv].U);
+      L.qkv_base[L.n_qkv] = base;
+      base += nrow;
+      L.n_qkv++;
+      i = j;
+    }
+    if ((st = pack_into(m, m->slot(FOXCUDA_ATTN_OUT, l).type, m->slot(FOXCUDA_ATTN_OUT, l).dev, E, nq, &L.o))) return st;
+    // gate|up interleaved per unit: U/2 gate rows then the same U/2 up rows
+    const RawTensor& g = m->slot(FOXCUDA_FFN_GATE, l);
+    const RawTensor& u = m->slot(FOXCUDA_FFN_UP, l);
+    if (g.type != u.type)
+      return fail(FOXCUDA_ERR_UNSUPPORTED, "model: ffn_gate and ffn_up types differ in layer %u", l);
+    {
+      const int nb = E / block_elems(g.type);
+      const int U = unit_rows(g.type, nb);
+      if (U < 0 || Fd % (U / 2)) return fail(FOXCUDA_ERR_UNSUPPORTED, "model: ffn width %d vs unit %d", Fd, U);
+      const size_t rb = row_bytes(g.type, E), half = (size_t)(U / 2) * rb;
+      void* cat = nullptr;
+      CK(cudaMalloc(&cat, g.bytes + u.bytes), "staging alloc");
+      CK(cudaMemcpy2D(cat, 2 * half, g.dev, half, half, Fd / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
+      CK(cudaMemcpy2D((uint8_t*)cat + half, 2 * half, u.dev, half, half, Fd / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
+      st = pack_into(m, g.type, cat, 2 * Fd, E, &L.gateup);
+      cudaDeviceSynchronize();
+      cudaFree(cat);
+      if (st) return st;
+    }
+    if ((st = pack_into(m, m->slot(FOXCUDA_FFN_DOWN, l).type, m->slot(FOXCUDA_FFN_DOWN, l).dev, E, Fd, &L.down))) return st;
+    CK(cudaDeviceSynchronize(), "finalize layer");
+    for (int role = FOXCUDA_ATTN_NORM; role < FOXCUDA_N_ROLES; ++role) free_raw(m->slot(role, l));
+  }
+  if ((st = norm_vec(m, m->slot(FOXCUDA_OUTPUT_NORM, 0), &m->out_norm))) return st;
+  if ((st = pack_into(m, head.type, head.dev, mi.n_vocab, E, &m->output))) return st;
+  CK(cudaDeviceSynchronize(), "finalize head");
+  m->embd = emb;
+  m->device_bytes += emb.bytes;
+  emb = RawTensor();  // ownership moves to m->embd
+  free_raw(outw);
+  free_raw(m->slot(FOXCUDA_OUTPUT_NORM, 0));
+  m->finalized = true;
+  return FOXCUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// context
+
+struct foxcuda_context {
+  foxcuda_model* m = nullptr;
+  uint32_t n_ctx = 0;
+  int kv_f16 = 1;
+  int attn_exact = 0;
+  cudaStream_t stream = nullptr;
+  float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  void *kc = nullptr, *vc = nullptr;
+  size_t kv_layer_elems = 0;
+  int* pos_dev = nullptr;
+  uint32_t* token_dev = nullptr;
+  uint32_t* tokens_dev = nullptr;  // prompt staging
+  size_t tokens_cap = 0;
+  float* attn_part = nullptr;
+  unsigned* attn_cnt = nullptr;
+  int S_max = 1;
+  uint32_t* ring = nullptr;
+  float* trace = nullptr;
+  bool trace_on = false;
+  uint32_t pos = 0;
+  cudaGraphExec_t g_body = nullptr, g_full = nullptr;
+  uint32_t* h_pinned = nullptr;  // [0] token in, [1..] picks out
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  double last_seconds = 0.0;
+  std::vector<void*> allocs;
+};
+
+struct foxcuda_sampler {
+  foxcuda_context* c = nullptr;
+  foxcuda_sampler_config cfg;
+  int k = 0;
+  SamplerDev* dev = nullptr;
+  cudaGraphExec_t g_decode = nullptr;
+  uint32_t n_out = 0;  // host mirror of dev->n_out
+};
+
+static cudaError_t ctx_alloc(foxcuda_context* c, size_t bytes, void** p) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e == cudaSuccess) { c->allocs.push_back(*p); cudaMemset(*p, 0, bytes ? bytes : 16); }
+  return e;
+}
+
+extern "C" void foxcuda_context_destroy(foxcuda_context* c) {
+  if (!c) return;
+  cudaSetDevice(c->m->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->g_body) cudaGraphExecDestroy(c->g_body);
+  if (c->g_full) cudaGraphExecDestroy(c->g_full);
+  for (void* p : c->allocs) cudaFree(p);
+  if (c->h_pinned) cudaFreeHost(c->h_pinned);
+  if (c->ev0) cudaEventDestroy(c->ev0);
+  if (c->ev1) cudaEventDestroy(c->ev1);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda_context_config* cfg,
+                                                 foxcuda_context** out) {
+  if (!m || !out) return fail(FOXCUDA_ERR_ARG, "context: null argument");
+  *out = nullptr;
+  if (!m->finalized) {
+    foxcuda_status st = foxcuda_model_finalize(m);
+    if (st) return st;
+  }
+  cudaSetDevice(m->device);
+  const foxcuda_model_info& mi = m->info;
+  foxcuda_context* c = new foxcuda_context();
+  c->m = m;
+  c->n_ctx = cfg && cfg->n_ctx ? cfg->n_ctx : 2048;
+  c->kv_f16 = cfg ? cfg->kv_type == FOXCUDA_KV_F16 : 1;
+  c->attn_exact = cfg ? cfg->attn_exact != 0 : 0;
+  if (c->attn_exact && c->n_ctx > 16384) {
+    delete c;
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "context: the exact attention mode holds at most 16384 positions");
+  }
+  const int nq = mi.n_head * mi.head_dim, nkv = mi.n_head_kv * mi.head_dim;
+  const int half = mi.head_dim / 2;
+  const int gqa = mi.n_head / mi.n_head_kv;
+  c->S_max = std::max(1, std::min(32, 2 * sm_count(m->device) / (int)mi.n_head_kv));
+  c->kv_layer_elems = (size_t)mi.n_head_kv * c->n_ctx * mi.head_dim;
+  const size_t kv_bytes = c->kv_layer_elems * mi.n_layer * (c->kv_f16 ? 2 : 4);
+  cudaError_t e = cudaSuccess;
+  auto A = [&](size_t bytes, void** p) { if (e == cudaSuccess) e = ctx_alloc(c, bytes, p); };
+  A(kv_bytes, &c->kc);
+  A(kv_bytes, &c->vc);
+  A((size_t)mi.n_embd * 4, (void**)&c->x);
+  A((size_t)nq * 4, (void**)&c->q);
+  A((size_t)nq * 4, (void**)&c->att);
+  A((size_t)mi.n_ff * 4, (void**)&c->h);
+  A((size_t)mi.n_vocab * 4, (void**)&c->logits);
+  A((size_t)c->n_ctx * half * 4, (void**)&c->rope_cos);
+  A((size_t)c->n_ctx * half * 4, (void**)&c->rope_sin);
+  A(16, (void**)&c->pos_dev);
+  A(16, (void**)&c->token_dev);
+  A((size_t)mi.n_head_kv * c->S_max * gqa * (mi.head_dim + 2) * 4, (void**)&c->attn_part);
+  A((size_t)mi.n_head_kv * 4, (void**)&c->attn_cnt);
+  A((size_t)c->n_ctx * 4, (void**)&c->ring);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMallocHost((void**)&c->h_pinned, 64);
+  if (e == cudaSuccess) e = cudaEventCreate(&c->ev0);
+  if (e == cudaSuccess) e = cudaEventCreate(&c->ev1);
+  if (e != cudaSuccess) {
+    foxcuda_context_destroy(c);
+    return cuda_fail(e, "context allocation");
+  }
+  // RoPE tables in double, cast to float (upstream src/forward.c:107-118)
+  std::vector<float> cs((size_t)c->n_ctx * half), sn((size_t)c->n_ctx * half);
+  for (uint32_t p = 0; p < c->n_ctx; ++p)
+    for (int i = 0; i < half; ++i) {
+      const double th = (double)p * pow((double)mi.rope_freq_base, -2.0 * (double)i / (double)mi.head_dim);
+      cs[(size_t)p * half + i] = (float)cos(th);
+      sn[(size_t)p * half + i] = (float)sin(th);
+    }
+  e = cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    foxcuda_context_destroy(c);
+    return cuda_fail(e, "context init");
+  }
+  *out = c;
+  return FOXCUDA_OK;
+}
+
+extern "C" void foxcuda_context_reset(foxcuda_context* c) {
+  if (!c) return;
+  cudaSetDevice(c->m->device);
+  cudaStreamSynchronize(c->stream);
+  c->pos = 0;
+  cudaMemsetAsync(c->pos_dev, 0, 4, c->stream);
+  cudaStreamSynchronize(c->stream);
+}
+
+extern "C" uint32_t foxcuda_context_position(const foxcuda_context* c) { return c ? c->pos : 0; }
+extern "C" double foxcuda_context_last_eval_seconds(const foxcuda_context* c) {
+  return c ? c->last_seconds : 0.0;
+}
+
+// One token through the layers (upstream src/forward.c:315-399): embedding,
+// then per layer the fused q|k|v (+RMSNorm, +RoPE, +KV write), attention, o
+// (+residual), gate|up (+RMSNorm, +SwiGLU), down (+residual); pos += 1.
+static cudaError_t enqueue_body(foxcuda_context* c, bool trace) {
+  foxcuda_model* m = c->m;
+  const foxcuda_model_info& mi = m->info;
+  cudaStream_t s = c->stream;
+  const int nq = mi.n_head * mi.head_dim, nkv = mi.n_head_kv * mi.head_dim;
+  const size_t elem = c->kv_f16 ? 2 : 4;
+  const size_t emb_rb = row_bytes(m->embd.type, mi.n_embd);
+  embed_kernel<<<(mi.n_embd + 255) / 256, 256, 0, s>>>(m->embd.type, m->embd.dev, emb_rb,
+                                                        (int)mi.n_embd, c->token_dev, c->x);
+  cudaError_t e = cudaGetLastError();
+  if (e) return e;
+  if (trace) cudaMemcpyAsync(c->trace, c->x, mi.n_embd * 4, cudaMemcpyDeviceToDevice, s);
+  for (uint32_t l = 0; l < mi.n_layer; ++l) {
+    const LayerW& L = m->layers[l];
+    void* kl = (uint8_t*)c->kc + (size_t)l * c->kv_layer_elems * elem;
+    void* vl = (uint8_t*)c->vc + (size_t)l * c->kv_layer_elems * elem;
+    for (int i = 0; i < L.n_qkv; ++i) {
+      const PackedMat& W = L.qkv[i];
+      GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
+      p.x = c->x; p.norm_w = L.attn_norm; p.eps = mi.rms_eps;
+      p.out = c->q; p.nq = nq; p.nkv = nkv; p.hd = mi.head_dim; p.n_ctx = c->n_ctx;
+      p.kv_f16 = c->kv_f16; p.rope_cos = c->rope_cos; p.rope_sin = c->rope_sin;
+      p.pos = c->pos_dev; p.kcache = kl; p.vcache = vl; p.row_base = L.qkv_base[i];
+      if ((e = launch_gemv(W.type, PRO_NORM, EPI_QKV, p, s))) return e;
+    }
+    AttnParams ap;
+    ap.q = c->q; ap.kcache = kl; ap.vcache = vl; ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
+    ap.hd = mi.head_dim; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
+    ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
+    ap.scale = 1.0f / sqrtf((float)mi.head_dim);
+    const dim3 ag(c->S_max, mi.n_head_kv);
+    if (c->attn_exact) {
+      const size_t sm = (size_t)c->n_ctx * 4;
+      if (sm > 48 * 1024)
+        cudaFuncSetAttribute(attention_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      attention_exact_kernel<<<mi.n_head, 128, sm, s>>>(ap);
+    } else switch (mi.head_dim / 32) {
+      case 2: attention_kernel<2><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+      case 4: attention_kernel<4><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+      case 8: attention_kernel<8><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+      default: attention_kernel<1><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+    }
+    if ((e = cudaGetLastError())) return e;
+    {
+      GemvParams p = gemv_base(L.o.type, L.o.dev, L.o.n_rows, L.o.K, L.o.nb, L.o.U);
+      p.x = c->att; p.out = c->x;
+      if ((e = launch_gemv(L.o.type, PRO_VEC, EPI_ADD, p, s))) return e;
+    }
+    {
+      GemvParams p = gemv_base(L.gateup.type, L.gateup.dev, L.gateup.n_rows, L.gateup.K,
+                               L.gateup.nb, L.gateup.U);
+      p.x = c->x; p.norm_w = L.ffn_norm; p.eps = mi.rms_eps; p.out = c->h;
+      if ((e = launch_gemv(L.gateup.type, PRO_NORM, EPI_SWIGLU, p, s))) return e;
+    }
+    {
+      GemvParams p = gemv_base(L.down.type, L.down.dev, L.down.n_rows, L.down.K, L.down.nb, L.down.U);
+      p.x = c->h; p.out = c->x;
+      if ((e = launch_gemv(L.down.type, PRO_VEC, EPI_ADD, p, s))) return e;
+    }
+    if (trace) cudaMemcpyAsync(c->trace + (size_t)(l + 1) * mi.n_embd, c->x, mi.n_embd * 4,
+                               cudaMemcpyDeviceToDevice, s);
+  }
+  advance_kernel<<<1, 32, 0, s>>>(c->pos_dev, 1);
+  return cudaGetLastError();
+}
+
+// Output norm on the last token and the head (upstream src/forward.c:403-408).
+static cudaError_t enqueue_head(foxcuda_context* c) {
+  foxcuda_model* m = c->m;
+  const PackedMat& H = m->output;
+  GemvParams p = gemv_base(H.type, H.dev, H.n_rows, H.K, H.nb, H.U);
+  p.x = c->x; p.norm_w = m->out_norm; p.eps = m->info.rms_eps; p.out = c->logits;
+  return launch_gemv(H.type, PRO_NORM, EPI_STORE, p, c->stream);
+}
+
+static cudaError_t enqueue_pick(foxcuda_sampler* sm, bool accept) {
+  foxcuda_context* c = sm->c;
+  const int nv = c->m->info.n_vocab;
+  const bool pen = sm->cfg.repeat_penalty > 1.0f;
+  if (pen) penalty_kernel<<<1, 256, 0, c->stream>>>(sm->dev, c->logits, nv, sm->cfg.repeat_penalty);
+  if (sm->cfg.temperature <= 0.0f) {
+    const int grid = std::min(1024, std::max(1, std::min(current_sms(), (nv + ARGMAX_THREADS - 1) / ARGMAX_THREADS)));
+    argmax_kernel<<<grid, ARGMAX_THREADS, 0, c->stream>>>(sm->dev, c->logits, nv, pen, accept,
+                                                           c->token_dev, c->ring, (int)c->n_ctx);
+  } else {
+    topk_sample_kernel<<<1, TOPK_THREADS, 0, c->stream>>>(sm->dev, c->logits, nv, sm->k,
+                                                          sm->cfg.temperature, sm->cfg.top_p, pen,
+                                                          accept, c->token_dev, c->ring,
+                                                          (int)c->n_ctx);
+  }
+  return cudaGetLastError();
+}
+
+static cudaError_t capture(foxcuda_context* c, cudaGraphExec_t* out, bool head, foxcuda_sampler* sm) {
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal);
+  if (e) return e;
+  e = enqueue_body(c, false);
+  if (!e && head) e = enqueue_head(c);
+  if (!e && sm) e = enqueue_pick(sm, true);
+  cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+  if (e) { if (g) cudaGraphDestroy(g); return e; }
+  if (e2) return e2;
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  return e;
+}
+
+extern "C" foxcuda_status foxcuda_context_set_trace(foxcuda_context* c, int on) {
+  if (!c) return fail(FOXCUDA_ERR_ARG, "trace: null context");
+  cudaSetDevice(c->m->device);
+  if (on && !c->trace) {
+    void* p = nullptr;
+    CK(ctx_alloc(c, (size_t)(c->m->info.n_layer + 1) * c->m->info.n_embd * 4, &p), "trace alloc");
+    c->trace = (float*)p;
+  }
+  c->trace_on = on != 0;
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_context_hidden(const foxcuda_context* c, uint32_t layer, float* out) {
+  if (!c || !out) return fail(FOXCUDA_ERR_ARG, "hidden: null argument");
+  if (!c->trace) return fail(FOXCUDA_ERR_ARG, "hidden: tracing is off");
+  if (layer > c->m->info.n_layer) return fail(FOXCUDA_ERR_ARG, "hidden: layer %u out of range", layer);
+  cudaSetDevice(c->m->device);
+  CK(cudaMemcpy(out, c->trace + (size_t)layer * c->m->info.n_embd, c->m->info.n_embd * 4,
+                cudaMemcpyDeviceToHost), "hidden copy");
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* tokens, size_t n,
+                                       float* logits_out) {
+  if (!c || !tokens || n == 0) return fail(FOXCUDA_ERR_ARG, "eval: nothing to evaluate");
+  const foxcuda_model_info& mi = c->m->info;
+  if ((size_t)c->pos + n > c->n_ctx)
+    return fail(FOXCUDA_ERR_ARG, "forward: %zu tokens past position %u would overrun the %u token context",
+                n, c->pos, c->n_ctx);
+  for (size_t i = 0; i < n; ++i)
+    if (tokens[i] >= mi.n_vocab)
+      return fail(FOXCUDA_ERR_ARG, "forward: token %u is outside the %u entry vocabulary", tokens[i], mi.n_vocab);
+  cudaSetDevice(c->m->device);
+  if (n > c->tokens_cap) {
+    void* p = nullptr;
+    CK(ctx_alloc(c, n * 4, &p), "token staging");
+    c->tokens_dev = (uint32_t*)p;
+    c->tokens_cap = n;
+  }
+  CK(cudaMemcpyAsync(c->tokens_dev, tokens, n * 4, cudaMemcpyHostToDevice, c->stream), "token upload");
+  if (!c->trace_on && !c->g_body) CK(capture(c, &c->g_body, false, nullptr), "capture");
+  if (!c->trace_on && !c->g_full) CK(capture(c, &c->g_full, true, nullptr), "capture");
+  CK(cudaEventRecord(c->ev0, c->stream), "event");
+  for (size_t i = 0; i < n; ++i) {
+    CK(cudaMemcpyAsync(c->token_dev, c->tokens_dev + i, 4, cudaMemcpyDeviceToDevice, c->stream), "token");
+    const bool last = i + 1 == n;
+    if (c->trace_on) {
+      CK(enqueue_body(c, true), "forward");
+      if (last) CK(enqueue_head(c), "head");
+    } else {
+      CK(cudaGraphLaunch(last ? c->g_full : c->g_body, c->stream), "graph launch");
+    }
+  }
+  CK(cudaEventRecord(c->ev1, c->stream), "event");
+  if (logits_out)
+    CK(cudaMemcpyAsync(logits_out, c->logits, (size_t)mi.n_vocab * 4, cudaMemcpyDeviceToHost, c->stream),
+       "logits copy");
+  CK(cudaStreamSynchronize(c->stream), "eval");
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+  c->last_seconds = ms / 1e3;
+  c->pos += (uint32_t)n;
+  return FOXCUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// sampler
+
+extern "C" foxcuda_status foxcuda_sampler_create(foxcuda_context* c, const foxcuda_sampler_config* cfg,
+                                                 foxcuda_sampler** out) {
+  if (!c || !out) return fail(FOXCUDA_ERR_ARG, "sampler: null argument");
+  *out = nullptr;
+  foxcuda_sampler_config k;
+  if (cfg) k = *cfg;
+  else k = {0.8f, 40, 0.95f, 1.1f, 64, 0};  // upstream defaults, src/sample.c:21-30
+  // upstream src/sample.c:59-66
+  if (k.top_k < 0) k.top_k = 0;
+  if (k.top_k > TOPK_MAX) k.top_k = TOPK_MAX;
+  if (k.top_p <= 0.0f || k.top_p > 1.0f) k.top_p = 1.0f;
+  if (k.repeat_penalty < 1.0f) k.repeat_penalty = 1.0f;
+  if (k.repeat_last_n > SAMPLER_MAX_HIST)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "sampler: repeat_last_n %u is above %d", k.repeat_last_n, SAMPLER_MAX_HIST);
+  cudaSetDevice(c->m->device);
+  foxcuda_sampler* s = new foxcuda_sampler();
+  s->c = c;
+  s->cfg = k;
+  const int nv = (int)c->m->info.n_vocab;
+  s->k = (k.top_k <= 0 || k.top_k > nv) ? std::min(nv, TOPK_MAX) : k.top_k;
+  cudaError_t e = cudaMalloc(&s->dev, sizeof(SamplerDev));
+  if (e == cudaSuccess) e = cudaMemset(s->dev, 0, sizeof(SamplerDev));
+  if (e == cudaSuccess) {
+    const uint32_t cap = k.repeat_last_n ? k.repeat_last_n : 1;
+    const unsigned long long rng = k.seed ? k.seed : 0x9E3779B97F4A7C15ull;
+    e = cudaMemcpy(&s->dev->hist_cap, &cap, 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(&s->dev->rng, &rng, 8, cudaMemcpyHostToDevice);
+  }
+  if (e != cudaSuccess) {
+    if (s->dev) cudaFree(s->dev);
+    delete s;
+    return cuda_fail(e, "sampler alloc");
+  }
+  *out = s;
+  return FOXCUDA_OK;
+}
+
+extern "C" void foxcuda_sampler_destroy(foxcuda_sampler* s) {
+  if (!s) return;
+  cudaSetDevice(s->c->m->device);
+  cudaStreamSynchronize(s->c->stream);
+  if (s->g_decode) cudaGraphExecDestroy(s->g_decode);
+  cudaFree(s->dev);
+  delete s;
+}
+
+extern "C" foxcuda_status foxcuda_sampler_accept(foxcuda_sampler* s, uint32_t token) {
+  if (!s) return fail(FOXCUDA_ERR_ARG, "sampler: null");
+  cudaSetDevice(s->c->m->device);
+  accept_kernel<<<1, 32, 0, s->c->stream>>>(s->dev, token);
+  CK(cudaGetLastError(), "accept");
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_sampler_pick(foxcuda_sampler* s, uint32_t* out) {
+  if (!s || !out) return fail(FOXCUDA_ERR_ARG, "sampler: null argument");
+  foxcuda_context* c = s->c;
+  cudaSetDevice(c->m->device);
+  CK(enqueue_pick(s, false), "pick");
+  s->n_out++;
+  CK(cudaMemcpyAsync(c->h_pinned + 1, c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream), "pick copy");
+  CK(cudaStreamSynchronize(c->stream), "pick");
+  *out = c->h_pinned[1];
+  return FOXCUDA_OK;
+}
+
+static foxcuda_status decode_steps(foxcuda_context* c, foxcuda_sampler* s, uint32_t token, size_t n,
+                                   uint32_t* out) {
+  const foxcuda_model_info& mi = c->m->info;
+  if (token >= mi.n_vocab) return fail(FOXCUDA_ERR_ARG, "forward: token %u is outside the vocabulary", token);
+  if ((size_t)c->pos + n > c->n_ctx)
+    return fail(FOXCUDA_ERR_ARG, "forward: %zu tokens past position %u would overrun the %u token context",
+                n, c->pos, c->n_ctx);
+  cudaSetDevice(c->m->device);
+  if (!s->g_decode) CK(capture(c, &s->g_decode, true, s), "capture");
+  c->h_pinned[0] = token;
+  CK(cudaMemcpyAsync(c->token_dev, c->h_pinned, 4, cudaMemcpyHostToDevice, c->stream), "token in");
+  CK(cudaEventRecord(c->ev0, c->stream), "event");
+  const uint32_t start = s->n_out;
+  for (size_t i = 0; i < n; ++i) CK(cudaGraphLaunch(s->g_decode, c->stream), "graph launch");
+  CK(cudaEventRecord(c->ev1, c->stream), "event");
+  s->n_out += (uint32_t)n;
+  if (n == 1) {
+    CK(cudaMemcpyAsync(c->h_pinned + 1, c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream), "token out");
+    CK(cudaStreamSynchronize(c->stream), "decode");
+    out[0] = c->h_pinned[1];
+  } else {
+    CK(cudaStreamSynchronize(c->stream), "generate");
+    const uint32_t cap = c->n_ctx;
+    for (size_t i = 0; i < n;) {  // the ring may wrap
+      const uint32_t at = (start + (uint32_t)i) % cap;
+      const size_t run = std::min<size_t>(n - i, cap - at);
+      CK(cudaMemcpy(out + i, c->ring + at, run * 4, cudaMemcpyDeviceToHost), "ring copy");
+      i += run;
+    }
+  }
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+  c->last_seconds = ms / 1e3;
+  c->pos += (uint32_t)n;
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_decode(foxcuda_context* c, foxcuda_sampler* s, uint32_t token,
+                                         uint32_t* next) {
+  if (!c || !s || !next || s->c != c) return fail(FOXCUDA_ERR_ARG, "decode: bad argument");
+  return decode_steps(c, s, token, 1, next);
+}
+
+extern "C" foxcuda_status foxcuda_generate(foxcuda_context* c, foxcuda_sampler* s, uint32_t token,
+                                           size_t n, uint32_t* out) {
+  if (!c || !s || !out || s->c != c || n == 0) return fail(FOXCUDA_ERR_ARG, "generate: bad argument");
+  return decode_steps(c, s, token, n, out);
+}

@@ -1,0 +1,496 @@
+// Dequantise-GEMV kernels for batch-1 decode (sm_100a).
+//
+// One CTA owns one unit of U whole rows at a time (pack.cuh): thread t decodes
+// block t % nb of row t / nb, so a thread's slice of the activation vector is
+// the same for every unit and lives in registers for the whole kernel. Per
+// block the thread forms upstream's integer partial sums with __dp4a, turns
+// them into the float terms upstream forms, and parks them in shared memory;
+// one thread per row then adds the row's terms in upstream's block order, so a
+// row comes out bit-identical to upstream's CPU kernel given the same input.
+//
+//   TQ1_0/TQ2_0  per-vector int8 activations  upstream src/gemv.c:11-97,
+//                src/ternary.c:59-93,177-188,226-246
+//   Q4_K/Q6_K    per-256 int8 activations     upstream src/kernels.c:465-500,
+//                531-569,571-602,636-661,722-805
+//   Q8_0         float activations            upstream src/kernels.c:98-113
+//
+// Prologues fold upstream's per-call work into every CTA (each recomputes it
+// from the L2-resident input vector, so no extra launch or grid sync):
+//   PRO_PREQ  int8 activations and scale(s) given
+//   PRO_VEC   float vector -> upstream's quantiser
+//   PRO_NORM  residual -> RMSNorm (double sum of squares, src/ops.c:7-22) ->
+//             upstream's quantiser
+// Epilogues: store; residual add (src/ops.c:50-54); RoPE on adjacent pairs
+// (src/ops.c:56-73) + K/V cache write for the fused q|k|v matrix; SwiGLU
+// (src/ops.c:41-48) for the interleaved gate|up matrix.
+#pragma once
+
+#include "common.cuh"
+#include "pack.cuh"
+
+namespace fox {
+
+enum Pro { PRO_PREQ = 0, PRO_VEC = 1, PRO_NORM = 2 };
+enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3 };
+
+// Largest CTA per type: 64 activation registers plus a prefetched unit must
+// fit the register file at this width.
+__host__ __device__ constexpr int gemv_max_threads(int t) {
+  return (t == T_Q4_K || t == T_Q6_K) ? 256 : 512;
+}
+constexpr int XQ_STRIDE = 272;  // padded bytes per 256-block of int8 activations
+
+struct GemvParams {
+  const uint8_t* w;  // packed weights
+  int n_rows, K, nb, U;
+  const float* x;         // PRO_VEC / PRO_NORM input, K floats
+  const float* norm_w;    // PRO_NORM weight, K floats
+  float eps;
+  const int8_t* xq;       // PRO_PREQ activations, K int8
+  const float* xq_scale;  // PRO_PREQ scale(s): 1 (ternary) or K/256 (K-quants)
+  float* out;             // STORE/ADD: n_rows; SWIGLU: n_rows/2; QKV: the q rows
+  // EPI_QKV
+  int nq, nkv, hd, n_ctx, kv_f16;
+  const float* rope_cos;  // [n_ctx][hd/2]
+  const float* rope_sin;
+  const int* pos;
+  void* kcache;           // this layer: [n_kv_heads][n_ctx][hd]
+  void* vcache;
+  int row_base;           // first row of this matrix within q|k|v
+};
+
+// ---------------------------------------------------------------------------
+// per-type block decoders
+
+template <int T> struct W;
+
+// TQ1_0: 5 base-3 levels per qs byte, 4 per qh byte. The level-l trit of byte
+// c is ((c*3^l mod 256)*3) >> 8; two bytes per 32-bit register (16-bit lanes)
+// are stepped together: p = q*3, trit = p >> 8 (a byte_perm collects the four
+// trits of a word), q' = p & 0xFF. The -1 offset is folded in as -sum(x).
+template <int L>
+FOX_DEV int tq1_word(uint32_t c, const uint32_t* xw, int x0, int xs, int acc) {
+  uint32_t lo = c & 0x00FF00FFu, hi = (c >> 8) & 0x00FF00FFu;
+#pragma unroll
+  for (int l = 0; l < L; ++l) {
+    const uint32_t pl = lo * 3u, ph = hi * 3u;
+    acc = dp4a(__byte_perm(pl, ph, 0x7351), xw[x0 + l * xs], acc);
+    lo = pl & 0x00FF00FFu;
+    hi = ph & 0x00FF00FFu;
+  }
+  return acc;
+}
+
+template <> struct W<T_TQ1_0> {
+  static constexpr int NT = 1, BE = 256, MAXT = 512;
+  static constexpr bool PREFETCH = true;
+  struct R { uint4 a, b, c; uint32_t h, d; };
+  static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
+    r.a = ldg_stream16(base + t * 16);
+    r.b = ldg_stream16(base + cnt * 16 + t * 16);
+    r.c = ldg_stream16(base + cnt * 32 + t * 16);
+    r.h = ldg_stream4(base + cnt * 48 + t * 4);
+    r.d = ldg_stream2(base + cnt * 52 + t * 2);
+  }
+  // elements: l*32+m (qs[m], m<32), 160+l*16+m (qs[32+m]), 240+l*4+m (qh[m])
+  static FOX_DEV int isum(const R& r, const uint32_t* xw, int sx) {
+    const uint32_t c[12] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w,
+                            r.c.x, r.c.y, r.c.z, r.c.w};
+    int acc = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) acc = tq1_word<5>(c[w], xw, w, 8, acc);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) acc = tq1_word<5>(c[8 + w], xw, 40 + w, 4, acc);
+    acc = tq1_word<4>(r.h, xw, 60, 1, acc);
+    return acc - sx;
+  }
+  static FOX_DEV void terms(const R& r, const uint32_t* xw, int sx, float, float* out) {
+    out[0] = __fmul_rn(h2f((uint16_t)r.d), __int2float_rn(isum(r, xw, sx)));
+  }
+};
+
+// TQ2_0: element j*128 + l*32 + m is bits 2l..2l+1 of qs[j*32+m], minus 1.
+template <> struct W<T_TQ2_0> {
+  static constexpr int NT = 1, BE = 256, MAXT = 512;
+  static constexpr bool PREFETCH = true;
+  struct R { uint4 q[4]; uint32_t d; };
+  static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r.q[i] = ldg_stream16(base + cnt * 16 * i + t * 16);
+    r.d = ldg_stream2(base + cnt * 64 + t * 2);
+  }
+  static FOX_DEV int isum(const R& r, const uint32_t* xw, int sx) {
+    const uint32_t c[16] = {r.q[0].x, r.q[0].y, r.q[0].z, r.q[0].w, r.q[1].x, r.q[1].y,
+                            r.q[1].z, r.q[1].w, r.q[2].x, r.q[2].y, r.q[2].z, r.q[2].w,
+                            r.q[3].x, r.q[3].y, r.q[3].z, r.q[3].w};
+    int acc = 0;
+#pragma unroll
+    for (int w = 0; w < 16; ++w)
+#pragma unroll
+      for (int l = 0; l < 4; ++l)
+        acc = dp4a((c[w] >> (2 * l)) & 0x03030303u, xw[(w >> 3) * 32 + l * 8 + (w & 7)], acc);
+    return acc - sx;
+  }
+  static FOX_DEV void terms(const R& r, const uint32_t* xw, int sx, float, float* out) {
+    out[0] = __fmul_rn(h2f((uint16_t)r.d), __int2float_rn(isum(r, xw, sx)));
+  }
+};
+
+// Q4_K: sub-block j (32 elements) = nibble (low for even j, high for odd) of
+// qs[(j/2)*32 + l]; 6-bit scale/min packed as upstream src/kernels.c:246-255.
+// Term j = ascale * (d*sc*dot - dmin*m*sum(x)) (src/kernels.c:591-598).
+template <> struct W<T_Q4_K> {
+  static constexpr int NT = 8, BE = 256, MAXT = 256;
+  static constexpr bool PREFETCH = false;
+  struct R { uint4 q[8]; uint32_t s0, s1, s2, dm; };
+  static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r.q[i] = ldg_stream16(base + cnt * 16 * i + t * 16);
+    r.s0 = ldg_stream4(base + cnt * 128 + t * 4);
+    r.s1 = ldg_stream4(base + cnt * 132 + t * 4);
+    r.s2 = ldg_stream4(base + cnt * 136 + t * 4);
+    r.dm = ldg_stream4(base + cnt * 140 + t * 4);
+  }
+  static FOX_DEV void scale_min(const R& r, int j, int& sc, int& m) {
+    const uint32_t sw[3] = {r.s0, r.s1, r.s2};
+#define SB(i) ((int)((sw[(i) >> 2] >> (8 * ((i) & 3))) & 0xffu))
+    if (j < 4) { sc = SB(j) & 63; m = SB(j + 4) & 63; }
+    else { sc = (SB(j + 4) & 0x0F) | ((SB(j - 4) >> 6) << 4); m = (SB(j + 4) >> 4) | ((SB(j) >> 6) << 4); }
+#undef SB
+  }
+  // integer dot of sub-block j's nibbles with x, and the sum of x
+  static FOX_DEV void sub(const R& r, const uint32_t* xw, int j, int& dot, int& sum) {
+    const uint4 a = r.q[(j >> 1) * 2], b = r.q[(j >> 1) * 2 + 1];
+    const uint32_t words[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    dot = 0; sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      dot = dp4a((words[k] >> (4 * (j & 1))) & 0x0F0F0F0Fu, xw[j * 8 + k], dot);
+      sum = dp4a(0x01010101u, xw[j * 8 + k], sum);
+    }
+  }
+  static FOX_DEV void ipart(const R& r, const uint32_t* xw, int32_t* out) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sub(r, xw, j, out[2 * j], out[2 * j + 1]);
+  }
+  static FOX_DEV void terms(const R& r, const uint32_t* xw, int, float as, float* out) {
+    const float d = h2f((uint16_t)(r.dm & 0xffff)), dmin = h2f((uint16_t)(r.dm >> 16));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      int sc, m, dot, sum;
+      scale_min(r, j, sc, m);
+      sub(r, xw, j, dot, sum);
+      const float a = __fmul_rn(__fmul_rn(d, (float)sc), __int2float_rn(dot));
+      const float b = __fmul_rn(__fmul_rn(dmin, (float)m), __int2float_rn(sum));
+      out[j] = __fmul_rn(as, __fsub_rn(a, b));
+    }
+  }
+};
+
+// Q6_K: group (half, sub) = sum over k of int8 scale[half*8 + sub + 2k] times
+// the dot of the signed 6-bit values of run k with x (src/kernels.c:531-569).
+// Term = (ascale * d) * group (src/kernels.c:654-657).
+template <> struct W<T_Q6_K> {
+  static constexpr int NT = 4, BE = 256, MAXT = 256;
+  static constexpr bool PREFETCH = false;
+  struct R { uint4 ql[8]; uint4 qh[4]; uint4 sc; uint32_t d; };
+  static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r.ql[i] = ldg_stream16(base + cnt * 16 * i + t * 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r.qh[i] = ldg_stream16(base + cnt * (128 + 16 * i) + t * 16);
+    r.sc = ldg_stream16(base + cnt * 192 + t * 16);
+    r.d = ldg_stream2(base + cnt * 208 + t * 2);
+  }
+  static FOX_DEV uint32_t wd(const uint4* v, int i) {
+    return (i & 3) == 0 ? v[i >> 2].x : (i & 3) == 1 ? v[i >> 2].y : (i & 3) == 2 ? v[i >> 2].z : v[i >> 2].w;
+  }
+  static FOX_DEV int group(const R& r, const uint32_t* xw, int half, int sub) {
+    const uint32_t scw[4] = {r.sc.x, r.sc.y, r.sc.z, r.sc.w};
+    int g = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      int dot = 0, s = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t ql = wd(r.ql, half * 16 + (k & 1) * 8 + sub * 4 + i);
+        const uint32_t qh = wd(r.qh, half * 8 + sub * 4 + i);
+        const uint32_t q = ((ql >> (4 * (k >> 1))) & 0x0F0F0F0Fu) |
+                           (((qh >> (2 * k)) & 0x03030303u) << 4);
+        const uint32_t xv = xw[half * 32 + 8 * k + sub * 4 + i];
+        dot = dp4a(q, xv, dot);
+        s = dp4a(0x01010101u, xv, s);
+      }
+      const int si = half * 8 + sub + 2 * k;
+      const int scale = (int)(int8_t)((scw[si >> 2] >> (8 * (si & 3))) & 0xffu);
+      g += scale * (dot - 32 * s);
+    }
+    return g;
+  }
+  static FOX_DEV void ipart(const R& r, const uint32_t* xw, int32_t* out) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) out[g] = group(r, xw, g >> 1, g & 1);
+  }
+  static FOX_DEV void terms(const R& r, const uint32_t* xw, int, float as, float* out) {
+    const float ad = __fmul_rn(as, h2f((uint16_t)r.d));
+#pragma unroll
+    for (int g = 0; g < 4; ++g) out[g] = __fmul_rn(ad, __int2float_rn(group(r, xw, g >> 1, g & 1)));
+  }
+};
+
+// Q8_0 against float activations: acc over the 32 elements in order, then
+// d * acc (src/kernels.c:98-113). int8 -> float via byte_perm into the
+// mantissa of 2^23 and one exact subtraction.
+template <> struct W<T_Q8_0> {
+  static constexpr int NT = 1, BE = 32, MAXT = 512;
+  static constexpr bool PREFETCH = true;
+  struct R { uint4 a, b; uint32_t d; };
+  static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
+    r.a = ldg_stream16(base + t * 16);
+    r.b = ldg_stream16(base + cnt * 16 + t * 16);
+    r.d = ldg_stream2(base + cnt * 32 + t * 2);
+  }
+  static FOX_DEV void termsf(const R& r, const float* xf, float* out) {
+    const uint32_t c[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+    float acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const uint32_t v = c[w] ^ 0x80808080u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float q = __fsub_rn(__uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540 + k)), 8388736.0f);
+        acc = __fadd_rn(acc, __fmul_rn(q, xf[4 * w + k]));
+      }
+    }
+    out[0] = __fmul_rn(h2f((uint16_t)r.d), acc);
+  }
+};
+
+template <int T> constexpr bool is_ternary() { return T == T_TQ1_0 || T == T_TQ2_0; }
+template <int T> constexpr bool is_kquant() { return T == T_Q4_K || T == T_Q6_K; }
+
+// Shared memory bytes a launch needs.
+inline size_t gemv_smem_bytes(int type, int pro, int K, int U, int nb) {
+  size_t s = 0;
+  if (pro != PRO_PREQ) s += (size_t)(K + K / 8) * 4;              // staged (padded) floats
+  if (type != T_Q8_0) s += (size_t)(K / 256) * XQ_STRIDE + (K / 256) * 4;  // int8 + scales
+  s = (s + 15) / 16 * 16;
+  s += 32 * 8;                                                    // reduction scratch
+  const int nt = type == T_Q4_K ? 8 : type == T_Q6_K ? 4 : 1;
+  s += (size_t)U * (nb * nt + 1) * 4 + (size_t)U * 4;
+  return s;
+}
+
+// ---------------------------------------------------------------------------
+
+template <int T, int PRO, int EPI>
+__global__ void __launch_bounds__(W<T>::MAXT)
+gemv_kernel(const GemvParams p) {
+  using Tr = W<T>;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int tid = threadIdx.x, nth = blockDim.x;
+  const int K = p.K, nb = p.nb, U = p.U, ut = U * nb;
+  const int nb256 = K / 256;
+
+  unsigned char* sp = smem;
+  float* xs = nullptr;
+  if (PRO != PRO_PREQ) { xs = (float*)sp; sp += (size_t)(K + K / 8) * 4; }
+  int8_t* xq = nullptr;
+  float* ascale = nullptr;
+  if (T != T_Q8_0) {
+    xq = (int8_t*)sp; sp += (size_t)nb256 * XQ_STRIDE;
+    ascale = (float*)sp; sp += nb256 * 4;
+  }
+  sp = (unsigned char*)(((uintptr_t)sp + 15) & ~(uintptr_t)15);
+  double* red = (double*)sp; sp += 32 * 8;
+  // per-row term slots, row stride padded by one so the chain threads of a
+  // unit read different banks
+  const int rstride = nb * Tr::NT + 1;
+  float* part = (float*)sp; sp += (size_t)U * rstride * 4;
+  float* vals = (float*)sp;
+
+  // Q8_0 keeps floats padded by 4 every 32 so per-thread 32-float reads of
+  // different blocks fall in different banks.
+  auto xsi = [&](int i) { return T == T_Q8_0 ? i + (i >> 5) * 4 : i; };
+
+  // ---------------- prologue: the activation vector ----------------------
+  if (PRO != PRO_PREQ) {
+    double ss = 0.0;
+    for (int i = tid * 4; i < K; i += nth * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(p.x + i);
+      if (PRO == PRO_NORM)
+        ss = ss + (double)v.x * (double)v.x + (double)v.y * (double)v.y +
+             (double)v.z * (double)v.z + (double)v.w * (double)v.w;
+      *reinterpret_cast<float4*>(xs + xsi(i)) = v;
+    }
+    if (PRO == PRO_NORM) {
+      const double sum = block_reduce<double>(ss, red, OpAddD(), 0.0);
+      const float scale = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)K), (double)p.eps)));
+      for (int i = tid * 4; i < K; i += nth * 4) {
+        float4 v = *reinterpret_cast<float4*>(xs + xsi(i));
+        const float4 w = *reinterpret_cast<const float4*>(p.norm_w + i);
+        v.x = __fmul_rn(__fmul_rn(v.x, scale), w.x);
+        v.y = __fmul_rn(__fmul_rn(v.y, scale), w.y);
+        v.z = __fmul_rn(__fmul_rn(v.z, scale), w.z);
+        v.w = __fmul_rn(__fmul_rn(v.w, scale), w.w);
+        *reinterpret_cast<float4*>(xs + xsi(i)) = v;
+      }
+    }
+    __syncthreads();
+  }
+
+  float act_scale = 1.0f;
+  if (is_ternary<T>()) {
+    if (PRO == PRO_PREQ) {
+      act_scale = p.xq_scale[0];
+    } else {
+      // upstream src/gemv.c:11-42: one absmax over the whole vector
+      float am = 0.0f;
+      for (int i = tid; i < K; i += nth) am = absmax_acc(am, xs[i]);
+      const float amax = block_reduce<float>(am, (float*)red, OpMax(), 0.0f);
+      const bool nz = amax > 0.0f;
+      const float inv = nz ? __fdiv_rn(127.0f, amax) : 0.0f;
+      act_scale = nz ? __fdiv_rn(amax, 127.0f) : 0.0f;
+      for (int i = tid * 4; i < K; i += nth * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(xs + i);
+        *reinterpret_cast<uint32_t*>(xq + (i >> 8) * XQ_STRIDE + (i & 255)) =
+            pack4(quant1(v.x, inv), quant1(v.y, inv), quant1(v.z, inv), quant1(v.w, inv));
+      }
+    }
+  } else if (is_kquant<T>()) {
+    if (PRO == PRO_PREQ) {
+      for (int b = tid; b < nb256; b += nth) ascale[b] = p.xq_scale[b];
+    } else {
+      // upstream src/kernels.c:722-754: one absmax per 256 block, a warp each
+      const int lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
+      for (int b = warp; b < nb256; b += nw) {
+        float v[8], am = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { v[k] = xs[b * 256 + lane * 8 + k]; am = absmax_acc(am, v[k]); }
+        am = warp_max(am);
+        const bool nz = am > 0.0f;
+        const float inv = nz ? __fdiv_rn(127.0f, am) : 0.0f;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(xq + b * XQ_STRIDE + lane * 8);
+        dst[0] = pack4(quant1(v[0], inv), quant1(v[1], inv), quant1(v[2], inv), quant1(v[3], inv));
+        dst[1] = pack4(quant1(v[4], inv), quant1(v[5], inv), quant1(v[6], inv), quant1(v[7], inv));
+        if (lane == 0) ascale[b] = nz ? __fdiv_rn(am, 127.0f) : 0.0f;
+      }
+    }
+  }
+  if (PRO != PRO_PREQ || is_kquant<T>()) __syncthreads();
+
+  // per-thread activation slice
+  const int blk = tid < ut ? tid % nb : 0;
+  uint32_t xw[T == T_Q8_0 ? 1 : 64];
+  float xf[T == T_Q8_0 ? 32 : 1];
+  int sx = 0;
+  float as = 1.0f;
+  if (T == T_Q8_0) {
+#pragma unroll
+    for (int k = 0; k < 32; k += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(xs + xsi(blk * 32 + k));
+      xf[k] = v.x; xf[k + 1] = v.y; xf[k + 2] = v.z; xf[k + 3] = v.w;
+    }
+  } else {
+    if (PRO == PRO_PREQ) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.xq + (size_t)blk * 256);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint4 v = src[i];
+        xw[4 * i] = v.x; xw[4 * i + 1] = v.y; xw[4 * i + 2] = v.z; xw[4 * i + 3] = v.w;
+      }
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(xq + blk * XQ_STRIDE);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint4 v = src[i];
+        xw[4 * i] = v.x; xw[4 * i + 1] = v.y; xw[4 * i + 2] = v.z; xw[4 * i + 3] = v.w;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 64; ++i) sx = dp4a(0x01010101u, xw[i], sx);
+    if (is_kquant<T>()) as = ascale[blk];
+  }
+
+  // ---------------- main loop over units ---------------------------------
+  const int units = (p.n_rows + U - 1) / U;
+  const long unit_bytes = (long)ut * block_bytes(T);
+  typename Tr::R cur, nxt;
+  int u = blockIdx.x;
+  if (Tr::PREFETCH && u < units) {
+    const int ru = min(U, p.n_rows - u * U);
+    if (tid < ru * nb) Tr::load(cur, p.w + u * unit_bytes, (long)ru * nb, tid);
+  }
+  const int prow = tid / nb, pcol = (tid - prow * nb) * Tr::NT;
+  for (; u < units; u += gridDim.x) {
+    const int ru = min(U, p.n_rows - u * U);
+    if (Tr::PREFETCH) {
+      const int un = u + gridDim.x;
+      if (un < units) {
+        const int run = min(U, p.n_rows - un * U);
+        if (tid < run * nb) Tr::load(nxt, p.w + un * unit_bytes, (long)run * nb, tid);
+      }
+    } else if (tid < ru * nb) {
+      Tr::load(cur, p.w + u * unit_bytes, (long)ru * nb, tid);
+    }
+    if (tid < ru * nb) {
+      float t[Tr::NT];
+      if constexpr (T == T_Q8_0) Tr::termsf(cur, xf, t);
+      else Tr::terms(cur, xw, sx, as, t);
+#pragma unroll
+      for (int k = 0; k < Tr::NT; ++k) part[prow * rstride + pcol + k] = t[k];
+    }
+    __syncthreads();
+    float v = 0.0f;
+    if (tid < ru) {
+      // upstream order: blocks in order, terms of a block in order, from 0.0f
+      const float* pr = part + tid * rstride;
+      float acc = 0.0f;
+      for (int i = 0; i < nb * Tr::NT; ++i) acc = __fadd_rn(acc, pr[i]);
+      v = is_ternary<T>() ? __fmul_rn(acc, act_scale) : acc;
+      const int r = u * U + tid;
+      if (EPI == EPI_STORE) p.out[r] = v;
+      if (EPI == EPI_ADD) p.out[r] = __fadd_rn(p.out[r], v);
+      if (EPI == EPI_QKV || EPI == EPI_SWIGLU) vals[tid] = v;
+    }
+    if (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
+      __syncthreads();
+      if (EPI == EPI_QKV && tid < ru) {
+        const int r = p.row_base + u * U + tid;
+        const int P = *p.pos;
+        const float mine = vals[tid];
+        if (r < p.nq + p.nkv) {
+          const float other = vals[tid ^ 1];
+          const int rr = r < p.nq ? r : r - p.nq;
+          const int i = (rr % p.hd) >> 1;
+          const float c = p.rope_cos[(size_t)P * (p.hd >> 1) + i];
+          const float s = p.rope_sin[(size_t)P * (p.hd >> 1) + i];
+          const bool odd = tid & 1;
+          const float x0 = odd ? other : mine, x1 = odd ? mine : other;
+          const float o = odd ? __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c))
+                              : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+          if (r < p.nq) {
+            p.out[r] = o;
+          } else {
+            const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+            if (p.kv_f16) reinterpret_cast<__half*>(p.kcache)[idx] = __float2half_rn(o);
+            else reinterpret_cast<float*>(p.kcache)[idx] = o;
+          }
+        } else {
+          const int rr = r - p.nq - p.nkv;
+          const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+          if (p.kv_f16) reinterpret_cast<__half*>(p.vcache)[idx] = __float2half_rn(mine);
+          else reinterpret_cast<float*>(p.vcache)[idx] = mine;
+        }
+      }
+      if (EPI == EPI_SWIGLU && tid < (ru >> 1)) {
+        const float g = vals[tid], up = vals[tid + (ru >> 1)];
+        p.out[u * (U >> 1) + tid] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g))), up);
+      }
+    }
+    __syncthreads();
+    if (Tr::PREFETCH) cur = nxt;
+  }
+}
+
+}  // namespace fox

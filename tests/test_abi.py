@@ -1,0 +1,52 @@
+"""The C-ABI library loads without a GPU and exports exactly what
+include/*.h declares (no compute is called)."""
+import ctypes
+import glob
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(ROOT, "rustfox_b200", "libfoxcuda.so")
+
+
+def declared():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names |= set(re.findall(r"\b(foxcuda_\w+)\s*\(", text))
+    return names
+
+
+def test_header_declares_entry_points():
+    assert {"foxcuda_gemv", "foxcuda_eval", "foxcuda_decode", "foxcuda_model_create"} <= declared()
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    if not os.path.exists(LIB):
+        pytest.fail(f"{LIB} is missing: build it with `python -m rustfox_b200.build`")
+    lib = ctypes.CDLL(LIB)
+    missing = [n for n in sorted(declared()) if not hasattr(lib, n)]
+    assert not missing, missing
+    out = subprocess.run(["nm", "-D", "--defined-only", LIB], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT (foxcuda_\w+)", out))
+    assert declared() <= exported
+
+
+def test_errors_without_a_device_are_statuses_not_crashes():
+    """With no usable GPU the entry points report a status and a message."""
+    import rustfox_b200 as rf
+    st = rf.lib().foxcuda_init(0)
+    if st == 0:
+        pytest.skip("a GPU is present")
+    assert st in (1, 5, 7) and rf.last_error()
+    assert rf.lib().foxcuda_gemv(34, None, None, 1, 256, None, None) == 1
+
+
+def test_python_api_mirrors_upstream_names():
+    import rustfox_b200 as rf
+    for name in ("gemv", "gemv_tq1_i8", "gemv_tq2_i8", "quantize_activations_i8", "dequant_row",
+                 "Model", "Context", "Sampler"):
+        assert hasattr(rf, name)

@@ -1,0 +1,184 @@
+"""End-to-end parity of the device token loop against the CPU oracle.
+
+Upstream's own forward test (tests/test_forward.c:248-336 in the RustFox tree)
+checks finite, non-constant logits, batched == stepped, greedy == argmax and
+in-range stochastic draws on a 2-layer F32 model. Here the same properties are
+checked on the tiny TQ1_0/Q8_0 benchmark model, plus what upstream leaves
+unpinned: per-layer hidden states against the restated CPU path and 128
+greedy tokens identical to it.
+
+Two device modes:
+  parity      fp32 KV cache and attention in upstream's serial operation order.
+              Bit-identical to the oracle at every layer when the oracle uses
+              the correctly rounded exponential the device uses.
+  production  fp16 KV cache (the benchmark configuration) and split-K
+              attention. Compared with the oracle run with the same fp16 K/V
+              rounding. Upstream quantises every GEMV input to int8 with one
+              absmax scale, a discontinuous map: one flipped rounding moves a
+              layer's output by the quantisation noise (~3e-3 relative), so
+              per-layer agreement is bounded by that, not by float error.
+Against upstream's own semantics (glibc expf, fp32 KV) the greedy tokens are
+compared in both modes.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+from oracle import oracle as O  # noqa: E402
+from rustfox_b200 import synth  # noqa: E402
+import rustfox_b200 as rf  # noqa: E402
+
+from conftest import rel_l2  # noqa: E402
+
+CFG = synth.CONFIGS["tiny"]
+N_CTX = 256
+PROMPT = synth.random_prompt(CFG, 64, seed=1)
+
+
+def test_parity_mode_is_bit_identical_per_layer(gpu_tiny, oracle_tiny):
+    with O.exp_mode(True):
+        want, want_h = oracle_tiny.context(N_CTX).eval(PROMPT, want_hidden=True)
+    ctx = gpu_tiny.context(N_CTX, kv="f32", attn_exact=True)
+    ctx.set_trace(True)
+    got = ctx.eval(PROMPT)
+    for l in range(CFG.n_layer + 1):
+        h = ctx.hidden(l)
+        assert np.array_equal(h.view(np.uint32), want_h[l].view(np.uint32)), (
+            f"layer {l}: rel L2 {rel_l2(h, want_h[l]):.3g}")
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    ctx.close()
+
+
+def test_parity_mode_greedy_128(gpu_tiny, oracle_tiny):
+    with O.exp_mode(True):
+        want = O.greedy_generate(oracle_tiny, PROMPT, 128, N_CTX)
+    got = rf.greedy_generate(gpu_tiny, PROMPT, 128, N_CTX, kv="f32", attn_exact=True)
+    assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
+
+
+def test_production_mode_first_eval(gpu_tiny, oracle_tiny):
+    with O.exp_mode(True):
+        want, want_h = oracle_tiny.context(N_CTX, kv_fp16=True).eval(PROMPT, want_hidden=True)
+    ctx = gpu_tiny.context(N_CTX, kv="f16")
+    ctx.set_trace(True)
+    got = ctx.eval(PROMPT)
+    assert ctx.pos == 64
+    assert np.isfinite(got).all() and np.ptp(got) > 0
+    errs = [rel_l2(ctx.hidden(l), want_h[l]) for l in range(CFG.n_layer + 1)]
+    assert errs[0] == 0.0                       # embedding row: exact
+    assert max(errs) <= 1e-2, errs               # quantisation-noise bound
+    assert rel_l2(got, want) <= 1e-2
+    assert int(np.argmax(got)) == int(np.argmax(want))
+    ctx.close()
+
+
+@pytest.mark.parametrize("kv", ["f16", "f32"])
+def test_production_mode_greedy_128(gpu_tiny, oracle_tiny, kv):
+    with O.exp_mode(True):
+        want = O.greedy_generate(oracle_tiny, PROMPT, 128, N_CTX, kv_fp16=(kv == "f16"))
+    got = rf.greedy_generate(gpu_tiny, PROMPT, 128, N_CTX, kv=kv)
+    assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
+
+
+@pytest.mark.parametrize("mode", ["parity", "production"])
+def test_greedy_128_vs_upstream_semantics(gpu_tiny, oracle_tiny, mode):
+    """The oracle with libm expf and an fp32 cache is upstream's arithmetic
+    (checked bit for bit against the upstream library in the CPU suite)."""
+    want = O.greedy_generate(oracle_tiny, PROMPT, 128, N_CTX)
+    if mode == "parity":
+        got = rf.greedy_generate(gpu_tiny, PROMPT, 128, N_CTX, kv="f32", attn_exact=True)
+    else:
+        got = rf.greedy_generate(gpu_tiny, PROMPT, 128, N_CTX, kv="f16")
+    assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
+
+
+def test_embedding_is_bit_exact(gpu_tiny, oracle_tiny):
+    tok = np.array([1234], dtype=np.uint32)
+    _, want_h = oracle_tiny.context(8).eval(tok, want_hidden=True)
+    ctx = gpu_tiny.context(8, kv="f32")
+    ctx.set_trace(True)
+    ctx.eval(tok)
+    assert np.array_equal(ctx.hidden(0).view(np.uint32), want_h[0].view(np.uint32))
+    ctx.close()
+
+
+def test_batched_equals_stepped(gpu_tiny):
+    """upstream test_forward.c:258-272: a 5-token eval == 5 single evals."""
+    prompt = np.array([1, 4, 9, 2, 7], dtype=np.uint32)
+    ctx = gpu_tiny.context(32)
+    a = ctx.eval(prompt)
+    ctx.reset()
+    for t in prompt:
+        b = ctx.eval([t])
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    ctx.close()
+
+
+def test_decode_matches_eval_then_pick(gpu_tiny):
+    """The one-graph decode step == eval + pick + accept through the API."""
+    prompt = synth.random_prompt(CFG, 16, seed=5)
+    c1 = gpu_tiny.context(64)
+    s1 = rf.Sampler(c1, temperature=0.0)
+    c1.eval(prompt, want_logits=False)
+    for t in prompt:
+        s1.accept(int(t))
+    tok = s1.pick()
+    s1.accept(tok)
+    seq1 = [tok]
+    for _ in range(8):
+        c1.eval([seq1[-1]], want_logits=False)
+        t = s1.pick()
+        s1.accept(t)
+        seq1.append(t)
+    c2 = gpu_tiny.context(64)
+    s2 = rf.Sampler(c2, temperature=0.0)
+    c2.eval(prompt, want_logits=False)
+    for t in prompt:
+        s2.accept(int(t))
+    tok2 = s2.pick()
+    s2.accept(tok2)
+    seq2 = [tok2]
+    for _ in range(8):
+        seq2.append(s2.decode(seq2[-1]))
+    assert seq1 == seq2
+    s1.close(); s2.close(); c1.close(); c2.close()
+
+
+def test_sampler_matches_oracle_sampler(gpu_tiny):
+    """Greedy with repeat penalty and seeded top-k/top-p draws on the device
+    pick what upstream's sampler picks from the same logits."""
+    prompt = synth.random_prompt(CFG, 32, seed=9)
+    ctx = gpu_tiny.context(64)
+    logits = ctx.eval(prompt)
+    base = dict(temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.1, repeat_last_n=64,
+                seed=0)
+    with O.exp_mode(True):
+        for cfg in [dict(temperature=0.0), dict(temperature=0.8, top_k=40, top_p=0.95, seed=1),
+                    dict(temperature=1.3, top_k=0, top_p=1.0, seed=7, repeat_penalty=1.0),
+                    dict(temperature=0.5, top_k=5, top_p=0.5, seed=12345)]:
+            s = rf.Sampler(ctx, **cfg)
+            o = O.OracleSampler(CFG.n_vocab, **{**base, **cfg})
+            for t in prompt:
+                s.accept(int(t))
+                o.accept(int(t))
+            for _ in range(20):  # same logits each draw; the rng advances
+                assert s.pick() == o.pick(logits), cfg
+            s.close()
+    after = ctx.eval([1])  # penalised logits were restored after each pick
+    assert np.isfinite(after).all()
+    ctx.close()
+
+
+def test_context_overrun_and_bad_token(gpu_tiny):
+    ctx = gpu_tiny.context(4)
+    with pytest.raises(rf.FoxError) as e:
+        ctx.eval(np.arange(5, dtype=np.uint32))
+    assert e.value.status == 1
+    with pytest.raises(rf.FoxError) as e:
+        ctx.eval([CFG.n_vocab])
+    assert e.value.status == 1
+    assert ctx.pos == 0
+    ctx.close()

@@ -1,0 +1,189 @@
+"""The CPU oracle, pinned (no GPU needed).
+
+1. Known answers from upstream's own tests (RustFox tests/test_ternary.c,
+   test_gemv.c, test_kernels.c), restated against the oracle.
+2. The oracle against the upstream library compiled from its own sources
+   (oracle/_ref, where it was built): bit-exact kernels, bit-exact forward.
+3. The oracle against the committed golden fixtures (tests/golden), which were
+   produced by the upstream library (tests/golden/make_golden.py), so the
+   oracle stays pinned on machines without the upstream sources.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from rustfox_b200 import formats as F
+from rustfox_b200 import synth
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+HAVE_REF = os.path.exists(O.REF_SO)
+
+
+def u32(a):
+    return np.asarray(a, dtype=np.float32).view(np.uint32)
+
+
+# ---- 1. known answers ------------------------------------------------------
+def test_tq1_code_known_answers():
+    """upstream test_ternary.c:112-118"""
+    c = np.array([255, 253, 0], dtype=np.uint8)
+    assert all(F.tq1_decode_level(c[:1], l)[0] == 1 for l in range(5))
+    assert all(F.tq1_decode_level(c[1:2], l)[0] == 1 for l in range(4))
+    assert F.tq1_decode_level(c[2:], 0)[0] == -1 and F.tq1_decode_level(c[2:], 4)[0] == -1
+
+
+def test_tq1_encoding_round_trips_every_code():
+    for v in range(243):
+        digits = [(v // 3 ** (4 - l)) % 3 - 1 for l in range(5)]
+        code = F.TQ1_ENC5[v:v + 1]
+        assert [int(F.tq1_decode_level(code, l)[0]) for l in range(5)] == digits
+    for v in range(81):
+        digits = [(v // 3 ** (3 - l)) % 3 - 1 for l in range(4)]
+        code = F.TQ1_ENC4[v:v + 1]
+        assert [int(F.tq1_decode_level(code, l)[0]) for l in range(4)] == digits
+
+
+def test_block_encoders_round_trip_through_oracle():
+    rng = np.random.default_rng(0)
+    trits = rng.integers(-1, 2, size=(3, 256))
+    d = np.ones(3, np.float16)
+    x = rng.integers(-127, 128, size=256 * 3, dtype=np.int8)
+    for enc, tt in ((F.encode_tq1, F.TQ1_0), (F.encode_tq2, F.TQ2_0)):
+        blocks = enc(trits, d).reshape(-1)
+        sums = O.block_partials(tt, x, blocks, 1, 768)
+        want = [int(np.dot(trits[b].astype(np.int64), x[b * 256:(b + 1) * 256])) for b in range(3)]
+        assert sums.tolist() == want
+
+
+def test_ternary_all_plus_and_all_minus():
+    """upstream test_ternary.c:95-136"""
+    n, nb = 768, 3
+    x = np.ones(n, np.int8)
+    tq1 = np.zeros((nb, 54), np.uint8)
+    tq1[:, :48], tq1[:, 48:52], tq1[:, 52:54] = 255, 253, [0x00, 0x3C]
+    tq2 = np.zeros((nb, 66), np.uint8)
+    tq2[:, :64], tq2[:, 64:66] = 0xAA, [0x00, 0x3C]
+    assert O.gemv_tq_i8(F.TQ1_0, x, 1.0, tq1, 1, n)[0] == n
+    assert O.gemv_tq_i8(F.TQ2_0, x, 1.0, tq2, 1, n)[0] == n
+    tq1[:, :52] = 0
+    tq2[:, :64] = 0
+    assert O.gemv_tq_i8(F.TQ1_0, x, 1.0, tq1, 1, n)[0] == -n
+    assert O.gemv_tq_i8(F.TQ2_0, x, 1.0, tq2, 1, n)[0] == -n
+
+
+def test_quantiser_edge_cases():
+    """upstream test_gemv.c:81-94"""
+    q, s = O.quantize_i8(np.zeros(512, np.float32))
+    assert s == 0.0 and not q.any()
+    q, s = O.quantize_i8(np.arange(512, dtype=np.float32) - 200.0)
+    assert s > 0 and q[-1] == 127 and q.min() >= -127
+
+
+def test_fp16_known_values():
+    """upstream test_kernels.c:199-204"""
+    assert O.f16_to_f32(0x3C00) == 1.0 and O.f16_to_f32(0x0000) == 0.0
+    assert O.f16_to_f32(0xBC00) == -1.0 and O.f16_to_f32(0x4000) == 2.0
+    assert O.f16_to_f32(0x3800) == 0.5 and O.f16_to_f32(0x0001) > 0.0
+    every = np.arange(65536, dtype=np.uint16)
+    finite = np.isfinite(every.view(np.float16))
+    ref = every.view(np.float16).astype(np.float32)
+    got = np.array([O.f16_to_f32(int(h)) for h in every[finite][::97]], np.float32)
+    assert np.array_equal(u32(got), u32(ref[finite][::97]))
+
+
+def test_gemv_argument_rejection():
+    """upstream test_gemv.c:309-316"""
+    w = np.zeros(37 * 2 * 66, np.uint8)
+    with pytest.raises(RuntimeError):
+        O.gemv(F.TQ2_0, np.ones(255, np.float32), w, 37, 255)
+
+
+def test_one_hot_probes_pin_element_order():
+    """upstream test_kernels.c:157-265: a one-hot activation reads back one
+    dequantised element (exactly for Q8_0 float activations; for the int8
+    K-quant path the probe's 127-level activation is exact too)."""
+    rng = np.random.default_rng(7)
+    for tt in (F.Q8_0, F.Q4_K, F.Q6_K):
+        n = 256
+        row = F.random_blocks(rng, tt, 1, n, 0.02)
+        deq = O.dequant_row(tt, row, n)
+        for k in (0, 1, 31, 32, 77, 128, 200, 255):
+            x = np.zeros(n, np.float32)
+            x[k] = 1.0
+            got = O.gemv(tt, x, row, 1, n)[0]
+            assert abs(got - deq[k]) <= 1e-5 * (1 + abs(deq[k])), (tt, k, got, deq[k])
+
+
+# ---- 2. against the upstream library ----------------------------------------
+needs_ref = pytest.mark.skipif(not HAVE_REF, reason="upstream library not built here")
+
+
+@needs_ref
+@pytest.mark.parametrize("tt,rows,cols", [(F.TQ1_0, 37, 2560), (F.TQ2_0, 37, 5120),
+                                          (F.Q4_K, 29, 4096), (F.Q6_K, 29, 4096),
+                                          (F.Q8_0, 29, 2560)])
+def test_oracle_gemv_equals_upstream(tt, rows, cols):
+    ref = O.RefLib()
+    rng = np.random.default_rng(tt + rows)
+    w = F.random_blocks(rng, tt, rows, cols, 0.02)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    assert np.array_equal(u32(O.gemv(tt, x, w, rows, cols)), u32(ref.gemv(tt, x, w, rows, cols)))
+
+
+@needs_ref
+def test_oracle_quantiser_and_dequant_equal_upstream():
+    ref = O.RefLib()
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 2, 4096).astype(np.float32)
+    q1, s1 = O.quantize_i8(x)
+    q2, s2 = ref.quantize_i8(x)
+    assert np.array_equal(q1, q2) and u32(s1) == u32(s2)
+    for tt in (F.Q8_0, F.Q4_K, F.Q6_K):
+        row = F.random_blocks(rng, tt, 1, 512, 0.02)
+        assert np.array_equal(u32(O.dequant_row(tt, row, 512)), u32(ref.dequant_row(tt, row, 512)))
+
+
+@needs_ref
+def test_oracle_forward_equals_upstream_fox_eval(tiny_model, oracle_tiny, tmp_path):
+    """The restated forward pass vs upstream's fox_eval on the tiny config:
+    identical logits bit for bit, and the same greedy tokens."""
+    ref = O.RefLib()
+    path = synth.write_gguf(tiny_model, str(tmp_path / "tiny.gguf"))
+    prompt = synth.random_prompt(tiny_model.cfg, 24, seed=3)
+    toks_ref, logits_ref = ref.greedy_generate(path, prompt, 16, 64, tiny_model.cfg.n_vocab,
+                                               n_threads=4)
+    logits = oracle_tiny.context(64).eval(prompt)
+    assert np.array_equal(u32(logits), u32(logits_ref))
+    toks = O.greedy_generate(oracle_tiny, prompt, 16, 64)
+    assert np.array_equal(toks, toks_ref)
+
+
+# ---- 3. against the golden fixtures ----------------------------------------
+def _golden(name):
+    p = os.path.join(GOLDEN, name)
+    if not os.path.exists(p):
+        pytest.skip(f"{name} not generated")
+    return np.load(p)
+
+
+def test_oracle_matches_golden_kernels():
+    g = _golden("kernels.npz")
+    for tt in (F.TQ1_0, F.TQ2_0, F.Q4_K, F.Q6_K, F.Q8_0):
+        k = F.TYPE_NAMES[tt]
+        w, x, rows, cols = g[f"{k}_w"], g[f"{k}_x"], int(g[f"{k}_rows"]), int(g[f"{k}_cols"])
+        assert np.array_equal(u32(O.gemv(tt, x, w, rows, cols)), u32(g[f"{k}_out"])), k
+    q, s = O.quantize_i8(g["quant_x"])
+    assert np.array_equal(q, g["quant_q"]) and u32(s) == u32(g["quant_scale"])
+
+
+def test_oracle_matches_golden_forward(tiny_model, oracle_tiny):
+    g = _golden("tiny_forward.npz")
+    assert F.BLOCK  # the model is regenerated from its seed; check it is the same model
+    digest = np.frombuffer(tiny_model.tensors["blk.0.attn_q.weight"][2][:64].tobytes(), np.uint8)
+    assert np.array_equal(digest, g["model_digest"])
+    logits = oracle_tiny.context(64).eval(g["prompt"])
+    assert np.array_equal(u32(logits), u32(g["logits"]))
+    toks = O.greedy_generate(oracle_tiny, g["prompt"], len(g["greedy"]), 64)
+    assert np.array_equal(toks, g["greedy"])
