@@ -1,0 +1,340 @@
+#!/usr/bin/env python
+"""Batch-1 greedy decode benchmark of the token loop (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the 4B-shape Llama model with TQ1_0
+linear weights and a Q8_0 embedding/head (seeded random-init, synthetic), a
+512-id random prompt, greedy decoding (`fox run --temp 0`: repeat penalty 1.1
+over the last 64 tokens), fp16 KV cache, context 4096. A step is one decode
+token. The weights (1.18 GB) are far larger than the 126 MB L2, so every step
+streams them from HBM; no L2 flush is needed.
+
+  value  tokens/s of K decode steps run on the device with the picked token fed
+         back on the device (CUDA graphs; CUDA-event time, max over ranks)
+  e2e    tokens/s of K decode steps through the C ABI (foxcuda_decode): each
+         step copies the input token from pinned host memory and reads the
+         picked token back
+  roofline  the dominant kernel (the fused gate|up TQ1_0 GEMV), timed live
+         with CUDA events on its launching stream over successive layers
+
+With --gpus N > 1 (torchrun) each rank decodes its own replica: the decode of
+one sequence is not split across GPUs here, so scaling is weak.
+
+--impl reference times upstream RustFox's own CPU implementation (the library
+built from the upstream sources, oracle/_ref) on this host's cores for the
+same metric and config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = ("batch-1 decode tok/s and achieved HBM GB/s (% of 8 TB/s) per model, 1/2/4/8 B200")
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="4b")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def workload(cfg, args) -> dict:
+    return {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} TQ1_0 linear + Q8_0 head, "
+                        f"batch-1 greedy decode after a {args.prompt}-id prompt",
+            "prompt": args.prompt, "n_ctx": args.ctx, "kv_cache": "f16",
+            "sampler": "greedy, repeat penalty 1.1 over 64",
+            "l2": "weights 1.18 GB per step > 126 MB L2: streamed from HBM, no flush"}
+
+
+def measured_hbm_gbs():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples every 200 ms while the timed regions run."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---- CPU side: upstream's own implementation ------------------------------
+def reference_decode(model, cfg, warmup: int, steps: int, budget_s: float = 60.0):
+    """Upstream fox_eval greedy decode on this host (oracle/_ref, the upstream
+    sources built with their default -O3 and AVX2/FMA code generation), the
+    loop of `fox run --temp 0` (src/cli.c:333-361) on token ids. Returns
+    (tok/s, cores, sample description, kind)."""
+    from oracle import oracle as O
+    from rustfox_b200 import synth
+    prompt = synth.random_prompt(cfg, 16, seed=1)
+    with tempfile.TemporaryDirectory() as d:
+        path = synth.write_gguf(model, os.path.join(d, "model.gguf"), tokenizer=False)
+        if os.path.exists(O.REF_FAST_SO):
+            ref = O.RefLib(fast=True)
+            kind = "reference"
+            cores = int(ref.L.fox_cpu_count_online())
+            m = ref.open_model(path)
+            n_ctx = 16 + warmup + steps + 8
+            ctx = ref.context(m, n_ctx, 32, 0)
+            smp_cfg = O.SamplerConfig(0.0, 40, 0.95, 1.1, 64, 0)
+            smp = ref.L.fox_sampler_create(O.C.byref(smp_cfg), cfg.n_vocab)
+            logits = ref.eval(ctx, prompt, cfg.n_vocab)
+            for t in prompt:
+                ref.L.fox_sampler_accept(smp, int(t))
+
+            def pick(lg):
+                o = np.zeros(1, np.uint32)
+                lg = np.ascontiguousarray(lg, np.float32)
+                ref.L.fox_sampler_pick(smp, O._ptr(lg), O._ptr(o))
+                ref.L.fox_sampler_accept(smp, int(o[0]))
+                return int(o[0])
+
+            tok = pick(logits)
+            t_tok = None
+            for _ in range(max(1, warmup)):
+                logits = ref.eval(ctx, [tok], cfg.n_vocab)
+                t_tok = ref.L.fox_context_last_eval_seconds(ctx)
+                tok = pick(logits)
+            n = max(2, min(steps, int(budget_s / max(t_tok, 1e-6))))
+            total = 0.0
+            for _ in range(n):
+                logits = ref.eval(ctx, [tok], cfg.n_vocab)
+                total += ref.L.fox_context_last_eval_seconds(ctx)
+                tok = pick(logits)
+            ref.L.fox_sampler_destroy(smp)
+            ref.L.fox_context_destroy(ctx)
+            ref.L.fox_model_close(m)
+        else:  # the upstream sources were not available where this was built
+            kind = "port"
+            cores = os.cpu_count() or 1
+            om = O.OracleModel(model)
+            octx = om.context(16 + warmup + steps + 8)
+            octx.eval(prompt)
+            n = max(2, min(steps, 8))
+            t0 = time.perf_counter()
+            for i in range(n):
+                octx.eval([int(prompt[i % len(prompt)])])
+            total = time.perf_counter() - t0
+    sample = (f"{n} greedy decode tokens after a 16-id prompt and {max(1, warmup)} warm-up "
+              f"tokens (fox_eval time per token, as `fox run` reports gen tok/s)")
+    return n / total, cores, sample, kind
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from rustfox_b200 import synth
+    cfg = synth.CONFIGS[args.config]
+    model = synth.generate(cfg)
+    v, cores, sample, kind = reference_decode(model, cfg, args.warmup, args.steps)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "i8 x ternary -> i32, f32", "data": "synthetic (seeded random-init weights, "
+            "uniform random prompt ids)",
+            "config": {**workload(cfg, args), "kv_cache": "f32 (upstream's cache)"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- GPU side ----------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import rustfox_b200 as rf
+    from rustfox_b200 import synth
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=10))
+
+    def barrier_max(x: float) -> float:
+        torch.cuda.synchronize()
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    cfg = synth.CONFIGS[args.config]
+    host_model = synth.generate(cfg)
+    model = rf.Model.from_synthetic(host_model, device=local)
+    ctx = model.context(args.ctx, kv="f16")
+    smp = rf.Sampler(ctx, temperature=0.0)  # `fox run --temp 0` defaults otherwise
+    prompt = synth.random_prompt(cfg, args.prompt, seed=1)
+    need = args.prompt + 2 * (args.warmup + args.steps) + 2
+    if need > args.ctx:
+        raise SystemExit(f"context {args.ctx} too small for {need} positions")
+    ctx.eval(prompt, want_logits=False)
+    for t in prompt:
+        smp.accept(int(t))
+    tok = smp.pick()
+    smp.accept(tok)
+
+    clocks = Clocks(local)
+    # device-resident decode: K graph launches, token fed back on the device
+    tok = int(smp.generate(tok, max(3, args.warmup))[-1])
+    pos0 = ctx.pos
+    barrier()
+    clocks.start()
+    toks = smp.generate(tok, args.steps)
+    dev_s = barrier_max(ctx.last_eval_seconds)
+    tok = int(toks[-1])
+
+    # end to end through the C ABI: H2D token, one-graph step, D2H pick
+    for _ in range(max(3, args.warmup)):
+        tok = smp.decode(tok)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = smp.decode(tok)
+    e2e_s = barrier_max(time.perf_counter() - t0)
+    clk = clocks.stop()
+
+    # the dominant kernel, timed live on its stream over successive layers
+    kern_us, w_bytes = ctx.bench_kernel("gate_up", reps=2 * cfg.n_layer)
+    algo_bytes = w_bytes + cfg.n_embd * 4 + cfg.n_ff * 4
+    peak, peak_kind = measured_hbm_gbs()
+    achieved = algo_bytes / (kern_us * 1e-6) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("gate_up_dram_bytes_per_launch")
+
+    wb = cfg.weight_bytes()
+    mean_pos = pos0 + args.steps / 2
+    bytes_tok = wb["layers"] + wb["output"] + wb["embd_row"] + wb["norms"] + \
+        cfg.kv_bytes_per_token(int(mean_pos))
+    value = world * args.steps / dev_s
+    per_gpu = args.steps / dev_s
+    launches_per_tok = 1 + cfg.n_layer * 5 + 1 + 1 + 2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            v, cores, sample, kind = reference_decode(host_model, cfg, 2, 8, budget_s=25.0)
+            cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample}
+        except Exception as e:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
+                   "sample": f"failed: {e}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dev_s / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "i8 x ternary -> i32, f32", "data": "synthetic (seeded random-init weights, "
+            "uniform random prompt ids)",
+            "config": {**workload(cfg, args), "parallelism": f"{world} replica(s)"},
+            "hbm_bytes_per_token": bytes_tok,
+            "hbm_gbs_per_gpu": bytes_tok * per_gpu / 1e9,
+            "hbm_frac_of_8tbs": bytes_tok * per_gpu / 1e9 / NOMINAL_HBM_GBS,
+            "roofline": {"bound": "hbm", "kernel": "fused gate|up TQ1_0 GEMV (+RMSNorm, SwiGLU)",
+                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": algo_bytes,
+                         "us_per_launch": kern_us},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * args.steps / e2e_s, "unit": "tok/s",
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": launches_per_tok * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    smp.close()
+    ctx.close()
+    model.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

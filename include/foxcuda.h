@@ -191,6 +191,31 @@ foxcuda_status foxcuda_decode(foxcuda_context *c, foxcuda_sampler *s, uint32_t t
 foxcuda_status foxcuda_generate(foxcuda_context *c, foxcuda_sampler *s, uint32_t token,
                                 size_t n, uint32_t *out);
 
+/* ---- diagnostics (no upstream counterpart; upstream only times whole evals,
+ * src/forward.c:421-435) ------------------------------------------------- */
+
+/* Launch kinds of a decode step */
+enum {
+    FOXCUDA_K_EMBED = 0, FOXCUDA_K_QKV, FOXCUDA_K_ATTN, FOXCUDA_K_O, FOXCUDA_K_GATEUP,
+    FOXCUDA_K_DOWN, FOXCUDA_K_ADVANCE, FOXCUDA_K_HEAD, FOXCUDA_K_PICK
+};
+
+/* One decode step of `token` (plus a pick when s is not NULL) run launch by
+ * launch with an event after each, so every launch's device time is
+ * separated. Writes up to cap (microseconds, kind) pairs; advances the
+ * context like a decode step. */
+foxcuda_status foxcuda_context_profile(foxcuda_context *c, foxcuda_sampler *s, uint32_t token,
+                                       float *us, int *kinds, int cap, int *n_out);
+
+/* Average device time of one launch of a layer GEMV kind (QKV, O, GATEUP,
+ * DOWN or HEAD) over `reps` back-to-back launches on the context's stream,
+ * cycling through the layers so the weights stream from HBM, and the GGUF
+ * weight bytes one launch reads. Overwrites the context's activations and the
+ * cache slot at the current position: reset the context before decoding. */
+foxcuda_status foxcuda_context_bench_kernel(foxcuda_context *c, int kind, int reps,
+                                            double *us_per_launch,
+                                            uint64_t *weight_bytes_per_launch);
+
 #ifdef __cplusplus
 }
 #endif

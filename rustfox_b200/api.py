@@ -91,7 +91,13 @@ _PROTOS = {
     "foxcuda_sampler_pick": (_st, [_vp, _vp]),
     "foxcuda_decode": (_st, [_vp, _vp, C.c_uint32, _vp]),
     "foxcuda_generate": (_st, [_vp, _vp, C.c_uint32, _sz, _vp]),
+    "foxcuda_context_profile": (_st, [_vp, _vp, C.c_uint32, _vp, _vp, C.c_int,
+                                      C.POINTER(C.c_int)]),
+    "foxcuda_context_bench_kernel": (_st, [_vp, C.c_int, C.c_int, C.POINTER(C.c_double),
+                                           C.POINTER(C.c_uint64)]),
 }
+
+KIND_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "advance", "head", "pick"]
 
 _lib = None
 
@@ -337,6 +343,27 @@ class Context:
 
     def sampler(self, **kw) -> "Sampler":
         return Sampler(self, **kw)
+
+    def profile_step(self, token: int, sampler: "Sampler" = None) -> list:
+        """One decode step launch by launch: [(kind name, microseconds), ...]."""
+        cap = 8192
+        us = np.zeros(cap, np.float32)
+        kinds = np.zeros(cap, np.int32)
+        n = C.c_int()
+        _check(lib().foxcuda_context_profile(self.h, sampler.h if sampler else None, int(token),
+                                             us.ctypes.data_as(C.c_void_p),
+                                             kinds.ctypes.data_as(C.c_void_p), cap, C.byref(n)))
+        return [(KIND_NAMES[k], float(t)) for k, t in zip(kinds[:n.value], us[:n.value])]
+
+    def bench_kernel(self, kind: str, reps: int = 64):
+        """(microseconds per launch, GGUF weight bytes per launch) of a layer
+        GEMV kind ("qkv", "o", "gate_up", "down", "head"); clobbers the
+        context's activations (reset before decoding)."""
+        us = C.c_double()
+        nbytes = C.c_uint64()
+        _check(lib().foxcuda_context_bench_kernel(self.h, KIND_NAMES.index(kind), reps,
+                                                  C.byref(us), C.byref(nbytes)))
+        return us.value, nbytes.value
 
 
 class Sampler:

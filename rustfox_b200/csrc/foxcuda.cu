@@ -633,6 +633,7 @@ struct foxcuda_context {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   double last_seconds = 0.0;
   std::vector<void*> allocs;
+  std::vector<std::pair<cudaEvent_t, int>>* prof = nullptr;  // diagnostics
 };
 
 struct foxcuda_sampler {
@@ -749,79 +750,139 @@ extern "C" double foxcuda_context_last_eval_seconds(const foxcuda_context* c) {
 // One token through the layers (upstream src/forward.c:315-399): embedding,
 // then per layer the fused q|k|v (+RMSNorm, +RoPE, +KV write), attention, o
 // (+residual), gate|up (+RMSNorm, +SwiGLU), down (+residual); pos += 1.
-static cudaError_t enqueue_body(foxcuda_context* c, bool trace) {
-  foxcuda_model* m = c->m;
-  const foxcuda_model_info& mi = m->info;
-  cudaStream_t s = c->stream;
-  const int nq = mi.n_head * mi.head_dim, nkv = mi.n_head_kv * mi.head_dim;
-  const size_t elem = c->kv_f16 ? 2 : 4;
-  const size_t emb_rb = row_bytes(m->embd.type, mi.n_embd);
-  embed_kernel<<<(mi.n_embd + 255) / 256, 256, 0, s>>>(m->embd.type, m->embd.dev, emb_rb,
-                                                        (int)mi.n_embd, c->token_dev, c->x);
-  cudaError_t e = cudaGetLastError();
-  if (e) return e;
-  if (trace) cudaMemcpyAsync(c->trace, c->x, mi.n_embd * 4, cudaMemcpyDeviceToDevice, s);
-  for (uint32_t l = 0; l < mi.n_layer; ++l) {
-    const LayerW& L = m->layers[l];
-    void* kl = (uint8_t*)c->kc + (size_t)l * c->kv_layer_elems * elem;
-    void* vl = (uint8_t*)c->vc + (size_t)l * c->kv_layer_elems * elem;
-    for (int i = 0; i < L.n_qkv; ++i) {
-      const PackedMat& W = L.qkv[i];
-      GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
-      p.x = c->x; p.norm_w = L.attn_norm; p.eps = mi.rms_eps;
-      p.out = c->q; p.nq = nq; p.nkv = nkv; p.hd = mi.head_dim; p.n_ctx = c->n_ctx;
-      p.kv_f16 = c->kv_f16; p.rope_cos = c->rope_cos; p.rope_sin = c->rope_sin;
-      p.pos = c->pos_dev; p.kcache = kl; p.vcache = vl; p.row_base = L.qkv_base[i];
-      if ((e = launch_gemv(W.type, PRO_NORM, EPI_QKV, p, s))) return e;
-    }
-    AttnParams ap;
-    ap.q = c->q; ap.kcache = kl; ap.vcache = vl; ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
-    ap.hd = mi.head_dim; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
-    ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
-    ap.scale = 1.0f / sqrtf((float)mi.head_dim);
-    const dim3 ag(c->S_max, mi.n_head_kv);
-    if (c->attn_exact) {
-      const size_t sm = (size_t)c->n_ctx * 4;
-      if (sm > 48 * 1024)
-        cudaFuncSetAttribute(attention_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-      attention_exact_kernel<<<mi.n_head, 128, sm, s>>>(ap);
-    } else switch (mi.head_dim / 32) {
-      case 2: attention_kernel<2><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
-      case 4: attention_kernel<4><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
-      case 8: attention_kernel<8><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
-      default: attention_kernel<1><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
-    }
-    if ((e = cudaGetLastError())) return e;
-    {
-      GemvParams p = gemv_base(L.o.type, L.o.dev, L.o.n_rows, L.o.K, L.o.nb, L.o.U);
-      p.x = c->att; p.out = c->x;
-      if ((e = launch_gemv(L.o.type, PRO_VEC, EPI_ADD, p, s))) return e;
-    }
-    {
-      GemvParams p = gemv_base(L.gateup.type, L.gateup.dev, L.gateup.n_rows, L.gateup.K,
-                               L.gateup.nb, L.gateup.U);
-      p.x = c->x; p.norm_w = L.ffn_norm; p.eps = mi.rms_eps; p.out = c->h;
-      if ((e = launch_gemv(L.gateup.type, PRO_NORM, EPI_SWIGLU, p, s))) return e;
-    }
-    {
-      GemvParams p = gemv_base(L.down.type, L.down.dev, L.down.n_rows, L.down.K, L.down.nb, L.down.U);
-      p.x = c->h; p.out = c->x;
-      if ((e = launch_gemv(L.down.type, PRO_VEC, EPI_ADD, p, s))) return e;
-    }
-    if (trace) cudaMemcpyAsync(c->trace + (size_t)(l + 1) * mi.n_embd, c->x, mi.n_embd * 4,
-                               cudaMemcpyDeviceToDevice, s);
+// Launch kinds of a decode step (diagnostics name them by these numbers).
+enum { PK_EMBED = 0, PK_QKV, PK_ATTN, PK_O, PK_GATEUP, PK_DOWN, PK_ADVANCE, PK_HEAD, PK_PICK };
+
+// While a context is being profiled an event follows every launch.
+static void mark(foxcuda_context* c, int kind);
+
+static void* kv_layer(const foxcuda_context* c, void* base, uint32_t l) {
+  return (uint8_t*)base + (size_t)l * c->kv_layer_elems * (c->kv_f16 ? 2 : 4);
+}
+
+static size_t packed_size(const PackedMat& W) { return foxcuda_packed_bytes(W.type, W.n_rows, W.K); }
+
+// Weight bytes (GGUF bytes) of one launch of a layer kernel, 0 for others.
+static uint64_t launch_weight_bytes(const foxcuda_model* m, int kind, uint32_t l) {
+  const LayerW& L = m->layers[l];
+  switch (kind) {
+    case PK_QKV: { uint64_t b = 0; for (int i = 0; i < L.n_qkv; ++i) b += (uint64_t)L.qkv[i].n_rows * row_bytes(L.qkv[i].type, L.qkv[i].K); return b; }
+    case PK_O: return (uint64_t)L.o.n_rows * row_bytes(L.o.type, L.o.K);
+    case PK_GATEUP: return (uint64_t)L.gateup.n_rows * row_bytes(L.gateup.type, L.gateup.K);
+    case PK_DOWN: return (uint64_t)L.down.n_rows * row_bytes(L.down.type, L.down.K);
+    case PK_HEAD: return (uint64_t)m->output.n_rows * row_bytes(m->output.type, m->output.K);
+    default: return 0;
   }
-  advance_kernel<<<1, 32, 0, s>>>(c->pos_dev, 1);
+}
+
+// The fused q|k|v GEMV(s) of layer l: RMSNorm + quantise prologue, RoPE and
+// K/V cache write epilogue.
+static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
+  const foxcuda_model_info& mi = c->m->info;
+  const LayerW& L = c->m->layers[l];
+  for (int i = 0; i < L.n_qkv; ++i) {
+    const PackedMat& W = L.qkv[i];
+    GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
+    p.x = c->x; p.norm_w = L.attn_norm; p.eps = mi.rms_eps;
+    p.out = c->q; p.nq = mi.n_head * mi.head_dim; p.nkv = mi.n_head_kv * mi.head_dim;
+    p.hd = mi.head_dim; p.n_ctx = c->n_ctx; p.kv_f16 = c->kv_f16;
+    p.rope_cos = c->rope_cos; p.rope_sin = c->rope_sin; p.pos = c->pos_dev;
+    p.kcache = kv_layer(c, c->kc, l); p.vcache = kv_layer(c, c->vc, l); p.row_base = L.qkv_base[i];
+    cudaError_t e = launch_gemv(W.type, PRO_NORM, EPI_QKV, p, c->stream);
+    if (e) return e;
+  }
+  return cudaSuccess;
+}
+
+static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
+  const foxcuda_model_info& mi = c->m->info;
+  cudaStream_t s = c->stream;
+  AttnParams ap;
+  ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+  ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
+  ap.hd = mi.head_dim; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
+  ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
+  ap.scale = 1.0f / sqrtf((float)mi.head_dim);
+  const dim3 ag(c->S_max, mi.n_head_kv);
+  if (c->attn_exact) {
+    const size_t sm = (size_t)c->n_ctx * 4;
+    if (sm > 48 * 1024)
+      cudaFuncSetAttribute(attention_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    attention_exact_kernel<<<mi.n_head, 128, sm, s>>>(ap);
+  } else switch (mi.head_dim / 32) {
+    case 2: attention_kernel<2><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+    case 4: attention_kernel<4><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+    case 8: attention_kernel<8><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+    default: attention_kernel<1><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+  }
   return cudaGetLastError();
 }
 
+static cudaError_t launch_o(foxcuda_context* c, uint32_t l) {
+  const PackedMat& W = c->m->layers[l].o;
+  GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
+  p.x = c->att; p.out = c->x;
+  return launch_gemv(W.type, PRO_VEC, EPI_ADD, p, c->stream);
+}
+
+static cudaError_t launch_gateup(foxcuda_context* c, uint32_t l) {
+  const LayerW& L = c->m->layers[l];
+  const PackedMat& W = L.gateup;
+  GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
+  p.x = c->x; p.norm_w = L.ffn_norm; p.eps = c->m->info.rms_eps; p.out = c->h;
+  return launch_gemv(W.type, PRO_NORM, EPI_SWIGLU, p, c->stream);
+}
+
+static cudaError_t launch_down(foxcuda_context* c, uint32_t l) {
+  const PackedMat& W = c->m->layers[l].down;
+  GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
+  p.x = c->h; p.out = c->x;
+  return launch_gemv(W.type, PRO_VEC, EPI_ADD, p, c->stream);
+}
+
 // Output norm on the last token and the head (upstream src/forward.c:403-408).
-static cudaError_t enqueue_head(foxcuda_context* c) {
+static cudaError_t launch_head(foxcuda_context* c) {
   foxcuda_model* m = c->m;
   const PackedMat& H = m->output;
   GemvParams p = gemv_base(H.type, H.dev, H.n_rows, H.K, H.nb, H.U);
   p.x = c->x; p.norm_w = m->out_norm; p.eps = m->info.rms_eps; p.out = c->logits;
   return launch_gemv(H.type, PRO_NORM, EPI_STORE, p, c->stream);
+}
+
+static cudaError_t enqueue_body(foxcuda_context* c, bool trace) {
+  foxcuda_model* m = c->m;
+  const foxcuda_model_info& mi = m->info;
+  cudaStream_t s = c->stream;
+  const size_t emb_rb = row_bytes(m->embd.type, mi.n_embd);
+  embed_kernel<<<(mi.n_embd + 255) / 256, 256, 0, s>>>(m->embd.type, m->embd.dev, emb_rb,
+                                                        (int)mi.n_embd, c->token_dev, c->x);
+  cudaError_t e = cudaGetLastError();
+  if (e) return e;
+  mark(c, PK_EMBED);
+  if (trace) cudaMemcpyAsync(c->trace, c->x, mi.n_embd * 4, cudaMemcpyDeviceToDevice, s);
+  for (uint32_t l = 0; l < mi.n_layer; ++l) {
+    if ((e = launch_qkv(c, l))) return e;
+    mark(c, PK_QKV);
+    if ((e = launch_attn(c, l))) return e;
+    mark(c, PK_ATTN);
+    if ((e = launch_o(c, l))) return e;
+    mark(c, PK_O);
+    if ((e = launch_gateup(c, l))) return e;
+    mark(c, PK_GATEUP);
+    if ((e = launch_down(c, l))) return e;
+    mark(c, PK_DOWN);
+    if (trace) cudaMemcpyAsync(c->trace + (size_t)(l + 1) * mi.n_embd, c->x, mi.n_embd * 4,
+                               cudaMemcpyDeviceToDevice, s);
+  }
+  advance_kernel<<<1, 32, 0, s>>>(c->pos_dev, 1);
+  mark(c, PK_ADVANCE);
+  return cudaGetLastError();
+}
+
+static cudaError_t enqueue_head(foxcuda_context* c) {
+  cudaError_t e = launch_head(c);
+  mark(c, PK_HEAD);
+  return e;
 }
 
 static cudaError_t enqueue_pick(foxcuda_sampler* sm, bool accept) {
@@ -839,6 +900,7 @@ static cudaError_t enqueue_pick(foxcuda_sampler* sm, bool accept) {
                                                           accept, c->token_dev, c->ring,
                                                           (int)c->n_ctx);
   }
+  mark(c, PK_PICK);
   return cudaGetLastError();
 }
 
@@ -1038,4 +1100,87 @@ extern "C" foxcuda_status foxcuda_generate(foxcuda_context* c, foxcuda_sampler* 
                                            size_t n, uint32_t* out) {
   if (!c || !s || !out || s->c != c || n == 0) return fail(FOXCUDA_ERR_ARG, "generate: bad argument");
   return decode_steps(c, s, token, n, out);
+}
+
+// ---------------------------------------------------------------------------
+// diagnostics
+
+static void mark(foxcuda_context* c, int kind) {
+  if (!c->prof) return;
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return;
+  cudaEventRecord(e, c->stream);
+  c->prof->push_back({e, kind});
+}
+
+extern "C" foxcuda_status foxcuda_context_profile(foxcuda_context* c, foxcuda_sampler* s,
+                                                  uint32_t token, float* us, int* kinds, int cap,
+                                                  int* n_out) {
+  if (!c || !us || !kinds || !n_out || cap <= 0 || (s && s->c != c))
+    return fail(FOXCUDA_ERR_ARG, "profile: bad argument");
+  if (token >= c->m->info.n_vocab) return fail(FOXCUDA_ERR_ARG, "profile: token outside vocabulary");
+  if (c->pos + 1 > c->n_ctx) return fail(FOXCUDA_ERR_ARG, "profile: context full");
+  cudaSetDevice(c->m->device);
+  std::vector<std::pair<cudaEvent_t, int>> marks;
+  c->h_pinned[0] = token;
+  CK(cudaMemcpyAsync(c->token_dev, c->h_pinned, 4, cudaMemcpyHostToDevice, c->stream), "token in");
+  cudaEvent_t start;
+  CK(cudaEventCreate(&start), "event");
+  cudaEventRecord(start, c->stream);
+  c->prof = &marks;
+  cudaError_t e = enqueue_body(c, false);
+  if (!e) e = enqueue_head(c);
+  if (!e && s) e = enqueue_pick(s, true);
+  c->prof = nullptr;
+  cudaError_t e2 = cudaStreamSynchronize(c->stream);
+  int n = 0;
+  cudaEvent_t prev = start;
+  for (auto& mk : marks) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, prev, mk.first);
+    if (n < cap) { us[n] = ms * 1e3f; kinds[n] = mk.second; ++n; }
+    if (prev != start) cudaEventDestroy(prev);
+    prev = mk.first;
+  }
+  if (prev != start) cudaEventDestroy(prev);
+  cudaEventDestroy(start);
+  *n_out = n;
+  if (e) return cuda_fail(e, "profile");
+  CK(e2, "profile");
+  c->pos += 1;
+  if (s) s->n_out += 1;
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_context_bench_kernel(foxcuda_context* c, int kind, int reps,
+                                                       double* us_per_launch,
+                                                       uint64_t* weight_bytes_per_launch) {
+  if (!c || !us_per_launch || !weight_bytes_per_launch || reps <= 0)
+    return fail(FOXCUDA_ERR_ARG, "bench_kernel: bad argument");
+  if (!(kind == PK_QKV || kind == PK_O || kind == PK_GATEUP || kind == PK_DOWN || kind == PK_HEAD))
+    return fail(FOXCUDA_ERR_ARG, "bench_kernel: kind %d is not a weight GEMV", kind);
+  cudaSetDevice(c->m->device);
+  const uint32_t nl = c->m->info.n_layer;
+  auto one = [&](int i) -> cudaError_t {
+    const uint32_t l = (uint32_t)i % nl;  // successive layers: weights come from HBM
+    switch (kind) {
+      case PK_QKV: return launch_qkv(c, l);
+      case PK_O: return launch_o(c, l);
+      case PK_GATEUP: return launch_gateup(c, l);
+      case PK_DOWN: return launch_down(c, l);
+      default: return launch_head(c);
+    }
+  };
+  for (int i = 0; i < 3; ++i) CK(one(i), "bench_kernel warm-up");
+  CK(cudaEventRecord(c->ev0, c->stream), "event");
+  for (int i = 0; i < reps; ++i) CK(one(i), "bench_kernel");
+  CK(cudaEventRecord(c->ev1, c->stream), "event");
+  CK(cudaStreamSynchronize(c->stream), "bench_kernel");
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+  uint64_t bytes = 0;
+  for (int i = 0; i < reps; ++i) bytes += launch_weight_bytes(c->m, kind, (uint32_t)i % nl);
+  *us_per_launch = ms * 1e3 / reps;
+  *weight_bytes_per_launch = bytes / reps;
+  return FOXCUDA_OK;
 }
