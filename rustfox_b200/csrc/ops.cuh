@@ -189,25 +189,50 @@ __global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const AttnParam
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  // The partials of the other CTAs are read through L2 (ld.global.cg: L1 is
+  // not coherent with their writes). Per (split, head): max and sum to shared
+  // memory, then the rescale factors, then every output dimension as an
+  // independent, pipelined sweep over the splits.
+  __shared__ float s_m[32][ATTN_MAX_GQA], s_l[32][ATTN_MAX_GQA], s_e[32][ATTN_MAX_GQA];
+  __shared__ float s_M[ATTN_MAX_GQA], s_L[ATTN_MAX_GQA];
   const float* base = p.part + (size_t)g * p.S_max * gqa * (hd + 2);
+  for (int i = threadIdx.x; i < S * gqa; i += blockDim.x) {
+    const int t = i / gqa, h = i % gqa;
+    const float* pt = base + ((size_t)t * gqa + h) * (hd + 2);
+    s_m[t][h] = __ldcg(pt + hd);
+    s_l[t][h] = __ldcg(pt + hd + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < gqa) {
+    const int h = threadIdx.x;
+    float M = -CUDART_INF_F;
+    for (int t = 0; t < S; ++t)
+      if (s_l[t][h] > 0.0f) M = fmaxf(M, s_m[t][h]);
+    s_M[h] = M;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < S * gqa; i += blockDim.x) {
+    const int t = i / gqa, h = i % gqa;
+    s_e[t][h] = s_l[t][h] > 0.0f ? expf_cr(s_m[t][h] - s_M[h]) : 0.0f;
+  }
+  __syncthreads();
+  if (threadIdx.x < gqa) {
+    const int h = threadIdx.x;
+    float L = 0.0f;
+    for (int t = 0; t < S; ++t)
+      if (s_l[t][h] > 0.0f) L = fmaf(s_l[t][h], s_e[t][h], L);
+    s_L[h] = L;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < gqa * hd; idx += blockDim.x) {
     const int h = idx / hd, d = idx % hd;
-    float M = -CUDART_INF_F;
+    float A = 0.0f;
+#pragma unroll 8
     for (int t = 0; t < S; ++t) {
-      const volatile float* pt = base + ((size_t)t * gqa + h) * (hd + 2);
-      if (pt[hd + 1] > 0.0f) M = fmaxf(M, pt[hd]);
+      const float v = __ldcg(base + ((size_t)t * gqa + h) * (hd + 2) + d);
+      if (s_l[t][h] > 0.0f) A = fmaf(v, s_e[t][h], A);
     }
-    float A = 0.0f, L = 0.0f;
-    for (int t = 0; t < S; ++t) {
-      const volatile float* pt = base + ((size_t)t * gqa + h) * (hd + 2);
-      const float lt = pt[hd + 1];
-      if (lt > 0.0f) {
-        const float e = expf_cr(pt[hd] - M);
-        A = fmaf(pt[d], e, A);
-        L = fmaf(lt, e, L);
-      }
-    }
-    p.out[(g * gqa + h) * hd + d] = A / L;
+    p.out[(g * gqa + h) * hd + d] = A / s_L[h];
   }
   if (threadIdx.x == 0) p.counters[g] = 0u;
 }
@@ -346,12 +371,26 @@ argmax_kernel(SamplerDev* st, float* logits, int n_vocab, int restore, int accep
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  // merge the per-CTA winners in parallel, read through L2 (ld.global.cg)
+  bv = -CUDART_INF_F;
+  bi = 0xffffffffu;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+    const float v = __ldcg(st->part_val + b);
+    const uint32_t i = __ldcg(st->part_idx + b);
+    if (better(v, i, bv, bi)) { bv = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    const volatile float* pv = st->part_val;
-    const volatile uint32_t* pi = st->part_idx;
-    bv = pv[0]; bi = pi[0];
-    for (int b = 1; b < (int)gridDim.x; ++b)
-      if (better(pv[b], pi[b], bv, bi)) { bv = pv[b]; bi = pi[b]; }
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
     if (bi >= (uint32_t)n_vocab) bi = 0;  // all NaN: upstream keeps index 0
     st->counter = 0;
     st->token = bi;
