@@ -71,6 +71,26 @@ foxcuda_status foxcuda_gemv_tq2_i8(const int8_t *q, const float *act_scale,
 foxcuda_status foxcuda_gemv(int ggml_type, const float *x, const void *weights,
                             size_t n_rows, size_t n_cols, float *out, void *stream);
 
+/* No counterpart in the reference: foxcuda_gemv for callers that must not
+ * allocate device memory. Examples are a server whose memory is already
+ * reserved for its own pool, a decode loop that must not meet an
+ * out-of-memory error mid-token, and a device without stream-ordered
+ * allocation. It allocates nothing. It repacks the weights into one static
+ * device array of FOXCUDA_GEMV_NOALLOC_MAX_BYTES, part of the library's
+ * module image, then runs the same packed kernel as foxcuda_gemv, so the
+ * results are identical. A matrix whose repacked size (n_rows x row bytes)
+ * exceeds the array is rejected with FOXCUDA_ERR_ARG.
+ * - The first call on each device looks up the array's address with that
+ *   device current. Make it before any stream capture.
+ * - No part of the array has to start zeroed: each call writes every byte it
+ *   reads.
+ * - The array is shared. Calls that overlap in time (other streams, or
+ *   unordered host threads) overwrite each other's data, so callers must
+ *   order them, for instance on one stream. */
+#define FOXCUDA_GEMV_NOALLOC_MAX_BYTES (32u << 20)
+foxcuda_status foxcuda_gemv_noalloc(int ggml_type, const float *x, const void *weights,
+                                    size_t n_rows, size_t n_cols, float *out, void *stream);
+
 /* replaces fox_dequant_row (include/fox/fox.h:367-368, src/kernels.c:874-941)
  * for F32, F16, Q8_0, Q4_K and Q6_K. */
 foxcuda_status foxcuda_dequant_row(int ggml_type, const void *row, size_t n, float *out,

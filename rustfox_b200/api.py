@@ -66,6 +66,7 @@ _PROTOS = {
     "foxcuda_gemv_tq1_i8": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_tq2_i8": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
+    "foxcuda_gemv_noalloc": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_dequant_row": (_st, [C.c_int, _vp, _sz, _vp, _vp]),
     "foxcuda_block_partials": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_packed_bytes": (_sz, [C.c_int, _sz, _sz]),

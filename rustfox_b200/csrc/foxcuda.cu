@@ -244,6 +244,64 @@ extern "C" foxcuda_status foxcuda_gemv(int type, const float* x, const void* w, 
   return FOXCUDA_OK;
 }
 
+// foxcuda_gemv without any allocation: the repacked weights go to one
+// file-scope device array instead of stream-ordered scratch. It is for callers
+// that must not allocate:
+// - a server that has reserved the device's memory for its own pool, so an
+//   allocation here would either fail or take memory the pool counts on;
+// - a decode loop that must not meet an out-of-memory error or an
+//   allocator's latency halfway through a token;
+// - a device or driver configuration without stream-ordered allocation.
+// The array is part of the module image. The driver places it when the
+// module loads, so the call itself never asks for memory.
+//
+// The first call on a device looks up the array's device address once, with
+// that device current, and caches it. Make that first call before any stream
+// capture. Nothing in the array has to start at zero or survive between
+// calls: every byte the GEMV reads was written by the same call's pack
+// launch. The array is shared, so calls whose work overlaps in time (two
+// streams, or two host threads without ordering between them) overwrite each
+// other's packed weights. Callers must order their calls, for instance on one
+// stream.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FOXCUDA_GEMV_NOALLOC_MAX_BYTES];
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64];  // per device ordinal, filled by the first call
+
+extern "C" foxcuda_status foxcuda_gemv_noalloc(int type, const float* x, const void* w,
+                                               size_t n_rows, size_t n_cols, float* out,
+                                               void* stream) {
+  int nb, U;
+  foxcuda_status st = check_gemv_args(type, x, w, n_rows, n_cols, out, &nb, &U);
+  if (st) return st;
+  const size_t need = n_rows * row_bytes(type, n_cols);
+  if (need > (size_t)FOXCUDA_GEMV_NOALLOC_MAX_BYTES)
+    return fail(FOXCUDA_ERR_ARG,
+                "gemv_noalloc: the repacked %zu x %zu matrix needs %zu bytes; the static "
+                "scratch holds %zu. Use foxcuda_gemv, or foxcuda_pack + foxcuda_gemv_packed",
+                n_rows, n_cols, need, (size_t)FOXCUDA_GEMV_NOALLOC_MAX_BYTES);
+  int dev = -1;
+  CK(cudaGetDevice(&dev), "gemv_noalloc: current device");
+  if (dev < 0 || dev >= (int)(sizeof g_noalloc_addr / sizeof g_noalloc_addr[0]))
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "gemv_noalloc: device ordinal %d is beyond 63", dev);
+  void* scratch;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* p = nullptr;
+      CK(cudaGetSymbolAddress(&p, g_noalloc_scratch), "gemv_noalloc: scratch address");
+      g_noalloc_addr[dev] = p;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  CK(pack_rows(type, w, n_rows, nb, U, scratch, s), "gemv_noalloc pack launch");
+  GemvParams p = gemv_base(type, scratch, n_rows, n_cols, nb, U);
+  p.x = x;
+  p.out = out;
+  CK(launch_gemv(type, PRO_VEC, EPI_STORE, p, s), "gemv_noalloc launch");
+  return FOXCUDA_OK;
+}
+
 static foxcuda_status gemv_tq_i8(int type, const int8_t* q, const float* act_scale, const void* w,
                                  size_t n_rows, size_t n_cols, float* out, void* stream) {
   int nb, U;
