@@ -96,6 +96,17 @@ foxcuda_status foxcuda_gemv_noalloc(int ggml_type, const float *x, const void *w
 foxcuda_status foxcuda_dequant_row(int ggml_type, const void *row, size_t n, float *out,
                                    void *stream);
 
+/* replaces attention_heads (src/forward.c:222-257, src/ops.c:24-39,75-81) for
+ * one token: q [n_head*head_dim] (already roped), kcache / vcache
+ * [n_head_kv][n_ctx][head_dim] of FOXCUDA_KV_F16 or FOXCUDA_KV_F32, positions
+ * 0..pos, out [n_head*head_dim]. exact = 1 runs upstream's serial operation
+ * order (bit-exact given the same exponential); 0 runs the split-K kernel of
+ * the decode step. Device pointers; scratch is stream-ordered. */
+foxcuda_status foxcuda_attention(const float *q, const void *kcache, const void *vcache,
+                                 int kv_type, uint32_t n_head, uint32_t n_head_kv,
+                                 uint32_t head_dim, uint32_t n_ctx, uint32_t pos, int exact,
+                                 float *out, void *stream);
+
 /* Integer partial sums exactly as upstream forms them, for bit-exact checks
  * (no single upstream entry point; the sums inside src/ternary.c:158-173,
  * 253-287 and src/kernels.c:465-569):

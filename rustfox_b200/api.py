@@ -67,6 +67,8 @@ _PROTOS = {
     "foxcuda_gemv_tq2_i8": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_noalloc": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
+    "foxcuda_attention": (_st, [_vp, _vp, _vp, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32,
+                                C.c_uint32, C.c_uint32, C.c_int, _vp, _vp]),
     "foxcuda_dequant_row": (_st, [C.c_int, _vp, _sz, _vp, _vp]),
     "foxcuda_block_partials": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_packed_bytes": (_sz, [C.c_int, _sz, _sz]),

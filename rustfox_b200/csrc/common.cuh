@@ -113,4 +113,76 @@ FOX_DEV uint16_t ldg_stream2(const void* p) {
   return r;
 }
 
+// unsigned bytes of a times signed bytes of b, accumulated
+FOX_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Weight loads from global memory (read-only, streamed past L1) or, with
+// SH, plain loads from a shared-memory copy of the same bytes.
+template <bool SH> FOX_DEV uint4 ld16(const void* p) {
+  if (SH) return *reinterpret_cast<const uint4*>(p);
+  return ldg_stream16(p);
+}
+template <bool SH> FOX_DEV uint32_t ld4(const void* p) {
+  if (SH) return *reinterpret_cast<const uint32_t*>(p);
+  return ldg_stream4(p);
+}
+template <bool SH> FOX_DEV uint16_t ld2(const void* p) {
+  if (SH) return *reinterpret_cast<const uint16_t*>(p);
+  return ldg_stream2(p);
+}
+
+// mbarrier and bulk-copy helpers (PTX). A CTA copies weights from global into
+// its shared memory with cp.async.bulk; completion is counted in bytes on an
+// mbarrier, which the threads poll with a bounded wait.
+FOX_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+FOX_DEV void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+FOX_DEV void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+FOX_DEV void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// global -> this CTA's shared memory; 16-byte aligned ends, size % 16 == 0
+FOX_DEV void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+FOX_DEV bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded: gives up after about a second and reports false.
+FOX_DEV bool mbar_wait(uint64_t* bar, unsigned parity) {
+  for (int i = 0; i < (1 << 22); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i >= 8) __nanosleep(256);
+  }
+  return false;
+}
+
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start before its predecessor ends; griddep_wait blocks
+// until the predecessor has completed and its writes are visible, and
+// griddep_launch_dependents lets the successor start early. Both are no-ops
+// for kernels launched without the attribute.
+FOX_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+FOX_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace fox

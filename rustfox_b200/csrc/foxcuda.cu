@@ -14,6 +14,8 @@
 #include "gemv.cuh"
 #include "ops.cuh"
 #include "pack.cuh"
+#include "slice.cuh"
+#include "rows.cuh"
 
 using namespace fox;
 
@@ -131,6 +133,120 @@ static cudaError_t launch_gemv(int type, int pro, int epi, const GemvParams& p, 
   }
 }
 
+// Ring mode (gemv.cuh): about RING_BYTES of a CTA's units in flight.
+constexpr size_t RING_BYTES = 96 * 1024;
+
+template <int T, int PRO, int EPI>
+static cudaError_t launch_ring_t(GemvParams p, cudaStream_t s) {
+  auto kern = gemv_kernel<T, PRO, EPI, true>;
+  const int threads = (p.U * p.nb + 31) / 32 * 32;
+  const size_t unit = (size_t)p.U * p.nb * block_bytes(T);
+  if (unit % 16) return launch_gemv_t<T, PRO, EPI>(p, s);  // not bulk-copyable
+  const size_t base = (gemv_smem_bytes(T, PRO, p.K, p.U, p.nb) + 15) / 16 * 16;
+  const int R = (int)std::max<size_t>(2, std::min<size_t>(8, RING_BYTES / unit));
+  const size_t smem = base + (size_t)R * unit + (size_t)R * 8;
+  static size_t attr_set = 0;  // per instantiation
+  if (smem > attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = smem;
+  }
+  int occ = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (occ < 1) return cudaErrorInvalidConfiguration;
+  const int units = (p.n_rows + p.U - 1) / p.U;
+  const int grid = std::min(units, occ * current_sms());
+  p.ring_slots = R;
+  p.slot_bytes = (int)unit;
+  p.ring_off = (int)base;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+template <int T>
+static cudaError_t launch_ring_pe(int pro, int epi, const GemvParams& p, cudaStream_t s) {
+  if (pro == PRO_VEC && epi == EPI_STORE) return launch_ring_t<T, PRO_VEC, EPI_STORE>(p, s);
+  if (pro == PRO_VEC && epi == EPI_ADD) return launch_ring_t<T, PRO_VEC, EPI_ADD>(p, s);
+  if (pro == PRO_NORM && epi == EPI_STORE) return launch_ring_t<T, PRO_NORM, EPI_STORE>(p, s);
+  if (pro == PRO_NORM && epi == EPI_QKV) return launch_ring_t<T, PRO_NORM, EPI_QKV>(p, s);
+  if (pro == PRO_NORM && epi == EPI_SWIGLU) return launch_ring_t<T, PRO_NORM, EPI_SWIGLU>(p, s);
+  return cudaErrorInvalidValue;
+}
+
+static cudaError_t launch_ring(int type, int pro, int epi, const GemvParams& p, cudaStream_t s) {
+  switch (type) {
+    case T_TQ1_0: return launch_ring_pe<T_TQ1_0>(pro, epi, p, s);
+    case T_TQ2_0: return launch_ring_pe<T_TQ2_0>(pro, epi, p, s);
+    case T_Q4_K: return launch_ring_pe<T_Q4_K>(pro, epi, p, s);
+    case T_Q6_K: return launch_ring_pe<T_Q6_K>(pro, epi, p, s);
+    case T_Q8_0: return launch_ring_pe<T_Q8_0>(pro, epi, p, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// resident-slice GEMV launch (layer matrices of ternary types)
+
+// Smallest even unit with 16-byte aligned planes: the finest row granularity
+// the packed layout allows, so the per-CTA runs come out even.
+static int slice_unit_rows(int nb) {
+  for (int U = 2; U <= 32; U += 2)
+    if ((U * nb) % 8 == 0) return U;
+  return -1;
+}
+
+template <int T, int PRO, int EPI>
+static cudaError_t launch_slice_t(const GemvParams& p, const SliceGeom& g, int grid, cudaStream_t s) {
+  auto kern = slice_kernel<T, PRO, EPI>;
+  static bool attr_set = false;  // per instantiation
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SLICE_MAX_SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(SLICE_THREADS);
+  cfg.dynamicSmemBytes = g.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p, g);
+}
+
+template <int T>
+static cudaError_t launch_slice_pe(int pro, int epi, const GemvParams& p, const SliceGeom& g, int grid,
+                                   cudaStream_t s) {
+  if (pro == PRO_VEC && epi == EPI_ADD) return launch_slice_t<T, PRO_VEC, EPI_ADD>(p, g, grid, s);
+  if (pro == PRO_VEC && epi == EPI_STORE) return launch_slice_t<T, PRO_VEC, EPI_STORE>(p, g, grid, s);
+  if (pro == PRO_NORM && epi == EPI_QKV) return launch_slice_t<T, PRO_NORM, EPI_QKV>(p, g, grid, s);
+  if (pro == PRO_NORM && epi == EPI_SWIGLU) return launch_slice_t<T, PRO_NORM, EPI_SWIGLU>(p, g, grid, s);
+  return cudaErrorInvalidValue;
+}
+
+static cudaError_t launch_slice(int type, int pro, int epi, const GemvParams& p, const SliceGeom& g,
+                                int grid, cudaStream_t s) {
+  switch (type) {
+    case T_TQ1_0: return launch_slice_pe<T_TQ1_0>(pro, epi, p, g, grid, s);
+    case T_TQ2_0: return launch_slice_pe<T_TQ2_0>(pro, epi, p, g, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // kernel-level entry points
 
@@ -219,7 +335,7 @@ extern "C" foxcuda_status foxcuda_gemv_packed(int type, const float* x, const vo
   GemvParams p = gemv_base(type, packed, n_rows, n_cols, nb, U);
   p.x = x;
   p.out = out;
-  CK(launch_gemv(type, PRO_VEC, EPI_STORE, p, (cudaStream_t)stream), "gemv launch");
+  CK(launch_ring(type, PRO_VEC, EPI_STORE, p, (cudaStream_t)stream), "gemv launch");
   return FOXCUDA_OK;
 }
 
@@ -349,6 +465,48 @@ extern "C" foxcuda_status foxcuda_dequant_row(int type, const void* row, size_t 
   return FOXCUDA_OK;
 }
 
+static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t s);
+
+extern "C" foxcuda_status foxcuda_attention(const float* q, const void* kcache, const void* vcache,
+                                            int kv_type, uint32_t n_head, uint32_t n_head_kv,
+                                            uint32_t head_dim, uint32_t n_ctx, uint32_t pos,
+                                            int exact, float* out, void* stream) {
+  if (!q || !kcache || !vcache || !out) return fail(FOXCUDA_ERR_ARG, "attention: null pointer");
+  if (kv_type != FOXCUDA_KV_F16 && kv_type != FOXCUDA_KV_F32)
+    return fail(FOXCUDA_ERR_ARG, "attention: kv_type %d", kv_type);
+  if (!n_head || !n_head_kv || n_head % n_head_kv || n_head / n_head_kv > ATTN_MAX_GQA ||
+      head_dim % 32 || head_dim > 32 * ATTN_MAX_DPL || head_dim == 0)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "attention: %u heads / %u kv heads / head_dim %u not covered",
+                n_head, n_head_kv, head_dim);
+  if (pos >= n_ctx) return fail(FOXCUDA_ERR_ARG, "attention: position %u outside %u", pos, n_ctx);
+  if (exact && n_ctx > 16384) return fail(FOXCUDA_ERR_UNSUPPORTED, "attention: exact mode holds 16384 positions");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int S_max = std::max(1, std::min(32, 2 * current_sms() / (int)n_head_kv));
+  const int gqa = (int)(n_head / n_head_kv);
+  const size_t part_bytes = (size_t)n_head_kv * S_max * gqa * (head_dim + 2) * 4;
+  void* scratch = nullptr;
+  CK(cudaMallocAsync(&scratch, 256 + part_bytes, s), "attention scratch");
+  int* pos_dev = (int*)scratch;
+  unsigned* cnt = (unsigned*)((uint8_t*)scratch + 16);
+  cudaError_t e = cudaMemsetAsync(scratch, 0, 256, s);
+  const int p32 = (int)pos;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(pos_dev, &p32, 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // p32 lives on this stack
+  if (e == cudaSuccess) {
+    AttnParams ap;
+    ap.q = q; ap.kcache = kcache; ap.vcache = vcache; ap.kv_f16 = kv_type == FOXCUDA_KV_F16;
+    ap.n_ctx = (int)n_ctx; ap.hd = (int)head_dim; ap.n_head = (int)n_head; ap.n_kv = (int)n_head_kv;
+    ap.S_max = S_max; ap.pos = pos_dev; ap.out = out;
+    ap.part = (float*)((uint8_t*)scratch + 256); ap.counters = cnt;
+    ap.scale = 1.0f / sqrtf((float)head_dim);
+    e = run_attention(ap, exact != 0, s);
+  }
+  cudaError_t e2 = cudaFreeAsync(scratch, s);
+  if (e != cudaSuccess) return cuda_fail(e, "attention");
+  CK(e2, "attention scratch free");
+  return FOXCUDA_OK;
+}
+
 // Integer partials straight from GGUF-layout blocks, through the same block
 // decoders the GEMV kernels use (the block bytes are regrouped in registers
 // into the plane order the decoders read).
@@ -408,12 +566,21 @@ extern "C" foxcuda_status foxcuda_block_partials(int type, const int8_t* q, cons
 
 struct PackedMat {
   int type = -1;
+  int src_type = -1;  // GGUF type of the uploaded tensor (bytes are counted in it)
   int n_rows = 0, K = 0, nb = 0, U = 0;
   uint8_t* dev = nullptr;
+  // row-per-lane Q8_0 head layout (rows.cuh)
+  bool rows32 = false;
+  // resident-slice launch (ternary layer matrices whose per-CTA run fits on chip)
+  bool slice = false;
+  int pro = PRO_VEC;
+  int grid = 0;
+  SliceGeom g;
 };
 
 struct RawTensor {
   int type = -1;
+  int src_type = -1;  // the GGUF type when the device holds a transcoded copy
   uint64_t ne0 = 0, ne1 = 0;
   uint8_t* dev = nullptr;
   size_t bytes = 0;
@@ -516,9 +683,9 @@ extern "C" foxcuda_status foxcuda_model_upload(foxcuda_model* m, int role, uint3
 }
 
 static foxcuda_status pack_into(foxcuda_model* m, int type, const void* src_dev, int n_rows, int K,
-                                PackedMat* out) {
+                                PackedMat* out, int U = 0) {
   const int nb = K / block_elems(type);
-  const int U = unit_rows(type, nb);
+  if (U <= 0) U = unit_rows(type, nb);
   if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "pack: %d columns has no unit layout", K);
   void* dst = nullptr;
   CK(dev_alloc(m, (size_t)n_rows * row_bytes(type, K), &dst), "weight alloc");
@@ -544,6 +711,60 @@ static foxcuda_status norm_vec(foxcuda_model* m, const RawTensor& r, float** out
 static void free_raw(RawTensor& r) {
   if (r.dev) cudaFree(r.dev);
   r = RawTensor();
+}
+
+// TQ1_0 layer matrices are held as TQ2_0 (tq1_to_tq2_kernel): the same trits
+// and scales, 66 instead of 54 bytes per block, and a quarter of the decode
+// work per weight. FOXCUDA_KEEP_TQ1=1 keeps the GGUF bytes as they are.
+static bool keep_tq1() {
+  const char* v = getenv("FOXCUDA_KEEP_TQ1");
+  return v && v[0] == '1';
+}
+
+static foxcuda_status transcode_tq1(RawTensor& r) {
+  if (r.type != T_TQ1_0 || r.ne1 <= 1 || keep_tq1()) return FOXCUDA_OK;
+  const long nblk = (long)(r.bytes / 54);
+  void* d = nullptr;
+  CK(cudaMalloc(&d, (size_t)nblk * 66), "transcode alloc");
+  tq1_to_tq2_kernel<<<(unsigned)((nblk + 127) / 128), 128>>>(r.dev, (uint8_t*)d, nblk);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "transcode");
+  }
+  cudaFree(r.dev);
+  r.dev = (uint8_t*)d;
+  r.bytes = (size_t)nblk * 66;
+  r.type = T_TQ2_0;
+  r.src_type = T_TQ1_0;
+  return FOXCUDA_OK;
+}
+
+// The resident-slice kernel takes a ternary layer matrix when its rows split
+// into the slice unit and every CTA's run of units fits in shared memory;
+// returns that unit, or 0 for the unit kernel's layout.
+static int slice_unit_for(const foxcuda_model* m, int type, int n_rows, int K, int pro) {
+  if (type != T_TQ1_0 && type != T_TQ2_0) return 0;
+  const int nb = K / 256;
+  const int U = slice_unit_rows(nb);
+  if (U < 0 || n_rows % U || (SLICE_THREADS / 2) / nb < 1) return 0;
+  const int sms = sm_count(m->device);
+  const int units = n_rows / U;
+  const int per = (units + sms - 1) / sms;
+  const int grid = (units + per - 1) / per;
+  if (slice_geom(type, pro, n_rows, K, U, grid).smem > SLICE_MAX_SMEM) return 0;
+  return U;
+}
+
+static void set_slice(const foxcuda_model* m, PackedMat* W, int pro) {
+  const int sms = sm_count(m->device);
+  const int units = W->n_rows / W->U;
+  const int per = (units + sms - 1) / sms;
+  W->grid = (units + per - 1) / per;
+  W->g = slice_geom(W->type, pro, W->n_rows, W->K, W->U, W->grid);
+  W->pro = pro;
+  W->slice = true;
 }
 
 extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
@@ -595,6 +816,9 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
   foxcuda_status st;
   for (uint32_t l = 0; l < mi.n_layer; ++l) {
     LayerW& L = m->layers[l];
+    for (int role : {FOXCUDA_ATTN_Q, FOXCUDA_ATTN_K, FOXCUDA_ATTN_V, FOXCUDA_ATTN_OUT,
+                     FOXCUDA_FFN_GATE, FOXCUDA_FFN_UP, FOXCUDA_FFN_DOWN})
+      if ((st = transcode_tq1(m->slot(role, l)))) return st;
     if ((st = norm_vec(m, m->slot(FOXCUDA_ATTN_NORM, l), &L.attn_norm))) return st;
     if ((st = norm_vec(m, m->slot(FOXCUDA_FFN_NORM, l), &L.ffn_norm))) return st;
     // q|k|v: rows concatenated; consecutive tensors of one type share a matrix
@@ -614,7 +838,12 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
         cudaMemcpy((uint8_t*)cat + off, qkv[k]->dev, qkv[k]->bytes, cudaMemcpyDeviceToDevice);
         off += qkv[k]->bytes;
       }
-      st = pack_into(m, qkv[i]->type, cat, nrow, E, &L.qkv[L.n_qkv]);
+      int su = slice_unit_for(m, qkv[i]->type, nrow, E, PRO_NORM);
+      for (int k = i; k < j && su; ++k)
+        if (rows[k] % su) su = 0;
+      st = pack_into(m, qkv[i]->type, cat, nrow, E, &L.qkv[L.n_qkv], su);
+      L.qkv[L.n_qkv].src_type = qkv[i]->src_type;
+      if (!st && su) set_slice(m, &L.qkv[L.n_qkv], PRO_NORM);
       cudaDeviceSynchronize();
       cudaFree(cat);
       if (st) return st;
@@ -626,7 +855,13 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
       L.n_qkv++;
       i = j;
     }
-    if ((st = pack_into(m, m->slot(FOXCUDA_ATTN_OUT, l).type, m->slot(FOXCUDA_ATTN_OUT, l).dev, E, nq, &L.o))) return st;
+    {
+      const RawTensor& o = m->slot(FOXCUDA_ATTN_OUT, l);
+      const int su = slice_unit_for(m, o.type, E, nq, PRO_VEC);
+      if ((st = pack_into(m, o.type, o.dev, E, nq, &L.o, su))) return st;
+      L.o.src_type = o.src_type;
+      if (su) set_slice(m, &L.o, PRO_VEC);
+    }
     // gate|up interleaved per unit: U/2 gate rows then the same U/2 up rows
     const RawTensor& g = m->slot(FOXCUDA_FFN_GATE, l);
     const RawTensor& u = m->slot(FOXCUDA_FFN_UP, l);
@@ -634,24 +869,46 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
       return fail(FOXCUDA_ERR_UNSUPPORTED, "model: ffn_gate and ffn_up types differ in layer %u", l);
     {
       const int nb = E / block_elems(g.type);
-      const int U = unit_rows(g.type, nb);
+      const int su = slice_unit_for(m, g.type, 2 * Fd, E, PRO_NORM);
+      const int U = su ? su : unit_rows(g.type, nb);
       if (U < 0 || Fd % (U / 2)) return fail(FOXCUDA_ERR_UNSUPPORTED, "model: ffn width %d vs unit %d", Fd, U);
       const size_t rb = row_bytes(g.type, E), half = (size_t)(U / 2) * rb;
       void* cat = nullptr;
       CK(cudaMalloc(&cat, g.bytes + u.bytes), "staging alloc");
       CK(cudaMemcpy2D(cat, 2 * half, g.dev, half, half, Fd / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
       CK(cudaMemcpy2D((uint8_t*)cat + half, 2 * half, u.dev, half, half, Fd / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
-      st = pack_into(m, g.type, cat, 2 * Fd, E, &L.gateup);
+      st = pack_into(m, g.type, cat, 2 * Fd, E, &L.gateup, U);
+      L.gateup.src_type = g.src_type;
+      if (!st && su) set_slice(m, &L.gateup, PRO_NORM);
       cudaDeviceSynchronize();
       cudaFree(cat);
       if (st) return st;
     }
-    if ((st = pack_into(m, m->slot(FOXCUDA_FFN_DOWN, l).type, m->slot(FOXCUDA_FFN_DOWN, l).dev, E, Fd, &L.down))) return st;
+    {
+      const RawTensor& d = m->slot(FOXCUDA_FFN_DOWN, l);
+      const int su = slice_unit_for(m, d.type, E, Fd, PRO_VEC);
+      if ((st = pack_into(m, d.type, d.dev, E, Fd, &L.down, su))) return st;
+      L.down.src_type = d.src_type;
+      if (su) set_slice(m, &L.down, PRO_VEC);
+    }
     CK(cudaDeviceSynchronize(), "finalize layer");
     for (int role = FOXCUDA_ATTN_NORM; role < FOXCUDA_N_ROLES; ++role) free_raw(m->slot(role, l));
   }
   if ((st = norm_vec(m, m->slot(FOXCUDA_OUTPUT_NORM, 0), &m->out_norm))) return st;
-  if ((st = pack_into(m, head.type, head.dev, mi.n_vocab, E, &m->output))) return st;
+  if (head.type == T_Q8_0 && mi.n_vocab % 32 == 0) {
+    // the row-per-lane layout of q8_rows_kernel
+    PackedMat& H = m->output;
+    void* dst = nullptr;
+    CK(dev_alloc(m, (size_t)mi.n_vocab * row_bytes(T_Q8_0, E), &dst), "head alloc");
+    const long total = (long)mi.n_vocab * (E / 32);
+    pack_q8_rows32_kernel<<<(unsigned)std::min<long>((total + 255) / 256, 8192), 256>>>(
+        head.dev, (int)mi.n_vocab, E / 32, (uint8_t*)dst);
+    CK(cudaGetLastError(), "head pack");
+    H.type = T_Q8_0; H.n_rows = (int)mi.n_vocab; H.K = E; H.nb = E / 32; H.U = 32;
+    H.dev = (uint8_t*)dst; H.rows32 = true;
+  } else if ((st = pack_into(m, head.type, head.dev, mi.n_vocab, E, &m->output))) {
+    return st;
+  }
   CK(cudaDeviceSynchronize(), "finalize head");
   m->embd = emb;
   m->device_bytes += emb.bytes;
@@ -676,7 +933,8 @@ struct foxcuda_context {
   void *kc = nullptr, *vc = nullptr;
   size_t kv_layer_elems = 0;
   int* pos_dev = nullptr;
-  uint32_t* token_dev = nullptr;
+  uint32_t* token_dev = nullptr;  // [0] the current token, [1] device error code
+  int* err_dev = nullptr;
   uint32_t* tokens_dev = nullptr;  // prompt staging
   size_t tokens_cap = 0;
   float* attn_part = nullptr;
@@ -764,6 +1022,10 @@ extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda
   A((size_t)mi.n_head_kv * c->S_max * gqa * (mi.head_dim + 2) * 4, (void**)&c->attn_part);
   A((size_t)mi.n_head_kv * 4, (void**)&c->attn_cnt);
   A((size_t)c->n_ctx * 4, (void**)&c->ring);
+  if (e == cudaSuccess) {
+    c->err_dev = reinterpret_cast<int*>(c->token_dev + 1);
+    e = cudaMemset(c->token_dev, 0, 16);
+  }
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMallocHost((void**)&c->h_pinned, 64);
   if (e == cudaSuccess) e = cudaEventCreate(&c->ev0);
@@ -821,16 +1083,27 @@ static void* kv_layer(const foxcuda_context* c, void* base, uint32_t l) {
 static size_t packed_size(const PackedMat& W) { return foxcuda_packed_bytes(W.type, W.n_rows, W.K); }
 
 // Weight bytes (GGUF bytes) of one launch of a layer kernel, 0 for others.
+static uint64_t gguf_bytes(const PackedMat& W) {
+  return (uint64_t)W.n_rows * row_bytes(W.src_type >= 0 ? W.src_type : W.type, W.K);
+}
+
 static uint64_t launch_weight_bytes(const foxcuda_model* m, int kind, uint32_t l) {
   const LayerW& L = m->layers[l];
   switch (kind) {
-    case PK_QKV: { uint64_t b = 0; for (int i = 0; i < L.n_qkv; ++i) b += (uint64_t)L.qkv[i].n_rows * row_bytes(L.qkv[i].type, L.qkv[i].K); return b; }
-    case PK_O: return (uint64_t)L.o.n_rows * row_bytes(L.o.type, L.o.K);
-    case PK_GATEUP: return (uint64_t)L.gateup.n_rows * row_bytes(L.gateup.type, L.gateup.K);
-    case PK_DOWN: return (uint64_t)L.down.n_rows * row_bytes(L.down.type, L.down.K);
-    case PK_HEAD: return (uint64_t)m->output.n_rows * row_bytes(m->output.type, m->output.K);
+    case PK_QKV: { uint64_t b = 0; for (int i = 0; i < L.n_qkv; ++i) b += gguf_bytes(L.qkv[i]); return b; }
+    case PK_O: return gguf_bytes(L.o);
+    case PK_GATEUP: return gguf_bytes(L.gateup);
+    case PK_DOWN: return gguf_bytes(L.down);
+    case PK_HEAD: return gguf_bytes(m->output);
     default: return 0;
   }
+}
+
+// A layer GEMV through the kernel its layout was packed for.
+static cudaError_t launch_mat(foxcuda_context* c, const PackedMat& W, int pro, int epi, GemvParams& p) {
+  p.err = c->err_dev;
+  if (W.slice) return launch_slice(W.type, pro, epi, p, W.g, W.grid, c->stream);
+  return launch_ring(W.type, pro, epi, p, c->stream);
 }
 
 // The fused q|k|v GEMV(s) of layer l: RMSNorm + quantise prologue, RoPE and
@@ -846,28 +1119,70 @@ static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
     p.hd = mi.head_dim; p.n_ctx = c->n_ctx; p.kv_f16 = c->kv_f16;
     p.rope_cos = c->rope_cos; p.rope_sin = c->rope_sin; p.pos = c->pos_dev;
     p.kcache = kv_layer(c, c->kc, l); p.vcache = kv_layer(c, c->vc, l); p.row_base = L.qkv_base[i];
-    cudaError_t e = launch_gemv(W.type, PRO_NORM, EPI_QKV, p, c->stream);
+    cudaError_t e = launch_mat(c, W, PRO_NORM, EPI_QKV, p);
     if (e) return e;
   }
   return cudaSuccess;
 }
 
-static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
-  const foxcuda_model_info& mi = c->m->info;
-  cudaStream_t s = c->stream;
-  AttnParams ap;
-  ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
-  ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
-  ap.hd = mi.head_dim; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
-  ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
-  ap.scale = 1.0f / sqrtf((float)mi.head_dim);
-  const dim3 ag(c->S_max, mi.n_head_kv);
-  if (c->attn_exact) {
-    const size_t sm = (size_t)c->n_ctx * 4;
-    if (sm > 48 * 1024)
-      cudaFuncSetAttribute(attention_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    attention_exact_kernel<<<mi.n_head, 128, sm, s>>>(ap);
-  } else switch (mi.head_dim / 32) {
+template <int HD, int G, bool F16>
+static cudaError_t launch_attn_tile_g(const AttnParams& ap, dim3 grid, cudaStream_t s) {
+  (void)grid;
+  constexpr size_t sm = attn_tile_smem<HD, F16>();
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel<HD, G, F16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  // one cluster of ATTN_SPLITS CTAs per KV head
+  attention_cluster_kernel<HD, G, F16><<<dim3(ATTN_SPLITS, ap.n_kv), 128, sm, s>>>(ap);
+  return cudaGetLastError();
+}
+
+static bool tile_group_ok(int g) { return g == 1 || g == 2 || g == 4 || g == 8; }
+
+// the tiled kernel for this group size (query heads per KV head)
+template <int HD, bool F16>
+static cudaError_t launch_attn_tile(const AttnParams& ap, dim3 grid, cudaStream_t s) {
+  switch (ap.n_head / ap.n_kv) {
+    case 1: return launch_attn_tile_g<HD, 1, F16>(ap, grid, s);
+    case 2: return launch_attn_tile_g<HD, 2, F16>(ap, grid, s);
+    case 4: return launch_attn_tile_g<HD, 4, F16>(ap, grid, s);
+    case 8: return launch_attn_tile_g<HD, 8, F16>(ap, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// One decode attention over a K/V cache: the serial upstream-order kernel,
+// or the split-K kernels (the tiled one for head_dim 64 and 128).
+static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t s) {
+  const dim3 ag(ap.S_max, ap.n_kv);
+  if (exact) {
+    const size_t sm = (size_t)ap.n_ctx * 4;
+    if (sm > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(attention_exact_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      if (e != cudaSuccess) return e;
+    }
+    attention_exact_kernel<<<ap.n_head, 128, sm, s>>>(ap);
+  } else if (!tile_group_ok(ap.n_head / ap.n_kv)) {
+    switch (ap.hd / 32) {
+      case 2: attention_kernel<2><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+      case 4: attention_kernel<4><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+      case 8: attention_kernel<8><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+      default: attention_kernel<1><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
+    }
+  } else if (ap.hd == 128 && ap.kv_f16) {
+    return launch_attn_tile<128, true>(ap, ag, s);
+  } else if (ap.hd == 128) {
+    return launch_attn_tile<128, false>(ap, ag, s);
+  } else if (ap.hd == 64 && ap.kv_f16) {
+    return launch_attn_tile<64, true>(ap, ag, s);
+  } else if (ap.hd == 64) {
+    return launch_attn_tile<64, false>(ap, ag, s);
+  } else switch (ap.hd / 32) {
     case 2: attention_kernel<2><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
     case 4: attention_kernel<4><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
     case 8: attention_kernel<8><<<ag, ATTN_THREADS, 0, s>>>(ap); break;
@@ -876,11 +1191,22 @@ static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
   return cudaGetLastError();
 }
 
+static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
+  const foxcuda_model_info& mi = c->m->info;
+  AttnParams ap;
+  ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+  ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
+  ap.hd = mi.head_dim; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
+  ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
+  ap.scale = 1.0f / sqrtf((float)mi.head_dim);
+  return run_attention(ap, c->attn_exact, c->stream);
+}
+
 static cudaError_t launch_o(foxcuda_context* c, uint32_t l) {
   const PackedMat& W = c->m->layers[l].o;
   GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
   p.x = c->att; p.out = c->x;
-  return launch_gemv(W.type, PRO_VEC, EPI_ADD, p, c->stream);
+  return launch_mat(c, W, PRO_VEC, EPI_ADD, p);
 }
 
 static cudaError_t launch_gateup(foxcuda_context* c, uint32_t l) {
@@ -888,14 +1214,39 @@ static cudaError_t launch_gateup(foxcuda_context* c, uint32_t l) {
   const PackedMat& W = L.gateup;
   GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
   p.x = c->x; p.norm_w = L.ffn_norm; p.eps = c->m->info.rms_eps; p.out = c->h;
-  return launch_gemv(W.type, PRO_NORM, EPI_SWIGLU, p, c->stream);
+  return launch_mat(c, W, PRO_NORM, EPI_SWIGLU, p);
 }
 
 static cudaError_t launch_down(foxcuda_context* c, uint32_t l) {
   const PackedMat& W = c->m->layers[l].down;
   GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
   p.x = c->h; p.out = c->x;
-  return launch_gemv(W.type, PRO_VEC, EPI_ADD, p, c->stream);
+  return launch_mat(c, W, PRO_VEC, EPI_ADD, p);
+}
+
+static cudaError_t launch_q8_rows(const GemvParams& p, cudaStream_t s) {
+  auto kern = q8_rows_kernel<PRO_NORM>;
+  const size_t smem = (size_t)p.K * 4 + 32 * 8;
+  static size_t attr_set = 0;
+  if (smem > 48 * 1024 && smem > attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set = smem;
+  }
+  const int pairs = (p.n_rows / 32 + 1) / 2;
+  const int warps = ROWS_THREADS / 32;
+  const int grid = std::max(1, std::min((pairs + warps - 1) / warps, 4 * current_sms()));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(ROWS_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 // Output norm on the last token and the head (upstream src/forward.c:403-408).
@@ -904,7 +1255,9 @@ static cudaError_t launch_head(foxcuda_context* c) {
   const PackedMat& H = m->output;
   GemvParams p = gemv_base(H.type, H.dev, H.n_rows, H.K, H.nb, H.U);
   p.x = c->x; p.norm_w = m->out_norm; p.eps = m->info.rms_eps; p.out = c->logits;
-  return launch_gemv(H.type, PRO_NORM, EPI_STORE, p, c->stream);
+  p.err = c->err_dev;
+  if (H.rows32) return launch_q8_rows(p, c->stream);
+  return launch_ring(H.type, PRO_NORM, EPI_STORE, p, c->stream);
 }
 
 static cudaError_t enqueue_body(foxcuda_context* c, bool trace) {
@@ -999,6 +1352,23 @@ extern "C" foxcuda_status foxcuda_context_hidden(const foxcuda_context* c, uint3
   return FOXCUDA_OK;
 }
 
+// A bounded device wait that gave up leaves a nonzero code in err_dev. The
+// code is copied to h_pinned[3] before each synchronising call returns and
+// reported here; the flag is cleared for the next step.
+static void enqueue_err_read(foxcuda_context* c) {
+  cudaMemcpyAsync(c->h_pinned + 3, c->err_dev, 4, cudaMemcpyDeviceToHost, c->stream);
+}
+
+static foxcuda_status check_err(foxcuda_context* c) {
+  const uint32_t code = c->h_pinned[3];
+  if (!code) return FOXCUDA_OK;
+  c->h_pinned[3] = 0;
+  cudaMemsetAsync(c->err_dev, 0, 4, c->stream);
+  cudaStreamSynchronize(c->stream);
+  return fail(FOXCUDA_ERR_INTERNAL, "device: a bounded wait for weights to reach shared memory "
+              "gave up (code %u); the step's outputs are not valid", code);
+}
+
 extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* tokens, size_t n,
                                        float* logits_out) {
   if (!c || !tokens || n == 0) return fail(FOXCUDA_ERR_ARG, "eval: nothing to evaluate");
@@ -1034,12 +1404,13 @@ extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* token
   if (logits_out)
     CK(cudaMemcpyAsync(logits_out, c->logits, (size_t)mi.n_vocab * 4, cudaMemcpyDeviceToHost, c->stream),
        "logits copy");
+  enqueue_err_read(c);
   CK(cudaStreamSynchronize(c->stream), "eval");
   float ms = 0.0f;
   cudaEventElapsedTime(&ms, c->ev0, c->ev1);
   c->last_seconds = ms / 1e3;
   c->pos += (uint32_t)n;
-  return FOXCUDA_OK;
+  return check_err(c);
 }
 
 // ---------------------------------------------------------------------------
@@ -1128,10 +1499,13 @@ static foxcuda_status decode_steps(foxcuda_context* c, foxcuda_sampler* s, uint3
   CK(cudaEventRecord(c->ev1, c->stream), "event");
   s->n_out += (uint32_t)n;
   if (n == 1) {
-    CK(cudaMemcpyAsync(c->h_pinned + 1, c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream), "token out");
+    // the picked token and the device error code in one 8-byte copy
+    CK(cudaMemcpyAsync(c->h_pinned + 1, c->token_dev, 8, cudaMemcpyDeviceToHost, c->stream), "token out");
     CK(cudaStreamSynchronize(c->stream), "decode");
     out[0] = c->h_pinned[1];
+    c->h_pinned[3] = c->h_pinned[2];
   } else {
+    enqueue_err_read(c);
     CK(cudaStreamSynchronize(c->stream), "generate");
     const uint32_t cap = c->n_ctx;
     for (size_t i = 0; i < n;) {  // the ring may wrap
@@ -1145,7 +1519,7 @@ static foxcuda_status decode_steps(foxcuda_context* c, foxcuda_sampler* s, uint3
   cudaEventElapsedTime(&ms, c->ev0, c->ev1);
   c->last_seconds = ms / 1e3;
   c->pos += (uint32_t)n;
-  return FOXCUDA_OK;
+  return check_err(c);
 }
 
 extern "C" foxcuda_status foxcuda_decode(foxcuda_context* c, foxcuda_sampler* s, uint32_t token,
@@ -1190,6 +1564,7 @@ extern "C" foxcuda_status foxcuda_context_profile(foxcuda_context* c, foxcuda_sa
   if (!e) e = enqueue_head(c);
   if (!e && s) e = enqueue_pick(s, true);
   c->prof = nullptr;
+  enqueue_err_read(c);
   cudaError_t e2 = cudaStreamSynchronize(c->stream);
   int n = 0;
   cudaEvent_t prev = start;
@@ -1207,7 +1582,7 @@ extern "C" foxcuda_status foxcuda_context_profile(foxcuda_context* c, foxcuda_sa
   CK(e2, "profile");
   c->pos += 1;
   if (s) s->n_out += 1;
-  return FOXCUDA_OK;
+  return check_err(c);
 }
 
 extern "C" foxcuda_status foxcuda_context_bench_kernel(foxcuda_context* c, int kind, int reps,
@@ -1233,6 +1608,7 @@ extern "C" foxcuda_status foxcuda_context_bench_kernel(foxcuda_context* c, int k
   CK(cudaEventRecord(c->ev0, c->stream), "event");
   for (int i = 0; i < reps; ++i) CK(one(i), "bench_kernel");
   CK(cudaEventRecord(c->ev1, c->stream), "event");
+  enqueue_err_read(c);
   CK(cudaStreamSynchronize(c->stream), "bench_kernel");
   float ms = 0.0f;
   cudaEventElapsedTime(&ms, c->ev0, c->ev1);
@@ -1240,5 +1616,5 @@ extern "C" foxcuda_status foxcuda_context_bench_kernel(foxcuda_context* c, int k
   for (int i = 0; i < reps; ++i) bytes += launch_weight_bytes(c->m, kind, (uint32_t)i % nl);
   *us_per_launch = ms * 1e3 / reps;
   *weight_bytes_per_launch = bytes / reps;
-  return FOXCUDA_OK;
+  return check_err(c);
 }

@@ -57,6 +57,10 @@ struct GemvParams {
   void* kcache;           // this layer: [n_kv_heads][n_ctx][hd]
   void* vcache;
   int row_base;           // first row of this matrix within q|k|v
+  int* err;               // set to a nonzero code when a bounded device wait gives up
+  // ring mode: units stream through ring_slots shared-memory slots of
+  // slot_bytes each, starting ring_off bytes into dynamic shared memory
+  int ring_slots, slot_bytes, ring_off;
 };
 
 // ---------------------------------------------------------------------------
@@ -85,12 +89,13 @@ template <> struct W<T_TQ1_0> {
   static constexpr int NT = 1, BE = 256, MAXT = 512;
   static constexpr bool PREFETCH = true;
   struct R { uint4 a, b, c; uint32_t h, d; };
+  template <bool SH = false>
   static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
-    r.a = ldg_stream16(base + t * 16);
-    r.b = ldg_stream16(base + cnt * 16 + t * 16);
-    r.c = ldg_stream16(base + cnt * 32 + t * 16);
-    r.h = ldg_stream4(base + cnt * 48 + t * 4);
-    r.d = ldg_stream2(base + cnt * 52 + t * 2);
+    r.a = ld16<SH>(base + t * 16);
+    r.b = ld16<SH>(base + cnt * 16 + t * 16);
+    r.c = ld16<SH>(base + cnt * 32 + t * 16);
+    r.h = ld4<SH>(base + cnt * 48 + t * 4);
+    r.d = ld2<SH>(base + cnt * 52 + t * 2);
   }
   // elements: l*32+m (qs[m], m<32), 160+l*16+m (qs[32+m]), 240+l*4+m (qh[m])
   static FOX_DEV int isum(const R& r, const uint32_t* xw, int sx) {
@@ -114,22 +119,24 @@ template <> struct W<T_TQ2_0> {
   static constexpr int NT = 1, BE = 256, MAXT = 512;
   static constexpr bool PREFETCH = true;
   struct R { uint4 q[4]; uint32_t d; };
+  template <bool SH = false>
   static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) r.q[i] = ldg_stream16(base + cnt * 16 * i + t * 16);
-    r.d = ldg_stream2(base + cnt * 64 + t * 2);
+    for (int i = 0; i < 4; ++i) r.q[i] = ld16<SH>(base + cnt * 16 * i + t * 16);
+    r.d = ld2<SH>(base + cnt * 64 + t * 2);
   }
   static FOX_DEV int isum(const R& r, const uint32_t* xw, int sx) {
     const uint32_t c[16] = {r.q[0].x, r.q[0].y, r.q[0].z, r.q[0].w, r.q[1].x, r.q[1].y,
                             r.q[1].z, r.q[1].w, r.q[2].x, r.q[2].y, r.q[2].z, r.q[2].w,
                             r.q[3].x, r.q[3].y, r.q[3].z, r.q[3].w};
-    int acc = 0;
+    // per level: mask in place (codes times 4^l), sum apart, shift back exactly
+    int acc[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int w = 0; w < 16; ++w)
 #pragma unroll
       for (int l = 0; l < 4; ++l)
-        acc = dp4a((c[w] >> (2 * l)) & 0x03030303u, xw[(w >> 3) * 32 + l * 8 + (w & 7)], acc);
-    return acc - sx;
+        acc[l] = dp4a_us(c[w] & (0x03030303u << (2 * l)), xw[(w >> 3) * 32 + l * 8 + (w & 7)], acc[l]);
+    return acc[0] + (acc[1] >> 2) + (acc[2] >> 4) + (acc[3] >> 6) - sx;
   }
   static FOX_DEV void terms(const R& r, const uint32_t* xw, int sx, float, float* out) {
     out[0] = __fmul_rn(h2f((uint16_t)r.d), __int2float_rn(isum(r, xw, sx)));
@@ -143,13 +150,14 @@ template <> struct W<T_Q4_K> {
   static constexpr int NT = 8, BE = 256, MAXT = 256;
   static constexpr bool PREFETCH = false;
   struct R { uint4 q[8]; uint32_t s0, s1, s2, dm; };
+  template <bool SH = false>
   static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) r.q[i] = ldg_stream16(base + cnt * 16 * i + t * 16);
-    r.s0 = ldg_stream4(base + cnt * 128 + t * 4);
-    r.s1 = ldg_stream4(base + cnt * 132 + t * 4);
-    r.s2 = ldg_stream4(base + cnt * 136 + t * 4);
-    r.dm = ldg_stream4(base + cnt * 140 + t * 4);
+    for (int i = 0; i < 8; ++i) r.q[i] = ld16<SH>(base + cnt * 16 * i + t * 16);
+    r.s0 = ld4<SH>(base + cnt * 128 + t * 4);
+    r.s1 = ld4<SH>(base + cnt * 132 + t * 4);
+    r.s2 = ld4<SH>(base + cnt * 136 + t * 4);
+    r.dm = ld4<SH>(base + cnt * 140 + t * 4);
   }
   static FOX_DEV void scale_min(const R& r, int j, int& sc, int& m) {
     const uint32_t sw[3] = {r.s0, r.s1, r.s2};
@@ -194,13 +202,14 @@ template <> struct W<T_Q6_K> {
   static constexpr int NT = 4, BE = 256, MAXT = 256;
   static constexpr bool PREFETCH = false;
   struct R { uint4 ql[8]; uint4 qh[4]; uint4 sc; uint32_t d; };
+  template <bool SH = false>
   static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) r.ql[i] = ldg_stream16(base + cnt * 16 * i + t * 16);
+    for (int i = 0; i < 8; ++i) r.ql[i] = ld16<SH>(base + cnt * 16 * i + t * 16);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) r.qh[i] = ldg_stream16(base + cnt * (128 + 16 * i) + t * 16);
-    r.sc = ldg_stream16(base + cnt * 192 + t * 16);
-    r.d = ldg_stream2(base + cnt * 208 + t * 2);
+    for (int i = 0; i < 4; ++i) r.qh[i] = ld16<SH>(base + cnt * (128 + 16 * i) + t * 16);
+    r.sc = ld16<SH>(base + cnt * 192 + t * 16);
+    r.d = ld2<SH>(base + cnt * 208 + t * 2);
   }
   static FOX_DEV uint32_t wd(const uint4* v, int i) {
     return (i & 3) == 0 ? v[i >> 2].x : (i & 3) == 1 ? v[i >> 2].y : (i & 3) == 2 ? v[i >> 2].z : v[i >> 2].w;
@@ -245,10 +254,11 @@ template <> struct W<T_Q8_0> {
   static constexpr int NT = 1, BE = 32, MAXT = 512;
   static constexpr bool PREFETCH = true;
   struct R { uint4 a, b; uint32_t d; };
+  template <bool SH = false>
   static FOX_DEV void load(R& r, const uint8_t* base, long cnt, int t) {
-    r.a = ldg_stream16(base + t * 16);
-    r.b = ldg_stream16(base + cnt * 16 + t * 16);
-    r.d = ldg_stream2(base + cnt * 32 + t * 2);
+    r.a = ld16<SH>(base + t * 16);
+    r.b = ld16<SH>(base + cnt * 16 + t * 16);
+    r.d = ld2<SH>(base + cnt * 32 + t * 2);
   }
   static FOX_DEV void termsf(const R& r, const float* xf, float* out) {
     const uint32_t c[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
@@ -283,7 +293,13 @@ inline size_t gemv_smem_bytes(int type, int pro, int K, int U, int nb) {
 
 // ---------------------------------------------------------------------------
 
-template <int T, int PRO, int EPI>
+// RING: instead of a register prefetch of the next unit, thread 0 keeps up to
+// ring_slots of this CTA's units in flight as bulk asynchronous copies into
+// shared memory (one mbarrier per slot, reissued as soon as a slot has been
+// read), so a CTA has tens of KB of weights in flight instead of one unit.
+// A ring launch carries programmatic stream serialisation: the first copies
+// start before the predecessor kernel has finished.
+template <int T, int PRO, int EPI, bool RING = false>
 __global__ void __launch_bounds__(W<T>::MAXT)
 gemv_kernel(const GemvParams p) {
   using Tr = W<T>;
@@ -291,6 +307,40 @@ gemv_kernel(const GemvParams p) {
   const int tid = threadIdx.x, nth = blockDim.x;
   const int K = p.K, nb = p.nb, U = p.U, ut = U * nb;
   const int nb256 = K / 256;
+  const int units = (p.n_rows + U - 1) / U;
+  const long unit_bytes = (long)ut * block_bytes(T);
+
+  uint8_t* ring = smem + p.ring_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + (size_t)p.ring_slots * p.slot_bytes);
+  const int R = p.ring_slots;
+  const int n_mine = (int)blockIdx.x < units ? (units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  // A partial last unit whose size is not a multiple of 16 bytes cannot be
+  // bulk-copied; it is read from global memory directly (it is always the
+  // last unit of its CTA, so no later use of its slot is affected).
+  auto direct = [&](int u) {
+    const int ru = min(U, p.n_rows - u * U);
+    return ((long)ru * nb * block_bytes(T)) % 16 != 0;
+  };
+  // the k-th unit of this CTA into slot k % R
+  auto issue = [&](int k) {
+    const int uu = blockIdx.x + k * gridDim.x;
+    if (direct(uu)) return;
+    const int ru = min(U, p.n_rows - uu * U);
+    const unsigned bytes = (unsigned)((long)ru * nb * block_bytes(T));
+    uint64_t* b = bars + k % R;
+    mbar_arrive_expect_tx(b, bytes);
+    bulk_g2s(ring + (size_t)(k % R) * p.slot_bytes, p.w + (size_t)uu * unit_bytes, bytes, b);
+  };
+  if (RING) {
+    if (tid == 0) {
+      for (int i = 0; i < R; ++i) mbar_init(bars + i, 1);
+      mbar_fence_init();
+      for (int k = 0; k < min(R, n_mine); ++k) issue(k);
+    }
+    griddep_launch_dependents();
+    griddep_wait();
+    __syncthreads();
+  }
 
   unsigned char* sp = smem;
   float* xs = nullptr;
@@ -413,34 +463,9 @@ gemv_kernel(const GemvParams p) {
   }
 
   // ---------------- main loop over units ---------------------------------
-  const int units = (p.n_rows + U - 1) / U;
-  const long unit_bytes = (long)ut * block_bytes(T);
-  typename Tr::R cur, nxt;
-  int u = blockIdx.x;
-  if (Tr::PREFETCH && u < units) {
-    const int ru = min(U, p.n_rows - u * U);
-    if (tid < ru * nb) Tr::load(cur, p.w + u * unit_bytes, (long)ru * nb, tid);
-  }
   const int prow = tid / nb, pcol = (tid - prow * nb) * Tr::NT;
-  for (; u < units; u += gridDim.x) {
-    const int ru = min(U, p.n_rows - u * U);
-    if (Tr::PREFETCH) {
-      const int un = u + gridDim.x;
-      if (un < units) {
-        const int run = min(U, p.n_rows - un * U);
-        if (tid < run * nb) Tr::load(nxt, p.w + un * unit_bytes, (long)run * nb, tid);
-      }
-    } else if (tid < ru * nb) {
-      Tr::load(cur, p.w + u * unit_bytes, (long)ru * nb, tid);
-    }
-    if (tid < ru * nb) {
-      float t[Tr::NT];
-      if constexpr (T == T_Q8_0) Tr::termsf(cur, xf, t);
-      else Tr::terms(cur, xw, sx, as, t);
-#pragma unroll
-      for (int k = 0; k < Tr::NT; ++k) part[prow * rstride + pcol + k] = t[k];
-    }
-    __syncthreads();
+  // rows of unit u in upstream's order from the parked terms, then the epilogue
+  auto finish = [&](int u, int ru) {
     float v = 0.0f;
     if (tid < ru) {
       // upstream order: blocks in order, terms of a block in order, from 0.0f
@@ -489,7 +514,64 @@ gemv_kernel(const GemvParams p) {
       }
     }
     __syncthreads();
-    if (Tr::PREFETCH) cur = nxt;
+  };
+  auto park = [&](const typename Tr::R& w) {
+    float t[Tr::NT];
+    if constexpr (T == T_Q8_0) Tr::termsf(w, xf, t);
+    else Tr::terms(w, xw, sx, as, t);
+#pragma unroll
+    for (int k = 0; k < Tr::NT; ++k) part[prow * rstride + pcol + k] = t[k];
+  };
+
+  typename Tr::R cur, nxt;
+  if constexpr (RING) {
+    for (int k = 0; k < n_mine; ++k) {
+      const int u = blockIdx.x + k * gridDim.x;
+      const int ru = min(U, p.n_rows - u * U);
+      const int slot = k % R;
+      const bool dir = direct(u);
+      const bool got = dir || mbar_wait(bars + slot, (k / R) & 1);
+      if (!__syncthreads_and(got)) {
+        if (tid == 0) {
+          if (p.err) atomicExch(p.err, 2);
+          // a second bounded wait for every copy still in flight
+          for (int j = k; j < min(n_mine, k + R); ++j)
+            if (!direct(blockIdx.x + j * gridDim.x)) mbar_wait(bars + j % R, (j / R) & 1);
+        }
+        __syncthreads();
+        return;
+      }
+      if (tid < ru * nb) {
+        if (dir) Tr::load(cur, p.w + u * unit_bytes, (long)ru * nb, tid);
+        else Tr::template load<true>(cur, ring + (size_t)slot * p.slot_bytes, (long)ru * nb, tid);
+        park(cur);
+      }
+      __syncthreads();  // the slot is free again
+      if (tid == 0 && k + R < n_mine) issue(k + R);
+      finish(u, ru);
+    }
+  } else {
+    int u = blockIdx.x;
+    if (Tr::PREFETCH && u < units) {
+      const int ru = min(U, p.n_rows - u * U);
+      if (tid < ru * nb) Tr::load(cur, p.w + u * unit_bytes, (long)ru * nb, tid);
+    }
+    for (; u < units; u += gridDim.x) {
+      const int ru = min(U, p.n_rows - u * U);
+      if (Tr::PREFETCH) {
+        const int un = u + gridDim.x;
+        if (un < units) {
+          const int run = min(U, p.n_rows - un * U);
+          if (tid < run * nb) Tr::load(nxt, p.w + un * unit_bytes, (long)run * nb, tid);
+        }
+      } else if (tid < ru * nb) {
+        Tr::load(cur, p.w + u * unit_bytes, (long)ru * nb, tid);
+      }
+      if (tid < ru * nb) park(cur);
+      __syncthreads();
+      finish(u, ru);
+      if (Tr::PREFETCH) cur = nxt;
+    }
   }
 }
 

@@ -59,6 +59,7 @@ __global__ void dequant_row_kernel(int type, const uint8_t* __restrict__ row, in
 __global__ void embed_kernel(int type, const uint8_t* __restrict__ table, size_t row_bytes,
                              int n_embd, const uint32_t* __restrict__ token,
                              float* __restrict__ x) {
+  griddep_launch_dependents();  // the first q|k|v GEMV may start streaming its weights
   const uint8_t* row = table + (size_t)(*token) * row_bytes;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_embd; e += gridDim.x * blockDim.x)
     x[e] = dequant_elem(type, row, e);
@@ -112,8 +113,67 @@ FOX_DEV void load_kv(const void* cache, bool f16, size_t off, float* v) {
   }
 }
 
+// The last CTA of KV head g to finish merges the S split partials
+// (max, sum, unnormalised output per query head) into the output.
+FOX_DEV void attn_merge(const AttnParams& p, int g, int S, int gqa, int hd) {
+  __shared__ bool is_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(p.counters + g, 1u) == (unsigned)(S - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // The partials of the other CTAs are read through L2 (ld.global.cg: L1 is
+  // not coherent with their writes). Per (split, head): max and sum to shared
+  // memory, then the rescale factors, then every output dimension as an
+  // independent, pipelined sweep over the splits.
+  __shared__ float s_m[32][ATTN_MAX_GQA], s_l[32][ATTN_MAX_GQA], s_e[32][ATTN_MAX_GQA];
+  __shared__ float s_M[ATTN_MAX_GQA], s_L[ATTN_MAX_GQA];
+  const float* base = p.part + (size_t)g * p.S_max * gqa * (hd + 2);
+  for (int i = threadIdx.x; i < S * gqa; i += blockDim.x) {
+    const int t = i / gqa, h = i % gqa;
+    const float* pt = base + ((size_t)t * gqa + h) * (hd + 2);
+    s_m[t][h] = __ldcg(pt + hd);
+    s_l[t][h] = __ldcg(pt + hd + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < gqa) {
+    const int h = threadIdx.x;
+    float M = -CUDART_INF_F;
+    for (int t = 0; t < S; ++t)
+      if (s_l[t][h] > 0.0f) M = fmaxf(M, s_m[t][h]);
+    s_M[h] = M;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < S * gqa; i += blockDim.x) {
+    const int t = i / gqa, h = i % gqa;
+    s_e[t][h] = s_l[t][h] > 0.0f ? expf_cr(s_m[t][h] - s_M[h]) : 0.0f;
+  }
+  __syncthreads();
+  if (threadIdx.x < gqa) {
+    const int h = threadIdx.x;
+    float L = 0.0f;
+    for (int t = 0; t < S; ++t)
+      if (s_l[t][h] > 0.0f) L = fmaf(s_l[t][h], s_e[t][h], L);
+    s_L[h] = L;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < gqa * hd; idx += blockDim.x) {
+    const int h = idx / hd, d = idx % hd;
+    float A = 0.0f;
+#pragma unroll 8
+    for (int t = 0; t < S; ++t) {
+      const float v = __ldcg(base + ((size_t)t * gqa + h) * (hd + 2) + d);
+      if (s_l[t][h] > 0.0f) A = fmaf(v, s_e[t][h], A);
+    }
+    p.out[(g * gqa + h) * hd + d] = A / s_L[h];
+  }
+  if (threadIdx.x == 0) p.counters[g] = 0u;
+}
+
 template <int DPL>
 __global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const AttnParams p) {
+  griddep_launch_dependents();  // the o projection may start streaming its weights
   const int s = blockIdx.x, g = blockIdx.y;
   const int P = *p.pos + 1;
   const int S = min(p.S_max, max(1, (P + 31) / 32));
@@ -127,7 +187,6 @@ __global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const AttnParam
   __shared__ float qs[ATTN_MAX_GQA * 32 * ATTN_MAX_DPL];
   __shared__ float wm[4][ATTN_MAX_GQA], wl[4][ATTN_MAX_GQA];
   __shared__ float wacc[4][ATTN_MAX_GQA * 32 * ATTN_MAX_DPL];
-  __shared__ bool is_last;
 
   for (int i = threadIdx.x; i < gqa * hd; i += blockDim.x) qs[i] = p.q[g * gqa * hd + i];
   __syncthreads();
@@ -183,58 +242,204 @@ __global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const AttnParam
     part[h * (hd + 2) + idx % hd] = A;
     if (idx % hd == 0) { part[h * (hd + 2) + hd] = M; part[h * (hd + 2) + hd + 1] = L; }
   }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(p.counters + g, 1u) == (unsigned)(S - 1);
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  // The partials of the other CTAs are read through L2 (ld.global.cg: L1 is
-  // not coherent with their writes). Per (split, head): max and sum to shared
-  // memory, then the rescale factors, then every output dimension as an
-  // independent, pipelined sweep over the splits.
-  __shared__ float s_m[32][ATTN_MAX_GQA], s_l[32][ATTN_MAX_GQA], s_e[32][ATTN_MAX_GQA];
-  __shared__ float s_M[ATTN_MAX_GQA], s_L[ATTN_MAX_GQA];
-  const float* base = p.part + (size_t)g * p.S_max * gqa * (hd + 2);
-  for (int i = threadIdx.x; i < S * gqa; i += blockDim.x) {
-    const int t = i / gqa, h = i % gqa;
-    const float* pt = base + ((size_t)t * gqa + h) * (hd + 2);
-    s_m[t][h] = __ldcg(pt + hd);
-    s_l[t][h] = __ldcg(pt + hd + 1);
-  }
-  __syncthreads();
-  if (threadIdx.x < gqa) {
-    const int h = threadIdx.x;
-    float M = -CUDART_INF_F;
-    for (int t = 0; t < S; ++t)
-      if (s_l[t][h] > 0.0f) M = fmaxf(M, s_m[t][h]);
-    s_M[h] = M;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < S * gqa; i += blockDim.x) {
-    const int t = i / gqa, h = i % gqa;
-    s_e[t][h] = s_l[t][h] > 0.0f ? expf_cr(s_m[t][h] - s_M[h]) : 0.0f;
-  }
-  __syncthreads();
-  if (threadIdx.x < gqa) {
-    const int h = threadIdx.x;
-    float L = 0.0f;
-    for (int t = 0; t < S; ++t)
-      if (s_l[t][h] > 0.0f) L = fmaf(s_l[t][h], s_e[t][h], L);
-    s_L[h] = L;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < gqa * hd; idx += blockDim.x) {
-    const int h = idx / hd, d = idx % hd;
-    float A = 0.0f;
-#pragma unroll 8
-    for (int t = 0; t < S; ++t) {
-      const float v = __ldcg(base + ((size_t)t * gqa + h) * (hd + 2) + d);
-      if (s_l[t][h] > 0.0f) A = fmaf(v, s_e[t][h], A);
+  attn_merge(p, g, S, gqa, hd);
+}
+
+// Shared memory of one attention tile: 128 K rows padded by 16 bytes, then
+// 128 V rows.
+template <int HD, bool F16>
+constexpr size_t attn_tile_smem() {
+  return (size_t)128 * (HD * (F16 ? 2 : 4) + 16) + (size_t)128 * HD * (F16 ? 2 : 4);
+}
+
+FOX_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+FOX_DEV void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
+
+// Cluster decode attention. The ATTN_SPLITS CTAs of one KV head form a
+// thread-block cluster; CTA r takes the r-th run of the positions, in tiles of
+// 128 (K/V staged in shared memory with cp.async before q is read, scores one
+// position per thread, a per-tile online softmax, the weighted V sum one
+// dimension per thread). Its partial (max, sum, unnormalised output per query
+// head) stays in its own shared memory. After a cluster barrier every CTA
+// merges 1/ATTN_SPLITS of the outputs by reading the others' partials through
+// distributed shared memory, and a second barrier keeps every partial alive
+// until the last remote read. No global scratch, fence or atomic.
+constexpr int ATTN_SPLITS = 8;  // portable cluster size
+
+FOX_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// address of the same shared variable in CTA `rank` of this cluster
+FOX_DEV const float* cluster_peer(const float* p, unsigned rank) {
+  uint64_t r;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(p), "r"(rank));
+  return reinterpret_cast<const float*>(r);
+}
+
+template <int HD, int G, bool F16>
+__global__ void __cluster_dims__(ATTN_SPLITS, 1, 1) __launch_bounds__(128)
+attention_cluster_kernel(const AttnParams p) {
+  griddep_launch_dependents();  // the o projection may start streaming its weights
+  constexpr int NT = 128, DPT = NT / HD;
+  constexpr int ESZ = F16 ? 2 : 4, RB = HD * ESZ, KSTRIDE = RB + 16;
+  const int r = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;  // r = rank in the cluster
+  const int lane = tid & 31, warp = tid >> 5;
+  const int P = *p.pos + 1;
+  const int chunk = (P + ATTN_SPLITS - 1) / ATTN_SPLITS;
+  const int j0 = min(P, r * chunk), j1 = min(P, j0 + chunk);
+
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + (size_t)NT * KSTRIDE;
+  __shared__ float qs[G][HD];
+  __shared__ float ps[G][NT];
+  __shared__ float rmax[4][G], rsum[4][G];
+  __shared__ float accs[DPT > 1 ? DPT - 1 : 1][G][HD];
+  __shared__ float part[G][HD + 2];           // this CTA's partial, read by the cluster
+  __shared__ float ew[ATTN_SPLITS][G], lw[ATTN_SPLITS][G];
+
+  const size_t head = (size_t)g * p.n_ctx * HD;
+  const uint8_t* kg = reinterpret_cast<const uint8_t*>(p.kcache) + head * ESZ;
+  const uint8_t* vg = reinterpret_cast<const uint8_t*>(p.vcache) + head * ESZ;
+  auto stage = [&](int t0, int n) {
+    const int pieces = n * (RB / 16);
+    for (int i = tid; i < pieces; i += NT) {
+      const int row = i / (RB / 16), c = i - row * (RB / 16);
+      cp_async16(sK + (size_t)row * KSTRIDE + c * 16, kg + (size_t)(t0 + row) * RB + c * 16);
+      cp_async16(sV + (size_t)i * 16, vg + (size_t)t0 * RB + (size_t)i * 16);
     }
-    p.out[(g * gqa + h) * hd + d] = A / s_L[h];
+  };
+  if (j0 < j1) stage(j0, min(NT, j1 - j0));  // in flight while q is read
+  for (int i = tid; i < G * HD; i += NT) qs[i / HD][i % HD] = p.q[(size_t)g * G * HD + i];
+
+  const int d = tid % HD, jsub = tid / HD;
+  float m[G], l[G], acc[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) { m[h] = -CUDART_INF_F; l[h] = 0.0f; acc[h] = 0.0f; }
+
+  for (int t0 = j0; t0 < j1; t0 += NT) {
+    const int n = min(NT, j1 - t0);
+    if (t0 != j0) stage(t0, n);
+    cp_async_wait_all();
+    __syncthreads();
+    const bool on = tid < n;
+    float sc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) sc[h] = 0.0f;
+    if (on) {
+      const uint4* kr = reinterpret_cast<const uint4*>(sK + (size_t)tid * KSTRIDE);
+#pragma unroll 4
+      for (int c = 0; c < RB / 16; ++c) {
+        const uint4 w = kr[c];
+        if (F16) {
+          const __half2* hw = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 kv = __half22float2(hw[e]);
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+              sc[h] = fmaf(qs[h][c * 8 + 2 * e], kv.x, sc[h]);
+              sc[h] = fmaf(qs[h][c * 8 + 2 * e + 1], kv.y, sc[h]);
+            }
+          }
+        } else {
+          const float* fw = reinterpret_cast<const float*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+#pragma unroll
+            for (int h = 0; h < G; ++h) sc[h] = fmaf(qs[h][c * 4 + e], fw[e], sc[h]);
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      sc[h] = on ? sc[h] * p.scale : -CUDART_INF_F;
+      const float mx = warp_max(sc[h]);
+      if (lane == 0) rmax[warp][h] = mx;
+    }
+    __syncthreads();
+    float corr[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float tmax = fmaxf(fmaxf(rmax[0][h], rmax[1][h]), fmaxf(rmax[2][h], rmax[3][h]));
+      const float mn = fmaxf(m[h], tmax);
+      corr[h] = m[h] == -CUDART_INF_F ? 0.0f : expf_cr(m[h] - mn);
+      float pj = 0.0f;
+      if (on) pj = expf_cr(sc[h] - mn);
+      ps[h][tid] = pj;
+      const float sm = warp_sum(pj);
+      if (lane == 0) rsum[warp][h] = sm;
+      m[h] = mn;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      l[h] = fmaf(l[h], corr[h], (rsum[0][h] + rsum[1][h]) + (rsum[2][h] + rsum[3][h]));
+      acc[h] *= corr[h];
+    }
+#pragma unroll 8
+    for (int jj = jsub; jj < n; jj += DPT) {
+      const float v = F16 ? __half2float(reinterpret_cast<const __half*>(sV)[(size_t)jj * HD + d])
+                          : reinterpret_cast<const float*>(sV)[(size_t)jj * HD + d];
+#pragma unroll
+      for (int h = 0; h < G; ++h) acc[h] = fmaf(ps[h][jj], v, acc[h]);
+    }
+    __syncthreads();
   }
-  if (threadIdx.x == 0) p.counters[g] = 0u;
+  if (DPT > 1) {
+    if (jsub > 0)
+#pragma unroll
+      for (int h = 0; h < G; ++h) accs[jsub - 1][h][d] = acc[h];
+    __syncthreads();
+    if (jsub == 0)
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        for (int k = 0; k < DPT - 1; ++k) acc[h] += accs[k][h][d];
+  }
+  if (jsub == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      part[h][d] = acc[h];
+      if (d == 0) { part[h][HD] = m[h]; part[h][HD + 1] = l[h]; }
+    }
+  }
+  cluster_sync_all();
+  // merge: rescale factors of every split, then this CTA's slice of outputs
+  if (tid < ATTN_SPLITS * G) {
+    const int t = tid / G, h = tid - t * G;
+    const float* pt = cluster_peer(&part[h][0], t);
+    ew[t][h] = pt[HD];
+    lw[t][h] = pt[HD + 1];
+  }
+  __syncthreads();
+  if (tid < G) {
+    const int h = tid;
+    float M = -CUDART_INF_F;
+    for (int t = 0; t < ATTN_SPLITS; ++t)
+      if (lw[t][h] > 0.0f) M = fmaxf(M, ew[t][h]);
+    float L = 0.0f;
+    for (int t = 0; t < ATTN_SPLITS; ++t) {
+      const float e = lw[t][h] > 0.0f ? expf_cr(ew[t][h] - M) : 0.0f;
+      ew[t][h] = e;
+      L = fmaf(lw[t][h], e, L);
+    }
+    rsum[0][h] = L;
+  }
+  __syncthreads();
+  constexpr int PER = G * HD / ATTN_SPLITS;  // outputs merged by each CTA
+  for (int k = tid; k < PER; k += NT) {
+    const int idx = r * PER + k, h = idx / HD, dd = idx - h * HD;
+    float A = 0.0f;
+#pragma unroll
+    for (int t = 0; t < ATTN_SPLITS; ++t)
+      if (lw[t][h] > 0.0f) A = fmaf(cluster_peer(&part[h][dd], t)[0], ew[t][h], A);
+    p.out[((size_t)g * G + h) * HD + dd] = A / rsum[0][h];
+  }
+  cluster_sync_all();  // no CTA leaves while another may still read its partial
 }
 
 // Attention in upstream's exact operation order (src/forward.c:222-257,

@@ -86,4 +86,62 @@ __global__ void pack_kernel(int type, const uint8_t* __restrict__ src, int n_row
   }
 }
 
+// TQ1_0 -> TQ2_0 on the device, one thread per 256 block. The decode
+// follows upstream's TQ1_0 rule (src/ternary.c:59-93): the level-l trit of
+// byte c is ((c * 3^l mod 256) * 3) >> 8, minus 1, for elements l*32 + m
+// (qs[m]), 160 + l*16 + m (qs[32+m]) and 240 + l*4 + m (qh[m]). Each trit + 1
+// is written as the 2-bit TQ2_0 code of the same element (bits 2l of
+// qs[j*32+m] for element j*128 + l*32 + m, src/ternary.c:177-188), and the
+// fp16 scale is copied. Every block's trits and scale are unchanged, so
+// every integer block sum, and everything computed from it, is unchanged.
+__global__ void tq1_to_tq2_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                  long n_blocks) {
+  const long b = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (b >= n_blocks) return;
+  const uint8_t* in = src + b * 54;
+  uint8_t codes[256];
+  const uint8_t pow3[5] = {1, 3, 9, 27, 81};
+  for (int l = 0; l < 5; ++l)
+    for (int m = 0; m < 32; ++m)
+      codes[l * 32 + m] = (uint8_t)(((unsigned)(uint8_t)(in[m] * pow3[l]) * 3u) >> 8);
+  for (int l = 0; l < 5; ++l)
+    for (int m = 0; m < 16; ++m)
+      codes[160 + l * 16 + m] = (uint8_t)(((unsigned)(uint8_t)(in[32 + m] * pow3[l]) * 3u) >> 8);
+  for (int l = 0; l < 4; ++l)
+    for (int m = 0; m < 4; ++m)
+      codes[240 + l * 4 + m] = (uint8_t)(((unsigned)(uint8_t)(in[48 + m] * pow3[l]) * 3u) >> 8);
+  uint8_t* out = dst + b * 66;
+  for (int j = 0; j < 2; ++j)
+    for (int m = 0; m < 32; ++m) {
+      unsigned q = 0;
+      for (int l = 0; l < 4; ++l) q |= (unsigned)codes[j * 128 + l * 32 + m] << (2 * l);
+      out[j * 32 + m] = (uint8_t)q;
+    }
+  out[64] = in[52];
+  out[65] = in[53];
+}
+
+// Q8_0 rows for q8_rows_kernel (rows.cuh): units of 32 rows; in a unit,
+// block b of row r puts qs[0..16) at plane 0 [b][r], qs[16..32) at plane 1
+// [b][r] and d at plane 2 [b][r]. A byte permutation of the GGUF bytes.
+__global__ void pack_q8_rows32_kernel(const uint8_t* __restrict__ src, int n_rows, int nb,
+                                      uint8_t* __restrict__ dst) {
+  const long total = (long)n_rows * nb;
+  for (long g = blockIdx.x * (long)blockDim.x + threadIdx.x; g < total;
+       g += (long)gridDim.x * blockDim.x) {
+    const long row = g / nb;
+    const int b = (int)(g - row * nb);
+    const long u = row / 32;
+    const int r = (int)(row - u * 32);
+    const uint8_t* in = src + g * 34;
+    uint8_t* base = dst + u * (long)nb * 32 * 34;
+    uint8_t* p0 = base + ((long)b * 32 + r) * 16;
+    uint8_t* p1 = base + (long)nb * 512 + ((long)b * 32 + r) * 16;
+    uint8_t* pd = base + (long)nb * 1024 + ((long)b * 32 + r) * 2;
+    for (int i = 0; i < 16; ++i) { p0[i] = in[2 + i]; p1[i] = in[18 + i]; }
+    pd[0] = in[0];
+    pd[1] = in[1];
+  }
+}
+
 }  // namespace fox

@@ -17,8 +17,11 @@ Two device modes:
               absmax scale, a discontinuous map: one flipped rounding moves a
               layer's output by the quantisation noise (~3e-3 relative), so
               per-layer agreement is bounded by that, not by float error.
-Against upstream's own semantics (glibc expf, fp32 KV) the greedy tokens are
-compared in both modes.
+Against upstream's own semantics (glibc expf, fp32 KV) the parity mode's
+greedy tokens are compared too. Production mode is compared step by step on a
+fixed token sequence (teacher forcing), because free-running greedy sequences
+part at the first near-tie a rounding difference flips, even between two
+builds of upstream itself.
 """
 import numpy as np
 import pytest
@@ -59,18 +62,23 @@ def test_parity_mode_greedy_128(gpu_tiny, oracle_tiny):
     assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
 
 
-def test_production_mode_first_eval(gpu_tiny, oracle_tiny):
+@pytest.mark.parametrize("kv", ["f16", "f32"])
+def test_production_mode_first_eval(gpu_tiny, oracle_tiny, kv):
     with O.exp_mode(True):
-        want, want_h = oracle_tiny.context(N_CTX, kv_fp16=True).eval(PROMPT, want_hidden=True)
-    ctx = gpu_tiny.context(N_CTX, kv="f16")
+        want, want_h = oracle_tiny.context(N_CTX, kv_fp16=(kv == "f16")).eval(PROMPT, want_hidden=True)
+    ctx = gpu_tiny.context(N_CTX, kv=kv)
     ctx.set_trace(True)
     got = ctx.eval(PROMPT)
     assert ctx.pos == 64
     assert np.isfinite(got).all() and np.ptp(got) > 0
     errs = [rel_l2(ctx.hidden(l), want_h[l]) for l in range(CFG.n_layer + 1)]
     assert errs[0] == 0.0                       # embedding row: exact
-    assert max(errs) <= 1e-2, errs               # quantisation-noise bound
-    assert rel_l2(got, want) <= 1e-2
+    # The band upstream's own builds differ by on this model (FMA on vs off,
+    # test_upstream_builds_differ_by_float_order: 1.4e-2 on the logits),
+    # with a margin: int8 re-quantisation turns any float reordering into
+    # discrete flips of this size.
+    assert max(errs) <= 3e-2, errs
+    assert rel_l2(got, want) <= 3e-2
     assert int(np.argmax(got)) == int(np.argmax(want))
     ctx.close()
 
@@ -79,16 +87,26 @@ def _first_divergence(a, b) -> int:
     return len(a) if np.array_equal(a, b) else int(np.argmax(a != b))
 
 
-@pytest.mark.parametrize("kv", ["f16", "f32"])
-def test_production_mode_greedy_prefix(gpu_tiny, oracle_tiny, kv):
-    """Split-K attention sums in a different order than upstream, so the
-    chaotic int8 quantisation eventually flips a near-tie; on this prompt the
-    first 42 (fp16 cache) and 59 (fp32 cache) tokens agree with the oracle run
-    with the same cache rounding. The test keeps a margin below those."""
+def test_production_mode_teacher_forced(gpu_tiny, oracle_tiny):
+    """Production mode (fp16 cache, split attention) against the oracle run
+    with the same cache rounding, step by step on one fixed token sequence,
+    so a rounding difference at one step does not change the next step's
+    input. Free-running greedy sequences part wherever a near-tie flips: even
+    upstream's own two builds part after a few tokens
+    (test_upstream_builds_differ_by_float_order). Every step here stays inside
+    the band those builds differ by, and the argmax agrees on nearly every
+    step."""
+    seq = synth.random_prompt(CFG, 96, seed=11)
     with O.exp_mode(True):
-        want = O.greedy_generate(oracle_tiny, PROMPT, 128, N_CTX, kv_fp16=(kv == "f16"))
-    got = rf.greedy_generate(gpu_tiny, PROMPT, 128, N_CTX, kv=kv)
-    assert _first_divergence(got, want) >= 24
+        octx = oracle_tiny.context(N_CTX, kv_fp16=True)
+        want = [octx.eval(PROMPT)] + [octx.eval([int(t)]) for t in seq]
+    ctx = gpu_tiny.context(N_CTX, kv="f16")
+    got = [ctx.eval(PROMPT)] + [ctx.eval([int(t)]) for t in seq]
+    errs = [rel_l2(a, b) for a, b in zip(got, want)]
+    agree = np.mean([int(np.argmax(a)) == int(np.argmax(b)) for a, b in zip(got, want)])
+    assert max(errs) <= 3e-2, max(errs)
+    assert agree >= 0.9, agree
+    ctx.close()
 
 
 def test_parity_mode_matches_upstream_until_libm_expf_differs(gpu_tiny, oracle_tiny):
