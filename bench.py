@@ -316,7 +316,7 @@ def run_ours(args):
                          "us_per_launch": kern_us},
             "cpu_baseline": cpu,
             "e2e": {"value": world * args.steps / e2e_s, "unit": "tok/s",
-                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+                    "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8},
             "gpu_launches": launches_per_tok * args.steps,
             "clocks": clk,
         }
