@@ -222,6 +222,51 @@ foxcuda_status foxcuda_decode(foxcuda_context *c, foxcuda_sampler *s, uint32_t t
 foxcuda_status foxcuda_generate(foxcuda_context *c, foxcuda_sampler *s, uint32_t token,
                                 size_t n, uint32_t *out);
 
+/* ---- tensor parallel (no upstream counterpart: upstream runs one process,
+ * src/threadpool.c; the split follows the scheme of include/fox/fox.h's
+ * fox_eval with Megatron-style shards) ------------------------------------
+ * Shard tp_rank of tp_size: q/k/v rows by heads, gate/up rows by 256-wide FFN
+ * blocks, head rows by vocabulary range (column-parallel); attn_output and
+ * ffn_down by the matching column blocks (row-parallel). A row-parallel shard
+ * quantises with the absmax of the whole vector (a max over shards), emits
+ * its per-block float terms, and every shard folds the gathered terms in
+ * upstream's block order: the sharded decode equals the unsharded one bit for
+ * bit. The steps below only enqueue work on foxcuda_context_stream(); the
+ * caller puts its collectives (max-allreduce of one float, all-gathers of the
+ * terms and of the {value, index} pairs) on the same stream between them. */
+typedef struct {
+    int32_t  tp_rank, tp_size;
+    uint32_t n_head, n_head_kv, n_ff;   /* this shard's heads and FFN width */
+    uint32_t vocab_begin, n_vocab;      /* this shard's head rows */
+    uint32_t o_blocks;                  /* attn_output column blocks per shard */
+    uint32_t ffn_blocks[8];             /* ffn_down column blocks of every shard */
+    uint32_t o_terms, down_terms;       /* float terms per block (1 ternary, 8 Q4_K,
+                                           4 Q6_K), the most over the layers */
+} foxcuda_tp_shape;
+
+foxcuda_status foxcuda_model_create_tp(const foxcuda_model_info *info, int device, int tp_rank,
+                                       int tp_size, foxcuda_model **out);
+foxcuda_status foxcuda_tp_info(const foxcuda_model *m, foxcuda_tp_shape *out);
+void          *foxcuda_context_stream(foxcuda_context *c);
+/* token >= 0 comes from the host; token < 0 embeds the last foxcuda_tp_pick */
+foxcuda_status foxcuda_tp_embed(foxcuda_context *c, int64_t token);
+foxcuda_status foxcuda_tp_attention(foxcuda_context *c, uint32_t layer);
+/* which: 0 = attention output (o input), 1 = FFN hidden (down input); device float */
+foxcuda_status foxcuda_tp_amax(foxcuda_context *c, int which, float *amax);
+foxcuda_status foxcuda_tp_terms(foxcuda_context *c, uint32_t layer, int which,
+                                const float *amax_all, float *terms, uint32_t stride);
+foxcuda_status foxcuda_tp_fold(foxcuda_context *c, uint32_t layer, int which,
+                               const float *gathered, uint32_t stride, const float *amax_all);
+foxcuda_status foxcuda_tp_ffn(foxcuda_context *c, uint32_t layer);
+/* best = {value, index bits} (2 device floats) */
+foxcuda_status foxcuda_tp_head(foxcuda_context *c, float *best);
+/* pairs = tp_size gathered {value, index} pairs (device); pos += 1 */
+foxcuda_status foxcuda_tp_pick(foxcuda_context *c, const float *pairs);
+foxcuda_status foxcuda_tp_advance(foxcuda_context *c);
+foxcuda_status foxcuda_tp_tokens(foxcuda_context *c, uint32_t first_pos, size_t n, uint32_t *out);
+/* this shard's logits of its last head evaluation (n <= its vocabulary rows) */
+foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
+
 /* ---- diagnostics (no upstream counterpart; upstream only times whole evals,
  * src/forward.c:421-435) ------------------------------------------------- */
 

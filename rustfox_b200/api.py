@@ -98,6 +98,21 @@ _PROTOS = {
                                       C.POINTER(C.c_int)]),
     "foxcuda_context_bench_kernel": (_st, [_vp, C.c_int, C.c_int, C.POINTER(C.c_double),
                                            C.POINTER(C.c_uint64)]),
+    "foxcuda_model_create_tp": (_st, [C.POINTER(ModelInfo), C.c_int, C.c_int, C.c_int,
+                                      C.POINTER(_vp)]),
+    "foxcuda_tp_info": (_st, [_vp, _vp]),
+    "foxcuda_context_stream": (_vp, [_vp]),
+    "foxcuda_tp_embed": (_st, [_vp, C.c_int64]),
+    "foxcuda_tp_attention": (_st, [_vp, C.c_uint32]),
+    "foxcuda_tp_amax": (_st, [_vp, C.c_int, _vp]),
+    "foxcuda_tp_terms": (_st, [_vp, C.c_uint32, C.c_int, _vp, _vp, C.c_uint32]),
+    "foxcuda_tp_fold": (_st, [_vp, C.c_uint32, C.c_int, _vp, C.c_uint32, _vp]),
+    "foxcuda_tp_ffn": (_st, [_vp, C.c_uint32]),
+    "foxcuda_tp_head": (_st, [_vp, _vp]),
+    "foxcuda_tp_pick": (_st, [_vp, _vp]),
+    "foxcuda_tp_advance": (_st, [_vp]),
+    "foxcuda_tp_tokens": (_st, [_vp, C.c_uint32, _sz, _vp]),
+    "foxcuda_context_logits": (_st, [_vp, _vp, _sz]),
 }
 
 KIND_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "advance", "head", "pick"]
@@ -217,14 +232,17 @@ def gemv_packed(ggml_type: int, x, packed, n_rows: int, n_cols: int, out=None):
 class Model:
     """Weights resident in HBM (upstream fox_model_open, src/model.c:146-303)."""
 
-    def __init__(self, info: dict, tensors, device: int = 0):
-        """tensors: iterable of (name, ggml_type, ne tuple, host array)."""
+    def __init__(self, info: dict, tensors, device: int = 0, tp_rank: int = 0, tp_size: int = 1):
+        """tensors: iterable of (name, ggml_type, ne tuple, host array). With
+        tp_size > 1 this is tensor-parallel shard tp_rank: every tensor is
+        uploaded whole and the library keeps this shard's part."""
         self.info = dict(info)
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         mi = ModelInfo(*(int(info[k]) for k in ("n_layer", "n_embd", "n_head", "n_head_kv",
                                                 "n_ff", "head_dim", "n_vocab")),
                        float(info["rms_eps"]), float(info["rope_freq_base"]))
         h = C.c_void_p()
-        _check(lib().foxcuda_model_create(C.byref(mi), device, C.byref(h)))
+        _check(lib().foxcuda_model_create_tp(C.byref(mi), device, tp_rank, tp_size, C.byref(h)))
         self.h = h
         self.device = device
         try:
@@ -242,12 +260,13 @@ class Model:
             raise
 
     @classmethod
-    def from_synthetic(cls, model, device: int = 0) -> "Model":
+    def from_synthetic(cls, model, device: int = 0, tp_rank: int = 0, tp_size: int = 1) -> "Model":
         c = model.cfg
         info = dict(n_layer=c.n_layer, n_embd=c.n_embd, n_head=c.n_head, n_head_kv=c.n_head_kv,
                     n_ff=c.n_ff, head_dim=c.head_dim, n_vocab=c.n_vocab, rms_eps=c.rms_eps,
                     rope_freq_base=c.rope_base)
-        return cls(info, ((n, tt, ne, d) for n, (tt, ne, d) in model.tensors.items()), device)
+        return cls(info, ((n, tt, ne, d) for n, (tt, ne, d) in model.tensors.items()), device,
+                   tp_rank, tp_size)
 
     @classmethod
     def from_gguf(cls, path: str, device: int = 0) -> "Model":

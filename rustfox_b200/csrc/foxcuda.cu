@@ -167,7 +167,7 @@ static cudaError_t launch_ring_t(GemvParams p, cudaStream_t s) {
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, p);
@@ -222,7 +222,7 @@ static cudaError_t launch_slice_t(const GemvParams& p, const SliceGeom& g, int g
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, p, g);
@@ -596,7 +596,14 @@ struct LayerW {
 };
 
 struct foxcuda_model {
-  foxcuda_model_info info;
+  foxcuda_model_info info;     // the whole model (what uploads are checked against)
+  foxcuda_model_info loc;      // this tensor-parallel shard (== info when tp_size == 1)
+  int tp_rank = 0, tp_size = 1;
+  uint32_t q_row0 = 0, kv_row0 = 0;        // first q row / k,v row of this shard
+  uint32_t o_block0 = 0, o_blocks = 0;     // attn_output column blocks of this shard
+  uint32_t f_block0 = 0, f_blocks = 0;     // FFN blocks (256 wide) of this shard
+  uint32_t f_blocks_all[8] = {0};          // FFN blocks of every shard, rank order
+  uint32_t vocab0 = 0;                     // first head row of this shard
   int device = 0;
   bool finalized = false;
   std::vector<RawTensor> raw;  // [role * (n_layer+1) + layer] staging until finalize
@@ -638,10 +645,62 @@ extern "C" foxcuda_status foxcuda_model_create(const foxcuda_model_info* info, i
   if (st) return st;
   foxcuda_model* m = new foxcuda_model();
   m->info = mi;
+  m->loc = mi;
+  m->o_blocks = mi.n_head * mi.head_dim / 256;
+  m->f_blocks = mi.n_ff / 256;
+  m->f_blocks_all[0] = m->f_blocks;
   m->device = device;
   m->raw.resize((size_t)FOXCUDA_N_ROLES * (mi.n_layer + 1));
   m->layers.resize(mi.n_layer);
   *out = m;
+  return FOXCUDA_OK;
+}
+
+// Tensor-parallel shard tp_rank of tp_size (upstream has no multi-GPU path;
+// the split is Megatron-style): q/k/v by heads, gate/up by 256-wide FFN blocks
+// and the head by vocab rows (column-parallel, no exchange); attn_output and
+// ffn_down by the matching column blocks (row-parallel: their block terms are
+// exchanged and folded in upstream's block order, see foxcuda_tp_terms).
+extern "C" foxcuda_status foxcuda_model_create_tp(const foxcuda_model_info* info, int device,
+                                                  int tp_rank, int tp_size, foxcuda_model** out) {
+  if (!info || !out) return fail(FOXCUDA_ERR_ARG, "model: null argument");
+  if (tp_size < 1 || tp_size > 8 || tp_rank < 0 || tp_rank >= tp_size)
+    return fail(FOXCUDA_ERR_ARG, "model: tensor-parallel rank %d of %d (at most 8 shards)", tp_rank, tp_size);
+  const foxcuda_model_info& mi = *info;
+  if (tp_size > 1) {
+    if (mi.n_head % tp_size || mi.n_head_kv % tp_size)
+      return fail(FOXCUDA_ERR_UNSUPPORTED, "model: %u query / %u kv heads do not split over %d shards",
+                  mi.n_head, mi.n_head_kv, tp_size);
+    if ((mi.n_head / tp_size * mi.head_dim) % 256)
+      return fail(FOXCUDA_ERR_UNSUPPORTED, "model: a shard's attention output is not whole 256-blocks");
+    if (mi.n_ff / 256 < (uint32_t)tp_size || mi.n_vocab % 32)
+      return fail(FOXCUDA_ERR_UNSUPPORTED, "model: FFN or vocabulary too small to split %d ways", tp_size);
+  }
+  foxcuda_status st = foxcuda_model_create(info, device, out);
+  if (st || tp_size == 1) return st;
+  foxcuda_model* m = *out;
+  m->tp_rank = tp_rank;
+  m->tp_size = tp_size;
+  const uint32_t hl = mi.n_head / tp_size, kvl = mi.n_head_kv / tp_size;
+  m->loc.n_head = hl;
+  m->loc.n_head_kv = kvl;
+  m->q_row0 = tp_rank * hl * mi.head_dim;
+  m->kv_row0 = tp_rank * kvl * mi.head_dim;
+  m->o_blocks = hl * mi.head_dim / 256;
+  m->o_block0 = tp_rank * m->o_blocks;
+  const uint32_t nbf = mi.n_ff / 256;
+  for (int k = 0; k < tp_size; ++k) m->f_blocks_all[k] = (k + 1) * nbf / tp_size - k * nbf / tp_size;
+  m->f_block0 = tp_rank * nbf / tp_size;
+  m->f_blocks = m->f_blocks_all[tp_rank];
+  m->loc.n_ff = m->f_blocks * 256;
+  const uint32_t per = (mi.n_vocab / tp_size + 31) / 32 * 32;
+  m->vocab0 = std::min(mi.n_vocab, tp_rank * per);
+  m->loc.n_vocab = std::min(mi.n_vocab, m->vocab0 + per) - m->vocab0;
+  if (m->loc.n_vocab == 0) {
+    foxcuda_model_destroy(m);
+    *out = nullptr;
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "model: vocabulary too small to split %d ways", tp_size);
+  }
   return FOXCUDA_OK;
 }
 
@@ -711,6 +770,30 @@ static foxcuda_status norm_vec(foxcuda_model* m, const RawTensor& r, float** out
 static void free_raw(RawTensor& r) {
   if (r.dev) cudaFree(r.dev);
   r = RawTensor();
+}
+
+// This shard's part of an uploaded matrix (rows r0.. of n, or column blocks
+// b0.. of nb per row), replacing the staged tensor.
+static foxcuda_status keep_rows(RawTensor& r, uint64_t r0, uint64_t n) {
+  const size_t rb = row_bytes(r.type, r.ne0);
+  void* d = nullptr;
+  CK(cudaMalloc(&d, n * rb), "shard alloc");
+  CK(cudaMemcpy(d, r.dev + r0 * rb, n * rb, cudaMemcpyDeviceToDevice), "shard rows");
+  cudaFree(r.dev);
+  r.dev = (uint8_t*)d; r.ne1 = n; r.bytes = n * rb;
+  return FOXCUDA_OK;
+}
+
+static foxcuda_status keep_col_blocks(RawTensor& r, uint64_t b0, uint64_t nb) {
+  const size_t rb = row_bytes(r.type, r.ne0);
+  const size_t bb = row_bytes(r.type, 256) * nb;  // bytes of nb 256-wide blocks
+  const size_t off = row_bytes(r.type, 256) * b0;
+  void* d = nullptr;
+  CK(cudaMalloc(&d, r.ne1 * bb), "shard alloc");
+  CK(cudaMemcpy2D(d, bb, r.dev + off, rb, bb, r.ne1, cudaMemcpyDeviceToDevice), "shard columns");
+  cudaFree(r.dev);
+  r.dev = (uint8_t*)d; r.ne0 = nb * 256; r.bytes = r.ne1 * bb;
+  return FOXCUDA_OK;
 }
 
 // TQ1_0 layer matrices are held as TQ2_0 (tq1_to_tq2_kernel): the same trits
@@ -814,8 +897,21 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
     return fail(FOXCUDA_ERR_UNSUPPORTED, "model: output head type %d has no kernel here", head.type);
 
   foxcuda_status st;
+  // this shard's widths (the whole model when tp_size == 1)
+  const bool tp = m->tp_size > 1;
+  const int nq_l = m->loc.n_head * mi.head_dim, nkv_l = m->loc.n_head_kv * mi.head_dim;
+  const int Fd_l = m->loc.n_ff;
   for (uint32_t l = 0; l < mi.n_layer; ++l) {
     LayerW& L = m->layers[l];
+    if (tp) {
+      if ((st = keep_rows(m->slot(FOXCUDA_ATTN_Q, l), m->q_row0, nq_l))) return st;
+      if ((st = keep_rows(m->slot(FOXCUDA_ATTN_K, l), m->kv_row0, nkv_l))) return st;
+      if ((st = keep_rows(m->slot(FOXCUDA_ATTN_V, l), m->kv_row0, nkv_l))) return st;
+      if ((st = keep_col_blocks(m->slot(FOXCUDA_ATTN_OUT, l), m->o_block0, m->o_blocks))) return st;
+      if ((st = keep_rows(m->slot(FOXCUDA_FFN_GATE, l), (uint64_t)m->f_block0 * 256, Fd_l))) return st;
+      if ((st = keep_rows(m->slot(FOXCUDA_FFN_UP, l), (uint64_t)m->f_block0 * 256, Fd_l))) return st;
+      if ((st = keep_col_blocks(m->slot(FOXCUDA_FFN_DOWN, l), m->f_block0, m->f_blocks))) return st;
+    }
     for (int role : {FOXCUDA_ATTN_Q, FOXCUDA_ATTN_K, FOXCUDA_ATTN_V, FOXCUDA_ATTN_OUT,
                      FOXCUDA_FFN_GATE, FOXCUDA_FFN_UP, FOXCUDA_FFN_DOWN})
       if ((st = transcode_tq1(m->slot(role, l)))) return st;
@@ -824,7 +920,7 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
     // q|k|v: rows concatenated; consecutive tensors of one type share a matrix
     const RawTensor* qkv[3] = {&m->slot(FOXCUDA_ATTN_Q, l), &m->slot(FOXCUDA_ATTN_K, l),
                                &m->slot(FOXCUDA_ATTN_V, l)};
-    const int rows[3] = {nq, nkv, nkv};
+    const int rows[3] = {nq_l, nkv_l, nkv_l};
     int i = 0, base = 0;
     L.n_qkv = 0;
     while (i < 3) {
@@ -856,9 +952,11 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
       i = j;
     }
     {
+      // row-parallel shards keep the unit layout: their terms come from the
+      // unit kernel (foxcuda_tp_terms)
       const RawTensor& o = m->slot(FOXCUDA_ATTN_OUT, l);
-      const int su = slice_unit_for(m, o.type, E, nq, PRO_VEC);
-      if ((st = pack_into(m, o.type, o.dev, E, nq, &L.o, su))) return st;
+      const int su = tp ? 0 : slice_unit_for(m, o.type, E, nq_l, PRO_VEC);
+      if ((st = pack_into(m, o.type, o.dev, E, nq_l, &L.o, su))) return st;
       L.o.src_type = o.src_type;
       if (su) set_slice(m, &L.o, PRO_VEC);
     }
@@ -869,15 +967,15 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
       return fail(FOXCUDA_ERR_UNSUPPORTED, "model: ffn_gate and ffn_up types differ in layer %u", l);
     {
       const int nb = E / block_elems(g.type);
-      const int su = slice_unit_for(m, g.type, 2 * Fd, E, PRO_NORM);
+      const int su = slice_unit_for(m, g.type, 2 * Fd_l, E, PRO_NORM);
       const int U = su ? su : unit_rows(g.type, nb);
-      if (U < 0 || Fd % (U / 2)) return fail(FOXCUDA_ERR_UNSUPPORTED, "model: ffn width %d vs unit %d", Fd, U);
+      if (U < 0 || Fd_l % (U / 2)) return fail(FOXCUDA_ERR_UNSUPPORTED, "model: ffn width %d vs unit %d", Fd_l, U);
       const size_t rb = row_bytes(g.type, E), half = (size_t)(U / 2) * rb;
       void* cat = nullptr;
       CK(cudaMalloc(&cat, g.bytes + u.bytes), "staging alloc");
-      CK(cudaMemcpy2D(cat, 2 * half, g.dev, half, half, Fd / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
-      CK(cudaMemcpy2D((uint8_t*)cat + half, 2 * half, u.dev, half, half, Fd / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
-      st = pack_into(m, g.type, cat, 2 * Fd, E, &L.gateup, U);
+      CK(cudaMemcpy2D(cat, 2 * half, g.dev, half, half, Fd_l / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
+      CK(cudaMemcpy2D((uint8_t*)cat + half, 2 * half, u.dev, half, half, Fd_l / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
+      st = pack_into(m, g.type, cat, 2 * Fd_l, E, &L.gateup, U);
       L.gateup.src_type = g.src_type;
       if (!st && su) set_slice(m, &L.gateup, PRO_NORM);
       cudaDeviceSynchronize();
@@ -886,8 +984,8 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
     }
     {
       const RawTensor& d = m->slot(FOXCUDA_FFN_DOWN, l);
-      const int su = slice_unit_for(m, d.type, E, Fd, PRO_VEC);
-      if ((st = pack_into(m, d.type, d.dev, E, Fd, &L.down, su))) return st;
+      const int su = tp ? 0 : slice_unit_for(m, d.type, E, Fd_l, PRO_VEC);
+      if ((st = pack_into(m, d.type, d.dev, E, Fd_l, &L.down, su))) return st;
       L.down.src_type = d.src_type;
       if (su) set_slice(m, &L.down, PRO_VEC);
     }
@@ -895,18 +993,21 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
     for (int role = FOXCUDA_ATTN_NORM; role < FOXCUDA_N_ROLES; ++role) free_raw(m->slot(role, l));
   }
   if ((st = norm_vec(m, m->slot(FOXCUDA_OUTPUT_NORM, 0), &m->out_norm))) return st;
-  if (head.type == T_Q8_0 && mi.n_vocab % 32 == 0) {
+  // this shard's head rows (all of them when tp_size == 1)
+  const uint32_t nv_l = m->loc.n_vocab;
+  const uint8_t* head_rows = head.dev + (size_t)m->vocab0 * row_bytes(head.type, E);
+  if (head.type == T_Q8_0 && nv_l % 32 == 0) {
     // the row-per-lane layout of q8_rows_kernel
     PackedMat& H = m->output;
     void* dst = nullptr;
-    CK(dev_alloc(m, (size_t)mi.n_vocab * row_bytes(T_Q8_0, E), &dst), "head alloc");
-    const long total = (long)mi.n_vocab * (E / 32);
+    CK(dev_alloc(m, (size_t)nv_l * row_bytes(T_Q8_0, E), &dst), "head alloc");
+    const long total = (long)nv_l * (E / 32);
     pack_q8_rows32_kernel<<<(unsigned)std::min<long>((total + 255) / 256, 8192), 256>>>(
-        head.dev, (int)mi.n_vocab, E / 32, (uint8_t*)dst);
+        head_rows, (int)nv_l, E / 32, (uint8_t*)dst);
     CK(cudaGetLastError(), "head pack");
-    H.type = T_Q8_0; H.n_rows = (int)mi.n_vocab; H.K = E; H.nb = E / 32; H.U = 32;
+    H.type = T_Q8_0; H.n_rows = (int)nv_l; H.K = E; H.nb = E / 32; H.U = 32;
     H.dev = (uint8_t*)dst; H.rows32 = true;
-  } else if ((st = pack_into(m, head.type, head.dev, mi.n_vocab, E, &m->output))) {
+  } else if ((st = pack_into(m, head.type, head_rows, nv_l, E, &m->output))) {
     return st;
   }
   CK(cudaDeviceSynchronize(), "finalize head");
@@ -990,7 +1091,8 @@ extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda
     if (st) return st;
   }
   cudaSetDevice(m->device);
-  const foxcuda_model_info& mi = m->info;
+  // buffers and kernels use this shard's head and FFN counts
+  const foxcuda_model_info& mi = m->loc;
   foxcuda_context* c = new foxcuda_context();
   c->m = m;
   c->n_ctx = cfg && cfg->n_ctx ? cfg->n_ctx : 2048;
@@ -1102,6 +1204,11 @@ static uint64_t launch_weight_bytes(const foxcuda_model* m, int kind, uint32_t l
 // A layer GEMV through the kernel its layout was packed for.
 static cudaError_t launch_mat(foxcuda_context* c, const PackedMat& W, int pro, int epi, GemvParams& p) {
   p.err = c->err_dev;
+  // The single-GPU step is a chain of these kernels and overlaps them. A
+  // tensor-parallel step puts collectives between its kernels, and a kernel
+  // overlapped after one of those read its input before it landed
+  // (measured: the head after the last fold), so it keeps plain stream order.
+  p.pdl = c->m->tp_size == 1;
   if (W.slice) return launch_slice(W.type, pro, epi, p, W.g, W.grid, c->stream);
   return launch_ring(W.type, pro, epi, p, c->stream);
 }
@@ -1115,7 +1222,7 @@ static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
     const PackedMat& W = L.qkv[i];
     GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
     p.x = c->x; p.norm_w = L.attn_norm; p.eps = mi.rms_eps;
-    p.out = c->q; p.nq = mi.n_head * mi.head_dim; p.nkv = mi.n_head_kv * mi.head_dim;
+    p.out = c->q; p.nq = c->m->loc.n_head * mi.head_dim; p.nkv = c->m->loc.n_head_kv * mi.head_dim;
     p.hd = mi.head_dim; p.n_ctx = c->n_ctx; p.kv_f16 = c->kv_f16;
     p.rope_cos = c->rope_cos; p.rope_sin = c->rope_sin; p.pos = c->pos_dev;
     p.kcache = kv_layer(c, c->kc, l); p.vcache = kv_layer(c, c->vc, l); p.row_base = L.qkv_base[i];
@@ -1196,7 +1303,7 @@ static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
   AttnParams ap;
   ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
   ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
-  ap.hd = mi.head_dim; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
+  ap.hd = mi.head_dim; ap.n_head = c->m->loc.n_head; ap.n_kv = c->m->loc.n_head_kv; ap.S_max = c->S_max;
   ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
   ap.scale = 1.0f / sqrtf((float)mi.head_dim);
   return run_attention(ap, c->attn_exact, c->stream);
@@ -1243,7 +1350,7 @@ static cudaError_t launch_q8_rows(const GemvParams& p, cudaStream_t s) {
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
   cfg.attrs = at;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, p);
@@ -1256,6 +1363,7 @@ static cudaError_t launch_head(foxcuda_context* c) {
   GemvParams p = gemv_base(H.type, H.dev, H.n_rows, H.K, H.nb, H.U);
   p.x = c->x; p.norm_w = m->out_norm; p.eps = m->info.rms_eps; p.out = c->logits;
   p.err = c->err_dev;
+  p.pdl = m->tp_size == 1;
   if (H.rows32) return launch_q8_rows(p, c->stream);
   return launch_ring(H.type, PRO_NORM, EPI_STORE, p, c->stream);
 }
@@ -1372,6 +1480,8 @@ static foxcuda_status check_err(foxcuda_context* c) {
 extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* tokens, size_t n,
                                        float* logits_out) {
   if (!c || !tokens || n == 0) return fail(FOXCUDA_ERR_ARG, "eval: nothing to evaluate");
+  if (c->m->tp_size > 1)
+    return fail(FOXCUDA_ERR_ARG, "eval: a tensor-parallel shard decodes through foxcuda_tp_*");
   const foxcuda_model_info& mi = c->m->info;
   if ((size_t)c->pos + n > c->n_ctx)
     return fail(FOXCUDA_ERR_ARG, "forward: %zu tokens past position %u would overrun the %u token context",
@@ -1420,6 +1530,8 @@ extern "C" foxcuda_status foxcuda_sampler_create(foxcuda_context* c, const foxcu
                                                  foxcuda_sampler** out) {
   if (!c || !out) return fail(FOXCUDA_ERR_ARG, "sampler: null argument");
   *out = nullptr;
+  if (c->m->tp_size > 1)
+    return fail(FOXCUDA_ERR_ARG, "sampler: a tensor-parallel shard picks through foxcuda_tp_*");
   foxcuda_sampler_config k;
   if (cfg) k = *cfg;
   else k = {0.8f, 40, 0.95f, 1.1f, 64, 0};  // upstream defaults, src/sample.c:21-30
@@ -1532,6 +1644,221 @@ extern "C" foxcuda_status foxcuda_generate(foxcuda_context* c, foxcuda_sampler* 
                                            size_t n, uint32_t* out) {
   if (!c || !s || !out || s->c != c || n == 0) return fail(FOXCUDA_ERR_ARG, "generate: bad argument");
   return decode_steps(c, s, token, n, out);
+}
+
+// ---------------------------------------------------------------------------
+// tensor-parallel decode steps (stream-ordered on the context's stream; the
+// caller puts its collectives on the same stream between them)
+
+extern "C" void* foxcuda_context_stream(foxcuda_context* c) { return c ? (void*)c->stream : nullptr; }
+
+extern "C" foxcuda_status foxcuda_tp_info(const foxcuda_model* m, foxcuda_tp_shape* out) {
+  if (!m || !out) return fail(FOXCUDA_ERR_ARG, "tp_info: null argument");
+  out->tp_rank = m->tp_rank;
+  out->tp_size = m->tp_size;
+  out->n_head = m->loc.n_head;
+  out->n_head_kv = m->loc.n_head_kv;
+  out->n_ff = m->loc.n_ff;
+  out->vocab_begin = m->vocab0;
+  out->n_vocab = m->loc.n_vocab;
+  out->o_blocks = m->o_blocks;
+  for (int k = 0; k < 8; ++k) out->ffn_blocks[k] = m->f_blocks_all[k];
+  auto nt = [](int t) -> uint32_t { return t == T_Q4_K ? 8 : t == T_Q6_K ? 4 : 1; };
+  out->o_terms = out->down_terms = 1;
+  if (m->finalized)
+    for (const LayerW& L : m->layers) {
+      out->o_terms = std::max(out->o_terms, nt(L.o.type));
+      out->down_terms = std::max(out->down_terms, nt(L.down.type));
+    }
+  return FOXCUDA_OK;
+}
+
+static foxcuda_status tp_check(foxcuda_context* c, uint32_t layer, bool need_layer) {
+  if (!c) return fail(FOXCUDA_ERR_ARG, "tp: null context");
+  if (need_layer && layer >= c->m->info.n_layer) return fail(FOXCUDA_ERR_ARG, "tp: layer %u", layer);
+  if (c->pos >= c->n_ctx) return fail(FOXCUDA_ERR_ARG, "tp: the %u token context is full", c->n_ctx);
+  cudaSetDevice(c->m->device);
+  return FOXCUDA_OK;
+}
+
+// Embedding of the token in device memory (set by foxcuda_tp_pick, or from
+// the host with token < n_vocab).
+extern "C" foxcuda_status foxcuda_tp_embed(foxcuda_context* c, int64_t token) {
+  foxcuda_status st = tp_check(c, 0, false);
+  if (st) return st;
+  const foxcuda_model_info& mi = c->m->info;
+  const size_t emb_rb = row_bytes(c->m->embd.type, mi.n_embd);
+  if (token >= 0) {
+    // the token travels as a launch argument: these calls do not wait for
+    // the device, so a staging word in host memory could be overwritten by
+    // the next call before its copy ran
+    if ((uint64_t)token >= mi.n_vocab) return fail(FOXCUDA_ERR_ARG, "tp: token outside the vocabulary");
+    embed_token_kernel<<<(mi.n_embd + 255) / 256, 256, 0, c->stream>>>(
+        c->m->embd.type, c->m->embd.dev, emb_rb, (int)mi.n_embd, (uint32_t)token, c->token_dev, c->x);
+  } else {
+    embed_kernel<<<(mi.n_embd + 255) / 256, 256, 0, c->stream>>>(c->m->embd.type, c->m->embd.dev, emb_rb,
+                                                                  (int)mi.n_embd, c->token_dev, c->x);
+  }
+  CK(cudaGetLastError(), "embed");
+  if (c->trace_on)
+    CK(cudaMemcpyAsync(c->trace, c->x, mi.n_embd * 4, cudaMemcpyDeviceToDevice, c->stream), "trace");
+  return FOXCUDA_OK;
+}
+
+// q|k|v rows and attention of this shard's heads
+extern "C" foxcuda_status foxcuda_tp_attention(foxcuda_context* c, uint32_t layer) {
+  foxcuda_status st = tp_check(c, layer, true);
+  if (st) return st;
+  CK(launch_qkv(c, layer), "tp qkv");
+  CK(launch_attn(c, layer), "tp attention");
+  return FOXCUDA_OK;
+}
+
+// which: 0 = the attention output (o projection input), 1 = the FFN hidden
+// vector (down projection input)
+extern "C" foxcuda_status foxcuda_tp_amax(foxcuda_context* c, int which, float* amax) {
+  foxcuda_status st = tp_check(c, 0, false);
+  if (st) return st;
+  if (!amax || (which != 0 && which != 1)) return fail(FOXCUDA_ERR_ARG, "tp_amax: bad argument");
+  const int n = which == 0 ? (int)(c->m->loc.n_head * c->m->info.head_dim) : (int)c->m->loc.n_ff;
+  amax_kernel<<<1, 1024, 0, c->stream>>>(which == 0 ? c->att : c->h, n, amax);
+  CK(cudaGetLastError(), "tp amax");
+  return FOXCUDA_OK;
+}
+
+template <int T>
+static cudaError_t launch_terms_t(const GemvParams& p, bool gscale, cudaStream_t s) {
+  if (gscale) return launch_gemv_t<T, PRO_GSCALE, EPI_TERMS>(p, s);
+  return launch_gemv_t<T, PRO_VEC, EPI_TERMS>(p, s);
+}
+
+// This shard's block terms of the o (which 0) or down (which 1) projection:
+// terms[row * stride + j] for its column blocks. Ternary shards quantise with
+// amax_all, the absmax over all shards; K-quant shards use their own 256-block
+// scales, which are the unsplit vector's.
+extern "C" foxcuda_status foxcuda_tp_terms(foxcuda_context* c, uint32_t layer, int which,
+                                           const float* amax_all, float* terms, uint32_t stride) {
+  foxcuda_status st = tp_check(c, layer, true);
+  if (st) return st;
+  if (!terms || (which != 0 && which != 1)) return fail(FOXCUDA_ERR_ARG, "tp_terms: bad argument");
+  const PackedMat& W = which == 0 ? c->m->layers[layer].o : c->m->layers[layer].down;
+  const int nt = W.type == T_Q4_K ? 8 : W.type == T_Q6_K ? 4 : 1;
+  if (stride < (uint32_t)(W.nb * nt)) return fail(FOXCUDA_ERR_ARG, "tp_terms: stride %u below %d", stride, W.nb * nt);
+  const bool tern = W.type == T_TQ1_0 || W.type == T_TQ2_0;
+  if (tern && !amax_all) return fail(FOXCUDA_ERR_ARG, "tp_terms: ternary shards need the global absmax");
+  GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
+  p.x = which == 0 ? c->att : c->h;
+  p.xq_scale = amax_all;
+  p.out = terms;
+  p.terms_stride = (int)stride;
+  cudaError_t e;
+  switch (W.type) {
+    case T_TQ1_0: e = launch_terms_t<T_TQ1_0>(p, true, c->stream); break;
+    case T_TQ2_0: e = launch_terms_t<T_TQ2_0>(p, true, c->stream); break;
+    case T_Q4_K: e = launch_terms_t<T_Q4_K>(p, false, c->stream); break;
+    case T_Q6_K: e = launch_terms_t<T_Q6_K>(p, false, c->stream); break;
+    default: return fail(FOXCUDA_ERR_UNSUPPORTED, "tp_terms: type %d", W.type);
+  }
+  CK(e, "tp terms");
+  return FOXCUDA_OK;
+}
+
+// Fold the gathered terms ([tp][n_embd][stride], shard order) into the
+// residual stream.
+extern "C" foxcuda_status foxcuda_tp_fold(foxcuda_context* c, uint32_t layer, int which,
+                                          const float* gathered, uint32_t stride,
+                                          const float* amax_all) {
+  foxcuda_status st = tp_check(c, layer, true);
+  if (st) return st;
+  if (!gathered || (which != 0 && which != 1)) return fail(FOXCUDA_ERR_ARG, "tp_fold: bad argument");
+  const foxcuda_model* m = c->m;
+  const PackedMat& W = which == 0 ? m->layers[layer].o : m->layers[layer].down;
+  const int nt = W.type == T_Q4_K ? 8 : W.type == T_Q6_K ? 4 : 1;
+  FoldParams f;
+  memset(&f, 0, sizeof f);
+  f.g = gathered;
+  f.tp = m->tp_size;
+  f.rows = (int)m->info.n_embd;
+  f.stride = (int)stride;
+  f.ternary = W.type == T_TQ1_0 || W.type == T_TQ2_0;
+  for (int k = 0; k < m->tp_size; ++k) {
+    const int blocks = which == 0 ? (int)m->o_blocks : (int)m->f_blocks_all[k];
+    f.count[k] = blocks * nt;
+    if ((uint32_t)f.count[k] > stride) return fail(FOXCUDA_ERR_ARG, "tp_fold: stride %u below %d", stride, f.count[k]);
+  }
+  f.amax = amax_all;
+  f.x = c->x;
+  if (f.ternary && !amax_all) return fail(FOXCUDA_ERR_ARG, "tp_fold: ternary shards need the global absmax");
+  fold_kernel<<<(f.rows + 255) / 256, 256, 0, c->stream>>>(f);
+  CK(cudaGetLastError(), "tp fold");
+  if (c->trace_on && which == 1)  // the layer's output, as foxcuda_context_hidden reads it
+    CK(cudaMemcpyAsync(c->trace + (size_t)(layer + 1) * m->info.n_embd, c->x, m->info.n_embd * 4,
+                       cudaMemcpyDeviceToDevice, c->stream), "trace");
+  return FOXCUDA_OK;
+}
+
+// gate|up rows of this shard's FFN blocks, SwiGLU into the hidden vector
+extern "C" foxcuda_status foxcuda_tp_ffn(foxcuda_context* c, uint32_t layer) {
+  foxcuda_status st = tp_check(c, layer, true);
+  if (st) return st;
+  CK(launch_gateup(c, layer), "tp gate|up");
+  return FOXCUDA_OK;
+}
+
+// Head rows of this shard and their best logit as {value, global index bits}.
+extern "C" foxcuda_status foxcuda_tp_head(foxcuda_context* c, float* best) {
+  foxcuda_status st = tp_check(c, 0, false);
+  if (st) return st;
+  if (!best) return fail(FOXCUDA_ERR_ARG, "tp_head: null output");
+  CK(launch_head(c), "tp head");
+  tp_argmax_kernel<<<1, 1024, 0, c->stream>>>(c->logits, (int)c->m->loc.n_vocab, c->m->vocab0, best);
+  CK(cudaGetLastError(), "tp argmax");
+  return FOXCUDA_OK;
+}
+
+// The next token from all shards' {value, index} pairs (on the device), the
+// position advanced. The token stays in device memory for foxcuda_tp_embed
+// (token -1) and is kept in the context's output ring.
+extern "C" foxcuda_status foxcuda_tp_pick(foxcuda_context* c, const float* pairs) {
+  foxcuda_status st = tp_check(c, 0, false);
+  if (st) return st;
+  if (!pairs) return fail(FOXCUDA_ERR_ARG, "tp_pick: null pairs");
+  tp_pick_kernel<<<1, 32, 0, c->stream>>>(pairs, c->m->tp_size, c->token_dev, c->ring, (int)c->n_ctx,
+                                          c->pos_dev);
+  advance_kernel<<<1, 32, 0, c->stream>>>(c->pos_dev, 1);
+  CK(cudaGetLastError(), "tp pick");
+  c->pos += 1;
+  return FOXCUDA_OK;
+}
+
+// Position advance without a pick (prompt tokens) and reading the picks back.
+extern "C" foxcuda_status foxcuda_tp_advance(foxcuda_context* c) {
+  foxcuda_status st = tp_check(c, 0, false);
+  if (st) return st;
+  advance_kernel<<<1, 32, 0, c->stream>>>(c->pos_dev, 1);
+  CK(cudaGetLastError(), "tp advance");
+  c->pos += 1;
+  return FOXCUDA_OK;
+}
+
+// This shard's logits of the last head evaluation (n floats to host).
+extern "C" foxcuda_status foxcuda_context_logits(foxcuda_context* c, float* out, size_t n) {
+  if (!c || !out) return fail(FOXCUDA_ERR_ARG, "logits: null argument");
+  if (n > c->m->loc.n_vocab) return fail(FOXCUDA_ERR_ARG, "logits: %zu above %u", n, c->m->loc.n_vocab);
+  cudaSetDevice(c->m->device);
+  CK(cudaStreamSynchronize(c->stream), "logits sync");
+  CK(cudaMemcpy(out, c->logits, n * 4, cudaMemcpyDeviceToHost), "logits copy");
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_tp_tokens(foxcuda_context* c, uint32_t first_pos, size_t n,
+                                            uint32_t* out) {
+  if (!c || !out) return fail(FOXCUDA_ERR_ARG, "tp_tokens: bad argument");
+  cudaSetDevice(c->m->device);
+  CK(cudaStreamSynchronize(c->stream), "tp sync");
+  for (size_t i = 0; i < n; ++i)
+    CK(cudaMemcpy(out + i, c->ring + (first_pos + i) % c->n_ctx, 4, cudaMemcpyDeviceToHost), "tp tokens");
+  return FOXCUDA_OK;
 }
 
 // ---------------------------------------------------------------------------

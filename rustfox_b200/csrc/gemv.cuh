@@ -16,10 +16,16 @@
 //
 // Prologues fold upstream's per-call work into every CTA (each recomputes it
 // from the L2-resident input vector, so no extra launch or grid sync):
-//   PRO_PREQ  int8 activations and scale(s) given
-//   PRO_VEC   float vector -> upstream's quantiser
-//   PRO_NORM  residual -> RMSNorm (double sum of squares, src/ops.c:7-22) ->
-//             upstream's quantiser
+//   PRO_PREQ    int8 activations and scale(s) given
+//   PRO_VEC     float vector -> upstream's quantiser
+//   PRO_NORM    residual -> RMSNorm (double sum of squares, src/ops.c:7-22) ->
+//               upstream's quantiser
+//   PRO_GSCALE  a tensor-parallel shard of a float vector, quantised with the
+//               absmax of the whole vector (xq_scale[0], from all shards), so
+//               its int8 values are the ones the unsplit vector gets
+// EPI_TERMS (tensor-parallel row shards) writes the per-block float terms
+// instead of folding them; the shards' terms are gathered and folded in
+// upstream's block order by fold_kernel.
 // Epilogues: store; residual add (src/ops.c:50-54); RoPE on adjacent pairs
 // (src/ops.c:56-73) + K/V cache write for the fused q|k|v matrix; SwiGLU
 // (src/ops.c:41-48) for the interleaved gate|up matrix.
@@ -30,8 +36,8 @@
 
 namespace fox {
 
-enum Pro { PRO_PREQ = 0, PRO_VEC = 1, PRO_NORM = 2 };
-enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3 };
+enum Pro { PRO_PREQ = 0, PRO_VEC = 1, PRO_NORM = 2, PRO_GSCALE = 3 };
+enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_TERMS = 4 };
 
 // Largest CTA per type: 64 activation registers plus a prefetched unit must
 // fit the register file at this width.
@@ -61,6 +67,11 @@ struct GemvParams {
   // ring mode: units stream through ring_slots shared-memory slots of
   // slot_bytes each, starting ring_off bytes into dynamic shared memory
   int ring_slots, slot_bytes, ring_off;
+  // EPI_TERMS: row r's block terms go to out[r * terms_stride + i]
+  int terms_stride;
+  // launch with programmatic stream serialisation (overlap the predecessor);
+  // only where every predecessor in the stream is a kernel of this chain
+  int pdl;
 };
 
 // ---------------------------------------------------------------------------
@@ -395,9 +406,14 @@ gemv_kernel(const GemvParams p) {
       act_scale = p.xq_scale[0];
     } else {
       // upstream src/gemv.c:11-42: one absmax over the whole vector
-      float am = 0.0f;
-      for (int i = tid; i < K; i += nth) am = absmax_acc(am, xs[i]);
-      const float amax = block_reduce<float>(am, (float*)red, OpMax(), 0.0f);
+      float amax;
+      if (PRO == PRO_GSCALE) {
+        amax = p.xq_scale[0];
+      } else {
+        float am = 0.0f;
+        for (int i = tid; i < K; i += nth) am = absmax_acc(am, xs[i]);
+        amax = block_reduce<float>(am, (float*)red, OpMax(), 0.0f);
+      }
       const bool nz = amax > 0.0f;
       const float inv = nz ? __fdiv_rn(127.0f, amax) : 0.0f;
       act_scale = nz ? __fdiv_rn(amax, 127.0f) : 0.0f;
@@ -466,6 +482,15 @@ gemv_kernel(const GemvParams p) {
   const int prow = tid / nb, pcol = (tid - prow * nb) * Tr::NT;
   // rows of unit u in upstream's order from the parked terms, then the epilogue
   auto finish = [&](int u, int ru) {
+    if (EPI == EPI_TERMS) {
+      const int tr = nb * Tr::NT;
+      for (int i = tid; i < ru * tr; i += nth) {
+        const int r = i / tr, c = i - r * tr;
+        p.out[(size_t)(u * U + r) * p.terms_stride + c] = part[r * rstride + c];
+      }
+      __syncthreads();
+      return;
+    }
     float v = 0.0f;
     if (tid < ru) {
       // upstream order: blocks in order, terms of a block in order, from 0.0f

@@ -65,6 +65,17 @@ __global__ void embed_kernel(int type, const uint8_t* __restrict__ table, size_t
     x[e] = dequant_elem(type, row, e);
 }
 
+// The same, for a token given as a launch argument (kept in *token for the
+// next step): nothing in host memory is read after the launch.
+__global__ void embed_token_kernel(int type, const uint8_t* __restrict__ table, size_t row_bytes,
+                                   int n_embd, uint32_t tok, uint32_t* token,
+                                   float* __restrict__ x) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) *token = tok;
+  const uint8_t* row = table + (size_t)tok * row_bytes;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_embd; e += gridDim.x * blockDim.x)
+    x[e] = dequant_elem(type, row, e);
+}
+
 __global__ void advance_kernel(int* pos, int by) {
   if (threadIdx.x == 0 && blockIdx.x == 0) *pos += by;
 }
@@ -744,6 +755,91 @@ topk_sample_kernel(SamplerDev* st, float* logits, int n_vocab, int k, float temp
   }
   __syncthreads();
   if (accept && tid == 0) accept_token(st, st->token);
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-parallel pieces. Upstream has one process and no exchange; these are
+// the steps around the exchanges of the sharded decode step, each written so
+// the sharded result equals the unsharded one bit for bit.
+
+// |x| max of a vector, one CTA (the shard's contribution to the global absmax
+// of upstream's quantiser, src/gemv.c:20-40)
+__global__ void __launch_bounds__(1024) amax_kernel(const float* __restrict__ v, int n, float* out) {
+  __shared__ float red[32];
+  float am = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) am = absmax_acc(am, v[i]);
+  am = block_reduce<float>(am, red, OpMax(), 0.0f);
+  if (threadIdx.x == 0) out[0] = am;
+}
+
+// Row sums of gathered block terms in upstream's block order: shard k holds
+// the column blocks after those of shards 0..k-1, so rank order then block
+// order is the global block order (src/gemv.c:86-95, ternary.c:236-244).
+// Then the row scale (ternary: the global absmax / 127) and the residual add.
+struct FoldParams {
+  const float* g;      // [tp][rows][stride] gathered terms
+  int tp, rows, stride, ternary;
+  int count[8];        // terms per row of each shard
+  const float* amax;   // ternary: global absmax
+  float* x;            // residual, += the row values
+};
+
+__global__ void fold_kernel(const FoldParams f) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= f.rows) return;
+  float acc = 0.0f;
+  for (int k = 0; k < f.tp; ++k) {
+    const float* t = f.g + ((size_t)k * f.rows + r) * f.stride;
+    for (int j = 0; j < f.count[k]; ++j) acc = __fadd_rn(acc, t[j]);
+  }
+  float v = acc;
+  if (f.ternary) {
+    const float amax = *f.amax;
+    v = __fmul_rn(acc, amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f);
+  }
+  f.x[r] = __fadd_rn(f.x[r], v);
+}
+
+// This shard's best logit (first strict maximum, ties to the lowest index,
+// src/sample.c:147-153) as {value, global index bits}.
+__global__ void __launch_bounds__(1024) tp_argmax_kernel(const float* __restrict__ logits, int n,
+                                                         uint32_t offset, float* best) {
+  __shared__ float sv[32];
+  __shared__ uint32_t si[32];
+  float bv = -CUDART_INF_F;
+  uint32_t bi = 0xffffffffu;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    if (better(logits[i], offset + i, bv, bi)) { bv = logits[i]; bi = offset + i; }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
+    best[0] = bv;
+    best[1] = __uint_as_float(bi);
+  }
+}
+
+// The winner over all shards' {value, index} pairs becomes the next token.
+__global__ void tp_pick_kernel(const float* __restrict__ pairs, int tp, uint32_t* token,
+                               uint32_t* ring, int ring_cap, const int* pos) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  float bv = -CUDART_INF_F;
+  uint32_t bi = 0xffffffffu;
+  for (int k = 0; k < tp; ++k) {
+    const float v = pairs[2 * k];
+    const uint32_t i = __float_as_uint(pairs[2 * k + 1]);
+    if (better(v, i, bv, bi)) { bv = v; bi = i; }
+  }
+  if (bi == 0xffffffffu) bi = 0;  // all NaN: upstream keeps index 0
+  token[0] = bi;
+  if (ring) ring[(*pos) % ring_cap] = bi;
 }
 
 }  // namespace fox

@@ -1,0 +1,119 @@
+"""Tensor-parallel greedy decode: one process per GPU, collectives over
+torch.distributed (NCCL on the GPUs).
+
+Upstream RustFox runs one process (src/threadpool.c) and has no multi-GPU
+path. The sharded step follows the library's tensor-parallel steps
+(include/foxcuda.h, foxcuda_tp_*): column-parallel q/k/v, attention, gate|up and
+head on each shard's rows; for the row-parallel o and down projections a
+max-allreduce of one float (the absmax upstream's quantiser takes over the
+whole vector, src/gemv.c:20-40), an all-gather of the per-block float terms,
+and a fold in upstream's block order. Every shard therefore holds the same
+residual stream as the unsharded decode, bit for bit, and the picked tokens
+are the unsharded greedy tokens (first strict maximum, src/sample.c:147-153).
+
+All library steps and collectives go on the context's CUDA stream, in the
+same order on every rank.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import api
+
+
+class TPShape(C.Structure):
+    _fields_ = [("tp_rank", C.c_int32), ("tp_size", C.c_int32), ("n_head", C.c_uint32),
+                ("n_head_kv", C.c_uint32), ("n_ff", C.c_uint32), ("vocab_begin", C.c_uint32),
+                ("n_vocab", C.c_uint32), ("o_blocks", C.c_uint32), ("ffn_blocks", C.c_uint32 * 8),
+                ("o_terms", C.c_uint32), ("down_terms", C.c_uint32)]
+
+
+def shape(model: api.Model) -> TPShape:
+    s = TPShape()
+    api._check(api.lib().foxcuda_tp_info(model.h, C.byref(s)))
+    return s
+
+
+class TPContext:
+    """One shard's decode state. `group` is the torch.distributed process
+    group spanning the shards (default: the world)."""
+
+    def __init__(self, model: api.Model, n_ctx: int, kv: str = "f16", attn_exact: bool = False,
+                 group=None):
+        import torch
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.model = model
+        self.ctx = api.Context(model, n_ctx, kv, attn_exact)
+        self.shape = shape(model)
+        self.world = self.shape.tp_size
+        info = model.info
+        self.n_layer, self.n_embd = int(info["n_layer"]), int(info["n_embd"])
+        dev = torch.device("cuda", model.device)
+        self.stream = torch.cuda.ExternalStream(api.lib().foxcuda_context_stream(self.ctx.h), device=dev)
+        # terms per row: o shards have o_blocks blocks, down shards up to the
+        # largest FFN share; 1 term per ternary block, 8 per Q4_K, 4 per Q6_K
+        self.stride_o = self.shape.o_blocks * self.shape.o_terms
+        self.stride_d = max(self.shape.ffn_blocks[:self.world]) * self.shape.down_terms
+        f = dict(dtype=torch.float32, device=dev)
+        self.amax = torch.zeros(2, **f)
+        self.terms_o = torch.zeros(self.n_embd * self.stride_o, **f)
+        self.terms_d = torch.zeros(self.n_embd * self.stride_d, **f)
+        self.gath_o = torch.zeros(self.world * self.n_embd * self.stride_o, **f)
+        self.gath_d = torch.zeros(self.world * self.n_embd * self.stride_d, **f)
+        self.best = torch.zeros(2, **f)
+        self.pairs = torch.zeros(2 * self.world, **f)
+
+    @staticmethod
+    def _p(t, off=0):
+        return C.c_void_p(t.data_ptr() + off * t.element_size())
+
+    def _row_parallel(self, layer: int, which: int):
+        import torch
+        L, dist = api.lib(), self.dist
+        amax = self.amax[which:which + 1]
+        terms, gath, stride = ((self.terms_o, self.gath_o, self.stride_o) if which == 0
+                               else (self.terms_d, self.gath_d, self.stride_d))
+        api._check(L.foxcuda_tp_amax(self.ctx.h, which, self._p(amax)))
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        api._check(L.foxcuda_tp_terms(self.ctx.h, layer, which, self._p(amax), self._p(terms), stride))
+        dist.all_gather_into_tensor(gath, terms, group=self.group)
+        api._check(L.foxcuda_tp_fold(self.ctx.h, layer, which, self._p(gath), stride, self._p(amax)))
+
+    def step(self, token: int | None, pick: bool):
+        """One token through the shards: token from the host, or (None) the
+        last pick on the device. With pick the next token is chosen."""
+        import torch
+        L = api.lib()
+        with torch.cuda.stream(self.stream):
+            api._check(L.foxcuda_tp_embed(self.ctx.h, -1 if token is None else int(token)))
+            for l in range(self.n_layer):
+                api._check(L.foxcuda_tp_attention(self.ctx.h, l))
+                self._row_parallel(l, 0)
+                api._check(L.foxcuda_tp_ffn(self.ctx.h, l))
+                self._row_parallel(l, 1)
+            if pick:
+                api._check(L.foxcuda_tp_head(self.ctx.h, self._p(self.best)))
+                self.dist.all_gather_into_tensor(self.pairs, self.best, group=self.group)
+                api._check(L.foxcuda_tp_pick(self.ctx.h, self._p(self.pairs)))
+            else:
+                api._check(L.foxcuda_tp_advance(self.ctx.h))
+
+    def generate(self, prompt, n_gen: int) -> np.ndarray:
+        """Greedy decode (no repeat penalty): the prompt, then n_gen picks."""
+        prompt = [int(t) for t in prompt]
+        start = self.ctx.pos
+        for i, t in enumerate(prompt):
+            self.step(t, pick=(i + 1 == len(prompt)))
+        for _ in range(n_gen - 1):
+            self.step(None, pick=True)
+        out = np.zeros(n_gen, dtype=np.uint32)
+        first = start + len(prompt) - 1
+        api._check(api.lib().foxcuda_tp_tokens(self.ctx.h, first, n_gen,
+                                               out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def close(self):
+        self.ctx.close()
