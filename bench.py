@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", action="store_true",
+                    help="one sequence split over the GPUs (tensor parallel, strong scaling) "
+                         "instead of one replica per GPU")
     return ap.parse_args()
 
 
@@ -328,10 +331,64 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_tp(args):
+    """Greedy decode (no repeat penalty) of one sequence sharded over the
+    ranks (rustfox_b200/tp.py); time per token is the max over ranks of the
+    CUDA-event time on each rank's context stream."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import rustfox_b200 as rf
+    from rustfox_b200 import synth
+    from rustfox_b200.tp import TPContext
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=10))
+    cfg = synth.CONFIGS[args.config]
+    host = synth.generate(cfg)
+    model = rf.Model.from_synthetic(host, device=local, tp_rank=rank, tp_size=world)
+    del host
+    n_ctx = args.prompt + args.warmup + args.steps + 8
+    ctx = TPContext(model, n_ctx, kv="f16")
+    prompt = synth.random_prompt(cfg, args.prompt, seed=1)
+    ctx.generate(prompt, max(3, args.warmup), graphs=True)  # captures the step graph
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ctx.stream)
+    ctx.replay(args.steps)
+    e1.record(ctx.stream)
+    torch.cuda.synchronize()
+    dt = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+    dt = float(dt.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": args.steps / dt, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "i8 x ternary -> i32, f32", "data": "synthetic (seeded random-init weights)",
+            "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} greedy decode, one "
+                                   f"sequence over {world} GPU(s)", "prompt": args.prompt,
+                       "kv_cache": "f16", "parallelism": f"tp{world}",
+                       "collectives": "torch.distributed NCCL per row-parallel GEMV (4 per layer), "
+                                      "the whole step replayed as one CUDA graph"}}),
+              flush=True)
+    ctx.close()
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.tp:
+        run_tp(args)
     else:
         run_ours(args)
 

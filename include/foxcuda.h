@@ -264,6 +264,9 @@ foxcuda_status foxcuda_tp_head(foxcuda_context *c, float *best);
 foxcuda_status foxcuda_tp_pick(foxcuda_context *c, const float *pairs);
 foxcuda_status foxcuda_tp_advance(foxcuda_context *c);
 foxcuda_status foxcuda_tp_tokens(foxcuda_context *c, uint32_t first_pos, size_t n, uint32_t *out);
+/* the host's position counter re-read from the device (after replaying a
+ * captured foxcuda_tp_* step, which advances only the device's) */
+foxcuda_status foxcuda_context_sync_position(foxcuda_context *c);
 /* this shard's logits of its last head evaluation (n <= its vocabulary rows) */
 foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
 

@@ -113,6 +113,7 @@ _PROTOS = {
     "foxcuda_tp_advance": (_st, [_vp]),
     "foxcuda_tp_tokens": (_st, [_vp, C.c_uint32, _sz, _vp]),
     "foxcuda_context_logits": (_st, [_vp, _vp, _sz]),
+    "foxcuda_context_sync_position": (_st, [_vp]),
 }
 
 KIND_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "advance", "head", "pick"]

@@ -1051,6 +1051,7 @@ struct foxcuda_context {
   double last_seconds = 0.0;
   std::vector<void*> allocs;
   std::vector<std::pair<cudaEvent_t, int>>* prof = nullptr;  // diagnostics
+  bool tp_steps = false;  // driven through foxcuda_tp_* (collectives between kernels)
 };
 
 struct foxcuda_sampler {
@@ -1208,7 +1209,7 @@ static cudaError_t launch_mat(foxcuda_context* c, const PackedMat& W, int pro, i
   // tensor-parallel step puts collectives between its kernels, and a kernel
   // overlapped after one of those read its input before it landed
   // (measured: the head after the last fold), so it keeps plain stream order.
-  p.pdl = c->m->tp_size == 1;
+  p.pdl = c->m->tp_size == 1 && !c->tp_steps;
   if (W.slice) return launch_slice(W.type, pro, epi, p, W.g, W.grid, c->stream);
   return launch_ring(W.type, pro, epi, p, c->stream);
 }
@@ -1363,7 +1364,7 @@ static cudaError_t launch_head(foxcuda_context* c) {
   GemvParams p = gemv_base(H.type, H.dev, H.n_rows, H.K, H.nb, H.U);
   p.x = c->x; p.norm_w = m->out_norm; p.eps = m->info.rms_eps; p.out = c->logits;
   p.err = c->err_dev;
-  p.pdl = m->tp_size == 1;
+  p.pdl = m->tp_size == 1 && !c->tp_steps;
   if (H.rows32) return launch_q8_rows(p, c->stream);
   return launch_ring(H.type, PRO_NORM, EPI_STORE, p, c->stream);
 }
@@ -1678,6 +1679,7 @@ static foxcuda_status tp_check(foxcuda_context* c, uint32_t layer, bool need_lay
   if (need_layer && layer >= c->m->info.n_layer) return fail(FOXCUDA_ERR_ARG, "tp: layer %u", layer);
   if (c->pos >= c->n_ctx) return fail(FOXCUDA_ERR_ARG, "tp: the %u token context is full", c->n_ctx);
   cudaSetDevice(c->m->device);
+  c->tp_steps = true;
   return FOXCUDA_OK;
 }
 
@@ -1838,6 +1840,17 @@ extern "C" foxcuda_status foxcuda_tp_advance(foxcuda_context* c) {
   advance_kernel<<<1, 32, 0, c->stream>>>(c->pos_dev, 1);
   CK(cudaGetLastError(), "tp advance");
   c->pos += 1;
+  return FOXCUDA_OK;
+}
+
+// The host's position counter after graph replays advanced the device's.
+extern "C" foxcuda_status foxcuda_context_sync_position(foxcuda_context* c) {
+  if (!c) return fail(FOXCUDA_ERR_ARG, "sync_position: null context");
+  cudaSetDevice(c->m->device);
+  int p = 0;
+  CK(cudaStreamSynchronize(c->stream), "sync");
+  CK(cudaMemcpy(&p, c->pos_dev, 4, cudaMemcpyDeviceToHost), "position");
+  c->pos = (uint32_t)p;
   return FOXCUDA_OK;
 }
 

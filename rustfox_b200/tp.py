@@ -70,16 +70,25 @@ class TPContext:
     def _p(t, off=0):
         return C.c_void_p(t.data_ptr() + off * t.element_size())
 
+    def _allreduce_max(self, t):
+        if self.world > 1:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX, group=self.group)
+
+    def _all_gather(self, out, inp):
+        if self.world > 1:
+            self.dist.all_gather_into_tensor(out, inp, group=self.group)
+        else:
+            out.copy_(inp)
+
     def _row_parallel(self, layer: int, which: int):
-        import torch
-        L, dist = api.lib(), self.dist
+        L = api.lib()
         amax = self.amax[which:which + 1]
         terms, gath, stride = ((self.terms_o, self.gath_o, self.stride_o) if which == 0
                                else (self.terms_d, self.gath_d, self.stride_d))
         api._check(L.foxcuda_tp_amax(self.ctx.h, which, self._p(amax)))
-        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        self._allreduce_max(amax)
         api._check(L.foxcuda_tp_terms(self.ctx.h, layer, which, self._p(amax), self._p(terms), stride))
-        dist.all_gather_into_tensor(gath, terms, group=self.group)
+        self._all_gather(gath, terms)
         api._check(L.foxcuda_tp_fold(self.ctx.h, layer, which, self._p(gath), stride, self._p(amax)))
 
     def step(self, token: int | None, pick: bool):
@@ -96,18 +105,48 @@ class TPContext:
                 self._row_parallel(l, 1)
             if pick:
                 api._check(L.foxcuda_tp_head(self.ctx.h, self._p(self.best)))
-                self.dist.all_gather_into_tensor(self.pairs, self.best, group=self.group)
+                self._all_gather(self.pairs, self.best)
                 api._check(L.foxcuda_tp_pick(self.ctx.h, self._p(self.pairs)))
             else:
                 api._check(L.foxcuda_tp_advance(self.ctx.h))
 
-    def generate(self, prompt, n_gen: int) -> np.ndarray:
-        """Greedy decode (no repeat penalty): the prompt, then n_gen picks."""
+    def capture(self):
+        """Record one decode step fed by the last pick (library kernels and the
+        NCCL collectives) as a CUDA graph. Its inputs are all on the device
+        (token, position), so each replay is the next step. Call after at
+        least one eager step (attributes set, communicators created)."""
+        import torch
+        self.graph = torch.cuda.CUDAGraph()
+        pos = self.ctx.pos
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.step(None, pick=True)
+        # capture does not run the step: the host counter goes back
+        self.ctx_pos_fix(pos)
+
+    def ctx_pos_fix(self, pos=None):
+        api._check(api.lib().foxcuda_context_sync_position(self.ctx.h))
+
+    def replay(self, n: int):
+        for _ in range(n):
+            self.graph.replay()
+        self.ctx_pos_fix()
+
+    def generate(self, prompt, n_gen: int, graphs: bool = False) -> np.ndarray:
+        """Greedy decode (no repeat penalty): the prompt, then n_gen picks;
+        with graphs the steps after the first two replay a captured step."""
         prompt = [int(t) for t in prompt]
         start = self.ctx.pos
         for i, t in enumerate(prompt):
             self.step(t, pick=(i + 1 == len(prompt)))
-        for _ in range(n_gen - 1):
+        rest = n_gen - 1
+        if graphs and rest > 1:
+            self.step(None, pick=True)
+            rest -= 1
+            if getattr(self, "graph", None) is None:
+                self.capture()
+            self.replay(rest)
+            rest = 0
+        for _ in range(rest):
             self.step(None, pick=True)
         out = np.zeros(n_gen, dtype=np.uint32)
         first = start + len(prompt) - 1

@@ -199,10 +199,26 @@ def test_two_shards_equal_the_unsharded_decode():
     procs = [ctx.Process(target=run_rank, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=600) for _ in range(2))
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    import queue
+    import time
+    res, t0 = {}, time.time()
+    try:
+        while len(res) < 2:
+            try:
+                r, out = q.get(timeout=2)
+                res[r] = out
+            except queue.Empty:
+                dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+                assert not dead, f"a rank exited with {dead}"
+                assert time.time() - t0 < 600, "ranks did not finish in time"
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
     assert res[0]["tokens"] == res[1]["tokens"]
     om = O.OracleModel(synth.generate(CFG))
     with O.exp_mode(True):

@@ -27,7 +27,7 @@ N_GEN = 32
 N_CTX = 96
 
 
-def run_rank(rank, world, port, cfg, kv, exact, out_q):
+def run_rank(rank, world, port, cfg, kv, exact, graphs, out_q):
     import datetime
     import torch.distributed as dist
     import rustfox_b200 as rf
@@ -38,7 +38,7 @@ def run_rank(rank, world, port, cfg, kv, exact, out_q):
     try:
         m = rf.Model.from_synthetic(synth.generate(cfg), device=rank, tp_rank=rank, tp_size=world)
         ctx = TPContext(m, N_CTX, kv=kv, attn_exact=exact)
-        toks = ctx.generate(PROMPT, N_GEN)
+        toks = ctx.generate(PROMPT, N_GEN, graphs=graphs)
         torch.cuda.synchronize()
         ctx.close()
         m.close()
@@ -47,28 +47,57 @@ def run_rank(rank, world, port, cfg, kv, exact, out_q):
         dist.destroy_process_group()
 
 
-def _tp_tokens(cfg, kv, exact, world=2):
+def _free_port() -> int:
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tp_tokens(cfg, kv, exact, graphs=False, world=2, limit_s=240):
+    """Runs the ranks as child processes; fails as soon as one of them exits
+    abnormally (its peers would otherwise wait in a collective) and kills
+    them all after limit_s."""
+    import queue
+    import time
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + (os.getpid() + 17 * world) % 900
-    procs = [ctx.Process(target=run_rank, args=(r, world, port, cfg, kv, exact, q)) for r in range(world)]
+    port = _free_port()
+    procs = [ctx.Process(target=run_rank, args=(r, world, port, cfg, kv, exact, graphs, q))
+             for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=900) for _ in range(world))
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    res, t0 = {}, time.time()
+    try:
+        while len(res) < world:
+            try:
+                r, toks = q.get(timeout=2)
+                res[r] = toks
+            except queue.Empty:
+                dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+                assert not dead, f"a rank exited with {dead}"
+                assert time.time() - t0 < limit_s, "ranks did not finish in time"
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
     for r in range(1, world):
         assert res[r] == res[0]
     return np.array(res[0], dtype=np.uint32)
 
 
 @pytest.mark.parametrize("cfg", [CFG, CFG_TQ2], ids=["tq1", "tq2"])
-@pytest.mark.parametrize("kv,exact", [("f32", True), ("f16", False)], ids=["parity", "production"])
-def test_two_shards_equal_one_gpu(cfg, kv, exact):
+@pytest.mark.parametrize("kv,exact,graphs", [("f32", True, False), ("f16", False, False),
+                                             ("f16", False, True)],
+                         ids=["parity", "production", "production-graph"])
+def test_two_shards_equal_one_gpu(cfg, kv, exact, graphs):
     import rustfox_b200 as rf
-    got = _tp_tokens(cfg, kv, exact)
+    got = _tp_tokens(cfg, kv, exact, graphs)
     host = synth.generate(cfg)
     m = rf.Model.from_synthetic(host)
     want = rf.greedy_generate(m, PROMPT, N_GEN, N_CTX, kv=kv, repeat_penalty=1.0, attn_exact=exact)
