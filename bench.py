@@ -67,12 +67,21 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
+TYPE_NAMES = {0: "F32", 1: "F16", 8: "Q8_0", 12: "Q4_K", 14: "Q6_K", 34: "TQ1_0", 35: "TQ2_0"}
+
+
 def workload(cfg, args) -> dict:
-    return {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} TQ1_0 linear + Q8_0 head, "
-                        f"batch-1 greedy decode after a {args.prompt}-id prompt",
+    lin = TYPE_NAMES[cfg.linear_type]
+    if cfg.attn_v_type and cfg.attn_v_type != cfg.linear_type:
+        lin += f" (attn_v {TYPE_NAMES[cfg.attn_v_type]})"
+    wb = cfg.weight_bytes()
+    gb = (wb["layers"] + wb["output"]) / 1e9
+    return {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} {lin} linear + "
+                        f"{TYPE_NAMES[cfg.output_type]} head, batch-1 greedy decode after a "
+                        f"{args.prompt}-id prompt",
             "prompt": args.prompt, "n_ctx": args.ctx, "kv_cache": "f16",
             "sampler": "greedy, repeat penalty 1.1 over 64",
-            "l2": "weights 1.18 GB per step > 126 MB L2: streamed from HBM, no flush"}
+            "l2": f"weights {gb:.2f} GB per step > 126 MB L2: streamed from HBM, no flush"}
 
 
 def measured_hbm_gbs():

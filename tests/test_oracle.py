@@ -8,6 +8,7 @@
    produced by the upstream library (tests/golden/make_golden.py), so the
    oracle stays pinned on machines without the upstream sources.
 """
+import ctypes as C
 import os
 
 import numpy as np
@@ -179,6 +180,45 @@ def test_upstream_builds_differ_by_float_order(tiny_model, tmp_path):
     assert 1e-3 < rel < 5e-2, rel
     assert int(np.argmax(l_par)) == int(np.argmax(l_fast))
     assert not np.array_equal(t_par, t_fast)
+
+
+@needs_ref
+@pytest.mark.parametrize("cfg", [
+    dict(temperature=0.0, repeat_penalty=1.1, repeat_last_n=64),
+    dict(temperature=0.0, repeat_penalty=1.0),
+    dict(temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.1, repeat_last_n=64, seed=1),
+    dict(temperature=1.3, top_k=0, top_p=1.0, repeat_penalty=1.0, seed=7),
+    dict(temperature=0.5, top_k=5, top_p=0.5, repeat_penalty=1.2, repeat_last_n=8, seed=12345),
+])
+def test_oracle_sampler_equals_upstream(cfg):
+    """The sampler restatement picks what upstream's fox_sampler_pick picks
+    (src/sample.c:47-195): penalty over the history, greedy or seeded
+    top-k / temperature / top-p draws, the rng advancing per draw."""
+    ref = O.RefLib()
+    n_vocab = 32000
+    full = dict(temperature=0.8, top_k=40, top_p=0.95, repeat_penalty=1.1, repeat_last_n=64, seed=0)
+    full.update(cfg)
+    scfg = O.SamplerConfig(full["temperature"], full["top_k"], full["top_p"],
+                           full["repeat_penalty"], full["repeat_last_n"], full["seed"])
+    up = ref.L.fox_sampler_create(C.byref(scfg), n_vocab)
+    ora = O.OracleSampler(n_vocab, **full)
+    rng = np.random.default_rng(5)
+    hist = rng.integers(0, n_vocab, 40)
+    for t in hist:
+        ref.L.fox_sampler_accept(up, int(t))
+        ora.accept(int(t))
+    try:
+        for step in range(60):
+            logits = rng.normal(0, 2, n_vocab).astype(np.float32)
+            logits[hist[step % len(hist)]] += 4.0  # make the penalty matter
+            out = np.zeros(1, dtype=np.uint32)
+            ref.L.fox_sampler_pick(up, O._ptr(logits.copy()), O._ptr(out))
+            got = ora.pick(logits.copy())
+            assert got == int(out[0]), (step, cfg)
+            ref.L.fox_sampler_accept(up, got)
+            ora.accept(got)
+    finally:
+        ref.L.fox_sampler_destroy(up)
 
 
 # ---- 3. against the golden fixtures ----------------------------------------
