@@ -291,7 +291,7 @@ def run_ours(args):
     tp = os.path.join(ROOT, "profiles", "roofline_traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
-            traffic = json.load(f).get("gate_up_dram_bytes_per_launch")
+            traffic = json.load(f).get(args.config, {}).get("gate_up_dram_bytes_per_launch")
 
     wb = cfg.weight_bytes()
     mean_pos = pos0 + args.steps / 2
@@ -321,7 +321,8 @@ def run_ours(args):
             "hbm_bytes_per_token": bytes_tok,
             "hbm_gbs_per_gpu": bytes_tok * per_gpu / 1e9,
             "hbm_frac_of_8tbs": bytes_tok * per_gpu / 1e9 / NOMINAL_HBM_GBS,
-            "roofline": {"bound": "hbm", "kernel": "fused gate|up TQ1_0 GEMV (+RMSNorm, SwiGLU)",
+            "roofline": {"bound": "hbm",
+                         "kernel": f"fused gate|up {TYPE_NAMES[cfg.linear_type]} GEMV (+RMSNorm, SwiGLU)",
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                          "algorithmic_bytes_per_launch": algo_bytes,
