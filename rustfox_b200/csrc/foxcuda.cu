@@ -63,6 +63,28 @@ static int current_sms() {
   return sm_count(d);
 }
 
+// The dynamic shared-memory opt-in is a property of a kernel on one device,
+// so each launcher keeps its high-water mark per device (`marks` has one
+// slot per device ordinal). The attribute only ever rises, under a lock, so
+// two threads cannot leave it below a mark that another thread relies on.
+constexpr int kMaxDevices = 64;
+static std::mutex g_smem_mu;
+
+template <typename K>
+static cudaError_t opt_in_smem(K kern, size_t smem, size_t* marks) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_smem_mu);
+  if (smem <= marks[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  marks[dev] = smem;
+  return cudaSuccess;
+}
+
 extern "C" foxcuda_status foxcuda_init(int device) {
   int n = 0;
   CK(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
@@ -94,14 +116,11 @@ static cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
   auto kern = gemv_kernel<T, PRO, EPI>;
   const int threads = (p.U * p.nb + 31) / 32 * 32;
   const size_t smem = gemv_smem_bytes(T, PRO, p.K, p.U, p.nb);
-  static size_t attr_set = 0;  // per instantiation
-  if (smem > 48 * 1024 && smem > attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = smem;
-  }
+  static size_t marks[kMaxDevices] = {};  // per instantiation
+  cudaError_t e = opt_in_smem(kern, smem, marks);
+  if (e != cudaSuccess) return e;
   int occ = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorInvalidConfiguration;
   const int units = (p.n_rows + p.U - 1) / p.U;
@@ -145,14 +164,11 @@ static cudaError_t launch_ring_t(GemvParams p, cudaStream_t s) {
   const size_t base = (gemv_smem_bytes(T, PRO, p.K, p.U, p.nb) + 15) / 16 * 16;
   const int R = (int)std::max<size_t>(2, std::min<size_t>(8, RING_BYTES / unit));
   const size_t smem = base + (size_t)R * unit + (size_t)R * 8;
-  static size_t attr_set = 0;  // per instantiation
-  if (smem > attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = smem;
-  }
+  static size_t marks[kMaxDevices] = {};  // per instantiation
+  cudaError_t e = opt_in_smem(kern, smem, marks);
+  if (e != cudaSuccess) return e;
   int occ = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem);
   if (e != cudaSuccess) return e;
   if (occ < 1) return cudaErrorInvalidConfiguration;
   const int units = (p.n_rows + p.U - 1) / p.U;
@@ -209,12 +225,9 @@ static int slice_unit_rows(int nb) {
 template <int T, int PRO, int EPI>
 static cudaError_t launch_slice_t(const GemvParams& p, const SliceGeom& g, int grid, cudaStream_t s) {
   auto kern = slice_kernel<T, PRO, EPI>;
-  static bool attr_set = false;  // per instantiation
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SLICE_MAX_SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static size_t marks[kMaxDevices] = {};  // per instantiation
+  cudaError_t e = opt_in_smem(kern, (size_t)SLICE_MAX_SMEM, marks);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(SLICE_THREADS);
@@ -1237,13 +1250,9 @@ template <int HD, int G, bool F16>
 static cudaError_t launch_attn_tile_g(const AttnParams& ap, dim3 grid, cudaStream_t s) {
   (void)grid;
   constexpr size_t sm = attn_tile_smem<HD, F16>();
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(attention_cluster_kernel<HD, G, F16>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static size_t marks[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(attention_cluster_kernel<HD, G, F16>, sm, marks);
+  if (e != cudaSuccess) return e;
   // one cluster of ATTN_SPLITS CTAs per KV head
   attention_cluster_kernel<HD, G, F16><<<dim3(ATTN_SPLITS, ap.n_kv), 128, sm, s>>>(ap);
   return cudaGetLastError();
@@ -1269,11 +1278,9 @@ static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t 
   const dim3 ag(ap.S_max, ap.n_kv);
   if (exact) {
     const size_t sm = (size_t)ap.n_ctx * 4;
-    if (sm > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(attention_exact_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-      if (e != cudaSuccess) return e;
-    }
+    static size_t marks[kMaxDevices] = {};
+    cudaError_t e = opt_in_smem(attention_exact_kernel, sm, marks);
+    if (e != cudaSuccess) return e;
     attention_exact_kernel<<<ap.n_head, 128, sm, s>>>(ap);
   } else if (!tile_group_ok(ap.n_head / ap.n_kv)) {
     switch (ap.hd / 32) {
@@ -1335,12 +1342,9 @@ static cudaError_t launch_down(foxcuda_context* c, uint32_t l) {
 static cudaError_t launch_q8_rows(const GemvParams& p, cudaStream_t s) {
   auto kern = q8_rows_kernel<PRO_NORM>;
   const size_t smem = (size_t)p.K * 4 + 32 * 8;
-  static size_t attr_set = 0;
-  if (smem > 48 * 1024 && smem > attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr_set = smem;
-  }
+  static size_t marks[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(kern, smem, marks);
+  if (e != cudaSuccess) return e;
   const int pairs = (p.n_rows / 32 + 1) / 2;
   const int warps = ROWS_THREADS / 32;
   const int grid = std::max(1, std::min((pairs + warps - 1) / warps, 4 * current_sms()));
