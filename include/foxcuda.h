@@ -65,6 +65,26 @@ foxcuda_status foxcuda_gemv_tq2_i8(const int8_t *q, const float *act_scale,
                                    const void *weights, size_t n_rows, size_t n_cols,
                                    float *out, void *stream);
 
+/* The per-token GEMVs of upstream's forward_batch (src/forward.c:188-213,
+ * each one fox_gemv_tq{1,2}_i8, src/gemv.c:155-192) for n_tokens tokens in
+ * one tensor-core pass (tcgen05 kind::i8 per 256-wide block). There is no
+ * single upstream entry point.
+ * - q is n_tokens x n_cols int8, token-major: each token is quantised with
+ *   its own scale. act_scale holds n_tokens floats. out is n_tokens x n_rows.
+ *   All are device pointers. q and the weights are 16-byte aligned.
+ * - Every token's row is bit-identical to foxcuda_gemv_tq{1,2}_i8 on that
+ *   token: the block sums are exact and the float fold is upstream's.
+ * - foxcuda_gemm_tq_i8 takes TQ1_0 or TQ2_0 GGUF rows. It transcodes TQ1_0 to
+ *   TQ2_0 (the same trits and scales) and packs into stream-ordered scratch.
+ * - foxcuda_gemm_tq2_i8_packed takes TQ2_0 already packed by foxcuda_pack and
+ *   allocates nothing. */
+foxcuda_status foxcuda_gemm_tq_i8(int ggml_type, const int8_t *q, const float *act_scale,
+                                  size_t n_tokens, const void *weights, size_t n_rows,
+                                  size_t n_cols, float *out, void *stream);
+foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t *q, const float *act_scale,
+                                          size_t n_tokens, const void *packed, size_t n_rows,
+                                          size_t n_cols, float *out, void *stream);
+
 /* replaces fox_gemv (include/fox/fox.h:363-365, src/kernels.c:809-872) for
  * TQ1_0, TQ2_0, Q4_K, Q6_K and Q8_0 weights in GGUF layout. Repacks the
  * weights into stream-ordered scratch memory, then runs the packed kernel. */

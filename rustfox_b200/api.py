@@ -65,6 +65,8 @@ _PROTOS = {
     "foxcuda_quantize_activations_i8": (_st, [_vp, _sz, _vp, _vp, _vp]),
     "foxcuda_gemv_tq1_i8": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_tq2_i8": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _vp]),
+    "foxcuda_gemm_tq_i8": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
+    "foxcuda_gemm_tq2_i8_packed": (_st, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_noalloc": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_attention": (_st, [_vp, _vp, _vp, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32,
@@ -188,6 +190,28 @@ def gemv_tq2_i8(q, scale, w, n_rows, n_cols, out=None):
     import torch
     out = torch.empty(n_rows, dtype=torch.float32, device=q.device) if out is None else out
     _check(lib().foxcuda_gemv_tq2_i8(_dp(q), _dp(scale), _dp(w), n_rows, n_cols, _dp(out), _stream()))
+    return out
+
+
+def gemm_tq_i8(ggml_type: int, q, scales, w, n_rows: int, n_cols: int, out=None):
+    """The per-token fox_gemv_tq{1,2}_i8 of upstream's forward_batch
+    (src/forward.c:188-213) for all rows of q (n_tokens x n_cols int8, one
+    scale per token) in one tensor-core pass; out is n_tokens x n_rows."""
+    import torch
+    n_tok = q.shape[0]
+    out = torch.empty(n_tok, n_rows, dtype=torch.float32, device=q.device) if out is None else out
+    _check(lib().foxcuda_gemm_tq_i8(ggml_type, _dp(q), _dp(scales), n_tok, _dp(w), n_rows, n_cols,
+                                    _dp(out), _stream()))
+    return out
+
+
+def gemm_tq2_i8_packed(q, scales, packed, n_rows: int, n_cols: int, out=None):
+    """gemm_tq_i8 on TQ2_0 weights already packed by pack()."""
+    import torch
+    n_tok = q.shape[0]
+    out = torch.empty(n_tok, n_rows, dtype=torch.float32, device=q.device) if out is None else out
+    _check(lib().foxcuda_gemm_tq2_i8_packed(_dp(q), _dp(scales), n_tok, _dp(packed), n_rows, n_cols,
+                                            _dp(out), _stream()))
     return out
 
 

@@ -16,6 +16,7 @@
 #include "pack.cuh"
 #include "slice.cuh"
 #include "rows.cuh"
+#include "tc.cuh"
 
 using namespace fox;
 
@@ -463,6 +464,104 @@ extern "C" foxcuda_status foxcuda_gemv_tq2_i8(const int8_t* q, const float* act_
                                               const void* w, size_t n_rows, size_t n_cols,
                                               float* out, void* stream) {
   return gemv_tq_i8(T_TQ2_0, q, act_scale, w, n_rows, n_cols, out, stream);
+}
+
+// ---------------------------------------------------------------------------
+// M-token ternary GEMM on the tensor cores (tc.cuh)
+
+template <int NT>
+static cudaError_t launch_tc_t(const TcParams& p, cudaStream_t s) {
+  const size_t smem = tc_smem_bytes(NT, p.nb);
+  static size_t marks[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(tc_tq2_kernel<NT>, smem, marks);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((p.n_rows + TC_ROWS - 1) / TC_ROWS), (unsigned)((p.n_tok + NT - 1) / NT));
+  tc_tq2_kernel<NT><<<grid, TC_THREADS, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+// The token tile is the smallest MMA N that holds all tokens, up to 64.
+static cudaError_t launch_tc(const TcParams& p, cudaStream_t s) {
+  if (p.n_tok <= 8) return launch_tc_t<8>(p, s);
+  if (p.n_tok <= 16) return launch_tc_t<16>(p, s);
+  if (p.n_tok <= 32) return launch_tc_t<32>(p, s);
+  return launch_tc_t<64>(p, s);
+}
+
+static foxcuda_status check_gemm_args(const int8_t* q, const float* act_scale, size_t n_tokens,
+                                      const void* w, size_t n_rows, size_t n_cols, const float* out) {
+  if (!q || !act_scale || !w || !out) return fail(FOXCUDA_ERR_ARG, "gemm: null pointer");
+  if (n_tokens == 0 || n_rows == 0 || n_cols == 0) return fail(FOXCUDA_ERR_ARG, "gemm: empty input");
+  if (n_cols % 256)
+    return fail(FOXCUDA_ERR_ARG, "gemm: %zu columns is not a multiple of 256", n_cols);
+  if (n_cols / 256 > (size_t)TC_MAX_NB || n_rows > (size_t)INT32_MAX || n_tokens > (1u << 20))
+    return fail(FOXCUDA_ERR_ARG, "gemm: %zu tokens x %zu x %zu is beyond this build's limits",
+                n_tokens, n_rows, n_cols);
+  if ((uintptr_t)q % 16 || (uintptr_t)w % 16)
+    return fail(FOXCUDA_ERR_ARG, "gemm: activations and weights must be 16-byte aligned");
+  return FOXCUDA_OK;
+}
+
+static TcParams tc_params(const int8_t* q, const float* act_scale, size_t n_tokens, const void* packed,
+                          size_t n_rows, size_t n_cols, int U, float* out) {
+  TcParams p;
+  p.w = (const uint8_t*)packed;
+  p.xq = q;
+  p.xs = act_scale;
+  p.out = out;
+  p.n_rows = (int)n_rows;
+  p.K = (int)n_cols;
+  p.nb = (int)(n_cols / 256);
+  p.U = U;
+  p.n_tok = (int)n_tokens;
+  p.err = nullptr;
+  return p;
+}
+
+extern "C" foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t* q, const float* act_scale,
+                                                     size_t n_tokens, const void* packed,
+                                                     size_t n_rows, size_t n_cols, float* out,
+                                                     void* stream) {
+  foxcuda_status st = check_gemm_args(q, act_scale, n_tokens, packed, n_rows, n_cols, out);
+  if (st) return st;
+  const int U = unit_rows(T_TQ2_0, (int)(n_cols / 256));
+  if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: %zu columns has no unit layout", n_cols);
+  CK(launch_tc(tc_params(q, act_scale, n_tokens, packed, n_rows, n_cols, U, out), (cudaStream_t)stream),
+     "gemm launch");
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_gemm_tq_i8(int type, const int8_t* q, const float* act_scale,
+                                             size_t n_tokens, const void* w, size_t n_rows,
+                                             size_t n_cols, float* out, void* stream) {
+  if (type != T_TQ1_0 && type != T_TQ2_0)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: ggml type %d; the tensor-core pass takes TQ1_0 and TQ2_0",
+                type);
+  foxcuda_status st = check_gemm_args(q, act_scale, n_tokens, w, n_rows, n_cols, out);
+  if (st) return st;
+  const int nb = (int)(n_cols / 256);
+  const int U = unit_rows(T_TQ2_0, nb);
+  if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: %zu columns has no unit layout", n_cols);
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t tq2_bytes = n_rows * (size_t)nb * 66;
+  const size_t tq1_bytes = type == T_TQ1_0 ? tq2_bytes : 0;  // the transcoded GGUF rows
+  uint8_t* scratch = nullptr;
+  CK(cudaMallocAsync((void**)&scratch, tq2_bytes + tq1_bytes, s), "gemm scratch");
+  const void* rows = w;
+  cudaError_t e = cudaSuccess;
+  if (type == T_TQ1_0) {
+    const long nblk = (long)n_rows * nb;
+    tq1_to_tq2_kernel<<<(unsigned)((nblk + 127) / 128), 128, 0, s>>>((const uint8_t*)w, scratch + tq2_bytes,
+                                                                     nblk);
+    e = cudaGetLastError();
+    rows = scratch + tq2_bytes;
+  }
+  if (e == cudaSuccess) e = pack_rows(T_TQ2_0, rows, n_rows, nb, U, scratch, s);
+  if (e == cudaSuccess) e = launch_tc(tc_params(q, act_scale, n_tokens, scratch, n_rows, n_cols, U, out), s);
+  cudaError_t e2 = cudaFreeAsync(scratch, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm");
+  CK(e2, "gemm scratch free");
+  return FOXCUDA_OK;
 }
 
 extern "C" foxcuda_status foxcuda_dequant_row(int type, const void* row, size_t n, float* out,

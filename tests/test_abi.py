@@ -45,6 +45,28 @@ def test_errors_without_a_device_are_statuses_not_crashes():
     assert rf.lib().foxcuda_gemv(34, None, None, 1, 256, None, None) == 1
 
 
+def test_gemm_argument_checks_run_before_any_device_call():
+    """foxcuda_gemm_tq_i8 / _packed reject bad arguments with a status and a
+    message before touching the device (host buffers stand in for device
+    pointers: only null, size and alignment are looked at)."""
+    import rustfox_b200 as rf
+    L = rf.lib()
+    buf = ctypes.create_string_buffer(1 << 12)
+    base = (ctypes.addressof(buf) + 15) // 16 * 16
+    p, odd = ctypes.c_void_p(base), ctypes.c_void_p(base + 4)
+    cases = [
+        (L.foxcuda_gemm_tq_i8(8, p, p, 1, p, 1, 256, p, None), 5),        # Q8_0: no tensor-core pass
+        (L.foxcuda_gemm_tq_i8(35, None, p, 1, p, 1, 256, p, None), 1),    # null activations
+        (L.foxcuda_gemm_tq_i8(35, p, p, 0, p, 1, 256, p, None), 1),       # no tokens
+        (L.foxcuda_gemm_tq_i8(34, p, p, 1, p, 1, 320, p, None), 1),       # K not a multiple of 256
+        (L.foxcuda_gemm_tq_i8(35, odd, p, 1, p, 1, 256, p, None), 1),     # unaligned activations
+        (L.foxcuda_gemm_tq2_i8_packed(p, p, 1, odd, 1, 256, p, None), 1),  # unaligned weights
+        (L.foxcuda_gemm_tq2_i8_packed(p, p, 1, p, 1, 256 * 257, p, None), 1),  # K beyond 65536
+    ]
+    for got, want in cases:
+        assert got == want and rf.last_error()
+
+
 def test_python_api_mirrors_upstream_names():
     import rustfox_b200 as rf
     for name in ("gemv", "gemv_tq1_i8", "gemv_tq2_i8", "quantize_activations_i8", "dequant_row",
