@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--tp", action="store_true",
                     help="one sequence split over the GPUs (tensor parallel, strong scaling) "
                          "instead of one replica per GPU")
+    ap.add_argument("--gemm", default=None, metavar="M[,M...]",
+                    help="time the M-token tensor-core pass over one layer's matrices "
+                         "(prefill / verification) instead of decoding")
     return ap.parse_args()
 
 
@@ -393,10 +396,81 @@ def run_tp(args):
         dist.destroy_process_group()
 
 
+def run_gemm(args):
+    """The M-token ternary pass (foxcuda_gemm_tq2_i8_packed, tcgen05 kind::i8)
+    over the seven matrices of one layer of the config (q, k, v, o, gate, up,
+    down), against M single-token decode GEMVs (foxcuda_gemv_packed) of the
+    same matrices. Enough packed copies of the layer are cycled that the
+    weights read per timed region exceed the L2 three times over.
+    CUDA-event time on the current stream, one GPU."""
+    import torch
+    import rustfox_b200 as rf
+    from rustfox_b200 import formats as F, synth
+    cfg = synth.CONFIGS[args.config]
+    torch.cuda.set_device(0)
+    e, f = cfg.n_embd, cfg.n_ff
+    nq, nkv = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
+    shapes = [(nq, e), (nkv, e), (nkv, e), (e, nq), (f, e), (f, e), (e, f)]
+    layer_bytes = sum(r * (k // 256) * 66 for r, k in shapes)
+    params = sum(r * k for r, k in shapes)
+    rng = np.random.default_rng(0)
+    one = [rf.pack(F.TQ2_0, torch.from_numpy(F.random_tq2_blocks(rng, r * k // 256, 0.02)
+                                            .reshape(-1)).cuda(), r, k) for r, k in shapes]
+    copies = [one] + [[p.clone() for p in one]
+                      for _ in range(max(1, int(np.ceil(3 * 126e6 / layer_bytes))) - 1)]
+    kmax = max(k for _, k in shapes)
+    rows = []
+    for m in [int(v) for v in args.gemm.split(",")]:
+        qs = {k: torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda")
+              for k in {k for _, k in shapes}}
+        s = torch.full((m,), 1e-3, dtype=torch.float32, device="cuda")
+        x = torch.randn(kmax, dtype=torch.float32, device="cuda")
+        outs = [torch.empty(m, r, dtype=torch.float32, device="cuda") for r, _ in shapes]
+
+        def tc_pass(layer):
+            for (r, k), pk, o in zip(shapes, layer, outs):
+                rf.gemm_tq2_i8_packed(qs[k], s, pk, r, k, out=o)
+
+        def gemv_pass(layer):
+            for _ in range(m):
+                for (r, k), pk, o in zip(shapes, layer, outs):
+                    rf.gemv_packed(F.TQ2_0, x[:k], pk, r, k, out=o[0])
+
+        res = {"M": m}
+        for name, fn in (("tc", tc_pass), ("gemv", gemv_pass)):
+            for i in range(max(3, args.warmup)):
+                fn(copies[i % len(copies)])
+            n = max(len(copies), args.steps)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for i in range(n):
+                fn(copies[i % len(copies)])
+            e1.record()
+            torch.cuda.synchronize()
+            res[f"{name}_us_per_layer"] = 1e3 * e0.elapsed_time(e1) / n
+        t = res["tc_us_per_layer"] * 1e-6
+        res["tc_weight_gbs"] = layer_bytes / t / 1e9
+        res["tc_int8_tops"] = 2.0 * m * params / t / 1e12
+        res["speedup_vs_gemv"] = res["gemv_us_per_layer"] / res["tc_us_per_layer"]
+        rows.append(res)
+    hbm, src = measured_hbm_gbs()
+    print(json.dumps({
+        "metric": "M-token ternary pass, one layer (q k v o gate up down)", "unit": "us",
+        "higher_is_better": False, "dtype": "i8 x ternary -> i32 (tcgen05 kind::i8), f32 fold",
+        "data": "synthetic (seeded random TQ2_0 weights, random int8 activations)",
+        "config": {"workload": f"{cfg.name} layer matrices, TQ2_0 packed",
+                   "layer_weight_bytes": layer_bytes, "l2": f"{len(copies)} layer copies cycled",
+                   "hbm_peak_gbs": hbm, "hbm_peak_source": src},
+        "results": rows}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.gemm:
+        run_gemm(args)
     elif args.tp:
         run_tp(args)
     else:
