@@ -210,6 +210,21 @@ foxcuda_status foxcuda_eval(foxcuda_context *c, const uint32_t *tokens, size_t n
  * embedding, n_layer = after the last layer), n_embd floats to host. Valid
  * after foxcuda_eval with foxcuda_context_set_trace(c, 1). */
 foxcuda_status foxcuda_context_set_trace(foxcuda_context *c, int on);
+
+/* How foxcuda_eval runs a prompt of several tokens (upstream forward_batch
+ * over n_batch chunks, src/forward.c:295-409,411-438). No upstream
+ * counterpart: upstream has one path.
+ * - mode 0 (the default) runs one decode step per token.
+ * - mode 1 runs chunks of up to 64 tokens. The projections take one
+ *   tensor-core pass each (the kernel of foxcuda_gemm_tq_i8). RMSNorm,
+ *   quantisation, RoPE, the K/V write, SwiGLU and the residual run row-wise
+ *   with the decode step's arithmetic, and attention runs per token at the
+ *   token's own position. Every token's values are meant to equal the
+ *   step-by-step ones.
+ * Mode 1 applies only to single-GPU models whose layer matrices are all
+ * ternary (held as TQ2_0). Other models, trace mode and tensor-parallel
+ * shards always step. */
+foxcuda_status foxcuda_context_set_prefill(foxcuda_context *c, int mode);
 foxcuda_status foxcuda_context_hidden(const foxcuda_context *c, uint32_t layer, float *out);
 
 /* replaces fox_sampler_config (include/fox/fox.h:453-460) */

@@ -89,6 +89,7 @@ _PROTOS = {
     "foxcuda_context_last_eval_seconds": (C.c_double, [_vp]),
     "foxcuda_eval": (_st, [_vp, _vp, _sz, _vp]),
     "foxcuda_context_set_trace": (_st, [_vp, C.c_int]),
+    "foxcuda_context_set_prefill": (_st, [_vp, C.c_int]),
     "foxcuda_context_hidden": (_st, [_vp, C.c_uint32, _vp]),
     "foxcuda_sampler_create": (_st, [_vp, C.POINTER(SamplerConfig), C.POINTER(_vp)]),
     "foxcuda_sampler_destroy": (None, [_vp]),
@@ -374,6 +375,11 @@ class Context:
 
     def set_trace(self, on: bool = True):
         _check(lib().foxcuda_context_set_trace(self.h, 1 if on else 0))
+
+    def set_prefill(self, chunks: bool = True):
+        """Prompts of several tokens in chunks through the tensor-core pass
+        (True) or one decode step per token (False, the default)."""
+        _check(lib().foxcuda_context_set_prefill(self.h, 1 if chunks else 0))
 
     def eval(self, tokens, want_logits: bool = True):
         """upstream fox_eval: logits (n_vocab, host) of the last token."""

@@ -17,6 +17,7 @@
 #include "slice.cuh"
 #include "rows.cuh"
 #include "tc.cuh"
+#include "prefill.cuh"
 
 using namespace fox;
 
@@ -1164,6 +1165,13 @@ struct foxcuda_context {
   std::vector<void*> allocs;
   std::vector<std::pair<cudaEvent_t, int>>* prof = nullptr;  // diagnostics
   bool tp_steps = false;  // driven through foxcuda_tp_* (collectives between kernels)
+  // prompt chunks through the tensor-core pass (foxcuda_context_set_prefill)
+  int prefill = 0;
+  bool pf_ready = false;
+  float *pf_x = nullptr, *pf_xs = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr;
+  float *pf_gu = nullptr, *pf_h = nullptr, *pf_t = nullptr;
+  int8_t* pf_xq = nullptr;
+  int* pf_pos = nullptr;
 };
 
 struct foxcuda_sampler {
@@ -1581,6 +1589,135 @@ static foxcuda_status check_err(foxcuda_context* c) {
               "gave up (code %u); the step's outputs are not valid", code);
 }
 
+// ---------------------------------------------------------------------------
+// prompt chunks through the tensor-core pass (prefill.cuh, tc.cuh)
+
+constexpr int PF_CHUNK = 64;  // tokens per chunk: the widest token tile of the pass
+
+// Threads of the decode kernel that normalises W's input vector: the chunk
+// forms its double sums of squares in the same partition.
+static int decode_threads(const PackedMat& W) {
+  return W.slice ? SLICE_THREADS : (W.U * W.nb + 31) / 32 * 32;
+}
+
+static bool prefill_eligible(const foxcuda_context* c) {
+  const foxcuda_model* m = c->m;
+  if (!c->prefill || c->trace_on || m->tp_size != 1) return false;
+  for (const LayerW& L : m->layers) {
+    if (L.n_qkv != 1) return false;
+    for (const PackedMat* W : {&L.qkv[0], &L.o, &L.gateup, &L.down})
+      if (W->type != T_TQ2_0 || W->nb > TC_MAX_NB || (size_t)W->K * 4 > 200 * 1024) return false;
+  }
+  return true;
+}
+
+static cudaError_t prefill_buffers(foxcuda_context* c) {
+  if (c->pf_ready) return cudaSuccess;
+  const foxcuda_model_info& mi = c->m->loc;
+  const size_t E = mi.n_embd, nq = (size_t)mi.n_head * mi.head_dim, nkv = (size_t)mi.n_head_kv * mi.head_dim;
+  const size_t F = mi.n_ff, M = PF_CHUNK;
+  const size_t kmax = std::max(E, std::max(nq, F));
+  cudaError_t e = cudaSuccess;
+  auto A = [&](size_t bytes, void** p) { if (e == cudaSuccess) e = ctx_alloc(c, bytes, p); };
+  A(M * E * 4, (void**)&c->pf_x);
+  A(M * kmax, (void**)&c->pf_xq);
+  A(M * 4, (void**)&c->pf_xs);
+  A(M * (nq + 2 * nkv) * 4, (void**)&c->pf_qkv);
+  A(M * nq * 4, (void**)&c->pf_q);
+  A(M * nq * 4, (void**)&c->pf_att);
+  A(M * 2 * F * 4, (void**)&c->pf_gu);
+  A(M * F * 4, (void**)&c->pf_h);
+  A(M * E * 4, (void**)&c->pf_t);
+  A(M * 4, (void**)&c->pf_pos);
+  if (e == cudaSuccess) c->pf_ready = true;
+  return e;
+}
+
+template <bool NORM>
+static cudaError_t quant_rows(foxcuda_context* c, const float* X, int K, const float* norm_w, int threads,
+                              int M) {
+  const size_t smem = (size_t)K * 4;
+  static size_t marks[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(quant_rows_kernel<NORM>, smem, marks);
+  if (e != cudaSuccess) return e;
+  quant_rows_kernel<NORM><<<M, threads, smem, c->stream>>>(X, K, norm_w, c->m->info.rms_eps, c->pf_xq,
+                                                          c->pf_xs);
+  return cudaGetLastError();
+}
+
+// out[t][r] for the chunk's quantised rows through W (TQ2_0, packed)
+static cudaError_t tc_rows(foxcuda_context* c, const PackedMat& W, int M, float* out) {
+  TcParams p = tc_params(c->pf_xq, c->pf_xs, (size_t)M, W.dev, (size_t)W.n_rows, (size_t)W.K, W.U, out);
+  p.err = c->err_dev;
+  return launch_tc(p, c->stream);
+}
+
+// M prompt tokens (device ids) at positions pos0.. through every layer; the
+// last one's residual row is left in c->x for the head, and the device
+// position moves past the chunk. Per token the values are the decode step's.
+static cudaError_t prefill_chunk(foxcuda_context* c, const uint32_t* tokens, int M, uint32_t pos0) {
+  foxcuda_model* m = c->m;
+  const foxcuda_model_info& mi = m->info;
+  cudaStream_t s = c->stream;
+  const int E = mi.n_embd, hd = mi.head_dim;
+  const int nq = m->loc.n_head * hd, nkv = m->loc.n_head_kv * hd, F = m->loc.n_ff, nqkv = nq + 2 * nkv;
+  const size_t rows_e = (size_t)M * E;
+  const unsigned add_grid = (unsigned)std::min<size_t>((rows_e + 255) / 256, 4096);
+  embed_rows_kernel<<<dim3((E + 255) / 256, M), 256, 0, s>>>(m->embd.type, m->embd.dev,
+                                                            row_bytes(m->embd.type, E), E, tokens, c->pf_x);
+  positions_kernel<<<(M + 127) / 128, 128, 0, s>>>(c->pf_pos, (int)pos0, M);
+  cudaError_t e = cudaGetLastError();
+  for (uint32_t l = 0; l < mi.n_layer && !e; ++l) {
+    const LayerW& L = m->layers[l];
+    // q|k|v, RoPE, K/V of every token of the chunk
+    if ((e = quant_rows<true>(c, c->pf_x, E, L.attn_norm, decode_threads(L.qkv[0]), M))) break;
+    if ((e = tc_rows(c, L.qkv[0], M, c->pf_qkv))) break;
+    qkv_rows_kernel<<<dim3((nqkv + 255) / 256, M), 256, 0, s>>>(
+        c->pf_qkv, nqkv, nq, nkv, hd, (int)c->n_ctx, (int)pos0, c->rope_cos, c->rope_sin, c->kv_f16,
+        kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->pf_q);
+    if ((e = cudaGetLastError())) break;
+    // attention of each token over positions 0..its own
+    AttnParams ap;
+    ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+    ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
+    ap.hd = hd; ap.n_head = m->loc.n_head; ap.n_kv = m->loc.n_head_kv; ap.S_max = c->S_max;
+    ap.part = c->attn_part; ap.counters = c->attn_cnt;
+    ap.scale = 1.0f / sqrtf((float)hd);
+    for (int t = 0; t < M && !e; ++t) {
+      ap.q = c->pf_q + (size_t)t * nq;
+      ap.pos = c->pf_pos + t;
+      ap.out = c->pf_att + (size_t)t * nq;
+      e = run_attention(ap, c->attn_exact, s);
+    }
+    if (e) break;
+    // o, residual
+    if ((e = quant_rows<false>(c, c->pf_att, nq, nullptr, 256, M))) break;
+    if ((e = tc_rows(c, L.o, M, c->pf_t))) break;
+    add_rows_kernel<<<add_grid, 256, 0, s>>>(c->pf_x, c->pf_t, rows_e);
+    // gate|up, SwiGLU
+    if ((e = quant_rows<true>(c, c->pf_x, E, L.ffn_norm, decode_threads(L.gateup), M))) break;
+    if ((e = tc_rows(c, L.gateup, M, c->pf_gu))) break;
+    swiglu_rows_kernel<<<dim3((F + 255) / 256, M), 256, 0, s>>>(c->pf_gu, 2 * F, L.gateup.U, c->pf_h);
+    // down, residual
+    if ((e = quant_rows<false>(c, c->pf_h, F, nullptr, 256, M))) break;
+    if ((e = tc_rows(c, L.down, M, c->pf_t))) break;
+    add_rows_kernel<<<add_grid, 256, 0, s>>>(c->pf_x, c->pf_t, rows_e);
+    e = cudaGetLastError();
+  }
+  if (e) return e;
+  if ((e = cudaMemcpyAsync(c->x, c->pf_x + (size_t)(M - 1) * E, (size_t)E * 4, cudaMemcpyDeviceToDevice, s)))
+    return e;
+  if ((e = cudaMemcpyAsync(c->token_dev, tokens + M - 1, 4, cudaMemcpyDeviceToDevice, s))) return e;
+  advance_kernel<<<1, 32, 0, s>>>(c->pos_dev, M);
+  return cudaGetLastError();
+}
+
+extern "C" foxcuda_status foxcuda_context_set_prefill(foxcuda_context* c, int mode) {
+  if (!c || (mode != 0 && mode != 1)) return fail(FOXCUDA_ERR_ARG, "set_prefill: mode is 0 or 1");
+  c->prefill = mode;
+  return FOXCUDA_OK;
+}
+
 extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* tokens, size_t n,
                                        float* logits_out) {
   if (!c || !tokens || n == 0) return fail(FOXCUDA_ERR_ARG, "eval: nothing to evaluate");
@@ -1603,8 +1740,15 @@ extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* token
   CK(cudaMemcpyAsync(c->tokens_dev, tokens, n * 4, cudaMemcpyHostToDevice, c->stream), "token upload");
   if (!c->trace_on && !c->g_body) CK(capture(c, &c->g_body, false, nullptr), "capture");
   if (!c->trace_on && !c->g_full) CK(capture(c, &c->g_full, true, nullptr), "capture");
+  const bool chunks = n >= 2 && prefill_eligible(c);
+  if (chunks) CK(prefill_buffers(c), "prefill buffers");
   CK(cudaEventRecord(c->ev0, c->stream), "event");
-  for (size_t i = 0; i < n; ++i) {
+  for (size_t i = 0; chunks && i < n; i += PF_CHUNK) {
+    const int M = (int)std::min<size_t>(PF_CHUNK, n - i);
+    CK(prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i), "prefill");
+    if (i + M == n) CK(enqueue_head(c), "head");
+  }
+  for (size_t i = 0; !chunks && i < n; ++i) {
     CK(cudaMemcpyAsync(c->token_dev, c->tokens_dev + i, 4, cudaMemcpyDeviceToDevice, c->stream), "token");
     const bool last = i + 1 == n;
     if (c->trace_on) {
