@@ -65,6 +65,7 @@ def test_gemm_argument_checks_run_before_any_device_call():
     ]
     for got, want in cases:
         assert got == want and rf.last_error()
+    assert L.foxcuda_context_set_prefill(None, 1) == 1 and rf.last_error()
 
 
 def test_python_api_mirrors_upstream_names():
