@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--gemm", default=None, metavar="M[,M...]",
                     help="time the M-token tensor-core pass over one layer's matrices "
                          "(prefill / verification) instead of decoding")
+    ap.add_argument("--prefill", action="store_true",
+                    help="time fox_eval of a --prompt long prompt (chunks through the tensor "
+                         "cores, and token by token) next to upstream's CPU fox_eval")
     return ap.parse_args()
 
 
@@ -465,12 +468,77 @@ def run_gemm(args):
         "results": rows}), flush=True)
 
 
+def reference_prompt(model, cfg, n_prompt: int):
+    """Upstream fox_eval of one prompt on this host's cores (oracle/_ref, the
+    upstream sources with their default -O3 and AVX2/FMA code generation,
+    n_batch 32 as `fox run` uses it). Returns (prompt tok/s, cores)."""
+    from oracle import oracle as O
+    from rustfox_b200 import synth
+    prompt = synth.random_prompt(cfg, n_prompt, seed=1)
+    with tempfile.TemporaryDirectory() as d:
+        path = synth.write_gguf(model, os.path.join(d, "model.gguf"), tokenizer=False)
+        ref = O.RefLib(fast=True)
+        cores = int(ref.L.fox_cpu_count_online())
+        m = ref.open_model(path)
+        ctx = ref.context(m, n_prompt + 8, 32, 0)
+        ref.eval(ctx, prompt, cfg.n_vocab)
+        secs = ref.L.fox_context_last_eval_seconds(ctx)
+        ref.L.fox_context_destroy(ctx)
+        ref.L.fox_model_close(m)
+    return n_prompt / secs, cores
+
+
+def run_prefill(args):
+    """Prompt evaluation: foxcuda_eval of an --prompt long prompt with the
+    chunk mode (tensor-core passes) and token by token (decode steps), CUDA
+    event time of the eval (median of up to 5 runs, after warm-up), next to
+    upstream's CPU fox_eval of a bounded prompt (32 ids, one n_batch chunk)."""
+    import torch
+    import rustfox_b200 as rf
+    from oracle import oracle as O
+    from rustfox_b200 import synth
+    cfg = synth.CONFIGS[args.config]
+    torch.cuda.set_device(0)
+    host = synth.generate(cfg)
+    model = rf.Model.from_synthetic(host)
+    prompt = synth.random_prompt(cfg, args.prompt, seed=1)
+    res = {}
+    for name, chunks in (("chunks", True), ("steps", False)):
+        ctx = rf.Context(model, args.prompt + 8, kv="f16")
+        ctx.set_prefill(chunks)
+        times = []
+        for i in range(max(1, args.warmup) + min(max(1, args.steps), 5)):
+            ctx.reset()
+            ctx.eval(prompt, want_logits=False)
+            if i >= max(1, args.warmup):
+                times.append(ctx.last_eval_seconds)
+        ctx.close()
+        res[f"{name}_tok_s"] = args.prompt / statistics.median(times)
+    res["chunks_vs_steps"] = res["chunks_tok_s"] / res["steps_tok_s"]
+    model.close()
+    cpu = None
+    if not args.no_cpu_baseline and os.path.exists(O.REF_FAST_SO):
+        n_ref = min(args.prompt, 32)
+        v, cores = reference_prompt(host, cfg, n_ref)
+        cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+               "sample": f"upstream fox_eval of a {n_ref}-id prompt (n_batch 32)"}
+    print(json.dumps({
+        "metric": "prompt tok/s (fox_eval of one prompt)", "unit": "tok/s", "higher_is_better": True,
+        "dtype": "i8 x ternary -> i32 (tcgen05 kind::i8 in chunks), f32",
+        "data": "synthetic (seeded random-init weights, uniform random prompt ids)",
+        "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd}, a {args.prompt}-id prompt",
+                   "kv_cache": "f16", "chunk": 64},
+        "results": res, "cpu_baseline": cpu}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.gemm:
         run_gemm(args)
+    elif args.prefill:
+        run_prefill(args)
     elif args.tp:
         run_tp(args)
     else:
