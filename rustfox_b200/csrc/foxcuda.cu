@@ -1223,7 +1223,7 @@ extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda
     delete c;
     return fail(FOXCUDA_ERR_UNSUPPORTED, "context: the exact attention mode holds at most 16384 positions");
   }
-  const int nq = mi.n_head * mi.head_dim, nkv = mi.n_head_kv * mi.head_dim;
+  const int nq = mi.n_head * mi.head_dim;
   const int half = mi.head_dim / 2;
   const int gqa = mi.n_head / mi.n_head_kv;
   c->S_max = std::max(1, std::min(32, 2 * sm_count(m->device) / (int)mi.n_head_kv));
@@ -1303,7 +1303,6 @@ static void* kv_layer(const foxcuda_context* c, void* base, uint32_t l) {
   return (uint8_t*)base + (size_t)l * c->kv_layer_elems * (c->kv_f16 ? 2 : 4);
 }
 
-static size_t packed_size(const PackedMat& W) { return foxcuda_packed_bytes(W.type, W.n_rows, W.K); }
 
 // Weight bytes (GGUF bytes) of one launch of a layer kernel, 0 for others.
 static uint64_t gguf_bytes(const PackedMat& W) {

@@ -647,7 +647,7 @@ topk_sample_kernel(SamplerDev* st, float* logits, int n_vocab, int k, float temp
                    float top_p, int restore, int accept, uint32_t* token_out,
                    uint32_t* ring, int ring_cap) {
   __shared__ unsigned hist[256];
-  __shared__ uint32_t prefix, want, thr_count;
+  __shared__ uint32_t prefix, want;
   __shared__ float cv[TOPK_MAX];
   __shared__ uint32_t ci[TOPK_MAX];
   __shared__ unsigned n_gt, n_eq_taken;
@@ -676,7 +676,7 @@ topk_sample_kernel(SamplerDev* st, float* logits, int n_vocab, int k, float temp
     __syncthreads();
   }
   // candidates: keys above the threshold, then equal keys in index order
-  if (tid == 0) { n_gt = 0; n_eq_taken = 0; thr_count = want; }
+  if (tid == 0) { n_gt = 0; n_eq_taken = 0; }
   __syncthreads();
   const uint32_t T = prefix;
   for (int i = tid; i < n_vocab; i += blockDim.x) {
