@@ -606,7 +606,7 @@ extern "C" foxcuda_status foxcuda_attention(const float* q, const void* kcache, 
   if (e == cudaSuccess) e = cudaMemcpyAsync(pos_dev, &p32, 4, cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // p32 lives on this stack
   if (e == cudaSuccess) {
-    AttnParams ap;
+    AttnParams ap{};
     ap.q = q; ap.kcache = kcache; ap.vcache = vcache; ap.kv_f16 = kv_type == FOXCUDA_KV_F16;
     ap.n_ctx = (int)n_ctx; ap.hd = (int)head_dim; ap.n_head = (int)n_head; ap.n_kv = (int)n_head_kv;
     ap.S_max = S_max; ap.pos = pos_dev; ap.out = out;
@@ -1360,8 +1360,21 @@ static cudaError_t launch_attn_tile_g(const AttnParams& ap, dim3 grid, cudaStrea
   cudaError_t e = opt_in_smem(attention_cluster_kernel<HD, G, F16>, sm, marks);
   if (e != cudaSuccess) return e;
   // one cluster of ATTN_SPLITS CTAs per KV head
-  attention_cluster_kernel<HD, G, F16><<<dim3(ATTN_SPLITS, ap.n_kv), 128, sm, s>>>(ap);
-  return cudaGetLastError();
+  if (!ap.pdl) {
+    attention_cluster_kernel<HD, G, F16><<<dim3(ATTN_SPLITS, ap.n_kv), 128, sm, s>>>(ap);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ATTN_SPLITS, ap.n_kv);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = sm;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_cluster_kernel<HD, G, F16>, ap);
 }
 
 static bool tile_group_ok(int g) { return g == 1 || g == 2 || g == 4 || g == 8; }
@@ -1412,14 +1425,27 @@ static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t 
   return cudaGetLastError();
 }
 
+// FOXCUDA_ATTN_PDL=1 launches the decode step's cluster attention with
+// programmatic stream serialisation (it stages the older K/V rows while the
+// q|k|v kernel finishes). Off by default.
+static bool attn_pdl() {
+  static const bool on = [] {
+    const char* v = getenv("FOXCUDA_ATTN_PDL");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
 static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
   const foxcuda_model_info& mi = c->m->info;
-  AttnParams ap;
+  AttnParams ap{};
   ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
   ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
   ap.hd = mi.head_dim; ap.n_head = c->m->loc.n_head; ap.n_kv = c->m->loc.n_head_kv; ap.S_max = c->S_max;
   ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
   ap.scale = 1.0f / sqrtf((float)mi.head_dim);
+  // the single-GPU step only: a tensor-parallel step keeps plain stream order
+  ap.pdl = attn_pdl() && c->m->tp_size == 1 && !c->tp_steps && !c->attn_exact ? 1 : 0;
   return run_attention(ap, c->attn_exact, c->stream);
 }
 
@@ -1676,7 +1702,7 @@ static cudaError_t prefill_chunk(foxcuda_context* c, const uint32_t* tokens, int
         kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->pf_q);
     if ((e = cudaGetLastError())) break;
     // attention of each token over positions 0..its own
-    AttnParams ap;
+    AttnParams ap{};
     ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
     ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
     ap.hd = hd; ap.n_head = m->loc.n_head; ap.n_kv = m->loc.n_head_kv; ap.S_max = c->S_max;

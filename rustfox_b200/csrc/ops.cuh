@@ -98,6 +98,10 @@ struct AttnParams {
   float* part;            // [n_kv][S_max][gqa][hd + 2]
   unsigned* counters;     // [n_kv], zero between launches
   float scale;
+  // 1: launched with programmatic stream serialisation right after the
+  // kernel that wrote q and position *pos of the cache; rows before *pos
+  // were written by earlier launches and are staged before the wait
+  int pdl;
 };
 
 constexpr int ATTN_THREADS = 128;
@@ -316,15 +320,29 @@ attention_cluster_kernel(const AttnParams p) {
   const size_t head = (size_t)g * p.n_ctx * HD;
   const uint8_t* kg = reinterpret_cast<const uint8_t*>(p.kcache) + head * ESZ;
   const uint8_t* vg = reinterpret_cast<const uint8_t*>(p.vcache) + head * ESZ;
-  auto stage = [&](int t0, int n) {
+  // rows t0 .. t0+n-1 of the cache into tile rows 0 .. n-1, except position skip
+  auto stage = [&](int t0, int n, int skip) {
     const int pieces = n * (RB / 16);
     for (int i = tid; i < pieces; i += NT) {
       const int row = i / (RB / 16), c = i - row * (RB / 16);
+      if (t0 + row == skip) continue;
       cp_async16(sK + (size_t)row * KSTRIDE + c * 16, kg + (size_t)(t0 + row) * RB + c * 16);
       cp_async16(sV + (size_t)i * 16, vg + (size_t)t0 * RB + (size_t)i * 16);
     }
   };
-  if (j0 < j1) stage(j0, min(NT, j1 - j0));  // in flight while q is read
+  // The first tile is in flight while q is read. Under programmatic launch
+  // the newest position (P - 1) and q come from the kernel still finishing:
+  // they are read after griddepcontrol.wait (a no-op for a plain launch).
+  const int n0 = j0 < j1 ? min(NT, j1 - j0) : 0;
+  const int cur = p.pdl ? P - 1 : -1;
+  if (n0) stage(j0, n0, cur);
+  griddep_wait();
+  if (cur >= j0 && cur < j0 + n0)
+    for (int c = tid; c < RB / 16; c += NT) {
+      const int row = cur - j0;
+      cp_async16(sK + (size_t)row * KSTRIDE + c * 16, kg + (size_t)cur * RB + c * 16);
+      cp_async16(sV + (size_t)row * RB + c * 16, vg + (size_t)cur * RB + c * 16);
+    }
   for (int i = tid; i < G * HD; i += NT) qs[i / HD][i % HD] = p.q[(size_t)g * G * HD + i];
 
   const int d = tid % HD, jsub = tid / HD;
@@ -334,7 +352,7 @@ attention_cluster_kernel(const AttnParams p) {
 
   for (int t0 = j0; t0 < j1; t0 += NT) {
     const int n = min(NT, j1 - t0);
-    if (t0 != j0) stage(t0, n);
+    if (t0 != j0) stage(t0, n, -1);
     cp_async_wait_all();
     __syncthreads();
     const bool on = tid < n;
