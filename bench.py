@@ -65,6 +65,9 @@ def parse():
     ap.add_argument("--prefill", action="store_true",
                     help="time fox_eval of a --prompt long prompt (chunks through the tensor "
                          "cores, and token by token) next to upstream's CPU fox_eval")
+    ap.add_argument("--batch", type=int, default=0, metavar="N",
+                    help="decode N sequences together at a --ctx long synthetic context "
+                         "(config 5: --config 8b-tq2 --batch 16 --ctx 32768)")
     return ap.parse_args()
 
 
@@ -531,6 +534,65 @@ def run_prefill(args):
         "results": res, "cpu_baseline": cpu}), flush=True)
 
 
+def run_batch(args):
+    """Config 5: --batch sequences of the --config model decoded together
+    (foxcuda_batch_generate: one pass per step, one CUDA graph per step) at a
+    --ctx long context. The K/V of every sequence is seeded N(0, 1) fp16
+    (foxcuda_context_fill_kv), a stand-in for the long prompts; sampling is
+    top-k 40 at temperature 0.8, top-p and repeat penalty off, seed 1 + i.
+    CUDA-event time of the timed steps on the batch's stream."""
+    import torch
+    import rustfox_b200 as rf
+    from rustfox_b200 import synth
+    cfg = synth.CONFIGS[args.config]
+    torch.cuda.set_device(0)
+    host = synth.generate(cfg)
+    wb = cfg.weight_bytes()
+    model = rf.Model.from_synthetic(host)
+    del host
+    n, warm = args.batch, max(3, args.warmup)
+    n_ctx = args.ctx + warm + args.steps + 8
+    ctxs = [rf.Context(model, n_ctx, kv="f16") for _ in range(n)]
+    for i, c in enumerate(ctxs):
+        c.fill_kv(args.ctx, seed=1 + i)
+    smp = [rf.Sampler(c, temperature=0.8, top_k=40, top_p=1.0, repeat_penalty=1.0, seed=1 + i)
+           for i, c in enumerate(ctxs)]
+    batch = rf.Batch(ctxs)
+    batch.generate(smp, warm, first=synth.random_prompt(cfg, n, seed=2))
+    clocks = Clocks(0)
+    clocks.start()
+    batch.generate(smp, args.steps)
+    secs = batch.last_seconds
+    ck = clocks.stop()
+    # algorithmic bytes of a step: the layer and head GGUF bytes once, the
+    # K/V every sequence reads (mean position of the timed steps) and writes
+    pos = args.ctx + warm + args.steps / 2.0
+    kv_row = cfg.n_head_kv * cfg.head_dim * 2
+    step_bytes = (wb["layers"] + wb["output"] + 2 * cfg.n_layer * pos * kv_row * n
+                  + 2 * cfg.n_layer * kv_row * n)
+    achieved = step_bytes / (secs / args.steps) / 1e9
+    hbm, src = measured_hbm_gbs()
+    print(json.dumps({
+        "metric": f"batch-{n} decode tok/s at {args.ctx} context", "value": n * args.steps / secs,
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": warm,
+        "ms_per_step": 1e3 * secs / args.steps, "higher_is_better": True, "scaling": None,
+        "vs_baseline": None, "dtype": "i8 x ternary -> i32 (tcgen05 kind::i8), f32",
+        "data": "synthetic (seeded random-init weights; seeded N(0,1) fp16 K/V in place of prompts)",
+        "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd}, {n} sequences at position "
+                               f"{args.ctx}, top-k 40 T 0.8", "batch": n, "ctx": args.ctx,
+                   "kv_cache": "f16", "l2": f"{step_bytes / 1e9:.1f} GB per step > 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": None, "peak_source": src,
+                     "bytes_per_step": step_bytes},
+        "clocks": ck}), flush=True)
+    batch.close()
+    for s in smp:
+        s.close()
+    for c in ctxs:
+        c.close()
+    model.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -539,6 +601,8 @@ def main():
         run_gemm(args)
     elif args.prefill:
         run_prefill(args)
+    elif args.batch:
+        run_batch(args)
     elif args.tp:
         run_tp(args)
     else:

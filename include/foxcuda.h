@@ -257,6 +257,32 @@ foxcuda_status foxcuda_decode(foxcuda_context *c, foxcuda_sampler *s, uint32_t t
 foxcuda_status foxcuda_generate(foxcuda_context *c, foxcuda_sampler *s, uint32_t token,
                                 size_t n, uint32_t *out);
 
+/* ---- decode batches (no upstream counterpart: upstream decodes one
+ * sequence per context, src/forward.c:411-438) ----------------------------
+ * A batch is a set of contexts of one single-GPU ternary model (layer
+ * matrices held as TQ2_0), equal in length, cache type and attention mode. A
+ * batch step advances every context by one token in one pass: the row
+ * kernels and one tensor-core pass per projection serve all of them, and
+ * each context keeps its own cache, position, logits and sampler. Every
+ * context's values are meant to equal its own decode step's, bit for bit.
+ * At most 64 contexts per batch. */
+typedef struct foxcuda_batch foxcuda_batch;
+foxcuda_status foxcuda_batch_create(foxcuda_context *const *ctxs, size_t n, foxcuda_batch **out);
+void           foxcuda_batch_destroy(foxcuda_batch *b);
+/* One token per context: tokens (host, n ids) or NULL for each context's
+ * device token (its last pick). logits: NULL or host n x n_vocab. */
+foxcuda_status foxcuda_batch_step(foxcuda_batch *b, const uint32_t *tokens, float *logits);
+/* n_steps steps, each followed by a pick with samplers[i] for context i and
+ * the picks fed back on the device (one CUDA graph per step). first: the
+ * first tokens (host, n ids) or NULL for the device tokens. out: host,
+ * n_steps x n, step-major. */
+foxcuda_status foxcuda_batch_generate(foxcuda_batch *b, foxcuda_sampler *const *samplers,
+                                      const uint32_t *first, size_t n_steps, uint32_t *out);
+double         foxcuda_batch_last_seconds(const foxcuda_batch *b);
+/* Benchmark stand-in for a long prompt: positions [0, n_pos) of every layer's
+ * K and V are set to seeded N(0, 1) values and the position to n_pos. */
+foxcuda_status foxcuda_context_fill_kv(foxcuda_context *c, uint32_t n_pos, uint64_t seed);
+
 /* ---- tensor parallel (no upstream counterpart: upstream runs one process,
  * src/threadpool.c; the split follows the scheme of include/fox/fox.h's
  * fox_eval with Megatron-style shards) ------------------------------------

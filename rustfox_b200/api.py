@@ -97,6 +97,12 @@ _PROTOS = {
     "foxcuda_sampler_pick": (_st, [_vp, _vp]),
     "foxcuda_decode": (_st, [_vp, _vp, C.c_uint32, _vp]),
     "foxcuda_generate": (_st, [_vp, _vp, C.c_uint32, _sz, _vp]),
+    "foxcuda_batch_create": (_st, [_vp, _sz, C.POINTER(_vp)]),
+    "foxcuda_batch_destroy": (None, [_vp]),
+    "foxcuda_batch_step": (_st, [_vp, _vp, _vp]),
+    "foxcuda_batch_generate": (_st, [_vp, _vp, _vp, _sz, _vp]),
+    "foxcuda_batch_last_seconds": (C.c_double, [_vp]),
+    "foxcuda_context_fill_kv": (_st, [_vp, C.c_uint32, C.c_uint64]),
     "foxcuda_context_profile": (_st, [_vp, _vp, C.c_uint32, _vp, _vp, C.c_int,
                                       C.POINTER(C.c_int)]),
     "foxcuda_context_bench_kernel": (_st, [_vp, C.c_int, C.c_int, C.POINTER(C.c_double),
@@ -376,6 +382,11 @@ class Context:
     def set_trace(self, on: bool = True):
         _check(lib().foxcuda_context_set_trace(self.h, 1 if on else 0))
 
+    def fill_kv(self, n_pos: int, seed: int = 1):
+        """Seeded N(0, 1) K/V at positions [0, n_pos) and the position set to
+        n_pos: a benchmark stand-in for a long prompt."""
+        _check(lib().foxcuda_context_fill_kv(self.h, n_pos, seed))
+
     def set_prefill(self, chunks: bool = True):
         """Prompts of several tokens in chunks through the tensor-core pass
         (True) or one decode step per token (False, the default)."""
@@ -457,6 +468,51 @@ class Sampler:
         _check(lib().foxcuda_generate(self.ctx.h, self.h, int(token), n,
                                       out.ctypes.data_as(C.c_void_p)))
         return out
+
+
+class Batch:
+    """Several contexts of one ternary model decoded together, one pass per
+    step (foxcuda_batch_*; no upstream counterpart)."""
+
+    def __init__(self, contexts):
+        self.contexts = list(contexts)
+        arr = (C.c_void_p * len(self.contexts))(*[c.h.value for c in self.contexts])
+        h = C.c_void_p()
+        _check(lib().foxcuda_batch_create(arr, len(self.contexts), C.byref(h)))
+        self.h = h
+        self.n_vocab = self.contexts[0].n_vocab
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().foxcuda_batch_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def step(self, tokens=None, want_logits: bool = True):
+        """One token per context (host ids, or None for the device tokens);
+        the logits (n, n_vocab) of every context."""
+        n = len(self.contexts)
+        t = None if tokens is None else np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty((n, self.n_vocab), dtype=np.float32) if want_logits else None
+        _check(lib().foxcuda_batch_step(self.h, t.ctypes.data_as(C.c_void_p) if t is not None else None,
+                                        out.ctypes.data_as(C.c_void_p) if out is not None else None))
+        return out
+
+    def generate(self, samplers, n_steps: int, first=None) -> np.ndarray:
+        """n_steps steps, each context picking with its sampler; (n_steps, n)."""
+        n = len(self.contexts)
+        arr = (C.c_void_p * n)(*[s.h.value for s in samplers])
+        f = None if first is None else np.ascontiguousarray(first, dtype=np.uint32)
+        out = np.empty((n_steps, n), dtype=np.uint32)
+        _check(lib().foxcuda_batch_generate(self.h, arr, f.ctypes.data_as(C.c_void_p) if f is not None else None,
+                                            n_steps, out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    @property
+    def last_seconds(self) -> float:
+        return lib().foxcuda_batch_last_seconds(self.h)
 
 
 def greedy_generate(model: Model, prompt, n_gen: int, n_ctx: int, kv: str = "f16",

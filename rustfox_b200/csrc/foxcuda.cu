@@ -2,6 +2,7 @@
 // context and its CUDA graphs.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -1494,15 +1495,19 @@ static cudaError_t launch_q8_rows(const GemvParams& p, cudaStream_t s) {
 }
 
 // Output norm on the last token and the head (upstream src/forward.c:403-408).
-static cudaError_t launch_head(foxcuda_context* c) {
+static cudaError_t launch_head_on(foxcuda_context* c, cudaStream_t s, bool pdl) {
   foxcuda_model* m = c->m;
   const PackedMat& H = m->output;
   GemvParams p = gemv_base(H.type, H.dev, H.n_rows, H.K, H.nb, H.U);
   p.x = c->x; p.norm_w = m->out_norm; p.eps = m->info.rms_eps; p.out = c->logits;
   p.err = c->err_dev;
-  p.pdl = m->tp_size == 1 && !c->tp_steps;
-  if (H.rows32) return launch_q8_rows(p, c->stream);
-  return launch_ring(H.type, PRO_NORM, EPI_STORE, p, c->stream);
+  p.pdl = pdl;
+  if (H.rows32) return launch_q8_rows(p, s);
+  return launch_ring(H.type, PRO_NORM, EPI_STORE, p, s);
+}
+
+static cudaError_t launch_head(foxcuda_context* c) {
+  return launch_head_on(c, c->stream, c->m->tp_size == 1 && !c->tp_steps);
 }
 
 static cudaError_t enqueue_body(foxcuda_context* c, bool trace) {
@@ -1541,23 +1546,28 @@ static cudaError_t enqueue_head(foxcuda_context* c) {
   return e;
 }
 
-static cudaError_t enqueue_pick(foxcuda_sampler* sm, bool accept) {
+static cudaError_t enqueue_pick_on(foxcuda_sampler* sm, bool accept, cudaStream_t s) {
   foxcuda_context* c = sm->c;
   const int nv = c->m->info.n_vocab;
   const bool pen = sm->cfg.repeat_penalty > 1.0f;
-  if (pen) penalty_kernel<<<1, 256, 0, c->stream>>>(sm->dev, c->logits, nv, sm->cfg.repeat_penalty);
+  if (pen) penalty_kernel<<<1, 256, 0, s>>>(sm->dev, c->logits, nv, sm->cfg.repeat_penalty);
   if (sm->cfg.temperature <= 0.0f) {
     const int grid = std::min(1024, std::max(1, std::min(current_sms(), (nv + ARGMAX_THREADS - 1) / ARGMAX_THREADS)));
-    argmax_kernel<<<grid, ARGMAX_THREADS, 0, c->stream>>>(sm->dev, c->logits, nv, pen, accept,
-                                                           c->token_dev, c->ring, (int)c->n_ctx);
+    argmax_kernel<<<grid, ARGMAX_THREADS, 0, s>>>(sm->dev, c->logits, nv, pen, accept,
+                                                   c->token_dev, c->ring, (int)c->n_ctx);
   } else {
-    topk_sample_kernel<<<1, TOPK_THREADS, 0, c->stream>>>(sm->dev, c->logits, nv, sm->k,
-                                                          sm->cfg.temperature, sm->cfg.top_p, pen,
-                                                          accept, c->token_dev, c->ring,
-                                                          (int)c->n_ctx);
+    topk_sample_kernel<<<1, TOPK_THREADS, 0, s>>>(sm->dev, c->logits, nv, sm->k,
+                                                  sm->cfg.temperature, sm->cfg.top_p, pen,
+                                                  accept, c->token_dev, c->ring,
+                                                  (int)c->n_ctx);
   }
-  mark(c, PK_PICK);
   return cudaGetLastError();
+}
+
+static cudaError_t enqueue_pick(foxcuda_sampler* sm, bool accept) {
+  cudaError_t e = enqueue_pick_on(sm, accept, sm->c->stream);
+  mark(sm->c, PK_PICK);
+  return e;
 }
 
 static cudaError_t capture(foxcuda_context* c, cudaGraphExec_t* out, bool head, foxcuda_sampler* sm) {
@@ -1625,15 +1635,20 @@ static int decode_threads(const PackedMat& W) {
   return W.slice ? SLICE_THREADS : (W.U * W.nb + 31) / 32 * 32;
 }
 
-static bool prefill_eligible(const foxcuda_context* c) {
-  const foxcuda_model* m = c->m;
-  if (!c->prefill || c->trace_on || m->tp_size != 1) return false;
+// Every layer matrix can take the tensor-core pass (ternary, held as TQ2_0)
+// and the row kernels (inputs of at most 200 KB of floats).
+static bool tc_layers_ok(const foxcuda_model* m) {
+  if (m->tp_size != 1) return false;
   for (const LayerW& L : m->layers) {
     if (L.n_qkv != 1) return false;
     for (const PackedMat* W : {&L.qkv[0], &L.o, &L.gateup, &L.down})
       if (W->type != T_TQ2_0 || W->nb > TC_MAX_NB || (size_t)W->K * 4 > 200 * 1024) return false;
   }
   return true;
+}
+
+static bool prefill_eligible(const foxcuda_context* c) {
+  return c->prefill && !c->trace_on && tc_layers_ok(c->m);
 }
 
 static cudaError_t prefill_buffers(foxcuda_context* c) {
@@ -1659,22 +1674,32 @@ static cudaError_t prefill_buffers(foxcuda_context* c) {
 }
 
 template <bool NORM>
-static cudaError_t quant_rows(foxcuda_context* c, const float* X, int K, const float* norm_w, int threads,
-                              int M) {
+static cudaError_t quant_rows_to(const float* X, int K, const float* norm_w, float eps, int threads, int M,
+                                 int8_t* XQ, float* XS, cudaStream_t s) {
   const size_t smem = (size_t)K * 4;
   static size_t marks[kMaxDevices] = {};
   cudaError_t e = opt_in_smem(quant_rows_kernel<NORM>, smem, marks);
   if (e != cudaSuccess) return e;
-  quant_rows_kernel<NORM><<<M, threads, smem, c->stream>>>(X, K, norm_w, c->m->info.rms_eps, c->pf_xq,
-                                                          c->pf_xs);
+  quant_rows_kernel<NORM><<<M, threads, smem, s>>>(X, K, norm_w, eps, XQ, XS);
   return cudaGetLastError();
 }
 
-// out[t][r] for the chunk's quantised rows through W (TQ2_0, packed)
+template <bool NORM>
+static cudaError_t quant_rows(foxcuda_context* c, const float* X, int K, const float* norm_w, int threads,
+                              int M) {
+  return quant_rows_to<NORM>(X, K, norm_w, c->m->info.rms_eps, threads, M, c->pf_xq, c->pf_xs, c->stream);
+}
+
+// out[t][r] for M quantised rows through W (TQ2_0, packed)
+static cudaError_t tc_rows_to(const int8_t* XQ, const float* XS, const PackedMat& W, int M, float* out, int* err,
+                              cudaStream_t s) {
+  TcParams p = tc_params(XQ, XS, (size_t)M, W.dev, (size_t)W.n_rows, (size_t)W.K, W.U, out);
+  p.err = err;
+  return launch_tc(p, s);
+}
+
 static cudaError_t tc_rows(foxcuda_context* c, const PackedMat& W, int M, float* out) {
-  TcParams p = tc_params(c->pf_xq, c->pf_xs, (size_t)M, W.dev, (size_t)W.n_rows, (size_t)W.K, W.U, out);
-  p.err = c->err_dev;
-  return launch_tc(p, c->stream);
+  return tc_rows_to(c->pf_xq, c->pf_xs, W, M, out, c->err_dev, c->stream);
 }
 
 // M prompt tokens (device ids) at positions pos0.. through every layer; the
@@ -1794,6 +1819,305 @@ extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* token
   c->last_seconds = ms / 1e3;
   c->pos += (uint32_t)n;
   return check_err(c);
+}
+
+// ---------------------------------------------------------------------------
+// decode batches: one pass per step over several contexts of one model
+
+constexpr int BATCH_MAX = 64;  // one token tile of the tensor-core pass
+
+struct foxcuda_batch {
+  foxcuda_model* m = nullptr;
+  std::vector<foxcuda_context*> ctx;
+  int n = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  double last_seconds = 0.0;
+  // per sequence (device arrays): position, token, layer-0 K and V caches
+  int** pos = nullptr;
+  uint32_t** tokp = nullptr;
+  void** kbase = nullptr;
+  void** vbase = nullptr;
+  uint32_t* toks = nullptr;
+  // rows of the pass, one per sequence
+  float *x = nullptr, *xs = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr;
+  float *gu = nullptr, *h = nullptr, *t = nullptr;
+  int8_t* xq = nullptr;
+  std::vector<void*> allocs;
+  cudaGraphExec_t graph = nullptr;  // a step and the picks, for foxcuda_batch_generate
+  std::vector<foxcuda_sampler*> graph_samplers;
+};
+
+extern "C" void foxcuda_batch_destroy(foxcuda_batch* b) {
+  if (!b) return;
+  cudaSetDevice(b->m->device);
+  if (b->stream) cudaStreamSynchronize(b->stream);
+  if (b->graph) cudaGraphExecDestroy(b->graph);
+  for (void* p : b->allocs) cudaFree(p);
+  if (b->ev0) cudaEventDestroy(b->ev0);
+  if (b->ev1) cudaEventDestroy(b->ev1);
+  if (b->stream) cudaStreamDestroy(b->stream);
+  delete b;
+}
+
+extern "C" foxcuda_status foxcuda_batch_create(foxcuda_context* const* ctxs, size_t n, foxcuda_batch** out) {
+  if (!ctxs || !out || n == 0) return fail(FOXCUDA_ERR_ARG, "batch: no contexts");
+  *out = nullptr;
+  if (n > (size_t)BATCH_MAX) return fail(FOXCUDA_ERR_ARG, "batch: %zu contexts; at most %d", n, BATCH_MAX);
+  foxcuda_context* c0 = ctxs[0];
+  for (size_t i = 0; i < n; ++i) {
+    const foxcuda_context* c = ctxs[i];
+    if (!c) return fail(FOXCUDA_ERR_ARG, "batch: context %zu is null", i);
+    if (c->m != c0->m) return fail(FOXCUDA_ERR_ARG, "batch: the contexts use different models");
+    if (c->n_ctx != c0->n_ctx || c->kv_f16 != c0->kv_f16 || c->attn_exact != c0->attn_exact)
+      return fail(FOXCUDA_ERR_ARG, "batch: the contexts differ in length, cache type or attention mode");
+    for (size_t j = 0; j < i; ++j)
+      if (ctxs[j] == c) return fail(FOXCUDA_ERR_ARG, "batch: context %zu appears twice", i);
+  }
+  foxcuda_model* m = c0->m;
+  if (!tc_layers_ok(m))
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "batch: the batched step needs single-GPU ternary layer "
+                "matrices (held as TQ2_0)");
+  cudaSetDevice(m->device);
+  foxcuda_batch* b = new foxcuda_batch();
+  b->m = m;
+  b->ctx.assign(ctxs, ctxs + n);
+  b->n = (int)n;
+  const foxcuda_model_info& mi = m->info;
+  const size_t E = mi.n_embd, nq = (size_t)mi.n_head * mi.head_dim, nkv = (size_t)mi.n_head_kv * mi.head_dim;
+  const size_t F = mi.n_ff, kmax = std::max(E, std::max(nq, F));
+  cudaError_t e = cudaSuccess;
+  auto A = [&](size_t bytes, void** p) {
+    if (e != cudaSuccess) return;
+    e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e == cudaSuccess) b->allocs.push_back(*p);
+  };
+  A(n * sizeof(int*), (void**)&b->pos);
+  A(n * sizeof(uint32_t*), (void**)&b->tokp);
+  A(n * sizeof(void*), (void**)&b->kbase);
+  A(n * sizeof(void*), (void**)&b->vbase);
+  A(n * 4, (void**)&b->toks);
+  A(n * E * 4, (void**)&b->x);
+  A(n * kmax, (void**)&b->xq);
+  A(n * 4, (void**)&b->xs);
+  A(n * (nq + 2 * nkv) * 4, (void**)&b->qkv);
+  A(n * nq * 4, (void**)&b->q);
+  A(n * nq * 4, (void**)&b->att);
+  A(n * 2 * F * 4, (void**)&b->gu);
+  A(n * F * 4, (void**)&b->h);
+  A(n * E * 4, (void**)&b->t);
+  std::vector<int*> pos(n);
+  std::vector<uint32_t*> tokp(n);
+  std::vector<void*> kb(n), vb(n);
+  for (size_t i = 0; i < n; ++i) {
+    pos[i] = ctxs[i]->pos_dev; tokp[i] = ctxs[i]->token_dev; kb[i] = ctxs[i]->kc; vb[i] = ctxs[i]->vc;
+  }
+  if (e == cudaSuccess) e = cudaMemcpy(b->pos, pos.data(), n * sizeof(int*), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(b->tokp, tokp.data(), n * sizeof(uint32_t*), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(b->kbase, kb.data(), n * sizeof(void*), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(b->vbase, vb.data(), n * sizeof(void*), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreate(&b->ev0);
+  if (e == cudaSuccess) e = cudaEventCreate(&b->ev1);
+  if (e != cudaSuccess) {
+    foxcuda_batch_destroy(b);
+    return cuda_fail(e, "batch allocation");
+  }
+  *out = b;
+  return FOXCUDA_OK;
+}
+
+// One token of every sequence through the layers and the head. Row i is
+// sequence i: its token (gathered from its context, or already in b->toks),
+// its position, its caches. Per sequence the values are its decode step's:
+// the tensor-core pass gives each row its single-token GEMV, and every other
+// kernel is the decode step's or repeats its arithmetic row-wise.
+static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
+  foxcuda_model* m = b->m;
+  const foxcuda_model_info& mi = m->info;
+  cudaStream_t s = b->stream;
+  foxcuda_context* c0 = b->ctx[0];
+  const int M = b->n, E = mi.n_embd, hd = mi.head_dim;
+  const int nq = mi.n_head * hd, nkv = mi.n_head_kv * hd, F = mi.n_ff, nqkv = nq + 2 * nkv;
+  const float eps = mi.rms_eps;
+  const size_t layer_bytes = c0->kv_layer_elems * (c0->kv_f16 ? 2 : 4);
+  const size_t rows_e = (size_t)M * E;
+  const unsigned add_grid = (unsigned)std::min<size_t>((rows_e + 255) / 256, 4096);
+  if (gather) gather_tokens_kernel<<<1, BATCH_MAX, 0, s>>>(b->tokp, M, b->toks);
+  embed_rows_kernel<<<dim3((E + 255) / 256, M), 256, 0, s>>>(m->embd.type, m->embd.dev,
+                                                            row_bytes(m->embd.type, E), E, b->toks, b->x);
+  cudaError_t e = cudaGetLastError();
+  for (uint32_t l = 0; l < mi.n_layer && !e; ++l) {
+    const LayerW& L = m->layers[l];
+    if ((e = quant_rows_to<true>(b->x, E, L.attn_norm, eps, decode_threads(L.qkv[0]), M, b->xq, b->xs, s)))
+      break;
+    if ((e = tc_rows_to(b->xq, b->xs, L.qkv[0], M, b->qkv, c0->err_dev, s))) break;
+    qkv_seqs_kernel<<<dim3((nqkv + 255) / 256, M), 256, 0, s>>>(
+        b->qkv, nqkv, nq, nkv, hd, (int)c0->n_ctx, b->pos, b->kbase, b->vbase, (size_t)l * layer_bytes,
+        c0->rope_cos, c0->rope_sin, c0->kv_f16, b->q);
+    if ((e = cudaGetLastError())) break;
+    for (int i = 0; i < M && !e; ++i) {
+      foxcuda_context* c = b->ctx[i];
+      AttnParams ap{};
+      ap.q = b->q + (size_t)i * nq; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+      ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
+      ap.hd = hd; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
+      ap.pos = c->pos_dev; ap.out = b->att + (size_t)i * nq; ap.part = c->attn_part; ap.counters = c->attn_cnt;
+      ap.scale = 1.0f / sqrtf((float)hd);
+      e = run_attention(ap, c->attn_exact, s);
+    }
+    if (e) break;
+    if ((e = quant_rows_to<false>(b->att, nq, nullptr, eps, 256, M, b->xq, b->xs, s))) break;
+    if ((e = tc_rows_to(b->xq, b->xs, L.o, M, b->t, c0->err_dev, s))) break;
+    add_rows_kernel<<<add_grid, 256, 0, s>>>(b->x, b->t, rows_e);
+    if ((e = quant_rows_to<true>(b->x, E, L.ffn_norm, eps, decode_threads(L.gateup), M, b->xq, b->xs, s)))
+      break;
+    if ((e = tc_rows_to(b->xq, b->xs, L.gateup, M, b->gu, c0->err_dev, s))) break;
+    swiglu_rows_kernel<<<dim3((F + 255) / 256, M), 256, 0, s>>>(b->gu, 2 * F, L.gateup.U, b->h);
+    if ((e = quant_rows_to<false>(b->h, F, nullptr, eps, 256, M, b->xq, b->xs, s))) break;
+    if ((e = tc_rows_to(b->xq, b->xs, L.down, M, b->t, c0->err_dev, s))) break;
+    add_rows_kernel<<<add_grid, 256, 0, s>>>(b->x, b->t, rows_e);
+    e = cudaGetLastError();
+  }
+  // each sequence's head on its own residual row, into its context's logits
+  for (int i = 0; i < M && !e; ++i) {
+    foxcuda_context* c = b->ctx[i];
+    e = cudaMemcpyAsync(c->x, b->x + (size_t)i * E, (size_t)E * 4, cudaMemcpyDeviceToDevice, s);
+    if (!e) e = launch_head_on(c, s, false);
+  }
+  if (e) return e;
+  advance_all_kernel<<<1, BATCH_MAX, 0, s>>>(b->pos, M);
+  return cudaGetLastError();
+}
+
+static foxcuda_status batch_begin(foxcuda_batch* b, size_t steps) {
+  for (foxcuda_context* c : b->ctx)
+    if ((size_t)c->pos + steps > c->n_ctx)
+      return fail(FOXCUDA_ERR_ARG, "batch: %zu tokens past position %u would overrun the %u token context",
+                  steps, c->pos, c->n_ctx);
+  cudaSetDevice(b->m->device);
+  for (foxcuda_context* c : b->ctx) CK(cudaStreamSynchronize(c->stream), "batch: context stream");
+  return FOXCUDA_OK;
+}
+
+// The device error word of every context (bounded waits that gave up).
+static foxcuda_status batch_errors(foxcuda_batch* b) {
+  for (foxcuda_context* c : b->ctx) {
+    uint32_t code = 0;
+    CK(cudaMemcpy(&code, c->err_dev, 4, cudaMemcpyDeviceToHost), "batch: error word");
+    if (code) {
+      cudaMemset(c->err_dev, 0, 4);
+      return fail(FOXCUDA_ERR_INTERNAL, "device: a bounded wait gave up (code %u); the step's outputs "
+                  "are not valid", code);
+    }
+  }
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_batch_step(foxcuda_batch* b, const uint32_t* tokens, float* logits) {
+  if (!b) return fail(FOXCUDA_ERR_ARG, "batch: null batch");
+  const uint32_t nv = b->m->info.n_vocab;
+  if (tokens)
+    for (int i = 0; i < b->n; ++i)
+      if (tokens[i] >= nv) return fail(FOXCUDA_ERR_ARG, "forward: token %u is outside the vocabulary", tokens[i]);
+  foxcuda_status st = batch_begin(b, 1);
+  if (st) return st;
+  if (tokens) CK(cudaMemcpyAsync(b->toks, tokens, (size_t)b->n * 4, cudaMemcpyHostToDevice, b->stream), "tokens");
+  CK(cudaEventRecord(b->ev0, b->stream), "event");
+  CK(enqueue_batch_body(b, tokens == nullptr), "batch step");
+  CK(cudaEventRecord(b->ev1, b->stream), "event");
+  for (int i = 0; logits && i < b->n; ++i)
+    CK(cudaMemcpyAsync(logits + (size_t)i * nv, b->ctx[i]->logits, (size_t)nv * 4, cudaMemcpyDeviceToHost,
+                       b->stream), "logits copy");
+  CK(cudaStreamSynchronize(b->stream), "batch step");
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, b->ev0, b->ev1);
+  b->last_seconds = ms / 1e3;
+  for (foxcuda_context* c : b->ctx) c->pos += 1;
+  return batch_errors(b);
+}
+
+extern "C" foxcuda_status foxcuda_batch_generate(foxcuda_batch* b, foxcuda_sampler* const* samplers,
+                                                 const uint32_t* first, size_t n_steps, uint32_t* out) {
+  if (!b || !samplers || !out || n_steps == 0) return fail(FOXCUDA_ERR_ARG, "batch: nothing to generate");
+  const uint32_t nv = b->m->info.n_vocab;
+  for (int i = 0; i < b->n; ++i) {
+    if (!samplers[i] || samplers[i]->c != b->ctx[i])
+      return fail(FOXCUDA_ERR_ARG, "batch: sampler %d does not belong to context %d", i, i);
+    if (first && first[i] >= nv) return fail(FOXCUDA_ERR_ARG, "forward: token %u is outside the vocabulary", first[i]);
+  }
+  foxcuda_status st = batch_begin(b, n_steps);
+  if (st) return st;
+  const bool same = b->graph && std::equal(b->graph_samplers.begin(), b->graph_samplers.end(), samplers);
+  if (!same) {
+    if (b->graph) cudaGraphExecDestroy(b->graph);
+    b->graph = nullptr;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal), "capture");
+    cudaError_t e = enqueue_batch_body(b, true);
+    for (int i = 0; i < b->n && !e; ++i) e = enqueue_pick_on(samplers[i], true, b->stream);
+    cudaError_t e2 = cudaStreamEndCapture(b->stream, &g);
+    if (e || e2) {
+      if (g) cudaGraphDestroy(g);
+      return cuda_fail(e ? e : e2, "batch capture");
+    }
+    e = cudaGraphInstantiate(&b->graph, g, 0);
+    cudaGraphDestroy(g);
+    CK(e, "batch graph");
+    b->graph_samplers.assign(samplers, samplers + b->n);
+  }
+  if (first)
+    for (int i = 0; i < b->n; ++i)
+      CK(cudaMemcpyAsync(b->ctx[i]->token_dev, first + i, 4, cudaMemcpyHostToDevice, b->stream), "token in");
+  std::vector<uint32_t> start(b->n);
+  for (int i = 0; i < b->n; ++i) start[i] = samplers[i]->n_out;
+  CK(cudaEventRecord(b->ev0, b->stream), "event");
+  for (size_t k = 0; k < n_steps; ++k) CK(cudaGraphLaunch(b->graph, b->stream), "graph launch");
+  CK(cudaEventRecord(b->ev1, b->stream), "event");
+  CK(cudaStreamSynchronize(b->stream), "batch generate");
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, b->ev0, b->ev1);
+  b->last_seconds = ms / 1e3;
+  std::vector<uint32_t> picks(n_steps);
+  for (int i = 0; i < b->n; ++i) {
+    foxcuda_context* c = b->ctx[i];
+    samplers[i]->n_out += (uint32_t)n_steps;
+    c->pos += (uint32_t)n_steps;
+    const uint32_t cap = c->n_ctx;
+    for (size_t k = 0; k < n_steps;) {  // the ring may wrap
+      const uint32_t at = (start[i] + (uint32_t)k) % cap;
+      const size_t run = std::min<size_t>(n_steps - k, cap - at);
+      CK(cudaMemcpy(picks.data() + k, c->ring + at, run * 4, cudaMemcpyDeviceToHost), "ring copy");
+      k += run;
+    }
+    for (size_t k = 0; k < n_steps; ++k) out[k * b->n + i] = picks[k];
+  }
+  return batch_errors(b);
+}
+
+extern "C" double foxcuda_batch_last_seconds(const foxcuda_batch* b) { return b ? b->last_seconds : 0.0; }
+
+extern "C" foxcuda_status foxcuda_context_fill_kv(foxcuda_context* c, uint32_t n_pos, uint64_t seed) {
+  if (!c) return fail(FOXCUDA_ERR_ARG, "fill_kv: null context");
+  if (n_pos > c->n_ctx) return fail(FOXCUDA_ERR_ARG, "fill_kv: %u positions in a %u token context", n_pos, c->n_ctx);
+  const foxcuda_model_info& mi = c->m->loc;
+  cudaSetDevice(c->m->device);
+  CK(cudaStreamSynchronize(c->stream), "fill_kv");
+  const size_t runs = (size_t)mi.n_layer * mi.n_head_kv;
+  const size_t total = runs * n_pos * mi.head_dim;
+  const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>((total + 255) / 256, 16384));
+  if (total) {
+    fill_kv_kernel<<<grid, 256, 0, c->stream>>>(c->kc, c->kv_f16, runs, (int)c->n_ctx, (int)mi.head_dim,
+                                                (int)n_pos, seed);
+    fill_kv_kernel<<<grid, 256, 0, c->stream>>>(c->vc, c->kv_f16, runs, (int)c->n_ctx, (int)mi.head_dim,
+                                                (int)n_pos, ~seed);
+    CK(cudaGetLastError(), "fill_kv launch");
+  }
+  const int p = (int)n_pos;
+  CK(cudaMemcpyAsync(c->pos_dev, &p, 4, cudaMemcpyHostToDevice, c->stream), "position");
+  CK(cudaStreamSynchronize(c->stream), "fill_kv");
+  c->pos = n_pos;
+  return FOXCUDA_OK;
 }
 
 // ---------------------------------------------------------------------------

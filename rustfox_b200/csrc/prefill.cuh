@@ -137,4 +137,83 @@ __global__ void positions_kernel(int* __restrict__ pos, int pos0, int n) {
   if (i < n) pos[i] = pos0 + i;
 }
 
+// ---- decode batches: row t is the next token of sequence t ---------------
+
+// qkv_rows_kernel for a batch of sequences: row t's position is *pos[t] and
+// its caches start at kbase[t] / vbase[t] plus layer_off bytes.
+__global__ void qkv_seqs_kernel(const float* __restrict__ QKV, int n_rows, int nq, int nkv, int hd,
+                                int n_ctx, int* const* __restrict__ pos, void* const* __restrict__ kbase,
+                                void* const* __restrict__ vbase, size_t layer_off,
+                                const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
+                                int kv_f16, float* __restrict__ Q) {
+  const int t = blockIdx.y, P = *pos[t];
+  void* kcache = reinterpret_cast<uint8_t*>(kbase[t]) + layer_off;
+  void* vcache = reinterpret_cast<uint8_t*>(vbase[t]) + layer_off;
+  const float* vals = QKV + (size_t)t * n_rows;
+  for (int rg = blockIdx.x * blockDim.x + threadIdx.x; rg < n_rows; rg += gridDim.x * blockDim.x) {
+    const float mine = vals[rg];
+    if (rg < nq + nkv) {
+      const float other = vals[rg ^ 1];
+      const int rr = rg < nq ? rg : rg - nq;
+      const int i = (rr % hd) >> 1;
+      const float c = rope_cos[(size_t)P * (hd >> 1) + i];
+      const float s = rope_sin[(size_t)P * (hd >> 1) + i];
+      const bool odd = rg & 1;
+      const float x0 = odd ? other : mine, x1 = odd ? mine : other;
+      const float o = odd ? __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c))
+                          : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+      if (rg < nq) {
+        Q[(size_t)t * nq + rg] = o;
+      } else {
+        const size_t idx = ((size_t)(rr / hd) * n_ctx + P) * hd + rr % hd;
+        if (kv_f16) reinterpret_cast<__half*>(kcache)[idx] = __float2half_rn(o);
+        else reinterpret_cast<float*>(kcache)[idx] = o;
+      }
+    } else {
+      const int rr = rg - nq - nkv;
+      const size_t idx = ((size_t)(rr / hd) * n_ctx + P) * hd + rr % hd;
+      if (kv_f16) reinterpret_cast<__half*>(vcache)[idx] = __float2half_rn(mine);
+      else reinterpret_cast<float*>(vcache)[idx] = mine;
+    }
+  }
+}
+
+__global__ void gather_tokens_kernel(uint32_t* const* __restrict__ src, int n, uint32_t* __restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) dst[i] = *src[i];
+}
+
+__global__ void advance_all_kernel(int* const* __restrict__ pos, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) *pos[i] += 1;
+}
+
+// splitmix64 (Steele, Lea and Flood, 2014): a counter-based 64-bit mix
+FOX_DEV uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Seeded normal values (Box-Muller on the two halves of splitmix64 of the
+// element index) for positions [0, n_pos) of every (layer, KV head) run of a
+// cache laid out [layer][kv_head][n_ctx][hd]. A benchmark stand-in for a long
+// prompt: upstream has no way to set its cache, so these contexts are not
+// compared with it.
+__global__ void fill_kv_kernel(void* cache, int kv_f16, size_t runs, int n_ctx, int hd, int n_pos,
+                               uint64_t seed) {
+  const size_t per = (size_t)n_pos * hd, total = runs * per;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t run = i / per, r = i - run * per;
+    const size_t idx = run * (size_t)n_ctx * hd + r;
+    const uint64_t h = splitmix64(seed ^ splitmix64(idx));
+    const float u1 = ((float)(uint32_t)(h >> 40) + 1.0f) * (1.0f / 16777217.0f);  // (0, 1]
+    const float u2 = (float)(uint32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);   // [0, 1)
+    const float v = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+    if (kv_f16) reinterpret_cast<__half*>(cache)[idx] = __float2half_rn(v);
+    else reinterpret_cast<float*>(cache)[idx] = v;
+  }
+}
+
 }  // namespace fox

@@ -66,6 +66,11 @@ def test_gemm_argument_checks_run_before_any_device_call():
     for got, want in cases:
         assert got == want and rf.last_error()
     assert L.foxcuda_context_set_prefill(None, 1) == 1 and rf.last_error()
+    h = ctypes.c_void_p()
+    assert L.foxcuda_batch_create(None, 0, ctypes.byref(h)) == 1 and not h.value
+    assert L.foxcuda_batch_step(None, None, None) == 1
+    assert L.foxcuda_batch_generate(None, None, None, 1, None) == 1
+    assert L.foxcuda_context_fill_kv(None, 0, 0) == 1
 
 
 def test_python_api_mirrors_upstream_names():
