@@ -225,6 +225,19 @@ foxcuda_status foxcuda_context_set_trace(foxcuda_context *c, int on);
  * ternary (held as TQ2_0). Other models, trace mode and tensor-parallel
  * shards always step. */
 foxcuda_status foxcuda_context_set_prefill(foxcuda_context *c, int mode);
+
+/* fox_eval with the logits of every token: logits_out is host n x n_vocab.
+ * This is the verification pass of speculative decoding, which upstream
+ * plans (README.md:86-89) but does not expose: its forward_batch keeps only
+ * the last row (src/forward.c:405-408).
+ * - Ternary single-GPU models run in chunks, one tensor-core pass per
+ *   projection, with the head on every row. Other models step.
+ * - Each row equals the logits the token-by-token decode gives that token.
+ * - The context advances by n. A caller that rejects part of the draft
+ *   rewinds with foxcuda_context_reset and a fresh eval, as upstream has no
+ *   partial rewind. */
+foxcuda_status foxcuda_eval_all(foxcuda_context *c, const uint32_t *tokens, size_t n,
+                                float *logits_out);
 foxcuda_status foxcuda_context_hidden(const foxcuda_context *c, uint32_t layer, float *out);
 
 /* replaces fox_sampler_config (include/fox/fox.h:453-460) */

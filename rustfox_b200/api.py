@@ -90,6 +90,7 @@ _PROTOS = {
     "foxcuda_eval": (_st, [_vp, _vp, _sz, _vp]),
     "foxcuda_context_set_trace": (_st, [_vp, C.c_int]),
     "foxcuda_context_set_prefill": (_st, [_vp, C.c_int]),
+    "foxcuda_eval_all": (_st, [_vp, _vp, _sz, _vp]),
     "foxcuda_context_hidden": (_st, [_vp, C.c_uint32, _vp]),
     "foxcuda_sampler_create": (_st, [_vp, C.POINTER(SamplerConfig), C.POINTER(_vp)]),
     "foxcuda_sampler_destroy": (None, [_vp]),
@@ -398,6 +399,15 @@ class Context:
         out = np.empty(self.n_vocab, dtype=np.float32) if want_logits else None
         _check(lib().foxcuda_eval(self.h, t.ctypes.data_as(C.c_void_p), t.size,
                                   out.ctypes.data_as(C.c_void_p) if out is not None else None))
+        return out
+
+    def eval_all(self, tokens) -> np.ndarray:
+        """The logits of every token, (n, n_vocab): the verification pass of
+        speculative decoding."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        out = np.empty((t.size, self.n_vocab), dtype=np.float32)
+        _check(lib().foxcuda_eval_all(self.h, t.ctypes.data_as(C.c_void_p), t.size,
+                                      out.ctypes.data_as(C.c_void_p)))
         return out
 
     def hidden(self, layer: int) -> np.ndarray:

@@ -1173,6 +1173,8 @@ struct foxcuda_context {
   float *pf_gu = nullptr, *pf_h = nullptr, *pf_t = nullptr;
   int8_t* pf_xq = nullptr;
   int* pf_pos = nullptr;
+  float* rows_logits = nullptr;  // foxcuda_eval_all staging, rows_cap x n_vocab
+  size_t rows_cap = 0;
 };
 
 struct foxcuda_sampler {
@@ -1814,6 +1816,75 @@ extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* token
        "logits copy");
   enqueue_err_read(c);
   CK(cudaStreamSynchronize(c->stream), "eval");
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+  c->last_seconds = ms / 1e3;
+  c->pos += (uint32_t)n;
+  return check_err(c);
+}
+
+// The logits of every token of `tokens` (speculative verification of a
+// draft, planned upstream in README.md:86-89; upstream's forward_batch keeps
+// only the last row, src/forward.c:405-408). Ternary models take the chunk
+// path (one tensor-core pass per projection) with the head on every row;
+// others step. Each row equals the step-by-step logits of that token.
+extern "C" foxcuda_status foxcuda_eval_all(foxcuda_context* c, const uint32_t* tokens, size_t n,
+                                           float* logits_out) {
+  if (!c || !tokens || n == 0 || !logits_out) return fail(FOXCUDA_ERR_ARG, "eval_all: nothing to evaluate");
+  if (c->m->tp_size > 1)
+    return fail(FOXCUDA_ERR_ARG, "eval_all: a tensor-parallel shard decodes through foxcuda_tp_*");
+  const foxcuda_model_info& mi = c->m->info;
+  const size_t nv = mi.n_vocab;
+  if ((size_t)c->pos + n > c->n_ctx)
+    return fail(FOXCUDA_ERR_ARG, "forward: %zu tokens past position %u would overrun the %u token context",
+                n, c->pos, c->n_ctx);
+  for (size_t i = 0; i < n; ++i)
+    if (tokens[i] >= mi.n_vocab)
+      return fail(FOXCUDA_ERR_ARG, "forward: token %u is outside the %u entry vocabulary", tokens[i], mi.n_vocab);
+  cudaSetDevice(c->m->device);
+  if (n > c->tokens_cap) {
+    void* p = nullptr;
+    CK(ctx_alloc(c, n * 4, &p), "token staging");
+    c->tokens_dev = (uint32_t*)p;
+    c->tokens_cap = n;
+  }
+  if (n > c->rows_cap) {
+    void* p = nullptr;
+    CK(ctx_alloc(c, n * nv * 4, &p), "logits staging");
+    c->rows_logits = (float*)p;
+    c->rows_cap = n;
+  }
+  CK(cudaMemcpyAsync(c->tokens_dev, tokens, n * 4, cudaMemcpyHostToDevice, c->stream), "token upload");
+  const bool chunks = n >= 2 && !c->trace_on && tc_layers_ok(c->m);
+  if (!chunks && !c->trace_on && !c->g_full) CK(capture(c, &c->g_full, true, nullptr), "capture");
+  if (chunks) CK(prefill_buffers(c), "prefill buffers");
+  CK(cudaEventRecord(c->ev0, c->stream), "event");
+  for (size_t i = 0; chunks && i < n; i += PF_CHUNK) {
+    const int M = (int)std::min<size_t>(PF_CHUNK, n - i);
+    CK(prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i), "prefill");
+    for (int t = 0; t < M; ++t) {
+      CK(cudaMemcpyAsync(c->x, c->pf_x + (size_t)t * mi.n_embd, (size_t)mi.n_embd * 4,
+                         cudaMemcpyDeviceToDevice, c->stream), "row");
+      CK(launch_head_on(c, c->stream, false), "head");
+      CK(cudaMemcpyAsync(c->rows_logits + (i + t) * nv, c->logits, nv * 4, cudaMemcpyDeviceToDevice,
+                         c->stream), "logits row");
+    }
+  }
+  for (size_t i = 0; !chunks && i < n; ++i) {
+    CK(cudaMemcpyAsync(c->token_dev, c->tokens_dev + i, 4, cudaMemcpyDeviceToDevice, c->stream), "token");
+    if (c->trace_on) {
+      CK(enqueue_body(c, true), "forward");
+      CK(enqueue_head(c), "head");
+    } else {
+      CK(cudaGraphLaunch(c->g_full, c->stream), "graph launch");
+    }
+    CK(cudaMemcpyAsync(c->rows_logits + i * nv, c->logits, nv * 4, cudaMemcpyDeviceToDevice, c->stream),
+       "logits row");
+  }
+  CK(cudaEventRecord(c->ev1, c->stream), "event");
+  CK(cudaMemcpyAsync(logits_out, c->rows_logits, n * nv * 4, cudaMemcpyDeviceToHost, c->stream), "logits copy");
+  enqueue_err_read(c);
+  CK(cudaStreamSynchronize(c->stream), "eval_all");
   float ms = 0.0f;
   cudaEventElapsedTime(&ms, c->ev0, c->ev1);
   c->last_seconds = ms / 1e3;

@@ -71,6 +71,7 @@ def test_gemm_argument_checks_run_before_any_device_call():
     assert L.foxcuda_batch_step(None, None, None) == 1
     assert L.foxcuda_batch_generate(None, None, None, 1, None) == 1
     assert L.foxcuda_context_fill_kv(None, 0, 0) == 1
+    assert L.foxcuda_eval_all(None, None, 0, None) == 1
 
 
 def test_python_api_mirrors_upstream_names():
