@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--gemm", default=None, metavar="M[,M...]",
                     help="time the M-token tensor-core pass over one layer's matrices "
                          "(prefill / verification) instead of decoding")
+    ap.add_argument("--split", action="store_true",
+                    help="with --gemm: also time the split form of the pass")
     ap.add_argument("--prefill", action="store_true",
                     help="time fox_eval of a --prompt long prompt (chunks through the tensor "
                          "cores, and token by token) next to upstream's CPU fox_eval")
@@ -442,8 +444,16 @@ def run_gemm(args):
                 for (r, k), pk, o in zip(shapes, layer, outs):
                     rf.gemv_packed(F.TQ2_0, x[:k], pk, r, k, out=o[0])
 
+        terms = (torch.empty(m * max(r * (k // 256) for r, k in shapes), dtype=torch.float32,
+                             device="cuda") if args.split else None)
+
+        def split_pass(layer):
+            for (r, k), pk, o in zip(shapes, layer, outs):
+                rf.gemm_tq2_i8_split(qs[k], s, pk, r, k, terms=terms, out=o)
+
         res = {"M": m}
-        for name, fn in (("tc", tc_pass), ("gemv", gemv_pass)):
+        kinds = [("tc", tc_pass), ("gemv", gemv_pass)] + ([("split", split_pass)] if args.split else [])
+        for name, fn in kinds:
             for i in range(max(3, args.warmup)):
                 fn(copies[i % len(copies)])
             n = max(len(copies), args.steps)

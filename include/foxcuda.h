@@ -84,6 +84,14 @@ foxcuda_status foxcuda_gemm_tq_i8(int ggml_type, const int8_t *q, const float *a
 foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t *q, const float *act_scale,
                                           size_t n_tokens, const void *packed, size_t n_rows,
                                           size_t n_cols, float *out, void *stream);
+/* foxcuda_gemm_tq2_i8_packed with each row's blocks split over CTAs, for few
+ * tokens, where the matrix alone has too few 128-row tiles to fill the GPU.
+ * It writes each block's float term to terms (device scratch of
+ * n_tokens x n_rows x n_cols/256 floats), then folds them in block order. The
+ * result is bit-identical to the unsplit pass. Not yet run on a B200. */
+foxcuda_status foxcuda_gemm_tq2_i8_split(const int8_t *q, const float *act_scale,
+                                         size_t n_tokens, const void *packed, size_t n_rows,
+                                         size_t n_cols, float *terms, float *out, void *stream);
 
 /* replaces fox_gemv (include/fox/fox.h:363-365, src/kernels.c:809-872) for
  * TQ1_0, TQ2_0, Q4_K, Q6_K and Q8_0 weights in GGUF layout. Repacks the

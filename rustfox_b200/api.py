@@ -67,6 +67,7 @@ _PROTOS = {
     "foxcuda_gemv_tq2_i8": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemm_tq_i8": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemm_tq2_i8_packed": (_st, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
+    "foxcuda_gemm_tq2_i8_split": (_st, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, _vp]),
     "foxcuda_gemv": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_noalloc": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_attention": (_st, [_vp, _vp, _vp, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32,
@@ -220,6 +221,19 @@ def gemm_tq2_i8_packed(q, scales, packed, n_rows: int, n_cols: int, out=None):
     out = torch.empty(n_tok, n_rows, dtype=torch.float32, device=q.device) if out is None else out
     _check(lib().foxcuda_gemm_tq2_i8_packed(_dp(q), _dp(scales), n_tok, _dp(packed), n_rows, n_cols,
                                             _dp(out), _stream()))
+    return out
+
+
+def gemm_tq2_i8_split(q, scales, packed, n_rows: int, n_cols: int, terms=None, out=None):
+    """gemm_tq2_i8_packed with each row's blocks split over CTAs (few tokens);
+    terms: device scratch of n_tokens * n_rows * n_cols/256 floats."""
+    import torch
+    n_tok = q.shape[0]
+    if terms is None:
+        terms = torch.empty(n_tok * n_rows * (n_cols // 256), dtype=torch.float32, device=q.device)
+    out = torch.empty(n_tok, n_rows, dtype=torch.float32, device=q.device) if out is None else out
+    _check(lib().foxcuda_gemm_tq2_i8_split(_dp(q), _dp(scales), n_tok, _dp(packed), n_rows, n_cols,
+                                           _dp(terms), _dp(out), _stream()))
     return out
 
 

@@ -533,6 +533,52 @@ extern "C" foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t* q, const floa
   return FOXCUDA_OK;
 }
 
+template <int NT>
+static cudaError_t launch_tc_split_t(const TcSplitParams& sp, cudaStream_t s) {
+  const TcParams& p = sp.p;
+  const size_t smem = tc_smem_bytes(NT, sp.bc);
+  static size_t marks[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(tc_tq2_split_kernel<NT>, smem, marks);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((p.n_rows + TC_ROWS - 1) / TC_ROWS), (unsigned)((p.n_tok + NT - 1) / NT),
+                  (unsigned)((p.nb + sp.bc - 1) / sp.bc));
+  tc_tq2_split_kernel<NT><<<grid, TC_THREADS, smem, s>>>(sp);
+  if ((e = cudaGetLastError())) return e;
+  const size_t total = (size_t)p.n_tok * p.n_rows;
+  tc_fold_kernel<<<(unsigned)std::min<size_t>((total + 255) / 256, 4096), 256, 0, s>>>(
+      sp.terms, p.xs, p.n_rows, p.nb, p.n_tok, p.out);
+  return cudaGetLastError();
+}
+
+// The blocks of a row are split so that the grid holds about two CTAs per SM.
+static cudaError_t launch_tc_split(const TcParams& p, float* terms, cudaStream_t s) {
+  const int nt = p.n_tok <= 8 ? 8 : p.n_tok <= 16 ? 16 : p.n_tok <= 32 ? 32 : 64;
+  const int tiles = ((p.n_rows + TC_ROWS - 1) / TC_ROWS) * ((p.n_tok + nt - 1) / nt);
+  const int splits = std::max(1, std::min(p.nb, (2 * current_sms() + tiles - 1) / tiles));
+  TcSplitParams sp;
+  sp.p = p;
+  sp.terms = terms;
+  sp.bc = (p.nb + splits - 1) / splits;
+  if (nt == 8) return launch_tc_split_t<8>(sp, s);
+  if (nt == 16) return launch_tc_split_t<16>(sp, s);
+  if (nt == 32) return launch_tc_split_t<32>(sp, s);
+  return launch_tc_split_t<64>(sp, s);
+}
+
+extern "C" foxcuda_status foxcuda_gemm_tq2_i8_split(const int8_t* q, const float* act_scale, size_t n_tokens,
+                                                    const void* packed, size_t n_rows, size_t n_cols,
+                                                    float* terms, float* out, void* stream) {
+  foxcuda_status st = check_gemm_args(q, act_scale, n_tokens, packed, n_rows, n_cols, out);
+  if (st) return st;
+  if (!terms) return fail(FOXCUDA_ERR_ARG, "gemm: null terms scratch");
+  const int U = unit_rows(T_TQ2_0, (int)(n_cols / 256));
+  if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: %zu columns has no unit layout", n_cols);
+  CK(launch_tc_split(tc_params(q, act_scale, n_tokens, packed, n_rows, n_cols, U, out), terms,
+                     (cudaStream_t)stream),
+     "gemm launch");
+  return FOXCUDA_OK;
+}
+
 extern "C" foxcuda_status foxcuda_gemm_tq_i8(int type, const int8_t* q, const float* act_scale,
                                              size_t n_tokens, const void* w, size_t n_rows,
                                              size_t n_cols, float* out, void* stream) {

@@ -299,4 +299,191 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_tq2_kernel(const TcParams p)
   if (warp == 0) tmem_dealloc(tmem, NCOLS);
 }
 
+// ---- split over K blocks (few tokens) ---------------------------------------
+// With few tokens a matrix has few 128-row tiles, and each CTA above walks all
+// K blocks of its tile one after another. The split form gives CTA z the
+// blocks [z*bc, z*bc + bc) of its tile. Per block it writes each row's float
+// term d_b * S_b (the same product the GEMV folds) to
+// terms[b][token][row], and tc_fold_kernel then adds each row's terms in
+// block order from 0.0f and scales by the token's activation scale. Every
+// operation and its order is the single-token GEMV's, so the result is still
+// bit-identical. The pipeline per CTA is the one of tc_tq2_kernel.
+struct TcSplitParams {
+  TcParams p;
+  float* terms;  // [nb][n_tok][n_rows]
+  int bc;        // blocks per CTA
+};
+
+template <int NT>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_tq2_split_kernel(const TcSplitParams sp) {
+  static_assert(NT == 8 || NT == 16 || NT == 32 || NT == 64, "token tile");
+  constexpr int HALF = NT / 2;
+  constexpr int BV = (NT * 16 + TC_THREADS - 1) / TC_THREADS;
+  constexpr uint32_t NCOLS = tc_tmem_cols(NT);
+  constexpr uint32_t IDESC = tc_idesc_i8(TC_ROWS, NT);
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t tmem_sh;
+
+  const TcParams& p = sp.p;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int R0 = blockIdx.x * TC_ROWS, T0 = blockIdx.y * NT;
+  const int nb = p.nb, U = p.U, n_rows = p.n_rows;
+  const int b0 = blockIdx.z * sp.bc, nbc = min(sp.bc, nb - b0);  // this CTA's blocks
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + 2 * tc_a_bytes();
+  uint16_t* sD = reinterpret_cast<uint16_t*>(smem + 2 * tc_a_bytes() + 2 * tc_b_bytes(NT));
+
+  if (warp == 0) {
+    tmem_alloc(&tmem_sh, NCOLS);
+    tmem_relinquish();
+  }
+  if (tid == 32) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    mbar_fence_init();
+  }
+  // block scales of the tile's rows for this CTA's blocks: sD[m * nbc + lb]
+  for (int i = tid; i < TC_ROWS * nbc; i += TC_THREADS) {
+    const int m = i / nbc, lb = i - m * nbc, r = R0 + m;
+    uint16_t d = 0;
+    if (r < n_rows) {
+      const int u = r / U, ru = min(U, n_rows - u * U);
+      const size_t base = (size_t)u * U * nb * 66, count = (size_t)ru * nb;
+      d = __ldg(reinterpret_cast<const unsigned short*>(p.w + base + count * 64 +
+                                                        ((size_t)(r - u * U) * nb + b0 + lb) * 2));
+    }
+    sD[i] = d;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
+
+  const uint8_t* wrow[2];
+  int mrow[2], plane[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = tid + j * TC_THREADS;
+    mrow[j] = i & (TC_ROWS - 1);
+    plane[j] = i >> 7;
+    const int r = R0 + mrow[j];
+    wrow[j] = nullptr;
+    if (r < n_rows) {
+      const int u = r / U, ru = min(U, n_rows - u * U);
+      const size_t base = (size_t)u * U * nb * 66, count = (size_t)ru * nb;
+      wrow[j] = p.w + base + count * 16 * plane[j] + (size_t)(r - u * U) * nb * 16;
+    }
+  }
+  uint4 ra[2], rb[BV];
+  auto load_block = [&](int b) {  // b: the block's index in the row
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      ra[j] = wrow[j] ? __ldg(reinterpret_cast<const uint4*>(wrow[j] + (size_t)b * 16))
+                      : make_uint4(0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u);
+#pragma unroll
+    for (int j = 0; j < BV; ++j) {
+      const int i = tid + j * TC_THREADS;
+      const int n = i % NT, c = i / NT;
+      rb[j] = make_uint4(0, 0, 0, 0);
+      if (i < NT * 16 && T0 + n < p.n_tok)
+        rb[j] = __ldg(reinterpret_cast<const uint4*>(p.xq + (size_t)(T0 + n) * p.K + (size_t)b * 256 + c * 16));
+    }
+  };
+  auto store_block = [&](int buf) {
+    uint8_t* a = sA + buf * tc_a_bytes();
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int m = mrow[j], pl = plane[j];
+      uint8_t* dst = a + (m >> 3) * 2048 + (m & 7) * 16;
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        const int kc = (pl >> 1) * 8 + l * 2 + (pl & 1);
+        uint4 v;
+        v.x = codes_to_i8((ra[j].x >> (2 * l)) & 0x03030303u);
+        v.y = codes_to_i8((ra[j].y >> (2 * l)) & 0x03030303u);
+        v.z = codes_to_i8((ra[j].z >> (2 * l)) & 0x03030303u);
+        v.w = codes_to_i8((ra[j].w >> (2 * l)) & 0x03030303u);
+        *reinterpret_cast<uint4*>(dst + kc * 128) = v;
+      }
+    }
+    uint8_t* bsm = sB + buf * tc_b_bytes(NT);
+#pragma unroll
+    for (int j = 0; j < BV; ++j) {
+      const int i = tid + j * TC_THREADS;
+      if (i < NT * 16) {
+        const int n = i % NT, c = i / NT;
+        *reinterpret_cast<uint4*>(bsm + (n >> 3) * 2048 + c * 128 + (n & 7) * 16) = rb[j];
+      }
+    }
+  };
+
+  const int q4 = warp & 3, half = warp >> 2, m = q4 * 32 + lane;
+  bool ok = true;
+  int last = -1;  // last committed local block
+  auto emit = [&](int lb) -> bool {  // the terms of local block lb
+    const int eb = lb & 1;
+    const bool got = mbar_wait(&bars[eb], (unsigned)((lb >> 1) & 1));
+    if (!__syncthreads_and(got)) return false;
+    tc_fence_after();
+    uint32_t v[HALF];
+    TmemLd<HALF>::run(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(eb * NT + half * HALF), v);
+    tmem_wait_ld();
+    const float d = h2f(sD[m * nbc + lb]);
+    const int r = R0 + m;
+    if (r < n_rows)
+#pragma unroll
+      for (int j = 0; j < HALF; ++j) {
+        const int t = T0 + half * HALF + j;
+        if (t < p.n_tok)
+          sp.terms[((size_t)(b0 + lb) * p.n_tok + t) * n_rows + r] = __fmul_rn(d, __int2float_rn((int)v[j]));
+      }
+    return true;
+  };
+
+  if (nbc > 0) load_block(b0);
+  for (int lb = 0; lb < nbc && ok; ++lb) {
+    const int buf = lb & 1;
+    store_block(buf);
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(sA + buf * tc_a_bytes());
+      const uint32_t bb0 = smem_u32(sB + buf * tc_b_bytes(NT));
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        mma_i8(tmem + (uint32_t)(buf * NT), umma_desc(a0 + s * 256, 128, 2048),
+               umma_desc(bb0 + s * 256, 128, 2048), IDESC, s > 0 ? 1u : 0u);
+      mma_commit(&bars[buf]);
+    }
+    last = lb;
+    if (lb + 1 < nbc) load_block(b0 + lb + 1);
+    if (lb >= 1) ok = emit(lb - 1);
+  }
+  if (ok && nbc > 0) ok = emit(nbc - 1);
+
+  if (!ok) {
+    if (tid == 0 && p.err) atomicExch(p.err, 1);
+    if (last >= 0) mbar_wait(&bars[last & 1], (unsigned)((last >> 1) & 1));
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, NCOLS);
+}
+
+// out[t][r] = (terms[0][t][r] + terms[1][t][r] + ...) * xs[t], added in block
+// order from 0.0f: the fold of the single-token GEMV.
+__global__ void tc_fold_kernel(const float* __restrict__ terms, const float* __restrict__ xs, int n_rows,
+                               int nb, int n_tok, float* __restrict__ out) {
+  const size_t total = (size_t)n_tok * n_rows, plane = total;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    float acc = 0.0f;
+    for (int b = 0; b < nb; ++b) acc = __fadd_rn(acc, terms[(size_t)b * plane + i]);
+    out[i] = __fmul_rn(acc, xs[i / n_rows]);
+  }
+}
+
 }  // namespace fox
