@@ -84,6 +84,16 @@ foxcuda_status foxcuda_gemm_tq_i8(int ggml_type, const int8_t *q, const float *a
 foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t *q, const float *act_scale,
                                           size_t n_tokens, const void *packed, size_t n_rows,
                                           size_t n_cols, float *out, void *stream);
+/* The same for Q4_K and Q6_K weights in GGUF layout (the per-token
+ * gemv_qk_i8 of src/kernels.c:571-805): q is n_tokens x n_cols int8, each
+ * token quantised with one scale per 256 block (upstream
+ * quantize_activations_k, src/kernels.c:722-754). act_scales holds
+ * n_tokens x n_cols/256 floats. Each token's row is meant to equal the
+ * single-token GEMV bit for bit. It runs 8 (Q6_K) or 16 (Q4_K) tokens per
+ * tile. Not yet run on a B200. */
+foxcuda_status foxcuda_gemm_kq_i8(int ggml_type, const int8_t *q, const float *act_scales,
+                                  size_t n_tokens, const void *weights, size_t n_rows,
+                                  size_t n_cols, float *out, void *stream);
 /* foxcuda_gemm_tq2_i8_packed with each row's blocks split over CTAs, for few
  * tokens, where the matrix alone has too few 128-row tiles to fill the GPU.
  * It writes each block's float term to terms (device scratch of

@@ -68,6 +68,7 @@ _PROTOS = {
     "foxcuda_gemm_tq_i8": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemm_tq2_i8_packed": (_st, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemm_tq2_i8_split": (_st, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, _vp]),
+    "foxcuda_gemm_kq_i8": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_noalloc": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_attention": (_st, [_vp, _vp, _vp, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32,
@@ -221,6 +222,18 @@ def gemm_tq2_i8_packed(q, scales, packed, n_rows: int, n_cols: int, out=None):
     out = torch.empty(n_tok, n_rows, dtype=torch.float32, device=q.device) if out is None else out
     _check(lib().foxcuda_gemm_tq2_i8_packed(_dp(q), _dp(scales), n_tok, _dp(packed), n_rows, n_cols,
                                             _dp(out), _stream()))
+    return out
+
+
+def gemm_kq_i8(ggml_type: int, q, scales, w, n_rows: int, n_cols: int, out=None):
+    """The per-token K-quant GEMV (upstream gemv_qk_i8, src/kernels.c:571-805)
+    for all rows of q (n_tokens x n_cols int8, per-256-block scales
+    n_tokens x n_cols/256) in one tensor-core pass; Q4_K or Q6_K GGUF rows."""
+    import torch
+    n_tok = q.shape[0]
+    out = torch.empty(n_tok, n_rows, dtype=torch.float32, device=q.device) if out is None else out
+    _check(lib().foxcuda_gemm_kq_i8(ggml_type, _dp(q), _dp(scales), n_tok, _dp(w), n_rows, n_cols,
+                                    _dp(out), _stream()))
     return out
 
 

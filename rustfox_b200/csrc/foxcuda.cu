@@ -18,6 +18,7 @@
 #include "slice.cuh"
 #include "rows.cuh"
 #include "tc.cuh"
+#include "tc_kquant.cuh"
 #include "prefill.cuh"
 
 using namespace fox;
@@ -576,6 +577,51 @@ extern "C" foxcuda_status foxcuda_gemm_tq2_i8_split(const int8_t* q, const float
   CK(launch_tc_split(tc_params(q, act_scale, n_tokens, packed, n_rows, n_cols, U, out), terms,
                      (cudaStream_t)stream),
      "gemm launch");
+  return FOXCUDA_OK;
+}
+
+template <int T, int NT>
+static cudaError_t launch_kq_t(const TcKParams& p, cudaStream_t s) {
+  const size_t smem = 2 * (size_t)tck_buf_bytes<T>(NT);
+  static size_t marks[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(tc_kq_kernel<T, NT>, smem, marks);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((p.n_rows + TC_ROWS - 1) / TC_ROWS), (unsigned)((p.n_tok + NT - 1) / NT));
+  tc_kq_kernel<T, NT><<<grid, TC_THREADS, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+// Token tiles: Q4_K up to 16 tokens (8 accumulators per block), Q6_K 8 (16).
+static cudaError_t launch_kq(int type, const TcKParams& p, cudaStream_t s) {
+  if (type == T_Q4_K) return p.n_tok <= 8 ? launch_kq_t<T_Q4_K, 8>(p, s) : launch_kq_t<T_Q4_K, 16>(p, s);
+  if (type == T_Q6_K) return launch_kq_t<T_Q6_K, 8>(p, s);
+  return cudaErrorInvalidValue;
+}
+
+extern "C" foxcuda_status foxcuda_gemm_kq_i8(int type, const int8_t* q, const float* act_scales,
+                                             size_t n_tokens, const void* w, size_t n_rows, size_t n_cols,
+                                             float* out, void* stream) {
+  if (type != T_Q4_K && type != T_Q6_K)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: ggml type %d; the K-quant tensor-core pass takes Q4_K and Q6_K",
+                type);
+  foxcuda_status st = check_gemm_args(q, act_scales, n_tokens, w, n_rows, n_cols, out);
+  if (st) return st;
+  const int nb = (int)(n_cols / 256);
+  const int U = unit_rows(type, nb);
+  if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: %zu columns has no unit layout", n_cols);
+  cudaStream_t s = (cudaStream_t)stream;
+  void* scratch = nullptr;
+  CK(cudaMallocAsync(&scratch, n_rows * row_bytes(type, n_cols), s), "gemm scratch");
+  cudaError_t e = pack_rows(type, w, n_rows, nb, U, scratch, s);
+  if (e == cudaSuccess) {
+    TcKParams p;
+    p.w = (const uint8_t*)scratch; p.xq = q; p.xs = act_scales; p.out = out; p.out_stride = (int)n_rows;
+    p.n_rows = (int)n_rows; p.K = (int)n_cols; p.nb = nb; p.U = U; p.n_tok = (int)n_tokens; p.err = nullptr;
+    e = launch_kq(type, p, s);
+  }
+  cudaError_t e2 = cudaFreeAsync(scratch, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm");
+  CK(e2, "gemm scratch free");
   return FOXCUDA_OK;
 }
 
