@@ -1755,7 +1755,7 @@ static cudaError_t prefill_buffers(foxcuda_context* c) {
   auto A = [&](size_t bytes, void** p) { if (e == cudaSuccess) e = ctx_alloc(c, bytes, p); };
   A(M * E * 4, (void**)&c->pf_x);
   A(M * kmax, (void**)&c->pf_xq);
-  A(M * 4, (void**)&c->pf_xs);
+  A(M * (kmax / 256 + 1) * 4, (void**)&c->pf_xs);  // one scale per token, or per 256 block (K-quants)
   A(M * (nq + 2 * nkv) * 4, (void**)&c->pf_qkv);
   A(M * nq * 4, (void**)&c->pf_q);
   A(M * nq * 4, (void**)&c->pf_att);
@@ -1845,6 +1845,98 @@ static cudaError_t prefill_chunk(foxcuda_context* c, const uint32_t* tokens, int
     // down, residual
     if ((e = quant_rows<false>(c, c->pf_h, F, nullptr, 256, M))) break;
     if ((e = tc_rows(c, L.down, M, c->pf_t))) break;
+    add_rows_kernel<<<add_grid, 256, 0, s>>>(c->pf_x, c->pf_t, rows_e);
+    e = cudaGetLastError();
+  }
+  if (e) return e;
+  if ((e = cudaMemcpyAsync(c->x, c->pf_x + (size_t)(M - 1) * E, (size_t)E * 4, cudaMemcpyDeviceToDevice, s)))
+    return e;
+  if ((e = cudaMemcpyAsync(c->token_dev, tokens + M - 1, 4, cudaMemcpyDeviceToDevice, s))) return e;
+  advance_kernel<<<1, 32, 0, s>>>(c->pos_dev, M);
+  return cudaGetLastError();
+}
+
+// ---- the same chunk for K-quant models (tc_kquant.cuh) ----------------------
+
+static bool is_kq(int t) { return t == T_Q4_K || t == T_Q6_K; }
+
+// Every layer matrix is Q4_K or Q6_K with inputs of at most 200 KB of floats.
+static bool kq_layers_ok(const foxcuda_model* m) {
+  if (m->tp_size != 1) return false;
+  for (const LayerW& L : m->layers) {
+    for (int i = 0; i < L.n_qkv; ++i)
+      if (!is_kq(L.qkv[i].type)) return false;
+    for (const PackedMat* W : {&L.o, &L.gateup, &L.down})
+      if (!is_kq(W->type) || (size_t)W->K * 4 > 200 * 1024) return false;
+  }
+  return (size_t)m->info.n_embd * 4 <= 200 * 1024;
+}
+
+template <bool NORM>
+static cudaError_t quant_rows_k(foxcuda_context* c, const float* X, int K, const float* norm_w, int threads,
+                                int M) {
+  const size_t smem = (size_t)K * 4;
+  static size_t marks[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(quant_rows_k_kernel<NORM>, smem, marks);
+  if (e != cudaSuccess) return e;
+  quant_rows_k_kernel<NORM><<<M, threads, smem, c->stream>>>(X, K, norm_w, c->m->info.rms_eps, c->pf_xq,
+                                                            c->pf_xs);
+  return cudaGetLastError();
+}
+
+static cudaError_t kq_rows(foxcuda_context* c, const PackedMat& W, int M, float* out, int out_stride) {
+  TcKParams p;
+  p.w = W.dev; p.xq = c->pf_xq; p.xs = c->pf_xs; p.out = out; p.out_stride = out_stride;
+  p.n_rows = W.n_rows; p.K = W.K; p.nb = W.K / 256; p.U = W.U; p.n_tok = M; p.err = c->err_dev;
+  return launch_kq(W.type, p, c->stream);
+}
+
+// prefill_chunk for K-quant layers: each q|k|v run is quantised with the
+// thread count of its own decode kernel and lands at its row offset.
+static cudaError_t prefill_chunk_kq(foxcuda_context* c, const uint32_t* tokens, int M, uint32_t pos0) {
+  foxcuda_model* m = c->m;
+  const foxcuda_model_info& mi = m->info;
+  cudaStream_t s = c->stream;
+  const int E = mi.n_embd, hd = mi.head_dim;
+  const int nq = m->loc.n_head * hd, nkv = m->loc.n_head_kv * hd, F = m->loc.n_ff, nqkv = nq + 2 * nkv;
+  const size_t rows_e = (size_t)M * E;
+  const unsigned add_grid = (unsigned)std::min<size_t>((rows_e + 255) / 256, 4096);
+  embed_rows_kernel<<<dim3((E + 255) / 256, M), 256, 0, s>>>(m->embd.type, m->embd.dev,
+                                                            row_bytes(m->embd.type, E), E, tokens, c->pf_x);
+  positions_kernel<<<(M + 127) / 128, 128, 0, s>>>(c->pf_pos, (int)pos0, M);
+  cudaError_t e = cudaGetLastError();
+  for (uint32_t l = 0; l < mi.n_layer && !e; ++l) {
+    const LayerW& L = m->layers[l];
+    for (int i = 0; i < L.n_qkv && !e; ++i) {
+      if ((e = quant_rows_k<true>(c, c->pf_x, E, L.attn_norm, decode_threads(L.qkv[i]), M))) break;
+      e = kq_rows(c, L.qkv[i], M, c->pf_qkv + L.qkv_base[i], nqkv);
+    }
+    if (e) break;
+    qkv_rows_kernel<<<dim3((nqkv + 255) / 256, M), 256, 0, s>>>(
+        c->pf_qkv, nqkv, nq, nkv, hd, (int)c->n_ctx, (int)pos0, c->rope_cos, c->rope_sin, c->kv_f16,
+        kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->pf_q);
+    if ((e = cudaGetLastError())) break;
+    AttnParams ap{};
+    ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+    ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
+    ap.hd = hd; ap.n_head = m->loc.n_head; ap.n_kv = m->loc.n_head_kv; ap.S_max = c->S_max;
+    ap.part = c->attn_part; ap.counters = c->attn_cnt;
+    ap.scale = 1.0f / sqrtf((float)hd);
+    for (int t = 0; t < M && !e; ++t) {
+      ap.q = c->pf_q + (size_t)t * nq;
+      ap.pos = c->pf_pos + t;
+      ap.out = c->pf_att + (size_t)t * nq;
+      e = run_attention(ap, c->attn_exact, s);
+    }
+    if (e) break;
+    if ((e = quant_rows_k<false>(c, c->pf_att, nq, nullptr, 256, M))) break;
+    if ((e = kq_rows(c, L.o, M, c->pf_t, E))) break;
+    add_rows_kernel<<<add_grid, 256, 0, s>>>(c->pf_x, c->pf_t, rows_e);
+    if ((e = quant_rows_k<true>(c, c->pf_x, E, L.ffn_norm, decode_threads(L.gateup), M))) break;
+    if ((e = kq_rows(c, L.gateup, M, c->pf_gu, 2 * F))) break;
+    swiglu_rows_kernel<<<dim3((F + 255) / 256, M), 256, 0, s>>>(c->pf_gu, 2 * F, L.gateup.U, c->pf_h);
+    if ((e = quant_rows_k<false>(c, c->pf_h, F, nullptr, 256, M))) break;
+    if ((e = kq_rows(c, L.down, M, c->pf_t, E))) break;
     add_rows_kernel<<<add_grid, 256, 0, s>>>(c->pf_x, c->pf_t, rows_e);
     e = cudaGetLastError();
   }
@@ -1947,13 +2039,16 @@ extern "C" foxcuda_status foxcuda_eval_all(foxcuda_context* c, const uint32_t* t
     c->rows_cap = n;
   }
   CK(cudaMemcpyAsync(c->tokens_dev, tokens, n * 4, cudaMemcpyHostToDevice, c->stream), "token upload");
-  const bool chunks = n >= 2 && !c->trace_on && tc_layers_ok(c->m);
+  const bool ternary = tc_layers_ok(c->m), kquant = !ternary && kq_layers_ok(c->m);
+  const bool chunks = n >= 2 && !c->trace_on && (ternary || kquant);
   if (!chunks && !c->trace_on && !c->g_full) CK(capture(c, &c->g_full, true, nullptr), "capture");
   if (chunks) CK(prefill_buffers(c), "prefill buffers");
   CK(cudaEventRecord(c->ev0, c->stream), "event");
   for (size_t i = 0; chunks && i < n; i += PF_CHUNK) {
     const int M = (int)std::min<size_t>(PF_CHUNK, n - i);
-    CK(prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i), "prefill");
+    CK(kquant ? prefill_chunk_kq(c, c->tokens_dev + i, M, c->pos + (uint32_t)i)
+              : prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i),
+       "prefill");
     for (int t = 0; t < M; ++t) {
       CK(cudaMemcpyAsync(c->x, c->pf_x + (size_t)t * mi.n_embd, (size_t)mi.n_embd * 4,
                          cudaMemcpyDeviceToDevice, c->stream), "row");

@@ -78,6 +78,53 @@ __global__ void quant_rows_kernel(const float* __restrict__ X, int K, const floa
   }
 }
 
+// The K-quant form (upstream quantize_activations_k, src/kernels.c:722-754):
+// the same RMSNorm, then one absmax scale per 256 block, a warp per block.
+// XS[t * (K / 256) + b] is block b's scale. Dynamic shared memory: K floats.
+template <bool NORM>
+__global__ void quant_rows_k_kernel(const float* __restrict__ X, int K, const float* __restrict__ norm_w,
+                                    float eps, int8_t* __restrict__ XQ, float* __restrict__ XS) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ double red[32];
+  const int t = blockIdx.x, tid = threadIdx.x, nth = blockDim.x;
+  const float* x = X + (size_t)t * K;
+  double ss = 0.0;
+  for (int i = tid * 4; i < K; i += nth * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(x + i);
+    if (NORM)
+      ss = ss + (double)v.x * (double)v.x + (double)v.y * (double)v.y + (double)v.z * (double)v.z +
+           (double)v.w * (double)v.w;
+    *reinterpret_cast<float4*>(xs + i) = v;
+  }
+  if (NORM) {
+    const double sum = block_reduce<double>(ss, red, OpAddD(), 0.0);
+    const float scale = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)K), (double)eps)));
+    for (int i = tid * 4; i < K; i += nth * 4) {
+      float4 v = *reinterpret_cast<float4*>(xs + i);
+      const float4 w = *reinterpret_cast<const float4*>(norm_w + i);
+      v.x = __fmul_rn(__fmul_rn(v.x, scale), w.x);
+      v.y = __fmul_rn(__fmul_rn(v.y, scale), w.y);
+      v.z = __fmul_rn(__fmul_rn(v.z, scale), w.z);
+      v.w = __fmul_rn(__fmul_rn(v.w, scale), w.w);
+      *reinterpret_cast<float4*>(xs + i) = v;
+    }
+  }
+  __syncthreads();  // a block's warp reads other threads' elements
+  const int lane = tid & 31, warp = tid >> 5, nw = nth >> 5, nb = K >> 8;
+  for (int b = warp; b < nb; b += nw) {
+    float v[8], am = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { v[k] = xs[b * 256 + lane * 8 + k]; am = absmax_acc(am, v[k]); }
+    am = warp_max(am);
+    const bool nz = am > 0.0f;
+    const float inv = nz ? __fdiv_rn(127.0f, am) : 0.0f;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(XQ + (size_t)t * K + b * 256 + lane * 8);
+    dst[0] = pack4(quant1(v[0], inv), quant1(v[1], inv), quant1(v[2], inv), quant1(v[3], inv));
+    dst[1] = pack4(quant1(v[4], inv), quant1(v[5], inv), quant1(v[6], inv), quant1(v[7], inv));
+    if (lane == 0) XS[(size_t)t * nb + b] = nz ? __fdiv_rn(am, 127.0f) : 0.0f;
+  }
+}
+
 // QKV[t] holds the q, k and v rows of token t (position pos0 + t). Adjacent
 // row pairs of q and k are rotated with the position's tables; q goes to
 // Q[t], k and v to the caches ([kv_head][n_ctx][hd], f16 or f32).

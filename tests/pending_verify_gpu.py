@@ -6,8 +6,10 @@ and rename it to test_verify_gpu.py once it passes there.
 
 Upstream plans speculative decoding (README.md:86-89) but its forward_batch
 keeps only the last row (src/forward.c:405-408). Row t of eval_all must be
-the logits fox_eval gives after token t. Ternary models take the chunk path
-(tensor-core passes); the K-quant model steps.
+the logits fox_eval gives after token t. Drafts of two or more tokens take
+the chunk path: the ternary pass for the TQ models, the K-quant pass
+(Q4_K with a Q6_K v and head, as in config 3) for the third; a one-token
+draft steps.
 """
 import numpy as np
 import pytest
