@@ -362,6 +362,32 @@ foxcuda_status foxcuda_context_sync_position(foxcuda_context *c);
 /* this shard's logits of its last head evaluation (n <= its vocabulary rows) */
 foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
 
+/* The same exchanges over peer memory (NVLink) instead of host collectives.
+ * Each rank's context owns an exchange arena. The arena holds every rank's
+ * absmax and pick slots, readiness flags, and this rank's block terms, and
+ * it is shared through CUDA IPC (plain peer loads and stores, no
+ * multicast).
+ * - foxcuda_tp_p2p_export writes this arena's IPC handle
+ *   (FOXCUDA_IPC_HANDLE_BYTES).
+ * - After every rank has exported, foxcuda_tp_p2p_open maps the others'
+ *   arenas. handles holds world x FOXCUDA_IPC_HANDLE_BYTES, rank order.
+ * - foxcuda_tp_p2p_row replaces amax + max-allreduce + terms + all-gather +
+ *   fold of one row-parallel projection. foxcuda_tp_p2p_pick replaces
+ *   head + all-gather + pick.
+ * - The values and their order are those of the collective form, so the
+ *   result is the single-GPU decode's, bit for bit.
+ * - Every wait is bounded. A wait that gives up sets the device error word
+ *   (code 2), which foxcuda_tp_tokens and later calls report.
+ * - After foxcuda_context_reset, every rank calls foxcuda_tp_p2p_clear
+ *   before any rank's next step.
+ * Not yet run on a B200. */
+#define FOXCUDA_IPC_HANDLE_BYTES 64
+foxcuda_status foxcuda_tp_p2p_export(foxcuda_context *c, void *handle);
+foxcuda_status foxcuda_tp_p2p_open(foxcuda_context *c, const void *handles);
+foxcuda_status foxcuda_tp_p2p_clear(foxcuda_context *c);
+foxcuda_status foxcuda_tp_p2p_row(foxcuda_context *c, uint32_t layer, int which);
+foxcuda_status foxcuda_tp_p2p_pick(foxcuda_context *c);
+
 /* ---- diagnostics (no upstream counterpart; upstream only times whole evals,
  * src/forward.c:421-435) ------------------------------------------------- */
 

@@ -20,6 +20,7 @@
 #include "tc.cuh"
 #include "tc_kquant.cuh"
 #include "prefill.cuh"
+#include "p2p.cuh"
 
 using namespace fox;
 
@@ -1267,6 +1268,13 @@ struct foxcuda_context {
   int* pf_pos = nullptr;
   float* rows_logits = nullptr;  // foxcuda_eval_all staging, rows_cap x n_vocab
   size_t rows_cap = 0;
+  // tensor-parallel exchanges over peer memory (p2p.cuh)
+  uint8_t* arena = nullptr;
+  size_t terms_d_off = 0;
+  int stride_o = 0, stride_d = 0;
+  uint8_t* peer_arena[TPX_MAX] = {};
+  bool p2p = false;
+  float* x_small = nullptr;  // [0..1] global absmax (o, down), [2..3] best pair, [4..] pairs
 };
 
 struct foxcuda_sampler {
@@ -1288,6 +1296,8 @@ extern "C" void foxcuda_context_destroy(foxcuda_context* c) {
   if (!c) return;
   cudaSetDevice(c->m->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  for (int k = 0; k < TPX_MAX; ++k)
+    if (c->peer_arena[k] && c->peer_arena[k] != c->arena) cudaIpcCloseMemHandle(c->peer_arena[k]);
   if (c->g_body) cudaGraphExecDestroy(c->g_body);
   if (c->g_full) cudaGraphExecDestroy(c->g_full);
   for (void* p : c->allocs) cudaFree(p);
@@ -2725,7 +2735,146 @@ extern "C" foxcuda_status foxcuda_tp_tokens(foxcuda_context* c, uint32_t first_p
   CK(cudaStreamSynchronize(c->stream), "tp sync");
   for (size_t i = 0; i < n; ++i)
     CK(cudaMemcpy(out + i, c->ring + (first_pos + i) % c->n_ctx, 4, cudaMemcpyDeviceToHost), "tp tokens");
+  uint32_t code = 0;
+  CK(cudaMemcpy(&code, c->err_dev, 4, cudaMemcpyDeviceToHost), "tp error word");
+  if (code) {
+    cudaMemset(c->err_dev, 0, 4);
+    return fail(FOXCUDA_ERR_INTERNAL, "device: a bounded wait gave up (code %u: %s); the tokens are not valid",
+                code, code == 2 ? "a peer's exchange did not arrive" : "weights did not reach shared memory");
+  }
   return FOXCUDA_OK;
+}
+
+// ---- exchanges over peer memory (p2p.cuh) ------------------------------------
+
+static uint32_t terms_per_block(int t) { return t == T_Q4_K ? 8u : t == T_Q6_K ? 4u : 1u; }
+
+static XParams xparams(const foxcuda_context* c) {
+  XParams x;
+  memset(&x, 0, sizeof x);
+  for (int k = 0; k < TPX_MAX; ++k) x.peers[k] = c->peer_arena[k];
+  x.rank = c->m->tp_rank;
+  x.world = c->m->tp_size;
+  x.pos = c->pos_dev;
+  x.err = c->err_dev;
+  return x;
+}
+
+extern "C" foxcuda_status foxcuda_tp_p2p_export(foxcuda_context* c, void* handle) {
+  if (!c || !handle) return fail(FOXCUDA_ERR_ARG, "tp_p2p_export: null argument");
+  foxcuda_model* m = c->m;
+  if (m->tp_size > TPX_MAX) return fail(FOXCUDA_ERR_UNSUPPORTED, "tp_p2p: at most %d shards", TPX_MAX);
+  cudaSetDevice(m->device);
+  if (!c->arena) {
+    uint32_t to = 1, td = 1, fmax = 1;
+    for (const LayerW& L : m->layers) {
+      to = std::max(to, terms_per_block(L.o.type));
+      td = std::max(td, terms_per_block(L.down.type));
+    }
+    for (int k = 0; k < m->tp_size; ++k) fmax = std::max(fmax, m->f_blocks_all[k]);
+    c->stride_o = (int)(std::max(1u, m->o_blocks) * to);
+    c->stride_d = (int)(fmax * td);
+    const size_t E = m->info.n_embd;
+    const size_t off_d = (AR_TERMS + E * (size_t)c->stride_o * 4 + 255) / 256 * 256;
+    const size_t bytes = off_d + E * (size_t)c->stride_d * 4;
+    void* p = nullptr;
+    CK(ctx_alloc(c, bytes, &p), "exchange arena");
+    CK(cudaMemset(p, 0, bytes), "exchange arena");
+    c->arena = (uint8_t*)p;
+    c->terms_d_off = off_d;
+    CK(ctx_alloc(c, (4 + 2 * TPX_MAX) * 4, (void**)&c->x_small), "exchange scalars");
+  }
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, c->arena), "exchange handle");
+  memcpy(handle, &h, sizeof h);
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_tp_p2p_open(foxcuda_context* c, const void* handles) {
+  if (!c || !handles) return fail(FOXCUDA_ERR_ARG, "tp_p2p_open: null argument");
+  if (!c->arena) return fail(FOXCUDA_ERR_ARG, "tp_p2p_open: export this context's arena first");
+  if (c->p2p) return fail(FOXCUDA_ERR_ARG, "tp_p2p_open: the peers are already open");
+  cudaSetDevice(c->m->device);
+  for (int k = 0; k < c->m->tp_size; ++k) {
+    if (k == c->m->tp_rank) {
+      c->peer_arena[k] = c->arena;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, (const uint8_t*)handles + (size_t)k * sizeof h, sizeof h);
+    void* p = nullptr;
+    CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "open a peer's arena");
+    c->peer_arena[k] = (uint8_t*)p;
+  }
+  c->p2p = true;
+  return FOXCUDA_OK;
+}
+
+// Zero this rank's slots (after foxcuda_context_reset the epochs repeat).
+// Every rank clears before any rank's next exchange.
+extern "C" foxcuda_status foxcuda_tp_p2p_clear(foxcuda_context* c) {
+  if (!c || !c->arena) return fail(FOXCUDA_ERR_ARG, "tp_p2p_clear: no arena");
+  cudaSetDevice(c->m->device);
+  CK(cudaStreamSynchronize(c->stream), "tp sync");
+  CK(cudaMemset(c->arena, 0, AR_TERMS), "clear slots");
+  return FOXCUDA_OK;
+}
+
+// foxcuda_tp_amax + max-allreduce + foxcuda_tp_terms + all-gather +
+// foxcuda_tp_fold, with the two exchanges over peer memory: the same values
+// in the same order, four launches and no host collective.
+extern "C" foxcuda_status foxcuda_tp_p2p_row(foxcuda_context* c, uint32_t layer, int which) {
+  foxcuda_status st = tp_check(c, layer, true);
+  if (st) return st;
+  if (!c->p2p) return fail(FOXCUDA_ERR_ARG, "tp_p2p_row: open the peers first");
+  if (which != 0 && which != 1) return fail(FOXCUDA_ERR_ARG, "tp_p2p_row: which is 0 (o) or 1 (down)");
+  const foxcuda_model* m = c->m;
+  const PackedMat& W = which == 0 ? m->layers[layer].o : m->layers[layer].down;
+  const bool tern = W.type == T_TQ1_0 || W.type == T_TQ2_0;
+  const XParams x = xparams(c);
+  const int phase = 2 * (int)layer + which + 1;
+  float* amax = c->x_small + which;
+  if (tern) {
+    const int n = which == 0 ? (int)(m->loc.n_head * m->info.head_dim) : (int)m->loc.n_ff;
+    amax_x_kernel<<<1, 1024, 0, c->stream>>>(x, which == 0 ? c->att : c->h, n, which, phase, amax);
+    CK(cudaGetLastError(), "tp amax exchange");
+  }
+  const size_t off = which == 0 ? AR_TERMS : c->terms_d_off;
+  const int stride = which == 0 ? c->stride_o : c->stride_d;
+  st = foxcuda_tp_terms(c, layer, which, tern ? amax : nullptr, (float*)(c->arena + off), (uint32_t)stride);
+  if (st) return st;
+  signal_x_kernel<<<1, 32, 0, c->stream>>>(x, which, phase);
+  FoldXParams f;
+  memset(&f, 0, sizeof f);
+  f.terms_off = off;
+  f.rows = (int)m->info.n_embd;
+  f.stride = stride;
+  f.ternary = tern;
+  f.which = which;
+  f.phase = phase;
+  const uint32_t nt = terms_per_block(W.type);
+  for (int k = 0; k < m->tp_size; ++k) f.count[k] = (int)((which == 0 ? m->o_blocks : m->f_blocks_all[k]) * nt);
+  f.amax = amax;
+  f.x = c->x;
+  fold_x_kernel<<<(f.rows + 255) / 256, 256, 0, c->stream>>>(x, f);
+  CK(cudaGetLastError(), "tp fold exchange");
+  if (c->trace_on && which == 1)
+    CK(cudaMemcpyAsync(c->trace + (size_t)(layer + 1) * m->info.n_embd, c->x, m->info.n_embd * 4,
+                       cudaMemcpyDeviceToDevice, c->stream), "trace");
+  return FOXCUDA_OK;
+}
+
+// foxcuda_tp_head + all-gather of the pairs + foxcuda_tp_pick over peer memory.
+extern "C" foxcuda_status foxcuda_tp_p2p_pick(foxcuda_context* c) {
+  foxcuda_status st = tp_check(c, 0, false);
+  if (st) return st;
+  if (!c->p2p) return fail(FOXCUDA_ERR_ARG, "tp_p2p_pick: open the peers first");
+  float* best = c->x_small + 2;
+  float* pairs = c->x_small + 4;
+  if ((st = foxcuda_tp_head(c, best))) return st;
+  pick_x_kernel<<<1, 32, 0, c->stream>>>(xparams(c), best, pairs);
+  CK(cudaGetLastError(), "tp pick exchange");
+  return foxcuda_tp_pick(c, pairs);
 }
 
 // ---------------------------------------------------------------------------

@@ -1,0 +1,177 @@
+// Tensor-parallel exchanges over peer memory (NVLink), in place of the four
+// NCCL collectives per layer of the sharded decode step.
+//
+// Every rank owns an exchange arena in its own device memory, shared with the
+// other ranks through CUDA IPC (plain peer loads and stores; no multicast):
+//   u64 amax[2][8]    at AR_AMAX   {epoch, absmax bits} of each rank, o / down
+//   u64 pick[8][2]    at AR_PICK   {epoch, value bits}, {epoch, index} of each rank
+//   u32 ready[2][8]   at AR_READY  epoch at which each rank's terms are complete
+//   float terms_o     at AR_TERMS  this rank's o terms   [n_embd][stride_o]
+//   float terms_d     after it     this rank's down terms [n_embd][stride_d]
+// A rank writes its slot in every rank's arena (its own included) and reads
+// the slots of its own arena; the block terms stay where they were written
+// and are read from the owner's arena.
+//
+// Epochs come from the device position, ((pos + 1) << 8) | phase with phase
+// 2 * layer + which + 1 (the pick is 255), so a captured step needs no host
+// input and every exchange of a run has its own epoch. A rank overwrites a
+// slot of the same phase only after an exchange that every rank reaches only
+// after reading that slot, so no value is lost. A slot is published with
+// st.release.sys and read with ld.acquire.sys. Every wait gives up after
+// about a second, sets the context's error word and lets the kernel finish.
+#pragma once
+
+#include "common.cuh"
+
+namespace fox {
+
+constexpr int TPX_MAX = 8;
+constexpr size_t AR_AMAX = 0, AR_PICK = 128, AR_READY = 256, AR_TERMS = 1024;
+
+struct XParams {
+  uint8_t* peers[TPX_MAX];  // every rank's arena, mapped here (this rank's own at [rank])
+  int rank, world;
+  const int* pos;           // device position: the epochs
+  int* err;                 // set to 2 when a wait gives up
+};
+
+FOX_DEV void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+FOX_DEV void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+FOX_DEV uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+FOX_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+FOX_DEV uint32_t tp_epoch(const int* pos, int phase) {
+  return ((uint32_t)(*pos + 1) << 8) | (uint32_t)phase;
+}
+
+// Bounded wait until the 32-bit word at p reaches ep (about a second).
+FOX_DEV bool wait_u32(const uint32_t* p, uint32_t ep) {
+  for (int i = 0; i < (1 << 22); ++i) {
+    if (ld_acquire_sys(p) == ep) return true;
+    if (i >= 16) __nanosleep(256);
+  }
+  return false;
+}
+FOX_DEV bool wait_hi(const uint64_t* p, uint32_t ep, uint64_t* out) {
+  for (int i = 0; i < (1 << 22); ++i) {
+    const uint64_t w = ld_acquire_sys(p);
+    if ((uint32_t)(w >> 32) == ep) { *out = w; return true; }
+    if (i >= 16) __nanosleep(256);
+  }
+  return false;
+}
+
+// This shard's absmax of v (one CTA), published to every rank; the largest
+// over all ranks (the absmax of the whole vector) into out[0].
+__global__ void __launch_bounds__(1024) amax_x_kernel(const XParams x, const float* __restrict__ v, int n,
+                                                      int which, int phase, float* out) {
+  __shared__ float red[32];
+  float am = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) am = absmax_acc(am, v[i]);
+  am = block_reduce<float>(am, red, OpMax(), 0.0f);
+  if (threadIdx.x != 0) return;
+  const uint32_t ep = tp_epoch(x.pos, phase);
+  const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(am);
+  for (int k = 0; k < x.world; ++k)
+    st_release_sys(reinterpret_cast<uint64_t*>(x.peers[k] + AR_AMAX) + which * TPX_MAX + x.rank, word);
+  const uint64_t* mine = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + AR_AMAX) + which * TPX_MAX;
+  float g = 0.0f;
+  for (int k = 0; k < x.world; ++k) {
+    uint64_t w = 0;
+    if (!wait_hi(mine + k, ep, &w)) {
+      if (x.err) atomicExch(x.err, 2);
+      g = 0.0f;
+      break;
+    }
+    g = fmaxf(g, __uint_as_float((uint32_t)w));
+  }
+  out[0] = g;
+}
+
+// After this rank's terms kernel (the previous launch): its terms are complete.
+__global__ void signal_x_kernel(const XParams x, int which, int phase) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  __threadfence_system();
+  const uint32_t ep = tp_epoch(x.pos, phase);
+  for (int k = 0; k < x.world; ++k)
+    st_release_sys(reinterpret_cast<uint32_t*>(x.peers[k] + AR_READY) + which * TPX_MAX + x.rank, ep);
+}
+
+// fold_kernel (ops.cuh) reading every rank's terms from its arena once all
+// ranks have signalled them: the same sums in the same order.
+struct FoldXParams {
+  size_t terms_off;     // byte offset of this projection's terms in an arena
+  int rows, stride, ternary, which, phase;
+  int count[TPX_MAX];   // terms per row of each rank
+  const float* amax;    // ternary: the global absmax
+  float* x;             // residual, += the row values
+};
+
+__global__ void fold_x_kernel(const XParams x, const FoldXParams f) {
+  __shared__ int ok_sh;
+  const uint32_t ep = tp_epoch(x.pos, f.phase);
+  const uint32_t* ready = reinterpret_cast<const uint32_t*>(x.peers[x.rank] + AR_READY) + f.which * TPX_MAX;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int k = 0; k < x.world && ok; ++k) ok = wait_u32(ready + k, ep);
+    ok_sh = ok;
+    if (!ok && x.err) atomicExch(x.err, 2);
+  }
+  __syncthreads();
+  if (!ok_sh) return;
+  // each thread's own acquire of the flags orders its reads of the terms
+  for (int k = 0; k < x.world; ++k) (void)ld_acquire_sys(ready + k);
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= f.rows) return;
+  float acc = 0.0f;
+  for (int k = 0; k < x.world; ++k) {
+    const float* t = reinterpret_cast<const float*>(x.peers[k] + f.terms_off) + (size_t)r * f.stride;
+    for (int j = 0; j < f.count[k]; ++j) acc = __fadd_rn(acc, __ldcg(t + j));
+  }
+  float v = acc;
+  if (f.ternary) {
+    const float amax = *f.amax;
+    v = __fmul_rn(acc, amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f);
+  }
+  f.x[r] = __fadd_rn(f.x[r], v);
+}
+
+// This rank's {value, index} (tp_argmax_kernel) published; every rank's pair
+// into pairs[2k], pairs[2k + 1] for tp_pick_kernel.
+__global__ void pick_x_kernel(const XParams x, const float* __restrict__ best, float* __restrict__ pairs) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint32_t ep = tp_epoch(x.pos, 255);
+  const uint64_t w0 = ((uint64_t)ep << 32) | __float_as_uint(best[0]);
+  const uint64_t w1 = ((uint64_t)ep << 32) | __float_as_uint(best[1]);
+  for (int k = 0; k < x.world; ++k) {
+    uint64_t* slot = reinterpret_cast<uint64_t*>(x.peers[k] + AR_PICK) + 2 * x.rank;
+    st_release_sys(slot, w0);
+    st_release_sys(slot + 1, w1);
+  }
+  const uint64_t* mine = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + AR_PICK);
+  for (int k = 0; k < x.world; ++k) {
+    uint64_t a = 0, b = 0;
+    if (!wait_hi(mine + 2 * k, ep, &a) || !wait_hi(mine + 2 * k + 1, ep, &b)) {
+      if (x.err) atomicExch(x.err, 2);
+      pairs[2 * k] = -CUDART_INF_F;
+      pairs[2 * k + 1] = __uint_as_float(0xffffffffu);
+      continue;
+    }
+    pairs[2 * k] = __uint_as_float((uint32_t)a);
+    pairs[2 * k + 1] = __uint_as_float((uint32_t)b);
+  }
+}
+
+}  // namespace fox

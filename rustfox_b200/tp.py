@@ -41,9 +41,15 @@ class TPContext:
     group spanning the shards (default: the world)."""
 
     def __init__(self, model: api.Model, n_ctx: int, kv: str = "f16", attn_exact: bool = False,
-                 group=None):
+                 group=None, exchange: str = "nccl"):
+        """exchange: "nccl" (torch.distributed collectives between the
+        library's steps) or "p2p" (the library's own exchanges over peer
+        memory, foxcuda_tp_p2p_*; no host collective in a step)."""
         import torch
         import torch.distributed as dist
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange is 'nccl' or 'p2p', not {exchange!r}")
+        self.exchange = exchange
         self.dist, self.group = dist, group
         self.model = model
         self.ctx = api.Context(model, n_ctx, kv, attn_exact)
@@ -65,6 +71,24 @@ class TPContext:
         self.gath_d = torch.zeros(self.world * self.n_embd * self.stride_d, **f)
         self.best = torch.zeros(2, **f)
         self.pairs = torch.zeros(2 * self.world, **f)
+        if exchange == "p2p":
+            self._open_peers()
+
+    def _open_peers(self):
+        """Every rank's exchange arena handle to every rank, then the peers
+        mapped (the one host collective, at setup)."""
+        L = api.lib()
+        n = 64  # FOXCUDA_IPC_HANDLE_BYTES
+        h = (C.c_uint8 * n)()
+        api._check(L.foxcuda_tp_p2p_export(self.ctx.h, h))
+        handles = [bytes(h)]
+        if self.world > 1:
+            handles = [None] * self.world
+            self.dist.all_gather_object(handles, bytes(h), group=self.group)
+        buf = (C.c_uint8 * (n * self.world)).from_buffer_copy(b"".join(handles))
+        api._check(L.foxcuda_tp_p2p_open(self.ctx.h, buf))
+        if self.world > 1:
+            self.dist.barrier(group=self.group)
 
     @staticmethod
     def _p(t, off=0):
@@ -82,6 +106,9 @@ class TPContext:
 
     def _row_parallel(self, layer: int, which: int):
         L = api.lib()
+        if self.exchange == "p2p":
+            api._check(L.foxcuda_tp_p2p_row(self.ctx.h, layer, which))
+            return
         amax = self.amax[which:which + 1]
         terms, gath, stride = ((self.terms_o, self.gath_o, self.stride_o) if which == 0
                                else (self.terms_d, self.gath_d, self.stride_d))
@@ -103,7 +130,9 @@ class TPContext:
                 self._row_parallel(l, 0)
                 api._check(L.foxcuda_tp_ffn(self.ctx.h, l))
                 self._row_parallel(l, 1)
-            if pick:
+            if pick and self.exchange == "p2p":
+                api._check(L.foxcuda_tp_p2p_pick(self.ctx.h))
+            elif pick:
                 api._check(L.foxcuda_tp_head(self.ctx.h, self._p(self.best)))
                 self._all_gather(self.pairs, self.best)
                 api._check(L.foxcuda_tp_pick(self.ctx.h, self._p(self.pairs)))
