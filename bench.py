@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--gemm", default=None, metavar="M[,M...]",
                     help="time the M-token tensor-core pass over one layer's matrices "
                          "(prefill / verification) instead of decoding")
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
+                    help="with --tp: collectives through NCCL, or the library's own exchanges "
+                         "over peer memory")
     ap.add_argument("--split", action="store_true",
                     help="with --gemm: also time the split form of the pass")
     ap.add_argument("--prefill", action="store_true",
@@ -371,7 +374,7 @@ def run_tp(args):
     model = rf.Model.from_synthetic(host, device=local, tp_rank=rank, tp_size=world)
     del host
     n_ctx = args.prompt + args.warmup + args.steps + 8
-    ctx = TPContext(model, n_ctx, kv="f16")
+    ctx = TPContext(model, n_ctx, kv="f16", exchange=args.exchange)
     prompt = synth.random_prompt(cfg, args.prompt, seed=1)
     ctx.generate(prompt, max(3, args.warmup), graphs=True)  # captures the step graph
     torch.cuda.synchronize()
@@ -395,9 +398,15 @@ def run_tp(args):
             "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} greedy decode, one "
                                    f"sequence over {world} GPU(s)", "prompt": args.prompt,
                        "kv_cache": "f16", "parallelism": f"tp{world}",
-                       "collectives": "torch.distributed NCCL per row-parallel GEMV (4 per layer), "
-                                      "the whole step replayed as one CUDA graph"}}),
+                       "collectives": (
+                           "torch.distributed NCCL per row-parallel GEMV (4 per layer), the whole "
+                           "step replayed as one CUDA graph" if args.exchange == "nccl" else
+                           "the library's exchanges over peer memory (CUDA IPC, 4 kernels per "
+                           "row-parallel GEMV, no host collective), the whole step replayed as one "
+                           "CUDA graph")}}),
               flush=True)
+    if world > 1:
+        dist.barrier()  # no rank unmaps a peer arena another may still read
     ctx.close()
     model.close()
     if world > 1:
