@@ -1,0 +1,135 @@
+"""The slot protocol of the tensor-parallel exchanges over peer memory
+(rustfox_b200/csrc/p2p.cuh), played out on the CPU: threads stand in for the
+ranks and share arenas with the same slots, epochs and readiness flags, with
+random delays between steps.
+
+What must hold is what the device code relies on:
+- every exchange reads each rank's value of its own epoch, never a later
+  one. A rank overwrites a slot of a given phase only after an exchange that
+  every rank reaches after reading it;
+- the fold, reading every rank's terms in rank then block order, gives the
+  unsharded in-order sum bit for bit.
+
+Each rank's step follows foxcuda_tp_p2p_row and foxcuda_tp_p2p_pick: publish
+the absmax into every arena, wait for all ranks' absmax in its own arena,
+write its terms, signal ready into every arena, wait for all ranks' ready,
+fold. The pick publishes a {value, index} pair, waits, and takes the first
+strict maximum.
+"""
+import random
+import threading
+import time
+
+import numpy as np
+import pytest
+
+TPX_MAX = 8
+
+
+def _epoch(pos, phase):
+    return ((pos + 1) << 8) | phase
+
+
+class Arena:
+    def __init__(self, rows, stride):
+        self.amax = np.zeros((2, TPX_MAX), dtype=np.uint64)
+        self.pick = np.zeros((TPX_MAX, 2), dtype=np.uint64)
+        self.ready = np.zeros((2, TPX_MAX), dtype=np.uint32)
+        self.terms = [np.zeros((rows, stride), dtype=np.float32) for _ in range(2)]
+
+
+def _wait(cond, what, limit=5.0):
+    t0 = time.time()
+    while not cond():
+        if time.time() - t0 > limit:
+            raise TimeoutError(what)
+        time.sleep(0)
+
+
+def _run(world, n_layer, n_tok, rows, blocks, seed):
+    rng = np.random.default_rng(seed)
+    # per (token, layer, which): every rank's shard absmax and block terms
+    amax = rng.random((n_tok, n_layer, 2, world)).astype(np.float32)
+    terms = rng.normal(0, 1, (n_tok, n_layer, 2, world, rows, blocks)).astype(np.float32)
+    picks = rng.normal(0, 1, (n_tok, world)).astype(np.float32)
+    arenas = [Arena(rows, blocks) for _ in range(world)]
+    out = [dict() for _ in range(world)]
+    errors = []
+
+    def rank_main(r):
+        rnd = random.Random(seed * 31 + r)
+        try:
+            for pos in range(n_tok):
+                for layer in range(n_layer):
+                    for which in (0, 1):
+                        phase = 2 * layer + which + 1
+                        ep = _epoch(pos, phase)
+                        time.sleep(rnd.random() * 1e-4)
+                        word = (ep << 32) | int(np.float32(amax[pos, layer, which, r]).view(np.uint32))
+                        for k in range(world):   # amax_x_kernel: publish
+                            arenas[k].amax[which, r] = np.uint64(word)
+                        g = np.float32(0)
+                        for k in range(world):   # ... and wait in the own arena
+                            _wait(lambda: int(arenas[r].amax[which, k]) >> 32 >= ep, "amax")
+                            w = int(arenas[r].amax[which, k])
+                            assert w >> 32 == ep, f"rank {r} saw a later absmax epoch"
+                            g = max(g, np.uint32(w & 0xffffffff).view(np.float32))
+                        out[r][("amax", pos, layer, which)] = g
+                        time.sleep(rnd.random() * 1e-4)
+                        arenas[r].terms[which][:] = terms[pos, layer, which, r]   # terms GEMV
+                        for k in range(world):   # signal_x_kernel
+                            arenas[k].ready[which, r] = np.uint32(ep)
+                        for k in range(world):   # fold_x_kernel: wait ...
+                            _wait(lambda: int(arenas[r].ready[which, k]) >= ep, "ready")
+                            assert int(arenas[r].ready[which, k]) == ep, f"rank {r} saw a later ready epoch"
+                        acc = np.zeros(rows, dtype=np.float32)
+                        for k in range(world):   # ... then rank order, block order
+                            t = arenas[k].terms[which]
+                            for j in range(blocks):
+                                acc = (acc + t[:, j]).astype(np.float32)
+                        out[r][("fold", pos, layer, which)] = acc
+                ep = _epoch(pos, 255)              # pick_x_kernel
+                v = int(np.float32(picks[pos, r]).view(np.uint32))
+                for k in range(world):
+                    arenas[k].pick[r, 0] = np.uint64((ep << 32) | v)
+                    arenas[k].pick[r, 1] = np.uint64((ep << 32) | (r * 1000 + pos))
+                best = None
+                for k in range(world):
+                    _wait(lambda: int(arenas[r].pick[k, 1]) >> 32 >= ep, "pick")
+                    a, b = int(arenas[r].pick[k, 0]), int(arenas[r].pick[k, 1])
+                    assert a >> 32 == ep and b >> 32 == ep, f"rank {r} saw a later pick epoch"
+                    val = np.uint32(a & 0xffffffff).view(np.float32)
+                    if best is None or val > best[0]:
+                        best = (val, b & 0xffffffff)
+                out[r][("pick", pos)] = best
+        except BaseException as e:  # noqa: BLE001 - reported to the main thread
+            errors.append(e)
+
+    threads = [threading.Thread(target=rank_main, args=(r,)) for r in range(world)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert not errors, errors
+    return out, amax, terms, picks
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_exchange_protocol_reads_every_value_once_and_folds_in_order(world):
+    n_layer, n_tok, rows, blocks = 3, 4, 5, 3
+    out, amax, terms, picks = _run(world, n_layer, n_tok, rows, blocks, seed=world)
+    for pos in range(n_tok):
+        for layer in range(n_layer):
+            for which in (0, 1):
+                want_amax = np.float32(amax[pos, layer, which].max())
+                want = np.zeros(rows, dtype=np.float32)
+                for k in range(world):
+                    for j in range(blocks):
+                        want = (want + terms[pos, layer, which, k, :, j]).astype(np.float32)
+                for r in range(world):
+                    assert out[r][("amax", pos, layer, which)] == want_amax
+                    assert np.array_equal(out[r][("fold", pos, layer, which)].view(np.uint32),
+                                          want.view(np.uint32))
+        k = int(np.argmax(picks[pos]))
+        for r in range(world):
+            assert out[r][("pick", pos)] == (picks[pos, k], k * 1000 + pos)
