@@ -1496,6 +1496,45 @@ static cudaError_t launch_attn_tile(const AttnParams& ap, dim3 grid, cudaStream_
   }
 }
 
+// The cluster attention of every sequence of a decode batch in one launch
+// (grid z = sequence; AttnParams' per-sequence fields).
+template <int HD, int G, bool F16>
+static cudaError_t launch_attn_seqs_g(const AttnParams& ap, int n_seq, cudaStream_t s) {
+  constexpr size_t sm = attn_tile_smem<HD, F16>();
+  static size_t marks[kMaxDevices] = {};
+  cudaError_t e = opt_in_smem(attention_cluster_kernel<HD, G, F16, true>, sm, marks);
+  if (e != cudaSuccess) return e;
+  attention_cluster_kernel<HD, G, F16, true><<<dim3(ATTN_SPLITS, ap.n_kv, n_seq), 128, sm, s>>>(ap);
+  return cudaGetLastError();
+}
+
+template <int HD, bool F16>
+static cudaError_t launch_attn_seqs_t(const AttnParams& ap, int n_seq, cudaStream_t s) {
+  switch (ap.n_head / ap.n_kv) {
+    case 1: return launch_attn_seqs_g<HD, 1, F16>(ap, n_seq, s);
+    case 2: return launch_attn_seqs_g<HD, 2, F16>(ap, n_seq, s);
+    case 4: return launch_attn_seqs_g<HD, 4, F16>(ap, n_seq, s);
+    case 8: return launch_attn_seqs_g<HD, 8, F16>(ap, n_seq, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// Whether a batch can take the one-launch form (the cluster kernel's shapes;
+// FOXCUDA_BATCH_ATTN_LOOP=1 keeps one launch per sequence).
+static bool attn_seqs_ok(const AttnParams& ap, bool exact) {
+  static const bool loop = [] {
+    const char* v = getenv("FOXCUDA_BATCH_ATTN_LOOP");
+    return v && v[0] == '1';
+  }();
+  return !loop && !exact && (ap.hd == 64 || ap.hd == 128) && tile_group_ok(ap.n_head / ap.n_kv);
+}
+
+static cudaError_t launch_attn_seqs(const AttnParams& ap, int n_seq, cudaStream_t s) {
+  if (ap.hd == 128) return ap.kv_f16 ? launch_attn_seqs_t<128, true>(ap, n_seq, s)
+                                     : launch_attn_seqs_t<128, false>(ap, n_seq, s);
+  return ap.kv_f16 ? launch_attn_seqs_t<64, true>(ap, n_seq, s) : launch_attn_seqs_t<64, false>(ap, n_seq, s);
+}
+
 // One decode attention over a K/V cache: the serial upstream-order kernel,
 // or the split-K kernels (the tiled one for head_dim 64 and 128).
 static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t s) {
@@ -2224,15 +2263,26 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
         b->qkv, nqkv, nq, nkv, hd, (int)c0->n_ctx, b->pos, b->kbase, b->vbase, (size_t)l * layer_bytes,
         c0->rope_cos, c0->rope_sin, c0->kv_f16, b->q);
     if ((e = cudaGetLastError())) break;
-    for (int i = 0; i < M && !e; ++i) {
-      foxcuda_context* c = b->ctx[i];
-      AttnParams ap{};
-      ap.q = b->q + (size_t)i * nq; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
-      ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
-      ap.hd = hd; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
-      ap.pos = c->pos_dev; ap.out = b->att + (size_t)i * nq; ap.part = c->attn_part; ap.counters = c->attn_cnt;
-      ap.scale = 1.0f / sqrtf((float)hd);
-      e = run_attention(ap, c->attn_exact, s);
+    AttnParams all{};
+    all.q = b->q; all.out = b->att; all.seq_stride = nq;
+    all.pos_list = b->pos; all.k_list = b->kbase; all.v_list = b->vbase; all.layer_off = (size_t)l * layer_bytes;
+    all.kv_f16 = c0->kv_f16; all.n_ctx = c0->n_ctx;
+    all.hd = hd; all.n_head = mi.n_head; all.n_kv = mi.n_head_kv; all.S_max = c0->S_max;
+    all.scale = 1.0f / sqrtf((float)hd);
+    if (attn_seqs_ok(all, c0->attn_exact)) {
+      e = launch_attn_seqs(all, M, s);
+    } else {
+      for (int i = 0; i < M && !e; ++i) {
+        foxcuda_context* c = b->ctx[i];
+        AttnParams ap{};
+        ap.q = b->q + (size_t)i * nq; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+        ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
+        ap.hd = hd; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.S_max = c->S_max;
+        ap.pos = c->pos_dev; ap.out = b->att + (size_t)i * nq; ap.part = c->attn_part;
+        ap.counters = c->attn_cnt;
+        ap.scale = 1.0f / sqrtf((float)hd);
+        e = run_attention(ap, c->attn_exact, s);
+      }
     }
     if (e) break;
     if ((e = quant_rows_to<false>(b->att, nq, nullptr, eps, 256, M, b->xq, b->xs, s))) break;

@@ -102,6 +102,14 @@ struct AttnParams {
   // kernel that wrote q and position *pos of the cache; rows before *pos
   // were written by earlier launches and are staged before the wait
   int pdl;
+  // decode batches (attention_cluster_kernel<..., SEQS>): sequence z reads
+  // q + z * seq_stride, writes out + z * seq_stride, its position at
+  // *pos_list[z] and its layer's caches at k_list[z] / v_list[z] + layer_off
+  int seq_stride;
+  int* const* pos_list;
+  void* const* k_list;
+  void* const* v_list;
+  size_t layer_off;
 };
 
 constexpr int ATTN_THREADS = 128;
@@ -295,7 +303,9 @@ FOX_DEV const float* cluster_peer(const float* p, unsigned rank) {
   return reinterpret_cast<const float*>(r);
 }
 
-template <int HD, int G, bool F16>
+// SEQS: one launch for a decode batch; grid z is the sequence, whose q, out,
+// position and caches come from AttnParams' per-sequence fields.
+template <int HD, int G, bool F16, bool SEQS = false>
 __global__ void __cluster_dims__(ATTN_SPLITS, 1, 1) __launch_bounds__(128)
 attention_cluster_kernel(const AttnParams p) {
   griddep_launch_dependents();  // the o projection may start streaming its weights
@@ -303,7 +313,20 @@ attention_cluster_kernel(const AttnParams p) {
   constexpr int ESZ = F16 ? 2 : 4, RB = HD * ESZ, KSTRIDE = RB + 16;
   const int r = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;  // r = rank in the cluster
   const int lane = tid & 31, warp = tid >> 5;
-  const int P = *p.pos + 1;
+  const float* q_in = p.q;
+  float* out = p.out;
+  const int* pos = p.pos;
+  const void* kcache = p.kcache;
+  const void* vcache = p.vcache;
+  if constexpr (SEQS) {
+    const int z = blockIdx.z;
+    q_in = p.q + (size_t)z * p.seq_stride;
+    out = p.out + (size_t)z * p.seq_stride;
+    pos = p.pos_list[z];
+    kcache = reinterpret_cast<const uint8_t*>(p.k_list[z]) + p.layer_off;
+    vcache = reinterpret_cast<const uint8_t*>(p.v_list[z]) + p.layer_off;
+  }
+  const int P = *pos + 1;
   const int chunk = (P + ATTN_SPLITS - 1) / ATTN_SPLITS;
   const int j0 = min(P, r * chunk), j1 = min(P, j0 + chunk);
 
@@ -318,8 +341,8 @@ attention_cluster_kernel(const AttnParams p) {
   __shared__ float ew[ATTN_SPLITS][G], lw[ATTN_SPLITS][G];
 
   const size_t head = (size_t)g * p.n_ctx * HD;
-  const uint8_t* kg = reinterpret_cast<const uint8_t*>(p.kcache) + head * ESZ;
-  const uint8_t* vg = reinterpret_cast<const uint8_t*>(p.vcache) + head * ESZ;
+  const uint8_t* kg = reinterpret_cast<const uint8_t*>(kcache) + head * ESZ;
+  const uint8_t* vg = reinterpret_cast<const uint8_t*>(vcache) + head * ESZ;
   // rows t0 .. t0+n-1 of the cache into tile rows 0 .. n-1, except position skip
   auto stage = [&](int t0, int n, int skip) {
     const int pieces = n * (RB / 16);
@@ -343,7 +366,7 @@ attention_cluster_kernel(const AttnParams p) {
       cp_async16(sK + (size_t)row * KSTRIDE + c * 16, kg + (size_t)cur * RB + c * 16);
       cp_async16(sV + (size_t)row * RB + c * 16, vg + (size_t)cur * RB + c * 16);
     }
-  for (int i = tid; i < G * HD; i += NT) qs[i / HD][i % HD] = p.q[(size_t)g * G * HD + i];
+  for (int i = tid; i < G * HD; i += NT) qs[i / HD][i % HD] = q_in[(size_t)g * G * HD + i];
 
   const int d = tid % HD, jsub = tid / HD;
   float m[G], l[G], acc[G];
@@ -466,7 +489,7 @@ attention_cluster_kernel(const AttnParams p) {
 #pragma unroll
     for (int t = 0; t < ATTN_SPLITS; ++t)
       if (lw[t][h] > 0.0f) A = fmaf(cluster_peer(&part[h][dd], t)[0], ew[t][h], A);
-    p.out[((size_t)g * G + h) * HD + dd] = A / rsum[0][h];
+    out[((size_t)g * G + h) * HD + dd] = A / rsum[0][h];
   }
   cluster_sync_all();  // no CTA leaves while another may still read its partial
 }
