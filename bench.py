@@ -213,6 +213,32 @@ def reference_decode(model, cfg, warmup: int, steps: int, budget_s: float = 60.0
     return n / total, cores, sample, kind
 
 
+def reference_cli(model, n_gen: int = 8):
+    """Upstream's own `fox run` binary (oracle/_ref/fox, built from the upstream
+    sources) on the same model with its byte-level vocabulary: --temp 0 (the
+    CLI's greedy with its default repeat penalty), all cores, the gen tok/s it
+    prints (src/cli.c:364-369). The prompt has no spaces: the CLI sizes its id
+    buffer from the prompt's length, and each space costs three byte ids.
+    Returns a dict for the record, or None when the binary is absent."""
+    from oracle import oracle as O
+    from rustfox_b200 import synth
+    fox = os.path.join(os.path.dirname(O.REF_FAST_SO), "fox")
+    if not os.path.exists(fox):
+        return None
+    prompt = "thequickbrownfox"
+    with tempfile.TemporaryDirectory() as d:
+        path = synth.write_gguf(model, os.path.join(d, "model.gguf"), tokenizer=True)
+        cmd = [fox, "run", path, "-p", prompt, "-n", str(n_gen), "--temp", "0", "--ctx", "64"]
+        res = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    out = {"command": "fox run model.gguf -p " + prompt + f" -n {n_gen} --temp 0 --ctx 64",
+           "exit": res.returncode}
+    for line in res.stderr.splitlines():
+        parts = line.split()
+        if parts and parts[0] in ("prompt", "gen") and "tok/s)" in line:
+            out[f"{parts[0]}_tok_s"] = float(line.rsplit("(", 1)[1].split()[0])
+    return out
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -220,6 +246,7 @@ def run_reference(args):
     from rustfox_b200 import synth
     cfg = synth.CONFIGS[args.config]
     model = synth.generate(cfg)
+    cli = reference_cli(model)
     v, cores, sample, kind = reference_decode(model, cfg, args.warmup, args.steps)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v,
@@ -229,7 +256,8 @@ def run_reference(args):
             "config": {**workload(cfg, args), "kv_cache": "f32 (upstream's cache)"},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
                              "sample": sample},
-            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "fox_run_cli": cli}
     print(json.dumps(line), flush=True)
 
 
