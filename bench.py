@@ -239,6 +239,18 @@ def reference_cli(model, n_gen: int = 8):
     return out
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), for the CPU-baseline record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -255,7 +267,7 @@ def run_reference(args):
             "uniform random prompt ids)",
             "config": {**workload(cfg, args), "kv_cache": "f32 (upstream's cache)"},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
-                             "sample": sample},
+                             "sample": sample, "cpu": cpu_model()},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "fox_run_cli": cli}
     print(json.dumps(line), flush=True)
@@ -347,7 +359,8 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             v, cores, sample, kind = reference_decode(host_model, cfg, 2, 8, budget_s=25.0)
-            cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample}
+            cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample,
+                   "cpu": cpu_model()}
         except Exception as e:  # the baseline is reported, never required
             cpu = {"value": None, "unit": "tok/s", "cores": None, "kind": "reference",
                    "sample": f"failed: {e}"}
