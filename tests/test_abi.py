@@ -78,6 +78,36 @@ def test_gemm_argument_checks_run_before_any_device_call():
     assert L.foxcuda_tp_p2p_row(None, 0, 0) == 1
 
 
+def test_struct_layouts_match_the_header(tmp_path):
+    """Every public struct of include/foxcuda.h has the size and field
+    offsets of its ctypes mirror (compiled with the system C compiler)."""
+    import shutil
+    from rustfox_b200 import api
+    from rustfox_b200.tp import TPShape
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    mirrors = {"foxcuda_model_info": api.ModelInfo, "foxcuda_context_config": api.ContextConfig,
+               "foxcuda_sampler_config": api.SamplerConfig, "foxcuda_tp_shape": TPShape}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "foxcuda.h"', "int main(void) {"]
+    for cname, py in mirrors.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname}.{fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c11", "-I", os.path.join(ROOT, "include"), "-o", str(exe), str(src)],
+                   check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run(
+        [str(exe)], capture_output=True, text=True, check=True).stdout.splitlines())
+    for cname, py in mirrors.items():
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert int(got[f"{cname}.{fname}"]) == getattr(py, fname).offset, f"{cname}.{fname}"
+
+
 def test_python_api_mirrors_upstream_names():
     import rustfox_b200 as rf
     for name in ("gemv", "gemv_tq1_i8", "gemv_tq2_i8", "quantize_activations_i8", "dequant_row",
