@@ -108,6 +108,26 @@ def test_struct_layouts_match_the_header(tmp_path):
             assert int(got[f"{cname}.{fname}"]) == getattr(py, fname).offset, f"{cname}.{fname}"
 
 
+def test_ctypes_prototypes_match_the_header():
+    """Every bound entry point takes as many arguments as its declaration,
+    and a pointer wherever the declaration has one."""
+    from rustfox_b200 import api
+    text = ""
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text += re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+    decls = {}
+    for m in re.finditer(r"\b(foxcuda_\w+)\s*\(([^)]*)\)\s*;", text):
+        params = [p.strip() for p in m.group(2).split(",")]
+        decls[m.group(1)] = [] if params == ["void"] or params == [""] else params
+    assert set(api._PROTOS) <= set(decls), set(api._PROTOS) - set(decls)
+    for name, (_, args) in api._PROTOS.items():
+        params = decls[name]
+        assert len(args) == len(params), f"{name}: {len(args)} bound, {len(params)} declared"
+        for a, p in zip(args, params):
+            if "*" in p:
+                assert a in (ctypes.c_void_p, ctypes.c_char_p) or hasattr(a, "_type_"), f"{name}: {p}"
+
+
 def test_python_api_mirrors_upstream_names():
     import rustfox_b200 as rf
     for name in ("gemv", "gemv_tq1_i8", "gemv_tq2_i8", "quantize_activations_i8", "dequant_row",
