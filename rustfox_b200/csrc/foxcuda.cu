@@ -1615,10 +1615,20 @@ static cudaError_t launch_down(foxcuda_context* c, uint32_t l) {
   return launch_mat(c, W, PRO_VEC, EPI_ADD, p);
 }
 
+// FOXCUDA_HEAD_DEPTH=2: the head with two blocks of look-ahead per warp
+// (twice the bytes in flight at the same occupancy). Off by default.
+static bool head_depth2() {
+  static const bool on = [] {
+    const char* v = getenv("FOXCUDA_HEAD_DEPTH");
+    return v && v[0] == '2';
+  }();
+  return on;
+}
+
 static cudaError_t launch_q8_rows(const GemvParams& p, cudaStream_t s) {
-  auto kern = q8_rows_kernel<PRO_NORM>;
+  auto kern = head_depth2() ? q8_rows_kernel<PRO_NORM, 2> : q8_rows_kernel<PRO_NORM, 1>;
   const size_t smem = (size_t)p.K * 4 + 32 * 8;
-  static size_t marks[kMaxDevices] = {};
+  static size_t marks[kMaxDevices] = {};  // one kernel per process (the variable is read once)
   cudaError_t e = opt_in_smem(kern, smem, marks);
   if (e != cudaSuccess) return e;
   const int pairs = (p.n_rows / 32 + 1) / 2;

@@ -81,8 +81,11 @@ FOX_DEV void q8_block(const Q8Pair& r, const float* xs, float& sa, float& sb) {
   }
 }
 
-template <int PRO>
+// DEPTH: blocks of look-ahead per warp (1, or 2 for twice the bytes in flight
+// at the same occupancy; the arithmetic is the same).
+template <int PRO, int DEPTH = 1>
 __global__ void __launch_bounds__(ROWS_THREADS) q8_rows_kernel(const GemvParams p) {
+  static_assert(DEPTH == 1 || DEPTH == 2, "look-ahead");
   griddep_launch_dependents();
   extern __shared__ __align__(16) unsigned char smem[];
   const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31;
@@ -95,11 +98,13 @@ __global__ void __launch_bounds__(ROWS_THREADS) q8_rows_kernel(const GemvParams 
   const size_t unit_bytes = (size_t)32 * nb * 34;
   int pu = blockIdx.x * warps + (tid >> 5);
 
-  // the first block of this warp's first rows is requested before the wait
-  Q8Pair cur, nxt;
+  // the first block(s) of this warp's first rows are requested before the wait
+  Q8Pair cur, nxt, nxt2;
   if (pu < pairs) {
     const bool hb = 2 * pu + 1 < units;
-    q8_load(cur, p.w + (size_t)(2 * pu) * unit_bytes, p.w + (size_t)(2 * pu + 1) * unit_bytes, nb, 0, lane, hb);
+    const uint8_t* ua = p.w + (size_t)(2 * pu) * unit_bytes;
+    q8_load(cur, ua, ua + unit_bytes, nb, 0, lane, hb);
+    if (DEPTH == 2 && nb > 1) q8_load(nxt, ua, ua + unit_bytes, nb, 1, lane, hb);
   }
   griddep_wait();
 
@@ -123,19 +128,26 @@ __global__ void __launch_bounds__(ROWS_THREADS) q8_rows_kernel(const GemvParams 
     const uint8_t* ub = ua + unit_bytes;
     float acca = 0.0f, accb = 0.0f;
     for (int b = 0; b < nb; ++b) {
-      if (b + 1 < nb) q8_load(nxt, ua, ub, nb, b + 1, lane, hb);
+      if (DEPTH == 1) {
+        if (b + 1 < nb) q8_load(nxt, ua, ub, nb, b + 1, lane, hb);
+      } else {
+        if (b + 2 < nb) q8_load(nxt2, ua, ub, nb, b + 2, lane, hb);
+      }
       float sa, sb;
       q8_block(cur, xs + (size_t)b * 32, sa, sb);
       acca = __fadd_rn(acca, __fmul_rn(h2f(cur.da), sa));
       accb = __fadd_rn(accb, __fmul_rn(h2f(cur.db), sb));
       if (b + 1 < nb) cur = nxt;
+      if (DEPTH == 2 && b + 2 < nb) nxt = nxt2;
     }
     p.out[(size_t)(2 * pu) * 32 + lane] = acca;
     if (hb) p.out[(size_t)(2 * pu + 1) * 32 + lane] = accb;
     const int pn = pu + gridDim.x * warps;
     if (pn < pairs) {
       const bool hn = 2 * pn + 1 < units;
-      q8_load(cur, p.w + (size_t)(2 * pn) * unit_bytes, p.w + (size_t)(2 * pn + 1) * unit_bytes, nb, 0, lane, hn);
+      const uint8_t* na = p.w + (size_t)(2 * pn) * unit_bytes;
+      q8_load(cur, na, na + unit_bytes, nb, 0, lane, hn);
+      if (DEPTH == 2 && nb > 1) q8_load(nxt, na, na + unit_bytes, nb, 1, lane, hn);
     }
   }
 }
