@@ -256,6 +256,10 @@ foxcuda_status foxcuda_context_set_prefill(foxcuda_context *c, int mode);
  *   partial rewind. */
 foxcuda_status foxcuda_eval_all(foxcuda_context *c, const uint32_t *tokens, size_t n,
                                 float *logits_out);
+/* Back to an earlier position (no upstream counterpart; upstream only
+ * resets). The cache entries from pos on are overwritten by the next
+ * tokens, which is how a rejected draft is dropped. */
+foxcuda_status foxcuda_context_rewind(foxcuda_context *c, uint32_t pos);
 foxcuda_status foxcuda_context_hidden(const foxcuda_context *c, uint32_t layer, float *out);
 
 /* replaces fox_sampler_config (include/fox/fox.h:453-460) */

@@ -93,6 +93,7 @@ _PROTOS = {
     "foxcuda_context_set_trace": (_st, [_vp, C.c_int]),
     "foxcuda_context_set_prefill": (_st, [_vp, C.c_int]),
     "foxcuda_eval_all": (_st, [_vp, _vp, _sz, _vp]),
+    "foxcuda_context_rewind": (_st, [_vp, C.c_uint32]),
     "foxcuda_context_hidden": (_st, [_vp, C.c_uint32, _vp]),
     "foxcuda_sampler_create": (_st, [_vp, C.POINTER(SamplerConfig), C.POINTER(_vp)]),
     "foxcuda_sampler_destroy": (None, [_vp]),
@@ -432,6 +433,10 @@ class Context:
         _check(lib().foxcuda_eval(self.h, t.ctypes.data_as(C.c_void_p), t.size,
                                   out.ctypes.data_as(C.c_void_p) if out is not None else None))
         return out
+
+    def rewind(self, pos: int):
+        """Back to an earlier position; the cache from there on is rewritten."""
+        _check(lib().foxcuda_context_rewind(self.h, pos))
 
     def eval_all(self, tokens) -> np.ndarray:
         """The logits of every token, (n, n_vocab): the verification pass of

@@ -1391,6 +1391,19 @@ extern "C" void foxcuda_context_reset(foxcuda_context* c) {
 }
 
 extern "C" uint32_t foxcuda_context_position(const foxcuda_context* c) { return c ? c->pos : 0; }
+
+// Back to an earlier position: the cache entries from there on are rewritten
+// by the next tokens (speculative decoding drops the rejected draft so).
+extern "C" foxcuda_status foxcuda_context_rewind(foxcuda_context* c, uint32_t pos) {
+  if (!c) return fail(FOXCUDA_ERR_ARG, "rewind: null context");
+  if (pos > c->pos) return fail(FOXCUDA_ERR_ARG, "rewind: position %u is past the current %u", pos, c->pos);
+  cudaSetDevice(c->m->device);
+  CK(cudaStreamSynchronize(c->stream), "rewind");
+  const int p = (int)pos;
+  CK(cudaMemcpy(c->pos_dev, &p, 4, cudaMemcpyHostToDevice), "rewind");
+  c->pos = pos;
+  return FOXCUDA_OK;
+}
 extern "C" double foxcuda_context_last_eval_seconds(const foxcuda_context* c) {
   return c ? c->last_seconds : 0.0;
 }

@@ -72,6 +72,7 @@ def test_gemm_argument_checks_run_before_any_device_call():
     assert L.foxcuda_batch_generate(None, None, None, 1, None) == 1
     assert L.foxcuda_context_fill_kv(None, 0, 0) == 1
     assert L.foxcuda_eval_all(None, None, 0, None) == 1
+    assert L.foxcuda_context_rewind(None, 0) == 1
     for fn in (L.foxcuda_tp_p2p_clear, L.foxcuda_tp_p2p_pick):
         assert fn(None) == 1
     assert L.foxcuda_tp_p2p_export(None, None) == 1 and L.foxcuda_tp_p2p_open(None, None) == 1
