@@ -385,6 +385,14 @@ foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
  * - After foxcuda_context_reset, every rank calls foxcuda_tp_p2p_clear
  *   before any rank's next step.
  * Not yet run on a B200. */
+/* Repeat penalty of the sharded greedy pick (upstream src/sample.c:95-107):
+ * each shard penalises the history tokens of its own vocabulary rows before
+ * its argmax. Prompt tokens given to foxcuda_tp_embed from the host, and
+ * every pick, enter the history, as `fox run` accepts them. The pick equals
+ * the unsharded sampler's. Call before the first step; penalty 1 leaves the
+ * pick plain greedy. Not yet run on a B200. */
+foxcuda_status foxcuda_tp_set_penalty(foxcuda_context *c, float penalty, uint32_t last_n);
+
 #define FOXCUDA_IPC_HANDLE_BYTES 64
 foxcuda_status foxcuda_tp_p2p_export(foxcuda_context *c, void *handle);
 foxcuda_status foxcuda_tp_p2p_open(foxcuda_context *c, const void *handles);

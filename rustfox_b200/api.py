@@ -125,6 +125,7 @@ _PROTOS = {
     "foxcuda_tp_pick": (_st, [_vp, _vp]),
     "foxcuda_tp_advance": (_st, [_vp]),
     "foxcuda_tp_tokens": (_st, [_vp, C.c_uint32, _sz, _vp]),
+    "foxcuda_tp_set_penalty": (_st, [_vp, C.c_float, C.c_uint32]),
     "foxcuda_tp_p2p_export": (_st, [_vp, _vp]),
     "foxcuda_tp_p2p_open": (_st, [_vp, _vp]),
     "foxcuda_tp_p2p_clear": (_st, [_vp]),

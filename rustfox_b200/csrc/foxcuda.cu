@@ -1275,6 +1275,9 @@ struct foxcuda_context {
   uint8_t* peer_arena[TPX_MAX] = {};
   bool p2p = false;
   float* x_small = nullptr;  // [0..1] global absmax (o, down), [2..3] best pair, [4..] pairs
+  // repeat penalty of the sharded greedy pick (foxcuda_tp_set_penalty)
+  SamplerDev* tp_smp = nullptr;
+  float tp_penalty = 1.0f;
 };
 
 struct foxcuda_sampler {
@@ -2634,6 +2637,9 @@ extern "C" foxcuda_status foxcuda_tp_embed(foxcuda_context* c, int64_t token) {
     if ((uint64_t)token >= mi.n_vocab) return fail(FOXCUDA_ERR_ARG, "tp: token outside the vocabulary");
     embed_token_kernel<<<(mi.n_embd + 255) / 256, 256, 0, c->stream>>>(
         c->m->embd.type, c->m->embd.dev, emb_rb, (int)mi.n_embd, (uint32_t)token, c->token_dev, c->x);
+    // a host token (the prompt) enters the penalty history, as `fox run`
+    // accepts the prompt into its sampler (src/cli.c:340-345)
+    if (c->tp_smp) accept_kernel<<<1, 32, 0, c->stream>>>(c->tp_smp, (uint32_t)token);
   } else {
     embed_kernel<<<(mi.n_embd + 255) / 256, 256, 0, c->stream>>>(c->m->embd.type, c->m->embd.dev, emb_rb,
                                                                   (int)mi.n_embd, c->token_dev, c->x);
@@ -2750,7 +2756,10 @@ extern "C" foxcuda_status foxcuda_tp_head(foxcuda_context* c, float* best) {
   if (st) return st;
   if (!best) return fail(FOXCUDA_ERR_ARG, "tp_head: null output");
   CK(launch_head(c), "tp head");
-  tp_argmax_kernel<<<1, 1024, 0, c->stream>>>(c->logits, (int)c->m->loc.n_vocab, c->m->vocab0, best);
+  const int nv = (int)c->m->loc.n_vocab;
+  if (c->tp_smp) tp_penalty_kernel<<<1, 256, 0, c->stream>>>(c->tp_smp, c->logits, nv, c->m->vocab0, c->tp_penalty);
+  tp_argmax_kernel<<<1, 1024, 0, c->stream>>>(c->logits, nv, c->m->vocab0, best);
+  if (c->tp_smp) tp_restore_kernel<<<1, 256, 0, c->stream>>>(c->tp_smp, c->logits, nv, c->m->vocab0);
   CK(cudaGetLastError(), "tp argmax");
   return FOXCUDA_OK;
 }
@@ -2764,6 +2773,7 @@ extern "C" foxcuda_status foxcuda_tp_pick(foxcuda_context* c, const float* pairs
   if (!pairs) return fail(FOXCUDA_ERR_ARG, "tp_pick: null pairs");
   tp_pick_kernel<<<1, 32, 0, c->stream>>>(pairs, c->m->tp_size, c->token_dev, c->ring, (int)c->n_ctx,
                                           c->pos_dev);
+  if (c->tp_smp) tp_accept_kernel<<<1, 32, 0, c->stream>>>(c->tp_smp, c->token_dev);
   advance_kernel<<<1, 32, 0, c->stream>>>(c->pos_dev, 1);
   CK(cudaGetLastError(), "tp pick");
   c->pos += 1;
@@ -2815,6 +2825,28 @@ extern "C" foxcuda_status foxcuda_tp_tokens(foxcuda_context* c, uint32_t first_p
     return fail(FOXCUDA_ERR_INTERNAL, "device: a bounded wait gave up (code %u: %s); the tokens are not valid",
                 code, code == 2 ? "a peer's exchange did not arrive" : "weights did not reach shared memory");
   }
+  return FOXCUDA_OK;
+}
+
+// Repeat penalty for the sharded greedy pick (upstream src/sample.c:95-107):
+// each shard penalises the history tokens of its vocabulary rows before its
+// argmax; the prompt tokens (foxcuda_tp_embed with a host token) and every
+// pick enter the history. Set before the first step.
+extern "C" foxcuda_status foxcuda_tp_set_penalty(foxcuda_context* c, float penalty, uint32_t last_n) {
+  if (!c) return fail(FOXCUDA_ERR_ARG, "tp_set_penalty: null context");
+  if (c->tp_smp) return fail(FOXCUDA_ERR_ARG, "tp_set_penalty: the penalty is already set");
+  if (!(penalty >= 1.0f)) return fail(FOXCUDA_ERR_ARG, "tp_set_penalty: penalty %g is below 1", penalty);
+  if (last_n > SAMPLER_MAX_HIST)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "tp_set_penalty: repeat_last_n %u is above %d", last_n, SAMPLER_MAX_HIST);
+  if (penalty == 1.0f) return FOXCUDA_OK;  // upstream skips the penalty at 1 (src/sample.c:98)
+  cudaSetDevice(c->m->device);
+  void* p = nullptr;
+  CK(ctx_alloc(c, sizeof(SamplerDev), &p), "tp penalty state");
+  CK(cudaMemset(p, 0, sizeof(SamplerDev)), "tp penalty state");
+  const uint32_t cap = last_n ? last_n : 1;
+  CK(cudaMemcpy(&reinterpret_cast<SamplerDev*>(p)->hist_cap, &cap, 4, cudaMemcpyHostToDevice), "tp penalty state");
+  c->tp_smp = reinterpret_cast<SamplerDev*>(p);
+  c->tp_penalty = penalty;
   return FOXCUDA_OK;
 }
 

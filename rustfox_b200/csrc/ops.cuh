@@ -867,6 +867,41 @@ __global__ void __launch_bounds__(1024) tp_argmax_kernel(const float* __restrict
   }
 }
 
+// Repeat penalty on a shard's vocabulary rows [vocab0, vocab0 + n): each
+// distinct history token whose row lives here is penalised as
+// penalty_kernel does (src/sample.c:95-107), at its local index. Every shard
+// holds the same history (every shard accepts the same picks), so the
+// shards together penalise exactly the logits the unsplit sampler does.
+FOX_DEV bool tp_hist_first(const SamplerDev* st, int i, uint32_t vocab0, int n) {
+  const uint32_t tok = st->hist[i];
+  bool first = tok >= vocab0 && tok - vocab0 < (uint32_t)n;
+  for (int j = 0; j < i && first; ++j) first = st->hist[j] != tok;
+  return first;
+}
+
+__global__ void tp_penalty_kernel(SamplerDev* st, float* logits, int n, uint32_t vocab0, float penalty) {
+  const int h = st->hist_len;
+  for (int i = threadIdx.x; i < h; i += blockDim.x) {
+    if (!tp_hist_first(st, i, vocab0, n)) continue;
+    const uint32_t tok = st->hist[i];
+    int c = 0;
+    for (int j = 0; j < h; ++j) c += st->hist[j] == tok;
+    float v = logits[tok - vocab0];
+    st->saved[i] = v;
+    for (int r = 0; r < c; ++r) v = v > 0.0f ? __fdiv_rn(v, penalty) : __fmul_rn(v, penalty);
+    logits[tok - vocab0] = v;
+  }
+}
+
+__global__ void tp_restore_kernel(SamplerDev* st, float* logits, int n, uint32_t vocab0) {
+  for (int i = threadIdx.x; i < (int)st->hist_len; i += blockDim.x)
+    if (tp_hist_first(st, i, vocab0, n)) logits[st->hist[i] - vocab0] = st->saved[i];
+}
+
+__global__ void tp_accept_kernel(SamplerDev* st, const uint32_t* token) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) accept_token(st, *token);
+}
+
 // The winner over all shards' {value, index} pairs becomes the next token.
 __global__ void tp_pick_kernel(const float* __restrict__ pairs, int tp, uint32_t* token,
                                uint32_t* ring, int ring_cap, const int* pos) {

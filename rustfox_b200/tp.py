@@ -41,10 +41,13 @@ class TPContext:
     group spanning the shards (default: the world)."""
 
     def __init__(self, model: api.Model, n_ctx: int, kv: str = "f16", attn_exact: bool = False,
-                 group=None, exchange: str = "nccl"):
+                 group=None, exchange: str = "nccl", repeat_penalty: float = 1.0,
+                 repeat_last_n: int = 64):
         """exchange: "nccl" (torch.distributed collectives between the
         library's steps) or "p2p" (the library's own exchanges over peer
-        memory, foxcuda_tp_p2p_*; no host collective in a step)."""
+        memory, foxcuda_tp_p2p_*; no host collective in a step).
+        repeat_penalty > 1 penalises the last repeat_last_n tokens (prompt
+        and picks) in the greedy pick, as upstream's sampler does."""
         import torch
         import torch.distributed as dist
         if exchange not in ("nccl", "p2p"):
@@ -71,6 +74,7 @@ class TPContext:
         self.gath_d = torch.zeros(self.world * self.n_embd * self.stride_d, **f)
         self.best = torch.zeros(2, **f)
         self.pairs = torch.zeros(2 * self.world, **f)
+        api._check(api.lib().foxcuda_tp_set_penalty(self.ctx.h, float(repeat_penalty), int(repeat_last_n)))
         if exchange == "p2p":
             self._open_peers()
 
@@ -161,8 +165,9 @@ class TPContext:
         self.ctx_pos_fix()
 
     def generate(self, prompt, n_gen: int, graphs: bool = False) -> np.ndarray:
-        """Greedy decode (no repeat penalty): the prompt, then n_gen picks;
-        with graphs the steps after the first two replay a captured step."""
+        """Greedy decode with the context's repeat penalty (none by default):
+        the prompt, then n_gen picks; with graphs the steps after the first
+        two replay a captured step."""
         prompt = [int(t) for t in prompt]
         start = self.ctx.pos
         for i, t in enumerate(prompt):

@@ -27,7 +27,7 @@ N_GEN = 32
 N_CTX = 96
 
 
-def run_rank(rank, world, port, cfg, kv, exact, graphs, out_q):
+def run_rank(rank, world, port, cfg, kv, exact, graphs, out_q, exchange="p2p", penalty=1.0):
     import datetime
     import torch.distributed as dist
     import rustfox_b200 as rf
@@ -37,7 +37,7 @@ def run_rank(rank, world, port, cfg, kv, exact, graphs, out_q):
                             world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
         m = rf.Model.from_synthetic(synth.generate(cfg), device=rank, tp_rank=rank, tp_size=world)
-        ctx = TPContext(m, N_CTX, kv=kv, attn_exact=exact, exchange="p2p")
+        ctx = TPContext(m, N_CTX, kv=kv, attn_exact=exact, exchange=exchange, repeat_penalty=penalty)
         toks = ctx.generate(PROMPT, N_GEN, graphs=graphs)
         torch.cuda.synchronize()
         dist.barrier()  # no rank unmaps while another may still read its arena
@@ -55,14 +55,15 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _tp_tokens(cfg, kv, exact, graphs, world, limit_s=240):
+def _tp_tokens(cfg, kv, exact, graphs, world, limit_s=240, exchange="p2p", penalty=1.0):
     import queue
     import time
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=run_rank, args=(r, world, port, cfg, kv, exact, graphs, q))
+    procs = [ctx.Process(target=run_rank,
+                         args=(r, world, port, cfg, kv, exact, graphs, q, exchange, penalty))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -101,5 +102,22 @@ def test_p2p_shards_equal_one_gpu(world, cfg, kv, exact, graphs):
     got = _tp_tokens(cfg, kv, exact, graphs, world)
     m = rf.Model.from_synthetic(synth.generate(cfg))
     want = rf.greedy_generate(m, PROMPT, N_GEN, N_CTX, kv=kv, repeat_penalty=1.0, attn_exact=exact)
+    m.close()
+    assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
+
+
+@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "graph"])
+def test_repeat_penalty_shards_equal_one_gpu(world, exchange, graphs):
+    """foxcuda_tp_set_penalty: the sharded pick with upstream's repeat penalty
+    (1.1 over the last 64 tokens, prompt included) equals the single-GPU
+    sampler's."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import rustfox_b200 as rf
+    got = _tp_tokens(CFG_TQ2, "f16", False, graphs, world, exchange=exchange, penalty=1.1)
+    m = rf.Model.from_synthetic(synth.generate(CFG_TQ2))
+    want = rf.greedy_generate(m, PROMPT, N_GEN, N_CTX, kv="f16", repeat_penalty=1.1)
     m.close()
     assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
