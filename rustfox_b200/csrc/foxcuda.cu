@@ -2124,6 +2124,14 @@ extern "C" foxcuda_status foxcuda_eval_all(foxcuda_context* c, const uint32_t* t
     CK(kquant ? prefill_chunk_kq(c, c->tokens_dev + i, M, c->pos + (uint32_t)i)
               : prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i),
        "prefill");
+    if (kquant && is_kq(c->m->output.type)) {
+      // a K-quant head quantises its input per 256 block like the layers:
+      // one K-quant pass gives every row's logits (the decode head's values)
+      const PackedMat& H = c->m->output;
+      CK(quant_rows_k<true>(c, c->pf_x, (int)mi.n_embd, c->m->out_norm, decode_threads(H), M), "head rows");
+      CK(kq_rows(c, H, M, c->rows_logits + i * nv, (int)nv), "head pass");
+      continue;
+    }
     for (int t = 0; t < M; ++t) {
       CK(cudaMemcpyAsync(c->x, c->pf_x + (size_t)t * mi.n_embd, (size_t)mi.n_embd * 4,
                          cudaMemcpyDeviceToDevice, c->stream), "row");
