@@ -1948,22 +1948,32 @@ static bool kq_layers_ok(const foxcuda_model* m) {
 }
 
 template <bool NORM>
-static cudaError_t quant_rows_k(foxcuda_context* c, const float* X, int K, const float* norm_w, int threads,
-                                int M) {
+static cudaError_t quant_rows_k_to(const float* X, int K, const float* norm_w, float eps, int threads, int M,
+                                   int8_t* XQ, float* XS, cudaStream_t s) {
   const size_t smem = (size_t)K * 4;
   static size_t marks[kMaxDevices] = {};
   cudaError_t e = opt_in_smem(quant_rows_k_kernel<NORM>, smem, marks);
   if (e != cudaSuccess) return e;
-  quant_rows_k_kernel<NORM><<<M, threads, smem, c->stream>>>(X, K, norm_w, c->m->info.rms_eps, c->pf_xq,
-                                                            c->pf_xs);
+  quant_rows_k_kernel<NORM><<<M, threads, smem, s>>>(X, K, norm_w, eps, XQ, XS);
   return cudaGetLastError();
 }
 
-static cudaError_t kq_rows(foxcuda_context* c, const PackedMat& W, int M, float* out, int out_stride) {
+template <bool NORM>
+static cudaError_t quant_rows_k(foxcuda_context* c, const float* X, int K, const float* norm_w, int threads,
+                                int M) {
+  return quant_rows_k_to<NORM>(X, K, norm_w, c->m->info.rms_eps, threads, M, c->pf_xq, c->pf_xs, c->stream);
+}
+
+static cudaError_t kq_rows_to(const int8_t* XQ, const float* XS, const PackedMat& W, int M, float* out,
+                              int out_stride, int* err, cudaStream_t s) {
   TcKParams p;
-  p.w = W.dev; p.xq = c->pf_xq; p.xs = c->pf_xs; p.out = out; p.out_stride = out_stride;
-  p.n_rows = W.n_rows; p.K = W.K; p.nb = W.K / 256; p.U = W.U; p.n_tok = M; p.err = c->err_dev;
-  return launch_kq(W.type, p, c->stream);
+  p.w = W.dev; p.xq = XQ; p.xs = XS; p.out = out; p.out_stride = out_stride;
+  p.n_rows = W.n_rows; p.K = W.K; p.nb = W.K / 256; p.U = W.U; p.n_tok = M; p.err = err;
+  return launch_kq(W.type, p, s);
+}
+
+static cudaError_t kq_rows(foxcuda_context* c, const PackedMat& W, int M, float* out, int out_stride) {
+  return kq_rows_to(c->pf_xq, c->pf_xs, W, M, out, out_stride, c->err_dev, c->stream);
 }
 
 // prefill_chunk for K-quant layers: each q|k|v run is quantised with the
@@ -2184,6 +2194,7 @@ struct foxcuda_batch {
   float *x = nullptr, *xs = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr;
   float *gu = nullptr, *h = nullptr, *t = nullptr;
   int8_t* xq = nullptr;
+  float* lg = nullptr;  // every sequence's logits (a K-quant head in one pass)
   std::vector<void*> allocs;
   cudaGraphExec_t graph = nullptr;  // a step and the picks, for foxcuda_batch_generate
   std::vector<foxcuda_sampler*> graph_samplers;
@@ -2240,7 +2251,8 @@ extern "C" foxcuda_status foxcuda_batch_create(foxcuda_context* const* ctxs, siz
   A(n * 4, (void**)&b->toks);
   A(n * E * 4, (void**)&b->x);
   A(n * kmax, (void**)&b->xq);
-  A(n * 4, (void**)&b->xs);
+  A(n * (kmax / 256 + 1) * 4, (void**)&b->xs);  // per token, or per 256 block (a K-quant head)
+  if (is_kq(m->output.type)) A(n * (size_t)mi.n_vocab * 4, (void**)&b->lg);
   A(n * (nq + 2 * nkv) * 4, (void**)&b->qkv);
   A(n * nq * 4, (void**)&b->q);
   A(n * nq * 4, (void**)&b->att);
@@ -2331,11 +2343,22 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
     add_rows_kernel<<<add_grid, 256, 0, s>>>(b->x, b->t, rows_e);
     e = cudaGetLastError();
   }
-  // each sequence's head on its own residual row, into its context's logits
-  for (int i = 0; i < M && !e; ++i) {
-    foxcuda_context* c = b->ctx[i];
-    e = cudaMemcpyAsync(c->x, b->x + (size_t)i * E, (size_t)E * 4, cudaMemcpyDeviceToDevice, s);
-    if (!e) e = launch_head_on(c, s, false);
+  if (!e && b->lg) {
+    // a K-quant head quantises per 256 block like the layers: one K-quant
+    // pass gives every sequence's logits (each its decode head's values)
+    const PackedMat& H = m->output;
+    const size_t nv = mi.n_vocab;
+    e = quant_rows_k_to<true>(b->x, E, m->out_norm, eps, decode_threads(H), M, b->xq, b->xs, s);
+    if (!e) e = kq_rows_to(b->xq, b->xs, H, M, b->lg, (int)nv, c0->err_dev, s);
+    for (int i = 0; i < M && !e; ++i)
+      e = cudaMemcpyAsync(b->ctx[i]->logits, b->lg + i * nv, nv * 4, cudaMemcpyDeviceToDevice, s);
+  } else {
+    // each sequence's head on its own residual row, into its context's logits
+    for (int i = 0; i < M && !e; ++i) {
+      foxcuda_context* c = b->ctx[i];
+      e = cudaMemcpyAsync(c->x, b->x + (size_t)i * E, (size_t)E * 4, cudaMemcpyDeviceToDevice, s);
+      if (!e) e = launch_head_on(c, s, false);
+    }
   }
   if (e) return e;
   advance_all_kernel<<<1, BATCH_MAX, 0, s>>>(b->pos, M);

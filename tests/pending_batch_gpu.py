@@ -23,6 +23,8 @@ import rustfox_b200 as rf  # noqa: E402
 N_CTX = 96
 TINY = synth.CONFIGS["tiny"].scaled(name="tiny-batch", n_layer=3)
 TINY_TQ2 = TINY.scaled(name="tiny-batch-tq2", linear_type=F.TQ2_0)
+# config 5's kind: ternary layers with a Q6_K head (one K-quant pass for all heads)
+TINY_Q6H = TINY.scaled(name="tiny-batch-q6h", linear_type=F.TQ2_0, output_type=F.Q6_K)
 MODELS = {}
 PROMPTS = [5, 17, 30]
 
@@ -42,7 +44,7 @@ def _contexts(model, cfg, kv, exact):
     return out
 
 
-@pytest.mark.parametrize("cfg", [TINY, TINY_TQ2], ids=["tq1", "tq2"])
+@pytest.mark.parametrize("cfg", [TINY, TINY_TQ2, TINY_Q6H], ids=["tq1", "tq2", "tq2-q6k-head"])
 @pytest.mark.parametrize("kv,exact", [("f16", False), ("f32", True)], ids=["production", "parity"])
 def test_batch_steps_equal_single_steps(cfg, kv, exact):
     model = _model(cfg)
