@@ -455,12 +455,14 @@ def run_tp(args):
 
 
 def run_gemm(args):
-    """The M-token ternary pass (foxcuda_gemm_tq2_i8_packed, tcgen05 kind::i8)
-    over the seven matrices of one layer of the config (q, k, v, o, gate, up,
-    down), against M single-token decode GEMVs (foxcuda_gemv_packed) of the
-    same matrices. Enough packed copies of the layer are cycled that the
-    weights read per timed region exceed the L2 three times over.
-    CUDA-event time on the current stream, one GPU."""
+    """The M-token tensor-core pass (tcgen05 kind::i8) over the seven matrices
+    of one layer of the config (q, k, v, o, gate, up, down), against M
+    single-token decode GEMVs (foxcuda_gemv_packed) of the same matrices:
+    foxcuda_gemm_tq2_i8_packed for ternary configs (TQ1_0 is held as TQ2_0),
+    foxcuda_gemm_kq_i8_packed for K-quant ones (Q4_K, with the config's v
+    type). Enough packed copies of the layer are cycled that the weights read
+    per timed region exceed the L2 three times over. CUDA-event time on the
+    current stream, one GPU."""
     import torch
     import rustfox_b200 as rf
     from rustfox_b200 import formats as F, synth
@@ -469,40 +471,48 @@ def run_gemm(args):
     e, f = cfg.n_embd, cfg.n_ff
     nq, nkv = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
     shapes = [(nq, e), (nkv, e), (nkv, e), (e, nq), (f, e), (f, e), (e, f)]
-    layer_bytes = sum(r * (k // 256) * 66 for r, k in shapes)
+    kq = cfg.linear_type in (F.Q4_K, F.Q6_K)
+    lin = cfg.linear_type if kq else F.TQ2_0
+    types = [lin, lin, (cfg.attn_v_type or cfg.linear_type) if kq else lin, lin, lin, lin, lin]
+    layer_bytes = sum(F.row_bytes(t, k) * r for t, (r, k) in zip(types, shapes))
     params = sum(r * k for r, k in shapes)
     rng = np.random.default_rng(0)
-    one = [rf.pack(F.TQ2_0, torch.from_numpy(F.random_tq2_blocks(rng, r * k // 256, 0.02)
-                                            .reshape(-1)).cuda(), r, k) for r, k in shapes]
+    one = [rf.pack(t, torch.from_numpy(F.random_blocks(rng, t, r, k, 0.01)).cuda(), r, k)
+           for t, (r, k) in zip(types, shapes)]
     copies = [one] + [[p.clone() for p in one]
                       for _ in range(max(1, int(np.ceil(3 * 126e6 / layer_bytes))) - 1)]
     kmax = max(k for _, k in shapes)
     rows = []
     for m in [int(v) for v in args.gemm.split(",")]:
-        qs = {k: torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda")
-              for k in {k for _, k in shapes}}
+        ks = {k for _, k in shapes}
+        qs = {k: torch.randint(-127, 128, (m, k), dtype=torch.int8, device="cuda") for k in ks}
         s = torch.full((m,), 1e-3, dtype=torch.float32, device="cuda")
+        sk = {k: torch.full((m, k // 256), 1e-3, dtype=torch.float32, device="cuda") for k in ks}
         x = torch.randn(kmax, dtype=torch.float32, device="cuda")
         outs = [torch.empty(m, r, dtype=torch.float32, device="cuda") for r, _ in shapes]
 
         def tc_pass(layer):
-            for (r, k), pk, o in zip(shapes, layer, outs):
-                rf.gemm_tq2_i8_packed(qs[k], s, pk, r, k, out=o)
+            for t, (r, k), pk, o in zip(types, shapes, layer, outs):
+                if kq:
+                    rf.gemm_kq_i8_packed(t, qs[k], sk[k], pk, r, k, out=o)
+                else:
+                    rf.gemm_tq2_i8_packed(qs[k], s, pk, r, k, out=o)
 
         def gemv_pass(layer):
             for _ in range(m):
-                for (r, k), pk, o in zip(shapes, layer, outs):
-                    rf.gemv_packed(F.TQ2_0, x[:k], pk, r, k, out=o[0])
+                for t, (r, k), pk, o in zip(types, shapes, layer, outs):
+                    rf.gemv_packed(t, x[:k], pk, r, k, out=o[0])
 
+        split = args.split and not kq
         terms = (torch.empty(m * max(r * (k // 256) for r, k in shapes), dtype=torch.float32,
-                             device="cuda") if args.split else None)
+                             device="cuda") if split else None)
 
         def split_pass(layer):
             for (r, k), pk, o in zip(shapes, layer, outs):
                 rf.gemm_tq2_i8_split(qs[k], s, pk, r, k, terms=terms, out=o)
 
         res = {"M": m}
-        kinds = [("tc", tc_pass), ("gemv", gemv_pass)] + ([("split", split_pass)] if args.split else [])
+        kinds = [("tc", tc_pass), ("gemv", gemv_pass)] + ([("split", split_pass)] if split else [])
         for name, fn in kinds:
             for i in range(max(3, args.warmup)):
                 fn(copies[i % len(copies)])
@@ -521,11 +531,12 @@ def run_gemm(args):
         res["speedup_vs_gemv"] = res["gemv_us_per_layer"] / res["tc_us_per_layer"]
         rows.append(res)
     hbm, src = measured_hbm_gbs()
+    names = "/".join(sorted({TYPE_NAMES[t] for t in types}))
     print(json.dumps({
-        "metric": "M-token ternary pass, one layer (q k v o gate up down)", "unit": "us",
-        "higher_is_better": False, "dtype": "i8 x ternary -> i32 (tcgen05 kind::i8), f32 fold",
-        "data": "synthetic (seeded random TQ2_0 weights, random int8 activations)",
-        "config": {"workload": f"{cfg.name} layer matrices, TQ2_0 packed",
+        "metric": "M-token pass, one layer (q k v o gate up down)", "unit": "us",
+        "higher_is_better": False, "dtype": "i8 x quantised weights -> i32 (tcgen05 kind::i8), f32 terms",
+        "data": f"synthetic (seeded random {names} weights, random int8 activations)",
+        "config": {"workload": f"{cfg.name} layer matrices, {names} packed",
                    "layer_weight_bytes": layer_bytes, "l2": f"{len(copies)} layer copies cycled",
                    "hbm_peak_gbs": hbm, "hbm_peak_source": src},
         "results": rows}), flush=True)

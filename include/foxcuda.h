@@ -94,6 +94,10 @@ foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t *q, const float *act_scal
 foxcuda_status foxcuda_gemm_kq_i8(int ggml_type, const int8_t *q, const float *act_scales,
                                   size_t n_tokens, const void *weights, size_t n_rows,
                                   size_t n_cols, float *out, void *stream);
+/* The same on weights already packed by foxcuda_pack: no scratch. */
+foxcuda_status foxcuda_gemm_kq_i8_packed(int ggml_type, const int8_t *q, const float *act_scales,
+                                         size_t n_tokens, const void *packed, size_t n_rows,
+                                         size_t n_cols, float *out, void *stream);
 /* foxcuda_gemm_tq2_i8_packed with each row's blocks split over CTAs, for few
  * tokens, where the matrix alone has too few 128-row tiles to fill the GPU.
  * It writes each block's float term to terms (device scratch of

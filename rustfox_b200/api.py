@@ -69,6 +69,7 @@ _PROTOS = {
     "foxcuda_gemm_tq2_i8_packed": (_st, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemm_tq2_i8_split": (_st, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, _vp]),
     "foxcuda_gemm_kq_i8": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
+    "foxcuda_gemm_kq_i8_packed": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_noalloc": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_attention": (_st, [_vp, _vp, _vp, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32,
@@ -241,6 +242,16 @@ def gemm_kq_i8(ggml_type: int, q, scales, w, n_rows: int, n_cols: int, out=None)
     out = torch.empty(n_tok, n_rows, dtype=torch.float32, device=q.device) if out is None else out
     _check(lib().foxcuda_gemm_kq_i8(ggml_type, _dp(q), _dp(scales), n_tok, _dp(w), n_rows, n_cols,
                                     _dp(out), _stream()))
+    return out
+
+
+def gemm_kq_i8_packed(ggml_type: int, q, scales, packed, n_rows: int, n_cols: int, out=None):
+    """gemm_kq_i8 on Q4_K / Q6_K weights already packed by pack()."""
+    import torch
+    n_tok = q.shape[0]
+    out = torch.empty(n_tok, n_rows, dtype=torch.float32, device=q.device) if out is None else out
+    _check(lib().foxcuda_gemm_kq_i8_packed(ggml_type, _dp(q), _dp(scales), n_tok, _dp(packed), n_rows,
+                                           n_cols, _dp(out), _stream()))
     return out
 
 

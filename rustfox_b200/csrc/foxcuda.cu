@@ -599,6 +599,24 @@ static cudaError_t launch_kq(int type, const TcKParams& p, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
+extern "C" foxcuda_status foxcuda_gemm_kq_i8_packed(int type, const int8_t* q, const float* act_scales,
+                                                    size_t n_tokens, const void* packed, size_t n_rows,
+                                                    size_t n_cols, float* out, void* stream) {
+  if (type != T_Q4_K && type != T_Q6_K)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: ggml type %d; the K-quant tensor-core pass takes Q4_K and Q6_K",
+                type);
+  foxcuda_status st = check_gemm_args(q, act_scales, n_tokens, packed, n_rows, n_cols, out);
+  if (st) return st;
+  const int nb = (int)(n_cols / 256);
+  const int U = unit_rows(type, nb);
+  if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: %zu columns has no unit layout", n_cols);
+  TcKParams p;
+  p.w = (const uint8_t*)packed; p.xq = q; p.xs = act_scales; p.out = out; p.out_stride = (int)n_rows;
+  p.n_rows = (int)n_rows; p.K = (int)n_cols; p.nb = nb; p.U = U; p.n_tok = (int)n_tokens; p.err = nullptr;
+  CK(launch_kq(type, p, (cudaStream_t)stream), "gemm launch");
+  return FOXCUDA_OK;
+}
+
 extern "C" foxcuda_status foxcuda_gemm_kq_i8(int type, const int8_t* q, const float* act_scales,
                                              size_t n_tokens, const void* w, size_t n_rows, size_t n_cols,
                                              float* out, void* stream) {
