@@ -655,6 +655,10 @@ def run_batch(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": None, "peak_source": src,
                      "bytes_per_step": step_bytes},
+        "cpu_baseline": None,
+        "cpu_baseline_note": "upstream has no way to set its cache (or to decode several sequences "
+                             "in one pass), so a 32k-position upstream decode would need the 32k-token "
+                             "prompt evaluated on the CPU first; not timed",
         "clocks": ck}), flush=True)
     batch.close()
     for s in smp:
