@@ -94,6 +94,12 @@ foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t *q, const float *act_scal
 foxcuda_status foxcuda_gemm_kq_i8(int ggml_type, const int8_t *q, const float *act_scales,
                                   size_t n_tokens, const void *weights, size_t n_rows,
                                   size_t n_cols, float *out, void *stream);
+/* Every tensor-core call above records a bounded wait that gave up in one
+ * device error word per device (the outputs of that call are then not
+ * valid). foxcuda_kernel_errors synchronises the stream, reports the word
+ * and clears it. The first tensor-core call on a device looks the word up;
+ * make it before any stream capture. */
+foxcuda_status foxcuda_kernel_errors(void *stream);
 /* The same on weights already packed by foxcuda_pack: no scratch. */
 foxcuda_status foxcuda_gemm_kq_i8_packed(int ggml_type, const int8_t *q, const float *act_scales,
                                          size_t n_tokens, const void *packed, size_t n_rows,

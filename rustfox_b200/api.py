@@ -70,6 +70,7 @@ _PROTOS = {
     "foxcuda_gemm_tq2_i8_split": (_st, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp, _vp]),
     "foxcuda_gemm_kq_i8": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemm_kq_i8_packed": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
+    "foxcuda_kernel_errors": (_st, [_vp]),
     "foxcuda_gemv": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_noalloc": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_attention": (_st, [_vp, _vp, _vp, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32,

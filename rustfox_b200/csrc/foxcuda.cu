@@ -471,6 +471,38 @@ extern "C" foxcuda_status foxcuda_gemv_tq2_i8(const int8_t* q, const float* act_
 }
 
 // ---------------------------------------------------------------------------
+// The error word of kernel-level calls: the tensor-core passes record a wait
+// that gave up here (contexts have their own). foxcuda_kernel_errors reads
+// and clears it. Its address is looked up once per device, by the first call
+// that needs it.
+static __device__ int g_kernel_err;
+static std::mutex g_kernel_err_mu;
+static int* g_kernel_err_addr[kMaxDevices];
+
+static int* kernel_err_ptr() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_kernel_err_mu);
+  if (!g_kernel_err_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_kernel_err) == cudaSuccess) g_kernel_err_addr[dev] = (int*)p;
+  }
+  return g_kernel_err_addr[dev];
+}
+
+extern "C" foxcuda_status foxcuda_kernel_errors(void* stream) {
+  int* p = kernel_err_ptr();
+  if (!p) return fail(FOXCUDA_ERR_INTERNAL, "kernel_errors: no device error word on the current device");
+  CK(cudaStreamSynchronize((cudaStream_t)stream), "kernel_errors");
+  int code = 0;
+  CK(cudaMemcpy(&code, p, 4, cudaMemcpyDeviceToHost), "kernel_errors");
+  if (!code) return FOXCUDA_OK;
+  CK(cudaMemset(p, 0, 4), "kernel_errors");
+  return fail(FOXCUDA_ERR_INTERNAL, "device: a bounded wait of a kernel-level tensor-core call gave up "
+              "(code %d); that call's output is not valid", code);
+}
+
+// ---------------------------------------------------------------------------
 // M-token ternary GEMM on the tensor cores (tc.cuh)
 
 template <int NT>
@@ -530,8 +562,9 @@ extern "C" foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t* q, const floa
   if (st) return st;
   const int U = unit_rows(T_TQ2_0, (int)(n_cols / 256));
   if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: %zu columns has no unit layout", n_cols);
-  CK(launch_tc(tc_params(q, act_scale, n_tokens, packed, n_rows, n_cols, U, out), (cudaStream_t)stream),
-     "gemm launch");
+  TcParams p = tc_params(q, act_scale, n_tokens, packed, n_rows, n_cols, U, out);
+  p.err = kernel_err_ptr();
+  CK(launch_tc(p, (cudaStream_t)stream), "gemm launch");
   return FOXCUDA_OK;
 }
 
@@ -575,9 +608,9 @@ extern "C" foxcuda_status foxcuda_gemm_tq2_i8_split(const int8_t* q, const float
   if (!terms) return fail(FOXCUDA_ERR_ARG, "gemm: null terms scratch");
   const int U = unit_rows(T_TQ2_0, (int)(n_cols / 256));
   if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: %zu columns has no unit layout", n_cols);
-  CK(launch_tc_split(tc_params(q, act_scale, n_tokens, packed, n_rows, n_cols, U, out), terms,
-                     (cudaStream_t)stream),
-     "gemm launch");
+  TcParams p = tc_params(q, act_scale, n_tokens, packed, n_rows, n_cols, U, out);
+  p.err = kernel_err_ptr();
+  CK(launch_tc_split(p, terms, (cudaStream_t)stream), "gemm launch");
   return FOXCUDA_OK;
 }
 
@@ -612,7 +645,7 @@ extern "C" foxcuda_status foxcuda_gemm_kq_i8_packed(int type, const int8_t* q, c
   if (U < 0) return fail(FOXCUDA_ERR_UNSUPPORTED, "gemm: %zu columns has no unit layout", n_cols);
   TcKParams p;
   p.w = (const uint8_t*)packed; p.xq = q; p.xs = act_scales; p.out = out; p.out_stride = (int)n_rows;
-  p.n_rows = (int)n_rows; p.K = (int)n_cols; p.nb = nb; p.U = U; p.n_tok = (int)n_tokens; p.err = nullptr;
+  p.n_rows = (int)n_rows; p.K = (int)n_cols; p.nb = nb; p.U = U; p.n_tok = (int)n_tokens; p.err = kernel_err_ptr();
   CK(launch_kq(type, p, (cudaStream_t)stream), "gemm launch");
   return FOXCUDA_OK;
 }
@@ -635,7 +668,7 @@ extern "C" foxcuda_status foxcuda_gemm_kq_i8(int type, const int8_t* q, const fl
   if (e == cudaSuccess) {
     TcKParams p;
     p.w = (const uint8_t*)scratch; p.xq = q; p.xs = act_scales; p.out = out; p.out_stride = (int)n_rows;
-    p.n_rows = (int)n_rows; p.K = (int)n_cols; p.nb = nb; p.U = U; p.n_tok = (int)n_tokens; p.err = nullptr;
+    p.n_rows = (int)n_rows; p.K = (int)n_cols; p.nb = nb; p.U = U; p.n_tok = (int)n_tokens; p.err = kernel_err_ptr();
     e = launch_kq(type, p, s);
   }
   cudaError_t e2 = cudaFreeAsync(scratch, s);
@@ -670,7 +703,11 @@ extern "C" foxcuda_status foxcuda_gemm_tq_i8(int type, const int8_t* q, const fl
     rows = scratch + tq2_bytes;
   }
   if (e == cudaSuccess) e = pack_rows(T_TQ2_0, rows, n_rows, nb, U, scratch, s);
-  if (e == cudaSuccess) e = launch_tc(tc_params(q, act_scale, n_tokens, scratch, n_rows, n_cols, U, out), s);
+  if (e == cudaSuccess) {
+    TcParams p = tc_params(q, act_scale, n_tokens, scratch, n_rows, n_cols, U, out);
+    p.err = kernel_err_ptr();
+    e = launch_tc(p, s);
+  }
   cudaError_t e2 = cudaFreeAsync(scratch, s);
   if (e != cudaSuccess) return cuda_fail(e, "gemm");
   CK(e2, "gemm scratch free");

@@ -43,6 +43,7 @@ def test_errors_without_a_device_are_statuses_not_crashes():
         pytest.skip("a GPU is present")
     assert st in (1, 5, 7) and rf.last_error()
     assert rf.lib().foxcuda_gemv(34, None, None, 1, 256, None, None) == 1
+    assert rf.lib().foxcuda_kernel_errors(None) == 7 and rf.last_error()
 
 
 def test_gemm_argument_checks_run_before_any_device_call():
