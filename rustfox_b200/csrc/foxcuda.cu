@@ -1321,6 +1321,10 @@ struct foxcuda_context {
   float *pf_gu = nullptr, *pf_h = nullptr, *pf_t = nullptr;
   int8_t* pf_xq = nullptr;
   int* pf_pos = nullptr;
+  // the one-launch attention of a chunk: token t's position pointer, caches
+  int** pf_pos_list = nullptr;
+  void** pf_k_list = nullptr;
+  void** pf_v_list = nullptr;
   float* rows_logits = nullptr;  // foxcuda_eval_all staging, rows_cap x n_vocab
   size_t rows_cap = 0;
   // tensor-parallel exchanges over peer memory (p2p.cuh)
@@ -1893,6 +1897,17 @@ static cudaError_t prefill_buffers(foxcuda_context* c) {
   A(M * F * 4, (void**)&c->pf_h);
   A(M * E * 4, (void**)&c->pf_t);
   A(M * 4, (void**)&c->pf_pos);
+  A(M * sizeof(int*), (void**)&c->pf_pos_list);
+  A(M * sizeof(void*), (void**)&c->pf_k_list);
+  A(M * sizeof(void*), (void**)&c->pf_v_list);
+  if (e == cudaSuccess) {
+    std::vector<int*> pl(M);
+    std::vector<void*> kl(M, c->kc), vl(M, c->vc);
+    for (size_t t = 0; t < M; ++t) pl[t] = c->pf_pos + t;
+    e = cudaMemcpy(c->pf_pos_list, pl.data(), M * sizeof(int*), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->pf_k_list, kl.data(), M * sizeof(void*), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->pf_v_list, vl.data(), M * sizeof(void*), cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) c->pf_ready = true;
   return e;
 }
@@ -1926,10 +1941,41 @@ static cudaError_t tc_rows(foxcuda_context* c, const PackedMat& W, int M, float*
   return tc_rows_to(c->pf_xq, c->pf_xs, W, M, out, c->err_dev, c->stream);
 }
 
+// Layer l's attention of every token of a chunk over positions 0..its own
+// (its K/V rows and the chunk's later ones are in the cache already; each
+// token reads only up to its own position). one_launch takes the cluster
+// kernel with grid z = token, every token naming the same caches; otherwise
+// one decode attention launch per token. Both give the decode step's values.
+static cudaError_t chunk_attention(foxcuda_context* c, uint32_t l, int M, bool one_launch) {
+  const foxcuda_model* m = c->m;
+  const int hd = m->info.head_dim, nq = m->loc.n_head * hd;
+  AttnParams ap{};
+  ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
+  ap.hd = hd; ap.n_head = m->loc.n_head; ap.n_kv = m->loc.n_head_kv; ap.S_max = c->S_max;
+  ap.scale = 1.0f / sqrtf((float)hd);
+  if (one_launch && attn_seqs_ok(ap, c->attn_exact)) {
+    ap.q = c->pf_q; ap.out = c->pf_att; ap.seq_stride = nq;
+    ap.pos_list = c->pf_pos_list; ap.k_list = c->pf_k_list; ap.v_list = c->pf_v_list;
+    ap.layer_off = (size_t)l * c->kv_layer_elems * (c->kv_f16 ? 2 : 4);
+    return launch_attn_seqs(ap, M, c->stream);
+  }
+  ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+  ap.part = c->attn_part; ap.counters = c->attn_cnt;
+  cudaError_t e = cudaSuccess;
+  for (int t = 0; t < M && !e; ++t) {
+    ap.q = c->pf_q + (size_t)t * nq;
+    ap.pos = c->pf_pos + t;
+    ap.out = c->pf_att + (size_t)t * nq;
+    e = run_attention(ap, c->attn_exact, c->stream);
+  }
+  return e;
+}
+
 // M prompt tokens (device ids) at positions pos0.. through every layer; the
 // last one's residual row is left in c->x for the head, and the device
 // position moves past the chunk. Per token the values are the decode step's.
-static cudaError_t prefill_chunk(foxcuda_context* c, const uint32_t* tokens, int M, uint32_t pos0) {
+static cudaError_t prefill_chunk(foxcuda_context* c, const uint32_t* tokens, int M, uint32_t pos0,
+                                 bool one_launch) {
   foxcuda_model* m = c->m;
   const foxcuda_model_info& mi = m->info;
   cudaStream_t s = c->stream;
@@ -1950,20 +1996,7 @@ static cudaError_t prefill_chunk(foxcuda_context* c, const uint32_t* tokens, int
         c->pf_qkv, nqkv, nq, nkv, hd, (int)c->n_ctx, (int)pos0, c->rope_cos, c->rope_sin, c->kv_f16,
         kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->pf_q);
     if ((e = cudaGetLastError())) break;
-    // attention of each token over positions 0..its own
-    AttnParams ap{};
-    ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
-    ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
-    ap.hd = hd; ap.n_head = m->loc.n_head; ap.n_kv = m->loc.n_head_kv; ap.S_max = c->S_max;
-    ap.part = c->attn_part; ap.counters = c->attn_cnt;
-    ap.scale = 1.0f / sqrtf((float)hd);
-    for (int t = 0; t < M && !e; ++t) {
-      ap.q = c->pf_q + (size_t)t * nq;
-      ap.pos = c->pf_pos + t;
-      ap.out = c->pf_att + (size_t)t * nq;
-      e = run_attention(ap, c->attn_exact, s);
-    }
-    if (e) break;
+    if ((e = chunk_attention(c, l, M, one_launch))) break;
     // o, residual
     if ((e = quant_rows<false>(c, c->pf_att, nq, nullptr, 256, M))) break;
     if ((e = tc_rows(c, L.o, M, c->pf_t))) break;
@@ -2033,7 +2066,8 @@ static cudaError_t kq_rows(foxcuda_context* c, const PackedMat& W, int M, float*
 
 // prefill_chunk for K-quant layers: each q|k|v run is quantised with the
 // thread count of its own decode kernel and lands at its row offset.
-static cudaError_t prefill_chunk_kq(foxcuda_context* c, const uint32_t* tokens, int M, uint32_t pos0) {
+static cudaError_t prefill_chunk_kq(foxcuda_context* c, const uint32_t* tokens, int M, uint32_t pos0,
+                                    bool one_launch) {
   foxcuda_model* m = c->m;
   const foxcuda_model_info& mi = m->info;
   cudaStream_t s = c->stream;
@@ -2056,19 +2090,7 @@ static cudaError_t prefill_chunk_kq(foxcuda_context* c, const uint32_t* tokens, 
         c->pf_qkv, nqkv, nq, nkv, hd, (int)c->n_ctx, (int)pos0, c->rope_cos, c->rope_sin, c->kv_f16,
         kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->pf_q);
     if ((e = cudaGetLastError())) break;
-    AttnParams ap{};
-    ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
-    ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
-    ap.hd = hd; ap.n_head = m->loc.n_head; ap.n_kv = m->loc.n_head_kv; ap.S_max = c->S_max;
-    ap.part = c->attn_part; ap.counters = c->attn_cnt;
-    ap.scale = 1.0f / sqrtf((float)hd);
-    for (int t = 0; t < M && !e; ++t) {
-      ap.q = c->pf_q + (size_t)t * nq;
-      ap.pos = c->pf_pos + t;
-      ap.out = c->pf_att + (size_t)t * nq;
-      e = run_attention(ap, c->attn_exact, s);
-    }
-    if (e) break;
+    if ((e = chunk_attention(c, l, M, one_launch))) break;
     if ((e = quant_rows_k<false>(c, c->pf_att, nq, nullptr, 256, M))) break;
     if ((e = kq_rows(c, L.o, M, c->pf_t, E))) break;
     add_rows_kernel<<<add_grid, 256, 0, s>>>(c->pf_x, c->pf_t, rows_e);
@@ -2121,7 +2143,7 @@ extern "C" foxcuda_status foxcuda_eval(foxcuda_context* c, const uint32_t* token
   CK(cudaEventRecord(c->ev0, c->stream), "event");
   for (size_t i = 0; chunks && i < n; i += PF_CHUNK) {
     const int M = (int)std::min<size_t>(PF_CHUNK, n - i);
-    CK(prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i), "prefill");
+    CK(prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i, false), "prefill");
     if (i + M == n) CK(enqueue_head(c), "head");
   }
   for (size_t i = 0; !chunks && i < n; ++i) {
@@ -2186,8 +2208,8 @@ extern "C" foxcuda_status foxcuda_eval_all(foxcuda_context* c, const uint32_t* t
   CK(cudaEventRecord(c->ev0, c->stream), "event");
   for (size_t i = 0; chunks && i < n; i += PF_CHUNK) {
     const int M = (int)std::min<size_t>(PF_CHUNK, n - i);
-    CK(kquant ? prefill_chunk_kq(c, c->tokens_dev + i, M, c->pos + (uint32_t)i)
-              : prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i),
+    CK(kquant ? prefill_chunk_kq(c, c->tokens_dev + i, M, c->pos + (uint32_t)i, true)
+              : prefill_chunk(c, c->tokens_dev + i, M, c->pos + (uint32_t)i, true),
        "prefill");
     if (kquant && is_kq(c->m->output.type)) {
       // a K-quant head quantises its input per 256 block like the layers:

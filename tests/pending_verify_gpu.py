@@ -9,7 +9,9 @@ keeps only the last row (src/forward.c:405-408). Row t of eval_all must be
 the logits fox_eval gives after token t. Drafts of two or more tokens take
 the chunk path: the ternary pass for the TQ models, the K-quant pass
 (Q4_K with a Q6_K v and head, as in config 3) for the third; a one-token
-draft steps.
+draft steps. In the production cases the chunk's attention is one
+cluster-kernel launch per layer (grid z = token); the parity cases keep the
+serial upstream-order kernel, one launch per token.
 """
 import numpy as np
 import pytest
