@@ -386,8 +386,10 @@ foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
  * - After every rank has exported, foxcuda_tp_p2p_open maps the others'
  *   arenas. handles holds world x FOXCUDA_IPC_HANDLE_BYTES, rank order.
  * - foxcuda_tp_p2p_row replaces amax + max-allreduce + terms + all-gather +
- *   fold of one row-parallel projection. foxcuda_tp_p2p_pick replaces
- *   head + all-gather + pick.
+ *   fold of one row-parallel projection: two kernels, the terms GEMV with
+ *   the absmax exchange and the readiness signal inside it, then the fold
+ *   (FOXCUDA_TP_P2P_FUSED=0 in the environment: four kernels).
+ *   foxcuda_tp_p2p_pick replaces head + all-gather + pick.
  * - The values and their order are those of the collective form, so the
  *   result is the single-GPU decode's, bit for bit.
  * - Every wait is bounded. A wait that gives up sets the device error word

@@ -1334,6 +1334,7 @@ struct foxcuda_context {
   uint8_t* peer_arena[TPX_MAX] = {};
   bool p2p = false;
   float* x_small = nullptr;  // [0..1] global absmax (o, down), [2..3] best pair, [4..] pairs
+  unsigned* x_count = nullptr;  // CTAs done of the fused terms GEMV (o, down)
   // repeat penalty of the sharded greedy pick (foxcuda_tp_set_penalty)
   SamplerDev* tp_smp = nullptr;
   float tp_penalty = 1.0f;
@@ -2996,6 +2997,7 @@ extern "C" foxcuda_status foxcuda_tp_p2p_export(foxcuda_context* c, void* handle
     c->arena = (uint8_t*)p;
     c->terms_d_off = off_d;
     CK(ctx_alloc(c, (4 + 2 * TPX_MAX) * 4, (void**)&c->x_small), "exchange scalars");
+    CK(ctx_alloc(c, 2 * sizeof(unsigned), (void**)&c->x_count), "exchange counters");
   }
   cudaIpcMemHandle_t h;
   CK(cudaIpcGetMemHandle(&h, c->arena), "exchange handle");
@@ -3030,12 +3032,57 @@ extern "C" foxcuda_status foxcuda_tp_p2p_clear(foxcuda_context* c) {
   cudaSetDevice(c->m->device);
   CK(cudaStreamSynchronize(c->stream), "tp sync");
   CK(cudaMemset(c->arena, 0, AR_TERMS), "clear slots");
+  CK(cudaMemset(c->x_count, 0, 2 * sizeof(unsigned)), "clear counters");
   return FOXCUDA_OK;
+}
+
+// FOXCUDA_TP_P2P_FUSED=0 keeps the absmax exchange and the readiness signal
+// in kernels of their own (four launches per row-parallel projection, not two).
+static bool p2p_fused() {
+  static const bool on = [] {
+    const char* v = getenv("FOXCUDA_TP_P2P_FUSED");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// The terms GEMV with both exchanges inside (gemv.cuh PRO_XAMAX, EPI_TERMS
+// with the readiness count): ternary shards trade the absmax in the
+// prologue; K-quant shards quantise with their own 256-block scales.
+template <int T>
+static cudaError_t launch_xterms_t(const GemvParams& p, cudaStream_t s) {
+  if constexpr (T == T_TQ1_0 || T == T_TQ2_0) return launch_gemv_t<T, PRO_XAMAX, EPI_TERMS>(p, s);
+  else return launch_gemv_t<T, PRO_VEC, EPI_TERMS>(p, s);
+}
+
+static cudaError_t launch_xterms(const foxcuda_context* c, const PackedMat& W, int which, int phase, float* amax,
+                                 float* terms, int stride) {
+  GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
+  p.x = which == 0 ? c->att : c->h;
+  p.out = terms;
+  p.terms_stride = stride;
+  p.pos = c->pos_dev;
+  p.err = c->err_dev;
+  for (int k = 0; k < TPX_MAX; ++k) p.x_peers[k] = c->peer_arena[k];
+  p.x_rank = c->m->tp_rank;
+  p.x_world = c->m->tp_size;
+  p.x_which = which;
+  p.x_phase = phase;
+  p.x_count = c->x_count + which;
+  p.x_amax = amax;
+  switch (W.type) {
+    case T_TQ1_0: return launch_xterms_t<T_TQ1_0>(p, c->stream);
+    case T_TQ2_0: return launch_xterms_t<T_TQ2_0>(p, c->stream);
+    case T_Q4_K: return launch_xterms_t<T_Q4_K>(p, c->stream);
+    case T_Q6_K: return launch_xterms_t<T_Q6_K>(p, c->stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 // foxcuda_tp_amax + max-allreduce + foxcuda_tp_terms + all-gather +
 // foxcuda_tp_fold, with the two exchanges over peer memory: the same values
-// in the same order, four launches and no host collective.
+// in the same order and no host collective. Two launches: the terms GEMV
+// with both exchanges inside it, then the fold.
 extern "C" foxcuda_status foxcuda_tp_p2p_row(foxcuda_context* c, uint32_t layer, int which) {
   foxcuda_status st = tp_check(c, layer, true);
   if (st) return st;
@@ -3047,16 +3094,20 @@ extern "C" foxcuda_status foxcuda_tp_p2p_row(foxcuda_context* c, uint32_t layer,
   const XParams x = xparams(c);
   const int phase = 2 * (int)layer + which + 1;
   float* amax = c->x_small + which;
-  if (tern) {
-    const int n = which == 0 ? (int)(m->loc.n_head * m->info.head_dim) : (int)m->loc.n_ff;
-    amax_x_kernel<<<1, 1024, 0, c->stream>>>(x, which == 0 ? c->att : c->h, n, which, phase, amax);
-    CK(cudaGetLastError(), "tp amax exchange");
-  }
   const size_t off = which == 0 ? AR_TERMS : c->terms_d_off;
   const int stride = which == 0 ? c->stride_o : c->stride_d;
-  st = foxcuda_tp_terms(c, layer, which, tern ? amax : nullptr, (float*)(c->arena + off), (uint32_t)stride);
-  if (st) return st;
-  signal_x_kernel<<<1, 32, 0, c->stream>>>(x, which, phase);
+  if (p2p_fused()) {
+    CK(launch_xterms(c, W, which, phase, amax, (float*)(c->arena + off), stride), "tp terms exchange");
+  } else {
+    if (tern) {
+      const int n = which == 0 ? (int)(m->loc.n_head * m->info.head_dim) : (int)m->loc.n_ff;
+      amax_x_kernel<<<1, 1024, 0, c->stream>>>(x, which == 0 ? c->att : c->h, n, which, phase, amax);
+      CK(cudaGetLastError(), "tp amax exchange");
+    }
+    st = foxcuda_tp_terms(c, layer, which, tern ? amax : nullptr, (float*)(c->arena + off), (uint32_t)stride);
+    if (st) return st;
+    signal_x_kernel<<<1, 32, 0, c->stream>>>(x, which, phase);
+  }
   FoldXParams f;
   memset(&f, 0, sizeof f);
   f.terms_off = off;

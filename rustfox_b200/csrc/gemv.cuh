@@ -23,20 +23,26 @@
 //   PRO_GSCALE  a tensor-parallel shard of a float vector, quantised with the
 //               absmax of the whole vector (xq_scale[0], from all shards), so
 //               its int8 values are the ones the unsplit vector gets
+//   PRO_XAMAX   as PRO_GSCALE, with the whole vector's absmax traded over
+//               peer memory inside the kernel (p2p.cuh slots): every CTA
+//               publishes the shard's absmax to every rank and takes the
+//               largest of all ranks' slots
 // EPI_TERMS (tensor-parallel row shards) writes the per-block float terms
 // instead of folding them; the shards' terms are gathered and folded in
-// upstream's block order by fold_kernel.
+// upstream's block order by fold_kernel (fold_x_kernel over peer memory,
+// where the CTA that finishes last publishes this rank's readiness).
 // Epilogues: store; residual add (src/ops.c:50-54); RoPE on adjacent pairs
 // (src/ops.c:56-73) + K/V cache write for the fused q|k|v matrix; SwiGLU
 // (src/ops.c:41-48) for the interleaved gate|up matrix.
 #pragma once
 
 #include "common.cuh"
+#include "p2p.cuh"
 #include "pack.cuh"
 
 namespace fox {
 
-enum Pro { PRO_PREQ = 0, PRO_VEC = 1, PRO_NORM = 2, PRO_GSCALE = 3 };
+enum Pro { PRO_PREQ = 0, PRO_VEC = 1, PRO_NORM = 2, PRO_GSCALE = 3, PRO_XAMAX = 4 };
 enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_TERMS = 4 };
 
 // Largest CTA per type: 64 activation registers plus a prefetched unit must
@@ -72,7 +78,62 @@ struct GemvParams {
   // launch with programmatic stream serialisation (overlap the predecessor);
   // only where every predecessor in the stream is a kernel of this chain
   int pdl;
+  // exchanges over peer memory (p2p.cuh), epochs from `pos`. PRO_XAMAX
+  // publishes into slot [x_which][x_rank] of every arena, waits for all
+  // ranks' slots in its own, and CTA 0 stores the result to x_amax (for the
+  // fold). EPI_TERMS with x_count set: each CTA counts itself done there and
+  // the last one publishes readiness [x_which][x_rank] in every arena.
+  uint8_t* x_peers[TPX_MAX];
+  int x_rank, x_world, x_which, x_phase;
+  unsigned* x_count;
+  float* x_amax;
 };
+
+// PRO_XAMAX: the largest absmax over all ranks. Every CTA publishes the same
+// shard value, so no CTA waits on another CTA of its own grid; a wait that
+// gives up sets the error word to 2 and yields 0 (the terms are then
+// garbage, and the host reports the word).
+FOX_DEV float x_trade_amax(const GemvParams& p, float am) {
+  __shared__ float g_sh;
+  if (threadIdx.x == 0) {
+    const uint32_t ep = tp_epoch(p.pos, p.x_phase);
+    const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(am);
+    for (int k = 0; k < p.x_world; ++k)
+      st_release_sys(reinterpret_cast<uint64_t*>(p.x_peers[k] + AR_AMAX) + p.x_which * TPX_MAX + p.x_rank, word);
+    const uint64_t* mine = reinterpret_cast<const uint64_t*>(p.x_peers[p.x_rank] + AR_AMAX) + p.x_which * TPX_MAX;
+    float g = 0.0f;
+    for (int k = 0; k < p.x_world; ++k) {
+      uint64_t w = 0;
+      if (!wait_hi(mine + k, ep, &w)) {
+        if (p.err) atomicExch(p.err, 2);
+        g = 0.0f;
+        break;
+      }
+      g = fmaxf(g, __uint_as_float((uint32_t)w));
+    }
+    if (blockIdx.x == 0 && p.x_amax) *p.x_amax = g;
+    g_sh = g;
+  }
+  __syncthreads();
+  return g_sh;
+}
+
+// EPI_TERMS under the peer exchange: this CTA's terms are written; the CTA
+// that counts itself last publishes this rank's readiness in every arena
+// and rearms the counter for the next launch (stream-ordered after this
+// one). Every thread fences its own terms at system scope before the count
+// (the last-block pattern), so a peer that acquires the flag sees them all.
+FOX_DEV void x_signal_ready(const GemvParams& p) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  if (atomicAdd(p.x_count, 1u) != gridDim.x - 1) return;
+  __threadfence_system();
+  *p.x_count = 0u;
+  const uint32_t ep = tp_epoch(p.pos, p.x_phase);
+  for (int k = 0; k < p.x_world; ++k)
+    st_release_sys(reinterpret_cast<uint32_t*>(p.x_peers[k] + AR_READY) + p.x_which * TPX_MAX + p.x_rank, ep);
+}
 
 // ---------------------------------------------------------------------------
 // per-type block decoders
@@ -413,6 +474,7 @@ gemv_kernel(const GemvParams p) {
         float am = 0.0f;
         for (int i = tid; i < K; i += nth) am = absmax_acc(am, xs[i]);
         amax = block_reduce<float>(am, (float*)red, OpMax(), 0.0f);
+        if (PRO == PRO_XAMAX) amax = x_trade_amax(p, amax);
       }
       const bool nz = amax > 0.0f;
       const float inv = nz ? __fdiv_rn(127.0f, amax) : 0.0f;
@@ -598,6 +660,7 @@ gemv_kernel(const GemvParams p) {
       if (Tr::PREFETCH) cur = nxt;
     }
   }
+  if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
 }
 
 }  // namespace fox

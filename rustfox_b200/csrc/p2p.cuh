@@ -21,6 +21,8 @@
 // about a second, sets the context's error word and lets the kernel finish.
 #pragma once
 
+#include <math_constants.h>
+
 #include "common.cuh"
 
 namespace fox {

@@ -15,6 +15,13 @@ the absmax into every arena, wait for all ranks' absmax in its own arena,
 write its terms, signal ready into every arena, wait for all ranks' ready,
 fold. The pick publishes a {value, index} pair, waits, and takes the first
 strict maximum.
+
+The fused form (gemv.cuh PRO_XAMAX with the EPI_TERMS readiness count, the
+default) runs the first three steps inside one kernel: every CTA, a thread
+here, publishes the same absmax and waits for all ranks' slots, writes the
+terms of its own rows, and counts itself done; the CTA that counts last
+publishes readiness. The fold starts after every CTA has finished (stream
+order: the threads are joined).
 """
 import random
 import threading
@@ -46,7 +53,22 @@ def _wait(cond, what, limit=5.0):
         time.sleep(0)
 
 
-def _run(world, n_layer, n_tok, rows, blocks, seed):
+def _trade_amax(arenas, world, r, which, ep, value):
+    """Publish this rank's absmax into every arena, then the largest of all
+    ranks' slots of this epoch in the own arena."""
+    word = (ep << 32) | int(np.float32(value).view(np.uint32))
+    for k in range(world):
+        arenas[k].amax[which, r] = np.uint64(word)
+    g = np.float32(0)
+    for k in range(world):
+        _wait(lambda: int(arenas[r].amax[which, k]) >> 32 >= ep, "amax")
+        w = int(arenas[r].amax[which, k])
+        assert w >> 32 == ep, f"rank {r} saw a later absmax epoch"
+        g = max(g, np.uint32(w & 0xffffffff).view(np.float32))
+    return g
+
+
+def _run(world, n_layer, n_tok, rows, blocks, seed, fused=False, ctas=3, count_early=False):
     rng = np.random.default_rng(seed)
     # per (token, layer, which): every rank's shard absmax and block terms
     amax = rng.random((n_tok, n_layer, 2, world)).astype(np.float32)
@@ -55,6 +77,50 @@ def _run(world, n_layer, n_tok, rows, blocks, seed):
     arenas = [Arena(rows, blocks) for _ in range(world)]
     out = [dict() for _ in range(world)]
     errors = []
+
+    def fused_kernel(r, pos, layer, which, ep, rnd):
+        """One launch of the fused terms GEMV on rank r: `ctas` CTAs, each
+        with its own rows, a shared completion counter."""
+        count = [0]
+        lock = threading.Lock()
+        seen = []
+        cta_errors = []
+        bounds = np.linspace(0, rows, ctas + 1).astype(int)
+
+        def cta(j):
+            try:
+                time.sleep(rnd.random() * 1e-4)
+                seen.append(_trade_amax(arenas, world, r, which, ep, amax[pos, layer, which, r]))
+                lo, hi = bounds[j], bounds[j + 1]
+
+                def write():
+                    arenas[r].terms[which][lo:hi] = terms[pos, layer, which, r, lo:hi]
+
+                if not count_early:
+                    time.sleep(rnd.random() * 1e-4)
+                    write()
+                with lock:   # atomicAdd on the counter
+                    last = count[0] == ctas - 1
+                    count[0] += 1
+                if last:     # the last CTA rearms the counter and publishes
+                    count[0] = 0
+                    for k in range(world):
+                        arenas[k].ready[which, r] = np.uint32(ep)
+                if count_early:  # planted: terms written after the count
+                    time.sleep(5e-3)
+                    write()
+            except BaseException as e:  # noqa: BLE001
+                cta_errors.append(e)
+
+        ts = [threading.Thread(target=cta, args=(j,)) for j in range(ctas)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join(timeout=60)
+        if cta_errors:
+            raise cta_errors[0]
+        assert len(set(float(g) for g in seen)) == 1, "the CTAs of one launch saw different absmax"
+        return seen[0]
 
     def rank_main(r):
         rnd = random.Random(seed * 31 + r)
@@ -65,20 +131,16 @@ def _run(world, n_layer, n_tok, rows, blocks, seed):
                         phase = 2 * layer + which + 1
                         ep = _epoch(pos, phase)
                         time.sleep(rnd.random() * 1e-4)
-                        word = (ep << 32) | int(np.float32(amax[pos, layer, which, r]).view(np.uint32))
-                        for k in range(world):   # amax_x_kernel: publish
-                            arenas[k].amax[which, r] = np.uint64(word)
-                        g = np.float32(0)
-                        for k in range(world):   # ... and wait in the own arena
-                            _wait(lambda: int(arenas[r].amax[which, k]) >> 32 >= ep, "amax")
-                            w = int(arenas[r].amax[which, k])
-                            assert w >> 32 == ep, f"rank {r} saw a later absmax epoch"
-                            g = max(g, np.uint32(w & 0xffffffff).view(np.float32))
-                        out[r][("amax", pos, layer, which)] = g
-                        time.sleep(rnd.random() * 1e-4)
-                        arenas[r].terms[which][:] = terms[pos, layer, which, r]   # terms GEMV
-                        for k in range(world):   # signal_x_kernel
-                            arenas[k].ready[which, r] = np.uint32(ep)
+                        if fused:
+                            out[r][("amax", pos, layer, which)] = fused_kernel(r, pos, layer, which, ep, rnd)
+                        else:
+                            # amax_x_kernel, the terms GEMV, signal_x_kernel
+                            out[r][("amax", pos, layer, which)] = _trade_amax(
+                                arenas, world, r, which, ep, amax[pos, layer, which, r])
+                            time.sleep(rnd.random() * 1e-4)
+                            arenas[r].terms[which][:] = terms[pos, layer, which, r]
+                            for k in range(world):
+                                arenas[k].ready[which, r] = np.uint32(ep)
                         for k in range(world):   # fold_x_kernel: wait ...
                             _wait(lambda: int(arenas[r].ready[which, k]) >= ep, "ready")
                             assert int(arenas[r].ready[which, k]) == ep, f"rank {r} saw a later ready epoch"
@@ -114,10 +176,9 @@ def _run(world, n_layer, n_tok, rows, blocks, seed):
     return out, amax, terms, picks
 
 
-@pytest.mark.parametrize("world", [2, 3, 8])
-def test_exchange_protocol_reads_every_value_once_and_folds_in_order(world):
-    n_layer, n_tok, rows, blocks = 3, 4, 5, 3
-    out, amax, terms, picks = _run(world, n_layer, n_tok, rows, blocks, seed=world)
+def _wrong(world, n_layer, n_tok, rows, blocks, out, amax, terms, picks):
+    """The (rank, what) pairs whose result is not the unsharded one."""
+    bad = []
     for pos in range(n_tok):
         for layer in range(n_layer):
             for which in (0, 1):
@@ -127,9 +188,31 @@ def test_exchange_protocol_reads_every_value_once_and_folds_in_order(world):
                     for j in range(blocks):
                         want = (want + terms[pos, layer, which, k, :, j]).astype(np.float32)
                 for r in range(world):
-                    assert out[r][("amax", pos, layer, which)] == want_amax
-                    assert np.array_equal(out[r][("fold", pos, layer, which)].view(np.uint32),
-                                          want.view(np.uint32))
+                    if out[r][("amax", pos, layer, which)] != want_amax:
+                        bad.append((r, "amax", pos, layer, which))
+                    if not np.array_equal(out[r][("fold", pos, layer, which)].view(np.uint32),
+                                          want.view(np.uint32)):
+                        bad.append((r, "fold", pos, layer, which))
         k = int(np.argmax(picks[pos]))
         for r in range(world):
-            assert out[r][("pick", pos)] == (picks[pos, k], k * 1000 + pos)
+            if out[r][("pick", pos)] != (picks[pos, k], k * 1000 + pos):
+                bad.append((r, "pick", pos))
+    return bad
+
+
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "separate"])
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_exchange_protocol_reads_every_value_once_and_folds_in_order(world, fused):
+    shape = (world, 3, 4, 5, 3)  # world, layers, tokens, rows, blocks
+    got = _run(*shape, seed=world, fused=fused)
+    assert _wrong(*shape, *got) == []
+
+
+def test_a_count_taken_before_the_terms_are_written_is_caught():
+    """The model of the fused kernel with a planted ordering mistake: CTAs
+    count themselves done before writing their terms, so the last count
+    publishes readiness over terms still missing. The check above sees the
+    folds read stale terms."""
+    shape = (2, 2, 2, 6, 3)
+    got = _run(*shape, seed=5, fused=True, ctas=3, count_early=True)
+    assert any(b[1] == "fold" for b in _wrong(*shape, *got))
