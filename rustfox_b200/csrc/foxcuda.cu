@@ -1502,14 +1502,32 @@ static uint64_t launch_weight_bytes(const foxcuda_model* m, int kind, uint32_t l
   }
 }
 
+// FOXCUDA_TP_PDL=1: a tensor-parallel step whose exchanges run over peer
+// memory launches its GEMVs and head with programmatic stream serialisation,
+// like the single-GPU step (its stream then holds only this library's
+// kernels). Off by default.
+static bool tp_pdl() {
+  static const bool on = [] {
+    const char* v = getenv("FOXCUDA_TP_PDL");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
+// Whether the context's GEMVs and head overlap their predecessors.
+static bool ctx_pdl(const foxcuda_context* c) {
+  if (c->m->tp_size == 1 && !c->tp_steps) return true;
+  // A tensor-parallel step with NCCL collectives between its kernels keeps
+  // plain stream order: a kernel overlapped after one of those read its
+  // input before it landed (measured: the head after the last fold, with
+  // the collective on the process group's own stream, joined by an event).
+  return c->p2p && tp_pdl();
+}
+
 // A layer GEMV through the kernel its layout was packed for.
 static cudaError_t launch_mat(foxcuda_context* c, const PackedMat& W, int pro, int epi, GemvParams& p) {
   p.err = c->err_dev;
-  // The single-GPU step is a chain of these kernels and overlaps them. A
-  // tensor-parallel step puts collectives between its kernels, and a kernel
-  // overlapped after one of those read its input before it landed
-  // (measured: the head after the last fold), so it keeps plain stream order.
-  p.pdl = c->m->tp_size == 1 && !c->tp_steps;
+  p.pdl = ctx_pdl(c);
   if (W.slice) return launch_slice(W.type, pro, epi, p, W.g, W.grid, c->stream);
   return launch_ring(W.type, pro, epi, p, c->stream);
 }
@@ -1735,9 +1753,7 @@ static cudaError_t launch_head_on(foxcuda_context* c, cudaStream_t s, bool pdl) 
   return launch_ring(H.type, PRO_NORM, EPI_STORE, p, s);
 }
 
-static cudaError_t launch_head(foxcuda_context* c) {
-  return launch_head_on(c, c->stream, c->m->tp_size == 1 && !c->tp_steps);
-}
+static cudaError_t launch_head(foxcuda_context* c) { return launch_head_on(c, c->stream, ctx_pdl(c)); }
 
 static cudaError_t enqueue_body(foxcuda_context* c, bool trace) {
   foxcuda_model* m = c->m;

@@ -121,7 +121,11 @@ struct FoldXParams {
   float* x;             // residual, += the row values
 };
 
+// It releases a programmatic successor at once, so that successor can stage
+// its weights while this kernel waits for the peers; the successor's
+// griddepcontrol.wait still waits for this whole grid and its writes.
 __global__ void fold_x_kernel(const XParams x, const FoldXParams f) {
+  griddep_launch_dependents();
   __shared__ int ok_sh;
   const uint32_t ep = tp_epoch(x.pos, f.phase);
   const uint32_t* ready = reinterpret_cast<const uint32_t*>(x.peers[x.rank] + AR_READY) + f.which * TPX_MAX;

@@ -9,7 +9,8 @@ The one-GPU case runs the exchange kernels with a single rank (each slot
 written and read in the rank's own arena). By default the absmax exchange and
 the readiness signal run inside the terms GEMV (two launches per
 row-parallel projection); one test keeps them in kernels of their own
-(FOXCUDA_TP_P2P_FUSED=0). The two-GPU case maps the peer's
+(FOXCUDA_TP_P2P_FUSED=0), and one launches the GEMVs and the head with
+programmatic stream serialisation (FOXCUDA_TP_PDL=1). The two-GPU case maps the peer's
 arena through CUDA IPC. The same harness as test_tp_gpu.py applies: ranks
 are child processes, and the parent fails as soon as one exits abnormally.
 """
@@ -30,10 +31,13 @@ N_GEN = 32
 N_CTX = 96
 
 
-def run_rank(rank, world, port, cfg, kv, exact, graphs, out_q, exchange="p2p", penalty=1.0, fused=True):
+def run_rank(rank, world, port, cfg, kv, exact, graphs, out_q, exchange="p2p", penalty=1.0, fused=True,
+             pdl=False):
     import datetime
     import os
-    os.environ["FOXCUDA_TP_P2P_FUSED"] = "1" if fused else "0"  # read once, at the first exchange
+    # read once by the library, at the first exchange and the first launch
+    os.environ["FOXCUDA_TP_P2P_FUSED"] = "1" if fused else "0"
+    os.environ["FOXCUDA_TP_PDL"] = "1" if pdl else "0"
     import torch.distributed as dist
     import rustfox_b200 as rf
     from rustfox_b200.tp import TPContext
@@ -60,7 +64,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _tp_tokens(cfg, kv, exact, graphs, world, limit_s=240, exchange="p2p", penalty=1.0, fused=True):
+def _tp_tokens(cfg, kv, exact, graphs, world, limit_s=240, exchange="p2p", penalty=1.0, fused=True,
+               pdl=False):
     import queue
     import time
     import torch.multiprocessing as mp
@@ -68,7 +73,7 @@ def _tp_tokens(cfg, kv, exact, graphs, world, limit_s=240, exchange="p2p", penal
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=run_rank,
-                         args=(r, world, port, cfg, kv, exact, graphs, q, exchange, penalty, fused))
+                         args=(r, world, port, cfg, kv, exact, graphs, q, exchange, penalty, fused, pdl))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -140,3 +145,19 @@ def test_p2p_separate_exchange_kernels_equal_one_gpu(world):
     want = rf.greedy_generate(m, PROMPT, N_GEN, N_CTX, kv="f16", repeat_penalty=1.0)
     m.close()
     assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
+
+
+@pytest.mark.parametrize("world", [1, 2])
+@pytest.mark.parametrize("graphs", [False, True], ids=["eager", "graph"])
+def test_p2p_programmatic_launch_equal_one_gpu(world, graphs):
+    """FOXCUDA_TP_PDL=1: the GEMVs and the head overlap their predecessors
+    (the fold releases them at its start), in parity and production mode."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import rustfox_b200 as rf
+    for kv, exact in (("f32", True), ("f16", False)):
+        got = _tp_tokens(CFG_TQ2, kv, exact, graphs, world, pdl=True)
+        m = rf.Model.from_synthetic(synth.generate(CFG_TQ2))
+        want = rf.greedy_generate(m, PROMPT, N_GEN, N_CTX, kv=kv, repeat_penalty=1.0, attn_exact=exact)
+        m.close()
+        assert np.array_equal(got, want), f"{kv}: first divergence at {np.argmax(got != want)}"
