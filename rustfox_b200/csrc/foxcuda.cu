@@ -1275,6 +1275,7 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
   CK(cudaDeviceSynchronize(), "finalize head");
   m->embd = emb;
   m->device_bytes += emb.bytes;
+  m->allocs.push_back(emb.dev);  // freed with the model
   emb = RawTensor();  // ownership moves to m->embd
   free_raw(outw);
   free_raw(m->slot(FOXCUDA_OUTPUT_NORM, 0));
