@@ -73,6 +73,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=0, metavar="N",
                     help="decode N sequences together at a --ctx long synthetic context "
                          "(config 5: --config 8b-tq2 --batch 16 --ctx 32768)")
+    ap.add_argument("--image", action="store_true",
+                    help="time the model load: tensors uploaded and packed on the device, "
+                         "against a device image opened from a file")
     return ap.parse_args()
 
 
@@ -668,10 +671,64 @@ def run_batch(args):
     model.close()
 
 
+def run_image(args):
+    """Model load, two ways, wall time of the (synchronous) model calls:
+    every tensor uploaded from host memory and packed on the device
+    (foxcuda_model_upload + finalize), and a device image of the same model
+    opened from a file (foxcuda_model_open_image; median of up to 3 opens,
+    the file in the page cache after it was written). Both models then
+    decode the same tokens."""
+    import shutil
+    import torch
+    import rustfox_b200 as rf
+    from rustfox_b200 import synth
+    cfg = synth.CONFIGS[args.config]
+    torch.cuda.set_device(0)
+    host = synth.generate(cfg)
+    t0 = time.perf_counter()
+    a = rf.Model.from_synthetic(host)
+    upload_s = time.perf_counter() - t0
+    d = tempfile.mkdtemp(prefix="foximg")
+    try:
+        path = os.path.join(d, "model.fdi")
+        t0 = time.perf_counter()
+        a.save_image(path)
+        save_s = time.perf_counter() - t0
+        size = os.path.getsize(path)
+        opens = []
+        b = None
+        for _ in range(max(1, min(args.steps, 3))):
+            if b is not None:
+                b.close()
+            t0 = time.perf_counter()
+            b = rf.Model.open_image(path)
+            opens.append(time.perf_counter() - t0)
+        prompt = synth.random_prompt(cfg, 16, seed=1)
+        same = bool(np.array_equal(rf.greedy_generate(a, prompt, 8, 64, repeat_penalty=1.0),
+                                   rf.greedy_generate(b, prompt, 8, 64, repeat_penalty=1.0)))
+        b.close()
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    a.close()
+    open_s = statistics.median(opens)
+    print(json.dumps({
+        "metric": "model load seconds", "value": open_s, "unit": "s", "higher_is_better": False,
+        "dtype": "bytes", "data": "synthetic (seeded random-init weights)",
+        "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd}: upload + pack vs device image"},
+        "results": {"upload_and_pack_s": upload_s, "image_open_s": open_s, "image_save_s": save_s,
+                    "image_bytes": size, "image_open_gbs": size / open_s / 1e9,
+                    "speedup": upload_s / open_s, "tokens_identical": same},
+        "cpu_baseline": None,
+        "note": "upstream loads through its own GGUF/foxpack reader on the host; no device "
+                "counterpart to time"}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.image:
+        run_image(args)
     elif args.gemm:
         run_gemm(args)
     elif args.prefill:

@@ -208,6 +208,25 @@ foxcuda_status foxcuda_model_upload(foxcuda_model *m, int role, uint32_t layer,
 foxcuda_status foxcuda_model_finalize(foxcuda_model *m);
 void           foxcuda_model_destroy(foxcuda_model *m);
 uint64_t       foxcuda_model_device_bytes(const foxcuda_model *m);
+/* replaces fox_model_get_info (include/fox/fox.h:429): the whole model's
+ * shape fields */
+foxcuda_status foxcuda_model_get_info(const foxcuda_model *m, foxcuda_model_info *out);
+
+/* Device images: the device-side counterpart of upstream's repacker
+ * (fox_repack_gguf, include/fox/fox.h:262, src/repack.c:170-315), which
+ * makes each layer one contiguous span of the file. An image holds a
+ * finalized model (or tensor-parallel shard) exactly as it sits in HBM:
+ * packed layouts, TQ1_0 layers already held as TQ2_0, norms as floats.
+ * - foxcuda_model_save_image writes it (FOXCUDA_ERR_IO on a file error).
+ * - foxcuda_model_open_image checks the header and every entry against the
+ *   model it describes before touching the device (FOXCUDA_ERR_FORMAT),
+ *   then reads the file through two pinned buffers into one device
+ *   allocation: no packing kernel and no GGUF parse. An image whose
+ *   matrices were laid out for another SM count is refused
+ *   (FOXCUDA_ERR_UNSUPPORTED); build that model from its GGUF instead.
+ * The opened model decodes exactly as the one that was saved. */
+foxcuda_status foxcuda_model_save_image(const foxcuda_model *m, const char *path);
+foxcuda_status foxcuda_model_open_image(const char *path, int device, foxcuda_model **out);
 
 /* KV cache element type */
 enum { FOXCUDA_KV_F16 = 0, FOXCUDA_KV_F32 = 1 };

@@ -86,6 +86,9 @@ _PROTOS = {
     "foxcuda_model_finalize": (_st, [_vp]),
     "foxcuda_model_destroy": (None, [_vp]),
     "foxcuda_model_device_bytes": (C.c_uint64, [_vp]),
+    "foxcuda_model_get_info": (_st, [_vp, C.POINTER(ModelInfo)]),
+    "foxcuda_model_save_image": (_st, [_vp, C.c_char_p]),
+    "foxcuda_model_open_image": (_st, [C.c_char_p, C.c_int, C.POINTER(_vp)]),
     "foxcuda_context_create": (_st, [_vp, C.POINTER(ContextConfig), C.POINTER(_vp)]),
     "foxcuda_context_destroy": (None, [_vp]),
     "foxcuda_context_reset": (None, [_vp]),
@@ -366,6 +369,28 @@ class Model:
                     rope_freq_base=float(get("rope.freq_base", 10000.0)))
         return cls(info, ((t.name, t.ggml_type, t.ne, g.tensor_bytes(t.name))
                           for t in g.tensors.values()), device)
+
+    def save_image(self, path: str) -> None:
+        """Writes this model's HBM layout to a device image (the device-side
+        counterpart of upstream's fox_repack_gguf, src/repack.c:170-315)."""
+        _check(lib().foxcuda_model_save_image(self.h, os.fsencode(path)))
+
+    @classmethod
+    def open_image(cls, path: str, device: int = 0) -> "Model":
+        """A model read from a device image onto `device`: one sequential
+        read into HBM, no GGUF parse and no packing."""
+        h = C.c_void_p()
+        _check(lib().foxcuda_model_open_image(os.fsencode(path), device, C.byref(h)))
+        self = cls.__new__(cls)
+        self.h = h
+        self.device = device
+        mi = ModelInfo()
+        _check(lib().foxcuda_model_get_info(self.h, C.byref(mi)))
+        self.info = {name: getattr(mi, name) for name, _ in ModelInfo._fields_}
+        from .tp import shape  # tp.py builds on this module
+        s = shape(self)
+        self.tp_rank, self.tp_size = int(s.tp_rank), int(s.tp_size)
+        return self
 
     @property
     def device_bytes(self) -> int:

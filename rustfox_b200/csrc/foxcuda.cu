@@ -3,10 +3,12 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cerrno>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <vector>
 
@@ -1280,6 +1282,367 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
   free_raw(outw);
   free_raw(m->slot(FOXCUDA_OUTPUT_NORM, 0));
   m->finalized = true;
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_model_get_info(const foxcuda_model* m, foxcuda_model_info* out) {
+  if (!m || !out) return fail(FOXCUDA_ERR_ARG, "model_get_info: null argument");
+  *out = m->info;
+  return FOXCUDA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// device images: a finalized model's HBM layout in one file
+//
+// Upstream's repacker (fox_repack_gguf, src/repack.c:170-315) rewrites a GGUF
+// so that each layer's tensors form one contiguous span, which its loader
+// then maps instead of gathering. The device image goes one step further: the
+// file holds the bytes exactly as they sit in HBM after finalize (TQ1_0
+// layers already held as TQ2_0, q|k|v concatenated, gate|up interleaved,
+// every matrix in its packed unit layout, norms as floats). Opening one is a
+// sequential read through two pinned buffers into one device allocation,
+// with no packing kernel and no staging copy on the device.
+//
+// Layout (little-endian): ImgHeader, n_entries ImgEntry, zero padding up to
+// data_off (a multiple of 4096), then the data section. Entry offsets are
+// relative to data_off and multiples of 256.
+
+namespace {
+
+constexpr char kImgMagic[8] = {'F', 'O', 'X', 'D', 'I', 'M', 'G', '1'};
+constexpr uint32_t kImgVersion = 1;
+enum ImgKind : uint32_t {
+  IK_EMBD = 0, IK_OUT_NORM, IK_OUTPUT, IK_ATTN_NORM, IK_FFN_NORM, IK_QKV, IK_O, IK_GATEUP, IK_DOWN, IK_N
+};
+constexpr uint32_t IMG_ROWS32 = 1, IMG_SLICE = 2;
+
+struct ImgHeader {
+  char magic[8];
+  uint32_t version, n_entries;
+  uint64_t data_off, data_bytes;
+  uint32_t sm_count, tp_rank, tp_size, vocab0;
+  foxcuda_model_info info, loc;
+  uint32_t q_row0, kv_row0, o_block0, o_blocks, f_block0, f_blocks, f_blocks_all[8];
+  uint64_t table_hash;  // FNV-1a 64 of the entry table
+};
+struct ImgEntry {
+  uint32_t kind, layer, index, flags;
+  int32_t type, src_type, n_rows, K, nb, U, pro, qkv_base;
+  uint64_t ne0, ne1;  // the embedding's GGUF shape
+  uint64_t offset, bytes;
+};
+static_assert(sizeof(ImgHeader) == 184 && sizeof(ImgEntry) == 80, "image records have no padding");
+
+constexpr size_t kImgChunk = 64ull << 20;  // bytes per pinned staging buffer
+
+uint64_t fnv1a(const void* p, size_t n) {
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < n; ++i) h = (h ^ reinterpret_cast<const uint8_t*>(p)[i]) * 1099511628211ull;
+  return h;
+}
+
+size_t mat_bytes(const PackedMat& W) { return (size_t)W.n_rows * row_bytes(W.type, W.K); }
+
+ImgEntry mat_entry(const PackedMat& W) {
+  ImgEntry e{};
+  e.type = W.type; e.src_type = W.src_type; e.n_rows = W.n_rows; e.K = W.K; e.nb = W.nb; e.U = W.U;
+  e.pro = W.pro;
+  e.flags = (W.rows32 ? IMG_ROWS32 : 0u) | (W.slice ? IMG_SLICE : 0u);
+  return e;
+}
+
+// Pinned staging buffers, a copy stream and an event per buffer, released on
+// every path (after the stream has drained).
+struct Staging {
+  void* buf[2] = {nullptr, nullptr};
+  cudaStream_t s = nullptr;
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  ~Staging() {
+    if (s) cudaStreamSynchronize(s);
+    for (int i = 0; i < 2; ++i) {
+      if (buf[i]) cudaFreeHost(buf[i]);
+      if (ev[i]) cudaEventDestroy(ev[i]);
+    }
+    if (s) cudaStreamDestroy(s);
+  }
+  cudaError_t init(int n_buf) {
+    cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    for (int i = 0; i < n_buf && e == cudaSuccess; ++i) {
+      e = cudaMallocHost(&buf[i], kImgChunk);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+    }
+    return e;
+  }
+};
+
+struct FileCloser {
+  void operator()(FILE* f) const {
+    if (f) fclose(f);
+  }
+};
+
+}  // namespace
+
+extern "C" foxcuda_status foxcuda_model_save_image(const foxcuda_model* m, const char* path) {
+  if (!m || !path) return fail(FOXCUDA_ERR_ARG, "save_image: null argument");
+  if (!m->finalized) return fail(FOXCUDA_ERR_ARG, "save_image: finalize the model first");
+  struct Src { ImgEntry e; const void* dev; };
+  std::vector<Src> src;
+  uint64_t off = 0;
+  auto add = [&](uint32_t kind, uint32_t layer, uint32_t index, const void* dev, uint64_t bytes, ImgEntry e) {
+    e.kind = kind; e.layer = layer; e.index = index; e.offset = off; e.bytes = bytes;
+    off = (off + bytes + 255) / 256 * 256;
+    src.push_back({e, dev});
+  };
+  const uint64_t E = m->info.n_embd;
+  {
+    ImgEntry e{};
+    e.type = m->embd.type; e.src_type = m->embd.src_type; e.ne0 = m->embd.ne0; e.ne1 = m->embd.ne1;
+    add(IK_EMBD, 0, 0, m->embd.dev, m->embd.bytes, e);
+  }
+  add(IK_OUT_NORM, 0, 0, m->out_norm, E * 4, ImgEntry{});
+  add(IK_OUTPUT, 0, 0, m->output.dev, mat_bytes(m->output), mat_entry(m->output));
+  for (uint32_t l = 0; l < m->info.n_layer; ++l) {
+    const LayerW& L = m->layers[l];
+    add(IK_ATTN_NORM, l, 0, L.attn_norm, E * 4, ImgEntry{});
+    add(IK_FFN_NORM, l, 0, L.ffn_norm, E * 4, ImgEntry{});
+    for (int i = 0; i < L.n_qkv; ++i) {
+      ImgEntry e = mat_entry(L.qkv[i]);
+      e.qkv_base = L.qkv_base[i];
+      add(IK_QKV, l, (uint32_t)i, L.qkv[i].dev, mat_bytes(L.qkv[i]), e);
+    }
+    add(IK_O, l, 0, L.o.dev, mat_bytes(L.o), mat_entry(L.o));
+    add(IK_GATEUP, l, 0, L.gateup.dev, mat_bytes(L.gateup), mat_entry(L.gateup));
+    add(IK_DOWN, l, 0, L.down.dev, mat_bytes(L.down), mat_entry(L.down));
+  }
+  std::vector<ImgEntry> table;
+  for (const Src& s : src) table.push_back(s.e);
+  ImgHeader h;
+  memset(&h, 0, sizeof h);
+  memcpy(h.magic, kImgMagic, 8);
+  h.version = kImgVersion;
+  h.n_entries = (uint32_t)table.size();
+  h.data_off = (sizeof h + table.size() * sizeof(ImgEntry) + 4095) / 4096 * 4096;
+  h.data_bytes = off;
+  h.sm_count = (uint32_t)sm_count(m->device);
+  h.tp_rank = (uint32_t)m->tp_rank; h.tp_size = (uint32_t)m->tp_size; h.vocab0 = m->vocab0;
+  h.info = m->info; h.loc = m->loc;
+  h.q_row0 = m->q_row0; h.kv_row0 = m->kv_row0; h.o_block0 = m->o_block0; h.o_blocks = m->o_blocks;
+  h.f_block0 = m->f_block0; h.f_blocks = m->f_blocks;
+  memcpy(h.f_blocks_all, m->f_blocks_all, sizeof h.f_blocks_all);
+  h.table_hash = fnv1a(table.data(), table.size() * sizeof(ImgEntry));
+
+  std::unique_ptr<FILE, FileCloser> f(fopen(path, "wb"));
+  if (!f) return fail(FOXCUDA_ERR_IO, "save_image: cannot create %s: %s", path, strerror(errno));
+  static const uint8_t zeros[4096] = {0};
+  auto put = [&](const void* p, size_t n) { return fwrite(p, 1, n, f.get()) == n; };
+  auto pad = [&](uint64_t n) {
+    while (n > 0) {
+      const size_t k = (size_t)std::min<uint64_t>(n, sizeof zeros);
+      if (!put(zeros, k)) return false;
+      n -= k;
+    }
+    return true;
+  };
+  auto io_fail = [&]() { return fail(FOXCUDA_ERR_IO, "save_image: writing %s: %s", path, strerror(errno)); };
+  const uint64_t head_bytes = sizeof h + table.size() * sizeof(ImgEntry);
+  if (!put(&h, sizeof h) || !put(table.data(), table.size() * sizeof(ImgEntry)) || !pad(h.data_off - head_bytes))
+    return io_fail();
+  cudaSetDevice(m->device);
+  Staging st;
+  CK(st.init(1), "save_image staging");
+  uint64_t pos = 0;
+  for (const Src& s : src) {
+    if (!pad(s.e.offset - pos)) return io_fail();
+    for (uint64_t done = 0; done < s.e.bytes;) {
+      const size_t n = (size_t)std::min<uint64_t>(kImgChunk, s.e.bytes - done);
+      CK(cudaMemcpyAsync(st.buf[0], (const uint8_t*)s.dev + done, n, cudaMemcpyDeviceToHost, st.s),
+         "save_image copy");
+      CK(cudaStreamSynchronize(st.s), "save_image copy");
+      if (!put(st.buf[0], n)) return io_fail();
+      done += n;
+    }
+    pos = s.e.offset + s.e.bytes;
+  }
+  if (!pad(h.data_bytes - pos)) return io_fail();
+  if (fclose(f.release()) != 0) return fail(FOXCUDA_ERR_IO, "save_image: closing %s: %s", path, strerror(errno));
+  return FOXCUDA_OK;
+}
+
+// Every check of an image that needs no device: the table against its hash,
+// each entry's place in the data, and its shape against the model (shard)
+// the header describes.
+static foxcuda_status check_image(const ImgHeader& h, const std::vector<ImgEntry>& t, const char* path) {
+  const foxcuda_model_info& mi = h.info;
+  const foxcuda_model_info& lo = h.loc;
+  if (h.tp_size < 1 || h.tp_size > 8 || h.tp_rank >= h.tp_size)
+    return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: shard %u of %u", path, h.tp_rank, h.tp_size);
+  if (fnv1a(t.data(), t.size() * sizeof(ImgEntry)) != h.table_hash)
+    return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: the tensor table is corrupt", path);
+  const uint64_t E = mi.n_embd;
+  const int nq = (int)(lo.n_head * mi.head_dim), nkv = (int)(lo.n_head_kv * mi.head_dim);
+  std::vector<int> seen((size_t)IK_N * (mi.n_layer + 1), 0);
+  std::vector<int> qkv_runs(mi.n_layer, 0), qkv_rows(mi.n_layer, 0);
+  for (size_t i = 0; i < t.size(); ++i) {
+    const ImgEntry& e = t[i];
+    const bool per_layer = e.kind == IK_ATTN_NORM || e.kind == IK_FFN_NORM || e.kind == IK_QKV ||
+                           e.kind == IK_O || e.kind == IK_GATEUP || e.kind == IK_DOWN;
+    if (e.kind >= IK_N || (per_layer ? e.layer >= mi.n_layer : e.layer != 0))
+      return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: entry %zu has kind %u, layer %u", path, i, e.kind, e.layer);
+    if (e.offset % 256 || e.offset > h.data_bytes || e.bytes > h.data_bytes - e.offset)
+      return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: entry %zu lies outside the data", path, i);
+    if (e.kind == IK_QKV) {
+      if (e.index >= 3 || e.index != (uint32_t)qkv_runs[e.layer] || e.qkv_base != qkv_rows[e.layer])
+        return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: q|k|v run %u of layer %u is out of order", path,
+                    e.index, e.layer);
+      qkv_runs[e.layer]++;
+      qkv_rows[e.layer] += e.n_rows;
+    } else if (e.index != 0 || seen[(size_t)e.kind * (mi.n_layer + 1) + e.layer]++) {
+      return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: entry %zu repeats kind %u of layer %u", path, i, e.kind,
+                  e.layer);
+    }
+    if (e.kind == IK_OUT_NORM || e.kind == IK_ATTN_NORM || e.kind == IK_FFN_NORM) {
+      if (e.bytes != E * 4)
+        return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: a norm is not %llu floats", path, (unsigned long long)E);
+    } else if (e.kind == IK_EMBD) {
+      if (e.ne0 != E || e.ne1 != mi.n_vocab || row_bytes(e.type, e.ne0) == 0 ||
+          e.bytes != e.ne1 * row_bytes(e.type, e.ne0))
+        return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: the embedding is not %llux%u", path,
+                    (unsigned long long)E, mi.n_vocab);
+    } else {
+      if (!type_gemv_ok(e.type) || e.n_rows <= 0 || e.K <= 0 || e.U <= 0 || row_bytes(e.type, e.K) == 0 ||
+          e.nb != e.K / block_elems(e.type) || e.bytes != (uint64_t)e.n_rows * row_bytes(e.type, e.K))
+        return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: matrix entry %zu (type %d, %d x %d) is inconsistent",
+                    path, i, e.type, e.n_rows, e.K);
+      bool ok = true;
+      if (e.kind == IK_OUTPUT) ok = e.K == (int)E && e.n_rows == (int)lo.n_vocab;
+      if (e.kind == IK_QKV) ok = e.K == (int)E && qkv_rows[e.layer] <= nq + 2 * nkv;
+      if (e.kind == IK_O) ok = e.K == nq && e.n_rows == (int)E;
+      if (e.kind == IK_GATEUP) ok = e.K == (int)E && e.n_rows == 2 * (int)lo.n_ff;
+      if (e.kind == IK_DOWN) ok = e.K == (int)lo.n_ff && e.n_rows == (int)E;
+      if (!ok)
+        return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: matrix entry %zu (%d x %d) does not fit the model",
+                    path, i, e.n_rows, e.K);
+    }
+  }
+  for (uint32_t k : {IK_EMBD, IK_OUT_NORM, IK_OUTPUT})
+    if (!seen[(size_t)k * (mi.n_layer + 1)])
+      return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: entry kind %u is missing", path, k);
+  for (uint32_t l = 0; l < mi.n_layer; ++l) {
+    for (uint32_t k : {IK_ATTN_NORM, IK_FFN_NORM, IK_O, IK_GATEUP, IK_DOWN})
+      if (!seen[(size_t)k * (mi.n_layer + 1) + l])
+        return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: layer %u lacks entry kind %u", path, l, k);
+    if (qkv_rows[l] != nq + 2 * nkv)
+      return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: layer %u has %d q|k|v rows, not %d", path, l,
+                  qkv_rows[l], nq + 2 * nkv);
+  }
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_model_open_image(const char* path, int device, foxcuda_model** out) {
+  if (!path || !out) return fail(FOXCUDA_ERR_ARG, "open_image: null argument");
+  *out = nullptr;
+  std::unique_ptr<FILE, FileCloser> f(fopen(path, "rb"));
+  if (!f) return fail(FOXCUDA_ERR_IO, "open_image: cannot open %s: %s", path, strerror(errno));
+  if (fseeko(f.get(), 0, SEEK_END) != 0) return fail(FOXCUDA_ERR_IO, "open_image: cannot size %s", path);
+  const uint64_t file_bytes = (uint64_t)ftello(f.get());
+  rewind(f.get());
+  ImgHeader h;
+  if (fread(&h, sizeof h, 1, f.get()) != 1) return fail(FOXCUDA_ERR_FORMAT, "open_image: %s is too short", path);
+  if (memcmp(h.magic, kImgMagic, 8) != 0)
+    return fail(FOXCUDA_ERR_FORMAT, "open_image: %s is not a foxcuda device image", path);
+  if (h.version != kImgVersion)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "open_image: %s has image version %u, this build reads %u", path,
+                h.version, kImgVersion);
+  if (h.info.n_layer == 0 || h.info.n_layer > 4096 || h.n_entries == 0 || h.n_entries > 16 + 8 * h.info.n_layer)
+    return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: %u entries for %u layers", path, h.n_entries, h.info.n_layer);
+  const uint64_t head_bytes = sizeof h + (uint64_t)h.n_entries * sizeof(ImgEntry);
+  if (h.data_off % 4096 || h.data_off < head_bytes || h.data_off > file_bytes ||
+      h.data_bytes != file_bytes - h.data_off)
+    return fail(FOXCUDA_ERR_FORMAT, "open_image: %s is truncated or padded (%llu bytes, %llu of data at %llu)",
+                path, (unsigned long long)file_bytes, (unsigned long long)h.data_bytes,
+                (unsigned long long)h.data_off);
+  std::vector<ImgEntry> table(h.n_entries);
+  if (fread(table.data(), sizeof(ImgEntry), table.size(), f.get()) != table.size())
+    return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: the tensor table is short", path);
+  foxcuda_status st = check_image(h, table, path);
+  if (st) return st;
+
+  // the device side
+  if ((st = foxcuda_init(device))) return st;
+  bool any_slice = false;
+  for (const ImgEntry& e : table) any_slice |= (e.flags & IMG_SLICE) != 0;
+  if (any_slice && h.sm_count != (uint32_t)sm_count(device))
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "open_image: %s was laid out for %u SMs and device %d has %d; build the "
+                "model from its GGUF here", path, h.sm_count, device, sm_count(device));
+  foxcuda_model* m = nullptr;
+  if ((st = foxcuda_model_create_tp(&h.info, device, (int)h.tp_rank, (int)h.tp_size, &m))) return st;
+  std::unique_ptr<foxcuda_model, void (*)(foxcuda_model*)> guard(m, foxcuda_model_destroy);
+  if (memcmp(&m->loc, &h.loc, sizeof h.loc) != 0 || m->vocab0 != h.vocab0 || m->o_block0 != h.o_block0 ||
+      m->f_block0 != h.f_block0 || m->f_blocks != h.f_blocks)
+    return fail(FOXCUDA_ERR_FORMAT, "open_image: %s: its shard geometry is not this build's", path);
+  void* arena = nullptr;
+  CK(dev_alloc(m, h.data_bytes, &arena), "open_image: device allocation");
+  {
+    Staging sg;
+    CK(sg.init(2), "open_image staging");
+    if (fseeko(f.get(), (off_t)h.data_off, SEEK_SET) != 0) return fail(FOXCUDA_ERR_IO, "open_image: seek in %s", path);
+    int i = 0;
+    for (uint64_t pos = 0; pos < h.data_bytes; ++i) {
+      const int b = i & 1;
+      if (i >= 2) CK(cudaEventSynchronize(sg.ev[b]), "open_image copy");  // this buffer's last copy is done
+      const size_t n = (size_t)std::min<uint64_t>(kImgChunk, h.data_bytes - pos);
+      if (fread(sg.buf[b], 1, n, f.get()) != n) return fail(FOXCUDA_ERR_IO, "open_image: reading %s", path);
+      CK(cudaMemcpyAsync((uint8_t*)arena + pos, sg.buf[b], n, cudaMemcpyHostToDevice, sg.s), "open_image copy");
+      CK(cudaEventRecord(sg.ev[b], sg.s), "open_image copy");
+      pos += n;
+    }
+    CK(cudaStreamSynchronize(sg.s), "open_image copy");
+  }
+  uint8_t* base = (uint8_t*)arena;
+  uint64_t used = 0;
+  auto set_mat = [&](const ImgEntry& e, PackedMat* W) -> foxcuda_status {
+    W->type = e.type; W->src_type = e.src_type; W->n_rows = e.n_rows; W->K = e.K; W->nb = e.nb; W->U = e.U;
+    W->dev = base + e.offset;
+    W->rows32 = (e.flags & IMG_ROWS32) != 0;
+    W->pro = e.pro;
+    if (e.flags & IMG_SLICE) {
+      set_slice(m, W, e.pro);
+      if (W->g.smem > SLICE_MAX_SMEM)
+        return fail(FOXCUDA_ERR_UNSUPPORTED, "open_image: %s: a slice matrix needs %zu bytes of shared memory",
+                    path, W->g.smem);
+    }
+    return FOXCUDA_OK;
+  };
+  for (const ImgEntry& e : table) {
+    used += e.bytes;
+    float* fp = reinterpret_cast<float*>(base + e.offset);
+    switch (e.kind) {
+      case IK_EMBD:
+        m->embd.type = e.type; m->embd.src_type = e.src_type; m->embd.ne0 = e.ne0; m->embd.ne1 = e.ne1;
+        m->embd.dev = base + e.offset; m->embd.bytes = e.bytes;
+        break;
+      case IK_OUT_NORM: m->out_norm = fp; break;
+      case IK_ATTN_NORM: m->layers[e.layer].attn_norm = fp; break;
+      case IK_FFN_NORM: m->layers[e.layer].ffn_norm = fp; break;
+      case IK_OUTPUT: st = set_mat(e, &m->output); break;
+      case IK_QKV: {
+        LayerW& L = m->layers[e.layer];
+        st = set_mat(e, &L.qkv[e.index]);
+        L.qkv_base[e.index] = e.qkv_base;
+        L.n_qkv = (int)e.index + 1;
+        break;
+      }
+      case IK_O: st = set_mat(e, &m->layers[e.layer].o); break;
+      case IK_GATEUP: st = set_mat(e, &m->layers[e.layer].gateup); break;
+      case IK_DOWN: st = set_mat(e, &m->layers[e.layer].down); break;
+      default: break;
+    }
+    if (st) return st;
+  }
+  m->device_bytes = used;
+  m->finalized = true;
+  *out = guard.release();
   return FOXCUDA_OK;
 }
 
