@@ -1042,7 +1042,11 @@ static foxcuda_status keep_rows(RawTensor& r, uint64_t r0, uint64_t n) {
   const size_t rb = row_bytes(r.type, r.ne0);
   void* d = nullptr;
   CK(cudaMalloc(&d, n * rb), "shard alloc");
-  CK(cudaMemcpy(d, r.dev + r0 * rb, n * rb, cudaMemcpyDeviceToDevice), "shard rows");
+  const cudaError_t e = cudaMemcpy(d, r.dev + r0 * rb, n * rb, cudaMemcpyDeviceToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "shard rows");
+  }
   cudaFree(r.dev);
   r.dev = (uint8_t*)d; r.ne1 = n; r.bytes = n * rb;
   return FOXCUDA_OK;
@@ -1054,7 +1058,11 @@ static foxcuda_status keep_col_blocks(RawTensor& r, uint64_t b0, uint64_t nb) {
   const size_t off = row_bytes(r.type, 256) * b0;
   void* d = nullptr;
   CK(cudaMalloc(&d, r.ne1 * bb), "shard alloc");
-  CK(cudaMemcpy2D(d, bb, r.dev + off, rb, bb, r.ne1, cudaMemcpyDeviceToDevice), "shard columns");
+  const cudaError_t e = cudaMemcpy2D(d, bb, r.dev + off, rb, bb, r.ne1, cudaMemcpyDeviceToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return cuda_fail(e, "shard columns");
+  }
   cudaFree(r.dev);
   r.dev = (uint8_t*)d; r.ne0 = nb * 256; r.bytes = r.ne1 * bb;
   return FOXCUDA_OK;
@@ -1194,9 +1202,14 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
       void* cat = nullptr;
       CK(cudaMalloc(&cat, bytes), "staging alloc");
       size_t off = 0;
-      for (int k = i; k < j; ++k) {
-        cudaMemcpy((uint8_t*)cat + off, qkv[k]->dev, qkv[k]->bytes, cudaMemcpyDeviceToDevice);
+      cudaError_t e = cudaSuccess;
+      for (int k = i; k < j && e == cudaSuccess; ++k) {
+        e = cudaMemcpy((uint8_t*)cat + off, qkv[k]->dev, qkv[k]->bytes, cudaMemcpyDeviceToDevice);
         off += qkv[k]->bytes;
+      }
+      if (e != cudaSuccess) {
+        cudaFree(cat);
+        return cuda_fail(e, "q|k|v concatenation");
       }
       int su = slice_unit_for(m, qkv[i]->type, nrow, E, PRO_NORM);
       for (int k = i; k < j && su; ++k)
@@ -1237,8 +1250,14 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
       const size_t rb = row_bytes(g.type, E), half = (size_t)(U / 2) * rb;
       void* cat = nullptr;
       CK(cudaMalloc(&cat, g.bytes + u.bytes), "staging alloc");
-      CK(cudaMemcpy2D(cat, 2 * half, g.dev, half, half, Fd_l / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
-      CK(cudaMemcpy2D((uint8_t*)cat + half, 2 * half, u.dev, half, half, Fd_l / (U / 2), cudaMemcpyDeviceToDevice), "interleave");
+      cudaError_t e = cudaMemcpy2D(cat, 2 * half, g.dev, half, half, Fd_l / (U / 2), cudaMemcpyDeviceToDevice);
+      if (e == cudaSuccess)
+        e = cudaMemcpy2D((uint8_t*)cat + half, 2 * half, u.dev, half, half, Fd_l / (U / 2),
+                         cudaMemcpyDeviceToDevice);
+      if (e != cudaSuccess) {
+        cudaFree(cat);
+        return cuda_fail(e, "interleave");
+      }
       st = pack_into(m, g.type, cat, 2 * Fd_l, E, &L.gateup, U);
       L.gateup.src_type = g.src_type;
       if (!st && su) set_slice(m, &L.gateup, PRO_NORM);
