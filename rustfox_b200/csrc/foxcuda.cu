@@ -507,15 +507,35 @@ extern "C" foxcuda_status foxcuda_kernel_errors(void* stream) {
 // ---------------------------------------------------------------------------
 // M-token ternary GEMM on the tensor cores (tc.cuh)
 
-template <int NT>
-static cudaError_t launch_tc_t(const TcParams& p, cudaStream_t s) {
+template <int NT, int D>
+static cudaError_t launch_tc_td(const TcParams& p, cudaStream_t s) {
   const size_t smem = tc_smem_bytes(NT, p.nb);
   static size_t marks[kMaxDevices] = {};
-  cudaError_t e = opt_in_smem(tc_tq2_kernel<NT>, smem, marks);
+  cudaError_t e = opt_in_smem(tc_tq2_kernel<NT, D>, smem, marks);
   if (e != cudaSuccess) return e;
   const dim3 grid((unsigned)((p.n_rows + TC_ROWS - 1) / TC_ROWS), (unsigned)((p.n_tok + NT - 1) / NT));
-  tc_tq2_kernel<NT><<<grid, TC_THREADS, smem, s>>>(p);
+  tc_tq2_kernel<NT, D><<<grid, TC_THREADS, smem, s>>>(p);
   return cudaGetLastError();
+}
+
+// FOXCUDA_TC_DEPTH=2 or 4: K blocks in flight per thread of the ternary
+// tensor-core pass (default 1, the next block only).
+static int tc_depth() {
+  static const int d = [] {
+    const char* v = getenv("FOXCUDA_TC_DEPTH");
+    const int x = v ? atoi(v) : 1;
+    return x == 2 || x == 4 ? x : 1;
+  }();
+  return d;
+}
+
+template <int NT>
+static cudaError_t launch_tc_t(const TcParams& p, cudaStream_t s) {
+  switch (tc_depth()) {
+    case 2: return launch_tc_td<NT, 2>(p, s);
+    case 4: return launch_tc_td<NT, 4>(p, s);
+    default: return launch_tc_td<NT, 1>(p, s);
+  }
 }
 
 // The token tile is the smallest MMA N that holds all tokens, up to 64.

@@ -132,9 +132,13 @@ template <> struct TmemLd<32> {
 // (code | 0x80) - 1, then ^ 0x80: code - 1 in every byte, no borrow across bytes
 FOX_DEV uint32_t codes_to_i8(uint32_t c) { return ((c | 0x80808080u) - 0x01010101u) ^ 0x80808080u; }
 
-template <int NT>
+// DEPTH: K blocks whose weights and activations are in flight in registers
+// (1: the next block only). Deeper queues overlap more global-load round
+// trips with the MMAs and folds; the data, the MMAs and the fold are the same.
+template <int NT, int DEPTH = 1>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_tq2_kernel(const TcParams p) {
   static_assert(NT == 8 || NT == 16 || NT == 32 || NT == 64, "token tile");
+  static_assert(DEPTH == 1 || DEPTH == 2 || DEPTH == 4, "look-ahead");
   constexpr int HALF = NT / 2;                    // TMEM columns read per thread
   constexpr int BV = (NT * 16 + TC_THREADS - 1) / TC_THREADS;  // 16-byte activation pieces per thread
   constexpr uint32_t NCOLS = tc_tmem_cols(NT);
@@ -194,23 +198,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_tq2_kernel(const TcParams p)
       wrow[j] = p.w + base + count * 16 * plane[j] + (size_t)(r - u * U) * nb * 16;
     }
   }
-  uint4 ra[2], rb[BV];
-  auto load_block = [&](int b) {
+  // one K block's pieces of this thread: weights (two planes) and activations
+  struct Blk { uint4 ra[2], rb[BV]; };
+  auto load_block = [&](Blk& q, int b) {
     // rows past the matrix get code 1 (weight 0) at every level: 0b01010101
 #pragma unroll
     for (int j = 0; j < 2; ++j)
-      ra[j] = wrow[j] ? __ldg(reinterpret_cast<const uint4*>(wrow[j] + (size_t)b * 16))
-                      : make_uint4(0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u);
+      q.ra[j] = wrow[j] ? __ldg(reinterpret_cast<const uint4*>(wrow[j] + (size_t)b * 16))
+                        : make_uint4(0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u);
 #pragma unroll
     for (int j = 0; j < BV; ++j) {
       const int i = tid + j * TC_THREADS;
       const int n = i % NT, c = i / NT;  // token fastest: conflict-free 16-byte stores
-      rb[j] = make_uint4(0, 0, 0, 0);
+      q.rb[j] = make_uint4(0, 0, 0, 0);
       if (i < NT * 16 && T0 + n < p.n_tok)
-        rb[j] = __ldg(reinterpret_cast<const uint4*>(p.xq + (size_t)(T0 + n) * p.K + (size_t)b * 256 + c * 16));
+        q.rb[j] = __ldg(reinterpret_cast<const uint4*>(p.xq + (size_t)(T0 + n) * p.K + (size_t)b * 256 + c * 16));
     }
   };
-  auto store_block = [&](int buf) {
+  auto store_block = [&](const Blk& q, int buf) {
+    const uint4(&ra)[2] = q.ra;
+    const uint4(&rb)[BV] = q.rb;
     uint8_t* a = sA + buf * tc_a_bytes();
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -258,10 +265,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_tq2_kernel(const TcParams p)
     return true;
   };
 
-  load_block(0);
+  // queue[i] holds block b + i at the top of iteration b
+  Blk queue[DEPTH];
+#pragma unroll
+  for (int i = 0; i < DEPTH; ++i)
+    if (i < nb) load_block(queue[i], i);
   for (int b = 0; b < nb && ok; ++b) {
     const int buf = b & 1;
-    store_block(buf);
+    store_block(queue[0], buf);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -276,7 +287,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_tq2_kernel(const TcParams p)
       mma_commit(&bars[buf]);
     }
     last = b;
-    if (b + 1 < nb) load_block(b + 1);
+#pragma unroll
+    for (int i = 0; i + 1 < DEPTH; ++i) queue[i] = queue[i + 1];
+    if (b + DEPTH < nb) load_block(queue[DEPTH - 1], b + DEPTH);
     if (b >= 1) ok = fold(b - 1);
   }
   if (ok) ok = fold(nb - 1);
