@@ -130,6 +130,18 @@ def test_ctypes_prototypes_match_the_header():
                 assert a in (ctypes.c_void_p, ctypes.c_char_p) or hasattr(a, "_type_"), f"{name}: {p}"
 
 
+def test_every_called_entry_point_has_a_prototype():
+    """A call without argtypes would pass 64-bit pointers and sizes through
+    ctypes' default int conversion: every foxcuda_* the package, the bench
+    or the tests call is in the prototype table."""
+    from rustfox_b200 import api
+    used = set()
+    files = glob.glob(os.path.join(ROOT, "rustfox_b200", "*.py")) + glob.glob(os.path.join(ROOT, "tests", "*.py"))
+    for f in files + [os.path.join(ROOT, "bench.py"), os.path.join(ROOT, "__graft_entry__.py")]:
+        used |= set(re.findall(r"\.(foxcuda_\w+)\s*\(", open(f).read()))
+    assert used and not used - set(api._PROTOS), sorted(used - set(api._PROTOS))
+
+
 def test_python_api_mirrors_upstream_names():
     import rustfox_b200 as rf
     for name in ("gemv", "gemv_tq1_i8", "gemv_tq2_i8", "quantize_activations_i8", "dequant_row",
