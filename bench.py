@@ -414,9 +414,9 @@ def run_tp(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=10))
     cfg = synth.CONFIGS[args.config]
-    host = synth.generate(cfg)
-    model = rf.Model.from_synthetic(host, device=local, tp_rank=rank, tp_size=world)
-    del host
+    # weights generated on the device: the 27B shape is 9 GB per rank, minutes
+    # of host-side generation while every GPU of the run is held
+    model = rf.Model.from_synthetic_device(cfg, device=local, tp_rank=rank, tp_size=world)
     n_ctx = args.prompt + args.warmup + args.steps + 8
     ctx = TPContext(model, n_ctx, kv="f16", exchange=args.exchange)
     prompt = synth.random_prompt(cfg, args.prompt, seed=1)
@@ -438,16 +438,17 @@ def run_tp(args):
             "metric": METRIC, "value": args.steps / dt, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "i8 x ternary -> i32, f32", "data": "synthetic (seeded random-init weights)",
+            "dtype": "i8 x ternary -> i32, f32",
+            "data": "synthetic (seeded random-init weights generated on the device)",
             "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} greedy decode, one "
                                    f"sequence over {world} GPU(s)", "prompt": args.prompt,
                        "kv_cache": "f16", "parallelism": f"tp{world}",
                        "collectives": (
                            "torch.distributed NCCL per row-parallel GEMV (4 per layer), the whole "
                            "step replayed as one CUDA graph" if args.exchange == "nccl" else
-                           "the library's exchanges over peer memory (CUDA IPC, 4 kernels per "
-                           "row-parallel GEMV, no host collective), the whole step replayed as one "
-                           "CUDA graph")}}),
+                           "the library's exchanges over peer memory (CUDA IPC; per row-parallel "
+                           "GEMV the terms GEMV with both exchanges inside and a fold, no host "
+                           "collective), the whole step replayed as one CUDA graph")}}),
               flush=True)
     if world > 1:
         dist.barrier()  # no rank unmaps a peer arena another may still read
@@ -620,10 +621,8 @@ def run_batch(args):
     from rustfox_b200 import synth
     cfg = synth.CONFIGS[args.config]
     torch.cuda.set_device(0)
-    host = synth.generate(cfg)
     wb = cfg.weight_bytes()
-    model = rf.Model.from_synthetic(host)
-    del host
+    model = rf.Model.from_synthetic_device(cfg)  # no CPU baseline here: no host copy needed
     n, warm = args.batch, max(3, args.warmup)
     n_ctx = args.ctx + warm + args.steps + 8
     ctxs = [rf.Context(model, n_ctx, kv="f16") for _ in range(n)]
@@ -651,7 +650,8 @@ def run_batch(args):
         "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": warm,
         "ms_per_step": 1e3 * secs / args.steps, "higher_is_better": True, "scaling": None,
         "vs_baseline": None, "dtype": "i8 x ternary -> i32 (tcgen05 kind::i8), f32",
-        "data": "synthetic (seeded random-init weights; seeded N(0,1) fp16 K/V in place of prompts)",
+        "data": "synthetic (seeded random-init weights generated on the device; seeded N(0,1) fp16 "
+                "K/V in place of prompts)",
         "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd}, {n} sequences at position "
                                f"{args.ctx}, top-k 40 T 0.8", "batch": n, "ctx": args.ctx,
                    "kv_cache": "f16", "l2": f"{step_bytes / 1e9:.1f} GB per step > 126 MB L2"},

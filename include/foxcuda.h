@@ -205,6 +205,15 @@ foxcuda_status foxcuda_model_create(const foxcuda_model_info *info, int device,
 foxcuda_status foxcuda_model_upload(foxcuda_model *m, int role, uint32_t layer,
                                     int ggml_type, uint64_t ne0, uint64_t ne1,
                                     const void *host_data, size_t bytes);
+/* No upstream counterpart (benchmark fixtures): foxcuda_model_upload with
+ * the tensor generated on the device from (seed, sigma), for synthetic
+ * models too large to generate on the host quickly. Every byte is a fixed
+ * function of (seed, block, field): uniform ternary codes (TQ2_0) or uniform
+ * bytes (Q4_K, Q6_K) with fp16 block scales |N(0, sigma)|, or Q8_0 of
+ * N(0, sigma) values. Other types answer FOXCUDA_ERR_UNSUPPORTED. */
+foxcuda_status foxcuda_model_upload_synthetic(foxcuda_model *m, int role, uint32_t layer,
+                                              int ggml_type, uint64_t ne0, uint64_t ne1,
+                                              uint64_t seed, float sigma);
 foxcuda_status foxcuda_model_finalize(foxcuda_model *m);
 void           foxcuda_model_destroy(foxcuda_model *m);
 uint64_t       foxcuda_model_device_bytes(const foxcuda_model *m);

@@ -83,6 +83,8 @@ _PROTOS = {
     "foxcuda_model_create": (_st, [C.POINTER(ModelInfo), C.c_int, C.POINTER(_vp)]),
     "foxcuda_model_upload": (_st, [_vp, C.c_int, C.c_uint32, C.c_int, C.c_uint64, C.c_uint64,
                                    _vp, _sz]),
+    "foxcuda_model_upload_synthetic": (_st, [_vp, C.c_int, C.c_uint32, C.c_int, C.c_uint64, C.c_uint64,
+                                             C.c_uint64, C.c_float]),
     "foxcuda_model_finalize": (_st, [_vp]),
     "foxcuda_model_destroy": (None, [_vp]),
     "foxcuda_model_device_bytes": (C.c_uint64, [_vp]),
@@ -349,6 +351,42 @@ class Model:
                     rope_freq_base=c.rope_base)
         return cls(info, ((n, tt, ne, d) for n, (tt, ne, d) in model.tensors.items()), device,
                    tp_rank, tp_size)
+
+    @classmethod
+    def from_synthetic_device(cls, cfg, device: int = 0, tp_rank: int = 0, tp_size: int = 1) -> "Model":
+        """A synthetic model of config `cfg` (rustfox_b200.synth) whose weights
+        are generated on the device (foxcuda_model_upload_synthetic): the same
+        shapes, types and distributions as synth.generate, another stream of
+        values, and no host-side generation. For benchmark shapes too large
+        to generate on the host (the 27B config)."""
+        from . import synth
+        info = dict(n_layer=cfg.n_layer, n_embd=cfg.n_embd, n_head=cfg.n_head, n_head_kv=cfg.n_head_kv,
+                    n_ff=cfg.n_ff, head_dim=cfg.head_dim, n_vocab=cfg.n_vocab, rms_eps=cfg.rms_eps,
+                    rope_freq_base=cfg.rope_base)
+        self = cls.__new__(cls)
+        self.info, self.device, self.tp_rank, self.tp_size = dict(info), device, tp_rank, tp_size
+        mi = ModelInfo(*(int(info[k]) for k in ("n_layer", "n_embd", "n_head", "n_head_kv", "n_ff",
+                                                "head_dim", "n_vocab")),
+                       float(info["rms_eps"]), float(info["rope_freq_base"]))
+        h = C.c_void_p()
+        _check(lib().foxcuda_model_create_tp(C.byref(mi), device, tp_rank, tp_size, C.byref(h)))
+        self.h = h
+        ones = np.ones(cfg.n_embd, dtype=np.float32)
+        try:
+            for i, (name, tt, ne, sigma) in enumerate(synth.tensor_specs(cfg)):
+                role, layer = _role_of(name)
+                ne1 = ne[1] if len(ne) > 1 else 1
+                if tt == F.F32:
+                    _check(lib().foxcuda_model_upload(self.h, role, layer, tt, ne[0], ne1,
+                                                      ones.ctypes.data_as(C.c_void_p), ones.nbytes))
+                else:
+                    _check(lib().foxcuda_model_upload_synthetic(self.h, role, layer, tt, ne[0], ne1,
+                                                                synth.device_seed(cfg.seed, i), sigma))
+            _check(lib().foxcuda_model_finalize(self.h))
+        except Exception:
+            self.close()
+            raise
+        return self
 
     @classmethod
     def from_gguf(cls, path: str, device: int = 0) -> "Model":

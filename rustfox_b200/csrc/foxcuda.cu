@@ -23,6 +23,7 @@
 #include "tc_kquant.cuh"
 #include "prefill.cuh"
 #include "p2p.cuh"
+#include "synthgen.cuh"
 
 using namespace fox;
 
@@ -1022,6 +1023,38 @@ extern "C" foxcuda_status foxcuda_model_upload(foxcuda_model* m, int role, uint3
   CK(cudaMalloc(&r.dev, bytes), "upload alloc");
   r.type = type; r.ne0 = ne0; r.ne1 = ne1; r.bytes = bytes;
   CK(cudaMemcpy(r.dev, host, bytes, cudaMemcpyHostToDevice), "upload copy");
+  return FOXCUDA_OK;
+}
+
+// foxcuda_model_upload with the tensor's bytes generated on the device
+// (synthgen.cuh) from (seed, sigma) instead of copied from the host.
+extern "C" foxcuda_status foxcuda_model_upload_synthetic(foxcuda_model* m, int role, uint32_t layer, int type,
+                                                         uint64_t ne0, uint64_t ne1, uint64_t seed,
+                                                         float sigma) {
+  if (!m) return fail(FOXCUDA_ERR_ARG, "upload_synthetic: null model");
+  if (m->finalized) return fail(FOXCUDA_ERR_ARG, "upload_synthetic: model already finalized");
+  if (role < 0 || role >= FOXCUDA_N_ROLES) return fail(FOXCUDA_ERR_ARG, "upload_synthetic: bad role %d", role);
+  if (role_per_layer(role) ? layer >= m->info.n_layer : layer != 0)
+    return fail(FOXCUDA_ERR_ARG, "upload_synthetic: bad layer %u for role %d", layer, role);
+  if (type != T_TQ2_0 && type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "upload_synthetic: no generator for ggml type %d (TQ2_0, Q8_0, Q4_K, "
+                "Q6_K)", type);
+  if (!(sigma > 0.0f)) return fail(FOXCUDA_ERR_ARG, "upload_synthetic: sigma %g", sigma);
+  if (ne1 == 0) ne1 = 1;
+  const size_t rb = row_bytes(type, ne0);
+  if (rb == 0) return fail(FOXCUDA_ERR_ARG, "upload_synthetic: %llu columns of type %d", (unsigned long long)ne0, type);
+  const size_t bytes = rb * ne1;
+  cudaSetDevice(m->device);
+  RawTensor& r = m->slot(role, layer);
+  if (r.dev) cudaFree(r.dev);
+  r = RawTensor();
+  CK(cudaMalloc(&r.dev, bytes), "upload alloc");
+  r.type = type; r.ne0 = ne0; r.ne1 = ne1; r.bytes = bytes;
+  const long n_blocks = (long)(bytes / block_bytes(type));
+  const unsigned grid = (unsigned)std::max<long>(1, std::min<long>((n_blocks + 255) / 256, 32 * sm_count(m->device)));
+  synth_fill_kernel<<<grid, 256>>>(type, r.dev, n_blocks, block_bytes(type), seed, (double)sigma);
+  CK(cudaGetLastError(), "synthetic fill");
+  CK(cudaDeviceSynchronize(), "synthetic fill");
   return FOXCUDA_OK;
 }
 

@@ -121,34 +121,39 @@ def _weights(rng, ggml_type, ne0, ne1, sigma):
     return F.random_blocks(rng, ggml_type, ne1, ne0, sigma)
 
 
+def tensor_specs(cfg: ModelConfig):
+    """(name, ggml_type, ne, sigma) of every tensor in GGUF order; F32 tensors
+    are the norm weights (all ones, sigma 0)."""
+    e = cfg.n_embd
+    yield "token_embd.weight", cfg.embd_type, (e, cfg.n_vocab), cfg.embd_sigma
+    yield "output_norm.weight", F.F32, (e,), 0.0
+    yield ("output.weight", cfg.output_type, (e, cfg.n_vocab),
+           cfg.embd_sigma if cfg.output_type == F.Q8_0 else 0.01)
+    types, shapes = cfg.linear_types(), cfg.shapes()
+    for l in range(cfg.n_layer):
+        yield f"blk.{l}.attn_norm.weight", F.F32, (e,), 0.0
+        for k in ("attn_q", "attn_k", "attn_v", "attn_output"):
+            yield (f"blk.{l}.{k}.weight", types[k], shapes[k],
+                   cfg.linear_sigma if types[k] == cfg.linear_type else 0.01)
+        yield f"blk.{l}.ffn_norm.weight", F.F32, (e,), 0.0
+        for k in ("ffn_gate", "ffn_up", "ffn_down"):
+            yield f"blk.{l}.{k}.weight", types[k], shapes[k], cfg.linear_sigma
+
+
 def generate(cfg: ModelConfig) -> SyntheticModel:
     """Deterministic in cfg (including cfg.seed)."""
     rng = np.random.Generator(np.random.PCG64(cfg.seed))
     m = SyntheticModel(cfg)
-    e = cfg.n_embd
-    ones = np.ones(e, dtype=np.float32)
-    m.tensors["token_embd.weight"] = (cfg.embd_type, (e, cfg.n_vocab),
-                                      _weights(rng, cfg.embd_type, e, cfg.n_vocab, cfg.embd_sigma))
-    m.tensors["output_norm.weight"] = (F.F32, (e,), ones)
-    m.tensors["output.weight"] = (cfg.output_type, (e, cfg.n_vocab),
-                                  _weights(rng, cfg.output_type, e, cfg.n_vocab,
-                                           cfg.embd_sigma if cfg.output_type == F.Q8_0
-                                           else 0.01))
-    types, shapes = cfg.linear_types(), cfg.shapes()
-    for l in range(cfg.n_layer):
-        m.tensors[f"blk.{l}.attn_norm.weight"] = (F.F32, (e,), ones)
-        for k in ("attn_q", "attn_k", "attn_v", "attn_output"):
-            ne0, ne1 = shapes[k]
-            sig = cfg.linear_sigma if types[k] == cfg.linear_type else 0.01
-            m.tensors[f"blk.{l}.{k}.weight"] = (types[k], (ne0, ne1),
-                                                _weights(rng, types[k], ne0, ne1, sig))
-        m.tensors[f"blk.{l}.ffn_norm.weight"] = (F.F32, (e,), ones)
-        for k in ("ffn_gate", "ffn_up", "ffn_down"):
-            ne0, ne1 = shapes[k]
-            m.tensors[f"blk.{l}.{k}.weight"] = (types[k], (ne0, ne1),
-                                                _weights(rng, types[k], ne0, ne1,
-                                                         cfg.linear_sigma))
+    ones = np.ones(cfg.n_embd, dtype=np.float32)
+    for name, tt, ne, sigma in tensor_specs(cfg):
+        m.tensors[name] = (tt, ne, ones if tt == F.F32 else _weights(rng, tt, ne[0], ne[1], sigma))
     return m
+
+
+def device_seed(cfg_seed: int, index: int) -> int:
+    """The seed of tensor `index` (GGUF order) of a model generated on the
+    device (foxcuda_model_upload_synthetic)."""
+    return (((cfg_seed + 1) * 0x9E3779B97F4A7C15) ^ ((index + 1) * 0xD1B54A32D192ED03)) & (2**64 - 1)
 
 
 def byte_vocab(n_vocab: int) -> list:
