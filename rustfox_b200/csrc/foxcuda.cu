@@ -637,15 +637,25 @@ extern "C" foxcuda_status foxcuda_gemm_tq2_i8_split(const int8_t* q, const float
   return FOXCUDA_OK;
 }
 
-template <int T, int NT>
-static cudaError_t launch_kq_t(const TcKParams& p, cudaStream_t s) {
+template <int T, int NT, int D>
+static cudaError_t launch_kq_td(const TcKParams& p, cudaStream_t s) {
   const size_t smem = 2 * (size_t)tck_buf_bytes<T>(NT);
   static size_t marks[kMaxDevices] = {};
-  cudaError_t e = opt_in_smem(tc_kq_kernel<T, NT>, smem, marks);
+  cudaError_t e = opt_in_smem(tc_kq_kernel<T, NT, D>, smem, marks);
   if (e != cudaSuccess) return e;
   const dim3 grid((unsigned)((p.n_rows + TC_ROWS - 1) / TC_ROWS), (unsigned)((p.n_tok + NT - 1) / NT));
-  tc_kq_kernel<T, NT><<<grid, TC_THREADS, smem, s>>>(p);
+  tc_kq_kernel<T, NT, D><<<grid, TC_THREADS, smem, s>>>(p);
   return cudaGetLastError();
+}
+
+// the K-block look-ahead of FOXCUDA_TC_DEPTH, as for the ternary pass
+template <int T, int NT>
+static cudaError_t launch_kq_t(const TcKParams& p, cudaStream_t s) {
+  switch (tc_depth()) {
+    case 2: return launch_kq_td<T, NT, 2>(p, s);
+    case 4: return launch_kq_td<T, NT, 4>(p, s);
+    default: return launch_kq_td<T, NT, 1>(p, s);
+  }
 }
 
 // Token tiles: Q4_K up to 16 tokens (8 accumulators per block), Q6_K 8 (16).

@@ -64,10 +64,12 @@ __host__ __device__ constexpr int tck_buf_bytes(int NT) {
   return tc_a_bytes() + KqTraits<T>::NBV * tc_b_bytes(NT) + TC_ROWS * KqTraits<T>::RS + NT * 16 * 4 + NT * 4;
 }
 
-template <int T, int NT>
+// DEPTH: K blocks in flight per thread in registers, as in tc_tq2_kernel.
+template <int T, int NT, int DEPTH = 1>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_kq_kernel(const TcKParams p) {
   using K = KqTraits<T>;
   static_assert(NT == 8 || NT == 16, "token tile");
+  static_assert(DEPTH == 1 || DEPTH == 2 || DEPTH == 4, "look-ahead");
   constexpr int HALF = NT / 2;
   constexpr int BV = (NT * 16 + TC_THREADS - 1) / TC_THREADS;
   constexpr uint32_t NCOLS = tck_tmem_cols<T>(NT);
@@ -114,11 +116,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_kq_kernel(const TcKParams p)
   // Q6_K: 2 (row, half, sub) triples (two ql planes and one qh plane) + the
   //       row's scales (threads 0..127) and d (threads 128..255).
   constexpr int NA = T == T_Q4_K ? 4 : 6;
-  uint4 ra[NA];
-  uint32_t rs[4];
-  uint4 rb[BV];
-  float ras = 0.0f;
-  auto load_block = [&](int b) {
+  struct Blk { uint4 ra[NA]; uint32_t rs[4]; uint4 rb[BV]; float ras; };
+  auto load_block = [&](Blk& q, int b) {
+    uint4(&ra)[NA] = q.ra;
+    uint32_t(&rs)[4] = q.rs;
+    uint4(&rb)[BV] = q.rb;
+    float& ras = q.ras;
     if (T == T_Q4_K) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -181,7 +184,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_kq_kernel(const TcKParams p)
     if (tid < NT && T0 + tid < p.n_tok) ras = __ldg(p.xs + (size_t)(T0 + tid) * nb + b);
   };
 
-  auto store_block = [&](int buf) {
+  auto store_block = [&](const Blk& q, int buf) {
+    const uint4(&ra)[NA] = q.ra;
+    const uint32_t(&rs)[4] = q.rs;
+    const uint4(&rb)[BV] = q.rb;
+    const float ras = q.ras;
     uint8_t* sb = smem + buf * BUF;
     uint8_t* a = sb;
     if (T == T_Q4_K) {
@@ -326,10 +333,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_kq_kernel(const TcKParams p)
     return true;
   };
 
-  load_block(0);
+  // queue[i] holds block b + i at the top of iteration b
+  Blk queue[DEPTH];
+#pragma unroll
+  for (int i = 0; i < DEPTH; ++i)
+    if (i < nb) load_block(queue[i], i);
   for (int b = 0; b < nb && ok; ++b) {
     const int buf = b & 1;
-    store_block(buf);
+    store_block(queue[0], buf);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -353,7 +364,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_kq_kernel(const TcKParams p)
       mma_commit(&bars[buf]);
     }
     last = b;
-    if (b + 1 < nb) load_block(b + 1);
+#pragma unroll
+    for (int i = 0; i + 1 < DEPTH; ++i) queue[i] = queue[i + 1];
+    if (b + DEPTH < nb) load_block(queue[DEPTH - 1], b + DEPTH);
     if (b >= 1) ok = fold(b - 1);
   }
   if (ok) ok = fold(nb - 1);
