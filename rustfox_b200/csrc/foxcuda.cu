@@ -1792,6 +1792,7 @@ struct foxcuda_sampler {
   int k = 0;
   SamplerDev* dev = nullptr;
   cudaGraphExec_t g_decode = nullptr;
+  cudaGraphExec_t g_decode_io = nullptr;  // g_decode with the token copies inside
   uint32_t n_out = 0;  // host mirror of dev->n_out
 };
 
@@ -2274,6 +2275,37 @@ static cudaError_t capture(foxcuda_context* c, cudaGraphExec_t* out, bool head, 
   e = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   return e;
+}
+
+// The decode step of foxcuda_decode with its copies inside the graph: the
+// token in from the context's pinned word, then the pick and the device
+// error word out in one 8-byte copy. A step is then one launch and one
+// synchronisation.
+static cudaError_t capture_io(foxcuda_context* c, foxcuda_sampler* sm, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal);
+  if (e) return e;
+  e = cudaMemcpyAsync(c->token_dev, c->h_pinned, 4, cudaMemcpyHostToDevice, c->stream);
+  if (!e) e = enqueue_body(c, false);
+  if (!e) e = enqueue_head(c);
+  if (!e) e = enqueue_pick(sm, true);
+  if (!e) e = cudaMemcpyAsync(c->h_pinned + 1, c->token_dev, 8, cudaMemcpyDeviceToHost, c->stream);
+  cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+  if (e) { if (g) cudaGraphDestroy(g); return e; }
+  if (e2) return e2;
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  return e;
+}
+
+// FOXCUDA_DECODE_IO_GRAPH=1: foxcuda_decode runs capture_io's graph (the
+// token copies inside it). Off by default.
+static bool decode_io_graph() {
+  static const bool on = [] {
+    const char* v = getenv("FOXCUDA_DECODE_IO_GRAPH");
+    return v && v[0] == '1';
+  }();
+  return on;
 }
 
 extern "C" foxcuda_status foxcuda_context_set_trace(foxcuda_context* c, int on) {
@@ -3082,6 +3114,7 @@ extern "C" void foxcuda_sampler_destroy(foxcuda_sampler* s) {
   cudaSetDevice(s->c->m->device);
   cudaStreamSynchronize(s->c->stream);
   if (s->g_decode) cudaGraphExecDestroy(s->g_decode);
+  if (s->g_decode_io) cudaGraphExecDestroy(s->g_decode_io);
   cudaFree(s->dev);
   delete s;
 }
@@ -3114,6 +3147,22 @@ static foxcuda_status decode_steps(foxcuda_context* c, foxcuda_sampler* s, uint3
     return fail(FOXCUDA_ERR_ARG, "forward: %zu tokens past position %u would overrun the %u token context",
                 n, c->pos, c->n_ctx);
   cudaSetDevice(c->m->device);
+  if (n == 1 && decode_io_graph()) {
+    if (!s->g_decode_io) CK(capture_io(c, s, &s->g_decode_io), "capture");
+    c->h_pinned[0] = token;  // the previous step has synchronised: no copy still reads it
+    CK(cudaEventRecord(c->ev0, c->stream), "event");
+    CK(cudaGraphLaunch(s->g_decode_io, c->stream), "graph launch");
+    CK(cudaEventRecord(c->ev1, c->stream), "event");
+    s->n_out += 1;
+    CK(cudaStreamSynchronize(c->stream), "decode");
+    out[0] = c->h_pinned[1];
+    c->h_pinned[3] = c->h_pinned[2];
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    c->last_seconds = ms / 1e3;
+    c->pos += 1;
+    return check_err(c);
+  }
   if (!s->g_decode) CK(capture(c, &s->g_decode, true, s), "capture");
   c->h_pinned[0] = token;
   CK(cudaMemcpyAsync(c->token_dev, c->h_pinned, 4, cudaMemcpyHostToDevice, c->stream), "token in");
