@@ -171,22 +171,24 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
   double* red = reinterpret_cast<double*>(smem + g.red_off);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + g.bar_off);  // [0] weights, [1] norm
 
-  // 1. everything constant comes in before the wait: the CTA's run of units
-  //    (contiguous in the packed matrix) and the norm weights
+  // 1. everything constant comes in before the wait: the norm weights first
+  //    (the prologue needs them before any weight, and issued after the
+  //    ~100 KB run they would land last), then the CTA's run of units
+  //    (contiguous in the packed matrix)
   if (tid == 0) {
     mbar_init(bar, 1);
     mbar_init(bar + 1, 1);
     mbar_fence_init();
+    if (PRO == PRO_NORM) {
+      mbar_arrive_expect_tx(bar + 1, (unsigned)(K * 4));
+      bulk_g2s(nw, p.norm_w, (unsigned)(K * 4), bar + 1);
+    }
     if (nu > 0) {
       const size_t total = (size_t)nu * g.unit_bytes;
       mbar_arrive_expect_tx(bar, (unsigned)total);
       const uint8_t* src = p.w + (size_t)u0 * g.unit_bytes;
       for (size_t o = 0; o < total; o += 32768)
         bulk_g2s(sw + o, src + o, (unsigned)std::min<size_t>(32768, total - o), bar);
-    }
-    if (PRO == PRO_NORM) {
-      mbar_arrive_expect_tx(bar + 1, (unsigned)(K * 4));
-      bulk_g2s(nw, p.norm_w, (unsigned)(K * 4), bar + 1);
     }
   }
   griddep_launch_dependents();
