@@ -3560,10 +3560,14 @@ static bool p2p_fused() {
 // The terms GEMV with both exchanges inside (gemv.cuh PRO_XAMAX, EPI_TERMS
 // with the readiness count): ternary shards trade the absmax in the
 // prologue; K-quant shards quantise with their own 256-block scales.
+// With programmatic launch (FOXCUDA_TP_PDL=1) it takes the ring form, whose
+// weight copies start before griddepcontrol.wait, so the shard's o or down
+// weights stream while the attention or gate|up kernel still runs.
 template <int T>
 static cudaError_t launch_xterms_t(const GemvParams& p, cudaStream_t s) {
-  if constexpr (T == T_TQ1_0 || T == T_TQ2_0) return launch_gemv_t<T, PRO_XAMAX, EPI_TERMS>(p, s);
-  else return launch_gemv_t<T, PRO_VEC, EPI_TERMS>(p, s);
+  constexpr int PRO = (T == T_TQ1_0 || T == T_TQ2_0) ? PRO_XAMAX : PRO_VEC;
+  if (p.pdl) return launch_ring_t<T, PRO, EPI_TERMS>(p, s);
+  return launch_gemv_t<T, PRO, EPI_TERMS>(p, s);
 }
 
 static cudaError_t launch_xterms(const foxcuda_context* c, const PackedMat& W, int which, int phase, float* amax,
@@ -3581,6 +3585,7 @@ static cudaError_t launch_xterms(const foxcuda_context* c, const PackedMat& W, i
   p.x_phase = phase;
   p.x_count = c->x_count + which;
   p.x_amax = amax;
+  p.pdl = ctx_pdl(c) ? 1 : 0;
   switch (W.type) {
     case T_TQ1_0: return launch_xterms_t<T_TQ1_0>(p, c->stream);
     case T_TQ2_0: return launch_xterms_t<T_TQ2_0>(p, c->stream);
