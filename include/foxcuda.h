@@ -208,9 +208,9 @@ foxcuda_status foxcuda_model_upload(foxcuda_model *m, int role, uint32_t layer,
 /* No upstream counterpart (benchmark fixtures): foxcuda_model_upload with
  * the tensor generated on the device from (seed, sigma), for synthetic
  * models too large to generate on the host quickly. Every byte is a fixed
- * function of (seed, block, field): uniform ternary codes (TQ2_0) or uniform
- * bytes (Q4_K, Q6_K) with fp16 block scales |N(0, sigma)|, or Q8_0 of
- * N(0, sigma) values. Other types answer FOXCUDA_ERR_UNSUPPORTED. */
+ * function of (seed, block, field): uniform ternary weights (TQ1_0, TQ2_0)
+ * or uniform bytes (Q4_K, Q6_K) with fp16 block scales |N(0, sigma)|, or
+ * Q8_0 of N(0, sigma) values. Other types answer FOXCUDA_ERR_UNSUPPORTED. */
 foxcuda_status foxcuda_model_upload_synthetic(foxcuda_model *m, int role, uint32_t layer,
                                               int ggml_type, uint64_t ne0, uint64_t ne1,
                                               uint64_t seed, float sigma);

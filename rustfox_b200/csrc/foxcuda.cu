@@ -1046,9 +1046,9 @@ extern "C" foxcuda_status foxcuda_model_upload_synthetic(foxcuda_model* m, int r
   if (role < 0 || role >= FOXCUDA_N_ROLES) return fail(FOXCUDA_ERR_ARG, "upload_synthetic: bad role %d", role);
   if (role_per_layer(role) ? layer >= m->info.n_layer : layer != 0)
     return fail(FOXCUDA_ERR_ARG, "upload_synthetic: bad layer %u for role %d", layer, role);
-  if (type != T_TQ2_0 && type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K)
-    return fail(FOXCUDA_ERR_UNSUPPORTED, "upload_synthetic: no generator for ggml type %d (TQ2_0, Q8_0, Q4_K, "
-                "Q6_K)", type);
+  if (type != T_TQ1_0 && type != T_TQ2_0 && type != T_Q8_0 && type != T_Q4_K && type != T_Q6_K)
+    return fail(FOXCUDA_ERR_UNSUPPORTED, "upload_synthetic: no generator for ggml type %d (TQ1_0, TQ2_0, Q8_0, "
+                "Q4_K, Q6_K)", type);
   if (!(sigma > 0.0f)) return fail(FOXCUDA_ERR_ARG, "upload_synthetic: sigma %g", sigma);
   if (ne1 == 0) ne1 = 1;
   const size_t rb = row_bytes(type, ne0);

@@ -3,10 +3,10 @@
 //
 // Every byte is a pure function of (seed, block, field) through a splitmix64
 // finalizer, so the result does not depend on the launch shape. The
-// distributions are the synthetic configs' (uniform ternary codes with fp16
-// block scales |N(0, sigma)|; Q8_0 of N(0, sigma) values; uniform K-quant
-// bytes with fp16 scales |N(0, sigma)|); normals come from Box-Muller in
-// double. The tests hold a numpy restatement of the same formulas.
+// distributions are the synthetic configs': uniform ternary weights (TQ1_0,
+// TQ2_0) and uniform K-quant bytes with fp16 block scales |N(0, sigma)|, and
+// Q8_0 of N(0, sigma) values. Normals come from Box-Muller in double. The
+// tests hold a numpy restatement of the same formulas.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -16,7 +16,10 @@
 namespace fox {
 
 // counter stride per block (indices of one block never overlap the next)
-constexpr uint64_t SG_TQ2 = 80, SG_Q8 = 48, SG_Q4K = 160, SG_Q6K = 224;
+constexpr uint64_t SG_TQ1 = 64, SG_TQ2 = 80, SG_Q8 = 48, SG_Q4K = 160, SG_Q6K = 224;
+
+// a uniform integer in [0, n) from the high half of a hash
+FOX_DEV uint32_t sg_below(uint64_t h, uint32_t n) { return (uint32_t)(((h >> 32) * n) >> 32); }
 
 FOX_DEV uint64_t sg_mix(uint64_t seed, uint64_t i) {
   uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
@@ -45,14 +48,22 @@ FOX_DEV void sg_put16(uint8_t* p, uint16_t v) {
   p[1] = (uint8_t)(v >> 8);
 }
 
-// one block of `type` (TQ2_0, Q8_0, Q4_K, Q6_K) at o, block index b
+// one block of `type` (TQ1_0, TQ2_0, Q8_0, Q4_K, Q6_K) at o, block index b
 FOX_DEV void sg_block(int type, uint8_t* o, uint64_t b, uint64_t seed, double sigma) {
   double z0, z1;
-  if (type == T_TQ2_0) {
+  if (type == T_TQ1_0) {
+    // five uniform trits per qs byte (a uniform value in [0, 243)), four per
+    // qh byte ([0, 81)), in the TQ1_0 byte encoding ceil(v * 256 / 3^k)
+    const uint64_t base = b * SG_TQ1;
+    for (int j = 0; j < 48; ++j) o[j] = (uint8_t)((sg_below(sg_mix(seed, base + j), 243) * 256u + 242u) / 243u);
+    for (int j = 48; j < 52; ++j) o[j] = (uint8_t)((sg_below(sg_mix(seed, base + j), 81) * 256u + 80u) / 81u);
+    sg_normal2(seed, base + 52, z0, z1);
+    sg_put16(o + 52, sg_half_abs(z0, sigma));
+  } else if (type == T_TQ2_0) {
     const uint64_t base = b * SG_TQ2;
     for (int j = 0; j < 64; ++j) {
       // a uniform choice among the 81 bytes of four codes in {0, 1, 2}
-      const uint32_t c = (uint32_t)(((sg_mix(seed, base + j) >> 32) * 81ull) >> 32);
+      const uint32_t c = sg_below(sg_mix(seed, base + j), 81);
       o[j] = (uint8_t)((c % 3) | ((c / 3 % 3) << 2) | ((c / 9 % 3) << 4) | ((c / 27) << 6));
     }
     sg_normal2(seed, base + 64, z0, z1);

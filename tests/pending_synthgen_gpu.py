@@ -22,6 +22,7 @@ import synthgen_mirror as M  # noqa: E402
 
 TINY = synth.CONFIGS["tiny"]
 CFGS = {
+    "tq1": TINY.scaled(name="tiny-dev-tq1", n_layer=2),
     "tq2": TINY.scaled(name="tiny-dev-tq2", n_layer=2, linear_type=F.TQ2_0),
     "q4k": TINY.scaled(name="tiny-dev-q4k", n_layer=2, linear_type=F.Q4_K, attn_v_type=F.Q6_K,
                        output_type=F.Q6_K, linear_sigma=0.01),

@@ -9,7 +9,7 @@ import numpy as np
 from rustfox_b200 import formats as F
 
 U64 = np.uint64
-STRIDE = {F.TQ2_0: 80, F.Q8_0: 48, F.Q4_K: 160, F.Q6_K: 224}
+STRIDE = {F.TQ1_0: 64, F.TQ2_0: 80, F.Q8_0: 48, F.Q4_K: 160, F.Q6_K: 224}
 
 
 def mix(seed: int, i: np.ndarray) -> np.ndarray:
@@ -25,6 +25,10 @@ def normal2(seed: int, i: np.ndarray):
     u2 = (mix(seed, i + U64(1)) >> U64(11)).astype(np.float64) * 2.0**-53
     r, t = np.sqrt(-2.0 * np.log(u1)), 6.283185307179586 * u2
     return r * np.cos(t), r * np.sin(t)
+
+
+def below(h: np.ndarray, n: int) -> np.ndarray:
+    return ((h >> U64(32)) * U64(n)) >> U64(32)
 
 
 def half_abs(z: np.ndarray, sigma: float) -> np.ndarray:
@@ -43,8 +47,15 @@ def blocks(ggml_type: int, n_rows: int, n_cols: int, seed: int, sigma: float) ->
     sigma = float(np.float32(sigma))  # the entry point takes a float
     base = np.arange(nb, dtype=U64)[:, None] * U64(STRIDE[ggml_type])
     out = np.zeros((nb, bb), dtype=np.uint8)
-    if ggml_type == F.TQ2_0:
-        c = ((mix(seed, base + np.arange(64, dtype=U64)) >> U64(32)) * U64(81)) >> U64(32)
+    if ggml_type == F.TQ1_0:
+        v5 = below(mix(seed, base + np.arange(48, dtype=U64)), 243)
+        out[:, :48] = ((v5 * U64(256) + U64(242)) // U64(243)).astype(np.uint8)
+        v4 = below(mix(seed, base + np.arange(48, 52, dtype=U64)), 81)
+        out[:, 48:52] = ((v4 * U64(256) + U64(80)) // U64(81)).astype(np.uint8)
+        z0, _ = normal2(seed, base[:, 0] + U64(52))
+        _put16(out, 52, half_abs(z0, sigma))
+    elif ggml_type == F.TQ2_0:
+        c = below(mix(seed, base + np.arange(64, dtype=U64)), 81)
         out[:, :64] = (c % U64(3) | (c // U64(3) % U64(3)) << U64(2) | (c // U64(9) % U64(3)) << U64(4)
                        | (c // U64(27)) << U64(6)).astype(np.uint8)
         z0, _ = normal2(seed, base[:, 0] + U64(64))

@@ -28,6 +28,17 @@ def test_ternary_codes_are_uniform_and_scales_half_normal():
     assert abs(d.mean() - 0.02 * np.sqrt(2 / np.pi)) < 0.02 * 0.1
 
 
+def test_tq1_0_bytes_encode_uniform_trits():
+    b = M.blocks(F.TQ1_0, 64, 4096, seed=9, sigma=0.02).reshape(-1, 54)
+    enc5, enc4 = {int(v): i for i, v in enumerate(F.TQ1_ENC5)}, {int(v): i for i, v in enumerate(F.TQ1_ENC4)}
+    v5 = np.array([enc5[int(x)] for x in b[:200, :48].reshape(-1)])  # every qs byte is an encoding
+    v4 = np.array([enc4[int(x)] for x in b[:200, 48:52].reshape(-1)])
+    trits = np.concatenate([(v5 // 3**k) % 3 for k in range(5)] + [(v4 // 3**k) % 3 for k in range(4)])
+    assert np.allclose(np.bincount(trits, minlength=3) / trits.size, 1 / 3, atol=0.01)
+    d = b[:, 52:54].copy().view(np.float16).astype(np.float64).reshape(-1)
+    assert abs(d.mean() - 0.02 * np.sqrt(2 / np.pi)) < 0.02 * 0.1
+
+
 def test_q8_0_values_are_normal():
     b = M.blocks(F.Q8_0, 256, 4096, seed=3, sigma=0.02).reshape(-1, 34)
     d = b[:, :2].copy().view(np.float16).astype(np.float32)
@@ -76,7 +87,7 @@ def test_upload_synthetic_checks_its_arguments():
     if L.foxcuda_model_create_tp(ctypes.byref(mi), 0, 0, 1, ctypes.byref(h)) != api.OK:
         pytest.skip("no GPU: the model-level checks need a model")
     try:
-        assert L.foxcuda_model_upload_synthetic(h, 4, 0, F.TQ1_0, 256, 8, 1, 0.02) == api.ERR_UNSUPPORTED
+        assert L.foxcuda_model_upload_synthetic(h, 4, 0, F.F16, 256, 8, 1, 0.02) == api.ERR_UNSUPPORTED
         assert L.foxcuda_model_upload_synthetic(h, 4, 0, F.TQ2_0, 300, 8, 1, 0.02) == api.ERR_ARG
         assert L.foxcuda_model_upload_synthetic(h, 4, 0, F.TQ2_0, 256, 8, 1, 0.0) == api.ERR_ARG
         assert L.foxcuda_model_upload_synthetic(h, 4, 5, F.TQ2_0, 256, 8, 1, 0.02) == api.ERR_ARG
