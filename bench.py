@@ -434,8 +434,20 @@ def run_tp(args):
         dist.all_reduce(dt, op=dist.ReduceOp.MAX)
     dt = float(dt.item())
     if rank == 0:
+        # the whole model's bytes per token (weights once, K/V at the mean
+        # position of the timed steps), against every rank's HBM together
+        wb = cfg.weight_bytes()
+        pos = args.prompt + max(3, args.warmup) + args.steps // 2
+        tok_bytes = (wb["layers"] + wb["output"] + wb["embd_row"] + wb["norms"]
+                     + cfg.kv_bytes_per_token(pos))
+        hbm, src = measured_hbm_gbs()
+        achieved = tok_bytes * args.steps / dt / 1e9
         print(json.dumps({
             "metric": METRIC, "value": args.steps / dt, "unit": "tok/s", "n_gpus": world,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm * world, "unit": "GB/s",
+                         "frac": achieved / (hbm * world), "traffic": None,
+                         "peak_source": f"{src} per GPU x {world}",
+                         "bytes_per_token": tok_bytes},
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "i8 x ternary -> i32, f32",
