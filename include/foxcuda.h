@@ -296,7 +296,10 @@ foxcuda_status foxcuda_eval_all(foxcuda_context *c, const uint32_t *tokens, size
                                 float *logits_out);
 /* Back to an earlier position (no upstream counterpart; upstream only
  * resets). The cache entries from pos on are overwritten by the next
- * tokens, which is how a rejected draft is dropped. */
+ * tokens, which is how a rejected draft is dropped. A context whose
+ * tensor-parallel exchanges run over peer memory refuses it (FOXCUDA_ERR_ARG):
+ * its exchange slots are tagged by position, so a replayed position would
+ * read a peer's stale slot. */
 foxcuda_status foxcuda_context_rewind(foxcuda_context *c, uint32_t pos);
 foxcuda_status foxcuda_context_hidden(const foxcuda_context *c, uint32_t layer, float *out);
 
@@ -422,8 +425,9 @@ foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
  *   result is the single-GPU decode's, bit for bit.
  * - Every wait is bounded. A wait that gives up sets the device error word
  *   (code 2), which foxcuda_tp_tokens and later calls report.
- * - After foxcuda_context_reset, every rank calls foxcuda_tp_p2p_clear
- *   before any rank's next step.
+ * - After foxcuda_context_reset, and after any call that reports the error
+ *   word, every rank calls foxcuda_tp_p2p_clear before any rank's next step:
+ *   a step whose wait gave up leaves its terms and slots unusable.
  * Not yet run on a B200. */
 /* Repeat penalty of the sharded greedy pick (upstream src/sample.c:95-107):
  * each shard penalises the history tokens of its own vocabulary rows before

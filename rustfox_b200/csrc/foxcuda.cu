@@ -1907,6 +1907,11 @@ extern "C" uint32_t foxcuda_context_position(const foxcuda_context* c) { return 
 extern "C" foxcuda_status foxcuda_context_rewind(foxcuda_context* c, uint32_t pos) {
   if (!c) return fail(FOXCUDA_ERR_ARG, "rewind: null context");
   if (pos > c->pos) return fail(FOXCUDA_ERR_ARG, "rewind: position %u is past the current %u", pos, c->pos);
+  // Peer-memory exchange slots are tagged with the position they serve: a
+  // replayed position would accept a peer's stale value as this step's.
+  if (c->p2p && pos != c->pos)
+    return fail(FOXCUDA_ERR_ARG, "rewind: not supported on a context with peer-memory exchanges "
+                "(reset every shard and clear its arena instead)");
   cudaSetDevice(c->m->device);
   CK(cudaStreamSynchronize(c->stream), "rewind");
   const int p = (int)pos;

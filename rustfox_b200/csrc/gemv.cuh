@@ -626,6 +626,9 @@ gemv_kernel(const GemvParams p) {
             if (!direct(blockIdx.x + j * gridDim.x)) mbar_wait(bars + j % R, (j / R) & 1);
         }
         __syncthreads();
+        // still counted, so the completion count is rearmed for the next
+        // exchange; the error word marks this step's terms as unusable
+        if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
         return;
       }
       if (tid < ru * nb) {

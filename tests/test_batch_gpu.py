@@ -1,8 +1,5 @@
 """Decode batches (foxcuda_batch_*) against each context's own decode step,
-bit for bit. Not collected yet (the file name does not start with test_):
-it has not run on a B200. Run it with
-    python -m pytest tests/pending_batch_gpu.py -q
-and rename it to test_batch_gpu.py once it passes there.
+bit for bit.
 
 Upstream decodes one sequence per context (src/forward.c:411-438). A batch
 step serves several contexts with one pass; every context's logits and

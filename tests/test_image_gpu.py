@@ -1,10 +1,6 @@
 """Device images on a B200: a model saved with foxcuda_model_save_image and
 opened with foxcuda_model_open_image decodes exactly as the model it came
-from, holds the same device bytes, and saves back to the same file. Not
-collected yet (the file name does not start with test_): it has not run on a
-B200. Run it with
-    python -m pytest tests/pending_image_gpu.py -q
-and rename it to test_image_gpu.py once it passes there.
+from, holds the same device bytes, and saves back to the same file.
 
 The cases cover TQ1_0 layers (held as TQ2_0 in HBM, so the image carries the
 transcoded bytes), TQ2_0, the K-quant model of config 3 (Q4_K with a Q6_K v

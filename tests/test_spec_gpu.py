@@ -1,9 +1,6 @@
 """Speculative decoding on the device (rustfox_b200/spec.py over
 foxcuda_eval_all and foxcuda_context_rewind) against plain greedy decoding,
-token for token. Not collected yet (the file name does not start with
-test_): it has not run on a B200. Run it with
-    python -m pytest tests/pending_spec_gpu.py -q
-and rename it to test_spec_gpu.py once it passes there.
+token for token.
 """
 import numpy as np
 import pytest

@@ -1,9 +1,6 @@
 """Tensor-parallel decode with the exchanges over peer memory
 (foxcuda_tp_p2p_*, TPContext(exchange="p2p")) against the single-GPU decode,
-bit for bit. Not collected yet (the file name does not start with test_): it
-has not run on a B200. Run it with
-    python -m pytest tests/pending_tp_p2p_gpu.py -q
-and rename it to test_tp_p2p_gpu.py once it passes there.
+bit for bit.
 
 The one-GPU case runs the exchange kernels with a single rank (each slot
 written and read in the rank's own arena). By default the absmax exchange and

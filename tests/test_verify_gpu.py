@@ -1,8 +1,5 @@
 """The verification pass (foxcuda_eval_all): the logits of every token of a
-draft, against the token-by-token decode, bit for bit. Not collected yet (the
-file name does not start with test_): it has not run on a B200. Run it with
-    python -m pytest tests/pending_verify_gpu.py -q
-and rename it to test_verify_gpu.py once it passes there.
+draft, against the token-by-token decode, bit for bit.
 
 Upstream plans speculative decoding (README.md:86-89) but its forward_batch
 keeps only the last row (src/forward.c:405-408). Row t of eval_all must be
