@@ -555,6 +555,8 @@ struct or_ctx {
     const or_model *m;
     uint32_t n_ctx, pos;
     int kv_mode;
+    int attn_nt;        /* 0: upstream's serial attention; > 0: the tile attention */
+    float *tile_o;      /* the tile attention's per-tile sums [nt][head_dim] */
     size_t nq, nkv, wide;
     float *kc, *vc, *x, *xb, *xb2, *q, *k, *v, *hb, *hb2, *att, *norm, *rc, *rs;
 };
@@ -598,9 +600,23 @@ or_ctx *or_ctx_create(const or_model *m, uint32_t n_ctx, int kv_mode)
     return c;
 }
 
+int or_ctx_set_attn_tiles(or_ctx *c, int nt)
+{
+    if (!c || nt < 0 || nt > 64) return fail(OR_ERR_ARG, "attention tiles: 0..64");
+    free(c->tile_o);
+    c->tile_o = NULL;
+    c->attn_nt = nt;
+    if (nt > 0) {
+        c->tile_o = (float *)calloc((size_t)nt * c->m->info.head_dim, 4);
+        if (!c->tile_o) return fail(OR_ERR_ARG, "attention tiles: out of memory");
+    }
+    return OR_OK;
+}
+
 void or_ctx_destroy(or_ctx *c)
 {
     if (!c) return;
+    free(c->tile_o);
     free(c->kc); free(c->vc); free(c->x); free(c->xb); free(c->xb2); free(c->q);
     free(c->k); free(c->v); free(c->hb); free(c->hb2); free(c->att); free(c->norm);
     free(c->rc); free(c->rs); free(c);
@@ -624,6 +640,88 @@ static int norm_w(or_ctx *c, const or_tensor *t, const float **w)
 static float kv_round(const or_ctx *c, float v)
 {
     return c->kv_mode ? or_f16_to_f32(or_f32_to_f16_rne(v)) : v;
+}
+
+/* libfoxcuda's tile attention (rustfox_b200/csrc/loop.cuh) for one query head
+ * over positions 0..P-1 of one KV head (rows `stride` floats apart). This is
+ * not upstream's order; it is the production mode of the device, restated so
+ * that mode is checked bit for bit. Positions are cut into tiles of
+ * T = 32 * ceil(ceil(P / nt) / 32). Per tile: every score is the sum of 32
+ * lane partials (hd/32 dimensions each: q0*k0, then fmaf in dimension order)
+ * by an xor butterfly, times scale; the tile's max; e = exp(s - max); the sum
+ * of e in ascending order; and per dimension fmaf(e, v, .) in ascending
+ * order. The tiles are merged in order with weights exp(m_t - M): fmaf of
+ * the sums, fmaf of the outputs, one division. */
+static void tile_attention_into(const float *qh, const float *K, const float *V, size_t stride,
+                                size_t hd, size_t P, int nt_target, float scale, float *out,
+                                float *sc, float *tile_o)
+{
+    const size_t nt = (size_t)nt_target, per = (P + nt - 1) / nt;
+    const size_t T = (per + 31) / 32 * 32, ntl = (P + T - 1) / T, dpl = hd / 32;
+    float m[64], l[64], w[64], M = -INFINITY, L = 0.0f;
+    size_t t, j, d, i, lane, off;
+    for (t = 0; t < ntl; t++) {
+        const size_t j0 = t * T, n = (P - j0 < T) ? P - j0 : T;
+        float mx = -INFINITY, lt = 0.0f;
+        for (j = 0; j < n; j++) {
+            const float *k = K + (j0 + j) * stride;
+            float p[32], np[32];
+            for (lane = 0; lane < 32; lane++) {
+                const float *qa = qh + lane * dpl, *ka = k + lane * dpl;
+                float a = qa[0] * ka[0];
+                for (i = 1; i < dpl; i++) a = fmaf(qa[i], ka[i], a);
+                p[lane] = a;
+            }
+            for (off = 16; off > 0; off >>= 1) {
+                for (lane = 0; lane < 32; lane++) np[lane] = p[lane] + p[lane ^ off];
+                memcpy(p, np, sizeof(p));
+            }
+            sc[j] = p[0] * scale;
+        }
+        for (j = 0; j < n; j++) mx = fmaxf(mx, sc[j]);
+        for (j = 0; j < n; j++) sc[j] = or_expf(sc[j] - mx);
+        for (j = 0; j < n; j++) lt = lt + sc[j];
+        for (d = 0; d < hd; d++) {
+            float o = 0.0f;
+            for (j = 0; j < n; j++) o = fmaf(sc[j], V[(j0 + j) * stride + d], o);
+            tile_o[t * hd + d] = o;
+        }
+        m[t] = mx;
+        l[t] = lt;
+    }
+    for (t = 0; t < ntl; t++) M = fmaxf(M, m[t]);
+    for (t = 0; t < ntl; t++) w[t] = or_expf(m[t] - M);
+    for (t = 0; t < ntl; t++) L = fmaf(l[t], w[t], L);
+    for (d = 0; d < hd; d++) {
+        float O = 0.0f;
+        for (t = 0; t < ntl; t++) O = fmaf(tile_o[t * hd + d], w[t], O);
+        out[d] = O / L;
+    }
+}
+
+int or_tile_attention(const float *qh, const float *K, const float *V, size_t stride, size_t hd,
+                      size_t P, int nt, float scale, float *out)
+{
+    float *sc, *tile_o;
+    if (!qh || !K || !V || !out || P == 0 || nt < 1 || nt > 64 || hd % 32 || hd == 0)
+        return fail(OR_ERR_ARG, "tile attention: bad argument");
+    sc = (float *)malloc(P * 4);
+    tile_o = (float *)malloc((size_t)nt * hd * 4);
+    if (!sc || !tile_o) {
+        free(sc);
+        free(tile_o);
+        return fail(OR_ERR_ARG, "tile attention: out of memory");
+    }
+    tile_attention_into(qh, K, V, stride, hd, P, nt, scale, out, sc, tile_o);
+    free(sc);
+    free(tile_o);
+    return OR_OK;
+}
+
+static void tile_attention(const or_ctx *c, const float *qh, const float *K, const float *V,
+                           size_t stride, size_t hd, size_t P, float scale, float *out)
+{
+    tile_attention_into(qh, K, V, stride, hd, P, c->attn_nt, scale, out, c->att, c->tile_o);
 }
 
 /* one token at position c->pos; upstream forward.c:295-397 restated for a
@@ -665,6 +763,11 @@ static int step(or_ctx *c, uint32_t token, float *hidden)
             const float *qh = c->q + h * hd;
             float *dst = c->xb + h * hd;
             size_t kvh = h / gqa;
+            if (c->attn_nt > 0) {
+                tile_attention(c, qh, c->kc + base + kvh * hd, c->vc + base + kvh * hd, c->nkv, hd,
+                               (size_t)c->pos + 1, scale, dst);
+                continue;
+            }
             for (j = 0; j <= c->pos; j++)
                 c->att[j] = or_dot_f32(qh, c->kc + base + j * c->nkv + kvh * hd, hd) * scale;
             or_softmax(c->att, (size_t)c->pos + 1);

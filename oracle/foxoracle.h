@@ -92,6 +92,13 @@ typedef struct or_ctx or_ctx;
 or_ctx  *or_ctx_create(const or_model *m, uint32_t n_ctx, int kv_mode);
 void     or_ctx_destroy(or_ctx *c);
 void     or_ctx_reset(or_ctx *c);
+/* 0: upstream's serial attention (the default); nt > 0: libfoxcuda's tile
+ * attention with tile target nt (its production mode) */
+int      or_ctx_set_attn_tiles(or_ctx *c, int nt);
+/* the same tile attention for one query head over P positions of one KV
+ * head (K, V rows `stride` floats apart) */
+int      or_tile_attention(const float *qh, const float *K, const float *V, size_t stride,
+                           size_t hd, size_t P, int nt, float scale, float *out);
 uint32_t or_ctx_pos(const or_ctx *c);
 /* Evaluates n tokens; logits (n_vocab) of the last token when want_logits.
  * hidden, when not NULL, receives the residual stream of the LAST token after

@@ -87,6 +87,8 @@ def lib():
         L.or_ctx_create.argtypes = [C.POINTER(OrModel), _u32, C.c_int]
         L.or_ctx_destroy.argtypes = [_vp]
         L.or_ctx_reset.argtypes = [_vp]
+        L.or_ctx_set_attn_tiles.argtypes = [_vp, C.c_int]
+        L.or_tile_attention.argtypes = [_vp, _vp, _vp, _sz, _sz, _sz, C.c_int, _fp, _vp]
         L.or_ctx_pos.restype = _u32
         L.or_ctx_pos.argtypes = [_vp]
         L.or_eval.argtypes = [_vp, _vp, _sz, _vp, _vp]
@@ -177,6 +179,18 @@ def dequant_row(ggml_type, row, n):
     return out
 
 
+def tile_attention(q, K, V, nt: int, scale: float):
+    """libfoxcuda's tile attention (its production mode) for one query head
+    q[hd] over the rows of K, V (P x hd float32)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    K = np.ascontiguousarray(K, dtype=np.float32)
+    V = np.ascontiguousarray(V, dtype=np.float32)
+    out = np.empty(q.size, dtype=np.float32)
+    _check(lib().or_tile_attention(_ptr(q), _ptr(K), _ptr(V), K.shape[1], q.size, K.shape[0], int(nt),
+                                   float(scale), _ptr(out)), "tile_attention")
+    return out
+
+
 def rmsnorm(x, w, eps):
     x = np.ascontiguousarray(x, dtype=np.float32)
     w = np.ascontiguousarray(w, dtype=np.float32)
@@ -210,17 +224,21 @@ class OracleModel:
                          _otensor(model.tensors["output_norm.weight"]),
                          _otensor(model.tensors["output.weight"]), self._layers)
 
-    def context(self, n_ctx: int, kv_fp16: bool = False) -> "OracleContext":
-        return OracleContext(self, n_ctx, kv_fp16)
+    def context(self, n_ctx: int, kv_fp16: bool = False, attn_tiles: int = 0) -> "OracleContext":
+        """attn_tiles 0: upstream's serial attention; > 0: libfoxcuda's tile
+        attention with that tile target (the device's production mode)."""
+        return OracleContext(self, n_ctx, kv_fp16, attn_tiles)
 
 
 class OracleContext:
-    def __init__(self, om: OracleModel, n_ctx: int, kv_fp16: bool):
+    def __init__(self, om: OracleModel, n_ctx: int, kv_fp16: bool, attn_tiles: int = 0):
         self.om = om
         self.cfg = om.model.cfg
         self.h = lib().or_ctx_create(C.byref(om.s), n_ctx, 1 if kv_fp16 else 0)
         if not self.h:
             raise MemoryError("oracle context")
+        if attn_tiles:
+            _check(lib().or_ctx_set_attn_tiles(self.h, int(attn_tiles)), "attention tiles")
 
     def __del__(self):
         if getattr(self, "h", None):
@@ -266,10 +284,10 @@ class OracleSampler:
 
 
 def greedy_generate(om: OracleModel, prompt, n_gen: int, n_ctx: int, kv_fp16=False,
-                    repeat_penalty=1.1, repeat_last_n=64):
+                    repeat_penalty=1.1, repeat_last_n=64, attn_tiles=0):
     """The `fox run --temp 0` loop (upstream src/cli.c:333-361) on the oracle:
     eval the prompt, accept it into the sampler history, then pick/accept/eval."""
-    ctx = om.context(n_ctx, kv_fp16)
+    ctx = om.context(n_ctx, kv_fp16, attn_tiles)
     smp = OracleSampler(om.model.cfg.n_vocab, temperature=0.0,
                         repeat_penalty=repeat_penalty, repeat_last_n=repeat_last_n)
     logits = ctx.eval(prompt)

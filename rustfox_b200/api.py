@@ -73,6 +73,7 @@ _PROTOS = {
     "foxcuda_kernel_errors": (_st, [_vp]),
     "foxcuda_gemv": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_noalloc": (_st, [C.c_int, _vp, _vp, _sz, _sz, _vp, _vp]),
+    "foxcuda_attn_tile_target": (C.c_int, [C.c_int, C.c_uint32]),
     "foxcuda_attention": (_st, [_vp, _vp, _vp, C.c_int, C.c_uint32, C.c_uint32, C.c_uint32,
                                 C.c_uint32, C.c_uint32, C.c_int, _vp, _vp]),
     "foxcuda_dequant_row": (_st, [C.c_int, _vp, _sz, _vp, _vp]),
@@ -142,7 +143,7 @@ _PROTOS = {
     "foxcuda_context_sync_position": (_st, [_vp]),
 }
 
-KIND_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "advance", "head", "pick"]
+KIND_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "advance", "head", "pick", "loop"]
 
 _lib = None
 
@@ -441,6 +442,12 @@ class Model:
 
     def __del__(self):
         self.close()
+
+    @property
+    def attn_tiles(self) -> int:
+        """The tile target of this model's tile attention (its production
+        mode): foxcuda_attn_tile_target for its device and all its KV heads."""
+        return int(lib().foxcuda_attn_tile_target(self.device, int(self.info["n_head_kv"])))
 
     def context(self, n_ctx: int, kv: str = "f16", attn_exact: bool = False) -> "Context":
         return Context(self, n_ctx, kv, attn_exact)

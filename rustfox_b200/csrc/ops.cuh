@@ -83,28 +83,24 @@ __global__ void advance_kernel(int* pos, int by) {
 // ---------------------------------------------------------------------------
 // Decode attention (upstream src/forward.c:222-257 + src/ops.c:24-39,75-81):
 // per query head, scores q.k_j * (1/sqrtf(hd)) for j <= pos, softmax, sum of
-// a_j v_j. Flash-decoding form: CTA (s, g) takes split s of the positions for
-// KV head g and all its query heads (the K/V rows are read once per group),
-// keeps an online softmax per warp, and writes (max, sum, unnormalised
-// output) partials; the last CTA of a KV head to finish merges them.
+// a_j v_j. Two forms: attention_exact_kernel below (upstream's serial order,
+// the parity mode) and the tile attention of loop.cuh (attention_tile_kernel
+// and the persistent decode step), whose order the oracle restates.
 
 struct AttnParams {
   const float* q;         // [n_head * hd], roped
   const void* kcache;     // this layer: [n_kv][n_ctx][hd]
   const void* vcache;
-  int kv_f16, n_ctx, hd, n_head, n_kv, S_max;
+  int kv_f16, n_ctx, hd, n_head, n_kv;
+  int nt;                 // tile target of the tile attention (loop.cuh)
   const int* pos;
   float* out;             // [n_head * hd]
-  float* part;            // [n_kv][S_max][gqa][hd + 2]
-  unsigned* counters;     // [n_kv], zero between launches
+  float* part;            // [n_seq][n_kv][nt][gqa][hd + 2] tile partials
+  unsigned* counters;     // [n_seq][n_kv], zero between launches
   float scale;
-  // 1: launched with programmatic stream serialisation right after the
-  // kernel that wrote q and position *pos of the cache; rows before *pos
-  // were written by earlier launches and are staged before the wait
-  int pdl;
-  // decode batches (attention_cluster_kernel<..., SEQS>): sequence z reads
-  // q + z * seq_stride, writes out + z * seq_stride, its position at
-  // *pos_list[z] and its layer's caches at k_list[z] / v_list[z] + layer_off
+  // several sequences in one launch (grid z): sequence z reads q + z *
+  // seq_stride, writes out + z * seq_stride, its position at *pos_list[z]
+  // and its layer's caches at k_list[z] / v_list[z] + layer_off
   int seq_stride;
   int* const* pos_list;
   void* const* k_list;
@@ -112,387 +108,8 @@ struct AttnParams {
   size_t layer_off;
 };
 
-constexpr int ATTN_THREADS = 128;
 constexpr int ATTN_MAX_GQA = 8;
 constexpr int ATTN_MAX_DPL = 8;  // head_dim <= 256
-
-template <int DPL>
-FOX_DEV void load_kv(const void* cache, bool f16, size_t off, float* v) {
-  if (f16) {
-    const __half* p = reinterpret_cast<const __half*>(cache) + off;
-    if (DPL == 4) {
-      const uint2 r = *reinterpret_cast<const uint2*>(p);
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
-      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
-    } else {
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) v[i] = __half2float(p[i]);
-    }
-  } else {
-    const float* p = reinterpret_cast<const float*>(cache) + off;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) v[i] = p[i];
-  }
-}
-
-// The last CTA of KV head g to finish merges the S split partials
-// (max, sum, unnormalised output per query head) into the output.
-FOX_DEV void attn_merge(const AttnParams& p, int g, int S, int gqa, int hd) {
-  __shared__ bool is_last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = atomicAdd(p.counters + g, 1u) == (unsigned)(S - 1);
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  // The partials of the other CTAs are read through L2 (ld.global.cg: L1 is
-  // not coherent with their writes). Per (split, head): max and sum to shared
-  // memory, then the rescale factors, then every output dimension as an
-  // independent, pipelined sweep over the splits.
-  __shared__ float s_m[32][ATTN_MAX_GQA], s_l[32][ATTN_MAX_GQA], s_e[32][ATTN_MAX_GQA];
-  __shared__ float s_M[ATTN_MAX_GQA], s_L[ATTN_MAX_GQA];
-  const float* base = p.part + (size_t)g * p.S_max * gqa * (hd + 2);
-  for (int i = threadIdx.x; i < S * gqa; i += blockDim.x) {
-    const int t = i / gqa, h = i % gqa;
-    const float* pt = base + ((size_t)t * gqa + h) * (hd + 2);
-    s_m[t][h] = __ldcg(pt + hd);
-    s_l[t][h] = __ldcg(pt + hd + 1);
-  }
-  __syncthreads();
-  if (threadIdx.x < gqa) {
-    const int h = threadIdx.x;
-    float M = -CUDART_INF_F;
-    for (int t = 0; t < S; ++t)
-      if (s_l[t][h] > 0.0f) M = fmaxf(M, s_m[t][h]);
-    s_M[h] = M;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < S * gqa; i += blockDim.x) {
-    const int t = i / gqa, h = i % gqa;
-    s_e[t][h] = s_l[t][h] > 0.0f ? expf_cr(s_m[t][h] - s_M[h]) : 0.0f;
-  }
-  __syncthreads();
-  if (threadIdx.x < gqa) {
-    const int h = threadIdx.x;
-    float L = 0.0f;
-    for (int t = 0; t < S; ++t)
-      if (s_l[t][h] > 0.0f) L = fmaf(s_l[t][h], s_e[t][h], L);
-    s_L[h] = L;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < gqa * hd; idx += blockDim.x) {
-    const int h = idx / hd, d = idx % hd;
-    float A = 0.0f;
-#pragma unroll 8
-    for (int t = 0; t < S; ++t) {
-      const float v = __ldcg(base + ((size_t)t * gqa + h) * (hd + 2) + d);
-      if (s_l[t][h] > 0.0f) A = fmaf(v, s_e[t][h], A);
-    }
-    p.out[(g * gqa + h) * hd + d] = A / s_L[h];
-  }
-  if (threadIdx.x == 0) p.counters[g] = 0u;
-}
-
-template <int DPL>
-__global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const AttnParams p) {
-  griddep_launch_dependents();  // the o projection may start streaming its weights
-  const int s = blockIdx.x, g = blockIdx.y;
-  const int P = *p.pos + 1;
-  const int S = min(p.S_max, max(1, (P + 31) / 32));
-  if (s >= S) return;
-  const int chunk = (P + S - 1) / S;
-  const int j0 = s * chunk, j1 = min(P, j0 + chunk);
-  const int gqa = p.n_head / p.n_kv, hd = p.hd;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const bool f16 = p.kv_f16 != 0;
-
-  __shared__ float qs[ATTN_MAX_GQA * 32 * ATTN_MAX_DPL];
-  __shared__ float wm[4][ATTN_MAX_GQA], wl[4][ATTN_MAX_GQA];
-  __shared__ float wacc[4][ATTN_MAX_GQA * 32 * ATTN_MAX_DPL];
-
-  for (int i = threadIdx.x; i < gqa * hd; i += blockDim.x) qs[i] = p.q[g * gqa * hd + i];
-  __syncthreads();
-
-  float m[ATTN_MAX_GQA], l[ATTN_MAX_GQA], acc[ATTN_MAX_GQA][DPL];
-#pragma unroll
-  for (int h = 0; h < ATTN_MAX_GQA; ++h) {
-    m[h] = -CUDART_INF_F; l[h] = 0.0f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[h][i] = 0.0f;
-  }
-  const size_t head_base = (size_t)g * p.n_ctx * hd + lane * DPL;
-  for (int j = j0 + warp; j < j1; j += 4) {
-    float k[DPL], v[DPL];
-    load_kv<DPL>(p.kcache, f16, head_base + (size_t)j * hd, k);
-    load_kv<DPL>(p.vcache, f16, head_base + (size_t)j * hd, v);
-#pragma unroll
-    for (int h = 0; h < ATTN_MAX_GQA; ++h) {
-      if (h >= gqa) continue;
-      float d = 0.0f;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) d = fmaf(qs[h * hd + lane * DPL + i], k[i], d);
-      const float sc = warp_sum(d) * p.scale;
-      const float mn = fmaxf(m[h], sc);
-      const float corr = expf_cr(m[h] - mn);
-      const float pr = expf_cr(sc - mn);
-      l[h] = l[h] * corr + pr;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) acc[h][i] = fmaf(pr, v[i], acc[h][i] * corr);
-      m[h] = mn;
-    }
-  }
-  // merge the four warps
-#pragma unroll
-  for (int h = 0; h < ATTN_MAX_GQA; ++h) {
-    if (h >= gqa) continue;
-    if (lane == 0) { wm[warp][h] = m[h]; wl[warp][h] = l[h]; }
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) wacc[warp][h * hd + lane * DPL + i] = acc[h][i];
-  }
-  __syncthreads();
-  float* part = p.part + ((size_t)g * p.S_max + s) * gqa * (hd + 2);
-  for (int idx = threadIdx.x; idx < gqa * hd; idx += blockDim.x) {
-    const int h = idx / hd;
-    float M = -CUDART_INF_F;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w][h]);
-    float A = 0.0f, L = 0.0f;
-    for (int w = 0; w < 4; ++w) {
-      const float e = wl[w][h] > 0.0f ? expf_cr(wm[w][h] - M) : 0.0f;
-      A = fmaf(wacc[w][idx], e, A);
-      L = fmaf(wl[w][h], e, L);
-    }
-    part[h * (hd + 2) + idx % hd] = A;
-    if (idx % hd == 0) { part[h * (hd + 2) + hd] = M; part[h * (hd + 2) + hd + 1] = L; }
-  }
-  attn_merge(p, g, S, gqa, hd);
-}
-
-// Shared memory of one attention tile: 128 K rows padded by 16 bytes, then
-// 128 V rows.
-template <int HD, bool F16>
-constexpr size_t attn_tile_smem() {
-  return (size_t)128 * (HD * (F16 ? 2 : 4) + 16) + (size_t)128 * HD * (F16 ? 2 : 4);
-}
-
-FOX_DEV void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-FOX_DEV void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
-}
-
-// Cluster decode attention. The ATTN_SPLITS CTAs of one KV head form a
-// thread-block cluster; CTA r takes the r-th run of the positions, in tiles of
-// 128 (K/V staged in shared memory with cp.async before q is read, scores one
-// position per thread, a per-tile online softmax, the weighted V sum one
-// dimension per thread). Its partial (max, sum, unnormalised output per query
-// head) stays in its own shared memory. After a cluster barrier every CTA
-// merges 1/ATTN_SPLITS of the outputs by reading the others' partials through
-// distributed shared memory, and a second barrier keeps every partial alive
-// until the last remote read. No global scratch, fence or atomic.
-constexpr int ATTN_SPLITS = 8;  // portable cluster size
-
-FOX_DEV void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// address of the same shared variable in CTA `rank` of this cluster
-FOX_DEV const float* cluster_peer(const float* p, unsigned rank) {
-  uint64_t r;
-  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(p), "r"(rank));
-  return reinterpret_cast<const float*>(r);
-}
-
-// SEQS: one launch for a decode batch; grid z is the sequence, whose q, out,
-// position and caches come from AttnParams' per-sequence fields.
-template <int HD, int G, bool F16, bool SEQS = false>
-__global__ void __cluster_dims__(ATTN_SPLITS, 1, 1) __launch_bounds__(128)
-attention_cluster_kernel(const AttnParams p) {
-  griddep_launch_dependents();  // the o projection may start streaming its weights
-  constexpr int NT = 128, DPT = NT / HD;
-  constexpr int ESZ = F16 ? 2 : 4, RB = HD * ESZ, KSTRIDE = RB + 16;
-  const int r = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;  // r = rank in the cluster
-  const int lane = tid & 31, warp = tid >> 5;
-  const float* q_in = p.q;
-  float* out = p.out;
-  const int* pos = p.pos;
-  const void* kcache = p.kcache;
-  const void* vcache = p.vcache;
-  if constexpr (SEQS) {
-    const int z = blockIdx.z;
-    q_in = p.q + (size_t)z * p.seq_stride;
-    out = p.out + (size_t)z * p.seq_stride;
-    pos = p.pos_list[z];
-    kcache = reinterpret_cast<const uint8_t*>(p.k_list[z]) + p.layer_off;
-    vcache = reinterpret_cast<const uint8_t*>(p.v_list[z]) + p.layer_off;
-  }
-  const int P = *pos + 1;
-  const int chunk = (P + ATTN_SPLITS - 1) / ATTN_SPLITS;
-  const int j0 = min(P, r * chunk), j1 = min(P, j0 + chunk);
-
-  extern __shared__ __align__(16) unsigned char smem[];
-  uint8_t* sK = smem;
-  uint8_t* sV = smem + (size_t)NT * KSTRIDE;
-  __shared__ float qs[G][HD];
-  __shared__ float ps[G][NT];
-  __shared__ float rmax[4][G], rsum[4][G];
-  __shared__ float accs[DPT > 1 ? DPT - 1 : 1][G][HD];
-  __shared__ float part[G][HD + 2];           // this CTA's partial, read by the cluster
-  __shared__ float ew[ATTN_SPLITS][G], lw[ATTN_SPLITS][G];
-
-  const size_t head = (size_t)g * p.n_ctx * HD;
-  const uint8_t* kg = reinterpret_cast<const uint8_t*>(kcache) + head * ESZ;
-  const uint8_t* vg = reinterpret_cast<const uint8_t*>(vcache) + head * ESZ;
-  // rows t0 .. t0+n-1 of the cache into tile rows 0 .. n-1, except position skip
-  auto stage = [&](int t0, int n, int skip) {
-    const int pieces = n * (RB / 16);
-    for (int i = tid; i < pieces; i += NT) {
-      const int row = i / (RB / 16), c = i - row * (RB / 16);
-      if (t0 + row == skip) continue;
-      cp_async16(sK + (size_t)row * KSTRIDE + c * 16, kg + (size_t)(t0 + row) * RB + c * 16);
-      cp_async16(sV + (size_t)i * 16, vg + (size_t)t0 * RB + (size_t)i * 16);
-    }
-  };
-  // The first tile is in flight while q is read. Under programmatic launch
-  // the newest position (P - 1) and q come from the kernel still finishing:
-  // they are read after griddepcontrol.wait (a no-op for a plain launch).
-  const int n0 = j0 < j1 ? min(NT, j1 - j0) : 0;
-  const int cur = p.pdl ? P - 1 : -1;
-  if (n0) stage(j0, n0, cur);
-  griddep_wait();
-  if (cur >= j0 && cur < j0 + n0)
-    for (int c = tid; c < RB / 16; c += NT) {
-      const int row = cur - j0;
-      cp_async16(sK + (size_t)row * KSTRIDE + c * 16, kg + (size_t)cur * RB + c * 16);
-      cp_async16(sV + (size_t)row * RB + c * 16, vg + (size_t)cur * RB + c * 16);
-    }
-  for (int i = tid; i < G * HD; i += NT) qs[i / HD][i % HD] = q_in[(size_t)g * G * HD + i];
-
-  const int d = tid % HD, jsub = tid / HD;
-  float m[G], l[G], acc[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) { m[h] = -CUDART_INF_F; l[h] = 0.0f; acc[h] = 0.0f; }
-
-  for (int t0 = j0; t0 < j1; t0 += NT) {
-    const int n = min(NT, j1 - t0);
-    if (t0 != j0) stage(t0, n, -1);
-    cp_async_wait_all();
-    __syncthreads();
-    const bool on = tid < n;
-    float sc[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) sc[h] = 0.0f;
-    if (on) {
-      const uint4* kr = reinterpret_cast<const uint4*>(sK + (size_t)tid * KSTRIDE);
-#pragma unroll 4
-      for (int c = 0; c < RB / 16; ++c) {
-        const uint4 w = kr[c];
-        if (F16) {
-          const __half2* hw = reinterpret_cast<const __half2*>(&w);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 kv = __half22float2(hw[e]);
-#pragma unroll
-            for (int h = 0; h < G; ++h) {
-              sc[h] = fmaf(qs[h][c * 8 + 2 * e], kv.x, sc[h]);
-              sc[h] = fmaf(qs[h][c * 8 + 2 * e + 1], kv.y, sc[h]);
-            }
-          }
-        } else {
-          const float* fw = reinterpret_cast<const float*>(&w);
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-#pragma unroll
-            for (int h = 0; h < G; ++h) sc[h] = fmaf(qs[h][c * 4 + e], fw[e], sc[h]);
-        }
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      sc[h] = on ? sc[h] * p.scale : -CUDART_INF_F;
-      const float mx = warp_max(sc[h]);
-      if (lane == 0) rmax[warp][h] = mx;
-    }
-    __syncthreads();
-    float corr[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float tmax = fmaxf(fmaxf(rmax[0][h], rmax[1][h]), fmaxf(rmax[2][h], rmax[3][h]));
-      const float mn = fmaxf(m[h], tmax);
-      corr[h] = m[h] == -CUDART_INF_F ? 0.0f : expf_cr(m[h] - mn);
-      float pj = 0.0f;
-      if (on) pj = expf_cr(sc[h] - mn);
-      ps[h][tid] = pj;
-      const float sm = warp_sum(pj);
-      if (lane == 0) rsum[warp][h] = sm;
-      m[h] = mn;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      l[h] = fmaf(l[h], corr[h], (rsum[0][h] + rsum[1][h]) + (rsum[2][h] + rsum[3][h]));
-      acc[h] *= corr[h];
-    }
-#pragma unroll 8
-    for (int jj = jsub; jj < n; jj += DPT) {
-      const float v = F16 ? __half2float(reinterpret_cast<const __half*>(sV)[(size_t)jj * HD + d])
-                          : reinterpret_cast<const float*>(sV)[(size_t)jj * HD + d];
-#pragma unroll
-      for (int h = 0; h < G; ++h) acc[h] = fmaf(ps[h][jj], v, acc[h]);
-    }
-    __syncthreads();
-  }
-  if (DPT > 1) {
-    if (jsub > 0)
-#pragma unroll
-      for (int h = 0; h < G; ++h) accs[jsub - 1][h][d] = acc[h];
-    __syncthreads();
-    if (jsub == 0)
-#pragma unroll
-      for (int h = 0; h < G; ++h)
-        for (int k = 0; k < DPT - 1; ++k) acc[h] += accs[k][h][d];
-  }
-  if (jsub == 0) {
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      part[h][d] = acc[h];
-      if (d == 0) { part[h][HD] = m[h]; part[h][HD + 1] = l[h]; }
-    }
-  }
-  cluster_sync_all();
-  // merge: rescale factors of every split, then this CTA's slice of outputs
-  if (tid < ATTN_SPLITS * G) {
-    const int t = tid / G, h = tid - t * G;
-    const float* pt = cluster_peer(&part[h][0], t);
-    ew[t][h] = pt[HD];
-    lw[t][h] = pt[HD + 1];
-  }
-  __syncthreads();
-  if (tid < G) {
-    const int h = tid;
-    float M = -CUDART_INF_F;
-    for (int t = 0; t < ATTN_SPLITS; ++t)
-      if (lw[t][h] > 0.0f) M = fmaxf(M, ew[t][h]);
-    float L = 0.0f;
-    for (int t = 0; t < ATTN_SPLITS; ++t) {
-      const float e = lw[t][h] > 0.0f ? expf_cr(ew[t][h] - M) : 0.0f;
-      ew[t][h] = e;
-      L = fmaf(lw[t][h], e, L);
-    }
-    rsum[0][h] = L;
-  }
-  __syncthreads();
-  constexpr int PER = G * HD / ATTN_SPLITS;  // outputs merged by each CTA
-  for (int k = tid; k < PER; k += NT) {
-    const int idx = r * PER + k, h = idx / HD, dd = idx - h * HD;
-    float A = 0.0f;
-#pragma unroll
-    for (int t = 0; t < ATTN_SPLITS; ++t)
-      if (lw[t][h] > 0.0f) A = fmaf(cluster_peer(&part[h][dd], t)[0], ew[t][h], A);
-    out[((size_t)g * G + h) * HD + dd] = A / rsum[0][h];
-  }
-  cluster_sync_all();  // no CTA leaves while another may still read its partial
-}
 
 // Attention in upstream's exact operation order (src/forward.c:222-257,
 // src/ops.c:24-39,75-81), one CTA per query head: sequential dot products,

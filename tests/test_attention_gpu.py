@@ -7,9 +7,10 @@ query head, scores q.k_j * (1/sqrtf(hd)) for j <= pos, fox_softmax
   exact = 1  must equal that serial order bit for bit. The reference here is
              numpy float32 in the same order, with the oracle's softmax run on
              the correctly rounded exponential the device uses.
-  exact = 0  is the split-K decode kernel. It sums in another order, so it is
-             compared with a float64 torch reference: max error within 1e-5 of
-             the output's scale (fp32 rounding of ~10^3-term sums).
+  exact = 0  is the tile attention of the decode step. It sums in another
+             order, which the oracle restates (oracle.tile_attention): bit
+             for bit against that, and within 1e-5 of the output's scale
+             against a float64 torch reference.
 Both run on fp32 and fp16 caches (fp16 values are exactly representable in
 fp32, so the references read the same numbers).
 """
@@ -92,13 +93,31 @@ def _ref_serial(q, k, v, n_head, n_kv, hd, pos):
 
 @pytest.mark.parametrize("f16", [True, False])
 @pytest.mark.parametrize("case", CASES)
-def test_split_kernel_matches_fp64(case, f16):
+def test_tile_kernel_matches_fp64(case, f16):
     n_head, n_kv, hd, n_ctx, pos = case
     q, k, v = _inputs(n_head, n_kv, hd, n_ctx, pos + hd, f16)
     got = _run(q, k, v, n_head, n_kv, hd, n_ctx, pos, 0, f16).double()
     want = _ref64(q, k, v, n_head, n_kv, hd, pos)
     err = (got - want).abs().max().item() / want.abs().max().item()
     assert err <= 1e-5, err
+
+
+@pytest.mark.parametrize("f16", [True, False])
+@pytest.mark.parametrize("case", CASES)
+def test_tile_kernel_is_the_oracles_tile_order(case, f16):
+    n_head, n_kv, hd, n_ctx, pos = case
+    q, k, v = _inputs(n_head, n_kv, hd, n_ctx, pos + 3 * hd, f16)
+    got = _run(q, k, v, n_head, n_kv, hd, n_ctx, pos, 0, f16).numpy()
+    nt = rf.lib().foxcuda_attn_tile_target(0, n_kv)
+    gqa = n_head // n_kv
+    qn = q.numpy().astype(np.float32).reshape(n_head, hd)
+    kn, vn = k.float().numpy(), v.float().numpy()
+    scale = np.float32(1.0) / np.sqrt(np.float32(hd), dtype=np.float32)
+    with O.exp_mode(True):
+        want = np.concatenate([O.tile_attention(qn[h], kn[h // gqa, : pos + 1], vn[h // gqa, : pos + 1], nt,
+                                                float(scale)) for h in range(n_head)])
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (
+        f"{np.count_nonzero(got != want)} of {got.size} differ")
 
 
 @pytest.mark.parametrize("f16", [True, False])

@@ -3,10 +3,11 @@
 Config 3 (8B) uses Q4_K for the linear weights with Q6_K attn_v and head;
 configs 4 and 5 use TQ2_0 linear weights. They run here at the tiny shape,
 with the same formats, seeded the same way: parity mode (fp32 cache, upstream's
-attention order) must reproduce the oracle bit for bit at every layer, and
-greedy decoding must pick the same tokens. The K-quant layers and the Q6_K
-head go through the ring-mode unit GEMV, the TQ2_0 layers through the
-resident-slice GEMV without transcoding.
+attention order) and production mode (fp16 cache, the tile attention, which
+the oracle restates) must reproduce the oracle bit for bit at every layer,
+and greedy decoding must pick the same tokens. The K-quant layers and the
+Q6_K head go through the ring-mode unit GEMV, the TQ2_0 layers through the
+persistent decode step without transcoding.
 """
 import numpy as np
 import pytest
@@ -63,12 +64,19 @@ def test_parity_mode_greedy(pair):
     assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
 
 
-def test_production_mode_within_band(pair):
+def test_production_mode_bit_identical(pair):
+    """fp16 cache and the tile attention, against the oracle with the same
+    cache rounding and tile order: every layer and the logits bit for bit."""
     cfg, m, om = pair
     prompt = synth.random_prompt(cfg, 48, seed=6)
     with O.exp_mode(True):
-        want = om.context(128, kv_fp16=True).eval(prompt)
+        want, want_h = om.context(128, kv_fp16=True, attn_tiles=m.attn_tiles).eval(prompt, want_hidden=True)
     ctx = m.context(128, kv="f16")
+    ctx.set_trace(True)
     got = ctx.eval(prompt)
-    assert rel_l2(got, want) <= 3e-2
+    for l in range(cfg.n_layer + 1):
+        h = ctx.hidden(l)
+        assert np.array_equal(h.view(np.uint32), want_h[l].view(np.uint32)), (
+            f"{cfg.name} layer {l}: rel L2 {rel_l2(h, want_h[l]):.3g}")
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     ctx.close()

@@ -248,3 +248,34 @@ def test_oracle_matches_golden_forward(tiny_model, oracle_tiny):
     assert np.array_equal(u32(logits), u32(g["logits"]))
     toks = O.greedy_generate(oracle_tiny, g["prompt"], len(g["greedy"]), 64)
     assert np.array_equal(toks, g["greedy"])
+
+
+# ---- 4. the tile attention (the device's production-mode order) ------------
+@pytest.mark.parametrize("P,hd,nt", [(1, 64, 18), (37, 128, 18), (540, 128, 18), (4096, 128, 9),
+                                     (300, 64, 64), (33, 128, 1)])
+def test_tile_attention_is_softmax_attention(P, hd, nt):
+    """The oracle's restatement of libfoxcuda's tile attention is an
+    attention: within fp32 rounding of a float64 softmax."""
+    rng = np.random.default_rng(P + hd + nt)
+    q = rng.normal(size=hd).astype(np.float32)
+    K = rng.normal(size=(P, hd)).astype(np.float32)
+    V = rng.normal(size=(P, hd)).astype(np.float32)
+    scale = np.float32(1.0) / np.sqrt(np.float32(hd), dtype=np.float32)
+    with O.exp_mode(True):
+        got = O.tile_attention(q, K, V, nt, float(scale))
+    s = (K.astype(np.float64) @ q.astype(np.float64)) * float(scale)
+    a = np.exp(s - s.max())
+    want = (a / a.sum()) @ V.astype(np.float64)
+    assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
+
+
+def test_tile_attention_context_stays_close_to_serial(tiny_model, oracle_tiny):
+    """An oracle context in tile mode gives finite logits close to upstream's
+    serial attention: only the attention's summation order differs."""
+    prompt = synth.random_prompt(synth.CONFIGS["tiny"], 40, seed=3)
+    with O.exp_mode(True):
+        serial = oracle_tiny.context(64).eval(prompt)
+        tiled = oracle_tiny.context(64, attn_tiles=18).eval(prompt)
+    assert np.isfinite(tiled).all()
+    rel = np.linalg.norm(tiled.astype(np.float64) - serial) / np.linalg.norm(serial.astype(np.float64))
+    assert rel <= 3e-2
