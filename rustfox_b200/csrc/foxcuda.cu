@@ -761,7 +761,7 @@ extern "C" foxcuda_status foxcuda_dequant_row(int type, const void* row, size_t 
   return FOXCUDA_OK;
 }
 
-static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t s);
+static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t s, bool pdl = false);
 
 // Tile target of the tile attention (loop.cuh): about one tile per SM over
 // all KV heads. Every path of a model (the persistent step, prompt chunks,
@@ -2035,30 +2035,42 @@ static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
 
 // The tile attention (loop.cuh) of n_seq sequences in one launch: grid
 // (nt, n_kv, n_seq); ap.part / ap.counters hold n_seq slots.
+// pdl: launched with programmatic stream serialisation, right after the
+// kernel that writes q and the newest K/V row and nothing else this kernel
+// reads (the decode step's q|k|v GEMV).
 template <int DPL>
-static cudaError_t launch_tile_t(const AttnParams& ap, int n_seq, cudaStream_t s) {
-  const size_t sm = attn_tile_smem_bytes(ap.n_ctx, ap.nt, ap.n_head / ap.n_kv);
+static cudaError_t launch_tile_t(const AttnParams& ap, int n_seq, cudaStream_t s, bool pdl) {
+  const size_t sm = attn_tile_smem_bytes(ap.n_ctx, ap.nt, ap.n_head / ap.n_kv, ap.hd, ap.kv_f16);
   static size_t marks[kMaxDevices] = {};
   cudaError_t e = opt_in_smem(attention_tile_kernel<DPL>, sm, marks);
   if (e != cudaSuccess) return e;
-  attention_tile_kernel<DPL><<<dim3(ap.nt, ap.n_kv, n_seq), 256, sm, s>>>(ap);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ap.nt, ap.n_kv, n_seq);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = sm;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_tile_kernel<DPL>, ap);
 }
 
-static cudaError_t launch_tiles(const AttnParams& ap, int n_seq, cudaStream_t s) {
+static cudaError_t launch_tiles(const AttnParams& ap, int n_seq, cudaStream_t s, bool pdl = false) {
   switch (ap.hd / 32) {
-    case 1: return launch_tile_t<1>(ap, n_seq, s);
-    case 2: return launch_tile_t<2>(ap, n_seq, s);
-    case 4: return launch_tile_t<4>(ap, n_seq, s);
-    case 8: return launch_tile_t<8>(ap, n_seq, s);
+    case 1: return launch_tile_t<1>(ap, n_seq, s, pdl);
+    case 2: return launch_tile_t<2>(ap, n_seq, s, pdl);
+    case 4: return launch_tile_t<4>(ap, n_seq, s, pdl);
+    case 8: return launch_tile_t<8>(ap, n_seq, s, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
 // One decode attention over a K/V cache: upstream's serial order (exact) or
 // the tile attention.
-static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t s) {
-  if (!exact) return launch_tiles(ap, 1, s);
+static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t s, bool pdl) {
+  if (!exact) return launch_tiles(ap, 1, s, pdl);
   const size_t sm = (size_t)ap.n_ctx * 4;
   static size_t marks[kMaxDevices] = {};
   cudaError_t e = opt_in_smem(attention_exact_kernel, sm, marks);
@@ -2075,7 +2087,9 @@ static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
   ap.hd = mi.head_dim; ap.n_head = c->m->loc.n_head; ap.n_kv = c->m->loc.n_head_kv; ap.nt = c->m->attn_nt;
   ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
   ap.scale = 1.0f / sqrtf((float)mi.head_dim);
-  return run_attention(ap, c->attn_exact, c->stream);
+  // the single-GPU step overlaps the q|k|v kernel; a tensor-parallel step
+  // keeps plain stream order
+  return run_attention(ap, c->attn_exact, c->stream, ctx_pdl(c) && c->m->tp_size == 1 && !c->tp_steps);
 }
 
 static cudaError_t launch_o(foxcuda_context* c, uint32_t l) {
@@ -2214,9 +2228,12 @@ static cudaError_t loop_setup(foxcuda_context* c) {
   const int nb_max = (int)std::max<uint32_t>(mi.n_embd, std::max<uint32_t>(nq, mi.n_ff)) / 256;
   const size_t xq = (size_t)nb_max * XQ_STRIDE;
   const int nt = m->attn_nt;
+  // staged K/V chunks of the attention: 64 rows of fp16, 32 of fp32
+  const int ch = c->kv_f16 ? 64 : 32;
   const size_t attn = c->attn_exact ? (size_t)c->n_ctx * 4
                                     : ((size_t)gqa * attn_tile_len((int)c->n_ctx, nt) +
-                                       (size_t)std::max(64, 3 * nt * gqa + 2 * gqa)) * 4;
+                                       (size_t)attn_sm_floats(nt, gqa)) * 4 +
+                                          2 * (size_t)ch * hd * (c->kv_f16 ? 2 : 4);
   const size_t fixed = 512 /* reduction */ + 4 * 8 /* mbarriers */ + 1024 /* static and alignment */;
   int n_slots = 4;
   int slot = 0;
@@ -2224,7 +2241,8 @@ static cudaError_t loop_setup(foxcuda_context* c) {
   for (; n_slots >= 2; --n_slots) {
     // the part/vals sizes depend on the pieces, which depend on the slot:
     // take the slot that leaves room for them
-    for (slot = (int)((dev_max - fixed - xq) / n_slots) / 128 * 128; slot >= 8192; slot -= 1024) {
+    for (slot = (int)((dev_max - fixed - std::max(xq, attn)) / n_slots) / 128 * 128; slot >= 8192;
+         slot -= 1024) {
       size_t rows = 0, pbytes = 0;
       for (LoopLayer& Y : layers)
         for (LoopMat& M : Y.m) {
@@ -2257,7 +2275,7 @@ static cudaError_t loop_setup(foxcuda_context* c) {
   p.embd = m->embd.dev; p.embd_type = m->embd.type; p.embd_rb = (long)row_bytes(m->embd.type, mi.n_embd);
   p.x = c->x; p.q = c->q; p.att = c->att; p.h = c->h;
   p.part = c->attn_part; p.cnt = c->attn_cnt; p.err = c->err_dev;
-  p.n_slots = n_slots; p.slot_bytes = slot;
+  p.n_slots = n_slots; p.slot_bytes = slot; p.attn_ch = ch;
   size_t off = 0;
   p.ring_off = 0; off += (size_t)n_slots * slot;
   p.scr_off = p.xq_off = (int)off;

@@ -108,6 +108,7 @@ struct LoopParams {
   int* err;        // 3: a grid barrier gave up; 1: a weight copy gave up
   float* trace;    // optional [(n_layer + 1) * n_embd]: x after the embedding and each layer
   int n_slots, slot_bytes;
+  int attn_ch;     // K/V rows per staged chunk of the attention
   int ring_off, xq_off, part_off, vals_off, scr_off, scr_bytes, bar_off, red_off;
 };
 
@@ -128,11 +129,13 @@ FOX_DEV void red_release_gpu_add(unsigned* p, unsigned v) {
 }
 
 // Every CTA arrives once; returns once the counter reaches target, or false
-// after about a second (then the error word is set).
+// after about a second (then the error word is set). The CTA's writes are
+// ordered before thread 0's release by the block barrier (a release is
+// cumulative), and the acquire that sees the count orders the reads after
+// it; the readers of another CTA's data use L2 loads (ld.cg).
 FOX_DEV bool grid_barrier(unsigned* bar, unsigned target, int* err, int* ok_sh) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     red_release_gpu_add(bar, 1u);
     int ok = 0;
     const uint64_t t0 = globaltimer_ns();
@@ -142,7 +145,6 @@ FOX_DEV bool grid_barrier(unsigned* bar, unsigned target, int* err, int* ok_sh) 
       if (i > 64) __nanosleep(32);
     }
     if (!ok && err) atomicExch(err, 3);
-    __threadfence();
     *ok_sh = ok;
   }
   __syncthreads();
@@ -200,44 +202,170 @@ struct TileArgs {
   float scale;
 };
 
-// Tile t of KV group g: the partials of every query head of the group. The
-// shared scratch holds gqa * T floats (scores, then weights) and 4 * 32 more.
-template <int DPL>
-FOX_DEV void attn_tile(const TileArgs& a, int g, int t, float* sc, float* sm) {
+// Floats of the tile attention's small scratch (per-head max and sum, then
+// the merge's per-tile values), a multiple of 4 so what follows stays
+// 16-byte aligned.
+__host__ __device__ inline int attn_sm_floats(int nt, int gqa) {
+  const int n = 3 * nt * gqa + 2 * gqa;
+  return ((n < 64 ? 64 : n) + 3) / 4 * 4;
+}
+
+FOX_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+FOX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+FOX_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+FOX_DEV void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// K/V rows of one KV head staged in shared memory, ch rows at a time.
+struct TileStage {
+  uint8_t* k;   // ch rows of K
+  uint8_t* v;   // ch rows of V
+  int ch;
+};
+
+// Rows [r0, r1) of a head's cache (row bytes rb) into buf, row r at
+// (r - r0) * rb, except row `skip`; asynchronous (cp.async, L2 only), one
+// commit group.
+FOX_DEV void stage_rows(uint8_t* buf, const uint8_t* head, int rb, int r0, int r1, int skip) {
+  const int per_row = rb >> 4, pieces = (r1 - r0) * per_row;
+  for (int i = threadIdx.x; i < pieces; i += blockDim.x) {
+    const int row = i / per_row;
+    if (r0 + row == skip) continue;
+    cp_async16(buf + (size_t)i * 16, head + (size_t)r0 * rb + (size_t)i * 16);
+  }
+  cp_async_commit();
+}
+
+// The first chunk of tile t of group g, K then V (two commit groups),
+// without the newest position P - 1: everything this tile reads that
+// earlier steps wrote. It may be issued before the step's q and newest K/V
+// row exist (before a grid barrier, or before griddepcontrol.wait).
+FOX_DEV void attn_tile_stage0(const TileArgs& a, const TileStage& st, int g, int t) {
+  const int T = attn_tile_len(a.P, a.nt), j0 = t * T, n = min(T, a.P - j0);
+  const int rb = a.hd * (a.f16 ? 2 : 4);
+  const size_t head = (size_t)g * a.n_ctx * rb;
+  const int c1 = j0 + min(n, st.ch);
+  stage_rows(st.k, reinterpret_cast<const uint8_t*>(a.kc) + head, rb, j0, c1, a.P - 1);
+  stage_rows(st.v, reinterpret_cast<const uint8_t*>(a.vc) + head, rb, j0, c1, a.P - 1);
+}
+
+// Row r of a staged chunk as floats (DPL elements from element e0).
+template <int DPL, bool F16>
+FOX_DEV void staged_row(const uint8_t* buf, int r, int hd, int e0, float* v) {
+  if (F16) {
+    const __half* p = reinterpret_cast<const __half*>(buf) + (size_t)r * hd + e0;
+#pragma unroll
+    for (int i = 0; i < DPL; i += 2) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p + i));
+      v[i] = f.x;
+      if (i + 1 < DPL) v[i + 1] = f.y;
+    }
+  } else {
+    const float* p = reinterpret_cast<const float*>(buf) + (size_t)r * hd + e0;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) v[i] = p[i];
+  }
+}
+
+// Scores of 16 rows (r0.., at most `valid` of them) of a staged chunk for one
+// query head: lane l forms the partial over its hd/32 dimensions for each
+// row, then a butterfly reduce-scatter (offsets 16, 8, 4, 2) and a last
+// exchange at offset 1 leave row r0 + (lane >> 1)'s dot in lanes 2k, 2k+1.
+// Every add pairs the same lane partials as an xor all-reduce (16, 8, 4, 2,
+// 1) does, so each dot is the all-reduce's value bit for bit, with 16
+// exchanges for 16 rows instead of 80.
+template <int DPL, bool F16>
+FOX_DEV float dot16(const uint8_t* buf, int r0, int valid, int hd, const float* qh, int lane) {
+  float P[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    P[i] = 0.0f;
+    if (i < valid) {
+      float k[DPL];
+      staged_row<DPL, F16>(buf, r0 + i, hd, lane * DPL, k);
+      float d = __fmul_rn(qh[0], k[0]);
+#pragma unroll
+      for (int e = 1; e < DPL; ++e) d = __fmaf_rn(qh[e], k[e], d);
+      P[i] = d;
+    }
+  }
+#pragma unroll
+  for (int o = 16, m = 16; o >= 2; o >>= 1, m >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < m / 2; ++i) {
+      const float send = up ? P[i] : P[i + m / 2];
+      const float keep = up ? P[i + m / 2] : P[i];
+      P[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+    }
+  }
+  return __fadd_rn(P[0], __shfl_xor_sync(0xffffffffu, P[0], 1));
+}
+
+// Tile t of KV group g, after attn_tile_stage0 for it: the partials of every
+// query head of the group. The shared scratch holds gqa * T floats (scores,
+// then weights) and attn_sm_floats more; K and V pass through st in chunks
+// of st.ch rows. q and the newest row are read here (they may come from the
+// work just before).
+template <int DPL, bool F16>
+FOX_DEV void attn_tile_t(const TileArgs& a, const TileStage& st, int g, int t, float* sc, float* sm) {
   const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
   const int T = attn_tile_len(a.P, a.nt);
   const int j0 = t * T, n = min(T, a.P - j0);
   const int hd = a.hd, gqa = a.gqa;
-  const bool f16 = a.f16 != 0;
-  const size_t head = (size_t)g * a.n_ctx * hd;
+  const int rb = hd * (F16 ? 2 : 4);
+  const uint8_t* kh = reinterpret_cast<const uint8_t*>(a.kc) + (size_t)g * a.n_ctx * rb;
+  const uint8_t* vh = reinterpret_cast<const uint8_t*>(a.vc) + (size_t)g * a.n_ctx * rb;
+  const int newest = a.P - 1;
   float qv[LOOP_MAX_GQA][DPL];
 #pragma unroll
   for (int h = 0; h < LOOP_MAX_GQA; ++h)
 #pragma unroll
     for (int i = 0; i < DPL; ++i)
       qv[h][i] = h < gqa ? __ldcg(a.q + ((size_t)g * gqa + h) * hd + lane * DPL + i) : 0.0f;
-  for (int j = warp; j < n; j += nw) {
-    float k[DPL];
-    load_row<DPL>(a.kc, f16, head + (size_t)(j0 + j) * hd + lane * DPL, k);
-#pragma unroll
-    for (int h = 0; h < LOOP_MAX_GQA; ++h) {
-      if (h >= gqa) break;
-      float d = __fmul_rn(qv[h][0], k[0]);
-#pragma unroll
-      for (int i = 1; i < DPL; ++i) d = __fmaf_rn(qv[h][i], k[i], d);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
-      if (lane == 0) sc[h * T + j] = __fmul_rn(d, a.scale);
+  // the newest row into the first chunk (staging left it out)
+  auto newest_row = [&](uint8_t* buf, const uint8_t* src) {
+    if (newest >= j0 && newest < j0 + min(n, st.ch))
+      for (int i = tid; i < (rb >> 2); i += nth)
+        reinterpret_cast<uint32_t*>(buf + (size_t)(newest - j0) * rb)[i] =
+            __ldcg(reinterpret_cast<const unsigned int*>(src + (size_t)newest * rb) + i);
+  };
+  for (int c0 = j0; c0 < j0 + n; c0 += st.ch) {
+    const int c1 = min(j0 + n, c0 + st.ch), cn = c1 - c0;
+    if (c0 == j0) {
+      cp_async_wait_one();  // chunk 0's K (its V may still be in flight)
+      newest_row(st.k, kh);
+    } else {
+      stage_rows(st.k, kh, rb, c0, c1, -1);
+      cp_async_wait_all();
     }
+    __syncthreads();
+    // tasks: (group of 16 rows, query head)
+    const int groups = (cn + 15) >> 4;
+    for (int task = warp; task < groups * gqa; task += nw) {
+      const int r0 = (task / gqa) * 16, h = task - (task / gqa) * gqa;
+      float qh[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        qh[i] = qv[0][i];
+#pragma unroll
+        for (int hh = 1; hh < LOOP_MAX_GQA; ++hh)
+          if (hh == h) qh[i] = qv[hh][i];
+      }
+      const float d = dot16<DPL, F16>(st.k, r0, cn - r0, hd, qh, lane);
+      const int r = r0 + (lane >> 1);
+      if (!(lane & 1) && r < cn) sc[h * T + (c0 - j0) + r] = __fmul_rn(d, a.scale);
+    }
+    __syncthreads();  // the buffer is refilled by the next chunk
   }
-  __syncthreads();
   float* s_m = sm;          // [gqa]
   float* s_l = sm + 32;     // [gqa]
-  if (warp < gqa) {
+  for (int h = warp; h < gqa; h += nw) {
     float mx = -CUDART_INF_F;
-    for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sc[warp * T + j]);
+    for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sc[h * T + j]);
     mx = warp_max(mx);
-    if (lane == 0) s_m[warp] = mx;
+    if (lane == 0) s_m[h] = mx;
   }
   __syncthreads();
   for (int i = tid; i < gqa * n; i += nth) {
@@ -250,22 +378,41 @@ FOX_DEV void attn_tile(const TileArgs& a, int g, int t, float* sc, float* sm) {
     for (int j = 0; j < n; ++j) l = __fadd_rn(l, sc[tid * T + j]);
     s_l[tid] = l;
   }
-  float* part = a.part + ((size_t)g * a.nt + t) * gqa * (hd + 2);
-  // one thread per dimension holds every head's sum: each V element is read once
-  for (int d = tid; d < hd; d += nth) {
-    float o[LOOP_MAX_GQA];
+  // thread (d, hg) holds the sums of heads hg, hg + hgs, ...: each in order
+  const int hgs = max(1, min(gqa, nth / hd));
+  const int d = tid % hd, hg = tid / hd;
+  const bool sums = hg < hgs;
+  float o[LOOP_MAX_GQA];
 #pragma unroll
-    for (int h = 0; h < LOOP_MAX_GQA; ++h) o[h] = 0.0f;
-#pragma unroll 4
-    for (int j = 0; j < n; ++j) {
-      const float v = load_elem(a.vc, f16, head + (size_t)(j0 + j) * hd + d);
-#pragma unroll
-      for (int h = 0; h < LOOP_MAX_GQA; ++h)
-        if (h < gqa) o[h] = __fmaf_rn(sc[h * T + j], v, o[h]);
+  for (int h = 0; h < LOOP_MAX_GQA; ++h) o[h] = 0.0f;
+  for (int c0 = j0; c0 < j0 + n; c0 += st.ch) {
+    const int c1 = min(j0 + n, c0 + st.ch), cn = c1 - c0;
+    if (c0 == j0) {
+      cp_async_wait_all();
+      newest_row(st.v, vh);
+    } else {
+      __syncthreads();
+      stage_rows(st.v, vh, rb, c0, c1, -1);
+      cp_async_wait_all();
     }
+    __syncthreads();
+    if (sums) {
+      const float* e = sc + (c0 - j0);
+#pragma unroll 4
+      for (int j = 0; j < cn; ++j) {
+        const float v = F16 ? __half2float(reinterpret_cast<const __half*>(st.v)[(size_t)j * hd + d])
+                            : reinterpret_cast<const float*>(st.v)[(size_t)j * hd + d];
+#pragma unroll
+        for (int h = 0; h < LOOP_MAX_GQA; ++h)
+          if (h < gqa && h % hgs == hg) o[h] = __fmaf_rn(e[h * T + j], v, o[h]);
+      }
+    }
+  }
+  float* part = a.part + ((size_t)g * a.nt + t) * gqa * (hd + 2);
+  if (sums) {
 #pragma unroll
     for (int h = 0; h < LOOP_MAX_GQA; ++h)
-      if (h < gqa) __stcg(part + (size_t)h * (hd + 2) + d, o[h]);
+      if (h < gqa && h % hgs == hg) __stcg(part + (size_t)h * (hd + 2) + d, o[h]);
   }
   __syncthreads();
   if (tid < gqa) {
@@ -274,12 +421,20 @@ FOX_DEV void attn_tile(const TileArgs& a, int g, int t, float* sc, float* sm) {
   }
 }
 
+template <int DPL>
+FOX_DEV void attn_tile(const TileArgs& a, const TileStage& st, int g, int t, float* sc, float* sm) {
+  if (a.f16) attn_tile_t<DPL, true>(a, st, g, t, sc, sm);
+  else attn_tile_t<DPL, false>(a, st, g, t, sc, sm);
+}
+
+constexpr int MERGE_BATCH = 32;  // tile partials a merging thread requests at once
+
 // After attn_tile: the CTA that completes KV group g's last tile merges all
 // its tiles into the output (and publishes the absmax of what it wrote).
-// The scratch holds 3 * nt * gqa + 2 * gqa floats.
+// The scratch holds attn_sm_floats(nt, gqa) floats.
 FOX_DEV void attn_merge_tiles(const TileArgs& a, int g, float* sm, float* red) {
   __shared__ int last_sh;
-  const int tid = threadIdx.x, nth = blockDim.x;
+  const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
   const int hd = a.hd, gqa = a.gqa;
   const int T = attn_tile_len(a.P, a.nt), nt = (a.P + T - 1) / T;
   __threadfence();
@@ -294,16 +449,25 @@ FOX_DEV void attn_merge_tiles(const TileArgs& a, int g, float* sm, float* red) {
   float* s_w = sm + 2 * a.nt * gqa;     // [nt][gqa]
   float* s_M = sm + 3 * a.nt * gqa;     // [gqa]
   float* s_L = s_M + gqa;               // [gqa]
+  // the first batch of this thread's first (head, dimension) partials is
+  // requested with the small values
+  const int h0 = tid / hd, d0 = tid - h0 * hd;
+  const bool first = tid < gqa * hd;
+  float ov[MERGE_BATCH];
+#pragma unroll
+  for (int t = 0; t < MERGE_BATCH; ++t)
+    ov[t] = (first && t < nt) ? __ldcg(base + ((size_t)t * gqa + h0) * (hd + 2) + d0) : 0.0f;
   for (int i = tid; i < nt * gqa; i += nth) {
     const float* pt = base + (size_t)i * (hd + 2);
     s_m[i] = __ldcg(pt + hd);
     s_l[i] = __ldcg(pt + hd + 1);
   }
   __syncthreads();
-  if (tid < gqa) {
+  for (int h = warp; h < gqa; h += nw) {
     float M = -CUDART_INF_F;
-    for (int t = 0; t < nt; ++t) M = fmaxf(M, s_m[t * gqa + tid]);
-    s_M[tid] = M;
+    for (int t = lane; t < nt; t += 32) M = fmaxf(M, s_m[t * gqa + h]);
+    M = warp_max(M);
+    if (lane == 0) s_M[h] = M;
   }
   __syncthreads();
   for (int i = tid; i < nt * gqa; i += nth) s_w[i] = expf_cr(__fsub_rn(s_m[i], s_M[i % gqa]));
@@ -318,8 +482,16 @@ FOX_DEV void attn_merge_tiles(const TileArgs& a, int g, float* sm, float* red) {
   for (int i = tid; i < gqa * hd; i += nth) {
     const int h = i / hd, d = i - h * hd;
     float O = 0.0f;
-    for (int t = 0; t < nt; ++t)
-      O = __fmaf_rn(__ldcg(base + ((size_t)t * gqa + h) * (hd + 2) + d), s_w[t * gqa + h], O);
+    for (int t0 = 0; t0 < nt; t0 += MERGE_BATCH) {
+      if (i != tid || t0 > 0) {
+#pragma unroll
+        for (int t = 0; t < MERGE_BATCH; ++t)
+          ov[t] = t0 + t < nt ? __ldcg(base + ((size_t)(t0 + t) * gqa + h) * (hd + 2) + d) : 0.0f;
+      }
+#pragma unroll
+      for (int t = 0; t < MERGE_BATCH; ++t)
+        if (t0 + t < nt) O = __fmaf_rn(ov[t], s_w[(t0 + t) * gqa + h], O);
+    }
     const float v = __fdiv_rn(O, s_L[h]);
     __stcg(a.out + ((size_t)g * gqa + h) * hd + d, v);
     am = absmax_acc(am, v);
@@ -379,11 +551,17 @@ FOX_DEV void attn_exact_head(const TileArgs& a, int h, float* att, float* red, f
 // Standalone tile attention (AttnParams, ops.cuh): grid (nt, n_kv, n_seq).
 // Sequence z reads its position at *pos_list[z] (or *pos), its q and output
 // at z * seq_stride, its caches at k_list[z] / v_list[z] + layer_off (or
-// kcache / vcache), and uses the partials and counters of slot z.
+// kcache / vcache), and uses the partials and counters of slot z. Under
+// programmatic launch (the decode step, right after the q|k|v kernel that
+// writes q and position P - 1) the older rows of the first chunk are staged
+// before griddepcontrol.wait; q and the newest row are read after it.
+constexpr int ATTN_STAGE_ROWS = 64;  // K/V rows per staged chunk of the standalone kernel
+
 template <int DPL>
 __global__ void __launch_bounds__(256, 1) attention_tile_kernel(const AttnParams k) {
   extern __shared__ __align__(16) float tsm[];
   __shared__ float red[32];
+  griddep_launch_dependents();  // the o projection may start streaming its weights
   const int t = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
   const int gqa = k.n_head / k.n_kv;
   TileArgs a;
@@ -399,16 +577,25 @@ __global__ void __launch_bounds__(256, 1) attention_tile_kernel(const AttnParams
   a.scale = k.scale;
   const int T = attn_tile_len(a.P, a.nt);
   if (t * T >= a.P) return;
-  float* sc = tsm;                       // gqa * T
-  float* sm = tsm + (size_t)gqa * T;     // max(64, 3 * nt * gqa + 2 * gqa)
-  attn_tile<DPL>(a, g, t, sc, sm);
+  const int Tmax = attn_tile_len(k.n_ctx, k.nt);
+  float* sc = tsm;                                   // gqa * Tmax
+  float* sm = tsm + (size_t)gqa * Tmax;              // attn_sm_floats
+  TileStage st;
+  st.ch = ATTN_STAGE_ROWS;
+  st.k = reinterpret_cast<uint8_t*>(sm + attn_sm_floats(k.nt, gqa));
+  st.v = st.k + (size_t)st.ch * k.hd * (k.kv_f16 ? 2 : 4);
+  attn_tile_stage0(a, st, g, t);
+  griddep_wait();
+  attn_tile<DPL>(a, st, g, t, sc, sm);
+  __syncthreads();
   attn_merge_tiles(a, g, sm, red);
 }
 
 // Shared memory of attention_tile_kernel for contexts of n_ctx positions.
-inline size_t attn_tile_smem_bytes(int n_ctx, int nt, int gqa) {
+inline size_t attn_tile_smem_bytes(int n_ctx, int nt, int gqa, int hd, int kv_f16) {
   const int T = attn_tile_len(n_ctx, nt);
-  return ((size_t)gqa * T + (size_t)std::max(64, 3 * nt * gqa + 2 * gqa)) * 4;
+  return ((size_t)gqa * T + (size_t)attn_sm_floats(nt, gqa)) * 4 +
+         2 * (size_t)ATTN_STAGE_ROWS * hd * (kv_f16 ? 2 : 4);
 }
 
 // ---- the persistent decode step --------------------------------------------
@@ -715,6 +902,15 @@ __global__ void __launch_bounds__(LOOP_THREADS, 1) loop_kernel(const LoopParams 
   const int T = attn_tile_len(P, p.attn_nt), n_tiles = (P + T - 1) / T;
   const int n_items = p.attn_exact ? p.n_head : p.n_kv * n_tiles;
   const int n_att_slots = p.attn_exact ? p.n_head : p.n_kv;
+  // the attention's shared memory (aliases xq, part and vals, idle then):
+  // scores, small scratch, then the staged K and V chunks
+  const int T_max = attn_tile_len(p.n_ctx, p.attn_nt);
+  float* a_sc = s.scr;
+  float* a_sm = a_sc + (size_t)gqa * T_max;
+  TileStage st;
+  st.ch = p.attn_ch;
+  st.k = reinterpret_cast<uint8_t*>(a_sm + attn_sm_floats(p.attn_nt, gqa));
+  st.v = st.k + (size_t)st.ch * p.hd * (p.kv_f16 ? 2 : 4);
 
   // the embedding (upstream src/forward.c:259-293), computed by every CTA for
   // its first prologue; CTA 0 also stores it as the residual
@@ -754,22 +950,25 @@ __global__ void __launch_bounds__(LOOP_THREADS, 1) loop_kernel(const LoopParams 
     }
     float sc = pro_norm(p, s, xv, nwv, p.n_embd);
     if (!(ok = loop_gemv<LE_QKV>(p, s, L.m[LM_QKV], sc, l, nullptr, nullptr))) break;
+    // the older K/V rows of this CTA's first tile move while the others finish
+    ta.kc = L.kc;
+    ta.vc = L.vc;
+    if (!p.attn_exact && cta < n_items) attn_tile_stage0(ta, st, cta / n_tiles, cta % n_tiles);
     if (!(ok = loop_barrier(p, s))) break;
     // every CTA has read the base by now: the next launch starts after this
     // launch's 5 * n_layer - 1 barriers
     if (l == 0 && cta == 0 && tid == 0) p.bar[1] = s.base + (unsigned)((5 * p.n_layer - 1) * G);
 
     // ---- attention
-    ta.kc = L.kc;
-    ta.vc = L.vc;
     for (int it = cta; it < n_items; it += G) {
       if (p.attn_exact) {
         attn_exact_head(ta, it, s.scr, s.red + 64, s.red + 96);
       } else {
         const int g = it / n_tiles, t = it - g * n_tiles;
-        float* sm = s.scr + (size_t)gqa * T;
-        attn_tile<DPL>(ta, g, t, s.scr, sm);
-        attn_merge_tiles(ta, g, sm, s.red + 64);
+        if (it != cta) attn_tile_stage0(ta, st, g, t);
+        attn_tile<DPL>(ta, st, g, t, a_sc, a_sm);
+        __syncthreads();
+        attn_merge_tiles(ta, g, a_sm, s.red + 64);
       }
       __syncthreads();
     }
@@ -803,6 +1002,7 @@ __global__ void __launch_bounds__(LOOP_THREADS, 1) loop_kernel(const LoopParams 
     sc = pro_vec(s, p.h, p.n_ff, p.amax_h, G);
     if (!(ok = loop_gemv<LE_ADD>(p, s, L.m[LM_DOWN], sc, l, p.trace, nullptr))) break;
   }
+  cp_async_wait_all();
   if (!ok) drain_copies(p, s);
 }
 

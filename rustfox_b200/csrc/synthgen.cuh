@@ -48,8 +48,8 @@ FOX_DEV void sg_put16(uint8_t* p, uint16_t v) {
   p[1] = (uint8_t)(v >> 8);
 }
 
-// one block of `type` (TQ1_0, TQ2_0, Q8_0, Q4_K, Q6_K) at o, block index b
-FOX_DEV void sg_block(int type, uint8_t* o, uint64_t b, uint64_t seed, double sigma) {
+// one block of `type` (TQ1_0, TQ2_0, Q8_0, Q4_K, Q6_K) into o, block index b
+FOX_DEV void sg_block_local(int type, uint8_t* o, uint64_t b, uint64_t seed, double sigma) {
   double z0, z1;
   if (type == T_TQ1_0) {
     // five uniform trits per qs byte (a uniform value in [0, 243)), four per
@@ -101,10 +101,18 @@ FOX_DEV void sg_block(int type, uint8_t* o, uint64_t b, uint64_t seed, double si
   }
 }
 
+// The block is formed in a local array and then stored byte by byte: storing
+// the fp16 scale straight into the block's global bytes lost its low byte on
+// the device (measured: the high byte right, the low byte zero), while the
+// same value formed locally is right.
 __global__ void synth_fill_kernel(int type, uint8_t* out, long n_blocks, int block_bytes, uint64_t seed,
                                   double sigma) {
-  for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < n_blocks; b += (long)gridDim.x * blockDim.x)
-    sg_block(type, out + b * block_bytes, (uint64_t)b, seed, sigma);
+  for (long b = blockIdx.x * (long)blockDim.x + threadIdx.x; b < n_blocks; b += (long)gridDim.x * blockDim.x) {
+    uint8_t blk[224];
+    sg_block_local(type, blk, (uint64_t)b, seed, sigma);
+    uint8_t* o = out + b * block_bytes;
+    for (int i = 0; i < block_bytes; ++i) o[i] = blk[i];
+  }
 }
 
 }  // namespace fox

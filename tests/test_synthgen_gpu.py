@@ -2,10 +2,7 @@
 Model.from_synthetic_device) against the numpy restatement of the generator
 (synthgen_mirror.py) uploaded from the host: the same logits bit for bit,
 the same greedy tokens, and the same device bytes (their device images are
-equal). Not collected yet (the file name does not start with test_): it has
-not run on a B200. Run it with
-    python -m pytest tests/pending_synthgen_gpu.py -q
-and rename it to test_synthgen_gpu.py once it passes there.
+equal).
 """
 import numpy as np
 import pytest

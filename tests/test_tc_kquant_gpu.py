@@ -1,8 +1,5 @@
 """The K-quant tensor-core pass (foxcuda_gemm_kq_i8, tcgen05 kind::i8 on
-Q4_K and Q6_K) against the oracle, bit for bit. Not collected yet (the file
-name does not start with test_): it has not run on a B200. Run it with
-    python -m pytest tests/pending_tc_kquant_gpu.py -q
-and rename it to test_tc_kquant_gpu.py once it passes there.
+Q4_K and Q6_K) against the oracle, bit for bit.
 
 Upstream's forward_batch runs one K-quant GEMV per token (src/forward.c:
 188-213, src/kernels.c:571-805), each token quantised with one scale per 256

@@ -1,8 +1,5 @@
 """The split form of the tensor-core pass (foxcuda_gemm_tq2_i8_split) against
-the oracle and the unsplit pass, bit for bit. Not collected yet (the file
-name does not start with test_): it has not run on a B200. Run it with
-    python -m pytest tests/pending_tc_split_gpu.py -q
-and rename it to test_tc_split_gpu.py once it passes there.
+the oracle and the unsplit pass, bit for bit.
 
 Upstream's forward_batch runs one fox_gemv_tq{1,2}_i8 per token
 (src/forward.c:188-213); the split pass must give each token that GEMV's row.
