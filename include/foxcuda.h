@@ -154,7 +154,7 @@ foxcuda_status foxcuda_dequant_row(int ggml_type, const void *row, size_t n, flo
  * stream-ordered. */
 /* The tile target of the tile attention (no upstream counterpart; upstream
  * attends serially, src/forward.c:222-257): the positions 0..P-1 are cut into
- * tiles of T = 32 * ceil(ceil(P / nt) / 32) and merged in tile order. A model
+ * tiles of T = ceil(P / nt) and merged in tile order; nt is at most 8. A model
  * uses the value for its device and its whole model's KV heads on every
  * path (decode step, prompt chunks, batches, tensor-parallel shards). */
 int foxcuda_attn_tile_target(int device, uint32_t n_head_kv);
@@ -458,8 +458,7 @@ foxcuda_status foxcuda_tp_p2p_pick(foxcuda_context *c);
 /* Launch kinds of a decode step */
 enum {
     FOXCUDA_K_EMBED = 0, FOXCUDA_K_QKV, FOXCUDA_K_ATTN, FOXCUDA_K_O, FOXCUDA_K_GATEUP,
-    FOXCUDA_K_DOWN, FOXCUDA_K_ADVANCE, FOXCUDA_K_HEAD, FOXCUDA_K_PICK,
-    FOXCUDA_K_LOOP  /* the persistent step: every layer of a token in one launch */
+    FOXCUDA_K_DOWN, FOXCUDA_K_ADVANCE, FOXCUDA_K_HEAD, FOXCUDA_K_PICK
 };
 
 /* One decode step of `token` (plus a pick when s is not NULL) run launch by
@@ -470,9 +469,9 @@ foxcuda_status foxcuda_context_profile(foxcuda_context *c, foxcuda_sampler *s, u
                                        float *us, int *kinds, int cap, int *n_out);
 
 /* Average device time of one launch of a layer GEMV kind (QKV, O, GATEUP,
- * DOWN or HEAD), or of the persistent step (LOOP, all layers), over `reps`
- * back-to-back launches on the context's stream, cycling through the layers
- * so the weights stream from HBM, and the GGUF weight bytes one launch reads. Overwrites the context's activations and the
+ * DOWN or HEAD) over `reps` back-to-back launches on the context's stream,
+ * cycling through the layers so the weights stream from HBM, and the GGUF
+ * weight bytes one launch reads. Overwrites the context's activations and the
  * cache slot at the current position: reset the context before decoding. */
 foxcuda_status foxcuda_context_bench_kernel(foxcuda_context *c, int kind, int reps,
                                             double *us_per_launch,

@@ -642,11 +642,11 @@ static float kv_round(const or_ctx *c, float v)
     return c->kv_mode ? or_f16_to_f32(or_f32_to_f16_rne(v)) : v;
 }
 
-/* libfoxcuda's tile attention (rustfox_b200/csrc/loop.cuh) for one query head
+/* libfoxcuda's tile attention (rustfox_b200/csrc/attn.cuh) for one query head
  * over positions 0..P-1 of one KV head (rows `stride` floats apart). This is
  * not upstream's order; it is the production mode of the device, restated so
  * that mode is checked bit for bit. Positions are cut into tiles of
- * T = 32 * ceil(ceil(P / nt) / 32). Per tile: every score is the sum of 32
+ * T = ceil(P / nt). Per tile: every score is the sum of 32
  * lane partials (hd/32 dimensions each: q0*k0, then fmaf in dimension order)
  * by an xor butterfly, times scale; the tile's max; e = exp(s - max); the sum
  * of e in ascending order; and per dimension fmaf(e, v, .) in ascending
@@ -656,8 +656,8 @@ static void tile_attention_into(const float *qh, const float *K, const float *V,
                                 size_t hd, size_t P, int nt_target, float scale, float *out,
                                 float *sc, float *tile_o)
 {
-    const size_t nt = (size_t)nt_target, per = (P + nt - 1) / nt;
-    const size_t T = (per + 31) / 32 * 32, ntl = (P + T - 1) / T, dpl = hd / 32;
+    const size_t nt = (size_t)nt_target, T = (P + nt - 1) / nt;
+    const size_t ntl = (P + T - 1) / T, dpl = hd / 32;
     float m[64], l[64], w[64], M = -INFINITY, L = 0.0f;
     size_t t, j, d, i, lane, off;
     for (t = 0; t < ntl; t++) {

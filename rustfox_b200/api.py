@@ -143,7 +143,7 @@ _PROTOS = {
     "foxcuda_context_sync_position": (_st, [_vp]),
 }
 
-KIND_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "advance", "head", "pick", "loop"]
+KIND_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "advance", "head", "pick"]
 
 _lib = None
 

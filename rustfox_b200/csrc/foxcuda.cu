@@ -23,7 +23,7 @@
 #include "tc_kquant.cuh"
 #include "prefill.cuh"
 #include "p2p.cuh"
-#include "loop.cuh"
+#include "attn.cuh"
 #include "synthgen.cuh"
 
 using namespace fox;
@@ -763,13 +763,16 @@ extern "C" foxcuda_status foxcuda_dequant_row(int type, const void* row, size_t 
 
 static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t s, bool pdl = false);
 
-// Tile target of the tile attention (loop.cuh): about one tile per SM over
-// all KV heads. Every path of a model (the persistent step, prompt chunks,
-// batches, tensor-parallel shards) uses the whole model's value, so they all
-// cut the positions into the same tiles.
+// Tile target of the tile attention (attn.cuh): about one tile per SM over
+// all KV heads, at most one portable cluster (8) per KV head. Every path of
+// a model (the decode step, prompt chunks, batches, tensor-parallel shards)
+// uses the whole model's value, so they all cut the positions into the same
+// tiles.
 static int attn_nt_for(int sms, int n_kv_full) {
   return std::max(1, std::min(ATTN_TILE_MAX, sms / std::max(1, n_kv_full)));
 }
+// K/V rows per staged chunk: 64 KB of shared memory for K and V together.
+static int attn_stage_rows(int kv_f16) { return kv_f16 ? 128 : 64; }
 
 extern "C" int foxcuda_attn_tile_target(int device, uint32_t n_head_kv) {
   return attn_nt_for(sm_count(device), (int)n_head_kv);
@@ -790,12 +793,9 @@ extern "C" foxcuda_status foxcuda_attention(const float* q, const void* kcache, 
   if (exact && n_ctx > 16384) return fail(FOXCUDA_ERR_UNSUPPORTED, "attention: exact mode holds 16384 positions");
   cudaStream_t s = (cudaStream_t)stream;
   const int nt = attn_nt_for(current_sms(), (int)n_head_kv);
-  const int gqa = (int)(n_head / n_head_kv);
-  const size_t part_bytes = (size_t)n_head_kv * nt * gqa * (head_dim + 2) * 4;
   void* scratch = nullptr;
-  CK(cudaMallocAsync(&scratch, 256 + part_bytes, s), "attention scratch");
+  CK(cudaMallocAsync(&scratch, 256, s), "attention scratch");
   int* pos_dev = (int*)scratch;
-  unsigned* cnt = (unsigned*)((uint8_t*)scratch + 16);
   cudaError_t e = cudaMemsetAsync(scratch, 0, 256, s);
   const int p32 = (int)pos;
   if (e == cudaSuccess) e = cudaMemcpyAsync(pos_dev, &p32, 4, cudaMemcpyHostToDevice, s);
@@ -804,8 +804,7 @@ extern "C" foxcuda_status foxcuda_attention(const float* q, const void* kcache, 
     AttnParams ap{};
     ap.q = q; ap.kcache = kcache; ap.vcache = vcache; ap.kv_f16 = kv_type == FOXCUDA_KV_F16;
     ap.n_ctx = (int)n_ctx; ap.hd = (int)head_dim; ap.n_head = (int)n_head; ap.n_kv = (int)n_head_kv;
-    ap.nt = nt; ap.pos = pos_dev; ap.out = out;
-    ap.part = (float*)((uint8_t*)scratch + 256); ap.counters = cnt;
+    ap.nt = nt; ap.stage_rows = attn_stage_rows(ap.kv_f16); ap.pos = pos_dev; ap.out = out;
     ap.scale = 1.0f / sqrtf((float)head_dim);
     e = run_attention(ap, exact != 0, s);
   }
@@ -1761,8 +1760,6 @@ struct foxcuda_context {
   int* err_dev = nullptr;
   uint32_t* tokens_dev = nullptr;  // prompt staging
   size_t tokens_cap = 0;
-  float* attn_part = nullptr;   // tile partials [n_kv][nt][gqa][hd + 2]
-  unsigned* attn_cnt = nullptr;  // [n_kv]
   uint32_t* ring = nullptr;
   float* trace = nullptr;
   bool trace_on = false;
@@ -1785,8 +1782,6 @@ struct foxcuda_context {
   int** pf_pos_list = nullptr;
   void** pf_k_list = nullptr;
   void** pf_v_list = nullptr;
-  float* pf_part = nullptr;     // tile partials of every token of a chunk
-  unsigned* pf_cnt = nullptr;
   float* rows_logits = nullptr;  // foxcuda_eval_all staging, rows_cap x n_vocab
   size_t rows_cap = 0;
   // tensor-parallel exchanges over peer memory (p2p.cuh)
@@ -1800,11 +1795,6 @@ struct foxcuda_context {
   // repeat penalty of the sharded greedy pick (foxcuda_tp_set_penalty)
   SamplerDev* tp_smp = nullptr;
   float tp_penalty = 1.0f;
-  // the persistent decode step (loop.cuh), when the model takes it
-  bool loop = false;
-  LoopParams lp{};
-  size_t loop_smem = 0;
-  int loop_grid = 0;
 };
 
 struct foxcuda_sampler {
@@ -1816,8 +1806,6 @@ struct foxcuda_sampler {
   cudaGraphExec_t g_decode_io = nullptr;  // g_decode with the token copies inside
   uint32_t n_out = 0;  // host mirror of dev->n_out
 };
-
-static cudaError_t loop_setup(foxcuda_context* c);
 
 static cudaError_t ctx_alloc(foxcuda_context* c, size_t bytes, void** p) {
   cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
@@ -1879,8 +1867,6 @@ extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda
   A((size_t)c->n_ctx * half * 4, (void**)&c->rope_sin);
   A(16, (void**)&c->pos_dev);
   A(16, (void**)&c->token_dev);
-  A((size_t)mi.n_head_kv * m->attn_nt * gqa * (mi.head_dim + 2) * 4, (void**)&c->attn_part);
-  A((size_t)mi.n_head_kv * 4, (void**)&c->attn_cnt);
   A((size_t)c->n_ctx * 4, (void**)&c->ring);
   if (e == cudaSuccess) {
     c->err_dev = reinterpret_cast<int*>(c->token_dev + 1);
@@ -1905,7 +1891,6 @@ extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda
   e = cudaMemcpy(c->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(c->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
-  if (e == cudaSuccess) e = loop_setup(c);
   if (e != cudaSuccess) {
     foxcuda_context_destroy(c);
     return cuda_fail(e, "context init");
@@ -1950,7 +1935,7 @@ extern "C" double foxcuda_context_last_eval_seconds(const foxcuda_context* c) {
 // then per layer the fused q|k|v (+RMSNorm, +RoPE, +KV write), attention, o
 // (+residual), gate|up (+RMSNorm, +SwiGLU), down (+residual); pos += 1.
 // Launch kinds of a decode step (diagnostics name them by these numbers).
-enum { PK_EMBED = 0, PK_QKV, PK_ATTN, PK_O, PK_GATEUP, PK_DOWN, PK_ADVANCE, PK_HEAD, PK_PICK, PK_LOOP };
+enum { PK_EMBED = 0, PK_QKV, PK_ATTN, PK_O, PK_GATEUP, PK_DOWN, PK_ADVANCE, PK_HEAD, PK_PICK };
 
 // While a context is being profiled an event follows every launch.
 static void mark(foxcuda_context* c, int kind);
@@ -1973,13 +1958,6 @@ static uint64_t launch_weight_bytes(const foxcuda_model* m, int kind, uint32_t l
     case PK_GATEUP: return gguf_bytes(L.gateup);
     case PK_DOWN: return gguf_bytes(L.down);
     case PK_HEAD: return gguf_bytes(m->output);
-    case PK_LOOP: {  // every layer matrix of the model
-      uint64_t b = 0;
-      for (uint32_t k = 0; k < m->info.n_layer; ++k)
-        for (int i = PK_QKV; i <= PK_DOWN; ++i)
-          if (i != PK_ATTN) b += launch_weight_bytes(m, i, k);
-      return b;
-    }
     default: return 0;
   }
 }
@@ -2033,33 +2011,52 @@ static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
   return cudaSuccess;
 }
 
-// The tile attention (loop.cuh) of n_seq sequences in one launch: grid
-// (nt, n_kv, n_seq); ap.part / ap.counters hold n_seq slots.
-// pdl: launched with programmatic stream serialisation, right after the
-// kernel that writes q and the newest K/V row and nothing else this kernel
-// reads (the decode step's q|k|v GEMV).
-template <int DPL>
-static cudaError_t launch_tile_t(const AttnParams& ap, int n_seq, cudaStream_t s, bool pdl) {
-  const size_t sm = attn_tile_smem_bytes(ap.n_ctx, ap.nt, ap.n_head / ap.n_kv, ap.hd, ap.kv_f16);
+// The tile attention (attn.cuh) of n_seq sequences in one launch: grid
+// (nt, n_kv, n_seq) in clusters of nt CTAs. pdl: launched with programmatic
+// stream serialisation, right after the kernel that writes q and the newest
+// K/V row and nothing else this kernel reads (the decode step's q|k|v GEMV).
+template <int DPL, bool F16, int G>
+static cudaError_t launch_tile_g(const AttnParams& ap, int n_seq, cudaStream_t s, bool pdl) {
+  auto kern = attention_tile_kernel<DPL, F16, G>;
+  const size_t sm = attn_tile_smem_bytes(ap.n_ctx, ap.nt, G, ap.hd, F16 ? 1 : 0, ap.stage_rows);
   static size_t marks[kMaxDevices] = {};
-  cudaError_t e = opt_in_smem(attention_tile_kernel<DPL>, sm, marks);
+  cudaError_t e = opt_in_smem(kern, sm, marks);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ap.nt, ap.n_kv, n_seq);
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = sm;
   cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = ap.nt;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attention_tile_kernel<DPL>, ap);
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, ap);
+}
+
+template <int DPL, bool F16>
+static cudaError_t launch_tile_f(const AttnParams& ap, int n_seq, cudaStream_t s, bool pdl) {
+  switch (ap.n_head / ap.n_kv) {
+    case 1: return launch_tile_g<DPL, F16, 1>(ap, n_seq, s, pdl);
+    case 2: return launch_tile_g<DPL, F16, 2>(ap, n_seq, s, pdl);
+    case 4: return launch_tile_g<DPL, F16, 4>(ap, n_seq, s, pdl);
+    case 8: return launch_tile_g<DPL, F16, 8>(ap, n_seq, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int DPL>
+static cudaError_t launch_tile_t(const AttnParams& ap, int n_seq, cudaStream_t s, bool pdl) {
+  return ap.kv_f16 ? launch_tile_f<DPL, true>(ap, n_seq, s, pdl) : launch_tile_f<DPL, false>(ap, n_seq, s, pdl);
 }
 
 static cudaError_t launch_tiles(const AttnParams& ap, int n_seq, cudaStream_t s, bool pdl = false) {
   switch (ap.hd / 32) {
-    case 1: return launch_tile_t<1>(ap, n_seq, s, pdl);
     case 2: return launch_tile_t<2>(ap, n_seq, s, pdl);
     case 4: return launch_tile_t<4>(ap, n_seq, s, pdl);
     case 8: return launch_tile_t<8>(ap, n_seq, s, pdl);
@@ -2085,7 +2082,7 @@ static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
   ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
   ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
   ap.hd = mi.head_dim; ap.n_head = c->m->loc.n_head; ap.n_kv = c->m->loc.n_head_kv; ap.nt = c->m->attn_nt;
-  ap.pos = c->pos_dev; ap.out = c->att; ap.part = c->attn_part; ap.counters = c->attn_cnt;
+  ap.stage_rows = attn_stage_rows(c->kv_f16); ap.pos = c->pos_dev; ap.out = c->att;
   ap.scale = 1.0f / sqrtf((float)mi.head_dim);
   // the single-GPU step overlaps the q|k|v kernel; a tensor-parallel step
   // keeps plain stream order
@@ -2160,191 +2157,10 @@ static cudaError_t launch_head_on(foxcuda_context* c, cudaStream_t s, bool pdl) 
 
 static cudaError_t launch_head(foxcuda_context* c) { return launch_head_on(c, c->stream, ctx_pdl(c)); }
 
-// ---------------------------------------------------------------------------
-// the persistent decode step (loop.cuh)
-
-// FOXCUDA_LOOP=0 keeps the launch-per-kernel decode step (for comparison).
-static bool loop_wanted() {
-  static const bool on = [] {
-    const char* v = getenv("FOXCUDA_LOOP");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
-static bool loop_mat(const PackedMat& W, int K, LoopMat* out) {
-  if (W.type != T_TQ2_0 || !W.slice || W.K != K || W.U <= 0 || (W.U & (W.U - 1)) || W.n_rows % W.U ||
-      W.nb > LOOP_PAIRS)
-    return false;
-  LoopMat& M = *out;
-  M.w = W.dev;
-  M.n_rows = W.n_rows;
-  M.nb = W.nb;
-  M.U = W.U;
-  M.ushift = __builtin_ctz((unsigned)W.U);
-  M.units = W.n_rows / W.U;
-  M.unit_bytes = W.U * W.nb * block_bytes(T_TQ2_0);
-  M.per = 0;
-  M.piece_units = 0;
-  return true;
-}
-
-// Pieces of at most slot_bytes, balanced over the CTA's run.
-static void loop_pieces(LoopMat& M, int grid, int slot_bytes) {
-  M.per = (M.units + grid - 1) / grid;
-  const int fit = std::max(1, slot_bytes / M.unit_bytes);
-  const int np = (M.per + fit - 1) / fit;
-  M.piece_units = (M.per + np - 1) / np;
-}
-
-// Decides whether the context takes the persistent step and lays out its
-// shared memory. A model it does not cover keeps the launch-per-kernel step.
-static cudaError_t loop_setup(foxcuda_context* c) {
-  foxcuda_model* m = c->m;
-  const foxcuda_model_info& mi = m->info;
-  if (!loop_wanted() || m->tp_size != 1 || c->tp_steps) return cudaSuccess;
-  const int hd = mi.head_dim, gqa = mi.n_head / mi.n_head_kv;
-  const int nq = mi.n_head * hd, nkv = mi.n_head_kv * hd;
-  if (mi.n_embd > 4 * LOOP_MAX_KR * LOOP_THREADS || gqa > LOOP_MAX_GQA || (hd != 64 && hd != 128))
-    return cudaSuccess;
-  std::vector<LoopLayer> layers(mi.n_layer);
-  for (uint32_t l = 0; l < mi.n_layer; ++l) {
-    const LayerW& L = m->layers[l];
-    if (L.n_qkv != 1 || L.qkv[0].n_rows != nq + 2 * nkv) return cudaSuccess;
-    LoopLayer& Y = layers[l];
-    if (!loop_mat(L.qkv[0], mi.n_embd, &Y.m[LM_QKV]) || !loop_mat(L.o, nq, &Y.m[LM_O]) ||
-        !loop_mat(L.gateup, mi.n_embd, &Y.m[LM_GU]) || !loop_mat(L.down, mi.n_ff, &Y.m[LM_DOWN]))
-      return cudaSuccess;
-    Y.attn_norm = L.attn_norm;
-    Y.ffn_norm = L.ffn_norm;
-    Y.kc = kv_layer(c, c->kc, l);
-    Y.vc = kv_layer(c, c->vc, l);
-  }
-  int dev_max = 0, sms = sm_count(m->device);
-  cudaError_t e = cudaDeviceGetAttribute(&dev_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
-  if (e) return e;
-  // shared memory: ring | xq | part | vals (the attention scratch aliases
-  // xq..vals) | mbarriers | reduction scratch
-  const int nb_max = (int)std::max<uint32_t>(mi.n_embd, std::max<uint32_t>(nq, mi.n_ff)) / 256;
-  const size_t xq = (size_t)nb_max * XQ_STRIDE;
-  const int nt = m->attn_nt;
-  // staged K/V chunks of the attention: 64 rows of fp16, 32 of fp32
-  const int ch = c->kv_f16 ? 64 : 32;
-  const size_t attn = c->attn_exact ? (size_t)c->n_ctx * 4
-                                    : ((size_t)gqa * attn_tile_len((int)c->n_ctx, nt) +
-                                       (size_t)attn_sm_floats(nt, gqa)) * 4 +
-                                          2 * (size_t)ch * hd * (c->kv_f16 ? 2 : 4);
-  const size_t fixed = 512 /* reduction */ + 4 * 8 /* mbarriers */ + 1024 /* static and alignment */;
-  int n_slots = 4;
-  int slot = 0;
-  size_t part = 0, vals = 0, scr = 0;
-  for (; n_slots >= 2; --n_slots) {
-    // the part/vals sizes depend on the pieces, which depend on the slot:
-    // take the slot that leaves room for them
-    for (slot = (int)((dev_max - fixed - std::max(xq, attn)) / n_slots) / 128 * 128; slot >= 8192;
-         slot -= 1024) {
-      size_t rows = 0, pbytes = 0;
-      for (LoopLayer& Y : layers)
-        for (LoopMat& M : Y.m) {
-          loop_pieces(M, sms, slot);
-          const size_t r = (size_t)M.piece_units * M.U;
-          rows = std::max(rows, r);
-          pbytes = std::max(pbytes, r * (M.nb + 1) * 4);
-        }
-      part = (pbytes + 15) / 16 * 16;
-      vals = (rows * 4 + 15) / 16 * 16;
-      scr = std::max(xq + part + vals, attn);
-      bool fits_units = true;
-      for (LoopLayer& Y : layers)
-        for (LoopMat& M : Y.m) fits_units = fits_units && M.unit_bytes <= slot;
-      if (fits_units && (size_t)n_slots * slot + scr + fixed <= (size_t)dev_max) break;
-    }
-    if (slot >= 8192) break;
-  }
-  if (n_slots < 2 || slot < 8192) return cudaSuccess;
-  for (LoopLayer& Y : layers)
-    for (LoopMat& M : Y.m) loop_pieces(M, sms, slot);
-  LoopParams& p = c->lp;
-  p = LoopParams{};
-  p.n_layer = (int)mi.n_layer; p.n_embd = (int)mi.n_embd; p.n_ff = (int)mi.n_ff; p.hd = hd;
-  p.n_head = (int)mi.n_head; p.n_kv = (int)mi.n_head_kv; p.nq = nq; p.nkv = nkv;
-  p.n_ctx = (int)c->n_ctx; p.kv_f16 = c->kv_f16;
-  p.eps = mi.rms_eps; p.attn_scale = 1.0f / sqrtf((float)hd);
-  p.attn_exact = c->attn_exact; p.attn_nt = nt;
-  p.rope_cos = c->rope_cos; p.rope_sin = c->rope_sin; p.pos = c->pos_dev; p.token = c->token_dev;
-  p.embd = m->embd.dev; p.embd_type = m->embd.type; p.embd_rb = (long)row_bytes(m->embd.type, mi.n_embd);
-  p.x = c->x; p.q = c->q; p.att = c->att; p.h = c->h;
-  p.part = c->attn_part; p.cnt = c->attn_cnt; p.err = c->err_dev;
-  p.n_slots = n_slots; p.slot_bytes = slot; p.attn_ch = ch;
-  size_t off = 0;
-  p.ring_off = 0; off += (size_t)n_slots * slot;
-  p.scr_off = p.xq_off = (int)off;
-  p.part_off = (int)(off + xq);
-  p.vals_off = (int)(off + xq + part);
-  p.scr_bytes = (int)scr;
-  off += scr;
-  off = (off + 15) / 16 * 16;
-  p.bar_off = (int)off; off += (size_t)n_slots * 8;
-  off = (off + 15) / 16 * 16;
-  p.red_off = (int)off; off += 512;
-  c->loop_smem = off;
-  c->loop_grid = sms;
-  void* d = nullptr;
-  if ((e = ctx_alloc(c, layers.size() * sizeof(LoopLayer), &d))) return e;
-  p.layers = (const LoopLayer*)d;
-  if ((e = cudaMemcpy(d, layers.data(), layers.size() * sizeof(LoopLayer), cudaMemcpyHostToDevice))) return e;
-  if ((e = ctx_alloc(c, 16, &d))) return e;
-  p.bar = (unsigned*)d;
-  if ((e = ctx_alloc(c, (size_t)std::max(mi.n_head, mi.n_head_kv) * 4, &d))) return e;
-  p.amax_att = (float*)d;
-  if ((e = ctx_alloc(c, (size_t)sms * 4, &d))) return e;
-  p.amax_h = (float*)d;
-  auto kern = hd == 128 ? loop_kernel<4> : loop_kernel<2>;
-  if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->loop_smem))) return e;
-  int per_sm = 0;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, LOOP_THREADS, c->loop_smem))) return e;
-  if (per_sm < 1) return cudaSuccess;
-  c->loop = true;
-  return cudaSuccess;
-}
-
-// The whole layer loop of one token: one cooperative launch.
-static cudaError_t launch_loop(foxcuda_context* c, bool trace) {
-  LoopParams p = c->lp;
-  p.trace = trace ? c->trace : nullptr;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(c->loop_grid);
-  cfg.blockDim = dim3(LOOP_THREADS);
-  cfg.dynamicSmemBytes = c->loop_smem;
-  cfg.stream = c->stream;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeCooperative;
-  at[0].val.cooperative = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  if (p.hd == 128) return cudaLaunchKernelEx(&cfg, loop_kernel<4>, p);
-  return cudaLaunchKernelEx(&cfg, loop_kernel<2>, p);
-}
-
-// After a step that reported the error word: the persistent step's barrier
-// counter and the tile counters may be left mid-count.
-static void loop_rearm(foxcuda_context* c) {
-  if (c->loop) cudaMemsetAsync(c->lp.bar, 0, 16, c->stream);
-  cudaMemsetAsync(c->attn_cnt, 0, (size_t)c->m->loc.n_head_kv * 4, c->stream);
-}
-
 static cudaError_t enqueue_body(foxcuda_context* c, bool trace) {
   foxcuda_model* m = c->m;
   const foxcuda_model_info& mi = m->info;
   cudaStream_t s = c->stream;
-  if (c->loop) {
-    cudaError_t e = launch_loop(c, trace);
-    if (e) return e;
-    mark(c, PK_LOOP);
-    advance_kernel<<<1, 32, 0, s>>>(c->pos_dev, 1);
-    mark(c, PK_ADVANCE);
-    return cudaGetLastError();
-  }
   const size_t emb_rb = row_bytes(m->embd.type, mi.n_embd);
   embed_kernel<<<(mi.n_embd + 255) / 256, 256, 0, s>>>(m->embd.type, m->embd.dev, emb_rb,
                                                         (int)mi.n_embd, c->token_dev, c->x);
@@ -2481,11 +2297,9 @@ static foxcuda_status check_err(foxcuda_context* c) {
   if (!code) return FOXCUDA_OK;
   c->h_pinned[3] = 0;
   cudaMemsetAsync(c->err_dev, 0, 4, c->stream);
-  loop_rearm(c);
   cudaStreamSynchronize(c->stream);
   return fail(FOXCUDA_ERR_INTERNAL, "device: a bounded wait gave up (code %u: 1 weights to shared memory, "
-              "2 a peer's exchange, 3 a grid barrier of the persistent step); the step's outputs are "
-              "not valid", code);
+              "2 a peer's exchange); the step's outputs are not valid", code);
 }
 
 // ---------------------------------------------------------------------------
@@ -2536,11 +2350,6 @@ static cudaError_t prefill_buffers(foxcuda_context* c) {
   A(M * sizeof(int*), (void**)&c->pf_pos_list);
   A(M * sizeof(void*), (void**)&c->pf_k_list);
   A(M * sizeof(void*), (void**)&c->pf_v_list);
-  {
-    const size_t gqa = mi.n_head / mi.n_head_kv;
-    A(M * mi.n_head_kv * c->m->attn_nt * gqa * (mi.head_dim + 2) * 4, (void**)&c->pf_part);
-    A(M * mi.n_head_kv * 4, (void**)&c->pf_cnt);
-  }
   if (e == cudaSuccess) {
     std::vector<int*> pl(M);
     std::vector<void*> kl(M, c->kc), vl(M, c->vc);
@@ -2593,16 +2402,15 @@ static cudaError_t chunk_attention(foxcuda_context* c, uint32_t l, int M, bool o
   AttnParams ap{};
   ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
   ap.hd = hd; ap.n_head = m->loc.n_head; ap.n_kv = m->loc.n_head_kv; ap.nt = m->attn_nt;
+  ap.stage_rows = attn_stage_rows(c->kv_f16);
   ap.scale = 1.0f / sqrtf((float)hd);
   if (one_launch && !c->attn_exact) {
     ap.q = c->pf_q; ap.out = c->pf_att; ap.seq_stride = nq;
     ap.pos_list = c->pf_pos_list; ap.k_list = c->pf_k_list; ap.v_list = c->pf_v_list;
     ap.layer_off = (size_t)l * c->kv_layer_elems * (c->kv_f16 ? 2 : 4);
-    ap.part = c->pf_part; ap.counters = c->pf_cnt;
     return launch_tiles(ap, M, c->stream);
   }
   ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
-  ap.part = c->attn_part; ap.counters = c->attn_cnt;
   cudaError_t e = cudaSuccess;
   for (int t = 0; t < M && !e; ++t) {
     ap.q = c->pf_q + (size_t)t * nq;
@@ -2914,8 +2722,6 @@ struct foxcuda_batch {
   float *gu = nullptr, *h = nullptr, *t = nullptr;
   int8_t* xq = nullptr;
   float* lg = nullptr;  // every sequence's logits (a K-quant head in one pass)
-  float* part = nullptr;     // tile partials of every sequence
-  unsigned* cnt = nullptr;
   std::vector<void*> allocs;
   cudaGraphExec_t graph = nullptr;  // a step and the picks, for foxcuda_batch_generate
   std::vector<foxcuda_sampler*> graph_samplers;
@@ -2980,9 +2786,6 @@ extern "C" foxcuda_status foxcuda_batch_create(foxcuda_context* const* ctxs, siz
   A(n * 2 * F * 4, (void**)&b->gu);
   A(n * F * 4, (void**)&b->h);
   A(n * E * 4, (void**)&b->t);
-  A(n * mi.n_head_kv * m->attn_nt * (mi.n_head / mi.n_head_kv) * (mi.head_dim + 2) * 4, (void**)&b->part);
-  A(n * mi.n_head_kv * 4, (void**)&b->cnt);
-  if (e == cudaSuccess) e = cudaMemset(b->cnt, 0, n * mi.n_head_kv * 4);
   std::vector<int*> pos(n);
   std::vector<uint32_t*> tokp(n);
   std::vector<void*> kb(n), vb(n);
@@ -3039,7 +2842,7 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
     all.kv_f16 = c0->kv_f16; all.n_ctx = c0->n_ctx;
     all.hd = hd; all.n_head = mi.n_head; all.n_kv = mi.n_head_kv; all.nt = m->attn_nt;
     all.scale = 1.0f / sqrtf((float)hd);
-    all.part = b->part; all.counters = b->cnt;
+    all.stage_rows = attn_stage_rows(c0->kv_f16);
     if (!c0->attn_exact) {
       e = launch_tiles(all, M, s);
     } else {
@@ -3049,8 +2852,7 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
         ap.q = b->q + (size_t)i * nq; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
         ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
         ap.hd = hd; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.nt = m->attn_nt;
-        ap.pos = c->pos_dev; ap.out = b->att + (size_t)i * nq; ap.part = c->attn_part;
-        ap.counters = c->attn_cnt;
+        ap.pos = c->pos_dev; ap.out = b->att + (size_t)i * nq; ap.stage_rows = attn_stage_rows(c->kv_f16);
         ap.scale = 1.0f / sqrtf((float)hd);
         e = run_attention(ap, c->attn_exact, s);
       }
@@ -3866,11 +3668,8 @@ extern "C" foxcuda_status foxcuda_context_bench_kernel(foxcuda_context* c, int k
                                                        uint64_t* weight_bytes_per_launch) {
   if (!c || !us_per_launch || !weight_bytes_per_launch || reps <= 0)
     return fail(FOXCUDA_ERR_ARG, "bench_kernel: bad argument");
-  if (!(kind == PK_QKV || kind == PK_O || kind == PK_GATEUP || kind == PK_DOWN || kind == PK_HEAD ||
-        kind == PK_LOOP))
-    return fail(FOXCUDA_ERR_ARG, "bench_kernel: kind %d is not a weight GEMV or the persistent step", kind);
-  if (kind == PK_LOOP && !c->loop)
-    return fail(FOXCUDA_ERR_UNSUPPORTED, "bench_kernel: this context does not take the persistent step");
+  if (!(kind == PK_QKV || kind == PK_O || kind == PK_GATEUP || kind == PK_DOWN || kind == PK_HEAD))
+    return fail(FOXCUDA_ERR_ARG, "bench_kernel: kind %d is not a weight GEMV", kind);
   cudaSetDevice(c->m->device);
   const uint32_t nl = c->m->info.n_layer;
   auto one = [&](int i) -> cudaError_t {
@@ -3880,7 +3679,6 @@ extern "C" foxcuda_status foxcuda_context_bench_kernel(foxcuda_context* c, int k
       case PK_O: return launch_o(c, l);
       case PK_GATEUP: return launch_gateup(c, l);
       case PK_DOWN: return launch_down(c, l);
-      case PK_LOOP: return launch_loop(c, false);
       default: return launch_head(c);
     }
   };

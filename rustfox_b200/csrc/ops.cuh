@@ -84,19 +84,18 @@ __global__ void advance_kernel(int* pos, int by) {
 // Decode attention (upstream src/forward.c:222-257 + src/ops.c:24-39,75-81):
 // per query head, scores q.k_j * (1/sqrtf(hd)) for j <= pos, softmax, sum of
 // a_j v_j. Two forms: attention_exact_kernel below (upstream's serial order,
-// the parity mode) and the tile attention of loop.cuh (attention_tile_kernel
-// and the persistent decode step), whose order the oracle restates.
+// the parity mode) and the tile attention of attn.cuh (attention_tile_kernel),
+// whose order the oracle restates.
 
 struct AttnParams {
   const float* q;         // [n_head * hd], roped
   const void* kcache;     // this layer: [n_kv][n_ctx][hd]
   const void* vcache;
   int kv_f16, n_ctx, hd, n_head, n_kv;
-  int nt;                 // tile target of the tile attention (loop.cuh)
+  int nt;                 // tile target of the tile attention (attn.cuh)
+  int stage_rows;         // K/V rows per staged chunk of the tile attention
   const int* pos;
   float* out;             // [n_head * hd]
-  float* part;            // [n_seq][n_kv][nt][gqa][hd + 2] tile partials
-  unsigned* counters;     // [n_seq][n_kv], zero between launches
   float scale;
   // several sequences in one launch (grid z): sequence z reads q + z *
   // seq_stride, writes out + z * seq_stride, its position at *pos_list[z]
