@@ -155,14 +155,16 @@ class Clocks:
 
 
 # ---- CPU side: upstream's own implementation ------------------------------
-def reference_decode(model, cfg, warmup: int, steps: int, budget_s: float = 60.0):
+def reference_decode(model, cfg, warmup: int, steps: int, budget_s: float = 60.0, n_prompt: int = 512):
     """Upstream fox_eval greedy decode on this host (oracle/_ref, the upstream
     sources built with their default -O3 and AVX2/FMA code generation), the
-    loop of `fox run --temp 0` (src/cli.c:333-361) on token ids. Returns
-    (tok/s, cores, sample description, kind)."""
+    loop of `fox run --temp 0` (src/cli.c:333-361) on token ids, after the
+    same n_prompt-id prompt as the device's decode (so both read a cache of
+    the same length; the prompt itself is not timed). Returns (tok/s, cores,
+    sample description, kind)."""
     from oracle import oracle as O
     from rustfox_b200 import synth
-    prompt = synth.random_prompt(cfg, 16, seed=1)
+    prompt = synth.random_prompt(cfg, n_prompt, seed=1)
     with tempfile.TemporaryDirectory() as d:
         path = synth.write_gguf(model, os.path.join(d, "model.gguf"), tokenizer=False)
         if os.path.exists(O.REF_FAST_SO):
@@ -170,7 +172,7 @@ def reference_decode(model, cfg, warmup: int, steps: int, budget_s: float = 60.0
             kind = "reference"
             cores = int(ref.L.fox_cpu_count_online())
             m = ref.open_model(path)
-            n_ctx = 16 + warmup + steps + 8
+            n_ctx = n_prompt + max(1, warmup) + steps + 8
             ctx = ref.context(m, n_ctx, 32, 0)
             smp_cfg = O.SamplerConfig(0.0, 40, 0.95, 1.1, 64, 0)
             smp = ref.L.fox_sampler_create(O.C.byref(smp_cfg), cfg.n_vocab)
@@ -204,14 +206,14 @@ def reference_decode(model, cfg, warmup: int, steps: int, budget_s: float = 60.0
             kind = "port"
             cores = os.cpu_count() or 1
             om = O.OracleModel(model)
-            octx = om.context(16 + warmup + steps + 8)
+            octx = om.context(n_prompt + max(1, warmup) + steps + 8)
             octx.eval(prompt)
             n = max(2, min(steps, 8))
             t0 = time.perf_counter()
             for i in range(n):
                 octx.eval([int(prompt[i % len(prompt)])])
             total = time.perf_counter() - t0
-    sample = (f"{n} greedy decode tokens after a 16-id prompt and {max(1, warmup)} warm-up "
+    sample = (f"{n} greedy decode tokens after a {n_prompt}-id prompt and {max(1, warmup)} warm-up "
               f"tokens (fox_eval time per token, as `fox run` reports gen tok/s)")
     return n / total, cores, sample, kind
 
@@ -262,7 +264,7 @@ def run_reference(args):
     cfg = synth.CONFIGS[args.config]
     model = synth.generate(cfg)
     cli = reference_cli(model)
-    v, cores, sample, kind = reference_decode(model, cfg, args.warmup, args.steps)
+    v, cores, sample, kind = reference_decode(model, cfg, args.warmup, args.steps, n_prompt=args.prompt)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -361,7 +363,7 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            v, cores, sample, kind = reference_decode(host_model, cfg, 2, 8, budget_s=25.0)
+            v, cores, sample, kind = reference_decode(host_model, cfg, 2, 8, budget_s=25.0, n_prompt=args.prompt)
             cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "sample": sample,
                    "cpu": cpu_model()}
         except Exception as e:  # the baseline is reported, never required
