@@ -18,8 +18,10 @@ streams them from HBM; no L2 flush is needed.
   roofline  the dominant kernel (the fused gate|up TQ1_0 GEMV), timed live
          with CUDA events on its launching stream over successive layers
 
-With --gpus N > 1 (torchrun) each rank decodes its own replica: the decode of
-one sequence is not split across GPUs here, so scaling is weak.
+Under torchrun (`--gpus N`, any N) the workload is config 4 instead: the 27B
+TQ2_0 model, one sequence split over the N ranks (tensor parallel, strong
+scaling; run_tp). N = 1 there is the single-GPU decode of the 27B model, the
+baseline of the speed-up. A plain `python bench.py` times config 2 on one GPU.
 
 --impl reference times upstream RustFox's own CPU implementation (the library
 built from the upstream sources, oracle/_ref) on this host's cores for the
@@ -52,7 +54,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="4b")
+    ap.add_argument("--config", default=None,
+                    help="model config (default: 4b; 27b under torchrun or with --tp)")
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -62,9 +65,9 @@ def parse():
     ap.add_argument("--gemm", default=None, metavar="M[,M...]",
                     help="time the M-token tensor-core pass over one layer's matrices "
                          "(prefill / verification) instead of decoding")
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
-                    help="with --tp: collectives through NCCL, or the library's own exchanges "
-                         "over peer memory")
+    ap.add_argument("--exchange", default="sums", choices=["nccl", "p2p", "sums"],
+                    help="tensor parallel: collectives through NCCL, the library's bit-exact "
+                         "term exchange over peer memory, or its partial-sum exchange")
     ap.add_argument("--split", action="store_true",
                     help="with --gemm: also time the split form of the pass")
     ap.add_argument("--prefill", action="store_true",
@@ -76,7 +79,15 @@ def parse():
     ap.add_argument("--image", action="store_true",
                     help="time the model load: tensors uploaded and packed on the device, "
                          "against a device image opened from a file")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.config is None:
+        args.config = "27b" if (args.tp or under_torchrun()) else "4b"
+    return args
+
+
+def under_torchrun() -> bool:
+    """Launched by torch.distributed.run (any number of ranks)."""
+    return "TORCHELASTIC_RUN_ID" in os.environ or "WORLD_SIZE" in os.environ
 
 
 def dist_env():
@@ -256,21 +267,54 @@ def cpu_model() -> str:
     return "unknown"
 
 
+def reference_decode_sampled(cfg, warmup: int, steps: int, n_prompt: int, budget_s: float = 40.0):
+    """Upstream's decode of a model too large to generate here in minutes
+    (config 4: 62 layers of 27B shape): the same decode timed on 1-layer and
+    2-layer models with the config's shapes, types, embedding and head
+    (bytes drawn uniformly, synth.timing_sample), the per-token time taken
+    as t1 + (n_layer - 1) * (t2 - t1). Returns (tok/s, cores, sample, kind)."""
+    from rustfox_b200 import synth
+    shared = {}
+    per = []
+    for n in (1, 2):
+        m = synth.timing_sample(cfg, n, shared=shared)
+        v, cores, _, kind = reference_decode(m, m.cfg, warmup, steps, budget_s=budget_s / 2,
+                                             n_prompt=n_prompt)
+        per.append(1.0 / v)
+    t = per[0] + (cfg.n_layer - 1) * max(per[1] - per[0], 0.0)
+    sample = (f"fox_eval per-token time of 1- and 2-layer models with {cfg.name}'s shapes, types, "
+              f"embedding and head ({per[0] * 1e3:.1f} and {per[1] * 1e3:.1f} ms after a "
+              f"{n_prompt}-id prompt), extended to {cfg.n_layer} layers as t1 + "
+              f"{cfg.n_layer - 1} x (t2 - t1)")
+    return 1.0 / t, cores, sample, kind
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
     from rustfox_b200 import synth
     cfg = synth.CONFIGS[args.config]
-    model = synth.generate(cfg)
-    cli = reference_cli(model)
-    v, cores, sample, kind = reference_decode(model, cfg, args.warmup, args.steps, n_prompt=args.prompt)
+    if args.config == "27b":  # the torchrun workload (run_tp)
+        cli = None
+        v, cores, sample, kind = reference_decode_sampled(cfg, args.warmup, args.steps, args.prompt)
+        work = {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} TQ2_0 linear + Q8_0 head, "
+                            f"batch-1 greedy decode after a {args.prompt}-id prompt",
+                "prompt": args.prompt, "sampler": "greedy, repeat penalty 1.1 over 64",
+                "parallelism": f"the upstream CPU decode (one process) against tp{world}"}
+    else:
+        model = synth.generate(cfg)
+        cli = reference_cli(model)
+        v, cores, sample, kind = reference_decode(model, cfg, args.warmup, args.steps,
+                                                  n_prompt=args.prompt)
+        work = workload(cfg, args)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if args.config == "27b" else "weak",
+            "vs_baseline": None,
             "dtype": "i8 x ternary -> i32, f32", "data": "synthetic (seeded random-init weights, "
             "uniform random prompt ids)",
-            "config": {**workload(cfg, args), "kv_cache": "f32 (upstream's cache)"},
+            "config": {**work, "kv_cache": "f32 (upstream's cache)"},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
                              "sample": sample, "cpu": cpu_model()},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -402,73 +446,162 @@ def run_ours(args):
 
 
 def run_tp(args):
-    """Greedy decode (no repeat penalty) of one sequence sharded over the
-    ranks (rustfox_b200/tp.py); time per token is the max over ranks of the
-    CUDA-event time on each rank's context stream."""
+    """One sequence of config 4 (27B TQ2_0 by default) decoded over the ranks
+    of a torchrun launch (strong scaling: the work per token is fixed, each
+    rank holds 1/N of it). N > 1: the shards of rustfox_b200/tp.py with the
+    sums exchange over peer memory by default (--exchange), the whole step
+    captured as one CUDA graph per rank; time per token is the max over
+    ranks of the CUDA-event time on each rank's context stream. N = 1: the
+    single-GPU decode step of the same model (the fastest one-GPU path, the
+    baseline the speed-up is read against). Greedy with upstream's repeat
+    penalty (1.1 over 64), as `fox run --temp 0`."""
     import datetime
     import torch
-    import torch.distributed as dist
     import rustfox_b200 as rf
     from rustfox_b200 import synth
     from rustfox_b200.tp import TPContext
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
+    dist = None
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=10))
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=5))
     cfg = synth.CONFIGS[args.config]
-    # weights generated on the device: the 27B shape is 9 GB per rank, minutes
-    # of host-side generation while every GPU of the run is held
+    # weights generated on the device: the 27B shape is 7.7 GB, minutes of
+    # host-side generation while every GPU of the run is held
     model = rf.Model.from_synthetic_device(cfg, device=local, tp_rank=rank, tp_size=world)
-    n_ctx = args.prompt + args.warmup + args.steps + 8
-    ctx = TPContext(model, n_ctx, kv="f16", exchange=args.exchange)
+    warm = max(3, args.warmup)
+    n_ctx = args.prompt + 2 * (warm + args.steps) + 8
     prompt = synth.random_prompt(cfg, args.prompt, seed=1)
-    ctx.generate(prompt, max(3, args.warmup), graphs=True)  # captures the step graph
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(ctx.stream)
-    ctx.replay(args.steps)
-    e1.record(ctx.stream)
-    torch.cuda.synchronize()
-    dt = torch.tensor([e0.elapsed_time(e1) / 1e3], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(dt, op=dist.ReduceOp.MAX)
-    dt = float(dt.item())
+    clocks = Clocks(local)
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    if world == 1:
+        ctx = model.context(n_ctx, kv="f16")
+        smp = rf.Sampler(ctx, temperature=0.0)
+        ctx.eval(prompt, want_logits=False)
+        for t in prompt:
+            smp.accept(int(t))
+        tok = smp.pick()
+        smp.accept(tok)
+        tok = int(smp.generate(tok, warm)[-1])
+        barrier()
+        clocks.start()
+        toks = smp.generate(tok, args.steps)
+        dev_s = ctx.last_eval_seconds
+        tok = int(toks[-1])
+        for _ in range(warm):
+            tok = smp.decode(tok)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            tok = smp.decode(tok)
+        e2e_s = time.perf_counter() - t0
+        clk = clocks.stop()
+        prof = {}
+        for kind, us in ctx.profile_step(tok):
+            prof[kind] = prof.get(kind, 0.0) + us
+        phases = {"qkv+attention": prof.get("qkv", 0) + prof.get("attention", 0),
+                  "o": prof.get("o", 0), "gate_up": prof.get("gate_up", 0),
+                  "down": prof.get("down", 0), "head+pick": prof.get("head", 0)}
+        d2h, exchange = 8, "none (one GPU: the single-GPU decode step)"
+        launches = 1 + 5 * cfg.n_layer + 2 + 2
+        smp.close()
+        ctx.close()
+    else:
+        ctx = TPContext(model, n_ctx, kv="f16", exchange=args.exchange, repeat_penalty=1.1,
+                        repeat_last_n=64)
+        toks = ctx.generate(prompt, warm, graphs=True)  # captures the step graph
+        barrier()
+        clocks.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ctx.stream)
+        ctx.replay(args.steps)
+        e1.record(ctx.stream)
+        torch.cuda.synchronize()
+        dev_s = e0.elapsed_time(e1) / 1e3
+        # end to end: the token from pinned host memory, the captured step,
+        # the pick (and position) read back, every step on every rank
+        tok = int(ctx.decode(0 if toks is None else int(toks[-1])))
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            tok = ctx.decode(tok)
+        e2e_s = time.perf_counter() - t0
+        clk = clocks.stop()
+        barrier()
+        phases = ctx.profile_step()
+        d2h = 12
+        exchange = {
+            "nccl": "torch.distributed NCCL per row-parallel GEMV (max-allreduce of the absmax, "
+                    "all-gather of the block terms), bit-identical to one GPU",
+            "p2p": "the library's exchanges over peer memory (CUDA IPC): per row-parallel GEMV "
+                   "the block terms of every rank folded in upstream's order, bit-identical to "
+                   "one GPU",
+            "sums": "the library's exchanges over peer memory (CUDA IPC): per row-parallel GEMV "
+                    "the absmax traded in its prologue and n_embd row sums pushed to every rank, "
+                    "added in rank order by the next GEMV's prologue (within 1e-3 of one GPU)"}[
+            args.exchange]
+        launches = 1 + 5 * cfg.n_layer + 3 + 4
+        ctx.close()
+    dev_s = max_over_ranks(dev_s)
+    e2e_s = max_over_ranks(e2e_s)
     if rank == 0:
         # the whole model's bytes per token (weights once, K/V at the mean
         # position of the timed steps), against every rank's HBM together
         wb = cfg.weight_bytes()
-        pos = args.prompt + max(3, args.warmup) + args.steps // 2
+        pos = args.prompt + warm + args.steps // 2
         tok_bytes = (wb["layers"] + wb["output"] + wb["embd_row"] + wb["norms"]
                      + cfg.kv_bytes_per_token(pos))
         hbm, src = measured_hbm_gbs()
-        achieved = tok_bytes * args.steps / dt / 1e9
+        achieved = tok_bytes * args.steps / dev_s / 1e9
         print(json.dumps({
-            "metric": METRIC, "value": args.steps / dt, "unit": "tok/s", "n_gpus": world,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm * world, "unit": "GB/s",
+            "metric": METRIC, "value": args.steps / dev_s, "unit": "tok/s", "n_gpus": world,
+            "roofline": {"bound": "hbm", "kernel": "the whole decode step (weights and K/V read "
+                                                   "once per token over all ranks)",
+                         "achieved": achieved, "peak": hbm * world, "unit": "GB/s",
                          "frac": achieved / (hbm * world), "traffic": None,
-                         "peak_source": f"{src} per GPU x {world}",
+                         "peak_kind": f"{src} {hbm:.0f} GB/s per GPU x {world}",
                          "bytes_per_token": tok_bytes},
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "steps": args.steps, "warmup": warm, "ms_per_step": 1e3 * dev_s / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "i8 x ternary -> i32, f32",
-            "data": "synthetic (seeded random-init weights generated on the device)",
-            "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} greedy decode, one "
-                                   f"sequence over {world} GPU(s)", "prompt": args.prompt,
-                       "kv_cache": "f16", "parallelism": f"tp{world}",
-                       "collectives": (
-                           "torch.distributed NCCL per row-parallel GEMV (4 per layer), the whole "
-                           "step replayed as one CUDA graph" if args.exchange == "nccl" else
-                           "the library's exchanges over peer memory (CUDA IPC; per row-parallel "
-                           "GEMV the terms GEMV with both exchanges inside and a fold, no host "
-                           "collective), the whole step replayed as one CUDA graph")}}),
-              flush=True)
-    if world > 1:
-        dist.barrier()  # no rank unmaps a peer arena another may still read
-    ctx.close()
+            "data": "synthetic (seeded random-init weights generated on the device, uniform "
+                    "random prompt ids)",
+            "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd} "
+                                   f"{TYPE_NAMES[cfg.linear_type]} linear + "
+                                   f"{TYPE_NAMES[cfg.output_type]} head, batch-1 greedy decode "
+                                   f"of one sequence over {world} GPU(s) after a "
+                                   f"{args.prompt}-id prompt",
+                       "prompt": args.prompt, "n_ctx": n_ctx, "kv_cache": "f16",
+                       "sampler": "greedy, repeat penalty 1.1 over 64",
+                       "parallelism": f"tp{world}", "exchange": exchange,
+                       "l2": f"weights {(wb['layers'] + wb['output']) / 1e9:.2f} GB per token "
+                             f"({(wb['layers'] + wb['output']) / 1e9 / world:.2f} GB per rank) "
+                             "> 126 MB L2: streamed from HBM, no flush",
+                       "why_not_config_2": "a torchrun launch times config 4 (27B TQ2_0) split "
+                                           "over the ranks, north_star's multi-GPU deliverable "
+                                           "(strong scaling); a plain `python bench.py` times "
+                                           "config 2 (4B TQ1_0) on one GPU"},
+            "phases_us_per_token": {k: round(v, 1) for k, v in phases.items()},
+            "limiting_phase": max(phases, key=phases.get) if phases else None,
+            "e2e": {"value": args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk}), flush=True)
+    barrier()  # no rank unmaps a peer arena another may still read
     model.close()
-    if world > 1:
+    if dist is not None:
         dist.destroy_process_group()
 
 
@@ -749,7 +882,7 @@ def main():
         run_prefill(args)
     elif args.batch:
         run_batch(args)
-    elif args.tp:
+    elif args.tp or under_torchrun():
         run_tp(args)
     else:
         run_ours(args)

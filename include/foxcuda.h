@@ -408,6 +408,9 @@ foxcuda_status foxcuda_tp_head(foxcuda_context *c, float *best);
 /* pairs = tp_size gathered {value, index} pairs (device); pos += 1 */
 foxcuda_status foxcuda_tp_pick(foxcuda_context *c, const float *pairs);
 foxcuda_status foxcuda_tp_advance(foxcuda_context *c);
+/* the next step's token copied from pinned host memory into the device word
+ * foxcuda_tp_embed(c, -1) reads (for a captured step fed from the host) */
+foxcuda_status foxcuda_tp_feed(foxcuda_context *c, uint32_t token);
 foxcuda_status foxcuda_tp_tokens(foxcuda_context *c, uint32_t first_pos, size_t n, uint32_t *out);
 /* the host's position counter re-read from the device (after replaying a
  * captured foxcuda_tp_* step, which advances only the device's) */
@@ -418,25 +421,33 @@ foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
 /* The same exchanges over peer memory (NVLink) instead of host collectives.
  * Each rank's context owns an exchange arena. The arena holds every rank's
  * absmax and pick slots, readiness flags, and this rank's block terms, and
- * it is shared through CUDA IPC (plain peer loads and stores, no
- * multicast).
+ * it is shared through CUDA IPC (plain peer loads and stores only).
  * - foxcuda_tp_p2p_export writes this arena's IPC handle
  *   (FOXCUDA_IPC_HANDLE_BYTES).
  * - After every rank has exported, foxcuda_tp_p2p_open maps the others'
  *   arenas. handles holds world x FOXCUDA_IPC_HANDLE_BYTES, rank order.
  * - foxcuda_tp_p2p_row replaces amax + max-allreduce + terms + all-gather +
- *   fold of one row-parallel projection: two kernels, the terms GEMV with
- *   the absmax exchange and the readiness signal inside it, then the fold
- *   (FOXCUDA_TP_P2P_FUSED=0 in the environment: four kernels).
- *   foxcuda_tp_p2p_pick replaces head + all-gather + pick.
- * - The values and their order are those of the collective form, so the
- *   result is the single-GPU decode's, bit for bit.
+ *   fold of one row-parallel projection. foxcuda_tp_p2p_pick replaces
+ *   head + all-gather + pick.
+ * - Two exchanges (foxcuda_tp_p2p_mode, the same on every rank, set
+ *   between steps):
+ *   FOXCUDA_TP_TERMS (default)  two kernels: the terms GEMV with the absmax
+ *     exchange and the readiness signal inside it, then the fold of every
+ *     rank's block terms in upstream's order (FOXCUDA_TP_P2P_FUSED=0 in the
+ *     environment: four kernels). The values and their order are those of
+ *     the collective form: the single-GPU decode's, bit for bit.
+ *   FOXCUDA_TP_SUMS  one kernel: the GEMV trades the absmax, folds this
+ *     shard's blocks per row and pushes the n_embd row values (rank 0's
+ *     with the residual added) to every rank; the next GEMV over the
+ *     residual (q|k|v or gate|up of this context) adds the ranks' rows in
+ *     rank order in its prologue, and the head is preceded by that sum as a
+ *     kernel of its own. Same result on every rank; the single-GPU decode's
+ *     up to float rounding of the partial sums (one rank: bit for bit).
  * - Every wait is bounded. A wait that gives up sets the device error word
  *   (code 2), which foxcuda_tp_tokens and later calls report.
  * - After foxcuda_context_reset, and after any call that reports the error
  *   word, every rank calls foxcuda_tp_p2p_clear before any rank's next step:
- *   a step whose wait gave up leaves its terms and slots unusable.
- * Not yet run on a B200. */
+ *   a step whose wait gave up leaves its terms and slots unusable. */
 /* Repeat penalty of the sharded greedy pick (upstream src/sample.c:95-107):
  * each shard penalises the history tokens of its own vocabulary rows before
  * its argmax. Prompt tokens given to foxcuda_tp_embed from the host, and
@@ -448,9 +459,17 @@ foxcuda_status foxcuda_tp_set_penalty(foxcuda_context *c, float penalty, uint32_
 #define FOXCUDA_IPC_HANDLE_BYTES 64
 foxcuda_status foxcuda_tp_p2p_export(foxcuda_context *c, void *handle);
 foxcuda_status foxcuda_tp_p2p_open(foxcuda_context *c, const void *handles);
+/* The peers' arenas from contexts of this process (one process driving
+ * several GPUs): ranks[k] is rank k's exported context, this one at its own
+ * rank. Peer access is enabled between distinct devices. Two ranks on one
+ * GPU must not both step: each rank's exchange waits for kernels of the
+ * other, and nothing makes two launches on one GPU run at the same time. */
+foxcuda_status foxcuda_tp_p2p_open_local(foxcuda_context *c, foxcuda_context *const *ranks);
 foxcuda_status foxcuda_tp_p2p_clear(foxcuda_context *c);
 foxcuda_status foxcuda_tp_p2p_row(foxcuda_context *c, uint32_t layer, int which);
 foxcuda_status foxcuda_tp_p2p_pick(foxcuda_context *c);
+enum { FOXCUDA_TP_TERMS = 0, FOXCUDA_TP_SUMS = 1 };
+foxcuda_status foxcuda_tp_p2p_mode(foxcuda_context *c, int mode);
 
 /* ---- diagnostics (no upstream counterpart; upstream only times whole evals,
  * src/forward.c:421-435) ------------------------------------------------- */

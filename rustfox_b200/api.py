@@ -139,6 +139,9 @@ _PROTOS = {
     "foxcuda_tp_p2p_clear": (_st, [_vp]),
     "foxcuda_tp_p2p_row": (_st, [_vp, C.c_uint32, C.c_int]),
     "foxcuda_tp_p2p_pick": (_st, [_vp]),
+    "foxcuda_tp_p2p_mode": (_st, [_vp, C.c_int]),
+    "foxcuda_tp_feed": (_st, [_vp, C.c_uint32]),
+    "foxcuda_tp_p2p_open_local": (_st, [_vp, _vp]),
     "foxcuda_context_logits": (_st, [_vp, _vp, _sz]),
     "foxcuda_context_sync_position": (_st, [_vp]),
 }

@@ -205,6 +205,15 @@ static cudaError_t launch_ring_pe(int pro, int epi, const GemvParams& p, cudaStr
   if (pro == PRO_NORM && epi == EPI_STORE) return launch_ring_t<T, PRO_NORM, EPI_STORE>(p, s);
   if (pro == PRO_NORM && epi == EPI_QKV) return launch_ring_t<T, PRO_NORM, EPI_QKV>(p, s);
   if (pro == PRO_NORM && epi == EPI_SWIGLU) return launch_ring_t<T, PRO_NORM, EPI_SWIGLU>(p, s);
+  // tensor-parallel sums exchange (p2p.cuh): the consumers that complete
+  // the residual, the row-parallel producers
+  if (pro == PRO_NFOLD && epi == EPI_QKV) return launch_ring_t<T, PRO_NFOLD, EPI_QKV>(p, s);
+  if (pro == PRO_NFOLD && epi == EPI_SWIGLU) return launch_ring_t<T, PRO_NFOLD, EPI_SWIGLU>(p, s);
+  if constexpr (T == T_TQ1_0 || T == T_TQ2_0) {
+    if (pro == PRO_XAMAX && epi == EPI_XSUM) return launch_ring_t<T, PRO_XAMAX, EPI_XSUM>(p, s);
+  } else if constexpr (T == T_Q4_K || T == T_Q6_K) {
+    if (pro == PRO_VEC && epi == EPI_XSUM) return launch_ring_t<T, PRO_VEC, EPI_XSUM>(p, s);
+  }
   return cudaErrorInvalidValue;
 }
 
@@ -257,6 +266,13 @@ static cudaError_t launch_slice_pe(int pro, int epi, const GemvParams& p, const 
   if (pro == PRO_VEC && epi == EPI_STORE) return launch_slice_t<T, PRO_VEC, EPI_STORE>(p, g, grid, s);
   if (pro == PRO_NORM && epi == EPI_QKV) return launch_slice_t<T, PRO_NORM, EPI_QKV>(p, g, grid, s);
   if (pro == PRO_NORM && epi == EPI_SWIGLU) return launch_slice_t<T, PRO_NORM, EPI_SWIGLU>(p, g, grid, s);
+  // tensor-parallel shards: the residual completed from the sums exchange,
+  // and the row-parallel producers of both exchanges (p2p.cuh)
+  if (pro == PRO_NFOLD && epi == EPI_QKV) return launch_slice_t<T, PRO_NFOLD, EPI_QKV>(p, g, grid, s);
+  if (pro == PRO_NFOLD && epi == EPI_SWIGLU) return launch_slice_t<T, PRO_NFOLD, EPI_SWIGLU>(p, g, grid, s);
+  if (pro == PRO_XAMAX && epi == EPI_XSUM) return launch_slice_t<T, PRO_XAMAX, EPI_XSUM>(p, g, grid, s);
+  if (pro == PRO_XAMAX && epi == EPI_TERMS) return launch_slice_t<T, PRO_XAMAX, EPI_TERMS>(p, g, grid, s);
+  if (pro == PRO_GSCALE && epi == EPI_TERMS) return launch_slice_t<T, PRO_GSCALE, EPI_TERMS>(p, g, grid, s);
   return cudaErrorInvalidValue;
 }
 
@@ -1306,10 +1322,11 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
       i = j;
     }
     {
-      // row-parallel shards keep the unit layout: their terms come from the
-      // unit kernel (foxcuda_tp_terms)
+      // row-parallel shards take the slice layout too: the slice kernel
+      // emits their block terms or row sums (foxcuda_tp_terms,
+      // foxcuda_tp_p2p_row)
       const RawTensor& o = m->slot(FOXCUDA_ATTN_OUT, l);
-      const int su = tp ? 0 : slice_unit_for(m, o.type, E, nq_l, PRO_VEC);
+      const int su = slice_unit_for(m, o.type, E, nq_l, PRO_VEC);
       if ((st = pack_into(m, o.type, o.dev, E, nq_l, &L.o, su))) return st;
       L.o.src_type = o.src_type;
       if (su) set_slice(m, &L.o, PRO_VEC);
@@ -1344,7 +1361,7 @@ extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
     }
     {
       const RawTensor& d = m->slot(FOXCUDA_FFN_DOWN, l);
-      const int su = tp ? 0 : slice_unit_for(m, d.type, E, Fd_l, PRO_VEC);
+      const int su = slice_unit_for(m, d.type, E, Fd_l, PRO_VEC);
       if ((st = pack_into(m, d.type, d.dev, E, Fd_l, &L.down, su))) return st;
       L.down.src_type = d.src_type;
       if (su) set_slice(m, &L.down, PRO_VEC);
@@ -1791,7 +1808,12 @@ struct foxcuda_context {
   uint8_t* peer_arena[TPX_MAX] = {};
   bool p2p = false;
   float* x_small = nullptr;  // [0..1] global absmax (o, down), [2..3] best pair, [4..] pairs
-  unsigned* x_count = nullptr;  // CTAs done of the fused terms GEMV (o, down)
+  unsigned* x_count = nullptr;  // CTAs done of the fused terms / sums GEMV (o, down)
+  int x_mode = FOXCUDA_TP_TERMS;  // the row-parallel exchange (foxcuda_tp_p2p_mode)
+  size_t y_off = 0;             // the sums area of the arena: [o, down][world][n_embd]
+  // a sums exchange whose residual is not completed yet (which, epoch phase;
+  // which < 0: none): the next GEMV over the residual completes it
+  int fold_which = -1, fold_phase = 0;
   // repeat penalty of the sharded greedy pick (foxcuda_tp_set_penalty)
   SamplerDev* tp_smp = nullptr;
   float tp_penalty = 1.0f;
@@ -1904,6 +1926,7 @@ extern "C" void foxcuda_context_reset(foxcuda_context* c) {
   cudaSetDevice(c->m->device);
   cudaStreamSynchronize(c->stream);
   c->pos = 0;
+  c->fold_which = -1;
   cudaMemsetAsync(c->pos_dev, 0, 4, c->stream);
   cudaStreamSynchronize(c->stream);
 }
@@ -1939,6 +1962,14 @@ enum { PK_EMBED = 0, PK_QKV, PK_ATTN, PK_O, PK_GATEUP, PK_DOWN, PK_ADVANCE, PK_H
 
 // While a context is being profiled an event follows every launch.
 static void mark(foxcuda_context* c, int kind);
+// tensor-parallel sums exchange: the residual completed before a GEMV over
+// it, by a kernel of its own or in the GEMV's prologue
+static cudaError_t enqueue_fold(foxcuda_context* c);
+static void set_nfold(const foxcuda_context* c, GemvParams& p);
+static foxcuda_status flush_fold(foxcuda_context* c) {
+  CK(enqueue_fold(c), "tp sums fold");
+  return FOXCUDA_OK;
+}
 
 static void* kv_layer(const foxcuda_context* c, void* base, uint32_t l) {
   return (uint8_t*)base + (size_t)l * c->kv_layer_elems * (c->kv_f16 ? 2 : 4);
@@ -1962,26 +1993,18 @@ static uint64_t launch_weight_bytes(const foxcuda_model* m, int kind, uint32_t l
   }
 }
 
-// FOXCUDA_TP_PDL=1: a tensor-parallel step whose exchanges run over peer
-// memory launches its GEMVs and head with programmatic stream serialisation,
-// like the single-GPU step (its stream then holds only this library's
-// kernels). Off by default.
-static bool tp_pdl() {
-  static const bool on = [] {
-    const char* v = getenv("FOXCUDA_TP_PDL");
-    return v && v[0] == '1';
-  }();
-  return on;
-}
 
-// Whether the context's GEMVs and head overlap their predecessors.
+// Whether the context's GEMVs, attention and head overlap their
+// predecessors (programmatic stream serialisation): the single-GPU step, and
+// a tensor-parallel step whose exchanges run over peer memory (its stream
+// holds only this library's kernels). A tensor-parallel step with NCCL
+// collectives between its kernels keeps plain stream order: a kernel
+// overlapped after one of those read its input before it landed (measured:
+// the head after the last fold, with the collective on the process group's
+// own stream, joined by an event).
 static bool ctx_pdl(const foxcuda_context* c) {
   if (c->m->tp_size == 1 && !c->tp_steps) return true;
-  // A tensor-parallel step with NCCL collectives between its kernels keeps
-  // plain stream order: a kernel overlapped after one of those read its
-  // input before it landed (measured: the head after the last fold, with
-  // the collective on the process group's own stream, joined by an event).
-  return c->p2p && tp_pdl();
+  return c->p2p;
 }
 
 // A layer GEMV through the kernel its layout was packed for.
@@ -1997,6 +2020,13 @@ static cudaError_t launch_mat(foxcuda_context* c, const PackedMat& W, int pro, i
 static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
   const foxcuda_model_info& mi = c->m->info;
   const LayerW& L = c->m->layers[l];
+  // a pending sums exchange: one fused matrix completes the residual in its
+  // prologue; runs of several types take the sum as a kernel first
+  const bool fold = c->fold_which >= 0 && L.n_qkv == 1;
+  if (c->fold_which >= 0 && !fold) {
+    cudaError_t e = enqueue_fold(c);
+    if (e) return e;
+  }
   for (int i = 0; i < L.n_qkv; ++i) {
     const PackedMat& W = L.qkv[i];
     GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
@@ -2005,9 +2035,11 @@ static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
     p.hd = mi.head_dim; p.n_ctx = c->n_ctx; p.kv_f16 = c->kv_f16;
     p.rope_cos = c->rope_cos; p.rope_sin = c->rope_sin; p.pos = c->pos_dev;
     p.kcache = kv_layer(c, c->kc, l); p.vcache = kv_layer(c, c->vc, l); p.row_base = L.qkv_base[i];
-    cudaError_t e = launch_mat(c, W, PRO_NORM, EPI_QKV, p);
+    if (fold) set_nfold(c, p);
+    cudaError_t e = launch_mat(c, W, fold ? PRO_NFOLD : PRO_NORM, EPI_QKV, p);
     if (e) return e;
   }
+  if (fold) c->fold_which = -1;
   return cudaSuccess;
 }
 
@@ -2084,9 +2116,7 @@ static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
   ap.hd = mi.head_dim; ap.n_head = c->m->loc.n_head; ap.n_kv = c->m->loc.n_head_kv; ap.nt = c->m->attn_nt;
   ap.stage_rows = attn_stage_rows(c->kv_f16); ap.pos = c->pos_dev; ap.out = c->att;
   ap.scale = 1.0f / sqrtf((float)mi.head_dim);
-  // the single-GPU step overlaps the q|k|v kernel; a tensor-parallel step
-  // keeps plain stream order
-  return run_attention(ap, c->attn_exact, c->stream, ctx_pdl(c) && c->m->tp_size == 1 && !c->tp_steps);
+  return run_attention(ap, c->attn_exact, c->stream, ctx_pdl(c));
 }
 
 static cudaError_t launch_o(foxcuda_context* c, uint32_t l) {
@@ -2101,7 +2131,10 @@ static cudaError_t launch_gateup(foxcuda_context* c, uint32_t l) {
   const PackedMat& W = L.gateup;
   GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
   p.x = c->x; p.norm_w = L.ffn_norm; p.eps = c->m->info.rms_eps; p.out = c->h;
-  return launch_mat(c, W, PRO_NORM, EPI_SWIGLU, p);
+  if (c->fold_which < 0) return launch_mat(c, W, PRO_NORM, EPI_SWIGLU, p);
+  set_nfold(c, p);  // completes the pending sums exchange in its prologue
+  c->fold_which = -1;
+  return launch_mat(c, W, PRO_NFOLD, EPI_SWIGLU, p);
 }
 
 static cudaError_t launch_down(foxcuda_context* c, uint32_t l) {
@@ -3203,6 +3236,12 @@ static foxcuda_status tp_check(foxcuda_context* c, uint32_t layer, bool need_lay
 extern "C" foxcuda_status foxcuda_tp_embed(foxcuda_context* c, int64_t token) {
   foxcuda_status st = tp_check(c, 0, false);
   if (st) return st;
+  // A pending sums exchange is completed even though the embedding replaces
+  // the residual: the completion waits for every rank's rows, and that wait
+  // is what keeps any rank from pushing the next rows of the same kind into
+  // an area another rank has not read yet (K-quant shards trade no absmax
+  // that would order it otherwise).
+  if ((st = flush_fold(c))) return st;
   const foxcuda_model_info& mi = c->m->info;
   const size_t emb_rb = row_bytes(c->m->embd.type, mi.n_embd);
   if (token >= 0) {
@@ -3239,6 +3278,7 @@ extern "C" foxcuda_status foxcuda_tp_attention(foxcuda_context* c, uint32_t laye
 extern "C" foxcuda_status foxcuda_tp_amax(foxcuda_context* c, int which, float* amax) {
   foxcuda_status st = tp_check(c, 0, false);
   if (st) return st;
+  if ((st = flush_fold(c))) return st;
   if (!amax || (which != 0 && which != 1)) return fail(FOXCUDA_ERR_ARG, "tp_amax: bad argument");
   const int n = which == 0 ? (int)(c->m->loc.n_head * c->m->info.head_dim) : (int)c->m->loc.n_ff;
   amax_kernel<<<1, 1024, 0, c->stream>>>(which == 0 ? c->att : c->h, n, amax);
@@ -3261,6 +3301,7 @@ extern "C" foxcuda_status foxcuda_tp_terms(foxcuda_context* c, uint32_t layer, i
   foxcuda_status st = tp_check(c, layer, true);
   if (st) return st;
   if (!terms || (which != 0 && which != 1)) return fail(FOXCUDA_ERR_ARG, "tp_terms: bad argument");
+  if ((st = flush_fold(c))) return st;
   const PackedMat& W = which == 0 ? c->m->layers[layer].o : c->m->layers[layer].down;
   const int nt = W.type == T_Q4_K ? 8 : W.type == T_Q6_K ? 4 : 1;
   if (stride < (uint32_t)(W.nb * nt)) return fail(FOXCUDA_ERR_ARG, "tp_terms: stride %u below %d", stride, W.nb * nt);
@@ -3271,7 +3312,12 @@ extern "C" foxcuda_status foxcuda_tp_terms(foxcuda_context* c, uint32_t layer, i
   p.xq_scale = amax_all;
   p.out = terms;
   p.terms_stride = (int)stride;
+  p.err = c->err_dev;
   cudaError_t e;
+  if (W.slice) {
+    CK(launch_slice(W.type, PRO_GSCALE, EPI_TERMS, p, W.g, W.grid, c->stream), "tp terms");
+    return FOXCUDA_OK;
+  }
   switch (W.type) {
     case T_TQ1_0: e = launch_terms_t<T_TQ1_0>(p, true, c->stream); break;
     case T_TQ2_0: e = launch_terms_t<T_TQ2_0>(p, true, c->stream); break;
@@ -3291,6 +3337,7 @@ extern "C" foxcuda_status foxcuda_tp_fold(foxcuda_context* c, uint32_t layer, in
   foxcuda_status st = tp_check(c, layer, true);
   if (st) return st;
   if (!gathered || (which != 0 && which != 1)) return fail(FOXCUDA_ERR_ARG, "tp_fold: bad argument");
+  if ((st = flush_fold(c))) return st;
   const foxcuda_model* m = c->m;
   const PackedMat& W = which == 0 ? m->layers[layer].o : m->layers[layer].down;
   const int nt = W.type == T_Q4_K ? 8 : W.type == T_Q6_K ? 4 : 1;
@@ -3330,6 +3377,7 @@ extern "C" foxcuda_status foxcuda_tp_head(foxcuda_context* c, float* best) {
   foxcuda_status st = tp_check(c, 0, false);
   if (st) return st;
   if (!best) return fail(FOXCUDA_ERR_ARG, "tp_head: null output");
+  if ((st = flush_fold(c))) return st;
   CK(launch_head(c), "tp head");
   const int nv = (int)c->m->loc.n_vocab;
   if (c->tp_smp) tp_penalty_kernel<<<1, 256, 0, c->stream>>>(c->tp_smp, c->logits, nv, c->m->vocab0, c->tp_penalty);
@@ -3355,10 +3403,26 @@ extern "C" foxcuda_status foxcuda_tp_pick(foxcuda_context* c, const float* pairs
   return FOXCUDA_OK;
 }
 
+// The next step's token from the host, for a captured step that embeds the
+// token in device memory: one copy from pinned host memory on the context's
+// stream (which is synchronised first, so the staging word is free).
+extern "C" foxcuda_status foxcuda_tp_feed(foxcuda_context* c, uint32_t token) {
+  if (!c) return fail(FOXCUDA_ERR_ARG, "tp_feed: null context");
+  if (token >= c->m->info.n_vocab) return fail(FOXCUDA_ERR_ARG, "tp_feed: token outside the vocabulary");
+  cudaSetDevice(c->m->device);
+  CK(cudaStreamSynchronize(c->stream), "tp feed sync");
+  c->h_pinned[0] = token;
+  CK(cudaMemcpyAsync(c->token_dev, c->h_pinned, 4, cudaMemcpyHostToDevice, c->stream), "tp feed");
+  return FOXCUDA_OK;
+}
+
 // Position advance without a pick (prompt tokens) and reading the picks back.
 extern "C" foxcuda_status foxcuda_tp_advance(foxcuda_context* c) {
   foxcuda_status st = tp_check(c, 0, false);
   if (st) return st;
+  // a prompt token's residual is not read again, but its completion is
+  // what orders the next pushes (foxcuda_tp_embed)
+  if ((st = flush_fold(c))) return st;
   advance_kernel<<<1, 32, 0, c->stream>>>(c->pos_dev, 1);
   CK(cudaGetLastError(), "tp advance");
   c->pos += 1;
@@ -3456,7 +3520,9 @@ extern "C" foxcuda_status foxcuda_tp_p2p_export(foxcuda_context* c, void* handle
     c->stride_d = (int)(fmax * td);
     const size_t E = m->info.n_embd;
     const size_t off_d = (AR_TERMS + E * (size_t)c->stride_o * 4 + 255) / 256 * 256;
-    const size_t bytes = off_d + E * (size_t)c->stride_d * 4;
+    const size_t off_y = (off_d + E * (size_t)c->stride_d * 4 + 255) / 256 * 256;
+    const size_t bytes = off_y + 2 * (size_t)m->tp_size * E * 4;
+    c->y_off = off_y;
     void* p = nullptr;
     CK(ctx_alloc(c, bytes, &p), "exchange arena");
     CK(cudaMemset(p, 0, bytes), "exchange arena");
@@ -3486,6 +3552,37 @@ extern "C" foxcuda_status foxcuda_tp_p2p_open(foxcuda_context* c, const void* ha
     void* p = nullptr;
     CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "open a peer's arena");
     c->peer_arena[k] = (uint8_t*)p;
+  }
+  c->p2p = true;
+  return FOXCUDA_OK;
+}
+
+// The peers' arenas when every rank's context lives in this process (one
+// process driving several GPUs, or several shards on one GPU): their device
+// pointers, with peer access enabled between distinct devices.
+extern "C" foxcuda_status foxcuda_tp_p2p_open_local(foxcuda_context* c, foxcuda_context* const* ranks) {
+  if (!c || !ranks) return fail(FOXCUDA_ERR_ARG, "tp_p2p_open_local: null argument");
+  if (!c->arena) return fail(FOXCUDA_ERR_ARG, "tp_p2p_open_local: export this context's arena first");
+  if (c->p2p) return fail(FOXCUDA_ERR_ARG, "tp_p2p_open_local: the peers are already open");
+  const foxcuda_model* m = c->m;
+  for (int k = 0; k < m->tp_size; ++k) {
+    const foxcuda_context* r = ranks[k];
+    if (!r || !r->arena || r->m->tp_size != m->tp_size || r->m->tp_rank != k || r->n_ctx != c->n_ctx)
+      return fail(FOXCUDA_ERR_ARG, "tp_p2p_open_local: entry %d is not an exported context of rank %d", k, k);
+    if (k == m->tp_rank && r != c) return fail(FOXCUDA_ERR_ARG, "tp_p2p_open_local: entry %d is not this context", k);
+  }
+  cudaSetDevice(m->device);
+  for (int k = 0; k < m->tp_size; ++k) {
+    const int dev = ranks[k]->m->device;
+    if (dev != m->device) {
+      int can = 0;
+      CK(cudaDeviceCanAccessPeer(&can, m->device, dev), "peer access query");
+      if (!can) return fail(FOXCUDA_ERR_UNSUPPORTED, "tp_p2p_open_local: device %d cannot reach device %d", m->device, dev);
+      const cudaError_t e = cudaDeviceEnablePeerAccess(dev, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else CK(e, "peer access");
+    }
+    c->peer_arena[k] = ranks[k]->arena;
   }
   c->p2p = true;
   return FOXCUDA_OK;
@@ -3541,6 +3638,7 @@ static cudaError_t launch_xterms(const foxcuda_context* c, const PackedMat& W, i
   p.x_count = c->x_count + which;
   p.x_amax = amax;
   p.pdl = ctx_pdl(c) ? 1 : 0;
+  if (W.slice) return launch_slice(W.type, PRO_XAMAX, EPI_TERMS, p, W.g, W.grid, c->stream);
   switch (W.type) {
     case T_TQ1_0: return launch_xterms_t<T_TQ1_0>(p, c->stream);
     case T_TQ2_0: return launch_xterms_t<T_TQ2_0>(p, c->stream);
@@ -3548,6 +3646,66 @@ static cudaError_t launch_xterms(const foxcuda_context* c, const PackedMat& W, i
     case T_Q6_K: return launch_xterms_t<T_Q6_K>(p, c->stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// The sums exchange's GEMV of one row-parallel projection: the absmax
+// traded in the prologue (ternary; K-quant shards quantise with their own
+// 256-block scales, which are the unsplit vector's), each row's value pushed
+// to every rank, readiness published by the last CTA (gemv.cuh EPI_XSUM).
+static cudaError_t launch_xsum(const foxcuda_context* c, const PackedMat& W, int which, int phase) {
+  const foxcuda_model* m = c->m;
+  GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
+  p.x = which == 0 ? c->att : c->h;
+  p.pos = c->pos_dev;
+  p.err = c->err_dev;
+  for (int k = 0; k < TPX_MAX; ++k) p.x_peers[k] = c->peer_arena[k];
+  p.x_rank = m->tp_rank;
+  p.x_world = m->tp_size;
+  p.x_which = which;
+  p.x_phase = phase;
+  p.x_count = c->x_count + which;
+  p.x_y_off = c->y_off + (size_t)which * m->tp_size * m->info.n_embd * 4;
+  p.x_res = c->x;
+  p.pdl = ctx_pdl(c) ? 1 : 0;
+  const bool tern = W.type == T_TQ1_0 || W.type == T_TQ2_0;
+  const int pro = tern ? PRO_XAMAX : PRO_VEC;
+  if (W.slice) return launch_slice(W.type, pro, EPI_XSUM, p, W.g, W.grid, c->stream);
+  return launch_ring(W.type, pro, EPI_XSUM, p, c->stream);
+}
+
+// A pending sums exchange completed into the residual by a GEMV's prologue
+// (PRO_NFOLD): the exchange's area, readiness slot and phase.
+static void set_nfold(const foxcuda_context* c, GemvParams& p) {
+  const foxcuda_model* m = c->m;
+  for (int k = 0; k < TPX_MAX; ++k) p.x_peers[k] = c->peer_arena[k];
+  p.x_rank = m->tp_rank;
+  p.x_world = m->tp_size;
+  p.pos = c->pos_dev;
+  p.f_y_off = c->y_off + (size_t)c->fold_which * m->tp_size * m->info.n_embd * 4;
+  p.f_which = c->fold_which;
+  p.f_phase = c->fold_phase;
+  p.f_out = c->x;
+}
+
+// A pending sums exchange completed into the residual by a kernel of its own.
+static cudaError_t enqueue_fold(foxcuda_context* c) {
+  if (c->fold_which < 0) return cudaSuccess;
+  const int E = (int)c->m->info.n_embd;
+  const size_t y = c->y_off + (size_t)c->fold_which * c->m->tp_size * E * 4;
+  fold_sum_x_kernel<<<(E + 255) / 256, 256, 0, c->stream>>>(xparams(c), y, c->fold_which, c->fold_phase, E, c->x);
+  c->fold_which = -1;
+  return cudaGetLastError();
+}
+
+
+// The row-parallel exchange of the steps that follow (every rank the same).
+extern "C" foxcuda_status foxcuda_tp_p2p_mode(foxcuda_context* c, int mode) {
+  if (!c) return fail(FOXCUDA_ERR_ARG, "tp_p2p_mode: null context");
+  if (mode != FOXCUDA_TP_TERMS && mode != FOXCUDA_TP_SUMS)
+    return fail(FOXCUDA_ERR_ARG, "tp_p2p_mode: mode %d is neither terms (0) nor sums (1)", mode);
+  if (c->fold_which >= 0) return fail(FOXCUDA_ERR_ARG, "tp_p2p_mode: a step is half done");
+  c->x_mode = mode;
+  return FOXCUDA_OK;
 }
 
 // foxcuda_tp_amax + max-allreduce + foxcuda_tp_terms + all-gather +
@@ -3564,6 +3722,18 @@ extern "C" foxcuda_status foxcuda_tp_p2p_row(foxcuda_context* c, uint32_t layer,
   const bool tern = W.type == T_TQ1_0 || W.type == T_TQ2_0;
   const XParams x = xparams(c);
   const int phase = 2 * (int)layer + which + 1;
+  if (c->x_mode == FOXCUDA_TP_SUMS) {
+    if ((st = flush_fold(c))) return st;
+    CK(launch_xsum(c, W, which, phase), "tp sums exchange");
+    c->fold_which = which;
+    c->fold_phase = phase;
+    if (c->trace_on && which == 1) {  // the layer's output, as foxcuda_context_hidden reads it
+      if ((st = flush_fold(c))) return st;
+      CK(cudaMemcpyAsync(c->trace + (size_t)(layer + 1) * m->info.n_embd, c->x, m->info.n_embd * 4,
+                         cudaMemcpyDeviceToDevice, c->stream), "trace");
+    }
+    return FOXCUDA_OK;
+  }
   float* amax = c->x_small + which;
   const size_t off = which == 0 ? AR_TERMS : c->terms_d_off;
   const int stride = which == 0 ? c->stride_o : c->stride_d;

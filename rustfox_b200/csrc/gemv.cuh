@@ -27,10 +27,19 @@
 //               peer memory inside the kernel (p2p.cuh slots): every CTA
 //               publishes the shard's absmax to every rank and takes the
 //               largest of all ranks' slots
+//   PRO_NFOLD   as PRO_NORM, with the residual first completed from a
+//               partial-sum exchange over peer memory: x = the ranks' row
+//               sums added in rank order (rank 0's carries the residual),
+//               read from this rank's arena once every rank has signalled;
+//               CTA 0 stores the completed residual back
 // EPI_TERMS (tensor-parallel row shards) writes the per-block float terms
 // instead of folding them; the shards' terms are gathered and folded in
 // upstream's block order by fold_kernel (fold_x_kernel over peer memory,
 // where the CTA that finishes last publishes this rank's readiness).
+// EPI_XSUM (tensor-parallel row shards, partial-sum exchange) stores each
+// row's value, this shard's blocks folded in order times the activation
+// scale (rank 0 adds the residual), into this rank's slot of every rank's
+// arena; the last CTA publishes readiness as EPI_TERMS does.
 // Epilogues: store; residual add (src/ops.c:50-54); RoPE on adjacent pairs
 // (src/ops.c:56-73) + K/V cache write for the fused q|k|v matrix; SwiGLU
 // (src/ops.c:41-48) for the interleaved gate|up matrix.
@@ -42,8 +51,8 @@
 
 namespace fox {
 
-enum Pro { PRO_PREQ = 0, PRO_VEC = 1, PRO_NORM = 2, PRO_GSCALE = 3, PRO_XAMAX = 4 };
-enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_TERMS = 4 };
+enum Pro { PRO_PREQ = 0, PRO_VEC = 1, PRO_NORM = 2, PRO_GSCALE = 3, PRO_XAMAX = 4, PRO_NFOLD = 5 };
+enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_TERMS = 4, EPI_XSUM = 5 };
 
 // Largest CTA per type: 64 activation registers plus a prefetched unit must
 // fit the register file at this width.
@@ -87,7 +96,58 @@ struct GemvParams {
   int x_rank, x_world, x_which, x_phase;
   unsigned* x_count;
   float* x_amax;
+  // EPI_XSUM: the partial-sum area of this projection (byte offset in every
+  // arena, [rank][n_rows] floats) and the residual rank 0 adds
+  size_t x_y_off;
+  const float* x_res;
+  // PRO_NFOLD: the partial-sum area to complete the residual from, its
+  // readiness slot and epoch phase, and where CTA 0 stores the residual
+  size_t f_y_off;
+  int f_which, f_phase;
+  float* f_out;
 };
+
+__host__ __device__ constexpr bool pro_norms(int pro) { return pro == PRO_NORM || pro == PRO_NFOLD; }
+
+// PRO_NFOLD: wait (bounded) until every rank has signalled its partial sums
+// of the exchange; every thread then acquires the flags itself, which orders
+// its reads of the sums. False when a wait gave up (error word set to 2).
+FOX_DEV bool nfold_wait(const GemvParams& p, int* ok_sh) {
+  if (threadIdx.x == 0) *ok_sh = 1;
+  __syncthreads();
+  const uint32_t ep = tp_epoch(p.pos, p.f_phase);
+  const uint32_t* ready = reinterpret_cast<const uint32_t*>(p.x_peers[p.x_rank] + AR_READY) + p.f_which * TPX_MAX;
+  if ((int)threadIdx.x < p.x_world && !wait_u32(ready + threadIdx.x, ep, p.err)) {
+    *ok_sh = 0;
+    if (p.err) atomicExch(p.err, 2);
+  }
+  __syncthreads();
+  const bool ok = *ok_sh != 0;
+  if (ok)
+    for (int k = 0; k < p.x_world; ++k) (void)ld_acquire_sys(ready + k);
+  return ok;
+}
+
+// Residual elements i..i+3 completed from the ranks' partial sums, added in
+// rank order (read through L2: the sums were written by other GPUs).
+FOX_DEV float4 nfold_x4(const GemvParams& p, int i, int n) {
+  const float* y = reinterpret_cast<const float*>(p.x_peers[p.x_rank] + p.f_y_off);
+  float4 a = __ldcg(reinterpret_cast<const float4*>(y + i));
+  for (int k = 1; k < p.x_world; ++k) {
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(y + (size_t)k * n + i));
+    a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
+    a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+  }
+  return a;
+}
+
+// EPI_XSUM: row r's value v into this rank's slot of every rank's arena
+// (rank 0's carries the residual).
+FOX_DEV void xsum_store(const GemvParams& p, int r, float v) {
+  if (p.x_rank == 0) v = __fadd_rn(p.x_res[r], v);
+  for (int k = 0; k < p.x_world; ++k)
+    reinterpret_cast<float*>(p.x_peers[k] + p.x_y_off)[(size_t)p.x_rank * p.n_rows + r] = v;
+}
 
 // PRO_XAMAX: the largest absmax over all ranks. Every CTA publishes the same
 // shard value, so no CTA waits on another CTA of its own grid; a wait that
@@ -104,7 +164,7 @@ FOX_DEV float x_trade_amax(const GemvParams& p, float am) {
     float g = 0.0f;
     for (int k = 0; k < p.x_world; ++k) {
       uint64_t w = 0;
-      if (!wait_hi(mine + k, ep, &w)) {
+      if (!wait_hi(mine + k, ep, &w, p.err)) {
         if (p.err) atomicExch(p.err, 2);
         g = 0.0f;
         break;
@@ -437,15 +497,21 @@ gemv_kernel(const GemvParams p) {
 
   // ---------------- prologue: the activation vector ----------------------
   if (PRO != PRO_PREQ) {
+    bool folded = false;
+    if (PRO == PRO_NFOLD) {
+      __shared__ int nf_ok;
+      folded = nfold_wait(p, &nf_ok);
+    }
     double ss = 0.0;
     for (int i = tid * 4; i < K; i += nth * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(p.x + i);
-      if (PRO == PRO_NORM)
+      const float4 v = folded ? nfold_x4(p, i, K) : *reinterpret_cast<const float4*>(p.x + i);
+      if (PRO == PRO_NFOLD && folded && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
+      if (pro_norms(PRO))
         ss = ss + (double)v.x * (double)v.x + (double)v.y * (double)v.y +
              (double)v.z * (double)v.z + (double)v.w * (double)v.w;
       *reinterpret_cast<float4*>(xs + xsi(i)) = v;
     }
-    if (PRO == PRO_NORM) {
+    if (pro_norms(PRO)) {
       const double sum = block_reduce<double>(ss, red, OpAddD(), 0.0);
       const float scale = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)K), (double)p.eps)));
       for (int i = tid * 4; i < K; i += nth * 4) {
@@ -563,6 +629,7 @@ gemv_kernel(const GemvParams p) {
       const int r = u * U + tid;
       if (EPI == EPI_STORE) p.out[r] = v;
       if (EPI == EPI_ADD) p.out[r] = __fadd_rn(p.out[r], v);
+      if (EPI == EPI_XSUM) xsum_store(p, r, v);
       if (EPI == EPI_QKV || EPI == EPI_SWIGLU) vals[tid] = v;
     }
     if (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
@@ -628,7 +695,7 @@ gemv_kernel(const GemvParams p) {
         __syncthreads();
         // still counted, so the completion count is rearmed for the next
         // exchange; the error word marks this step's terms as unusable
-        if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
+        if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
         return;
       }
       if (tid < ru * nb) {
@@ -663,7 +730,7 @@ gemv_kernel(const GemvParams p) {
       if (Tr::PREFETCH) cur = nxt;
     }
   }
-  if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
+  if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
 }
 
 }  // namespace fox

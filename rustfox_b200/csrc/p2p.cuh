@@ -2,15 +2,29 @@
 // NCCL collectives per layer of the sharded decode step.
 //
 // Every rank owns an exchange arena in its own device memory, shared with the
-// other ranks through CUDA IPC (plain peer loads and stores; no multicast):
+// other ranks through CUDA IPC (plain peer loads and stores only):
 //   u64 amax[2][8]    at AR_AMAX   {epoch, absmax bits} of each rank, o / down
 //   u64 pick[8][2]    at AR_PICK   {epoch, value bits}, {epoch, index} of each rank
 //   u32 ready[2][8]   at AR_READY  epoch at which each rank's terms are complete
 //   float terms_o     at AR_TERMS  this rank's o terms   [n_embd][stride_o]
 //   float terms_d     after it     this rank's down terms [n_embd][stride_d]
+//   float sums[2][world][n_embd]   every rank's row sums of the o / down
+//                                  projection (the partial-sum exchange)
 // A rank writes its slot in every rank's arena (its own included) and reads
 // the slots of its own arena; the block terms stay where they were written
-// and are read from the owner's arena.
+// and are read from the owner's arena, the row sums are pushed to every
+// rank and read locally.
+//
+// Two exchanges of a row-parallel projection:
+//   terms   every rank folds all ranks' block terms in upstream's block
+//           order: the sharded decode equals the single-GPU one bit for bit
+//   sums    every rank pushes its rows (its blocks folded in order, times the
+//           activation scale; rank 0 adds the residual) and every rank adds
+//           the ranks' rows in rank order: n_embd floats per rank instead of
+//           n_embd x blocks, the same value on every rank, and within
+//           float rounding of the single-GPU decode (one rank: bit for bit)
+// Both quantise with the absmax of the whole vector, traded in the GEMV's
+// prologue, so the int8 activations are the single-GPU ones.
 //
 // Epochs come from the device position, ((pos + 1) << 8) | phase with phase
 // 2 * layer + which + 1 (the pick is 255), so a captured step needs no host
@@ -58,19 +72,29 @@ FOX_DEV uint32_t tp_epoch(const int* pos, int phase) {
   return ((uint32_t)(*pos + 1) << 8) | (uint32_t)phase;
 }
 
-// Bounded wait until the 32-bit word at p reaches ep (about a second).
-FOX_DEV bool wait_u32(const uint32_t* p, uint32_t ep) {
+// An earlier wait of this context already gave up (its error word is set):
+// the step is lost, so later waits give up at once instead of each running
+// out its own limit.
+FOX_DEV bool step_failed(const int* err) {
+  return err && *reinterpret_cast<const volatile int*>(err) != 0;
+}
+
+// Bounded wait until the 32-bit word at p reaches ep (about a second), or
+// until the context's error word shows the step already failed.
+FOX_DEV bool wait_u32(const uint32_t* p, uint32_t ep, const int* err) {
   for (int i = 0; i < (1 << 22); ++i) {
     if (ld_acquire_sys(p) == ep) return true;
     if (i >= 16) __nanosleep(256);
+    if ((i & 255) == 255 && step_failed(err)) return false;
   }
   return false;
 }
-FOX_DEV bool wait_hi(const uint64_t* p, uint32_t ep, uint64_t* out) {
+FOX_DEV bool wait_hi(const uint64_t* p, uint32_t ep, uint64_t* out, const int* err) {
   for (int i = 0; i < (1 << 22); ++i) {
     const uint64_t w = ld_acquire_sys(p);
     if ((uint32_t)(w >> 32) == ep) { *out = w; return true; }
     if (i >= 16) __nanosleep(256);
+    if ((i & 255) == 255 && step_failed(err)) return false;
   }
   return false;
 }
@@ -92,7 +116,7 @@ __global__ void __launch_bounds__(1024) amax_x_kernel(const XParams x, const flo
   float g = 0.0f;
   for (int k = 0; k < x.world; ++k) {
     uint64_t w = 0;
-    if (!wait_hi(mine + k, ep, &w)) {
+    if (!wait_hi(mine + k, ep, &w, x.err)) {
       if (x.err) atomicExch(x.err, 2);
       g = 0.0f;
       break;
@@ -131,7 +155,7 @@ __global__ void fold_x_kernel(const XParams x, const FoldXParams f) {
   const uint32_t* ready = reinterpret_cast<const uint32_t*>(x.peers[x.rank] + AR_READY) + f.which * TPX_MAX;
   if (threadIdx.x == 0) {
     int ok = 1;
-    for (int k = 0; k < x.world && ok; ++k) ok = wait_u32(ready + k, ep);
+    for (int k = 0; k < x.world && ok; ++k) ok = wait_u32(ready + k, ep, x.err);
     ok_sh = ok;
     if (!ok && x.err) atomicExch(x.err, 2);
   }
@@ -154,6 +178,33 @@ __global__ void fold_x_kernel(const XParams x, const FoldXParams f) {
   f.x[r] = __fadd_rn(f.x[r], v);
 }
 
+// The residual completed from the sums exchange (the ranks' rows added in
+// rank order), as a kernel of its own: before the head, or where the next
+// GEMV does not complete it in its prologue (gemv.cuh PRO_NFOLD, the same
+// additions in the same order). Releases its successor at once.
+__global__ void fold_sum_x_kernel(const XParams x, size_t y_off, int which, int phase, int n,
+                                  float* __restrict__ out) {
+  griddep_launch_dependents();
+  __shared__ int ok_sh;
+  const uint32_t ep = tp_epoch(x.pos, phase);
+  const uint32_t* ready = reinterpret_cast<const uint32_t*>(x.peers[x.rank] + AR_READY) + which * TPX_MAX;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int k = 0; k < x.world && ok; ++k) ok = wait_u32(ready + k, ep, x.err);
+    ok_sh = ok;
+    if (!ok && x.err) atomicExch(x.err, 2);
+  }
+  __syncthreads();
+  if (!ok_sh) return;
+  for (int k = 0; k < x.world; ++k) (void)ld_acquire_sys(ready + k);
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const float* y = reinterpret_cast<const float*>(x.peers[x.rank] + y_off);
+  float a = __ldcg(y + r);
+  for (int k = 1; k < x.world; ++k) a = __fadd_rn(a, __ldcg(y + (size_t)k * n + r));
+  out[r] = a;
+}
+
 // This rank's {value, index} (tp_argmax_kernel) published; every rank's pair
 // into pairs[2k], pairs[2k + 1] for tp_pick_kernel.
 __global__ void pick_x_kernel(const XParams x, const float* __restrict__ best, float* __restrict__ pairs) {
@@ -169,7 +220,7 @@ __global__ void pick_x_kernel(const XParams x, const float* __restrict__ best, f
   const uint64_t* mine = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + AR_PICK);
   for (int k = 0; k < x.world; ++k) {
     uint64_t a = 0, b = 0;
-    if (!wait_hi(mine + 2 * k, ep, &a) || !wait_hi(mine + 2 * k + 1, ep, &b)) {
+    if (!wait_hi(mine + 2 * k, ep, &a, x.err) || !wait_hi(mine + 2 * k + 1, ep, &b, x.err)) {
       if (x.err) atomicExch(x.err, 2);
       pairs[2 * k] = -CUDART_INF_F;
       pairs[2 * k + 1] = __uint_as_float(0xffffffffu);

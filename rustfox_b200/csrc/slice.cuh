@@ -142,7 +142,7 @@ inline SliceGeom slice_geom(int type, int pro, int n_rows, int K, int U, int gri
   const size_t pbytes = (size_t)rows * (nb + 1) * 4;
   g.x_off = g.part_off = s; s += std::max(xbytes, pbytes);
   s = (s + 15) / 16 * 16;
-  g.nw_off = s; if (pro == PRO_NORM) s += (size_t)K * 4;
+  g.nw_off = s; if (pro_norms(pro)) s += (size_t)K * 4;
   g.xq_off = s; s += (size_t)nb * XQ_STRIDE;
   s = (s + 15) / 16 * 16;
   g.vals_off = s; s += (size_t)rows * 4;
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     mbar_init(bar, 1);
     mbar_init(bar + 1, 1);
     mbar_fence_init();
-    if (PRO == PRO_NORM) {
+    if (pro_norms(PRO)) {
       mbar_arrive_expect_tx(bar + 1, (unsigned)(K * 4));
       bulk_g2s(nw, p.norm_w, (unsigned)(K * 4), bar + 1);
     }
@@ -199,17 +199,23 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
   bool got = true;
   float am = 0.0f;
   if (PRO != PRO_PREQ) {
+    bool folded = false;
+    if (PRO == PRO_NFOLD) {
+      __shared__ int nf_ok;
+      folded = nfold_wait(p, &nf_ok);
+    }
     double ss = 0.0;
     for (int i = tid * 4; i < K; i += nth * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(p.x + i);
-      if (PRO == PRO_NORM)
+      const float4 v = folded ? nfold_x4(p, i, K) : *reinterpret_cast<const float4*>(p.x + i);
+      if (PRO == PRO_NFOLD && folded && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
+      if (pro_norms(PRO))
         ss = ss + (double)v.x * (double)v.x + (double)v.y * (double)v.y +
              (double)v.z * (double)v.z + (double)v.w * (double)v.w;
       else
         am = absmax_acc(absmax_acc(absmax_acc(absmax_acc(am, v.x), v.y), v.z), v.w);
       *reinterpret_cast<float4*>(xs + i) = v;
     }
-    if (PRO == PRO_NORM) {
+    if (pro_norms(PRO)) {
       const double sum = block_reduce<double>(ss, red, OpAddD(), 0.0);
       const float scale = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)K), (double)p.eps)));
       got = mbar_wait(bar + 1, 0);
@@ -234,8 +240,15 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
       *reinterpret_cast<uint4*>(xq + (i >> 8) * XQ_STRIDE + (i & 255)) =
           *reinterpret_cast<const uint4*>(p.xq + i);
   } else {
-    // upstream src/gemv.c:11-42: one absmax over the whole vector
-    const float amax = block_reduce<float>(am, (float*)red, OpMax(), 0.0f);
+    // upstream src/gemv.c:11-42: one absmax over the whole vector (over
+    // every shard's slice: given under PRO_GSCALE, traded under PRO_XAMAX)
+    float amax;
+    if (PRO == PRO_GSCALE) {
+      amax = p.xq_scale[0];
+    } else {
+      amax = block_reduce<float>(am, (float*)red, OpMax(), 0.0f);
+      if (PRO == PRO_XAMAX) amax = x_trade_amax(p, amax);
+    }
     const bool nz = amax > 0.0f;
     const float inv = nz ? __fdiv_rn(127.0f, amax) : 0.0f;
     act_scale = nz ? __fdiv_rn(amax, 127.0f) : 0.0f;
@@ -292,9 +305,12 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     // memory is released
     if (tid == 0) {
       mbar_wait(bar, 0);
-      if (PRO == PRO_NORM) mbar_wait(bar + 1, 0);
+      if (pro_norms(PRO)) mbar_wait(bar + 1, 0);
     }
     __syncthreads();
+    // still counted, so the completion count is rearmed for the next
+    // exchange; the error word marks this step's sums as unusable
+    if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
     return;
   }
 
@@ -318,15 +334,22 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
   }
   __syncthreads();
 
-  // 6. rows in upstream's order, then the epilogue
+  // 6. rows in upstream's order, then the epilogue (EPI_TERMS: the block
+  //    terms themselves, folded by the exchange's fold)
   const int row0 = u0 * U;
-  for (int r = tid; r < rows; r += nth) {
+  if (EPI == EPI_TERMS)
+    for (int i = tid; i < rows * nb; i += nth) {
+      const int r = i / nb, c = i - r * nb;
+      p.out[(size_t)(row0 + r) * p.terms_stride + c] = part[r * rstride + c];
+    }
+  for (int r = tid; r < rows && EPI != EPI_TERMS; r += nth) {
     const float* pr = part + r * rstride;
     float acc = 0.0f;
     for (int i = 0; i < nb; ++i) acc = __fadd_rn(acc, pr[i]);
     const float v = __fmul_rn(acc, act_scale);
     if (EPI == EPI_STORE) p.out[row0 + r] = v;
     if (EPI == EPI_ADD) p.out[row0 + r] = __fadd_rn(p.out[row0 + r], v);
+    if (EPI == EPI_XSUM) xsum_store(p, row0 + r, v);
     if (EPI == EPI_QKV || EPI == EPI_SWIGLU) vals[r] = v;
   }
   if (EPI == EPI_QKV || EPI == EPI_SWIGLU) __syncthreads();
@@ -368,6 +391,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
       p.out[(u0 + ul) * hu + i] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf_cr(-gt))), up);
     }
   }
+  if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
 }
 
 }  // namespace fox

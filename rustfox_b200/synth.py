@@ -150,6 +150,46 @@ def generate(cfg: ModelConfig) -> SyntheticModel:
     return m
 
 
+def _timing_blocks(rng, ggml_type: int, ne0: int, ne1: int, sigma: float) -> np.ndarray:
+    """Uniform random bytes in the layout of ggml_type with every scale a
+    finite fp16 of size sigma (ternary codes kept in 0..2)."""
+    nb = ne1 * (ne0 // F.BLOCK[ggml_type][0])
+    if ggml_type == F.Q8_0:
+        b = rng.integers(0, 256, size=(nb, 34), dtype=np.uint8)
+        b[:, 0:2] = np.full((nb, 1), sigma / 127.0 * 3.0, np.float16).view(np.uint8)
+    elif ggml_type == F.TQ2_0:
+        b = rng.integers(0, 256, size=(nb, 66), dtype=np.uint8)
+        q = b[:, :64]
+        q ^= q & (q >> 1) & np.uint8(0x55)  # a code of 3 becomes 2
+        b[:, 64:66] = np.full((nb, 1), sigma, np.float16).view(np.uint8)
+    else:
+        raise ValueError(f"no timing sample for type {ggml_type}")
+    return b.reshape(-1)
+
+
+def timing_sample(cfg: ModelConfig, n_layer: int, seed: int = 0, shared: dict | None = None) -> SyntheticModel:
+    """A model with cfg's shapes and types and n_layer layers whose bytes are
+    drawn uniformly (valid scales), for timing a CPU decode of a model too
+    large to generate quickly: every layer reuses the same tensors, and
+    `shared` (a dict, filled on first use) carries the embedding and head
+    from one sample to the next. A decode's time does not depend on these
+    values; its results are not meant to be compared."""
+    c = cfg.scaled(n_layer=n_layer)
+    rng = np.random.Generator(np.random.PCG64(seed))
+    shared = {} if shared is None else shared
+    m = SyntheticModel(c)
+    ones = np.ones(c.n_embd, dtype=np.float32)
+    for name, tt, ne, sigma in tensor_specs(c):
+        if tt == F.F32:
+            m.tensors[name] = (tt, ne, ones)
+            continue
+        key = name if not name.startswith("blk.") else name.split(".", 2)[2]
+        if key not in shared:
+            shared[key] = _timing_blocks(rng, tt, ne[0], ne[1], sigma)
+        m.tensors[name] = (tt, ne, shared[key])
+    return m
+
+
 def device_seed(cfg_seed: int, index: int) -> int:
     """The seed of tensor `index` (GGUF order) of a model generated on the
     device (foxcuda_model_upload_synthetic)."""

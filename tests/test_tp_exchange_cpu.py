@@ -216,3 +216,153 @@ def test_a_count_taken_before_the_terms_are_written_is_caught():
     shape = (2, 2, 2, 6, 3)
     got = _run(*shape, seed=5, fused=True, ctas=3, count_early=True)
     assert any(b[1] == "fold" for b in _wrong(*shape, *got))
+
+
+# ---- the sums exchange (gemv.cuh EPI_XSUM / PRO_NFOLD, p2p.cuh) -------------
+#
+# Each row-parallel producer pushes its row values into its own slot of every
+# rank's sums area (one area per projection kind, o or down, not one per
+# layer), and its last CTA publishes readiness. The residual is completed by
+# the next GEMV over it (gate|up after o, the next layer's q|k|v after down,
+# the head after the last layer, the position advance of a prompt token),
+# which waits for every rank's readiness and adds the ranks' rows in rank
+# order. With ternary shards the producer trades the absmax first; K-quant
+# shards do not, so the single area per kind must be safe on the interleaving
+# of the completions alone: a rank pushes o of layer l only after completing
+# down of layer l - 1, which needs every rank's down push, which each rank
+# makes only after completing o of layer l - 1; across tokens the last
+# completion of a token plays that part, so it is made even where nothing
+# reads the residual (a prompt token).
+
+def _run_sums(world, n_layer, n_tok, rows, seed, trade, ctas=3, ready_early=False, drop_prompt_fold=False):
+    rng = np.random.default_rng(seed)
+    vals = rng.normal(0, 1, (n_tok, n_layer, 2, world, rows)).astype(np.float32)
+    amaxes = rng.random((n_tok, n_layer, 2, world)).astype(np.float32)
+    picks = [pos % 2 == 1 for pos in range(n_tok)]  # tokens with a head
+    sums = [np.zeros((2, world, rows), dtype=np.float32) for _ in range(world)]
+    ready = [np.zeros((2, TPX_MAX), dtype=np.uint32) for _ in range(world)]
+    amx = [Arena(1, 1) for _ in range(world)]
+    got = [dict() for _ in range(world)]
+    errors = []
+
+    def produce(r, pos, layer, which, rnd):
+        ep = _epoch(pos, 2 * layer + which + 1)
+        count = [0]
+        lock = threading.Lock()
+        bounds = np.linspace(0, rows, ctas + 1).astype(int)
+        cta_errors = []
+
+        def cta(j):
+            try:
+                time.sleep(rnd.random() * 1e-4)
+                if trade:
+                    _trade_amax(amx, world, r, which, ep, amaxes[pos, layer, which, r])
+                lo, hi = bounds[j], bounds[j + 1]
+
+                def push():
+                    for k in range(world):
+                        sums[k][which, r, lo:hi] = vals[pos, layer, which, r, lo:hi]
+
+                if not ready_early:
+                    push()
+                with lock:
+                    last = count[0] == ctas - 1
+                    count[0] += 1
+                if last:
+                    count[0] = 0
+                    for k in range(world):
+                        ready[k][which, r] = np.uint32(ep)
+                if ready_early:  # planted: rows pushed after readiness
+                    time.sleep(5e-3)
+                    push()
+            except BaseException as e:  # noqa: BLE001
+                cta_errors.append(e)
+
+        ts = [threading.Thread(target=cta, args=(j,)) for j in range(ctas)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join(timeout=60)
+        if cta_errors:
+            raise cta_errors[0]
+        return (pos, layer, which)
+
+    def complete(r, pending):
+        pos, layer, which = pending
+        ep = _epoch(pos, 2 * layer + which + 1)
+        for k in range(world):
+            _wait(lambda: int(ready[r][which, k]) >= ep, "ready")
+            assert int(ready[r][which, k]) == ep, f"rank {r} saw a later ready epoch"
+        acc = sums[r][which, 0].copy()
+        for k in range(1, world):
+            acc = (acc + sums[r][which, k]).astype(np.float32)
+        got[r][pending] = acc
+
+    def rank_main(r):
+        rnd = random.Random(seed * 17 + r)
+        try:
+            for pos in range(n_tok):
+                pending = None
+                for layer in range(n_layer):
+                    for which in (0, 1):
+                        time.sleep(rnd.random() * 1e-4)
+                        if pending is not None:  # q|k|v or gate|up completes it
+                            complete(r, pending)
+                        pending = produce(r, pos, layer, which, rnd)
+                # the head, or a prompt token's advance, completes the last
+                # one (planted: the prompt token drops it)
+                if picks[pos] or not drop_prompt_fold:
+                    complete(r, pending)
+        except BaseException as e:  # noqa: BLE001
+            errors.append(e)
+
+    threads = [threading.Thread(target=rank_main, args=(r,)) for r in range(world)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    # a rank that saw a later epoch than its own, or gave up waiting
+    bad = [("error", repr(e)) for e in errors]
+    for r in range(world):
+        for (pos, layer, which), acc in got[r].items():
+            want = vals[pos, layer, which, 0].copy()
+            for k in range(1, world):
+                want = (want + vals[pos, layer, which, k]).astype(np.float32)
+            if not np.array_equal(acc.view(np.uint32), want.view(np.uint32)):
+                bad.append((r, pos, layer, which))
+            ref = got[0].get((pos, layer, which))
+            if ref is None or not np.array_equal(acc.view(np.uint32), ref.view(np.uint32)):
+                bad.append((r, "ranks differ", pos, layer, which))
+    n_reads = sum(len(g) for g in got)
+    return bad, n_reads
+
+
+@pytest.mark.parametrize("trade", [True, False], ids=["ternary", "kquant"])
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_sums_protocol_reads_every_rows_of_their_own_step(world, trade):
+    """Every completion reads each rank's rows of its own layer and token,
+    in rank order, the same on every rank, with one sums area per kind."""
+    n_layer, n_tok = 3, 4
+    bad, n = _run_sums(world, n_layer, n_tok, rows=7, seed=world + 10 * trade, trade=trade)
+    assert bad == []
+    assert n == world * n_tok * 2 * n_layer  # every exchange is completed
+
+
+def test_sums_readiness_before_the_rows_is_caught():
+    """The model with a planted ordering mistake: readiness published before
+    the rows are pushed. The check above sees completions read stale rows."""
+    bad, _ = _run_sums(2, 2, 2, rows=6, seed=3, trade=False, ready_early=True)
+    assert bad
+
+
+def test_sums_dropping_a_prompt_tokens_completion_is_caught():
+    """Planted in the model: a prompt token skips its last completion. With
+    K-quant shards (no absmax trade) nothing then keeps a fast rank from
+    pushing the next token's o rows (or readiness) over those a slower rank
+    still reads; the device completes it at the position advance for that
+    reason. Seen as stale rows, a later epoch, or a wait that gives up."""
+    hits = 0
+    for seed in range(6):
+        bad, _ = _run_sums(8, 3, 6, rows=7, seed=100 + seed, trade=False, drop_prompt_fold=True)
+        hits += bool(bad)
+    assert hits
