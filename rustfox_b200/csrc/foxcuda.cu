@@ -285,6 +285,41 @@ static cudaError_t launch_slice(int type, int pro, int epi, const GemvParams& p,
   }
 }
 
+template <int T, int PRO, int EPI>
+static cudaError_t launch_stream_t(const GemvParams& p, const StreamGeom& g, int grid, cudaStream_t s) {
+  auto kern = stream_kernel<T, PRO, EPI>;
+  static size_t marks[kMaxDevices] = {};  // per instantiation
+  cudaError_t e = opt_in_smem(kern, (size_t)STREAM_MAX_SMEM, marks);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(STREAM_THREADS);
+  cfg.dynamicSmemBytes = g.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p, g);
+}
+
+template <int T>
+static cudaError_t launch_stream_pe(int pro, int epi, const GemvParams& p, const StreamGeom& g, int grid,
+                                    cudaStream_t s) {
+  if (pro == PRO_VEC && epi == EPI_ADD) return launch_stream_t<T, PRO_VEC, EPI_ADD>(p, g, grid, s);
+  if (pro == PRO_VEC && epi == EPI_STORE) return launch_stream_t<T, PRO_VEC, EPI_STORE>(p, g, grid, s);
+  if (pro == PRO_NORM && epi == EPI_QKV) return launch_stream_t<T, PRO_NORM, EPI_QKV>(p, g, grid, s);
+  if (pro == PRO_NORM && epi == EPI_SWIGLU) return launch_stream_t<T, PRO_NORM, EPI_SWIGLU>(p, g, grid, s);
+  if (pro == PRO_NFOLD && epi == EPI_QKV) return launch_stream_t<T, PRO_NFOLD, EPI_QKV>(p, g, grid, s);
+  if (pro == PRO_NFOLD && epi == EPI_SWIGLU) return launch_stream_t<T, PRO_NFOLD, EPI_SWIGLU>(p, g, grid, s);
+  if (pro == PRO_XAMAX && epi == EPI_XSUM) return launch_stream_t<T, PRO_XAMAX, EPI_XSUM>(p, g, grid, s);
+  if (pro == PRO_XAMAX && epi == EPI_TERMS) return launch_stream_t<T, PRO_XAMAX, EPI_TERMS>(p, g, grid, s);
+  if (pro == PRO_GSCALE && epi == EPI_TERMS) return launch_stream_t<T, PRO_GSCALE, EPI_TERMS>(p, g, grid, s);
+  return cudaErrorInvalidValue;
+}
+
+
 // ---------------------------------------------------------------------------
 // kernel-level entry points
 
@@ -894,12 +929,25 @@ struct PackedMat {
   uint8_t* dev = nullptr;
   // row-per-lane Q8_0 head layout (rows.cuh)
   bool rows32 = false;
-  // resident-slice launch (ternary layer matrices whose per-CTA run fits on chip)
+  // resident-slice launch (ternary layer matrices whose per-CTA run fits on
+  // chip), or the streaming slice launch (larger ones)
   bool slice = false;
+  bool stream = false;
   int pro = PRO_VEC;
   int grid = 0;
   SliceGeom g;
+  StreamGeom sg;
 };
+
+// A ternary layer matrix through the slice kernel its plan chose.
+static cudaError_t launch_sliced(const PackedMat& W, int pro, int epi, const GemvParams& p, cudaStream_t s) {
+  if (W.slice) return launch_slice(W.type, pro, epi, p, W.g, W.grid, s);
+  switch (W.type) {
+    case T_TQ1_0: return launch_stream_pe<T_TQ1_0>(pro, epi, p, W.sg, W.grid, s);
+    case T_TQ2_0: return launch_stream_pe<T_TQ2_0>(pro, epi, p, W.sg, W.grid, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 struct RawTensor {
   int type = -1;
@@ -1189,30 +1237,44 @@ static foxcuda_status transcode_tq1(RawTensor& r) {
   return FOXCUDA_OK;
 }
 
-// The resident-slice kernel takes a ternary layer matrix when its rows split
-// into the slice unit and every CTA's run of units fits in shared memory;
-// returns that unit, or 0 for the unit kernel's layout.
+// The slice kernels' plan for a ternary layer matrix over one CTA per SM:
+// resident when every CTA's run of units fits in shared memory (returns 1),
+// else streamed in chunks through a ring of buffers (returns 2); 0 when
+// neither fits.
+static int slice_plan(const foxcuda_model* m, int type, int n_rows, int K, int U, int pro, int* grid_out,
+                      SliceGeom* g_out, StreamGeom* sg_out) {
+  const int sms = sm_count(m->device);
+  const int units = n_rows / U;
+  const int per = (units + sms - 1) / sms;
+  const int grid = (units + per - 1) / per;
+  if (grid_out) *grid_out = grid;
+  const SliceGeom g = slice_geom(type, pro, n_rows, K, U, grid);
+  if (g.smem <= SLICE_MAX_SMEM) {
+    if (g_out) *g_out = g;
+    return 1;
+  }
+  const StreamGeom sg = stream_geom(type, pro, n_rows, K, U, grid);
+  if (sg.nbuf == 0) return 0;
+  if (sg_out) *sg_out = sg;
+  return 2;
+}
+
+// The slice kernels take a ternary layer matrix when its rows split into
+// the slice unit and a plan fits a CTA's shared memory; returns that unit,
+// or 0 for the unit kernel's layout.
 static int slice_unit_for(const foxcuda_model* m, int type, int n_rows, int K, int pro) {
   if (type != T_TQ1_0 && type != T_TQ2_0) return 0;
   const int nb = K / 256;
   const int U = slice_unit_rows(nb);
   if (U < 0 || n_rows % U || (SLICE_THREADS / 2) / nb < 1) return 0;
-  const int sms = sm_count(m->device);
-  const int units = n_rows / U;
-  const int per = (units + sms - 1) / sms;
-  const int grid = (units + per - 1) / per;
-  if (slice_geom(type, pro, n_rows, K, U, grid).smem > SLICE_MAX_SMEM) return 0;
-  return U;
+  return slice_plan(m, type, n_rows, K, U, pro, nullptr, nullptr, nullptr) ? U : 0;
 }
 
 static void set_slice(const foxcuda_model* m, PackedMat* W, int pro) {
-  const int sms = sm_count(m->device);
-  const int units = W->n_rows / W->U;
-  const int per = (units + sms - 1) / sms;
-  W->grid = (units + per - 1) / per;
-  W->g = slice_geom(W->type, pro, W->n_rows, W->K, W->U, W->grid);
+  const int plan = slice_plan(m, W->type, W->n_rows, W->K, W->U, pro, &W->grid, &W->g, &W->sg);
   W->pro = pro;
-  W->slice = true;
+  W->slice = plan == 1;
+  W->stream = plan == 2;
 }
 
 extern "C" foxcuda_status foxcuda_model_finalize(foxcuda_model* m) {
@@ -1460,7 +1522,7 @@ ImgEntry mat_entry(const PackedMat& W) {
   ImgEntry e{};
   e.type = W.type; e.src_type = W.src_type; e.n_rows = W.n_rows; e.K = W.K; e.nb = W.nb; e.U = W.U;
   e.pro = W.pro;
-  e.flags = (W.rows32 ? IMG_ROWS32 : 0u) | (W.slice ? IMG_SLICE : 0u);
+  e.flags = (W.rows32 ? IMG_ROWS32 : 0u) | ((W.slice || W.stream) ? IMG_SLICE : 0u);
   return e;
 }
 
@@ -1721,9 +1783,8 @@ extern "C" foxcuda_status foxcuda_model_open_image(const char* path, int device,
     W->pro = e.pro;
     if (e.flags & IMG_SLICE) {
       set_slice(m, W, e.pro);
-      if (W->g.smem > SLICE_MAX_SMEM)
-        return fail(FOXCUDA_ERR_UNSUPPORTED, "open_image: %s: a slice matrix needs %zu bytes of shared memory",
-                    path, W->g.smem);
+      if (!W->slice && !W->stream)
+        return fail(FOXCUDA_ERR_UNSUPPORTED, "open_image: %s: a slice matrix has no plan on this device", path);
     }
     return FOXCUDA_OK;
   };
@@ -1806,6 +1867,7 @@ struct foxcuda_context {
   size_t terms_d_off = 0;
   int stride_o = 0, stride_d = 0;
   uint8_t* peer_arena[TPX_MAX] = {};
+  bool peer_ipc[TPX_MAX] = {};  // mapped through CUDA IPC (closed with the context)
   bool p2p = false;
   float* x_small = nullptr;  // [0..1] global absmax (o, down), [2..3] best pair, [4..] pairs
   unsigned* x_count = nullptr;  // CTAs done of the fused terms / sums GEMV (o, down)
@@ -1840,7 +1902,7 @@ extern "C" void foxcuda_context_destroy(foxcuda_context* c) {
   cudaSetDevice(c->m->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   for (int k = 0; k < TPX_MAX; ++k)
-    if (c->peer_arena[k] && c->peer_arena[k] != c->arena) cudaIpcCloseMemHandle(c->peer_arena[k]);
+    if (c->peer_arena[k] && c->peer_ipc[k]) cudaIpcCloseMemHandle(c->peer_arena[k]);
   if (c->g_body) cudaGraphExecDestroy(c->g_body);
   if (c->g_full) cudaGraphExecDestroy(c->g_full);
   for (void* p : c->allocs) cudaFree(p);
@@ -2011,7 +2073,7 @@ static bool ctx_pdl(const foxcuda_context* c) {
 static cudaError_t launch_mat(foxcuda_context* c, const PackedMat& W, int pro, int epi, GemvParams& p) {
   p.err = c->err_dev;
   p.pdl = ctx_pdl(c);
-  if (W.slice) return launch_slice(W.type, pro, epi, p, W.g, W.grid, c->stream);
+  if (W.slice || W.stream) return launch_sliced(W, pro, epi, p, c->stream);
   return launch_ring(W.type, pro, epi, p, c->stream);
 }
 
@@ -2343,7 +2405,7 @@ constexpr int PF_CHUNK = 64;  // tokens per chunk: the widest token tile of the 
 // Threads of the decode kernel that normalises W's input vector: the chunk
 // forms its double sums of squares in the same partition.
 static int decode_threads(const PackedMat& W) {
-  return W.slice ? SLICE_THREADS : (W.U * W.nb + 31) / 32 * 32;
+  return W.slice ? SLICE_THREADS : W.stream ? STREAM_THREADS : (W.U * W.nb + 31) / 32 * 32;
 }
 
 // Every layer matrix can take the tensor-core pass (ternary, held as TQ2_0)
@@ -3314,8 +3376,8 @@ extern "C" foxcuda_status foxcuda_tp_terms(foxcuda_context* c, uint32_t layer, i
   p.terms_stride = (int)stride;
   p.err = c->err_dev;
   cudaError_t e;
-  if (W.slice) {
-    CK(launch_slice(W.type, PRO_GSCALE, EPI_TERMS, p, W.g, W.grid, c->stream), "tp terms");
+  if (W.slice || W.stream) {
+    CK(launch_sliced(W, PRO_GSCALE, EPI_TERMS, p, c->stream), "tp terms");
     return FOXCUDA_OK;
   }
   switch (W.type) {
@@ -3552,6 +3614,7 @@ extern "C" foxcuda_status foxcuda_tp_p2p_open(foxcuda_context* c, const void* ha
     void* p = nullptr;
     CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "open a peer's arena");
     c->peer_arena[k] = (uint8_t*)p;
+    c->peer_ipc[k] = true;
   }
   c->p2p = true;
   return FOXCUDA_OK;
@@ -3638,7 +3701,7 @@ static cudaError_t launch_xterms(const foxcuda_context* c, const PackedMat& W, i
   p.x_count = c->x_count + which;
   p.x_amax = amax;
   p.pdl = ctx_pdl(c) ? 1 : 0;
-  if (W.slice) return launch_slice(W.type, PRO_XAMAX, EPI_TERMS, p, W.g, W.grid, c->stream);
+  if (W.slice || W.stream) return launch_sliced(W, PRO_XAMAX, EPI_TERMS, p, c->stream);
   switch (W.type) {
     case T_TQ1_0: return launch_xterms_t<T_TQ1_0>(p, c->stream);
     case T_TQ2_0: return launch_xterms_t<T_TQ2_0>(p, c->stream);
@@ -3669,7 +3732,7 @@ static cudaError_t launch_xsum(const foxcuda_context* c, const PackedMat& W, int
   p.pdl = ctx_pdl(c) ? 1 : 0;
   const bool tern = W.type == T_TQ1_0 || W.type == T_TQ2_0;
   const int pro = tern ? PRO_XAMAX : PRO_VEC;
-  if (W.slice) return launch_slice(W.type, pro, EPI_XSUM, p, W.g, W.grid, c->stream);
+  if (W.slice || W.stream) return launch_sliced(W, pro, EPI_XSUM, p, c->stream);
   return launch_ring(W.type, pro, EPI_XSUM, p, c->stream);
 }
 

@@ -394,4 +394,360 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
   if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
 }
 
+// ---------------------------------------------------------------------------
+// Streaming slice kernel: a ternary layer matrix larger than the shared
+// memory of the grid (the 27B layer matrices: up to 57 MB against 148 x
+// 224 KB). One CTA per SM owns a contiguous run of units, as above, and
+// takes it in chunks through a ring of nbuf shared-memory buffers (one
+// mbarrier each): chunks 0..nbuf-1 are copied before griddepcontrol.wait,
+// and chunk c + nbuf is issued into the buffer chunk c has just freed, so
+// nbuf - 1 chunks (about 100 KB per SM) are in flight while one is decoded
+// by the CTA's 24 warps.
+// The block terms of every chunk are parked for the whole run and folded
+// once after the last chunk (a per-chunk fold would leave most warps idle
+// at a barrier once per chunk). Decode, fold order and epilogues are the
+// resident kernel's, so the rows are bit-identical to it. An activation vector longer than SLICE_STAGE_X
+// bytes (the 21504-wide down input) is read from global memory (L2) in each
+// prologue pass rather than staged.
+constexpr int STREAM_THREADS = 768;  // one CTA per SM: 24 warps decode each chunk
+constexpr size_t STREAM_MAX_SMEM = 200 * 1024;
+constexpr size_t STREAM_CHUNK_BYTES = 48 * 1024;
+constexpr size_t SLICE_STAGE_X = 24 * 1024;
+constexpr int STREAM_MAX_BUF = 8;
+
+struct StreamGeom {
+  int units, per;      // units in the matrix; at most `per` per CTA
+  int chunk, nch;      // units per chunk, chunks per CTA
+  int nbuf;            // chunk buffers
+  int stage_x;         // the activation vector is staged in shared memory
+  size_t unit_bytes, chunk_bytes;
+  size_t smem;
+  size_t w_off, x_off, nw_off, xq_off, part_off, vals_off, red_off, bar_off;
+};
+
+// Plan over `grid` CTAs; nbuf 0 when not even two one-unit buffers fit.
+inline StreamGeom stream_geom(int type, int pro, int n_rows, int K, int U, int grid) {
+  StreamGeom g;
+  const int nb = K / 256;
+  g.units = n_rows / U;
+  g.per = (g.units + grid - 1) / grid;
+  g.unit_bytes = (size_t)U * nb * block_bytes(type);
+  // about STREAM_CHUNK_BYTES per chunk, rounded to whole passes of the
+  // (SLICE_THREADS / 2) / nb row slots where that keeps it near the target
+  int chunk = (int)std::max<size_t>(1, std::min<size_t>((size_t)g.per, STREAM_CHUNK_BYTES / g.unit_bytes));
+  const int slots = (STREAM_THREADS / 2) / nb;
+  for (int c = chunk; c >= (chunk * 3) / 4 && c >= 1; --c)
+    if ((c * U) % slots == 0) { chunk = c; break; }
+  g.chunk = chunk;
+  g.nch = (g.per + g.chunk - 1) / g.chunk;
+  g.chunk_bytes = (g.chunk * g.unit_bytes + 15) / 16 * 16;
+  g.stage_x = pro != PRO_PREQ && (size_t)K * 4 <= SLICE_STAGE_X ? 1 : 0;
+  const int rows = g.per * U;  // the row terms of the whole run wait for one fold
+  size_t s = 0;
+  const size_t xbytes = g.stage_x ? (size_t)K * 4 : 0;
+  const size_t pbytes = (size_t)rows * (nb + 1) * 4;
+  g.x_off = g.part_off = s; s += std::max(xbytes, pbytes);
+  s = (s + 15) / 16 * 16;
+  g.nw_off = s; if (pro_norms(pro)) s += (size_t)K * 4;
+  g.xq_off = s; s += (size_t)nb * XQ_STRIDE;
+  s = (s + 15) / 16 * 16;
+  g.vals_off = s; s += (size_t)rows * 4;
+  s = (s + 15) / 16 * 16;
+  g.red_off = s; s += 32 * 8;
+  g.bar_off = s; s += 8 * (1 + STREAM_MAX_BUF);  // the norm weights, then one per buffer
+  s = (s + 127) / 128 * 128;
+  g.w_off = s;
+  const size_t room = STREAM_MAX_SMEM > s ? STREAM_MAX_SMEM - s : 0;
+  g.nbuf = (int)std::min<size_t>(STREAM_MAX_BUF, std::min<size_t>((size_t)g.nch, room / g.chunk_bytes));
+  if (g.nch > 1 && g.nbuf < 2) g.nbuf = 0;
+  if (g.nch == 1 && g.nbuf < 1) g.nbuf = 0;
+  g.smem = s + (size_t)g.nbuf * g.chunk_bytes;
+  (void)type;
+  return g;
+}
+
+template <int T, int PRO, int EPI>
+__global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvParams p, const StreamGeom g) {
+  using H = HalfW<T>;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int tid = threadIdx.x, nth = blockDim.x;
+  const int K = p.K, nb = p.nb, U = p.U;
+  const int u0 = blockIdx.x * g.per;
+  const int nu = min(g.per, g.units - u0);
+  uint8_t* sw = smem + g.w_off;  // nbuf chunk buffers of g.chunk_bytes
+  float* xs = reinterpret_cast<float*>(smem + g.x_off);
+  float* nw = reinterpret_cast<float*>(smem + g.nw_off);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + g.xq_off);
+  float* part = reinterpret_cast<float*>(smem + g.part_off);
+  float* vals = reinterpret_cast<float*>(smem + g.vals_off);
+  double* red = reinterpret_cast<double*>(smem + g.red_off);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + g.bar_off);  // [0] norm, [1 + b] buffer b
+
+  // chunk c of this CTA's run: units [c * chunk, min(nu, (c + 1) * chunk))
+  auto chunk_units = [&](int c) { return min(g.chunk, nu - c * g.chunk); };
+  auto issue = [&](int c) {
+    const int cu = chunk_units(c);
+    if (cu <= 0) return;
+    uint64_t* b = bar + 1 + c % g.nbuf;
+    uint8_t* dst = sw + (size_t)(c % g.nbuf) * g.chunk_bytes;
+    const size_t total = (size_t)cu * g.unit_bytes;
+    mbar_arrive_expect_tx(b, (unsigned)total);
+    const uint8_t* src = p.w + (size_t)(u0 + c * g.chunk) * g.unit_bytes;
+    for (size_t o = 0; o < total; o += 32768)
+      bulk_g2s(dst + o, src + o, (unsigned)std::min<size_t>(32768, total - o), b);
+  };
+
+  // 1. everything constant comes in before the wait: the norm weights
+  //    first, then the CTA's first nbuf chunks
+  if (tid == 0) {
+    for (int b = 0; b <= g.nbuf; ++b) mbar_init(bar + b, 1);
+    mbar_fence_init();
+    if (pro_norms(PRO)) {
+      mbar_arrive_expect_tx(bar, (unsigned)(K * 4));
+      bulk_g2s(nw, p.norm_w, (unsigned)(K * 4), bar);
+    }
+    for (int c = 0; c < min(g.nbuf, g.nch); ++c) issue(c);
+  }
+  griddep_launch_dependents();
+  // 2. the activations come from the previous kernel
+  griddep_wait();
+  __syncthreads();  // the barriers are initialised before anyone polls them
+
+  bool got = true;
+  float am = 0.0f;
+  float norm_scale = 1.0f;
+  bool folded = false;
+  if (PRO == PRO_NFOLD) {
+    __shared__ int nf_ok;
+    folded = nfold_wait(p, &nf_ok);
+  }
+  // the input, completed from the ranks' row sums under PRO_NFOLD
+  auto load4 = [&](int i) -> float4 {
+    if (PRO == PRO_NFOLD && folded) return nfold_x4(p, i, K);
+    return *reinterpret_cast<const float4*>(p.x + i);
+  };
+  auto norm4 = [&](float4 v, int i) -> float4 {
+    const float4 w = *reinterpret_cast<const float4*>(nw + i);
+    v.x = __fmul_rn(__fmul_rn(v.x, norm_scale), w.x);
+    v.y = __fmul_rn(__fmul_rn(v.y, norm_scale), w.y);
+    v.z = __fmul_rn(__fmul_rn(v.z, norm_scale), w.z);
+    v.w = __fmul_rn(__fmul_rn(v.w, norm_scale), w.w);
+    return v;
+  };
+  // the prologue's value of element i..i+3 after the first pass: staged, or
+  // recomputed from global memory (the same operations, the same values)
+  auto value4 = [&](int i) -> float4 {
+    if (g.stage_x) return *reinterpret_cast<const float4*>(xs + i);
+    const float4 v = load4(i);
+    return pro_norms(PRO) ? norm4(v, i) : v;
+  };
+  if (PRO != PRO_PREQ) {
+    double ss = 0.0;
+    for (int i = tid * 4; i < K; i += nth * 4) {
+      const float4 v = load4(i);
+      if (PRO == PRO_NFOLD && folded && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
+      if (pro_norms(PRO))
+        ss = ss + (double)v.x * (double)v.x + (double)v.y * (double)v.y +
+             (double)v.z * (double)v.z + (double)v.w * (double)v.w;
+      else
+        am = absmax_acc(absmax_acc(absmax_acc(absmax_acc(am, v.x), v.y), v.z), v.w);
+      if (g.stage_x) *reinterpret_cast<float4*>(xs + i) = v;
+    }
+    if (pro_norms(PRO)) {
+      const double sum = block_reduce<double>(ss, red, OpAddD(), 0.0);
+      norm_scale = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)K), (double)p.eps)));
+      got = mbar_wait(bar, 0);
+      // normalise (x * scale * w, upstream src/ops.c:7-22) and take the absmax
+      // in the same pass
+      for (int i = tid * 4; i < K; i += nth * 4) {
+        const float4 v = norm4(g.stage_x ? *reinterpret_cast<const float4*>(xs + i) : load4(i), i);
+        if (g.stage_x) *reinterpret_cast<float4*>(xs + i) = v;
+        am = absmax_acc(absmax_acc(absmax_acc(absmax_acc(am, v.x), v.y), v.z), v.w);
+      }
+    }
+  }
+  float act_scale;
+  if (PRO == PRO_PREQ) {
+    act_scale = p.xq_scale[0];
+    for (int i = tid * 16; i < K; i += nth * 16)
+      *reinterpret_cast<uint4*>(xq + (i >> 8) * XQ_STRIDE + (i & 255)) =
+          *reinterpret_cast<const uint4*>(p.xq + i);
+  } else {
+    // upstream src/gemv.c:11-42: one absmax over the whole vector (over
+    // every shard's slice: given under PRO_GSCALE, traded under PRO_XAMAX)
+    float amax;
+    if (PRO == PRO_GSCALE) {
+      amax = p.xq_scale[0];
+    } else {
+      amax = block_reduce<float>(am, (float*)red, OpMax(), 0.0f);
+      if (PRO == PRO_XAMAX) amax = x_trade_amax(p, amax);
+    }
+    const bool nz = amax > 0.0f;
+    const float inv = nz ? __fdiv_rn(127.0f, amax) : 0.0f;
+    act_scale = nz ? __fdiv_rn(amax, 127.0f) : 0.0f;
+    for (int i = tid * 4; i < K; i += nth * 4) {
+      const float4 v = value4(i);
+      *reinterpret_cast<uint32_t*>(xq + (i >> 8) * XQ_STRIDE + (i & 255)) =
+          pack4(quant1(v.x, inv), quant1(v.y, inv), quant1(v.z, inv), quant1(v.w, inv));
+    }
+  }
+  __syncthreads();
+
+  // 3. this lane's half-block activations (fixed column for the whole kernel)
+  const int lane = tid & 31, h = lane >> 4;
+  const int pair = (tid >> 5) * 16 + (lane & 15);
+  const int S = (nth >> 1) / nb;               // row slots
+  const bool active = pair < S * nb;
+  const int col = active ? pair % nb : 0, slot = active ? pair / nb : 0;
+  uint32_t xa[H::NX];
+  int sx = 0;
+  {
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(xq + col * XQ_STRIDE);
+    if (T == T_TQ2_0) {  // the half's 32 words are contiguous
+      const uint4* x4 = reinterpret_cast<const uint4*>(xw + 32 * h);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 v = x4[i];
+        xa[4 * i] = v.x; xa[4 * i + 1] = v.y; xa[4 * i + 2] = v.z; xa[4 * i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < H::NX; ++i) xa[i] = xw[H::xword(h, i)];
+    }
+    int s4[4] = {0, 0, 0, 0};
+    if (T == T_TQ1_0) {
+#pragma unroll
+      for (int i = 0; i < 30; ++i) s4[i & 3] = dp4a(0x01010101u, xa[i], s4[i & 3]);
+      // qh words: only this half's two bytes
+      const uint32_t m = h ? 0x01010000u : 0x00000101u;
+#pragma unroll
+      for (int i = 30; i < 34; ++i) s4[i & 3] = dp4a(m, xa[i], s4[i & 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < H::NX; ++i) s4[i & 3] = dp4a(0x01010101u, xa[i], s4[i & 3]);
+    }
+    sx = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+  }
+
+  const long cnt = (long)U * nb;
+  const int ushift = __ffs(U) - 1;  // U is a power of two (2, 4 or 8)
+  const int rstride = nb + 1;
+  for (int c = 0; c < g.nch; ++c) {
+    const int cu = chunk_units(c);
+    if (cu <= 0) break;
+    // 4. this chunk's weights on chip: warp 0 polls (the other 23 warps
+    //    wait at the barrier instead of spending issue slots on polls), the
+    //    barrier passes the completed phase on to the CTA; the CTA leaves
+    //    together if any wait gave up
+    if (tid < 32) got = got && mbar_wait(bar + 1 + c % g.nbuf, (c / g.nbuf) & 1);
+    if (!__syncthreads_and(got)) {
+      if (tid == 0 && p.err) atomicExch(p.err, 1);
+      // give copies still in flight a second bounded wait before the shared
+      // memory is released
+      if (tid == 0) {
+        for (int j = c; j < min(g.nch, c + g.nbuf); ++j)
+          if (chunk_units(j) > 0) mbar_wait(bar + 1 + j % g.nbuf, (j / g.nbuf) & 1);
+        if (pro_norms(PRO)) mbar_wait(bar, 0);
+      }
+      __syncthreads();
+      // still counted, so the completion count is rearmed for the next
+      // exchange; the error word marks this step's sums as unusable
+      if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
+      return;
+    }
+    const uint8_t* wbuf = sw + (size_t)(c % g.nbuf) * g.chunk_bytes;
+
+    // 5. block terms of the chunk's rows, parked with the run's other rows
+    //    (folded once, after the last chunk): pair (slot, col) takes rows
+    //    slot, slot + S, ...
+    const int rows = cu * U;
+    const int rbase = c * g.chunk * U;  // the chunk's first row within the run
+    // every lane runs the same number of passes (the shuffle needs the warp)
+    const int passes = (rows + S - 1) / S;
+    for (int ps = 0; ps < passes; ++ps) {
+      const int r = slot + ps * S;
+      const bool on = active && r < rows;
+      int v = 0;
+      const int ul = on ? r >> ushift : 0, t = on ? (r - ul * U) * nb + col : 0;
+      const uint8_t* base = wbuf + (size_t)ul * g.unit_bytes;
+      if (on) v = H::isum(base, cnt, t, h, xa) - sx;
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (on && h == 0)
+        part[(rbase + r) * rstride + col] = __fmul_rn(H::scale(base, cnt, t), __int2float_rn(v));
+    }
+    __syncthreads();
+    // the buffer is free: chunk c + nbuf streams in behind the others
+    if (tid == 0 && c + g.nbuf < g.nch) issue(c + g.nbuf);
+  }
+  // a CTA without units still waits out its norm-weight copy when the first
+  // wait gave up, before its shared memory is released
+  if (nu <= 0 && !__syncthreads_and(got)) {
+    if (tid == 0) {
+      if (p.err) atomicExch(p.err, 1);
+      if (pro_norms(PRO)) mbar_wait(bar, 0);
+    }
+    __syncthreads();
+  }
+
+  // 6. rows in upstream's order, then the epilogue (EPI_TERMS: the block
+  //    terms themselves, folded by the exchange's fold)
+  const int rows = max(nu, 0) * U;
+  const int row0 = u0 * U;
+  if (EPI == EPI_TERMS)
+    for (int i = tid; i < rows * nb; i += nth) {
+      const int r = i / nb, cc = i - r * nb;
+      p.out[(size_t)(row0 + r) * p.terms_stride + cc] = part[r * rstride + cc];
+    }
+  for (int r = tid; r < rows && EPI != EPI_TERMS; r += nth) {
+    const float* pr = part + r * rstride;
+    float acc = 0.0f;
+    for (int i = 0; i < nb; ++i) acc = __fadd_rn(acc, pr[i]);
+    const float v = __fmul_rn(acc, act_scale);
+    if (EPI == EPI_STORE) p.out[row0 + r] = v;
+    if (EPI == EPI_ADD) p.out[row0 + r] = __fadd_rn(p.out[row0 + r], v);
+    if (EPI == EPI_XSUM) xsum_store(p, row0 + r, v);
+    if (EPI == EPI_QKV || EPI == EPI_SWIGLU) vals[r] = v;
+  }
+  if (EPI == EPI_QKV || EPI == EPI_SWIGLU) __syncthreads();
+  if (EPI == EPI_QKV) {
+    const int P = *p.pos;
+    for (int r = tid; r < rows; r += nth) {
+      const int rg = p.row_base + row0 + r;
+      const float mine = vals[r];
+      if (rg < p.nq + p.nkv) {
+        const float other = vals[r ^ 1];
+        const int rr = rg < p.nq ? rg : rg - p.nq;
+        const int i = (rr % p.hd) >> 1;
+        const float cs = p.rope_cos[(size_t)P * (p.hd >> 1) + i];
+        const float sn = p.rope_sin[(size_t)P * (p.hd >> 1) + i];
+        const bool odd = r & 1;
+        const float x0 = odd ? other : mine, x1 = odd ? mine : other;
+        const float o = odd ? __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs))
+                            : __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        if (rg < p.nq) {
+          p.out[rg] = o;
+        } else {
+          const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+          if (p.kv_f16) reinterpret_cast<__half*>(p.kcache)[idx] = __float2half_rn(o);
+          else reinterpret_cast<float*>(p.kcache)[idx] = o;
+        }
+      } else {
+        const int rr = rg - p.nq - p.nkv;
+        const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+        if (p.kv_f16) reinterpret_cast<__half*>(p.vcache)[idx] = __float2half_rn(mine);
+        else reinterpret_cast<float*>(p.vcache)[idx] = mine;
+      }
+    }
+  }
+  if (EPI == EPI_SWIGLU) {
+    const int hu = U >> 1;
+    for (int k = tid; k < max(nu, 0) * hu; k += nth) {
+      const int ul = k / hu, i = k - ul * hu;
+      const float gt = vals[ul * U + i], up = vals[ul * U + hu + i];
+      p.out[(u0 + ul) * hu + i] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf_cr(-gt))), up);
+    }
+  }
+  if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
+}
+
 }  // namespace fox

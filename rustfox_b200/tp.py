@@ -290,4 +290,12 @@ class TPContext:
         return out
 
     def close(self):
+        """Releases the captured step first: a graph that holds NCCL
+        collectives must be gone before the process group is destroyed."""
+        g = getattr(self, "graph", None)
+        if g is not None:
+            import torch
+            torch.cuda.synchronize()
+            g.reset()
+            self.graph = None
         self.ctx.close()
