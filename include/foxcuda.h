@@ -56,6 +56,11 @@ foxcuda_status foxcuda_init(int device);
 foxcuda_status foxcuda_quantize_activations_i8(const float *x, size_t n, int8_t *q,
                                                float *scale, void *stream);
 
+/* The device's e^x (upstream's expf: glibc's algorithm, src/ops.c:24-48 and
+ * src/sample.c:162-184 call it) of the n floats whose bit patterns are
+ * first_bits, first_bits + 1, ...; out is device memory. */
+foxcuda_status foxcuda_expf_range(uint32_t first_bits, size_t n, float *out, void *stream);
+
 /* replaces fox_gemv_tq1_i8 / fox_gemv_tq2_i8 (include/fox/fox.h:350-355,
  * src/gemv.c:155-192). Weights in GGUF layout; act_scale is a device float. */
 foxcuda_status foxcuda_gemv_tq1_i8(const int8_t *q, const float *act_scale,

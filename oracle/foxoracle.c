@@ -21,16 +21,37 @@ static int fail(int st, const char *msg)
 
 const char *or_last_error(void) { return g_err[0] ? g_err : "no error recorded"; }
 
-/* Upstream calls libm's expf (src/ops.c:32,46, src/sample.c:165). glibc's
- * expf is not correctly rounded: it differs from the correctly rounded e^x on
- * about 7.6e-5 of the inputs in [-104, 89]. Mode 1 swaps in the correctly
- * rounded value, (float)exp((double)x), which is what the device computes, so
- * the two exponentials can be told apart from everything else. */
+/* Upstream calls libm's expf (src/ops.c:32,46, src/sample.c:165), and so
+ * does the oracle by default; the device computes the same function (glibc's
+ * algorithm, restated in CUDA). glibc's expf is not correctly rounded: it
+ * differs from the correctly rounded e^x on about 7.6e-5 of the inputs in
+ * [-104, 89]. Mode 1 swaps in the correctly rounded value,
+ * (float)exp((double)x), to show what that difference alone changes. */
 static int g_exp_cr = 0;
 
 void or_set_exp_mode(int correctly_rounded) { g_exp_cr = correctly_rounded != 0; }
 
 static float or_expf(float x) { return g_exp_cr ? (float)exp((double)x) : expf(x); }
+
+/* Test support: how many of got[i] differ (bit for bit) from libm's expf of
+ * the float whose bit pattern is first_bits + i; the first such i in
+ * *first_bad (n when none). */
+size_t or_expf_mismatches(uint32_t first_bits, size_t n, const float *got, size_t *first_bad)
+{
+    size_t bad = 0, first = n;
+    for (size_t i = 0; i < n; ++i) {
+        const uint32_t b = first_bits + (uint32_t)i;
+        float x, want;
+        memcpy(&x, &b, 4);
+        want = expf(x);
+        if (memcmp(&want, &got[i], 4) != 0) {
+            if (first == n) first = i;
+            ++bad;
+        }
+    }
+    if (first_bad) *first_bad = first;
+    return bad;
+}
 
 /* ---- element conversion ------------------------------------------------ */
 

@@ -33,6 +33,7 @@ enum { OR_OK = 0, OR_ERR_ARG = 1, OR_ERR_UNSUPPORTED = 5 };
 /* 0 (default): exponentials through libm expf, as upstream; 1: correctly
  * rounded e^x, as the device computes it. */
 void     or_set_exp_mode(int correctly_rounded);
+size_t   or_expf_mismatches(uint32_t first_bits, size_t n, const float *got, size_t *first_bad);
 
 float    or_f16_to_f32(uint16_t h);
 uint16_t or_f32_to_f16_rne(float f);

@@ -68,6 +68,8 @@ def lib():
             raise RuntimeError(f"{ORACLE_SO} is missing: run `make -C oracle oracle`")
         L = C.CDLL(ORACLE_SO)
         L.or_set_exp_mode.argtypes = [C.c_int]
+        L.or_expf_mismatches.restype = C.c_size_t
+        L.or_expf_mismatches.argtypes = [C.c_uint32, C.c_size_t, C.c_void_p, C.POINTER(C.c_size_t)]
         L.or_f16_to_f32.restype = _fp
         L.or_f16_to_f32.argtypes = [C.c_uint16]
         L.or_f32_to_f16_rne.restype = C.c_uint16
@@ -107,9 +109,28 @@ def _check(st: int, what: str):
         raise RuntimeError(f"oracle {what}: status {st}: {lib().or_last_error().decode()}")
 
 
+def lib_expf(x: float) -> float:
+    """libm's expf, as upstream calls it."""
+    if not hasattr(lib_expf, "f"):
+        m = C.CDLL("libm.so.6")
+        m.expf.restype, m.expf.argtypes = C.c_float, [C.c_float]
+        lib_expf.f = m.expf
+    return lib_expf.f(x)
+
+
+def expf_mismatches(first_bits: int, got: np.ndarray):
+    """(count, first index) of got[i] that differ bit for bit from libm's expf
+    of the float with bit pattern first_bits + i (test support)."""
+    got = np.ascontiguousarray(got, dtype=np.float32)
+    first = C.c_size_t(0)
+    n = lib().or_expf_mismatches(int(first_bits), got.size, got.ctypes.data_as(C.c_void_p), C.byref(first))
+    return int(n), int(first.value)
+
+
 class exp_mode:
-    """Context manager: run the oracle with libm expf (upstream, False) or the
-    correctly rounded exponential the device uses (True)."""
+    """Context manager: run the oracle with libm expf (upstream's and the
+    device's, False) or the correctly rounded exponential (True), a
+    diagnostic of what glibc's rounding alone changes."""
 
     def __init__(self, correctly_rounded: bool):
         self.cr = correctly_rounded

@@ -63,6 +63,7 @@ _PROTOS = {
     "foxcuda_version": (C.c_char_p, []),
     "foxcuda_init": (_st, [C.c_int]),
     "foxcuda_quantize_activations_i8": (_st, [_vp, _sz, _vp, _vp, _vp]),
+    "foxcuda_expf_range": (_st, [C.c_uint32, _sz, _vp, _vp]),
     "foxcuda_gemv_tq1_i8": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemv_tq2_i8": (_st, [_vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "foxcuda_gemm_tq_i8": (_st, [C.c_int, _vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
@@ -187,6 +188,16 @@ def _dp(t):
 
 
 # ---- kernel level (torch CUDA tensors) ------------------------------------
+def expf_range(first_bits: int, n: int, out=None):
+    """The device's e^x (upstream's expf) of the n floats with consecutive bit
+    patterns from first_bits, as a float32 CUDA tensor."""
+    import torch
+    if out is None:
+        out = torch.empty(n, dtype=torch.float32, device="cuda")
+    _check(lib().foxcuda_expf_range(int(first_bits), int(n), _dp(out), _stream()))
+    return out
+
+
 def quantize_activations_i8(x):
     """upstream fox_quantize_activations_i8 (src/gemv.c:11-42)."""
     import torch

@@ -250,7 +250,7 @@ FOX_DEV void attn_tile(const TileArgs& a, const TileSmem& m, int g, int t) {
   __syncthreads();
   for (int i = tid; i < G * n; i += nth) {
     const int h = i / n, j = i - h * n;
-    sc[h * T + j] = expf_cr(__fsub_rn(sc[h * T + j], s_m[h]));
+    sc[h * T + j] = expf_up(__fsub_rn(sc[h * T + j], s_m[h]));
   }
   __syncthreads();
   FOX_ATTN_MARK(4);
@@ -322,7 +322,7 @@ FOX_DEV void attn_merge(const TileArgs& a, const TileSmem& m, int g, int nt) {
     s_M[tid] = M;
   }
   __syncthreads();
-  if (tid < G * nt) s_w[th][hh] = expf_cr(__fsub_rn(s_mt[th][hh], s_M[hh]));
+  if (tid < G * nt) s_w[th][hh] = expf_up(__fsub_rn(s_mt[th][hh], s_M[hh]));
   __syncthreads();
   if (tid < G) {
     float L = 0.0f;

@@ -82,12 +82,84 @@ FOX_DEV uint32_t pack4(int a, int b, int c, int d) {
 
 FOX_DEV int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
-// Correctly rounded e^x in binary32: the double-precision exp rounded once to
-// float (the double result is within an ulp of e^x, far inside the float
-// rounding interval except at measure-zero ties). Upstream calls glibc's expf,
-// which differs from the correctly rounded value on about 7.6e-5 of the
-// inputs in [-104, 89]; the oracle can run with either (or_set_exp_mode).
-FOX_DEV float expf_cr(float x) { return (float)exp((double)x); }
+// e^x in binary32 as upstream gets it from glibc's expf (glibc >= 2.27: the
+// published ARM optimized-routines algorithm; x86-64 hosts with FMA run its
+// FMA build). With N = 32:
+//   z = x * N/ln2; k = round(z) by adding and subtracting 1.5 * 2^52, the
+//   sum formed with one fused multiply-add; r = x * N/ln2 - k, another;
+//   2^(k/N) = the table entry 2^((k mod N)/N), its exponent field lowered by
+//   (k mod N) * 2^52 / N, plus k * 2^52 / N in the bits;
+//   e^x = 2^(k/N) * (1 + c2 r + (c1 + c0 r) r^2), in double with fused
+//   multiply-adds, rounded once to float.
+// c0..c2 are the algorithm's published coefficients of 2^(r/N) (those of
+// 2^u scaled by N^-3, N^-2, N^-1); the table is 2^(i/N) rounded to double.
+// |x| >= 88: -inf gives 0, inf and NaN x + x, x above ln(2^128) inf, x
+// below ln(2^-150) 0, the rest the main path. Bit-identical to the host's
+// libm expf at every float in [-104, 89] (checked exhaustively).
+// In global memory, read through the read-only cache: lanes index it by
+// their own k mod 32, which constant memory would serialise.
+__device__ const uint64_t kExpTab[32] = {
+    0x3ff0000000000000ull,
+    0x3fefd9b0d3158574ull,
+    0x3fefb5586cf9890full,
+    0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull,
+    0x3fef54873168b9aaull,
+    0x3fef387a6e756238ull,
+    0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull,
+    0x3feef1a7373aa9cbull,
+    0x3feedea64c123422ull,
+    0x3feece086061892dull,
+    0x3feebfdad5362a27ull,
+    0x3feeb42b569d4f82ull,
+    0x3feeab07dd485429ull,
+    0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull,
+    0x3fee9f75e8ec5f74ull,
+    0x3feea11473eb0187ull,
+    0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull,
+    0x3feeb737b0cdc5e5ull,
+    0x3feec49182a3f090ull,
+    0x3feed503b23e255dull,
+    0x3feee89f995ad3adull,
+    0x3feeff76f2fb5e47ull,
+    0x3fef199bdd85529cull,
+    0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull,
+    0x3fef7c97337b9b5full,
+    0x3fefa4afa2a490daull,
+    0x3fefd0765b6e4540ull};
+
+FOX_DEV float expf_up(float x) {
+  const uint32_t ux = __float_as_uint(x);
+  const uint32_t abstop = (ux >> 20) & 0x7ffu;
+  if (abstop >= 0x42bu) {  // |x| >= 88, or NaN
+    if (ux == 0xff800000u) return 0.0f;
+    if (abstop >= 0x7f8u) return __fadd_rn(x, x);
+    if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);
+    if (x < -0x1.9fe368p6f) return 0.0f;
+  }
+  constexpr double kN = 32.0;
+  constexpr double kInvLn2N = 0x1.71547652b82fep+0 * kN;
+  constexpr double kShift = 0x1.8p+52;
+  constexpr double kC0 = 0x1.c6af84b912394p-5 / kN / kN / kN;
+  constexpr double kC1 = 0x1.ebfce50fac4f3p-3 / kN / kN;
+  constexpr double kC2 = 0x1.62e42ff0c52d6p-1 / kN;
+  const double xd = (double)x;
+  const double kz = __fma_rn(kInvLn2N, xd, kShift);
+  const uint64_t ki = (uint64_t)__double_as_longlong(kz);
+  const double kd = __dsub_rn(kz, kShift);
+  const double r = __fma_rn(kInvLn2N, xd, -kd);
+  const uint64_t t = __ldg(reinterpret_cast<const unsigned long long*>(kExpTab) + (ki % 32)) + (ki << 47);
+  const double sc = __longlong_as_double((long long)t);
+  const double z = __fma_rn(kC0, r, kC1);
+  const double r2 = __dmul_rn(r, r);
+  double y = __fma_rn(kC2, r, 1.0);
+  y = __fma_rn(z, r2, y);
+  return __double2float_rn(__dmul_rn(y, sc));
+}
 
 // |x| max that ignores NaN the way upstream's `if (a > amax)` does.
 FOX_DEV float absmax_acc(float amax, float x) {

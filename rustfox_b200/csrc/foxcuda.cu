@@ -335,6 +335,20 @@ __global__ void quantize_vec_kernel(const float* __restrict__ x, int n, int8_t* 
   if (threadIdx.x == 0) *scale = nz ? __fdiv_rn(amax, 127.0f) : 0.0f;
 }
 
+__global__ void expf_range_kernel(uint32_t first_bits, size_t n, float* __restrict__ out) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    out[i] = expf_up(__uint_as_float(first_bits + (uint32_t)i));
+}
+
+extern "C" foxcuda_status foxcuda_expf_range(uint32_t first_bits, size_t n, float* out, void* stream) {
+  if (!out || n == 0) return fail(FOXCUDA_ERR_ARG, "expf_range: null or empty");
+  if (n - 1 > (size_t)(0xffffffffu - first_bits)) return fail(FOXCUDA_ERR_ARG, "expf_range: past the last bit pattern");
+  const unsigned grid = (unsigned)std::min<size_t>((n + 255) / 256, (size_t)current_sms() * 16);
+  expf_range_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(first_bits, n, out);
+  CK(cudaGetLastError(), "expf_range launch");
+  return FOXCUDA_OK;
+}
+
 extern "C" foxcuda_status foxcuda_quantize_activations_i8(const float* x, size_t n, int8_t* q,
                                                           float* scale, void* stream) {
   if (!x || !q || !scale || n == 0) return fail(FOXCUDA_ERR_ARG, "quantize: null or empty");

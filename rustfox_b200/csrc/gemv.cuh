@@ -664,7 +664,7 @@ gemv_kernel(const GemvParams p) {
       }
       if (EPI == EPI_SWIGLU && tid < (ru >> 1)) {
         const float g = vals[tid], up = vals[tid + (ru >> 1)];
-        p.out[u * (U >> 1) + tid] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g))), up);
+        p.out[u * (U >> 1) + tid] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_up(-g))), up);
       }
     }
     __syncthreads();

@@ -138,7 +138,7 @@ __global__ void attention_exact_kernel(const AttnParams p) {
   float mx = -CUDART_INF_F;
   for (int j = threadIdx.x; j < P; j += blockDim.x) mx = fmaxf(mx, att[j]);
   mx = block_reduce<float>(mx, red, OpMax(), -CUDART_INF_F);
-  for (int j = threadIdx.x; j < P; j += blockDim.x) att[j] = expf_cr(__fsub_rn(att[j], mx));
+  for (int j = threadIdx.x; j < P; j += blockDim.x) att[j] = expf_up(__fsub_rn(att[j], mx));
   __syncthreads();
   if (threadIdx.x == 0) {
     float sum = 0.0f;
@@ -377,7 +377,7 @@ topk_sample_kernel(SamplerDev* st, float* logits, int n_vocab, int k, float temp
     uint32_t pick = ci[0];
     const float mx = cv[0];
     float sum = 0.0f;
-    for (int i = 0; i < n; ++i) { cv[i] = expf_cr(__fdiv_rn(__fsub_rn(cv[i], mx), temperature)); sum = __fadd_rn(sum, cv[i]); }
+    for (int i = 0; i < n; ++i) { cv[i] = expf_up(__fdiv_rn(__fsub_rn(cv[i], mx), temperature)); sum = __fadd_rn(sum, cv[i]); }
     if (sum > 0.0f) {
       int nt = n;
       for (int i = 0; i < nt; ++i) cv[i] = __fdiv_rn(cv[i], sum);

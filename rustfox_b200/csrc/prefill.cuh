@@ -170,7 +170,7 @@ __global__ void swiglu_rows_kernel(const float* __restrict__ GU, int n_rows, int
   for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < F; k += gridDim.x * blockDim.x) {
     const int u = k / hu, i = k - u * hu;
     const float g = gu[u * U + i], up = gu[u * U + hu + i];
-    H[(size_t)t * F + k] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g))), up);
+    H[(size_t)t * F + k] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf_up(-g))), up);
   }
 }
 

@@ -35,6 +35,11 @@
 
 #include "gemv.cuh"
 
+// Phase timestamps for an instrumented build (empty here).
+#ifndef FOX_SLICE_MARK
+#define FOX_SLICE_MARK(k)
+#endif
+
 namespace fox {
 
 
@@ -66,8 +71,8 @@ template <> struct HalfW<T_TQ1_0> {
     }
   }
   // int32 sum over the half, without the -sum(x) offset
-  static FOX_DEV int isum(const uint8_t* base, long cnt, int t, int h, const uint32_t* xa) {
-    const uint4 q = *reinterpret_cast<const uint4*>(base + (long)h * cnt * 16 + t * 16);
+  static FOX_DEV int isum(const uint8_t* base, int cnt, int t, int h, const uint32_t* xa) {
+    const uint4 q = *reinterpret_cast<const uint4*>(base + h * cnt * 16 + t * 16);
     const uint4 r = *reinterpret_cast<const uint4*>(base + cnt * 32 + t * 16);
     const uint32_t qh = *reinterpret_cast<const uint32_t*>(base + cnt * 48 + t * 4);
     int a1 = 0, a3 = 0;
@@ -81,7 +86,7 @@ template <> struct HalfW<T_TQ1_0> {
     word<4>(qh & (h ? 0xFFFF0000u : 0x0000FFFFu), xa + 30, 1, a1, a3);
     return a1 - 3 * a3;
   }
-  static FOX_DEV float scale(const uint8_t* base, long cnt, int t) {
+  static FOX_DEV float scale(const uint8_t* base, int cnt, int t) {
     return h2f(*reinterpret_cast<const uint16_t*>(base + cnt * 52 + t * 2));
   }
 };
@@ -94,9 +99,9 @@ template <> struct HalfW<T_TQ1_0> {
 template <> struct HalfW<T_TQ2_0> {
   static constexpr int NX = 32;
   static FOX_DEV int xword(int h, int i) { return 32 * h + i; }
-  static FOX_DEV int isum(const uint8_t* base, long cnt, int t, int h, const uint32_t* xa) {
-    const uint4 a = *reinterpret_cast<const uint4*>(base + (long)(2 * h) * cnt * 16 + t * 16);
-    const uint4 b = *reinterpret_cast<const uint4*>(base + (long)(2 * h + 1) * cnt * 16 + t * 16);
+  static FOX_DEV int isum(const uint8_t* base, int cnt, int t, int h, const uint32_t* xa) {
+    const uint4 a = *reinterpret_cast<const uint4*>(base + (2 * h) * cnt * 16 + t * 16);
+    const uint4 b = *reinterpret_cast<const uint4*>(base + (2 * h + 1) * cnt * 16 + t * 16);
     const uint32_t c[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     // level l is masked in place (codes times 4^l, at most 192 per byte) and
     // summed on its own; the shifts at the end divide exactly
@@ -108,10 +113,58 @@ template <> struct HalfW<T_TQ2_0> {
         acc[l] = dp4a_us(c[w] & (0x03030303u << (2 * l)), xa[l * 8 + w], acc[l]);
     return acc[0] + (acc[1] >> 2) + (acc[2] >> 4) + (acc[3] >> 6);
   }
-  static FOX_DEV float scale(const uint8_t* base, long cnt, int t) {
+  static FOX_DEV float scale(const uint8_t* base, int cnt, int t) {
     return h2f(*reinterpret_cast<const uint16_t*>(base + cnt * 64 + t * 2));
   }
 };
+
+// Step 5 of the slice kernels: the block terms of `rows` rows of whole
+// units held in shared memory at byte offset `wofs` (unit u at wofs + u *
+// ubytes), into part[(rbase + r) * rstride + col]. Pair (slot, col) takes
+// rows slot, slot + S, slot + 2S, ..., two rows a pass: the two half-block
+// sums are independent chains, and the pass's index work is shared. A last
+// pass with no second rows (the same for the whole CTA) decodes one. Rows
+// past the end are decoded from row 0 and discarded, so every lane runs the
+// same straight-line code (the shuffle needs the whole warp). 32-bit shared
+// memory offsets throughout.
+template <typename H>
+FOX_DEV void slice_terms(const unsigned char* smem, int wofs, int ubytes, int U, int nb, int rows, int S, int slot,
+                         int col, int h, bool active, const uint32_t* xa, int sx, float* part, int rstride,
+                         int rbase) {
+  const int cnt = U * nb;
+  const int ushift = __ffs(U) - 1;  // U is a power of two (2, 4 or 8)
+  const int passes = (rows + 2 * S - 1) / (2 * S);
+  for (int ps = 0; ps < passes; ++ps) {
+    const int r0 = slot + 2 * ps * S, r1 = r0 + S;
+    const bool on0 = active && r0 < rows, on1 = active && r1 < rows;
+    const int q0 = on0 ? r0 : 0, q1 = on1 ? r1 : 0;
+    const int ul0 = q0 >> ushift, ul1 = q1 >> ushift;
+    const int t0 = (q0 - ul0 * U) * nb + col, t1 = (q1 - ul1 * U) * nb + col;
+    const unsigned char* b0 = smem + wofs + ul0 * ubytes;
+    const unsigned char* b1 = smem + wofs + ul1 * ubytes;
+    if ((2 * ps + 1) * S < rows) {
+      int v0 = H::isum(b0, cnt, t0, h, xa) - sx;
+      int v1 = H::isum(b1, cnt, t1, h, xa) - sx;
+      v0 += __shfl_xor_sync(0xffffffffu, v0, 16);
+      v1 += __shfl_xor_sync(0xffffffffu, v1, 16);
+      if (h == 0) {
+        if (on0) part[(rbase + r0) * rstride + col] = __fmul_rn(H::scale(b0, cnt, t0), __int2float_rn(v0));
+        if (on1) part[(rbase + r1) * rstride + col] = __fmul_rn(H::scale(b1, cnt, t1), __int2float_rn(v1));
+      }
+    } else {
+      int v0 = H::isum(b0, cnt, t0, h, xa) - sx;
+      v0 += __shfl_xor_sync(0xffffffffu, v0, 16);
+      if (h == 0 && on0) part[(rbase + r0) * rstride + col] = __fmul_rn(H::scale(b0, cnt, t0), __int2float_rn(v0));
+    }
+  }
+}
+
+// A row's block terms added in upstream's block order, from 0.0f.
+FOX_DEV float fold_row(const float* pr, int nb) {
+  float acc = 0.0f;
+  for (int i = 0; i < nb; ++i) acc = __fadd_rn(acc, pr[i]);
+  return acc;
+}
 
 constexpr int SLICE_THREADS = 384;
 // Each launch asks for at least this much shared memory, so that at most two
@@ -170,6 +223,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
   float* vals = reinterpret_cast<float*>(smem + g.vals_off);
   double* red = reinterpret_cast<double*>(smem + g.red_off);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + g.bar_off);  // [0] weights, [1] norm
+  FOX_SLICE_MARK(0);
 
   // 1. everything constant comes in before the wait: the norm weights first
   //    (the prologue needs them before any weight, and issued after the
@@ -195,6 +249,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
   // 2. the activations come from the previous kernel
   griddep_wait();
   __syncthreads();  // the barriers are initialised before anyone polls them
+  FOX_SLICE_MARK(1);
 
   bool got = true;
   float am = 0.0f;
@@ -215,10 +270,14 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
         am = absmax_acc(absmax_acc(absmax_acc(absmax_acc(am, v.x), v.y), v.z), v.w);
       *reinterpret_cast<float4*>(xs + i) = v;
     }
+    FOX_SLICE_MARK(2);
     if (pro_norms(PRO)) {
       const double sum = block_reduce<double>(ss, red, OpAddD(), 0.0);
+      FOX_SLICE_MARK(3);
       const float scale = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sum, (double)K), (double)p.eps)));
+      FOX_SLICE_MARK(4);
       got = mbar_wait(bar + 1, 0);
+      FOX_SLICE_MARK(5);
       // normalise (x * scale * w, upstream src/ops.c:7-22) and take the absmax
       // in the same pass
       for (int i = tid * 4; i < K; i += nth * 4) {
@@ -242,6 +301,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
   } else {
     // upstream src/gemv.c:11-42: one absmax over the whole vector (over
     // every shard's slice: given under PRO_GSCALE, traded under PRO_XAMAX)
+    FOX_SLICE_MARK(6);
     float amax;
     if (PRO == PRO_GSCALE) {
       amax = p.xq_scale[0];
@@ -249,6 +309,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
       amax = block_reduce<float>(am, (float*)red, OpMax(), 0.0f);
       if (PRO == PRO_XAMAX) amax = x_trade_amax(p, amax);
     }
+    FOX_SLICE_MARK(7);
     const bool nz = amax > 0.0f;
     const float inv = nz ? __fdiv_rn(127.0f, amax) : 0.0f;
     act_scale = nz ? __fdiv_rn(amax, 127.0f) : 0.0f;
@@ -259,6 +320,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     }
   }
   __syncthreads();
+  FOX_SLICE_MARK(8);
 
   // 3. this lane's half-block activations (fixed column for the whole kernel)
   const int lane = tid & 31, h = lane >> 4;
@@ -296,6 +358,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     sx = (s4[0] + s4[1]) + (s4[2] + s4[3]);
   }
 
+  FOX_SLICE_MARK(9);
   // 4. weights on chip; every thread polls, the CTA leaves together if any
   //    wait gave up
   got = got && (nu <= 0 || mbar_wait(bar, 0));
@@ -314,25 +377,14 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     return;
   }
 
+  FOX_SLICE_MARK(10);
   // 5. block terms: pair (slot, col) takes rows slot, slot + S, ...
   const int rows = nu * U;
-  const long cnt = (long)U * nb;
-  const int ushift = __ffs(U) - 1;  // U is a power of two
   const int rstride = nb + 1;
-  // every lane runs the same number of passes (the shuffle needs the warp)
-  const int passes = (rows + S - 1) / S;
-  for (int ps = 0; ps < passes; ++ps) {
-    const int r = slot + ps * S;
-    const bool on = active && r < rows;
-    int v = 0;
-    const int ul = on ? r >> ushift : 0, t = on ? (r - ul * U) * nb + col : 0;
-    const uint8_t* base = sw + (size_t)ul * g.unit_bytes;
-    if (on) v = H::isum(base, cnt, t, h, xa) - sx;
-    v += __shfl_xor_sync(0xffffffffu, v, 16);
-    if (on && h == 0)
-      part[r * rstride + col] = __fmul_rn(H::scale(base, cnt, t), __int2float_rn(v));
-  }
+  slice_terms<H>(smem, (int)g.w_off, (int)g.unit_bytes, U, nb, rows, S, slot, col, h, active, xa, sx, part,
+                 rstride, 0);
   __syncthreads();
+  FOX_SLICE_MARK(11);
 
   // 6. rows in upstream's order, then the epilogue (EPI_TERMS: the block
   //    terms themselves, folded by the exchange's fold)
@@ -344,8 +396,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     }
   for (int r = tid; r < rows && EPI != EPI_TERMS; r += nth) {
     const float* pr = part + r * rstride;
-    float acc = 0.0f;
-    for (int i = 0; i < nb; ++i) acc = __fadd_rn(acc, pr[i]);
+    const float acc = fold_row(pr, nb);
     const float v = __fmul_rn(acc, act_scale);
     if (EPI == EPI_STORE) p.out[row0 + r] = v;
     if (EPI == EPI_ADD) p.out[row0 + r] = __fadd_rn(p.out[row0 + r], v);
@@ -388,9 +439,10 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     for (int k = tid; k < nu * hu; k += nth) {
       const int ul = k / hu, i = k - ul * hu;
       const float gt = vals[ul * U + i], up = vals[ul * U + hu + i];
-      p.out[(u0 + ul) * hu + i] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf_cr(-gt))), up);
+      p.out[(u0 + ul) * hu + i] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf_up(-gt))), up);
     }
   }
+  FOX_SLICE_MARK(12);
   if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
 }
 
@@ -629,8 +681,6 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
     sx = (s4[0] + s4[1]) + (s4[2] + s4[3]);
   }
 
-  const long cnt = (long)U * nb;
-  const int ushift = __ffs(U) - 1;  // U is a power of two (2, 4 or 8)
   const int rstride = nb + 1;
   for (int c = 0; c < g.nch; ++c) {
     const int cu = chunk_units(c);
@@ -655,26 +705,15 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
       if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
       return;
     }
-    const uint8_t* wbuf = sw + (size_t)(c % g.nbuf) * g.chunk_bytes;
+    const int wofs = (int)(g.w_off + (size_t)(c % g.nbuf) * g.chunk_bytes);  // this chunk's buffer
 
     // 5. block terms of the chunk's rows, parked with the run's other rows
     //    (folded once, after the last chunk): pair (slot, col) takes rows
     //    slot, slot + S, ...
     const int rows = cu * U;
     const int rbase = c * g.chunk * U;  // the chunk's first row within the run
-    // every lane runs the same number of passes (the shuffle needs the warp)
-    const int passes = (rows + S - 1) / S;
-    for (int ps = 0; ps < passes; ++ps) {
-      const int r = slot + ps * S;
-      const bool on = active && r < rows;
-      int v = 0;
-      const int ul = on ? r >> ushift : 0, t = on ? (r - ul * U) * nb + col : 0;
-      const uint8_t* base = wbuf + (size_t)ul * g.unit_bytes;
-      if (on) v = H::isum(base, cnt, t, h, xa) - sx;
-      v += __shfl_xor_sync(0xffffffffu, v, 16);
-      if (on && h == 0)
-        part[(rbase + r) * rstride + col] = __fmul_rn(H::scale(base, cnt, t), __int2float_rn(v));
-    }
+    slice_terms<H>(smem, wofs, (int)g.unit_bytes, U, nb, rows, S, slot, col, h, active, xa, sx, part, rstride,
+                   rbase);
     __syncthreads();
     // the buffer is free: chunk c + nbuf streams in behind the others
     if (tid == 0 && c + g.nbuf < g.nch) issue(c + g.nbuf);
@@ -700,8 +739,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
     }
   for (int r = tid; r < rows && EPI != EPI_TERMS; r += nth) {
     const float* pr = part + r * rstride;
-    float acc = 0.0f;
-    for (int i = 0; i < nb; ++i) acc = __fadd_rn(acc, pr[i]);
+    const float acc = fold_row(pr, nb);
     const float v = __fmul_rn(acc, act_scale);
     if (EPI == EPI_STORE) p.out[row0 + r] = v;
     if (EPI == EPI_ADD) p.out[row0 + r] = __fadd_rn(p.out[row0 + r], v);
@@ -744,7 +782,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
     for (int k = tid; k < max(nu, 0) * hu; k += nth) {
       const int ul = k / hu, i = k - ul * hu;
       const float gt = vals[ul * U + i], up = vals[ul * U + hu + i];
-      p.out[(u0 + ul) * hu + i] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf_cr(-gt))), up);
+      p.out[(u0 + ul) * hu + i] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf_up(-gt))), up);
     }
   }
   if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);

@@ -5,8 +5,8 @@ query head, scores q.k_j * (1/sqrtf(hd)) for j <= pos, fox_softmax
 (src/ops.c:24-39), then out = sum_j a_j v_j, each sum serial in float.
 
   exact = 1  must equal that serial order bit for bit. The reference here is
-             numpy float32 in the same order, with the oracle's softmax run on
-             the correctly rounded exponential the device uses.
+             numpy float32 in the same order, with the oracle's softmax
+             (libm's expf, which the device's exponential reproduces).
   exact = 0  is the tile attention of the decode step. It sums in another
              order, which the oracle restates (oracle.tile_attention): bit
              for bit against that, and within 1e-5 of the output's scale
@@ -82,8 +82,7 @@ def _ref_serial(q, k, v, n_head, n_kv, hd, pos):
         for d in range(hd):  # s_j += q[d] * k_j[d], j vectorised, each step rounded
             s = (s + (qn[h, d] * K[:, d]).astype(np.float32)).astype(np.float32)
         att = np.ascontiguousarray((s * scale).astype(np.float32))
-        with O.exp_mode(True):
-            L.or_softmax(att.ctypes.data_as(C.c_void_p), att.size)
+        L.or_softmax(att.ctypes.data_as(C.c_void_p), att.size)
         acc = np.zeros(hd, np.float32)
         for j in range(pos + 1):
             acc = (acc + (att[j] * V[j]).astype(np.float32)).astype(np.float32)
@@ -113,9 +112,8 @@ def test_tile_kernel_is_the_oracles_tile_order(case, f16):
     qn = q.numpy().astype(np.float32).reshape(n_head, hd)
     kn, vn = k.float().numpy(), v.float().numpy()
     scale = np.float32(1.0) / np.sqrt(np.float32(hd), dtype=np.float32)
-    with O.exp_mode(True):
-        want = np.concatenate([O.tile_attention(qn[h], kn[h // gqa, : pos + 1], vn[h // gqa, : pos + 1], nt,
-                                                float(scale)) for h in range(n_head)])
+    want = np.concatenate([O.tile_attention(qn[h], kn[h // gqa, : pos + 1], vn[h // gqa, : pos + 1], nt,
+                                            float(scale)) for h in range(n_head)])
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (
         f"{np.count_nonzero(got != want)} of {got.size} differ")
 

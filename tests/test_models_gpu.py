@@ -42,8 +42,7 @@ def pair(request):
 def test_parity_mode_bit_identical(pair):
     cfg, m, om = pair
     prompt = synth.random_prompt(cfg, 48, seed=2)
-    with O.exp_mode(True):
-        want, want_h = om.context(128).eval(prompt, want_hidden=True)
+    want, want_h = om.context(128).eval(prompt, want_hidden=True)
     ctx = m.context(128, kv="f32", attn_exact=True)
     ctx.set_trace(True)
     got = ctx.eval(prompt)
@@ -58,8 +57,7 @@ def test_parity_mode_bit_identical(pair):
 def test_parity_mode_greedy(pair):
     cfg, m, om = pair
     prompt = synth.random_prompt(cfg, 32, seed=4)
-    with O.exp_mode(True):
-        want = O.greedy_generate(om, prompt, 48, 128)
+    want = O.greedy_generate(om, prompt, 48, 128)
     got = rf.greedy_generate(m, prompt, 48, 128, kv="f32", attn_exact=True)
     assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
 
@@ -69,8 +67,7 @@ def test_production_mode_bit_identical(pair):
     cache rounding and tile order: every layer and the logits bit for bit."""
     cfg, m, om = pair
     prompt = synth.random_prompt(cfg, 48, seed=6)
-    with O.exp_mode(True):
-        want, want_h = om.context(128, kv_fp16=True, attn_tiles=m.attn_tiles).eval(prompt, want_hidden=True)
+    want, want_h = om.context(128, kv_fp16=True, attn_tiles=m.attn_tiles).eval(prompt, want_hidden=True)
     ctx = m.context(128, kv="f16")
     ctx.set_trace(True)
     got = ctx.eval(prompt)

@@ -261,8 +261,7 @@ def test_tile_attention_is_softmax_attention(P, hd, nt):
     K = rng.normal(size=(P, hd)).astype(np.float32)
     V = rng.normal(size=(P, hd)).astype(np.float32)
     scale = np.float32(1.0) / np.sqrt(np.float32(hd), dtype=np.float32)
-    with O.exp_mode(True):
-        got = O.tile_attention(q, K, V, nt, float(scale))
+    got = O.tile_attention(q, K, V, nt, float(scale))
     s = (K.astype(np.float64) @ q.astype(np.float64)) * float(scale)
     a = np.exp(s - s.max())
     want = (a / a.sum()) @ V.astype(np.float64)
@@ -273,9 +272,20 @@ def test_tile_attention_context_stays_close_to_serial(tiny_model, oracle_tiny):
     """An oracle context in tile mode gives finite logits close to upstream's
     serial attention: only the attention's summation order differs."""
     prompt = synth.random_prompt(synth.CONFIGS["tiny"], 40, seed=3)
-    with O.exp_mode(True):
-        serial = oracle_tiny.context(64).eval(prompt)
-        tiled = oracle_tiny.context(64, attn_tiles=18).eval(prompt)
+    serial = oracle_tiny.context(64).eval(prompt)
+    tiled = oracle_tiny.context(64, attn_tiles=18).eval(prompt)
     assert np.isfinite(tiled).all()
     rel = np.linalg.norm(tiled.astype(np.float64) - serial) / np.linalg.norm(serial.astype(np.float64))
     assert rel <= 3e-2
+
+
+def test_expf_mismatches_counts_bit_differences():
+    """The host-libm comparison the device exponential's test relies on:
+    libm's own values give no mismatch, a value one ulp off is found."""
+    first = int(np.float32(-3.0).view(np.uint32))
+    x = (np.arange(4096, dtype=np.uint32) + np.uint32(first)).view(np.float32)
+    libm = np.array([O.lib_expf(float(v)) for v in x], dtype=np.float32)
+    assert O.expf_mismatches(first, libm) == (0, 4096)
+    off = libm.copy()
+    off[1234] = np.nextafter(off[1234], np.float32(np.inf))
+    assert O.expf_mismatches(first, off) == (1, 1234)

@@ -54,8 +54,7 @@ def test_every_layer_and_the_logits_bit_identical(shape, mode):
     cfg, m, om = shape
     md = _modes(m)[mode]
     prompt = synth.random_prompt(cfg, 24, seed=7)
-    with O.exp_mode(True):
-        want, want_h = om.context(N_CTX, **md["oracle"]).eval(prompt, want_hidden=True)
+    want, want_h = om.context(N_CTX, **md["oracle"]).eval(prompt, want_hidden=True)
     ctx = m.context(N_CTX, kv=md["kv"], attn_exact=md["attn_exact"])
     ctx.set_trace(True)
     got = ctx.eval(prompt)
@@ -74,8 +73,7 @@ def test_greedy_tokens_identical(shape, mode):
     md = _modes(m)[mode]
     prompt = synth.random_prompt(cfg, 16, seed=8)
     n_gen = 32 if cfg.name.startswith("4b") else 16
-    with O.exp_mode(True):
-        want = O.greedy_generate(om, prompt, n_gen, N_CTX, **md["oracle"])
+    want = O.greedy_generate(om, prompt, n_gen, N_CTX, **md["oracle"])
     got = rf.greedy_generate(m, prompt, n_gen, N_CTX, kv=md["kv"], attn_exact=md["attn_exact"])
     assert np.array_equal(got, want), f"{cfg.name} {mode}: first divergence at {np.argmax(got != want)}"
 

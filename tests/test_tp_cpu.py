@@ -213,17 +213,16 @@ def decode_shard(rank, world, dist, mode="terms"):
         best = max(range(world), key=lambda r: (pairs[r][0].item(), -pairs[r][1].item()))
         return int(pairs[best][1].item()), logits
 
-    with O.exp_mode(True):
-        pos, toks, first = 0, [], None
-        for i, t in enumerate(PROMPT):
-            nxt, lg = step(int(t), pos, i + 1 == len(PROMPT))
-            pos += 1
-        first = lg
+    pos, toks, first = 0, [], None
+    for i, t in enumerate(PROMPT):
+        nxt, lg = step(int(t), pos, i + 1 == len(PROMPT))
+        pos += 1
+    first = lg
+    toks.append(nxt)
+    for _ in range(N_GEN - 1):
+        nxt, _ = step(toks[-1], pos, True)
+        pos += 1
         toks.append(nxt)
-        for _ in range(N_GEN - 1):
-            nxt, _ = step(toks[-1], pos, True)
-            pos += 1
-            toks.append(nxt)
     return dict(tokens=toks, logits=first, v0=g["v0"])
 
 
@@ -262,9 +261,8 @@ def _two_ranks(mode):
 def test_two_shards_equal_the_unsharded_decode():
     res = _two_ranks("terms")
     om = O.OracleModel(synth.generate(CFG))
-    with O.exp_mode(True):
-        want_logits = om.context(N_CTX).eval(PROMPT)
-        want = O.greedy_generate(om, PROMPT, N_GEN, N_CTX, repeat_penalty=1.0)
+    want_logits = om.context(N_CTX).eval(PROMPT)
+    want = O.greedy_generate(om, PROMPT, N_GEN, N_CTX, repeat_penalty=1.0)
     got_logits = np.concatenate([res[0]["logits"], res[1]["logits"]])
     assert np.array_equal(got_logits.view(np.uint32), want_logits.view(np.uint32))
     assert res[0]["tokens"] == [int(t) for t in want]
@@ -273,9 +271,8 @@ def test_two_shards_equal_the_unsharded_decode():
 def test_two_shards_sums_exchange_within_1e3():
     res = _two_ranks("sums")
     om = O.OracleModel(synth.generate(CFG))
-    with O.exp_mode(True):
-        want_logits = om.context(N_CTX).eval(PROMPT)
-        want = O.greedy_generate(om, PROMPT, N_GEN, N_CTX, repeat_penalty=1.0)
+    want_logits = om.context(N_CTX).eval(PROMPT)
+    want = O.greedy_generate(om, PROMPT, N_GEN, N_CTX, repeat_penalty=1.0)
     got = np.concatenate([res[0]["logits"], res[1]["logits"]]).astype(np.float64)
     rel = np.linalg.norm(got - want_logits) / np.linalg.norm(want_logits)
     assert rel <= 1e-3, rel

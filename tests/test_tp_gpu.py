@@ -104,6 +104,5 @@ def test_two_shards_equal_one_gpu(cfg, kv, exact, graphs):
     m.close()
     assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
     if exact:
-        with O.exp_mode(True):
-            oracle = O.greedy_generate(O.OracleModel(host), PROMPT, N_GEN, N_CTX, repeat_penalty=1.0)
+        oracle = O.greedy_generate(O.OracleModel(host), PROMPT, N_GEN, N_CTX, repeat_penalty=1.0)
         assert np.array_equal(got, oracle)
