@@ -1886,7 +1886,7 @@ struct foxcuda_context {
   float* x_small = nullptr;  // [0..1] global absmax (o, down), [2..3] best pair, [4..] pairs
   unsigned* x_count = nullptr;  // CTAs done of the fused terms / sums GEMV (o, down)
   int x_mode = FOXCUDA_TP_TERMS;  // the row-parallel exchange (foxcuda_tp_p2p_mode)
-  size_t y_off = 0;             // the sums area of the arena: [o, down][world][n_embd]
+  size_t y_off = 0;             // the sums area of the arena: [o, down][world][n_embd] words
   // a sums exchange whose residual is not completed yet (which, epoch phase;
   // which < 0: none): the next GEMV over the residual completes it
   int fold_which = -1, fold_phase = 0;
@@ -3597,7 +3597,7 @@ extern "C" foxcuda_status foxcuda_tp_p2p_export(foxcuda_context* c, void* handle
     const size_t E = m->info.n_embd;
     const size_t off_d = (AR_TERMS + E * (size_t)c->stride_o * 4 + 255) / 256 * 256;
     const size_t off_y = (off_d + E * (size_t)c->stride_d * 4 + 255) / 256 * 256;
-    const size_t bytes = off_y + 2 * (size_t)m->tp_size * E * 4;
+    const size_t bytes = off_y + 2 * (size_t)m->tp_size * E * 8;
     c->y_off = off_y;
     void* p = nullptr;
     CK(ctx_alloc(c, bytes, &p), "exchange arena");
@@ -3728,7 +3728,7 @@ static cudaError_t launch_xterms(const foxcuda_context* c, const PackedMat& W, i
 // The sums exchange's GEMV of one row-parallel projection: the absmax
 // traded in the prologue (ternary; K-quant shards quantise with their own
 // 256-block scales, which are the unsplit vector's), each row's value pushed
-// to every rank, readiness published by the last CTA (gemv.cuh EPI_XSUM).
+// to every rank as an {epoch, value} word (gemv.cuh EPI_XSUM).
 static cudaError_t launch_xsum(const foxcuda_context* c, const PackedMat& W, int which, int phase) {
   const foxcuda_model* m = c->m;
   GemvParams p = gemv_base(W.type, W.dev, W.n_rows, W.K, W.nb, W.U);
@@ -3740,8 +3740,7 @@ static cudaError_t launch_xsum(const foxcuda_context* c, const PackedMat& W, int
   p.x_world = m->tp_size;
   p.x_which = which;
   p.x_phase = phase;
-  p.x_count = c->x_count + which;
-  p.x_y_off = c->y_off + (size_t)which * m->tp_size * m->info.n_embd * 4;
+  p.x_y_off = c->y_off + (size_t)which * m->tp_size * m->info.n_embd * 8;
   p.x_res = c->x;
   p.pdl = ctx_pdl(c) ? 1 : 0;
   const bool tern = W.type == T_TQ1_0 || W.type == T_TQ2_0;
@@ -3758,7 +3757,7 @@ static void set_nfold(const foxcuda_context* c, GemvParams& p) {
   p.x_rank = m->tp_rank;
   p.x_world = m->tp_size;
   p.pos = c->pos_dev;
-  p.f_y_off = c->y_off + (size_t)c->fold_which * m->tp_size * m->info.n_embd * 4;
+  p.f_y_off = c->y_off + (size_t)c->fold_which * m->tp_size * m->info.n_embd * 8;
   p.f_which = c->fold_which;
   p.f_phase = c->fold_phase;
   p.f_out = c->x;
@@ -3768,7 +3767,7 @@ static void set_nfold(const foxcuda_context* c, GemvParams& p) {
 static cudaError_t enqueue_fold(foxcuda_context* c) {
   if (c->fold_which < 0) return cudaSuccess;
   const int E = (int)c->m->info.n_embd;
-  const size_t y = c->y_off + (size_t)c->fold_which * c->m->tp_size * E * 4;
+  const size_t y = c->y_off + (size_t)c->fold_which * c->m->tp_size * E * 8;
   fold_sum_x_kernel<<<(E + 255) / 256, 256, 0, c->stream>>>(xparams(c), y, c->fold_which, c->fold_phase, E, c->x);
   c->fold_which = -1;
   return cudaGetLastError();

@@ -30,16 +30,16 @@
 //   PRO_NFOLD   as PRO_NORM, with the residual first completed from a
 //               partial-sum exchange over peer memory: x = the ranks' row
 //               sums added in rank order (rank 0's carries the residual),
-//               read from this rank's arena once every rank has signalled;
-//               CTA 0 stores the completed residual back
+//               each read from this rank's arena once it carries the
+//               exchange's epoch; CTA 0 stores the completed residual back
 // EPI_TERMS (tensor-parallel row shards) writes the per-block float terms
 // instead of folding them; the shards' terms are gathered and folded in
 // upstream's block order by fold_kernel (fold_x_kernel over peer memory,
 // where the CTA that finishes last publishes this rank's readiness).
 // EPI_XSUM (tensor-parallel row shards, partial-sum exchange) stores each
 // row's value, this shard's blocks folded in order times the activation
-// scale (rank 0 adds the residual), into this rank's slot of every rank's
-// arena; the last CTA publishes readiness as EPI_TERMS does.
+// scale (rank 0 adds the residual), as an {epoch, value} word into this
+// rank's slot of every rank's arena.
 // Epilogues: store; residual add (src/ops.c:50-54); RoPE on adjacent pairs
 // (src/ops.c:56-73) + K/V cache write for the fused q|k|v matrix; SwiGLU
 // (src/ops.c:41-48) for the interleaved gate|up matrix.
@@ -109,44 +109,51 @@ struct GemvParams {
 
 __host__ __device__ constexpr bool pro_norms(int pro) { return pro == PRO_NORM || pro == PRO_NFOLD; }
 
-// PRO_NFOLD: wait (bounded) until every rank has signalled its partial sums
-// of the exchange; every thread then acquires the flags itself, which orders
-// its reads of the sums. False when a wait gave up (error word set to 2).
-FOX_DEV bool nfold_wait(const GemvParams& p, int* ok_sh) {
-  if (threadIdx.x == 0) *ok_sh = 1;
-  __syncthreads();
-  const uint32_t ep = tp_epoch(p.pos, p.f_phase);
-  const uint32_t* ready = reinterpret_cast<const uint32_t*>(p.x_peers[p.x_rank] + AR_READY) + p.f_which * TPX_MAX;
-  if ((int)threadIdx.x < p.x_world && !wait_u32(ready + threadIdx.x, ep, p.err)) {
-    *ok_sh = 0;
-    if (p.err) atomicExch(p.err, 2);
-  }
-  __syncthreads();
-  const bool ok = *ok_sh != 0;
-  if (ok)
-    for (int k = 0; k < p.x_world; ++k) (void)ld_acquire_sys(ready + k);
-  return ok;
-}
-
-// Residual elements i..i+3 completed from the ranks' partial sums, added in
-// rank order (read through L2: the sums were written by other GPUs).
-FOX_DEV float4 nfold_x4(const GemvParams& p, int i, int n) {
-  const float* y = reinterpret_cast<const float*>(p.x_peers[p.x_rank] + p.f_y_off);
-  float4 a = __ldcg(reinterpret_cast<const float4*>(y + i));
-  for (int k = 1; k < p.x_world; ++k) {
-    const float4 b = __ldcg(reinterpret_cast<const float4*>(y + (size_t)k * n + i));
-    a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
-    a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+// PRO_NFOLD: elements i..i+3 of the residual completed from a sums exchange:
+// the ranks' {epoch, value} words read until each carries this exchange's
+// epoch (bounded; a wait that gives up sets the error word to 2 and *ok to
+// false), the values added in rank order.
+FOX_DEV float4 nfold_x4(const GemvParams& p, int i, int n, uint32_t ep, bool* ok) {
+  const uint64_t* y = reinterpret_cast<const uint64_t*>(p.x_peers[p.x_rank] + p.f_y_off);
+  float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int k = 0; k < p.x_world; ++k) {
+    const uint64_t* w = y + (size_t)k * n + i;
+    uint64_t v0 = 0, v1 = 0, v2 = 0, v3 = 0;
+    bool got = false;
+    for (int it = 0; it < (1 << 22); ++it) {
+      ld_volatile_v2(w, v0, v1);
+      ld_volatile_v2(w + 2, v2, v3);
+      if ((uint32_t)(v0 >> 32) == ep && (uint32_t)(v1 >> 32) == ep && (uint32_t)(v2 >> 32) == ep &&
+          (uint32_t)(v3 >> 32) == ep) {
+        got = true;
+        break;
+      }
+      if (it >= 16) __nanosleep(64);
+      if ((it & 255) == 255 && step_failed(p.err)) break;
+    }
+    if (!got) {
+      if (p.err) atomicExch(p.err, 2);
+      *ok = false;
+    }
+    const float4 b = make_float4(__uint_as_float((uint32_t)v0), __uint_as_float((uint32_t)v1),
+                                 __uint_as_float((uint32_t)v2), __uint_as_float((uint32_t)v3));
+    if (k == 0) {
+      a = b;
+    } else {
+      a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
+      a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+    }
   }
   return a;
 }
 
-// EPI_XSUM: row r's value v into this rank's slot of every rank's arena
-// (rank 0's carries the residual).
-FOX_DEV void xsum_store(const GemvParams& p, int r, float v) {
+// EPI_XSUM: row r's value v as an {epoch, value} word into this rank's slot
+// of every rank's arena (rank 0's carries the residual).
+FOX_DEV void xsum_store(const GemvParams& p, int r, float v, uint32_t ep) {
   if (p.x_rank == 0) v = __fadd_rn(p.x_res[r], v);
+  const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(v);
   for (int k = 0; k < p.x_world; ++k)
-    reinterpret_cast<float*>(p.x_peers[k] + p.x_y_off)[(size_t)p.x_rank * p.n_rows + r] = v;
+    st_relaxed_sys(reinterpret_cast<uint64_t*>(p.x_peers[k] + p.x_y_off) + (size_t)p.x_rank * p.n_rows + r, word);
 }
 
 // PRO_XAMAX: the largest absmax over all ranks. Every CTA publishes the same
@@ -159,7 +166,7 @@ FOX_DEV float x_trade_amax(const GemvParams& p, float am) {
     const uint32_t ep = tp_epoch(p.pos, p.x_phase);
     const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(am);
     for (int k = 0; k < p.x_world; ++k)
-      st_release_sys(reinterpret_cast<uint64_t*>(p.x_peers[k] + AR_AMAX) + p.x_which * TPX_MAX + p.x_rank, word);
+      st_relaxed_sys(reinterpret_cast<uint64_t*>(p.x_peers[k] + AR_AMAX) + p.x_which * TPX_MAX + p.x_rank, word);
     const uint64_t* mine = reinterpret_cast<const uint64_t*>(p.x_peers[p.x_rank] + AR_AMAX) + p.x_which * TPX_MAX;
     float g = 0.0f;
     for (int k = 0; k < p.x_world; ++k) {
@@ -497,15 +504,12 @@ gemv_kernel(const GemvParams p) {
 
   // ---------------- prologue: the activation vector ----------------------
   if (PRO != PRO_PREQ) {
-    bool folded = false;
-    if (PRO == PRO_NFOLD) {
-      __shared__ int nf_ok;
-      folded = nfold_wait(p, &nf_ok);
-    }
+    const uint32_t fep = PRO == PRO_NFOLD ? tp_epoch(p.pos, p.f_phase) : 0u;
+    bool fok = true;
     double ss = 0.0;
     for (int i = tid * 4; i < K; i += nth * 4) {
-      const float4 v = folded ? nfold_x4(p, i, K) : *reinterpret_cast<const float4*>(p.x + i);
-      if (PRO == PRO_NFOLD && folded && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
+      const float4 v = PRO == PRO_NFOLD ? nfold_x4(p, i, K, fep, &fok) : *reinterpret_cast<const float4*>(p.x + i);
+      if (PRO == PRO_NFOLD && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
       if (pro_norms(PRO))
         ss = ss + (double)v.x * (double)v.x + (double)v.y * (double)v.y +
              (double)v.z * (double)v.z + (double)v.w * (double)v.w;
@@ -629,7 +633,7 @@ gemv_kernel(const GemvParams p) {
       const int r = u * U + tid;
       if (EPI == EPI_STORE) p.out[r] = v;
       if (EPI == EPI_ADD) p.out[r] = __fadd_rn(p.out[r], v);
-      if (EPI == EPI_XSUM) xsum_store(p, r, v);
+      if (EPI == EPI_XSUM) xsum_store(p, r, v, tp_epoch(p.pos, p.x_phase));
       if (EPI == EPI_QKV || EPI == EPI_SWIGLU) vals[tid] = v;
     }
     if (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
@@ -695,7 +699,7 @@ gemv_kernel(const GemvParams p) {
         __syncthreads();
         // still counted, so the completion count is rearmed for the next
         // exchange; the error word marks this step's terms as unusable
-        if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
+        if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
         return;
       }
       if (tid < ru * nb) {
@@ -730,7 +734,7 @@ gemv_kernel(const GemvParams p) {
       if (Tr::PREFETCH) cur = nxt;
     }
   }
-  if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
+  if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
 }
 
 }  // namespace fox

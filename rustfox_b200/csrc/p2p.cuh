@@ -8,8 +8,8 @@
 //   u32 ready[2][8]   at AR_READY  epoch at which each rank's terms are complete
 //   float terms_o     at AR_TERMS  this rank's o terms   [n_embd][stride_o]
 //   float terms_d     after it     this rank's down terms [n_embd][stride_d]
-//   float sums[2][world][n_embd]   every rank's row sums of the o / down
-//                                  projection (the partial-sum exchange)
+//   u64 sums[2][world][n_embd]     every rank's row sums of the o / down
+//                                  projection, {epoch, value bits} words
 // A rank writes its slot in every rank's arena (its own included) and reads
 // the slots of its own arena; the block terms stay where they were written
 // and are read from the owner's arena, the row sums are pushed to every
@@ -30,9 +30,13 @@
 // 2 * layer + which + 1 (the pick is 255), so a captured step needs no host
 // input and every exchange of a run has its own epoch. A rank overwrites a
 // slot of the same phase only after an exchange that every rank reaches only
-// after reading that slot, so no value is lost. A slot is published with
-// st.release.sys and read with ld.acquire.sys. Every wait gives up after
-// about a second, sets the context's error word and lets the kernel finish.
+// after reading that slot, so no value is lost. The absmax and pick slots and
+// the row sums are {epoch, value} words, each written and read in one 64-bit
+// access (relaxed, system scope): a reader that sees its epoch has its value,
+// with no fence on either side. The block terms of the terms exchange are
+// plain floats, published behind a readiness flag (st.release.sys, read with
+// ld.acquire.sys). Every wait gives up after about a second, sets the
+// context's error word and lets the kernel finish.
 #pragma once
 
 #include <math_constants.h>
@@ -68,6 +72,22 @@ FOX_DEV uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// Self-validating words ({epoch, value} in one aligned 64-bit word, written
+// and read in one access) need no fence: a reader that sees its epoch sees
+// its value. Relaxed system-scope accesses keep them out of the L1 and
+// let the stores leave without waiting for earlier writes.
+FOX_DEV void st_relaxed_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+FOX_DEV uint64_t ld_relaxed_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+FOX_DEV void ld_volatile_v2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 FOX_DEV uint32_t tp_epoch(const int* pos, int phase) {
   return ((uint32_t)(*pos + 1) << 8) | (uint32_t)phase;
 }
@@ -91,7 +111,7 @@ FOX_DEV bool wait_u32(const uint32_t* p, uint32_t ep, const int* err) {
 }
 FOX_DEV bool wait_hi(const uint64_t* p, uint32_t ep, uint64_t* out, const int* err) {
   for (int i = 0; i < (1 << 22); ++i) {
-    const uint64_t w = ld_acquire_sys(p);
+    const uint64_t w = ld_relaxed_sys(p);
     if ((uint32_t)(w >> 32) == ep) { *out = w; return true; }
     if (i >= 16) __nanosleep(256);
     if ((i & 255) == 255 && step_failed(err)) return false;
@@ -111,7 +131,7 @@ __global__ void __launch_bounds__(1024) amax_x_kernel(const XParams x, const flo
   const uint32_t ep = tp_epoch(x.pos, phase);
   const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(am);
   for (int k = 0; k < x.world; ++k)
-    st_release_sys(reinterpret_cast<uint64_t*>(x.peers[k] + AR_AMAX) + which * TPX_MAX + x.rank, word);
+    st_relaxed_sys(reinterpret_cast<uint64_t*>(x.peers[k] + AR_AMAX) + which * TPX_MAX + x.rank, word);
   const uint64_t* mine = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + AR_AMAX) + which * TPX_MAX;
   float g = 0.0f;
   for (int k = 0; k < x.world; ++k) {
@@ -179,29 +199,27 @@ __global__ void fold_x_kernel(const XParams x, const FoldXParams f) {
 }
 
 // The residual completed from the sums exchange (the ranks' rows added in
-// rank order), as a kernel of its own: before the head, or where the next
-// GEMV does not complete it in its prologue (gemv.cuh PRO_NFOLD, the same
-// additions in the same order). Releases its successor at once.
+// rank order, each {epoch, value} word read until it carries this
+// exchange's epoch), as a kernel of its own: before the head, or where the
+// next GEMV does not complete it in its prologue (gemv.cuh PRO_NFOLD, the
+// same additions in the same order). Releases its successor at once.
 __global__ void fold_sum_x_kernel(const XParams x, size_t y_off, int which, int phase, int n,
                                   float* __restrict__ out) {
   griddep_launch_dependents();
-  __shared__ int ok_sh;
   const uint32_t ep = tp_epoch(x.pos, phase);
-  const uint32_t* ready = reinterpret_cast<const uint32_t*>(x.peers[x.rank] + AR_READY) + which * TPX_MAX;
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    for (int k = 0; k < x.world && ok; ++k) ok = wait_u32(ready + k, ep, x.err);
-    ok_sh = ok;
-    if (!ok && x.err) atomicExch(x.err, 2);
-  }
-  __syncthreads();
-  if (!ok_sh) return;
-  for (int k = 0; k < x.world; ++k) (void)ld_acquire_sys(ready + k);
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n) return;
-  const float* y = reinterpret_cast<const float*>(x.peers[x.rank] + y_off);
-  float a = __ldcg(y + r);
-  for (int k = 1; k < x.world; ++k) a = __fadd_rn(a, __ldcg(y + (size_t)k * n + r));
+  const uint64_t* y = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + y_off);
+  float a = 0.0f;
+  for (int k = 0; k < x.world; ++k) {
+    uint64_t w = 0;
+    if (!wait_hi(y + (size_t)k * n + r, ep, &w, x.err)) {
+      if (x.err) atomicExch(x.err, 2);
+      return;
+    }
+    const float v = __uint_as_float((uint32_t)w);
+    a = k == 0 ? v : __fadd_rn(a, v);
+  }
   out[r] = a;
 }
 
@@ -214,8 +232,8 @@ __global__ void pick_x_kernel(const XParams x, const float* __restrict__ best, f
   const uint64_t w1 = ((uint64_t)ep << 32) | __float_as_uint(best[1]);
   for (int k = 0; k < x.world; ++k) {
     uint64_t* slot = reinterpret_cast<uint64_t*>(x.peers[k] + AR_PICK) + 2 * x.rank;
-    st_release_sys(slot, w0);
-    st_release_sys(slot + 1, w1);
+    st_relaxed_sys(slot, w0);
+    st_relaxed_sys(slot + 1, w1);
   }
   const uint64_t* mine = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + AR_PICK);
   for (int k = 0; k < x.world; ++k) {

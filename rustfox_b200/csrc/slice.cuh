@@ -254,15 +254,12 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
   bool got = true;
   float am = 0.0f;
   if (PRO != PRO_PREQ) {
-    bool folded = false;
-    if (PRO == PRO_NFOLD) {
-      __shared__ int nf_ok;
-      folded = nfold_wait(p, &nf_ok);
-    }
+    const uint32_t fep = PRO == PRO_NFOLD ? tp_epoch(p.pos, p.f_phase) : 0u;
+    bool fok = true;
     double ss = 0.0;
     for (int i = tid * 4; i < K; i += nth * 4) {
-      const float4 v = folded ? nfold_x4(p, i, K) : *reinterpret_cast<const float4*>(p.x + i);
-      if (PRO == PRO_NFOLD && folded && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
+      const float4 v = PRO == PRO_NFOLD ? nfold_x4(p, i, K, fep, &fok) : *reinterpret_cast<const float4*>(p.x + i);
+      if (PRO == PRO_NFOLD && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
       if (pro_norms(PRO))
         ss = ss + (double)v.x * (double)v.x + (double)v.y * (double)v.y +
              (double)v.z * (double)v.z + (double)v.w * (double)v.w;
@@ -372,8 +369,8 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     }
     __syncthreads();
     // still counted, so the completion count is rearmed for the next
-    // exchange; the error word marks this step's sums as unusable
-    if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
+    // exchange; the error word marks this step's terms as unusable
+    if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
     return;
   }
 
@@ -400,7 +397,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     const float v = __fmul_rn(acc, act_scale);
     if (EPI == EPI_STORE) p.out[row0 + r] = v;
     if (EPI == EPI_ADD) p.out[row0 + r] = __fadd_rn(p.out[row0 + r], v);
-    if (EPI == EPI_XSUM) xsum_store(p, row0 + r, v);
+    if (EPI == EPI_XSUM) xsum_store(p, row0 + r, v, tp_epoch(p.pos, p.x_phase));
     if (EPI == EPI_QKV || EPI == EPI_SWIGLU) vals[r] = v;
   }
   if (EPI == EPI_QKV || EPI == EPI_SWIGLU) __syncthreads();
@@ -443,7 +440,7 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
     }
   }
   FOX_SLICE_MARK(12);
-  if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
+  if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
 }
 
 // ---------------------------------------------------------------------------
@@ -568,14 +565,11 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
   bool got = true;
   float am = 0.0f;
   float norm_scale = 1.0f;
-  bool folded = false;
-  if (PRO == PRO_NFOLD) {
-    __shared__ int nf_ok;
-    folded = nfold_wait(p, &nf_ok);
-  }
+  const uint32_t fep = PRO == PRO_NFOLD ? tp_epoch(p.pos, p.f_phase) : 0u;
+  bool fok = true;
   // the input, completed from the ranks' row sums under PRO_NFOLD
   auto load4 = [&](int i) -> float4 {
-    if (PRO == PRO_NFOLD && folded) return nfold_x4(p, i, K);
+    if (PRO == PRO_NFOLD) return nfold_x4(p, i, K, fep, &fok);
     return *reinterpret_cast<const float4*>(p.x + i);
   };
   auto norm4 = [&](float4 v, int i) -> float4 {
@@ -597,7 +591,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
     double ss = 0.0;
     for (int i = tid * 4; i < K; i += nth * 4) {
       const float4 v = load4(i);
-      if (PRO == PRO_NFOLD && folded && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
+      if (PRO == PRO_NFOLD && blockIdx.x == 0) *reinterpret_cast<float4*>(p.f_out + i) = v;
       if (pro_norms(PRO))
         ss = ss + (double)v.x * (double)v.x + (double)v.y * (double)v.y +
              (double)v.z * (double)v.z + (double)v.w * (double)v.w;
@@ -702,7 +696,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
       __syncthreads();
       // still counted, so the completion count is rearmed for the next
       // exchange; the error word marks this step's sums as unusable
-      if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
+      if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
       return;
     }
     const int wofs = (int)(g.w_off + (size_t)(c % g.nbuf) * g.chunk_bytes);  // this chunk's buffer
@@ -743,7 +737,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
     const float v = __fmul_rn(acc, act_scale);
     if (EPI == EPI_STORE) p.out[row0 + r] = v;
     if (EPI == EPI_ADD) p.out[row0 + r] = __fadd_rn(p.out[row0 + r], v);
-    if (EPI == EPI_XSUM) xsum_store(p, row0 + r, v);
+    if (EPI == EPI_XSUM) xsum_store(p, row0 + r, v, tp_epoch(p.pos, p.x_phase));
     if (EPI == EPI_QKV || EPI == EPI_SWIGLU) vals[r] = v;
   }
   if (EPI == EPI_QKV || EPI == EPI_SWIGLU) __syncthreads();
@@ -785,7 +779,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
       p.out[(u0 + ul) * hu + i] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf_up(-gt))), up);
     }
   }
-  if ((EPI == EPI_TERMS || EPI == EPI_XSUM) && p.x_count) x_signal_ready(p);
+  if (EPI == EPI_TERMS && p.x_count) x_signal_ready(p);
 }
 
 }  // namespace fox

@@ -220,35 +220,34 @@ def test_a_count_taken_before_the_terms_are_written_is_caught():
 
 # ---- the sums exchange (gemv.cuh EPI_XSUM / PRO_NFOLD, p2p.cuh) -------------
 #
-# Each row-parallel producer pushes its row values into its own slot of every
-# rank's sums area (one area per projection kind, o or down, not one per
-# layer), and its last CTA publishes readiness. The residual is completed by
-# the next GEMV over it (gate|up after o, the next layer's q|k|v after down,
-# the head after the last layer, the position advance of a prompt token),
-# which waits for every rank's readiness and adds the ranks' rows in rank
-# order. With ternary shards the producer trades the absmax first; K-quant
-# shards do not, so the single area per kind must be safe on the interleaving
-# of the completions alone: a rank pushes o of layer l only after completing
-# down of layer l - 1, which needs every rank's down push, which each rank
-# makes only after completing o of layer l - 1; across tokens the last
-# completion of a token plays that part, so it is made even where nothing
-# reads the residual (a prompt token).
+# Each row-parallel producer pushes its row values, each as one {epoch, value}
+# word, into its own slot of every rank's sums area (one area per projection
+# kind, o or down, not one per layer); nothing else is published. The
+# residual is completed by the next GEMV over it (gate|up after o, the next
+# layer's q|k|v after down, the head after the last layer, the position
+# advance of a prompt token), which reads every rank's words until each
+# carries the exchange's epoch and adds the ranks' rows in rank order. With
+# ternary shards the producer trades the absmax first; K-quant shards do not,
+# so the single area per kind must be safe on the interleaving of the
+# completions alone: a rank pushes o of layer l only after completing down of
+# layer l - 1, which needs every rank's down words, which each rank pushes
+# only after completing o of layer l - 1; across tokens the last completion
+# of a token plays that part, so it is made even where nothing reads the
+# residual (a prompt token).
 
-def _run_sums(world, n_layer, n_tok, rows, seed, trade, ctas=3, ready_early=False, drop_prompt_fold=False):
+def _run_sums(world, n_layer, n_tok, rows, seed, trade, ctas=3, drop_prompt_fold=False, skip_epoch_check=False):
     rng = np.random.default_rng(seed)
     vals = rng.normal(0, 1, (n_tok, n_layer, 2, world, rows)).astype(np.float32)
     amaxes = rng.random((n_tok, n_layer, 2, world)).astype(np.float32)
     picks = [pos % 2 == 1 for pos in range(n_tok)]  # tokens with a head
-    sums = [np.zeros((2, world, rows), dtype=np.float32) for _ in range(world)]
-    ready = [np.zeros((2, TPX_MAX), dtype=np.uint32) for _ in range(world)]
+    # words[k][which][rank][row] = (epoch, value), replaced whole (one access)
+    words = [[[[(0, np.float32(0))] * rows for _ in range(world)] for _ in range(2)] for _ in range(world)]
     amx = [Arena(1, 1) for _ in range(world)]
     got = [dict() for _ in range(world)]
     errors = []
 
     def produce(r, pos, layer, which, rnd):
         ep = _epoch(pos, 2 * layer + which + 1)
-        count = [0]
-        lock = threading.Lock()
         bounds = np.linspace(0, rows, ctas + 1).astype(int)
         cta_errors = []
 
@@ -257,24 +256,9 @@ def _run_sums(world, n_layer, n_tok, rows, seed, trade, ctas=3, ready_early=Fals
                 time.sleep(rnd.random() * 1e-4)
                 if trade:
                     _trade_amax(amx, world, r, which, ep, amaxes[pos, layer, which, r])
-                lo, hi = bounds[j], bounds[j + 1]
-
-                def push():
+                for row in range(bounds[j], bounds[j + 1]):
                     for k in range(world):
-                        sums[k][which, r, lo:hi] = vals[pos, layer, which, r, lo:hi]
-
-                if not ready_early:
-                    push()
-                with lock:
-                    last = count[0] == ctas - 1
-                    count[0] += 1
-                if last:
-                    count[0] = 0
-                    for k in range(world):
-                        ready[k][which, r] = np.uint32(ep)
-                if ready_early:  # planted: rows pushed after readiness
-                    time.sleep(5e-3)
-                    push()
+                        words[k][which][r][row] = (ep, vals[pos, layer, which, r, row])
             except BaseException as e:  # noqa: BLE001
                 cta_errors.append(e)
 
@@ -290,12 +274,16 @@ def _run_sums(world, n_layer, n_tok, rows, seed, trade, ctas=3, ready_early=Fals
     def complete(r, pending):
         pos, layer, which = pending
         ep = _epoch(pos, 2 * layer + which + 1)
+        acc = None
         for k in range(world):
-            _wait(lambda: int(ready[r][which, k]) >= ep, "ready")
-            assert int(ready[r][which, k]) == ep, f"rank {r} saw a later ready epoch"
-        acc = sums[r][which, 0].copy()
-        for k in range(1, world):
-            acc = (acc + sums[r][which, k]).astype(np.float32)
+            row_vals = np.zeros(rows, dtype=np.float32)
+            for row in range(rows):
+                if not skip_epoch_check:
+                    _wait(lambda: words[r][which][k][row][0] >= ep, "sums word")
+                e, v = words[r][which][k][row]
+                assert skip_epoch_check or e == ep, f"rank {r} saw a later epoch"
+                row_vals[row] = v
+            acc = row_vals if acc is None else (acc + row_vals).astype(np.float32)
         got[r][pending] = acc
 
     def rank_main(r):
@@ -348,19 +336,23 @@ def test_sums_protocol_reads_every_rows_of_their_own_step(world, trade):
     assert n == world * n_tok * 2 * n_layer  # every exchange is completed
 
 
-def test_sums_readiness_before_the_rows_is_caught():
-    """The model with a planted ordering mistake: readiness published before
-    the rows are pushed. The check above sees completions read stale rows."""
-    bad, _ = _run_sums(2, 2, 2, rows=6, seed=3, trade=False, ready_early=True)
-    assert bad
+def test_sums_without_the_epoch_check_is_caught():
+    """The model with a planted mistake: the completion takes whatever words
+    are there instead of waiting for its epoch. The check above sees rows
+    of another step (or none yet)."""
+    hits = 0
+    for seed in range(4):
+        bad, _ = _run_sums(3, 2, 3, rows=6, seed=30 + seed, trade=False, skip_epoch_check=True)
+        hits += bool(bad)
+    assert hits
 
 
 def test_sums_dropping_a_prompt_tokens_completion_is_caught():
     """Planted in the model: a prompt token skips its last completion. With
     K-quant shards (no absmax trade) nothing then keeps a fast rank from
-    pushing the next token's o rows (or readiness) over those a slower rank
-    still reads; the device completes it at the position advance for that
-    reason. Seen as stale rows, a later epoch, or a wait that gives up."""
+    pushing the next token's o rows over those a slower rank still reads;
+    the device completes it at the position advance for that reason. Seen
+    as stale rows, a later epoch, or a wait that gives up."""
     hits = 0
     for seed in range(6):
         bad, _ = _run_sums(8, 3, 6, rows=7, seed=100 + seed, trade=False, drop_prompt_fold=True)
