@@ -438,8 +438,7 @@ foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
  *   between steps):
  *   FOXCUDA_TP_TERMS (default)  two kernels: the terms GEMV with the absmax
  *     exchange and the readiness signal inside it, then the fold of every
- *     rank's block terms in upstream's order (FOXCUDA_TP_P2P_FUSED=0 in the
- *     environment: four kernels). The values and their order are those of
+ *     rank's block terms in upstream's order. The values and their order are those of
  *     the collective form: the single-GPU decode's, bit for bit.
  *   FOXCUDA_TP_SUMS  one kernel: the GEMV trades the absmax, folds this
  *     shard's blocks per row and pushes the n_embd row values (rank 0's

@@ -3676,16 +3676,6 @@ extern "C" foxcuda_status foxcuda_tp_p2p_clear(foxcuda_context* c) {
   return FOXCUDA_OK;
 }
 
-// FOXCUDA_TP_P2P_FUSED=0 keeps the absmax exchange and the readiness signal
-// in kernels of their own (four launches per row-parallel projection, not two).
-static bool p2p_fused() {
-  static const bool on = [] {
-    const char* v = getenv("FOXCUDA_TP_P2P_FUSED");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 // The terms GEMV with both exchanges inside (gemv.cuh PRO_XAMAX, EPI_TERMS
 // with the readiness count): ternary shards trade the absmax in the
 // prologue; K-quant shards quantise with their own 256-block scales.
@@ -3813,18 +3803,7 @@ extern "C" foxcuda_status foxcuda_tp_p2p_row(foxcuda_context* c, uint32_t layer,
   float* amax = c->x_small + which;
   const size_t off = which == 0 ? AR_TERMS : c->terms_d_off;
   const int stride = which == 0 ? c->stride_o : c->stride_d;
-  if (p2p_fused()) {
-    CK(launch_xterms(c, W, which, phase, amax, (float*)(c->arena + off), stride), "tp terms exchange");
-  } else {
-    if (tern) {
-      const int n = which == 0 ? (int)(m->loc.n_head * m->info.head_dim) : (int)m->loc.n_ff;
-      amax_x_kernel<<<1, 1024, 0, c->stream>>>(x, which == 0 ? c->att : c->h, n, which, phase, amax);
-      CK(cudaGetLastError(), "tp amax exchange");
-    }
-    st = foxcuda_tp_terms(c, layer, which, tern ? amax : nullptr, (float*)(c->arena + off), (uint32_t)stride);
-    if (st) return st;
-    signal_x_kernel<<<1, 32, 0, c->stream>>>(x, which, phase);
-  }
+  CK(launch_xterms(c, W, which, phase, amax, (float*)(c->arena + off), stride), "tp terms exchange");
   FoldXParams f;
   memset(&f, 0, sizeof f);
   f.terms_off = off;

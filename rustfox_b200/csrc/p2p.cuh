@@ -119,42 +119,6 @@ FOX_DEV bool wait_hi(const uint64_t* p, uint32_t ep, uint64_t* out, const int* e
   return false;
 }
 
-// This shard's absmax of v (one CTA), published to every rank; the largest
-// over all ranks (the absmax of the whole vector) into out[0].
-__global__ void __launch_bounds__(1024) amax_x_kernel(const XParams x, const float* __restrict__ v, int n,
-                                                      int which, int phase, float* out) {
-  __shared__ float red[32];
-  float am = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) am = absmax_acc(am, v[i]);
-  am = block_reduce<float>(am, red, OpMax(), 0.0f);
-  if (threadIdx.x != 0) return;
-  const uint32_t ep = tp_epoch(x.pos, phase);
-  const uint64_t word = ((uint64_t)ep << 32) | __float_as_uint(am);
-  for (int k = 0; k < x.world; ++k)
-    st_relaxed_sys(reinterpret_cast<uint64_t*>(x.peers[k] + AR_AMAX) + which * TPX_MAX + x.rank, word);
-  const uint64_t* mine = reinterpret_cast<const uint64_t*>(x.peers[x.rank] + AR_AMAX) + which * TPX_MAX;
-  float g = 0.0f;
-  for (int k = 0; k < x.world; ++k) {
-    uint64_t w = 0;
-    if (!wait_hi(mine + k, ep, &w, x.err)) {
-      if (x.err) atomicExch(x.err, 2);
-      g = 0.0f;
-      break;
-    }
-    g = fmaxf(g, __uint_as_float((uint32_t)w));
-  }
-  out[0] = g;
-}
-
-// After this rank's terms kernel (the previous launch): its terms are complete.
-__global__ void signal_x_kernel(const XParams x, int which, int phase) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  __threadfence_system();
-  const uint32_t ep = tp_epoch(x.pos, phase);
-  for (int k = 0; k < x.world; ++k)
-    st_release_sys(reinterpret_cast<uint32_t*>(x.peers[k] + AR_READY) + which * TPX_MAX + x.rank, ep);
-}
-
 // fold_kernel (ops.cuh) reading every rank's terms from its arena once all
 // ranks have signalled them: the same sums in the same order.
 struct FoldXParams {

@@ -16,8 +16,8 @@ write its terms, signal ready into every arena, wait for all ranks' ready,
 fold. The pick publishes a {value, index} pair, waits, and takes the first
 strict maximum.
 
-The fused form (gemv.cuh PRO_XAMAX with the EPI_TERMS readiness count, the
-default) runs the first three steps inside one kernel: every CTA, a thread
+The device (gemv.cuh and slice.cuh PRO_XAMAX with the EPI_TERMS readiness
+count) runs the first three steps inside one kernel: every CTA, a thread
 here, publishes the same absmax and waits for all ranks' slots, writes the
 terms of its own rows, and counts itself done; the CTA that counts last
 publishes readiness. The fold starts after every CTA has finished (stream

@@ -9,10 +9,9 @@
 The one-GPU case runs the exchange kernels with a single rank (each slot
 written and read in the rank's own arena). The GEMVs, the attention and the
 head overlap their predecessors (programmatic stream serialisation), as in
-the single-GPU step. By default the absmax exchange and the readiness signal
-run inside the terms GEMV (two launches per row-parallel projection); one
-test keeps them in kernels of their own (FOXCUDA_TP_P2P_FUSED=0). The
-two-GPU case maps the peer's arena through CUDA IPC. The same harness as
+the single-GPU step. The absmax exchange and the readiness signal run inside
+the terms GEMV (two launches per row-parallel projection). The two-GPU case
+maps the peer's arena through CUDA IPC. The same harness as
 test_tp_gpu.py applies: ranks are child processes, and the parent fails as
 soon as one exits abnormally.
 
@@ -39,12 +38,8 @@ N_GEN = 32
 N_CTX = 96
 
 
-def run_rank(rank, world, port, cfg, kv, exact, graphs, out_q, exchange="p2p", penalty=1.0, fused=True,
-             trace=False):
+def run_rank(rank, world, port, cfg, kv, exact, graphs, out_q, exchange="p2p", penalty=1.0, trace=False):
     import datetime
-    import os
-    # read once by the library, at the first exchange
-    os.environ["FOXCUDA_TP_P2P_FUSED"] = "1" if fused else "0"
     import torch.distributed as dist
     import rustfox_b200 as rf
     from rustfox_b200.tp import TPContext
@@ -91,8 +86,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _tp_run(cfg, kv, exact, graphs, world, limit_s=240, exchange="p2p", penalty=1.0, fused=True,
-            trace=False):
+def _tp_run(cfg, kv, exact, graphs, world, limit_s=240, exchange="p2p", penalty=1.0, trace=False):
     import queue
     import time
     import torch.multiprocessing as mp
@@ -100,7 +94,7 @@ def _tp_run(cfg, kv, exact, graphs, world, limit_s=240, exchange="p2p", penalty=
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=run_rank,
-                         args=(r, world, port, cfg, kv, exact, graphs, q, exchange, penalty, fused, trace))
+                         args=(r, world, port, cfg, kv, exact, graphs, q, exchange, penalty, trace))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -160,20 +154,6 @@ def test_repeat_penalty_shards_equal_one_gpu(world, exchange, graphs):
     got = _tp_tokens(CFG_TQ2, "f16", False, graphs, world, exchange=exchange, penalty=1.1)
     m = rf.Model.from_synthetic(synth.generate(CFG_TQ2))
     want = rf.greedy_generate(m, PROMPT, N_GEN, N_CTX, kv="f16", repeat_penalty=1.1)
-    m.close()
-    assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
-
-
-@pytest.mark.parametrize("world", [1, 2])
-def test_p2p_separate_exchange_kernels_equal_one_gpu(world):
-    """FOXCUDA_TP_P2P_FUSED=0: the absmax exchange and the readiness signal in
-    kernels of their own, four launches per row-parallel projection."""
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
-    import rustfox_b200 as rf
-    got = _tp_tokens(CFG_TQ2, "f16", False, True, world, fused=False)
-    m = rf.Model.from_synthetic(synth.generate(CFG_TQ2))
-    want = rf.greedy_generate(m, PROMPT, N_GEN, N_CTX, kv="f16", repeat_penalty=1.0)
     m.close()
     assert np.array_equal(got, want), f"first divergence at {np.argmax(got != want)}"
 
