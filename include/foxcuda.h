@@ -95,7 +95,7 @@ foxcuda_status foxcuda_gemm_tq2_i8_packed(const int8_t *q, const float *act_scal
  * quantize_activations_k, src/kernels.c:722-754). act_scales holds
  * n_tokens x n_cols/256 floats. Each token's row is meant to equal the
  * single-token GEMV bit for bit. It runs 8 (Q6_K) or 16 (Q4_K) tokens per
- * tile. Not yet run on a B200. */
+ * tile. */
 foxcuda_status foxcuda_gemm_kq_i8(int ggml_type, const int8_t *q, const float *act_scales,
                                   size_t n_tokens, const void *weights, size_t n_rows,
                                   size_t n_cols, float *out, void *stream);
@@ -113,7 +113,7 @@ foxcuda_status foxcuda_gemm_kq_i8_packed(int ggml_type, const int8_t *q, const f
  * tokens, where the matrix alone has too few 128-row tiles to fill the GPU.
  * It writes each block's float term to terms (device scratch of
  * n_tokens x n_rows x n_cols/256 floats), then folds them in block order. The
- * result is bit-identical to the unsplit pass. Not yet run on a B200. */
+ * result is bit-identical to the unsplit pass. */
 foxcuda_status foxcuda_gemm_tq2_i8_split(const int8_t *q, const float *act_scale,
                                          size_t n_tokens, const void *packed, size_t n_rows,
                                          size_t n_cols, float *terms, float *out, void *stream);
@@ -457,7 +457,7 @@ foxcuda_status foxcuda_context_logits(foxcuda_context *c, float *out, size_t n);
  * its argmax. Prompt tokens given to foxcuda_tp_embed from the host, and
  * every pick, enter the history, as `fox run` accepts them. The pick equals
  * the unsharded sampler's. Call before the first step; penalty 1 leaves the
- * pick plain greedy. Not yet run on a B200. */
+ * pick plain greedy. */
 foxcuda_status foxcuda_tp_set_penalty(foxcuda_context *c, float penalty, uint32_t last_n);
 
 #define FOXCUDA_IPC_HANDLE_BYTES 64

@@ -585,24 +585,12 @@ static cudaError_t launch_tc_td(const TcParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-// FOXCUDA_TC_DEPTH=2 or 4: K blocks in flight per thread of the ternary
-// tensor-core pass (default 1, the next block only).
-static int tc_depth() {
-  static const int d = [] {
-    const char* v = getenv("FOXCUDA_TC_DEPTH");
-    const int x = v ? atoi(v) : 1;
-    return x == 2 || x == 4 ? x : 1;
-  }();
-  return d;
-}
-
+// Two K blocks in flight per thread of the ternary tensor-core pass. Measured
+// on one 4B layer against one and four: 172 / 188 / 172 us at 8 tokens,
+// 226 / 313 / 236 at 64 (the prompt chunk), 494 / 476 / 518 at 512.
 template <int NT>
 static cudaError_t launch_tc_t(const TcParams& p, cudaStream_t s) {
-  switch (tc_depth()) {
-    case 2: return launch_tc_td<NT, 2>(p, s);
-    case 4: return launch_tc_td<NT, 4>(p, s);
-    default: return launch_tc_td<NT, 1>(p, s);
-  }
+  return launch_tc_td<NT, 2>(p, s);
 }
 
 // The token tile is the smallest MMA N that holds all tokens, up to 64.
@@ -714,14 +702,10 @@ static cudaError_t launch_kq_td(const TcKParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-// the K-block look-ahead of FOXCUDA_TC_DEPTH, as for the ternary pass
+// one K block of look-ahead (the depth that was measured for this pass)
 template <int T, int NT>
 static cudaError_t launch_kq_t(const TcKParams& p, cudaStream_t s) {
-  switch (tc_depth()) {
-    case 2: return launch_kq_td<T, NT, 2>(p, s);
-    case 4: return launch_kq_td<T, NT, 4>(p, s);
-    default: return launch_kq_td<T, NT, 1>(p, s);
-  }
+  return launch_kq_td<T, NT, 1>(p, s);
 }
 
 // Token tiles: Q4_K up to 16 tokens (8 accumulators per block), Q6_K 8 (16).
@@ -1225,14 +1209,10 @@ static foxcuda_status keep_col_blocks(RawTensor& r, uint64_t b0, uint64_t nb) {
 
 // TQ1_0 layer matrices are held as TQ2_0 (tq1_to_tq2_kernel): the same trits
 // and scales, 66 instead of 54 bytes per block, and a quarter of the decode
-// work per weight. FOXCUDA_KEEP_TQ1=1 keeps the GGUF bytes as they are.
-static bool keep_tq1() {
-  const char* v = getenv("FOXCUDA_KEEP_TQ1");
-  return v && v[0] == '1';
-}
-
+// work per weight. Measured on the 4B step: 661 tok/s held as TQ2_0, 510
+// decoding the GGUF TQ1_0 bytes.
 static foxcuda_status transcode_tq1(RawTensor& r) {
-  if (r.type != T_TQ1_0 || r.ne1 <= 1 || keep_tq1()) return FOXCUDA_OK;
+  if (r.type != T_TQ1_0 || r.ne1 <= 1) return FOXCUDA_OK;
   const long nblk = (long)(r.bytes / 54);
   void* d = nullptr;
   CK(cudaMalloc(&d, (size_t)nblk * 66), "transcode alloc");
@@ -1901,7 +1881,6 @@ struct foxcuda_sampler {
   int k = 0;
   SamplerDev* dev = nullptr;
   cudaGraphExec_t g_decode = nullptr;
-  cudaGraphExec_t g_decode_io = nullptr;  // g_decode with the token copies inside
   uint32_t n_out = 0;  // host mirror of dev->n_out
 };
 
@@ -2220,18 +2199,10 @@ static cudaError_t launch_down(foxcuda_context* c, uint32_t l) {
   return launch_mat(c, W, PRO_VEC, EPI_ADD, p);
 }
 
-// FOXCUDA_HEAD_DEPTH=2: the head with two blocks of look-ahead per warp
-// (twice the bytes in flight at the same occupancy). Off by default.
-static bool head_depth2() {
-  static const bool on = [] {
-    const char* v = getenv("FOXCUDA_HEAD_DEPTH");
-    return v && v[0] == '2';
-  }();
-  return on;
-}
-
+// One block of look-ahead per warp: two (twice the bytes in flight at the
+// same occupancy) measured the same, 661 against 661 tok/s for the 4B step.
 static cudaError_t launch_q8_rows(const GemvParams& p, cudaStream_t s) {
-  auto kern = head_depth2() ? q8_rows_kernel<PRO_NORM, 2> : q8_rows_kernel<PRO_NORM, 1>;
+  auto kern = q8_rows_kernel<PRO_NORM, 1>;
   const size_t smem = (size_t)p.K * 4 + 32 * 8;
   static size_t marks[kMaxDevices] = {};  // one kernel per process (the variable is read once)
   cudaError_t e = opt_in_smem(kern, smem, marks);
@@ -2341,36 +2312,6 @@ static cudaError_t capture(foxcuda_context* c, cudaGraphExec_t* out, bool head, 
   return e;
 }
 
-// The decode step of foxcuda_decode with its copies inside the graph: the
-// token in from the context's pinned word, then the pick and the device
-// error word out in one 8-byte copy. A step is then one launch and one
-// synchronisation.
-static cudaError_t capture_io(foxcuda_context* c, foxcuda_sampler* sm, cudaGraphExec_t* out) {
-  cudaGraph_t g = nullptr;
-  cudaError_t e = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal);
-  if (e) return e;
-  e = cudaMemcpyAsync(c->token_dev, c->h_pinned, 4, cudaMemcpyHostToDevice, c->stream);
-  if (!e) e = enqueue_body(c, false);
-  if (!e) e = enqueue_head(c);
-  if (!e) e = enqueue_pick(sm, true);
-  if (!e) e = cudaMemcpyAsync(c->h_pinned + 1, c->token_dev, 8, cudaMemcpyDeviceToHost, c->stream);
-  cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
-  if (e) { if (g) cudaGraphDestroy(g); return e; }
-  if (e2) return e2;
-  e = cudaGraphInstantiate(out, g, 0);
-  cudaGraphDestroy(g);
-  return e;
-}
-
-// FOXCUDA_DECODE_IO_GRAPH=1: foxcuda_decode runs capture_io's graph (the
-// token copies inside it). Off by default.
-static bool decode_io_graph() {
-  static const bool on = [] {
-    const char* v = getenv("FOXCUDA_DECODE_IO_GRAPH");
-    return v && v[0] == '1';
-  }();
-  return on;
-}
 
 extern "C" foxcuda_status foxcuda_context_set_trace(foxcuda_context* c, int on) {
   if (!c) return fail(FOXCUDA_ERR_ARG, "trace: null context");
@@ -3178,7 +3119,6 @@ extern "C" void foxcuda_sampler_destroy(foxcuda_sampler* s) {
   cudaSetDevice(s->c->m->device);
   cudaStreamSynchronize(s->c->stream);
   if (s->g_decode) cudaGraphExecDestroy(s->g_decode);
-  if (s->g_decode_io) cudaGraphExecDestroy(s->g_decode_io);
   cudaFree(s->dev);
   delete s;
 }
@@ -3211,22 +3151,6 @@ static foxcuda_status decode_steps(foxcuda_context* c, foxcuda_sampler* s, uint3
     return fail(FOXCUDA_ERR_ARG, "forward: %zu tokens past position %u would overrun the %u token context",
                 n, c->pos, c->n_ctx);
   cudaSetDevice(c->m->device);
-  if (n == 1 && decode_io_graph()) {
-    if (!s->g_decode_io) CK(capture_io(c, s, &s->g_decode_io), "capture");
-    c->h_pinned[0] = token;  // the previous step has synchronised: no copy still reads it
-    CK(cudaEventRecord(c->ev0, c->stream), "event");
-    CK(cudaGraphLaunch(s->g_decode_io, c->stream), "graph launch");
-    CK(cudaEventRecord(c->ev1, c->stream), "event");
-    s->n_out += 1;
-    CK(cudaStreamSynchronize(c->stream), "decode");
-    out[0] = c->h_pinned[1];
-    c->h_pinned[3] = c->h_pinned[2];
-    float ms = 0.0f;
-    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
-    c->last_seconds = ms / 1e3;
-    c->pos += 1;
-    return check_err(c);
-  }
   if (!s->g_decode) CK(capture(c, &s->g_decode, true, s), "capture");
   c->h_pinned[0] = token;
   CK(cudaMemcpyAsync(c->token_dev, c->h_pinned, 4, cudaMemcpyHostToDevice, c->stream), "token in");
