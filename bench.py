@@ -76,6 +76,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=0, metavar="N",
                     help="decode N sequences together at a --ctx long synthetic context "
                          "(config 5: --config 8b-tq2 --batch 16 --ctx 32768)")
+    ap.add_argument("--contiguous", action="store_true",
+                    help="with --batch: one contiguous cache per sequence instead of pages "
+                         "from one shared pool")
     ap.add_argument("--image", action="store_true",
                     help="time the model load: tensors uploaded and packed on the device, "
                          "against a device image opened from a file")
@@ -762,6 +765,8 @@ def run_batch(args):
     --ctx long context. The K/V of every sequence is seeded N(0, 1) fp16
     (foxcuda_context_fill_kv), a stand-in for the long prompts; sampling is
     top-k 40 at temperature 0.8, top-p and repeat penalty off, seed 1 + i.
+    The caches are pages of one shared pool (foxcuda_kv_pool_create), as a
+    server holds them; --contiguous gives each sequence its own cache.
     CUDA-event time of the timed steps on the batch's stream."""
     import torch
     import rustfox_b200 as rf
@@ -772,7 +777,9 @@ def run_batch(args):
     model = rf.Model.from_synthetic_device(cfg)  # no CPU baseline here: no host copy needed
     n, warm = args.batch, max(3, args.warmup)
     n_ctx = args.ctx + warm + args.steps + 8
-    ctxs = [rf.Context(model, n_ctx, kv="f16") for _ in range(n)]
+    pages = (n_ctx + rf.api.KV_PAGE - 1) // rf.api.KV_PAGE
+    pool = None if args.contiguous else model.kv_pool(n * pages)
+    ctxs = [rf.Context(model, n_ctx, kv="f16", pool=pool) for _ in range(n)]
     for i, c in enumerate(ctxs):
         c.fill_kv(args.ctx, seed=1 + i)
     smp = [rf.Sampler(c, temperature=0.8, top_k=40, top_p=1.0, repeat_penalty=1.0, seed=1 + i)
@@ -801,7 +808,9 @@ def run_batch(args):
                 "K/V in place of prompts)",
         "config": {"workload": f"{cfg.name} {cfg.n_layer}L/{cfg.n_embd}, {n} sequences at position "
                                f"{args.ctx}, top-k 40 T 0.8", "batch": n, "ctx": args.ctx,
-                   "kv_cache": "f16", "l2": f"{step_bytes / 1e9:.1f} GB per step > 126 MB L2"},
+                   "kv_cache": "f16, " + ("one contiguous cache per sequence" if pool is None else
+                                          f"paged: {rf.api.KV_PAGE}-position pages of one shared pool"),
+                   "l2": f"{step_bytes / 1e9:.1f} GB per step > 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": None, "peak_source": src,
                      "bytes_per_step": step_bytes},
@@ -815,6 +824,8 @@ def run_batch(args):
         s.close()
     for c in ctxs:
         c.close()
+    if pool is not None:
+        pool.close()
     model.close()
 
 

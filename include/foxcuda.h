@@ -264,6 +264,24 @@ typedef struct {
  * last_eval_seconds (include/fox/fox.h:433-450, src/forward.c:56-165) */
 foxcuda_status foxcuda_context_create(foxcuda_model *m, const foxcuda_context_config *cfg,
                                       foxcuda_context **out);
+/* Paged K/V cache (upstream keeps one contiguous fp32 cache per context,
+ * src/forward.c:91-92). A pool holds n_pages pages per layer, each
+ * FOXCUDA_KV_PAGE positions of every KV head, and is shared by contexts of
+ * one model and cache type. A paged context takes ceil(n_ctx / page) pages
+ * at creation (FOXCUDA_ERR_NOMEM when the pool is short) and gives them back
+ * when destroyed; a block table in device memory maps its positions to
+ * them, and every kernel that reads or writes K/V goes through it. Values
+ * are the contiguous cache's, bit for bit. A batch takes contexts that are
+ * all contiguous or all from one pool. The pool outlives its contexts:
+ * foxcuda_kv_pool_destroy answers FOXCUDA_ERR_ARG while any holds pages. */
+#define FOXCUDA_KV_PAGE 64
+typedef struct foxcuda_kv_pool foxcuda_kv_pool;
+foxcuda_status foxcuda_kv_pool_create(foxcuda_model *m, uint32_t n_pages, int kv_type,
+                                      foxcuda_kv_pool **out);
+uint32_t       foxcuda_kv_pool_free_pages(foxcuda_kv_pool *p);
+foxcuda_status foxcuda_kv_pool_destroy(foxcuda_kv_pool *p);
+foxcuda_status foxcuda_context_create_paged(foxcuda_model *m, const foxcuda_context_config *cfg,
+                                            foxcuda_kv_pool *pool, foxcuda_context **out);
 void           foxcuda_context_destroy(foxcuda_context *c);
 void           foxcuda_context_reset(foxcuda_context *c);
 uint32_t       foxcuda_context_position(const foxcuda_context *c);

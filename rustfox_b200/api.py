@@ -94,6 +94,10 @@ _PROTOS = {
     "foxcuda_model_save_image": (_st, [_vp, C.c_char_p]),
     "foxcuda_model_open_image": (_st, [C.c_char_p, C.c_int, C.POINTER(_vp)]),
     "foxcuda_context_create": (_st, [_vp, C.POINTER(ContextConfig), C.POINTER(_vp)]),
+    "foxcuda_context_create_paged": (_st, [_vp, C.POINTER(ContextConfig), _vp, C.POINTER(_vp)]),
+    "foxcuda_kv_pool_create": (_st, [_vp, C.c_uint32, C.c_int, C.POINTER(_vp)]),
+    "foxcuda_kv_pool_free_pages": (C.c_uint32, [_vp]),
+    "foxcuda_kv_pool_destroy": (_st, [_vp]),
     "foxcuda_context_destroy": (None, [_vp]),
     "foxcuda_context_reset": (None, [_vp]),
     "foxcuda_context_position": (C.c_uint32, [_vp]),
@@ -463,8 +467,36 @@ class Model:
         mode): foxcuda_attn_tile_target for its device and all its KV heads."""
         return int(lib().foxcuda_attn_tile_target(self.device, int(self.info["n_head_kv"])))
 
-    def context(self, n_ctx: int, kv: str = "f16", attn_exact: bool = False) -> "Context":
-        return Context(self, n_ctx, kv, attn_exact)
+    def context(self, n_ctx: int, kv: str = "f16", attn_exact: bool = False, pool: "KvPool" = None) -> "Context":
+        """A decode context; with `pool` its K/V cache is paged from that pool."""
+        return Context(self, n_ctx, kv, attn_exact, pool)
+
+    def kv_pool(self, n_pages: int, kv: str = "f16") -> "KvPool":
+        return KvPool(self, n_pages, kv)
+
+
+KV_PAGE = 64  # positions per page (FOXCUDA_KV_PAGE)
+
+
+class KvPool:
+    """A pool of K/V pages shared by paged contexts of one model
+    (foxcuda_kv_pool_*): n_pages pages per layer of KV_PAGE positions."""
+
+    def __init__(self, model: "Model", n_pages: int, kv: str = "f16"):
+        self.model = model
+        h = C.c_void_p()
+        _check(lib().foxcuda_kv_pool_create(model.h, int(n_pages), KV_F16 if kv == "f16" else KV_F32,
+                                            C.byref(h)))
+        self.h = h
+
+    @property
+    def free_pages(self) -> int:
+        return int(lib().foxcuda_kv_pool_free_pages(self.h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            _check(lib().foxcuda_kv_pool_destroy(self.h))
+            self.h = None
 
 
 def _role_of(name: str):
@@ -480,15 +512,21 @@ def _role_of(name: str):
 class Context:
     """upstream fox_context (src/forward.c:9-165): KV cache, scratch, position."""
 
-    def __init__(self, model: Model, n_ctx: int, kv: str = "f16", attn_exact: bool = False):
+    def __init__(self, model: Model, n_ctx: int, kv: str = "f16", attn_exact: bool = False,
+                 pool: "KvPool" = None):
         """kv: "f16" (default) or "f32" cache; attn_exact: attention in
-        upstream's serial operation order (the bit-exact parity mode)."""
+        upstream's serial operation order (the bit-exact parity mode); pool:
+        page the cache from a KvPool."""
         self.model = model
+        self.pool = pool
         self.n_vocab = int(model.info["n_vocab"])
         self.n_embd = int(model.info["n_embd"])
         cfg = ContextConfig(n_ctx, KV_F16 if kv == "f16" else KV_F32, 1 if attn_exact else 0)
         h = C.c_void_p()
-        _check(lib().foxcuda_context_create(model.h, C.byref(cfg), C.byref(h)))
+        if pool is None:
+            _check(lib().foxcuda_context_create(model.h, C.byref(cfg), C.byref(h)))
+        else:
+            _check(lib().foxcuda_context_create_paged(model.h, C.byref(cfg), pool.h, C.byref(h)))
         self.h = h
 
     def close(self):
@@ -661,10 +699,10 @@ class Batch:
 
 def greedy_generate(model: Model, prompt, n_gen: int, n_ctx: int, kv: str = "f16",
                     repeat_penalty: float = 1.1, repeat_last_n: int = 64,
-                    attn_exact: bool = False):
+                    attn_exact: bool = False, pool: "KvPool" = None):
     """`fox run --temp 0` on token ids (upstream src/cli.c:333-361): eval the
     prompt, accept it, pick, then decode steps on the device."""
-    ctx = Context(model, n_ctx, kv, attn_exact)
+    ctx = Context(model, n_ctx, kv, attn_exact, pool)
     smp = Sampler(ctx, temperature=0.0, repeat_penalty=repeat_penalty,
                   repeat_last_n=repeat_last_n)
     ctx.eval(prompt, want_logits=False)

@@ -70,15 +70,23 @@ struct TileStage {
   int ch;
 };
 
-// Rows [r0, r1) of a head's cache (row bytes rb) into buf, row r at
-// (r - r0) * rb, except row `skip`; asynchronous (cp.async, L2 only), one
-// commit group.
-FOX_DEV void stage_rows(uint8_t* buf, const uint8_t* head, int rb, int r0, int r1, int skip) {
-  const int per_row = rb >> 4, pieces = (r1 - r0) * per_row;
+// Where KV head g's positions of one sequence and layer live: the cache
+// base, and its block table when paged (common.cuh kv_row).
+struct KvHead {
+  const uint8_t* base;
+  const int* table;
+  int n_ctx, n_kv, g, rb;  // rb: row bytes
+  FOX_DEV const uint8_t* row(int pos) const { return base + kv_row(table, n_ctx, n_kv, g, pos) * rb; }
+};
+
+// Positions [r0, r1) of a head into buf, position r at (r - r0) * rb,
+// except position `skip`; asynchronous (cp.async, L2 only), one commit group.
+FOX_DEV void stage_rows(uint8_t* buf, const KvHead& kv, int r0, int r1, int skip) {
+  const int per_row = kv.rb >> 4, pieces = (r1 - r0) * per_row;
   for (int i = threadIdx.x; i < pieces; i += blockDim.x) {
     const int row = i / per_row;
     if (r0 + row == skip) continue;
-    cp_async16(buf + (uint32_t)i * 16, head + (uint32_t)r0 * rb + (uint32_t)i * 16);
+    cp_async16(buf + (uint32_t)i * 16, kv.row(r0 + row) + (uint32_t)(i - row * per_row) * 16);
   }
   cp_async_commit();
 }
@@ -174,11 +182,15 @@ FOX_DEV TileSmem tile_smem(float* base, int n_ctx, int nt, int gqa, int hd, int 
 
 struct TileArgs {
   const float* q;     // the group's query heads start at q + g * gqa * hd
-  const void* kc;     // [n_kv][n_ctx][hd] of this layer (and sequence)
+  const void* kc;     // this layer's (and sequence's) caches (common.cuh kv_row)
   const void* vc;
+  const int* table;   // block table of a paged cache (nullptr: contiguous)
   float* out;         // [n_head * hd]
-  int n_ctx, hd, nt, P;
+  int n_ctx, n_kv, hd, nt, P;
   float scale;
+  FOX_DEV KvHead head(const void* c, int g, int rb) const {
+    return KvHead{reinterpret_cast<const uint8_t*>(c), table, n_ctx, n_kv, g, rb};
+  }
 };
 
 // The first chunk of tile t of group g, K then V (two commit groups),
@@ -188,10 +200,9 @@ template <bool F16>
 FOX_DEV void attn_tile_stage0(const TileArgs& a, const TileStage& st, int g, int t) {
   const int T = attn_tile_len(a.P, a.nt), j0 = t * T, n = min(T, a.P - j0);
   const int rb = a.hd * (F16 ? 2 : 4);
-  const uint32_t head = (uint32_t)g * (uint32_t)a.n_ctx * (uint32_t)rb;
   const int c1 = j0 + min(n, st.ch);
-  stage_rows(st.k, reinterpret_cast<const uint8_t*>(a.kc) + head, rb, j0, c1, a.P - 1);
-  stage_rows(st.v, reinterpret_cast<const uint8_t*>(a.vc) + head, rb, j0, c1, a.P - 1);
+  stage_rows(st.k, a.head(a.kc, g, rb), j0, c1, a.P - 1);
+  stage_rows(st.v, a.head(a.vc, g, rb), j0, c1, a.P - 1);
 }
 
 // Tile t of KV group g (after attn_tile_stage0): every query head's max,
@@ -203,8 +214,7 @@ FOX_DEV void attn_tile(const TileArgs& a, const TileSmem& m, int g, int t) {
   const int j0 = t * T, n = min(T, a.P - j0);
   const int hd = a.hd, ch = m.st.ch;
   const int rb = hd * (F16 ? 2 : 4);
-  const uint8_t* kh = reinterpret_cast<const uint8_t*>(a.kc) + (uint32_t)g * (uint32_t)a.n_ctx * (uint32_t)rb;
-  const uint8_t* vh = reinterpret_cast<const uint8_t*>(a.vc) + (uint32_t)g * (uint32_t)a.n_ctx * (uint32_t)rb;
+  const KvHead kh = a.head(a.kc, g, rb), vh = a.head(a.vc, g, rb);
   const int newest = a.P - 1;
   float* sc = m.sc;
   float* s_m = m.ml;        // [G]
@@ -213,11 +223,11 @@ FOX_DEV void attn_tile(const TileArgs& a, const TileSmem& m, int g, int t) {
   for (int i = tid; i < G * hd; i += nth) m.q[i] = __ldcg(a.q + (uint32_t)g * G * hd + i);
   // the newest row into the first chunk (staging left it out)
   const bool has_newest = newest >= j0 && newest < j0 + min(n, ch);
-  auto newest_row = [&](uint8_t* buf, const uint8_t* src) {
+  auto newest_row = [&](uint8_t* buf, const KvHead& src) {
     if (has_newest)
       for (int i = tid; i < (rb >> 2); i += nth)
         reinterpret_cast<uint32_t*>(buf + (uint32_t)(newest - j0) * rb)[i] =
-            __ldcg(reinterpret_cast<const unsigned int*>(src + (uint32_t)newest * rb) + i);
+            __ldcg(reinterpret_cast<const unsigned int*>(src.row(newest)) + i);
   };
   for (int c0 = j0; c0 < j0 + n; c0 += ch) {
     const int c1 = min(j0 + n, c0 + ch), cn = c1 - c0;
@@ -225,7 +235,7 @@ FOX_DEV void attn_tile(const TileArgs& a, const TileSmem& m, int g, int t) {
       cp_async_wait_one();  // chunk 0's K (its V may still be in flight)
       newest_row(m.st.k, kh);
     } else {
-      stage_rows(m.st.k, kh, rb, c0, c1, -1);
+      stage_rows(m.st.k, kh, c0, c1, -1);
       cp_async_wait_all();
     }
     __syncthreads();
@@ -275,7 +285,7 @@ FOX_DEV void attn_tile(const TileArgs& a, const TileSmem& m, int g, int t) {
       newest_row(m.st.v, vh);
     } else {
       __syncthreads();
-      stage_rows(m.st.v, vh, rb, c0, c1, -1);
+      stage_rows(m.st.v, vh, c0, c1, -1);
       cp_async_wait_all();
     }
     __syncthreads();
@@ -348,7 +358,8 @@ FOX_DEV void attn_merge(const TileArgs& a, const TileSmem& m, int g, int nt) {
 // Tile attention (AttnParams, ops.cuh): grid (nt, n_kv, n_seq) in clusters
 // of nt CTAs (the tiles of one KV head of one sequence). Sequence z reads its
 // position at *pos_list[z] (or *pos), its q and output at z * seq_stride,
-// and its caches at k_list[z] / v_list[z] + layer_off (or kcache / vcache).
+// and its caches at k_list[z] / v_list[z] + layer_off (or kcache / vcache),
+// paged through table_list[z] (or kv_table) when given.
 // Under programmatic launch (the decode step, right after the q|k|v kernel
 // that writes q and position P - 1) the older rows of the first chunk are
 // staged before griddepcontrol.wait; q and the newest row are read after it.
@@ -363,7 +374,8 @@ __global__ void __launch_bounds__(256, 1) attention_tile_kernel(const AttnParams
   a.out = k.out + (size_t)z * k.seq_stride;
   a.kc = k.k_list ? (const void*)(reinterpret_cast<const uint8_t*>(k.k_list[z]) + k.layer_off) : k.kcache;
   a.vc = k.v_list ? (const void*)(reinterpret_cast<const uint8_t*>(k.v_list[z]) + k.layer_off) : k.vcache;
-  a.n_ctx = k.n_ctx; a.hd = k.hd; a.nt = k.nt;
+  a.table = k.table_list ? k.table_list[z] : k.kv_table;
+  a.n_ctx = k.n_ctx; a.n_kv = k.n_kv; a.hd = k.hd; a.nt = k.nt;
   a.P = (k.pos_list ? *k.pos_list[z] : *k.pos) + 1;
   a.scale = k.scale;
   const int T = attn_tile_len(a.P, a.nt), nt = (a.P + T - 1) / T;

@@ -82,6 +82,17 @@ FOX_DEV uint32_t pack4(int a, int b, int c, int d) {
 
 FOX_DEV int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
+// K/V cache rows of one layer. Contiguous: [kv_head][n_ctx][hd]. Paged (a
+// block table given): position p of a sequence lives in physical page
+// table[p / KV_PAGE] of the layer's page pool, and a page holds KV_PAGE
+// positions of every KV head, [kv_head][KV_PAGE][hd]. The row of (kvh, p),
+// in units of hd elements.
+constexpr int KV_PAGE = 64;
+FOX_DEV size_t kv_row(const int* table, int n_ctx, int n_kv, int kvh, int pos) {
+  if (!table) return (size_t)kvh * n_ctx + pos;
+  return ((size_t)__ldg(table + (pos >> 6)) * n_kv + kvh) * KV_PAGE + (pos & (KV_PAGE - 1));
+}
+
 // e^x in binary32 as upstream gets it from glibc's expf (glibc >= 2.27: the
 // published ARM optimized-routines algorithm; x86-64 hosts with FMA run its
 // FMA build). With N = 32:

@@ -1501,6 +1501,7 @@ struct ImgEntry {
   uint64_t offset, bytes;
 };
 static_assert(sizeof(ImgHeader) == 184 && sizeof(ImgEntry) == 80, "image records have no padding");
+static_assert(FOXCUDA_KV_PAGE == KV_PAGE, "the header's page size is the kernels'");
 
 constexpr size_t kImgChunk = 64ull << 20;  // bytes per pinned staging buffer
 
@@ -1817,6 +1818,23 @@ extern "C" foxcuda_status foxcuda_model_open_image(const char* path, int device,
 // ---------------------------------------------------------------------------
 // context
 
+// A pool of K/V pages shared by the contexts of one model: n_pages pages per
+// layer, each KV_PAGE positions of every KV head ([kv_head][KV_PAGE][hd]),
+// laid out [layer][page]. A paged context takes ceil(n_ctx / KV_PAGE) pages
+// at creation and gives them back when destroyed; its block table maps its
+// logical pages to them (common.cuh kv_row).
+struct foxcuda_kv_pool {
+  foxcuda_model* m = nullptr;
+  int kv_f16 = 1;
+  uint32_t n_pages = 0;
+  size_t layer_elems = 0;
+  void* k = nullptr;
+  void* v = nullptr;
+  std::vector<int> free_pages;
+  uint32_t users = 0;   // contexts holding pages
+  std::mutex mu;
+};
+
 struct foxcuda_context {
   foxcuda_model* m = nullptr;
   uint32_t n_ctx = 0;
@@ -1826,7 +1844,10 @@ struct foxcuda_context {
   float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   void *kc = nullptr, *vc = nullptr;
-  size_t kv_layer_elems = 0;
+  size_t kv_layer_elems = 0;     // elements between two layers' caches
+  int* kv_table = nullptr;       // paged cache: the block table (device), else nullptr
+  foxcuda_kv_pool* pool = nullptr;
+  std::vector<int> pages;        // this context's pages of the pool, in table order
   int* pos_dev = nullptr;
   uint32_t* token_dev = nullptr;  // [0] the current token, [1] device error code
   int* err_dev = nullptr;
@@ -1903,11 +1924,16 @@ extern "C" void foxcuda_context_destroy(foxcuda_context* c) {
   if (c->ev0) cudaEventDestroy(c->ev0);
   if (c->ev1) cudaEventDestroy(c->ev1);
   if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->pool) {
+    std::lock_guard<std::mutex> lk(c->pool->mu);
+    for (auto it = c->pages.rbegin(); it != c->pages.rend(); ++it) c->pool->free_pages.push_back(*it);
+    c->pool->users -= 1;
+  }
   delete c;
 }
 
-extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda_context_config* cfg,
-                                                 foxcuda_context** out) {
+static foxcuda_status context_create(foxcuda_model* m, const foxcuda_context_config* cfg, foxcuda_kv_pool* pool,
+                                     foxcuda_context** out) {
   if (!m || !out) return fail(FOXCUDA_ERR_ARG, "context: null argument");
   *out = nullptr;
   if (!m->finalized) {
@@ -1929,12 +1955,40 @@ extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda
   const int nq = mi.n_head * mi.head_dim;
   const int half = mi.head_dim / 2;
   const int gqa = mi.n_head / mi.n_head_kv;
-  c->kv_layer_elems = (size_t)mi.n_head_kv * c->n_ctx * mi.head_dim;
-  const size_t kv_bytes = c->kv_layer_elems * mi.n_layer * (c->kv_f16 ? 2 : 4);
   cudaError_t e = cudaSuccess;
   auto A = [&](size_t bytes, void** p) { if (e == cudaSuccess) e = ctx_alloc(c, bytes, p); };
-  A(kv_bytes, &c->kc);
-  A(kv_bytes, &c->vc);
+  if (pool) {
+    if (pool->m != m || pool->kv_f16 != c->kv_f16) {
+      delete c;
+      return fail(FOXCUDA_ERR_ARG, "context: the page pool is for another model or cache type");
+    }
+    const uint32_t need = (c->n_ctx + KV_PAGE - 1) / KV_PAGE;
+    {
+      std::lock_guard<std::mutex> lk(pool->mu);
+      if (pool->free_pages.size() < need) {
+        const size_t have = pool->free_pages.size();
+        delete c;
+        return fail(FOXCUDA_ERR_NOMEM, "context: %u pages needed, %zu free in the pool", need, have);
+      }
+      for (uint32_t i = 0; i < need; ++i) {
+        c->pages.push_back(pool->free_pages.back());
+        pool->free_pages.pop_back();
+      }
+      pool->users += 1;
+    }
+    c->pool = pool;
+    c->kc = pool->k;
+    c->vc = pool->v;
+    c->kv_layer_elems = pool->layer_elems;
+    A(c->pages.size() * sizeof(int), (void**)&c->kv_table);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(c->kv_table, c->pages.data(), c->pages.size() * sizeof(int), cudaMemcpyHostToDevice);
+  } else {
+    c->kv_layer_elems = (size_t)mi.n_head_kv * c->n_ctx * mi.head_dim;
+    const size_t kv_bytes = c->kv_layer_elems * mi.n_layer * (c->kv_f16 ? 2 : 4);
+    A(kv_bytes, &c->kc);
+    A(kv_bytes, &c->vc);
+  }
   A((size_t)mi.n_embd * 4, (void**)&c->x);
   A((size_t)nq * 4, (void**)&c->q);
   A((size_t)nq * 4, (void**)&c->att);
@@ -1973,6 +2027,76 @@ extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda
     return cuda_fail(e, "context init");
   }
   *out = c;
+  return FOXCUDA_OK;
+}
+
+extern "C" foxcuda_status foxcuda_context_create(foxcuda_model* m, const foxcuda_context_config* cfg,
+                                                 foxcuda_context** out) {
+  return context_create(m, cfg, nullptr, out);
+}
+
+extern "C" foxcuda_status foxcuda_context_create_paged(foxcuda_model* m, const foxcuda_context_config* cfg,
+                                                       foxcuda_kv_pool* pool, foxcuda_context** out) {
+  if (!pool) return fail(FOXCUDA_ERR_ARG, "context: null page pool");
+  return context_create(m, cfg, pool, out);
+}
+
+// The pool's pages are handed out in a fixed shuffled order, so a context's
+// pages are scattered over the pool from its first one (the block table is
+// what makes them a sequence).
+extern "C" foxcuda_status foxcuda_kv_pool_create(foxcuda_model* m, uint32_t n_pages, int kv_type,
+                                                 foxcuda_kv_pool** out) {
+  if (!m || !out || n_pages == 0) return fail(FOXCUDA_ERR_ARG, "kv_pool: bad argument");
+  *out = nullptr;
+  if (!m->finalized) {
+    foxcuda_status st = foxcuda_model_finalize(m);
+    if (st) return st;
+  }
+  cudaSetDevice(m->device);
+  const foxcuda_model_info& mi = m->loc;
+  auto pool = std::make_unique<foxcuda_kv_pool>();
+  pool->m = m;
+  pool->kv_f16 = kv_type == FOXCUDA_KV_F16;
+  pool->n_pages = n_pages;
+  pool->layer_elems = (size_t)n_pages * mi.n_head_kv * KV_PAGE * mi.head_dim;
+  const size_t bytes = pool->layer_elems * mi.n_layer * (pool->kv_f16 ? 2 : 4);
+  cudaError_t e = cudaMalloc(&pool->k, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&pool->v, bytes);
+  if (e == cudaSuccess) e = cudaMemset(pool->k, 0, bytes);
+  if (e == cudaSuccess) e = cudaMemset(pool->v, 0, bytes);
+  if (e != cudaSuccess) {
+    if (pool->k) cudaFree(pool->k);
+    if (pool->v) cudaFree(pool->v);
+    return cuda_fail(e, "kv_pool allocation");
+  }
+  std::vector<int> order(n_pages);
+  for (uint32_t i = 0; i < n_pages; ++i) order[i] = (int)i;
+  uint64_t st = 0x243F6A8885A308D3ull;
+  for (uint32_t i = n_pages - 1; i > 0; --i) {  // Fisher-Yates with a fixed xorshift stream
+    st ^= st << 13; st ^= st >> 7; st ^= st << 17;
+    std::swap(order[i], order[st % (i + 1)]);
+  }
+  pool->free_pages.assign(order.rbegin(), order.rend());  // handed out from the back: order[0] first
+  *out = pool.release();
+  return FOXCUDA_OK;
+}
+
+extern "C" uint32_t foxcuda_kv_pool_free_pages(foxcuda_kv_pool* p) {
+  if (!p) return 0;
+  std::lock_guard<std::mutex> lk(p->mu);
+  return (uint32_t)p->free_pages.size();
+}
+
+extern "C" foxcuda_status foxcuda_kv_pool_destroy(foxcuda_kv_pool* p) {
+  if (!p) return FOXCUDA_OK;
+  {
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (p->users) return fail(FOXCUDA_ERR_ARG, "kv_pool: %u contexts still hold pages", p->users);
+  }
+  cudaSetDevice(p->m->device);
+  cudaFree(p->k);
+  cudaFree(p->v);
+  delete p;
   return FOXCUDA_OK;
 }
 
@@ -2090,6 +2214,7 @@ static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
     p.hd = mi.head_dim; p.n_ctx = c->n_ctx; p.kv_f16 = c->kv_f16;
     p.rope_cos = c->rope_cos; p.rope_sin = c->rope_sin; p.pos = c->pos_dev;
     p.kcache = kv_layer(c, c->kc, l); p.vcache = kv_layer(c, c->vc, l); p.row_base = L.qkv_base[i];
+    p.kv_table = c->kv_table;
     if (fold) set_nfold(c, p);
     cudaError_t e = launch_mat(c, W, fold ? PRO_NFOLD : PRO_NORM, EPI_QKV, p);
     if (e) return e;
@@ -2166,7 +2291,7 @@ static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t 
 static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
   const foxcuda_model_info& mi = c->m->info;
   AttnParams ap{};
-  ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+  ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l); ap.kv_table = c->kv_table;
   ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
   ap.hd = mi.head_dim; ap.n_head = c->m->loc.n_head; ap.n_kv = c->m->loc.n_head_kv; ap.nt = c->m->attn_nt;
   ap.stage_rows = attn_stage_rows(c->kv_f16); ap.pos = c->pos_dev; ap.out = c->att;
@@ -2460,7 +2585,7 @@ static cudaError_t chunk_attention(foxcuda_context* c, uint32_t l, int M, bool o
     ap.layer_off = (size_t)l * c->kv_layer_elems * (c->kv_f16 ? 2 : 4);
     return launch_tiles(ap, M, c->stream);
   }
-  ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+  ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l); ap.kv_table = c->kv_table;
   cudaError_t e = cudaSuccess;
   for (int t = 0; t < M && !e; ++t) {
     ap.q = c->pf_q + (size_t)t * nq;
@@ -2494,7 +2619,7 @@ static cudaError_t prefill_chunk(foxcuda_context* c, const uint32_t* tokens, int
     if ((e = tc_rows(c, L.qkv[0], M, c->pf_qkv))) break;
     qkv_rows_kernel<<<dim3((nqkv + 255) / 256, M), 256, 0, s>>>(
         c->pf_qkv, nqkv, nq, nkv, hd, (int)c->n_ctx, (int)pos0, c->rope_cos, c->rope_sin, c->kv_f16,
-        kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->pf_q);
+        kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->kv_table, c->pf_q);
     if ((e = cudaGetLastError())) break;
     if ((e = chunk_attention(c, l, M, one_launch))) break;
     // o, residual
@@ -2588,7 +2713,7 @@ static cudaError_t prefill_chunk_kq(foxcuda_context* c, const uint32_t* tokens, 
     if (e) break;
     qkv_rows_kernel<<<dim3((nqkv + 255) / 256, M), 256, 0, s>>>(
         c->pf_qkv, nqkv, nq, nkv, hd, (int)c->n_ctx, (int)pos0, c->rope_cos, c->rope_sin, c->kv_f16,
-        kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->pf_q);
+        kv_layer(c, c->kc, l), kv_layer(c, c->vc, l), c->kv_table, c->pf_q);
     if ((e = cudaGetLastError())) break;
     if ((e = chunk_attention(c, l, M, one_launch))) break;
     if ((e = quant_rows_k<false>(c, c->pf_att, nq, nullptr, 256, M))) break;
@@ -2766,6 +2891,7 @@ struct foxcuda_batch {
   uint32_t** tokp = nullptr;
   void** kbase = nullptr;
   void** vbase = nullptr;
+  const int** tables = nullptr;  // block tables of paged contexts (else nullptr)
   uint32_t* toks = nullptr;
   // rows of the pass, one per sequence
   float *x = nullptr, *xs = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr;
@@ -2800,6 +2926,9 @@ extern "C" foxcuda_status foxcuda_batch_create(foxcuda_context* const* ctxs, siz
     if (c->m != c0->m) return fail(FOXCUDA_ERR_ARG, "batch: the contexts use different models");
     if (c->n_ctx != c0->n_ctx || c->kv_f16 != c0->kv_f16 || c->attn_exact != c0->attn_exact)
       return fail(FOXCUDA_ERR_ARG, "batch: the contexts differ in length, cache type or attention mode");
+    if (c->pool != c0->pool)
+      return fail(FOXCUDA_ERR_ARG, "batch: the contexts' caches are not all from the same page pool "
+                  "(or all contiguous)");
     for (size_t j = 0; j < i; ++j)
       if (ctxs[j] == c) return fail(FOXCUDA_ERR_ARG, "batch: context %zu appears twice", i);
   }
@@ -2846,6 +2975,12 @@ extern "C" foxcuda_status foxcuda_batch_create(foxcuda_context* const* ctxs, siz
   if (e == cudaSuccess) e = cudaMemcpy(b->tokp, tokp.data(), n * sizeof(uint32_t*), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(b->kbase, kb.data(), n * sizeof(void*), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(b->vbase, vb.data(), n * sizeof(void*), cudaMemcpyHostToDevice);
+  if (c0->pool) {
+    std::vector<const int*> tb(n);
+    for (size_t i = 0; i < n; ++i) tb[i] = ctxs[i]->kv_table;
+    A(n * sizeof(int*), (void**)&b->tables);
+    if (e == cudaSuccess) e = cudaMemcpy(b->tables, tb.data(), n * sizeof(int*), cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreate(&b->ev0);
   if (e == cudaSuccess) e = cudaEventCreate(&b->ev1);
@@ -2884,11 +3019,12 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
     if ((e = tc_rows_to(b->xq, b->xs, L.qkv[0], M, b->qkv, c0->err_dev, s))) break;
     qkv_seqs_kernel<<<dim3((nqkv + 255) / 256, M), 256, 0, s>>>(
         b->qkv, nqkv, nq, nkv, hd, (int)c0->n_ctx, b->pos, b->kbase, b->vbase, (size_t)l * layer_bytes,
-        c0->rope_cos, c0->rope_sin, c0->kv_f16, b->q);
+        b->tables, c0->rope_cos, c0->rope_sin, c0->kv_f16, b->q);
     if ((e = cudaGetLastError())) break;
     AttnParams all{};
     all.q = b->q; all.out = b->att; all.seq_stride = nq;
     all.pos_list = b->pos; all.k_list = b->kbase; all.v_list = b->vbase; all.layer_off = (size_t)l * layer_bytes;
+    all.table_list = b->tables;
     all.kv_f16 = c0->kv_f16; all.n_ctx = c0->n_ctx;
     all.hd = hd; all.n_head = mi.n_head; all.n_kv = mi.n_head_kv; all.nt = m->attn_nt;
     all.scale = 1.0f / sqrtf((float)hd);
@@ -2900,6 +3036,7 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
         foxcuda_context* c = b->ctx[i];
         AttnParams ap{};
         ap.q = b->q + (size_t)i * nq; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l);
+        ap.kv_table = c->kv_table;
         ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
         ap.hd = hd; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.nt = m->attn_nt;
         ap.pos = c->pos_dev; ap.out = b->att + (size_t)i * nq; ap.stage_rows = attn_stage_rows(c->kv_f16);
@@ -3060,9 +3197,11 @@ extern "C" foxcuda_status foxcuda_context_fill_kv(foxcuda_context* c, uint32_t n
   const unsigned grid = (unsigned)std::max<size_t>(1, std::min<size_t>((total + 255) / 256, 16384));
   if (total) {
     fill_kv_kernel<<<grid, 256, 0, c->stream>>>(c->kc, c->kv_f16, runs, (int)c->n_ctx, (int)mi.head_dim,
-                                                (int)n_pos, seed);
+                                                (int)n_pos, (int)mi.n_head_kv, c->kv_layer_elems, c->kv_table,
+                                                seed);
     fill_kv_kernel<<<grid, 256, 0, c->stream>>>(c->vc, c->kv_f16, runs, (int)c->n_ctx, (int)mi.head_dim,
-                                                (int)n_pos, ~seed);
+                                                (int)n_pos, (int)mi.n_head_kv, c->kv_layer_elems, c->kv_table,
+                                                ~seed);
     CK(cudaGetLastError(), "fill_kv launch");
   }
   const int p = (int)n_pos;

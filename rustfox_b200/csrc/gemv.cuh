@@ -75,8 +75,9 @@ struct GemvParams {
   const float* rope_cos;  // [n_ctx][hd/2]
   const float* rope_sin;
   const int* pos;
-  void* kcache;           // this layer: [n_kv_heads][n_ctx][hd]
+  void* kcache;           // this layer's caches (common.cuh kv_row)
   void* vcache;
+  const int* kv_table;    // the block table of a paged cache (nullptr: contiguous)
   int row_base;           // first row of this matrix within q|k|v
   int* err;               // set to a nonzero code when a bounded device wait gives up
   // ring mode: units stream through ring_slots shared-memory slots of
@@ -655,13 +656,13 @@ gemv_kernel(const GemvParams p) {
           if (r < p.nq) {
             p.out[r] = o;
           } else {
-            const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+            const size_t idx = kv_row(p.kv_table, p.n_ctx, p.nkv / p.hd, rr / p.hd, P) * p.hd + rr % p.hd;
             if (p.kv_f16) reinterpret_cast<__half*>(p.kcache)[idx] = __float2half_rn(o);
             else reinterpret_cast<float*>(p.kcache)[idx] = o;
           }
         } else {
           const int rr = r - p.nq - p.nkv;
-          const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+          const size_t idx = kv_row(p.kv_table, p.n_ctx, p.nkv / p.hd, rr / p.hd, P) * p.hd + rr % p.hd;
           if (p.kv_f16) reinterpret_cast<__half*>(p.vcache)[idx] = __float2half_rn(mine);
           else reinterpret_cast<float*>(p.vcache)[idx] = mine;
         }

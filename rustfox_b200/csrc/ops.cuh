@@ -89,8 +89,9 @@ __global__ void advance_kernel(int* pos, int by) {
 
 struct AttnParams {
   const float* q;         // [n_head * hd], roped
-  const void* kcache;     // this layer: [n_kv][n_ctx][hd]
+  const void* kcache;     // this layer's caches (common.cuh kv_row)
   const void* vcache;
+  const int* kv_table;    // block table of a paged cache (nullptr: contiguous)
   int kv_f16, n_ctx, hd, n_head, n_kv;
   int nt;                 // tile target of the tile attention (attn.cuh)
   int stage_rows;         // K/V rows per staged chunk of the tile attention
@@ -104,6 +105,7 @@ struct AttnParams {
   int* const* pos_list;
   void* const* k_list;
   void* const* v_list;
+  const int* const* table_list;  // per sequence, when the caches are paged
   size_t layer_off;
 };
 
@@ -123,11 +125,11 @@ __global__ void attention_exact_kernel(const AttnParams p) {
   const int h = blockIdx.x, hd = p.hd, gqa = p.n_head / p.n_kv, kvh = h / gqa;
   const int P = *p.pos + 1;
   const float* qh = p.q + (size_t)h * hd;
-  const size_t base = (size_t)kvh * p.n_ctx * hd;
   for (int j = threadIdx.x; j < P; j += blockDim.x) {
     float s = 0.0f;
+    const size_t base = kv_row(p.kv_table, p.n_ctx, p.n_kv, kvh, j) * hd;
     for (int d = 0; d < hd; ++d) {
-      const size_t at = base + (size_t)j * hd + d;
+      const size_t at = base + d;
       const float k = p.kv_f16 ? __half2float(reinterpret_cast<const __half*>(p.kcache)[at])
                                : reinterpret_cast<const float*>(p.kcache)[at];
       s = __fadd_rn(s, __fmul_rn(qh[d], k));
@@ -153,7 +155,7 @@ __global__ void attention_exact_kernel(const AttnParams p) {
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float acc = 0.0f;
     for (int j = 0; j < P; ++j) {
-      const size_t at = base + (size_t)j * hd + d;
+      const size_t at = kv_row(p.kv_table, p.n_ctx, p.n_kv, kvh, j) * hd + d;
       const float v = p.kv_f16 ? __half2float(reinterpret_cast<const __half*>(p.vcache)[at])
                                : reinterpret_cast<const float*>(p.vcache)[at];
       acc = __fadd_rn(acc, __fmul_rn(att[j], v));

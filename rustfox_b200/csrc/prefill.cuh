@@ -127,11 +127,12 @@ __global__ void quant_rows_k_kernel(const float* __restrict__ X, int K, const fl
 
 // QKV[t] holds the q, k and v rows of token t (position pos0 + t). Adjacent
 // row pairs of q and k are rotated with the position's tables; q goes to
-// Q[t], k and v to the caches ([kv_head][n_ctx][hd], f16 or f32).
+// Q[t], k and v to the caches (common.cuh kv_row: contiguous, or paged
+// through `table`; f16 or f32).
 __global__ void qkv_rows_kernel(const float* __restrict__ QKV, int n_rows, int nq, int nkv, int hd,
                                 int n_ctx, int pos0, const float* __restrict__ rope_cos,
                                 const float* __restrict__ rope_sin, int kv_f16, void* kcache,
-                                void* vcache, float* __restrict__ Q) {
+                                void* vcache, const int* __restrict__ table, float* __restrict__ Q) {
   const int t = blockIdx.y, P = pos0 + t;
   const float* vals = QKV + (size_t)t * n_rows;
   for (int rg = blockIdx.x * blockDim.x + threadIdx.x; rg < n_rows; rg += gridDim.x * blockDim.x) {
@@ -149,13 +150,13 @@ __global__ void qkv_rows_kernel(const float* __restrict__ QKV, int n_rows, int n
       if (rg < nq) {
         Q[(size_t)t * nq + rg] = o;
       } else {
-        const size_t idx = ((size_t)(rr / hd) * n_ctx + P) * hd + rr % hd;
+        const size_t idx = kv_row(table, n_ctx, nkv / hd, rr / hd, P) * hd + rr % hd;
         if (kv_f16) reinterpret_cast<__half*>(kcache)[idx] = __float2half_rn(o);
         else reinterpret_cast<float*>(kcache)[idx] = o;
       }
     } else {
       const int rr = rg - nq - nkv;
-      const size_t idx = ((size_t)(rr / hd) * n_ctx + P) * hd + rr % hd;
+      const size_t idx = kv_row(table, n_ctx, nkv / hd, rr / hd, P) * hd + rr % hd;
       if (kv_f16) reinterpret_cast<__half*>(vcache)[idx] = __float2half_rn(mine);
       else reinterpret_cast<float*>(vcache)[idx] = mine;
     }
@@ -187,13 +188,16 @@ __global__ void positions_kernel(int* __restrict__ pos, int pos0, int n) {
 // ---- decode batches: row t is the next token of sequence t ---------------
 
 // qkv_rows_kernel for a batch of sequences: row t's position is *pos[t] and
-// its caches start at kbase[t] / vbase[t] plus layer_off bytes.
+// its caches start at kbase[t] / vbase[t] plus layer_off bytes (paged
+// through tables[t] when tables is given).
 __global__ void qkv_seqs_kernel(const float* __restrict__ QKV, int n_rows, int nq, int nkv, int hd,
                                 int n_ctx, int* const* __restrict__ pos, void* const* __restrict__ kbase,
                                 void* const* __restrict__ vbase, size_t layer_off,
+                                const int* const* __restrict__ tables,
                                 const float* __restrict__ rope_cos, const float* __restrict__ rope_sin,
                                 int kv_f16, float* __restrict__ Q) {
   const int t = blockIdx.y, P = *pos[t];
+  const int* tab = tables ? tables[t] : nullptr;
   void* kcache = reinterpret_cast<uint8_t*>(kbase[t]) + layer_off;
   void* vcache = reinterpret_cast<uint8_t*>(vbase[t]) + layer_off;
   const float* vals = QKV + (size_t)t * n_rows;
@@ -212,13 +216,13 @@ __global__ void qkv_seqs_kernel(const float* __restrict__ QKV, int n_rows, int n
       if (rg < nq) {
         Q[(size_t)t * nq + rg] = o;
       } else {
-        const size_t idx = ((size_t)(rr / hd) * n_ctx + P) * hd + rr % hd;
+        const size_t idx = kv_row(tab, n_ctx, nkv / hd, rr / hd, P) * hd + rr % hd;
         if (kv_f16) reinterpret_cast<__half*>(kcache)[idx] = __float2half_rn(o);
         else reinterpret_cast<float*>(kcache)[idx] = o;
       }
     } else {
       const int rr = rg - nq - nkv;
-      const size_t idx = ((size_t)(rr / hd) * n_ctx + P) * hd + rr % hd;
+      const size_t idx = kv_row(tab, n_ctx, nkv / hd, rr / hd, P) * hd + rr % hd;
       if (kv_f16) reinterpret_cast<__half*>(vcache)[idx] = __float2half_rn(mine);
       else reinterpret_cast<float*>(vcache)[idx] = mine;
     }
@@ -244,17 +248,21 @@ FOX_DEV uint64_t splitmix64(uint64_t z) {
 }
 
 // Seeded normal values (Box-Muller on the two halves of splitmix64 of the
-// element index) for positions [0, n_pos) of every (layer, KV head) run of a
-// cache laid out [layer][kv_head][n_ctx][hd]. A benchmark stand-in for a long
-// prompt: upstream has no way to set its cache, so these contexts are not
-// compared with it.
+// logical element index, layer-major [layer][kv_head][n_ctx][hd]) for
+// positions [0, n_pos) of every (layer, KV head) run of a cache, stored
+// where kv_row puts them (layer_elems apart). A benchmark stand-in for a
+// long prompt: upstream has no way to set its cache, so these contexts are
+// not compared with it.
 __global__ void fill_kv_kernel(void* cache, int kv_f16, size_t runs, int n_ctx, int hd, int n_pos,
-                               uint64_t seed) {
+                               int n_kv, size_t layer_elems, const int* __restrict__ table, uint64_t seed) {
   const size_t per = (size_t)n_pos * hd, total = runs * per;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t run = i / per, r = i - run * per;
-    const size_t idx = run * (size_t)n_ctx * hd + r;
-    const uint64_t h = splitmix64(seed ^ splitmix64(idx));
+    const size_t logical = run * (size_t)n_ctx * hd + r;
+    const int layer = (int)(run / n_kv), kvh = (int)(run % n_kv);
+    const int pos = (int)(r / hd), d = (int)(r - (size_t)pos * hd);
+    const size_t idx = (size_t)layer * layer_elems + kv_row(table, n_ctx, n_kv, kvh, pos) * hd + d;
+    const uint64_t h = splitmix64(seed ^ splitmix64(logical));
     const float u1 = ((float)(uint32_t)(h >> 40) + 1.0f) * (1.0f / 16777217.0f);  // (0, 1]
     const float u2 = (float)(uint32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);   // [0, 1)
     const float v = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);

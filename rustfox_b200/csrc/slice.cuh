@@ -419,13 +419,13 @@ __global__ void __launch_bounds__(SLICE_THREADS, 2) slice_kernel(const GemvParam
         if (rg < p.nq) {
           p.out[rg] = o;
         } else {
-          const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+          const size_t idx = kv_row(p.kv_table, p.n_ctx, p.nkv / p.hd, rr / p.hd, P) * p.hd + rr % p.hd;
           if (p.kv_f16) reinterpret_cast<__half*>(p.kcache)[idx] = __float2half_rn(o);
           else reinterpret_cast<float*>(p.kcache)[idx] = o;
         }
       } else {
         const int rr = rg - p.nq - p.nkv;
-        const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+        const size_t idx = kv_row(p.kv_table, p.n_ctx, p.nkv / p.hd, rr / p.hd, P) * p.hd + rr % p.hd;
         if (p.kv_f16) reinterpret_cast<__half*>(p.vcache)[idx] = __float2half_rn(mine);
         else reinterpret_cast<float*>(p.vcache)[idx] = mine;
       }
@@ -759,13 +759,13 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) stream_kernel(const GemvPar
         if (rg < p.nq) {
           p.out[rg] = o;
         } else {
-          const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+          const size_t idx = kv_row(p.kv_table, p.n_ctx, p.nkv / p.hd, rr / p.hd, P) * p.hd + rr % p.hd;
           if (p.kv_f16) reinterpret_cast<__half*>(p.kcache)[idx] = __float2half_rn(o);
           else reinterpret_cast<float*>(p.kcache)[idx] = o;
         }
       } else {
         const int rr = rg - p.nq - p.nkv;
-        const size_t idx = ((size_t)(rr / p.hd) * p.n_ctx + P) * p.hd + rr % p.hd;
+        const size_t idx = kv_row(p.kv_table, p.n_ctx, p.nkv / p.hd, rr / p.hd, P) * p.hd + rr % p.hd;
         if (p.kv_f16) reinterpret_cast<__half*>(p.vcache)[idx] = __float2half_rn(mine);
         else reinterpret_cast<float*>(p.vcache)[idx] = mine;
       }
