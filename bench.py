@@ -791,6 +791,14 @@ def run_batch(args):
     batch.generate(smp, args.steps)
     secs = batch.last_seconds
     ck = clocks.stop()
+    # the attention launches on their own: one profiled step (events after
+    # each phase on the batch's stream), its position at the end of the run
+    prof = batch.profile_step(synth.random_prompt(cfg, n, seed=3))
+    phase_us = {}
+    for kind, us in prof:
+        phase_us[kind] = phase_us.get(kind, 0.0) + us
+    attn_us = phase_us.get("attention", 0.0) / cfg.n_layer
+    p_prof = args.ctx + warm + args.steps + 1  # positions each sequence reads in that step
     # algorithmic bytes of a step: the layer and head GGUF bytes once, the
     # K/V every sequence reads (mean position of the timed steps) and writes
     pos = args.ctx + warm + args.steps / 2.0
@@ -798,6 +806,8 @@ def run_batch(args):
     step_bytes = (wb["layers"] + wb["output"] + 2 * cfg.n_layer * pos * kv_row * n
                   + 2 * cfg.n_layer * kv_row * n)
     achieved = step_bytes / (secs / args.steps) / 1e9
+    attn_bytes = 2 * p_prof * kv_row * n  # one layer's K and V of every sequence
+    attn_gbs = attn_bytes / (attn_us * 1e-6) / 1e9 if attn_us > 0 else None
     hbm, src = measured_hbm_gbs()
     print(json.dumps({
         "metric": f"batch-{n} decode tok/s at {args.ctx} context", "value": n * args.steps / secs,
@@ -811,9 +821,12 @@ def run_batch(args):
                    "kv_cache": "f16, " + ("one contiguous cache per sequence" if pool is None else
                                           f"paged: {rf.api.KV_PAGE}-position pages of one shared pool"),
                    "l2": f"{step_bytes / 1e9:.1f} GB per step > 126 MB L2"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "traffic": None, "peak_source": src,
-                     "bytes_per_step": step_bytes},
+        "roofline": {"bound": "hbm", "kernel": "attention_tile_kernel (one launch per layer, all sequences)",
+                     "achieved": attn_gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": attn_gbs / hbm if attn_gbs else None, "traffic": None, "peak_source": src,
+                     "algorithmic_bytes_per_launch": attn_bytes, "us_per_launch": attn_us},
+        "step_roofline": {"achieved": achieved, "frac": achieved / hbm, "bytes_per_step": step_bytes},
+        "phases_us_per_step": {k: round(v, 1) for k, v in phase_us.items()},
         "cpu_baseline": None,
         "cpu_baseline_note": "upstream has no way to set its cache (or to decode several sequences "
                              "in one pass), so a 32k-position upstream decode would need the 32k-token "

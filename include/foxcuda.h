@@ -386,6 +386,12 @@ foxcuda_status foxcuda_batch_step(foxcuda_batch *b, const uint32_t *tokens, floa
 foxcuda_status foxcuda_batch_generate(foxcuda_batch *b, foxcuda_sampler *const *samplers,
                                       const uint32_t *first, size_t n_steps, uint32_t *out);
 double         foxcuda_batch_last_seconds(const foxcuda_batch *b);
+/* One batch step on host tokens with a CUDA event after each phase (embed,
+ * then per layer qkv, attention, o, gate_up, down, then head, advance): the
+ * phase kinds (as foxcuda_context_profile numbers them) and microseconds,
+ * at most cap of them, their count in *n_out. */
+foxcuda_status foxcuda_batch_profile(foxcuda_batch *b, const uint32_t *tokens, float *us, int *kinds,
+                                     int cap, int *n_out);
 /* Benchmark stand-in for a long prompt: positions [0, n_pos) of every layer's
  * K and V are set to seeded N(0, 1) values and the position to n_pos. */
 foxcuda_status foxcuda_context_fill_kv(foxcuda_context *c, uint32_t n_pos, uint64_t seed);

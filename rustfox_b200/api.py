@@ -119,6 +119,7 @@ _PROTOS = {
     "foxcuda_batch_step": (_st, [_vp, _vp, _vp]),
     "foxcuda_batch_generate": (_st, [_vp, _vp, _vp, _sz, _vp]),
     "foxcuda_batch_last_seconds": (C.c_double, [_vp]),
+    "foxcuda_batch_profile": (_st, [_vp, _vp, _vp, _vp, C.c_int, C.POINTER(C.c_int)]),
     "foxcuda_context_fill_kv": (_st, [_vp, C.c_uint32, C.c_uint64]),
     "foxcuda_context_profile": (_st, [_vp, _vp, C.c_uint32, _vp, _vp, C.c_int,
                                       C.POINTER(C.c_int)]),
@@ -695,6 +696,17 @@ class Batch:
     @property
     def last_seconds(self) -> float:
         return lib().foxcuda_batch_last_seconds(self.h)
+
+    def profile_step(self, tokens) -> list:
+        """One step on host tokens, phase by phase: [(kind name, microseconds), ...]."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        cap = 4096
+        us = np.zeros(cap, np.float32)
+        kinds = np.zeros(cap, np.int32)
+        n = C.c_int()
+        _check(lib().foxcuda_batch_profile(self.h, t.ctypes.data_as(C.c_void_p), us.ctypes.data_as(C.c_void_p),
+                                           kinds.ctypes.data_as(C.c_void_p), cap, C.byref(n)))
+        return [(KIND_NAMES[k], float(v)) for k, v in zip(kinds[:n.value], us[:n.value])]
 
 
 def greedy_generate(model: Model, prompt, n_gen: int, n_ctx: int, kv: str = "f16",

@@ -33,6 +33,7 @@ namespace fox {
 #define FOX_ATTN_MARK(k)
 #endif
 
+constexpr int ATTN_THREADS = 256;    // threads of a tile CTA
 constexpr int ATTN_TILE_MAX = 8;     // tile target NT: the tiles of a KV head form one portable cluster
 constexpr int ATTN_TILE_GQA = 8;     // query heads per KV head
 
@@ -364,7 +365,7 @@ FOX_DEV void attn_merge(const TileArgs& a, const TileSmem& m, int g, int nt) {
 // that writes q and position P - 1) the older rows of the first chunk are
 // staged before griddepcontrol.wait; q and the newest row are read after it.
 template <int DPL, bool F16, int G>
-__global__ void __launch_bounds__(256, 1) attention_tile_kernel(const AttnParams k) {
+__global__ void __launch_bounds__(ATTN_THREADS, 1) attention_tile_kernel(const AttnParams k) {
   extern __shared__ __align__(16) float tsm[];
   griddep_launch_dependents();  // the o projection may start streaming its weights
   FOX_ATTN_MARK(0);

@@ -820,8 +820,9 @@ static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t 
 static int attn_nt_for(int sms, int n_kv_full) {
   return std::max(1, std::min(ATTN_TILE_MAX, sms / std::max(1, n_kv_full)));
 }
-// K/V rows per staged chunk: 64 KB of shared memory for K and V together.
-static int attn_stage_rows(int kv_f16) { return kv_f16 ? 128 : 64; }
+// K/V rows per staged chunk of the tile attention: 64 KB of shared memory
+// for K and V together.
+static int attn_stage_rows(const AttnParams& ap, int) { return ap.kv_f16 ? 128 : 64; }
 
 extern "C" int foxcuda_attn_tile_target(int device, uint32_t n_head_kv) {
   return attn_nt_for(sm_count(device), (int)n_head_kv);
@@ -853,7 +854,7 @@ extern "C" foxcuda_status foxcuda_attention(const float* q, const void* kcache, 
     AttnParams ap{};
     ap.q = q; ap.kcache = kcache; ap.vcache = vcache; ap.kv_f16 = kv_type == FOXCUDA_KV_F16;
     ap.n_ctx = (int)n_ctx; ap.hd = (int)head_dim; ap.n_head = (int)n_head; ap.n_kv = (int)n_head_kv;
-    ap.nt = nt; ap.stage_rows = attn_stage_rows(ap.kv_f16); ap.pos = pos_dev; ap.out = out;
+    ap.nt = nt; ap.pos = pos_dev; ap.out = out;
     ap.scale = 1.0f / sqrtf((float)head_dim);
     e = run_attention(ap, exact != 0, s);
   }
@@ -2228,15 +2229,17 @@ static cudaError_t launch_qkv(foxcuda_context* c, uint32_t l) {
 // stream serialisation, right after the kernel that writes q and the newest
 // K/V row and nothing else this kernel reads (the decode step's q|k|v GEMV).
 template <int DPL, bool F16, int G>
-static cudaError_t launch_tile_g(const AttnParams& ap, int n_seq, cudaStream_t s, bool pdl) {
+static cudaError_t launch_tile_g(const AttnParams& ap_in, int n_seq, cudaStream_t s, bool pdl) {
   auto kern = attention_tile_kernel<DPL, F16, G>;
+  AttnParams ap = ap_in;
+  ap.stage_rows = attn_stage_rows(ap, G);
   const size_t sm = attn_tile_smem_bytes(ap.n_ctx, ap.nt, G, ap.hd, F16 ? 1 : 0, ap.stage_rows);
   static size_t marks[kMaxDevices] = {};
   cudaError_t e = opt_in_smem(kern, sm, marks);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ap.nt, ap.n_kv, n_seq);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(ATTN_THREADS);
   cfg.dynamicSmemBytes = sm;
   cfg.stream = s;
   cudaLaunchAttribute at[2];
@@ -2294,7 +2297,7 @@ static cudaError_t launch_attn(foxcuda_context* c, uint32_t l) {
   ap.q = c->q; ap.kcache = kv_layer(c, c->kc, l); ap.vcache = kv_layer(c, c->vc, l); ap.kv_table = c->kv_table;
   ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
   ap.hd = mi.head_dim; ap.n_head = c->m->loc.n_head; ap.n_kv = c->m->loc.n_head_kv; ap.nt = c->m->attn_nt;
-  ap.stage_rows = attn_stage_rows(c->kv_f16); ap.pos = c->pos_dev; ap.out = c->att;
+  ap.pos = c->pos_dev; ap.out = c->att;
   ap.scale = 1.0f / sqrtf((float)mi.head_dim);
   return run_attention(ap, c->attn_exact, c->stream, ctx_pdl(c));
 }
@@ -2577,7 +2580,6 @@ static cudaError_t chunk_attention(foxcuda_context* c, uint32_t l, int M, bool o
   AttnParams ap{};
   ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
   ap.hd = hd; ap.n_head = m->loc.n_head; ap.n_kv = m->loc.n_head_kv; ap.nt = m->attn_nt;
-  ap.stage_rows = attn_stage_rows(c->kv_f16);
   ap.scale = 1.0f / sqrtf((float)hd);
   if (one_launch && !c->attn_exact) {
     ap.q = c->pf_q; ap.out = c->pf_att; ap.seq_stride = nq;
@@ -2901,7 +2903,17 @@ struct foxcuda_batch {
   std::vector<void*> allocs;
   cudaGraphExec_t graph = nullptr;  // a step and the picks, for foxcuda_batch_generate
   std::vector<foxcuda_sampler*> graph_samplers;
+  std::vector<std::pair<cudaEvent_t, int>>* prof = nullptr;  // phase marks (foxcuda_batch_profile)
 };
+
+// An event after the launches of one phase of a profiled batch step.
+static void bmark(foxcuda_batch* b, int kind) {
+  if (!b->prof) return;
+  cudaEvent_t e;
+  if (cudaEventCreate(&e) != cudaSuccess) return;
+  cudaEventRecord(e, b->stream);
+  b->prof->push_back({e, kind});
+}
 
 extern "C" void foxcuda_batch_destroy(foxcuda_batch* b) {
   if (!b) return;
@@ -3012,6 +3024,7 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
   embed_rows_kernel<<<dim3((E + 255) / 256, M), 256, 0, s>>>(m->embd.type, m->embd.dev,
                                                             row_bytes(m->embd.type, E), E, b->toks, b->x);
   cudaError_t e = cudaGetLastError();
+  bmark(b, PK_EMBED);
   for (uint32_t l = 0; l < mi.n_layer && !e; ++l) {
     const LayerW& L = m->layers[l];
     if ((e = quant_rows_to<true>(b->x, E, L.attn_norm, eps, decode_threads(L.qkv[0]), M, b->xq, b->xs, s)))
@@ -3021,6 +3034,7 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
         b->qkv, nqkv, nq, nkv, hd, (int)c0->n_ctx, b->pos, b->kbase, b->vbase, (size_t)l * layer_bytes,
         b->tables, c0->rope_cos, c0->rope_sin, c0->kv_f16, b->q);
     if ((e = cudaGetLastError())) break;
+    bmark(b, PK_QKV);
     AttnParams all{};
     all.q = b->q; all.out = b->att; all.seq_stride = nq;
     all.pos_list = b->pos; all.k_list = b->kbase; all.v_list = b->vbase; all.layer_off = (size_t)l * layer_bytes;
@@ -3028,7 +3042,6 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
     all.kv_f16 = c0->kv_f16; all.n_ctx = c0->n_ctx;
     all.hd = hd; all.n_head = mi.n_head; all.n_kv = mi.n_head_kv; all.nt = m->attn_nt;
     all.scale = 1.0f / sqrtf((float)hd);
-    all.stage_rows = attn_stage_rows(c0->kv_f16);
     if (!c0->attn_exact) {
       e = launch_tiles(all, M, s);
     } else {
@@ -3039,23 +3052,27 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
         ap.kv_table = c->kv_table;
         ap.kv_f16 = c->kv_f16; ap.n_ctx = c->n_ctx;
         ap.hd = hd; ap.n_head = mi.n_head; ap.n_kv = mi.n_head_kv; ap.nt = m->attn_nt;
-        ap.pos = c->pos_dev; ap.out = b->att + (size_t)i * nq; ap.stage_rows = attn_stage_rows(c->kv_f16);
+        ap.pos = c->pos_dev; ap.out = b->att + (size_t)i * nq;
         ap.scale = 1.0f / sqrtf((float)hd);
         e = run_attention(ap, c->attn_exact, s);
       }
     }
     if (e) break;
+    bmark(b, PK_ATTN);
     if ((e = quant_rows_to<false>(b->att, nq, nullptr, eps, 256, M, b->xq, b->xs, s))) break;
     if ((e = tc_rows_to(b->xq, b->xs, L.o, M, b->t, c0->err_dev, s))) break;
     add_rows_kernel<<<add_grid, 256, 0, s>>>(b->x, b->t, rows_e);
+    bmark(b, PK_O);
     if ((e = quant_rows_to<true>(b->x, E, L.ffn_norm, eps, decode_threads(L.gateup), M, b->xq, b->xs, s)))
       break;
     if ((e = tc_rows_to(b->xq, b->xs, L.gateup, M, b->gu, c0->err_dev, s))) break;
     swiglu_rows_kernel<<<dim3((F + 255) / 256, M), 256, 0, s>>>(b->gu, 2 * F, L.gateup.U, b->h);
+    bmark(b, PK_GATEUP);
     if ((e = quant_rows_to<false>(b->h, F, nullptr, eps, 256, M, b->xq, b->xs, s))) break;
     if ((e = tc_rows_to(b->xq, b->xs, L.down, M, b->t, c0->err_dev, s))) break;
     add_rows_kernel<<<add_grid, 256, 0, s>>>(b->x, b->t, rows_e);
     e = cudaGetLastError();
+    bmark(b, PK_DOWN);
   }
   if (!e && b->lg) {
     // a K-quant head quantises per 256 block like the layers: one K-quant
@@ -3075,7 +3092,9 @@ static cudaError_t enqueue_batch_body(foxcuda_batch* b, bool gather) {
     }
   }
   if (e) return e;
+  bmark(b, PK_HEAD);
   advance_all_kernel<<<1, BATCH_MAX, 0, s>>>(b->pos, M);
+  bmark(b, PK_ADVANCE);
   return cudaGetLastError();
 }
 
@@ -3122,6 +3141,41 @@ extern "C" foxcuda_status foxcuda_batch_step(foxcuda_batch* b, const uint32_t* t
   float ms = 0.0f;
   cudaEventElapsedTime(&ms, b->ev0, b->ev1);
   b->last_seconds = ms / 1e3;
+  for (foxcuda_context* c : b->ctx) c->pos += 1;
+  return batch_errors(b);
+}
+
+// One batch step (as foxcuda_batch_step, no logits copied out) with an
+// event after each phase: kinds and microseconds per phase, as
+// foxcuda_context_profile gives them for a decode step.
+extern "C" foxcuda_status foxcuda_batch_profile(foxcuda_batch* b, const uint32_t* tokens, float* us,
+                                                int* kinds, int cap, int* n_out) {
+  if (!b || !tokens || !us || !kinds || !n_out || cap <= 0) return fail(FOXCUDA_ERR_ARG, "batch profile: bad argument");
+  const uint32_t nv = b->m->info.n_vocab;
+  for (int i = 0; i < b->n; ++i)
+    if (tokens[i] >= nv) return fail(FOXCUDA_ERR_ARG, "forward: token %u is outside the vocabulary", tokens[i]);
+  foxcuda_status st = batch_begin(b, 1);
+  if (st) return st;
+  CK(cudaMemcpyAsync(b->toks, tokens, (size_t)b->n * 4, cudaMemcpyHostToDevice, b->stream), "tokens");
+  std::vector<std::pair<cudaEvent_t, int>> marks;
+  CK(cudaEventRecord(b->ev0, b->stream), "event");
+  b->prof = &marks;
+  cudaError_t e = enqueue_batch_body(b, false);
+  b->prof = nullptr;
+  cudaError_t e2 = cudaStreamSynchronize(b->stream);
+  int n = 0;
+  cudaEvent_t prev = b->ev0;
+  for (auto& mk : marks) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, prev, mk.first);
+    if (n < cap) { us[n] = ms * 1e3f; kinds[n] = mk.second; ++n; }
+    if (prev != b->ev0) cudaEventDestroy(prev);
+    prev = mk.first;
+  }
+  if (prev != b->ev0) cudaEventDestroy(prev);
+  *n_out = n;
+  if (e) return cuda_fail(e, "batch profile");
+  CK(e2, "batch profile");
   for (foxcuda_context* c : b->ctx) c->pos += 1;
   return batch_errors(b);
 }

@@ -94,7 +94,7 @@ struct AttnParams {
   const int* kv_table;    // block table of a paged cache (nullptr: contiguous)
   int kv_f16, n_ctx, hd, n_head, n_kv;
   int nt;                 // tile target of the tile attention (attn.cuh)
-  int stage_rows;         // K/V rows per staged chunk of the tile attention
+  int stage_rows;         // K/V rows per ring slot of the tile attention (set by its launch)
   const int* pos;
   float* out;             // [n_head * hd]
   float scale;
@@ -305,21 +305,31 @@ __global__ void __launch_bounds__(TOPK_THREADS)
 topk_sample_kernel(SamplerDev* st, float* logits, int n_vocab, int k, float temperature,
                    float top_p, int restore, int accept, uint32_t* token_out,
                    uint32_t* ring, int ring_cap) {
+  constexpr int NWARP = TOPK_THREADS / 32;
   __shared__ unsigned hist[256];
   __shared__ uint32_t prefix, want;
-  __shared__ float cv[TOPK_MAX];
-  __shared__ uint32_t ci[TOPK_MAX];
-  __shared__ unsigned n_gt, n_eq_taken;
-  const int tid = threadIdx.x;
-  // radix select: the key of the k-th largest element
+  __shared__ float cv[2 * TOPK_MAX];  // [0, TOPK_MAX): candidates; above: keys equal to the threshold
+  __shared__ uint32_t ci[2 * TOPK_MAX];
+  __shared__ unsigned n_gt, n_eq, n_eq_taken, wcount[NWARP];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // radix select: the key of the k-th largest element. The histogram adds
+  // are aggregated per warp over lanes with the same digit (logits crowd a
+  // few top-byte digits).
   if (tid == 0) { prefix = 0; want = k; }
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint32_t pmask = shift == 24 ? 0u : (0xffffffffu << (shift + 8));
-    for (int i = tid; i < n_vocab; i += blockDim.x) {
-      const uint32_t key = order_key(logits[i]);
-      if ((key & pmask) == (prefix & pmask)) atomicAdd(&hist[(key >> shift) & 0xff], 1u);
+    const uint32_t pre = prefix & pmask;
+    for (int base = 0; base < n_vocab; base += TOPK_THREADS) {
+      const int i = base + tid;
+      uint32_t digit = 0xffffffffu;  // no digit: out of range or another prefix
+      if (i < n_vocab) {
+        const uint32_t key = order_key(logits[i]);
+        if ((key & pmask) == pre) digit = (key >> shift) & 0xffu;
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, digit);
+      if (digit != 0xffffffffu && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], (unsigned)__popc(peers));
     }
     __syncthreads();
     if (tid == 0) {
@@ -334,24 +344,50 @@ topk_sample_kernel(SamplerDev* st, float* logits, int n_vocab, int k, float temp
     }
     __syncthreads();
   }
-  // candidates: keys above the threshold, then equal keys in index order
-  if (tid == 0) { n_gt = 0; n_eq_taken = 0; }
+  // candidates: every key above the threshold T (fewer than k), then keys
+  // equal to T in index order until there are k
+  if (tid == 0) { n_gt = 0; n_eq = 0; }
   __syncthreads();
   const uint32_t T = prefix;
   for (int i = tid; i < n_vocab; i += blockDim.x) {
-    const uint32_t key = order_key(logits[i]);
+    const float v = logits[i];
+    const uint32_t key = order_key(v);
     if (key > T) {
       const unsigned slot = atomicAdd(&n_gt, 1u);
-      cv[slot] = logits[i];
+      cv[slot] = v;
       ci[slot] = i;
+    } else if (key == T) {
+      const unsigned slot = atomicAdd(&n_eq, 1u);
+      if (slot < TOPK_MAX) { cv[TOPK_MAX + slot] = v; ci[TOPK_MAX + slot] = i; }
     }
   }
   __syncthreads();
-  if (tid == 0) {  // equal keys: lowest indices first (stable selection)
-    unsigned slot = n_gt;
-    for (int i = 0; i < n_vocab && slot < (unsigned)k; ++i)
-      if (order_key(logits[i]) == T) { cv[slot] = logits[i]; ci[slot] = i; ++slot; }
-    n_eq_taken = slot;
+  const unsigned need = (unsigned)k - n_gt;
+  if (n_eq <= need) {
+    // all of them (their order is the sort's business)
+    for (unsigned j = tid; j < n_eq; j += blockDim.x) { cv[n_gt + j] = cv[TOPK_MAX + j]; ci[n_gt + j] = ci[TOPK_MAX + j]; }
+    if (tid == 0) n_eq_taken = n_gt + n_eq;
+  } else {
+    // more equal keys than places: the lowest indices, by an ordered scan of
+    // the vocabulary TOPK_THREADS ids at a time
+    unsigned taken = 0;
+    for (int base = 0; base < n_vocab && taken < need; base += TOPK_THREADS) {
+      const int i = base + tid;
+      const bool eq = i < n_vocab && order_key(logits[i]) == T;
+      const unsigned bal = __ballot_sync(0xffffffffu, eq);
+      if (lane == 0) wcount[warp] = (unsigned)__popc(bal);
+      __syncthreads();
+      unsigned off = taken, all = 0;
+      for (int w = 0; w < NWARP; ++w) {
+        if (w < warp) off += wcount[w];
+        all += wcount[w];
+      }
+      off += (unsigned)__popc(bal & ((1u << lane) - 1u));
+      if (eq && off < need) { cv[n_gt + off] = logits[i]; ci[n_gt + off] = i; }
+      taken += all;  // the same in every thread
+      __syncthreads();  // wcount is rewritten by the next block
+    }
+    if (tid == 0) n_eq_taken = n_gt + min(taken, need);
   }
   __syncthreads();
   const int n = (int)n_eq_taken;

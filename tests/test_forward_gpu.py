@@ -191,3 +191,48 @@ def test_context_overrun_and_bad_token(gpu_tiny):
     assert e.value.status == 1
     assert ctx.pos == 0
     ctx.close()
+
+
+def _head_rows(sm):
+    _, ne, arr = sm.tensors["output.weight"]
+    return arr.view(np.uint8).reshape(ne[1], -1)
+
+
+def test_topk_ties_match_oracle_sampler():
+    """Exact ties at the k-th largest logit (output rows duplicated, so their
+    logits are equal bit for bit): the device takes the tied tokens of lowest
+    index, as upstream's sort does, whether all the tied tokens fit among the
+    k or only some of them (then by index), and when every logit is equal."""
+    cfg = CFG.scaled(name="tiny-ties", n_layer=1)
+    prompt = synth.random_prompt(cfg, 8, seed=3)
+    m0 = rf.Model.from_synthetic(synth.generate(cfg))
+    c0 = m0.context(64)
+    base_logits = c0.eval(prompt)
+    c0.close()
+    m0.close()
+    order = np.lexsort((np.arange(cfg.n_vocab), -base_logits))  # rank -> token
+    tied = synth.generate(cfg)
+    rows = _head_rows(tied)
+    rows[order[39]] = rows[order[38]]           # ranks 38, 39 tie: both among the top 40
+    rows[order[-51:]] = rows[order[299]]        # 51 tokens tie at rank 299: one of them in the top 300
+    flat = synth.generate(cfg)
+    frows = _head_rows(flat)
+    frows[1:] = frows[0]                        # every logit equal
+    samplers = [dict(temperature=0.8, top_k=40, top_p=1.0, seed=1),
+                dict(temperature=1.0, top_k=300, top_p=0.9, seed=5),
+                dict(temperature=0.7, top_k=0, top_p=1.0, seed=2)]
+    for sm in (tied, flat):
+        m = rf.Model.from_synthetic(sm)
+        ctx = m.context(64)
+        logits = ctx.eval(prompt)
+        if sm is tied:
+            assert logits[order[39]] == logits[order[38]]
+        for scfg in samplers:
+            kw = dict(repeat_penalty=1.0, repeat_last_n=64, **scfg)
+            s = rf.Sampler(ctx, **kw)
+            o = O.OracleSampler(cfg.n_vocab, **kw)
+            for _ in range(20):
+                assert s.pick() == o.pick(logits), scfg
+            s.close()
+        ctx.close()
+        m.close()
