@@ -33,7 +33,6 @@ namespace fox {
 #define FOX_ATTN_MARK(k)
 #endif
 
-constexpr int ATTN_THREADS = 256;    // threads of a tile CTA
 constexpr int ATTN_TILE_MAX = 8;     // tile target NT: the tiles of a KV head form one portable cluster
 constexpr int ATTN_TILE_GQA = 8;     // query heads per KV head
 
@@ -44,8 +43,6 @@ FOX_DEV void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 FOX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-FOX_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-FOX_DEV void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 FOX_DEV unsigned cluster_ctarank() {
   unsigned r;
@@ -64,12 +61,12 @@ FOX_DEV const float* cluster_peer(const float* p, unsigned rank) {
   return reinterpret_cast<const float*>(r);
 }
 
-// K/V rows of one KV head staged in shared memory, ch rows at a time.
-struct TileStage {
-  uint8_t* k;   // ch rows of K
-  uint8_t* v;   // ch rows of V
-  int ch;
-};
+constexpr int ATTN_THREADS = 256;  // threads of a tile CTA (8 warps)
+constexpr int ATTN_RING = 3;       // staged chunks per CTA: ATTN_RING - 1 in flight while one is read
+
+FOX_DEV void cp_async_wait_ring() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(ATTN_RING - 1) : "memory");
+}
 
 // Where KV head g's positions of one sequence and layer live: the cache
 // base, and its block table when paged (common.cuh kv_row).
@@ -81,62 +78,88 @@ struct KvHead {
 };
 
 // Positions [r0, r1) of a head into buf, position r at (r - r0) * rb,
-// except position `skip`; asynchronous (cp.async, L2 only), one commit group.
+// except position `skip`; asynchronous (cp.async, L2 only), no commit. The
+// row is rb / 16 pieces of 16 bytes and that count divides ATTN_THREADS
+// (head_dim 64, 128 or 256), so each thread copies the same piece of every
+// (ATTN_THREADS / pieces)-th row.
 FOX_DEV void stage_rows(uint8_t* buf, const KvHead& kv, int r0, int r1, int skip) {
-  const int per_row = kv.rb >> 4, pieces = (r1 - r0) * per_row;
-  for (int i = threadIdx.x; i < pieces; i += blockDim.x) {
-    const int row = i / per_row;
+  const int per_row = kv.rb >> 4;
+  const int col = (int)threadIdx.x % per_row, rstep = ATTN_THREADS / per_row;
+  for (int row = (int)threadIdx.x / per_row; r0 + row < r1; row += rstep) {
     if (r0 + row == skip) continue;
-    cp_async16(buf + (uint32_t)i * 16, kv.row(r0 + row) + (uint32_t)(i - row * per_row) * 16);
+    cp_async16(buf + (uint32_t)row * kv.rb + col * 16, kv.row(r0 + row) + col * 16);
   }
-  cp_async_commit();
 }
 
-// Row r of a staged chunk as floats (DPL elements from element e0).
+// NW consecutive 32-bit words from p (aligned to 4 * NW bytes, at most 16),
+// with vector loads.
+template <int NW>
+FOX_DEV void load_words(const uint8_t* p, unsigned (&w)[NW]) {
+  if constexpr (NW == 1) {
+    w[0] = *reinterpret_cast<const unsigned*>(p);
+  } else if constexpr (NW == 2) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    w[0] = u.x; w[1] = u.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < NW / 4; ++i) {
+      const uint4 u = reinterpret_cast<const uint4*>(p)[i];
+      w[4 * i] = u.x; w[4 * i + 1] = u.y; w[4 * i + 2] = u.z; w[4 * i + 3] = u.w;
+    }
+  }
+}
+
+// Row r of a staged chunk as floats: DPL elements from element e0.
 template <int DPL, bool F16>
 FOX_DEV void staged_row(const uint8_t* buf, int r, int hd, int e0, float* v) {
-  if (F16) {
-    const __half* p = reinterpret_cast<const __half*>(buf) + (size_t)r * hd + e0;
+  constexpr int ES = F16 ? 2 : 4, NW = DPL * ES / 4;
+  unsigned w[NW];
+  load_words<NW>(buf + ((uint32_t)r * hd + e0) * ES, w);
 #pragma unroll
-    for (int i = 0; i < DPL; i += 2) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p + i));
-      v[i] = f.x;
-      if (i + 1 < DPL) v[i + 1] = f.y;
+  for (int i = 0; i < NW; ++i) {
+    if (F16) {
+      v[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xffffu)));
+      v[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+    } else {
+      v[i] = __uint_as_float(w[i]);
     }
-  } else {
-    const float* p = reinterpret_cast<const float*>(buf) + (size_t)r * hd + e0;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) v[i] = p[i];
   }
 }
 
-// Scores of 16 rows (r0.., at most `valid` of them) of a staged chunk for one
-// query head: lane l forms the partial over its hd/32 dimensions for each
-// row, then a butterfly reduce-scatter (offsets 16, 8, 4, 2) and a last
-// exchange at offset 1 leave row r0 + (lane >> 1)'s dot in lanes 2k, 2k+1.
-// Every add pairs the same lane partials as an xor all-reduce (16, 8, 4, 2,
-// 1) does, so each dot is the all-reduce's value bit for bit, with 16
-// exchanges for 16 rows instead of 80.
-template <int DPL, bool F16>
-FOX_DEV float dot16(const uint8_t* buf, int r0, int valid, int hd, const float* qh, int lane) {
+// Element d of row r of a staged chunk.
+template <bool F16>
+FOX_DEV float staged_one(const uint8_t* buf, int r, int hd, int d) {
+  if (F16) return __half2float(reinterpret_cast<const __half*>(buf)[(uint32_t)r * hd + d]);
+  return reinterpret_cast<const float*>(buf)[(uint32_t)r * hd + d];
+}
+
+// Scores of 8 rows held in registers (kf, the lane's hd/32 dimensions of
+// each; at most `valid` rows) for one query head: lane l forms the partial
+// over its dimensions for each row (q0*k0, then fmaf in dimension order),
+// then a butterfly reduce-scatter (offsets 16, 8, 4) and two exchanges (2,
+// 1) leave row (lane >> 2)'s dot in lanes 4k..4k+3. Every add pairs the
+// same lane partials as an xor all-reduce (16, 8, 4, 2, 1) does, so each dot
+// is the all-reduce's value bit for bit, with 9 exchanges for 8 rows
+// instead of 40.
+template <int DPL>
+FOX_DEV float dot8(const float (&kf)[8][DPL], int valid, const float* qh, int lane) {
   float q[DPL];
 #pragma unroll
   for (int e = 0; e < DPL; ++e) q[e] = qh[lane * DPL + e];
-  float P[16];
+  float P[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 8; ++i) {
     P[i] = 0.0f;
     if (i < valid) {
-      float k[DPL];
-      staged_row<DPL, F16>(buf, r0 + i, hd, lane * DPL, k);
-      float d = __fmul_rn(q[0], k[0]);
+      float d = __fmul_rn(q[0], kf[i][0]);
 #pragma unroll
-      for (int e = 1; e < DPL; ++e) d = __fmaf_rn(q[e], k[e], d);
+      for (int e = 1; e < DPL; ++e) d = __fmaf_rn(q[e], kf[i][e], d);
       P[i] = d;
     }
   }
 #pragma unroll
-  for (int o = 16, m = 16; o >= 2; o >>= 1, m >>= 1) {
+  for (int lv = 0; lv < 3; ++lv) {
+    const int o = 16 >> lv, m = 8 >> lv;
     const bool up = (lane & o) != 0;
 #pragma unroll
     for (int i = 0; i < m / 2; ++i) {
@@ -145,39 +168,42 @@ FOX_DEV float dot16(const uint8_t* buf, int r0, int valid, int hd, const float* 
       P[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
     }
   }
-  return __fadd_rn(P[0], __shfl_xor_sync(0xffffffffu, P[0], 1));
+  const float r = __fadd_rn(P[0], __shfl_xor_sync(0xffffffffu, P[0], 2));
+  return __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));
 }
 
 // Shared memory of a tile CTA (floats unless noted):
-//   sc    G * Tmax   scores, then weights
+//   sc    G * ts     scores, then weights (ts: tile length rounded up to 4)
 //   q     G * hd     the group's query heads
-//   ml    64         per-head max [0, 32), sum [32, 64); the merge's w [32..)
+//   ml    64         per-head max [0, 32), sum [32, 64)
 //   part  G * hd     this tile's unnormalised outputs (read by the cluster)
-//   K, V  2 * ch * row bytes  staged rows
+//   ring  ATTN_RING * ch * row bytes: staged chunks of K, then of V
 struct TileSmem {
   float* sc;
   float* q;
   float* ml;
   float* part;
-  TileStage st;
+  uint8_t* ring;
+  int ch, ts, slot;  // rows per chunk, score row stride, bytes per ring slot
 };
 
+__host__ __device__ inline int attn_score_stride(int n_ctx, int nt) { return (attn_tile_len(n_ctx, nt) + 3) & ~3; }
+
 inline size_t attn_tile_smem_bytes(int n_ctx, int nt, int gqa, int hd, int kv_f16, int ch) {
-  const size_t tmax = (size_t)attn_tile_len(n_ctx, nt);
-  const size_t floats = ((size_t)gqa * tmax + 3) / 4 * 4 + (size_t)gqa * hd + 64 + (size_t)gqa * hd;
-  return floats * 4 + 2 * (size_t)ch * hd * (kv_f16 ? 2 : 4);
+  const size_t floats = (size_t)gqa * attn_score_stride(n_ctx, nt) + 2 * (size_t)gqa * hd + 64;
+  return floats * 4 + (size_t)ATTN_RING * ch * hd * (kv_f16 ? 2 : 4);
 }
 
 FOX_DEV TileSmem tile_smem(float* base, int n_ctx, int nt, int gqa, int hd, int kv_f16, int ch) {
   TileSmem m;
-  const int tmax = attn_tile_len(n_ctx, nt);
+  m.ts = attn_score_stride(n_ctx, nt);
   m.sc = base;
-  m.q = base + (gqa * tmax + 3) / 4 * 4;
+  m.q = base + gqa * m.ts;
   m.ml = m.q + gqa * hd;
   m.part = m.ml + 64;
-  m.st.k = reinterpret_cast<uint8_t*>(m.part + gqa * hd);
-  m.st.v = m.st.k + (uint32_t)ch * hd * (kv_f16 ? 2 : 4);
-  m.st.ch = ch;
+  m.ring = reinterpret_cast<uint8_t*>(m.part + gqa * hd);
+  m.ch = ch;
+  m.slot = ch * hd * (kv_f16 ? 2 : 4);
   return m;
 }
 
@@ -194,121 +220,189 @@ struct TileArgs {
   }
 };
 
-// The first chunk of tile t of group g, K then V (two commit groups),
-// without the newest position P - 1: everything this tile reads that
-// earlier steps wrote, so it may be issued before griddepcontrol.wait.
+// Tile t's positions [j0, j0 + n), nk chunks of ch rows.
+struct TileGeom {
+  int j0, n, nk;
+};
+FOX_DEV TileGeom tile_geom(const TileArgs& a, int t, int ch) {
+  const int T = attn_tile_len(a.P, a.nt);
+  TileGeom tg;
+  tg.j0 = t * T;
+  tg.n = min(T, a.P - tg.j0);
+  tg.nk = (tg.n + ch - 1) / ch;
+  return tg;
+}
+
+// Chunk c of the tile's staging order (K chunks 0..nk-1, then V chunks
+// 0..nk-1) into ring slot c % ATTN_RING, without position `skip`; one commit
+// group per call, empty past the last chunk.
+FOX_DEV void attn_issue(const TileSmem& m, const KvHead& kh, const KvHead& vh, const TileGeom& tg, int c,
+                        int skip) {
+  if (c < 2 * tg.nk) {
+    const bool isv = c >= tg.nk;
+    const int r0 = tg.j0 + (isv ? c - tg.nk : c) * m.ch;
+    KvHead src = kh;  // (a select of the base alone keeps both heads in registers)
+    if (isv) src.base = vh.base;
+    stage_rows(m.ring + (uint32_t)(c % ATTN_RING) * m.slot, src, r0, min(tg.j0 + tg.n, r0 + m.ch), skip);
+  }
+  cp_async_commit();
+}
+
+// The first ATTN_RING - 1 chunks of tile t of group g, without the newest
+// position P - 1: everything they hold that earlier steps wrote, so they may
+// be issued before griddepcontrol.wait.
 template <bool F16>
-FOX_DEV void attn_tile_stage0(const TileArgs& a, const TileStage& st, int g, int t) {
-  const int T = attn_tile_len(a.P, a.nt), j0 = t * T, n = min(T, a.P - j0);
+FOX_DEV void attn_tile_stage0(const TileArgs& a, const TileSmem& m, int g, int t) {
   const int rb = a.hd * (F16 ? 2 : 4);
-  const int c1 = j0 + min(n, st.ch);
-  stage_rows(st.k, a.head(a.kc, g, rb), j0, c1, a.P - 1);
-  stage_rows(st.v, a.head(a.vc, g, rb), j0, c1, a.P - 1);
+  const KvHead kh = a.head(a.kc, g, rb), vh = a.head(a.vc, g, rb);
+  const TileGeom tg = tile_geom(a, t, m.ch);
+  for (int c = 0; c < ATTN_RING - 1; ++c) attn_issue(m, kh, vh, tg, c, a.P - 1);
 }
 
 // Tile t of KV group g (after attn_tile_stage0): every query head's max,
 // sum and unnormalised output into the CTA's shared memory (ml, part).
+// The chunks stream through the ring, ATTN_RING - 1 in flight: the K chunks
+// give the scores; after the last of them come the tile's max and the
+// weights (while the first V chunks are in flight); the V chunks give the
+// outputs and, in the same ascending order, the sums.
 template <int DPL, bool F16, int G>
 FOX_DEV void attn_tile(const TileArgs& a, const TileSmem& m, int g, int t) {
-  const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nth >> 5;
-  const int T = attn_tile_len(a.P, a.nt);
-  const int j0 = t * T, n = min(T, a.P - j0);
-  const int hd = a.hd, ch = m.st.ch;
+  constexpr int NW = ATTN_THREADS / 32;
+  __shared__ float s_wm[NW];  // the max pass: each warp's max of its head
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hd = a.hd, ch = m.ch, ts = m.ts;
   const int rb = hd * (F16 ? 2 : 4);
   const KvHead kh = a.head(a.kc, g, rb), vh = a.head(a.vc, g, rb);
+  const TileGeom tg = tile_geom(a, t, ch);
+  const int j0 = tg.j0, n = tg.n, nk = tg.nk;
   const int newest = a.P - 1;
   float* sc = m.sc;
   float* s_m = m.ml;        // [G]
   float* s_l = m.ml + 32;   // [G]
   FOX_ATTN_MARK(1);
-  for (int i = tid; i < G * hd; i += nth) m.q[i] = __ldcg(a.q + (uint32_t)g * G * hd + i);
-  // the newest row into the first chunk (staging left it out)
-  const bool has_newest = newest >= j0 && newest < j0 + min(n, ch);
-  auto newest_row = [&](uint8_t* buf, const KvHead& src) {
-    if (has_newest)
-      for (int i = tid; i < (rb >> 2); i += nth)
-        reinterpret_cast<uint32_t*>(buf + (uint32_t)(newest - j0) * rb)[i] =
-            __ldcg(reinterpret_cast<const unsigned int*>(src.row(newest)) + i);
-  };
-  for (int c0 = j0; c0 < j0 + n; c0 += ch) {
-    const int c1 = min(j0 + n, c0 + ch), cn = c1 - c0;
-    if (c0 == j0) {
-      cp_async_wait_one();  // chunk 0's K (its V may still be in flight)
-      newest_row(m.st.k, kh);
-    } else {
-      stage_rows(m.st.k, kh, c0, c1, -1);
-      cp_async_wait_all();
+  for (int i = tid; i < G * hd; i += ATTN_THREADS) m.q[i] = __ldcg(a.q + (uint32_t)g * G * hd + i);
+  // V chunks: thread (d, hg) sums dim d of heads hg, hg + hgs, ... (hpt of
+  // them), each over the positions in order; the warps holding d < 32 also
+  // sum the weights (thread d == 0 keeps them)
+  const int hgs = max(1, min(G, ATTN_THREADS / hd)), hpt = G / hgs;
+  const int d = tid % hd, hg = tid / hd;
+  const bool vact = hg < hgs;
+  const bool lsum = d < 32;  // uniform within a warp (hd is a multiple of 32)
+  float o[G], l[G];
+#pragma unroll
+  for (int k = 0; k < G; ++k) o[k] = l[k] = 0.0f;
+  for (int c = 0; c < 2 * nk; ++c) {
+    attn_issue(m, kh, vh, tg, c + ATTN_RING - 1, -1);
+    cp_async_wait_ring();  // chunk c has landed (this thread's copies)
+    const bool isv = c >= nk;
+    const int ci = isv ? c - nk : c;
+    const int c0 = j0 + ci * ch, cn = min(ch, j0 + n - c0);
+    const uint8_t* slot = m.ring + (uint32_t)(c % ATTN_RING) * m.slot;
+    if (c < ATTN_RING - 1 && newest >= c0 && newest < c0 + cn) {
+      // staged before the newest row was written: that row now
+      KvHead h = kh;
+      if (isv) h.base = vh.base;
+      const unsigned* src = reinterpret_cast<const unsigned*>(h.row(newest));
+      unsigned* dst = reinterpret_cast<unsigned*>(m.ring + (uint32_t)(c % ATTN_RING) * m.slot +
+                                                  (uint32_t)(newest - c0) * rb);
+      for (int i = tid; i < (rb >> 2); i += ATTN_THREADS) dst[i] = __ldcg(src + i);
     }
     __syncthreads();
     FOX_ATTN_MARK(2);
-    // tasks: (group of 16 rows, query head)
-    const int groups = (cn + 15) >> 4;
-    for (int task = warp; task < groups * G; task += nw) {
-      const int r0 = (task / G) * 16, h = task % G;
-      const float d = dot16<DPL, F16>(m.st.k, r0, cn - r0, hd, m.q + h * hd, lane);
-      const int r = r0 + (lane >> 1);
-      if (!(lane & 1) && r < cn) sc[h * T + (c0 - j0) + r] = __fmul_rn(d, a.scale);
-    }
-    __syncthreads();  // the buffer is refilled by the next chunk
-  }
-  FOX_ATTN_MARK(3);
-  for (int h = warp; h < G; h += nw) {
-    float mx = -CUDART_INF_F;
-    for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sc[h * T + j]);
-    mx = warp_max(mx);
-    if (lane == 0) s_m[h] = mx;
-  }
-  __syncthreads();
-  for (int i = tid; i < G * n; i += nth) {
-    const int h = i / n, j = i - h * n;
-    sc[h * T + j] = expf_up(__fsub_rn(sc[h * T + j], s_m[h]));
-  }
-  __syncthreads();
-  FOX_ATTN_MARK(4);
-  if (tid < G) {
-    float l = 0.0f;
-    for (int j = 0; j < n; ++j) l = __fadd_rn(l, sc[tid * T + j]);
-    s_l[tid] = l;
-  }
-  // thread (d, hg) holds the sums of heads hg, hg + hgs, ... (hpt of them),
-  // each over the positions in order
-  const int hgs = max(1, min(G, nth / hd));
-  const int hpt = G / hgs;
-  const int d = tid % hd, hg = tid / hd;
-  const bool sums = hg < hgs;
-  float o[G];
+    if (!isv) {
+      // tasks (group of 8 rows, head part): hsplit warps share a group,
+      // the task of part p taking heads p, p + hsplit, ...; the rows stay in
+      // registers across its heads
+      const int groups = (cn + 7) >> 3;
+      const int hsplit = min(G, NW / groups >= 8 ? 8 : NW / groups >= 4 ? 4 : NW / groups >= 2 ? 2 : 1);
+      const int hpw = G / hsplit;
+      for (int task = warp; task < groups * hsplit; task += NW) {
+        const int r0 = (task / hsplit) * 8, hp = task % hsplit, valid = min(8, cn - r0);
+        float kf[8][DPL];
 #pragma unroll
-  for (int k = 0; k < G; ++k) o[k] = 0.0f;
-  for (int c0 = j0; c0 < j0 + n; c0 += ch) {
-    const int c1 = min(j0 + n, c0 + ch), cn = c1 - c0;
-    if (c0 == j0) {
-      cp_async_wait_all();
-      newest_row(m.st.v, vh);
-    } else {
-      __syncthreads();
-      stage_rows(m.st.v, vh, c0, c1, -1);
-      cp_async_wait_all();
-    }
-    __syncthreads();
-    FOX_ATTN_MARK(5);
-    if (sums) {
-      const float* e = sc + (c0 - j0) + hg * T;
-      const int estep = hgs * T;
-#pragma unroll 4
-      for (int j = 0; j < cn; ++j) {
-        const float v = F16 ? __half2float(reinterpret_cast<const __half*>(m.st.v)[j * hd + d])
-                            : reinterpret_cast<const float*>(m.st.v)[j * hd + d];
+        for (int i = 0; i < 8; ++i)
+          if (i < valid) staged_row<DPL, F16>(slot, r0 + i, hd, lane * DPL, kf[i]);
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+          if (k < hpw) {
+            const int h = hp + k * hsplit;
+            const float d = dot8<DPL>(kf, valid, m.q + h * hd, lane);
+            const int r = r0 + (lane >> 2);
+            if (!(lane & 3) && r < cn) sc[h * ts + ci * ch + r] = __fmul_rn(d, a.scale);
+          }
+        }
+      }
+      if (c == nk - 1) {
+        // the tile's max per head (NW / G warps per head), then the weights
+        __syncthreads();
+        FOX_ATTN_MARK(3);
+        constexpr int WPH = NW / G > 0 ? NW / G : 1;  // warps per head
+        for (int h0 = 0; h0 < G; h0 += NW / WPH) {
+          const int h = h0 + warp / WPH;
+          float mx = -CUDART_INF_F;
+          if (h < G)
+            for (int j = (warp % WPH) * 32 + lane; j < n; j += WPH * 32) mx = fmaxf(mx, sc[h * ts + j]);
+          mx = warp_max(mx);
+          if (lane == 0) s_wm[warp] = mx;
+          __syncthreads();
+          if (tid < NW / WPH && h0 + tid < G) {
+            float M = -CUDART_INF_F;
+            for (int w = 0; w < WPH; ++w) M = fmaxf(M, s_wm[tid * WPH + w]);
+            s_m[h0 + tid] = M;
+          }
+          __syncthreads();
+        }
+        for (int h = 0; h < G; ++h)
+          for (int j = tid; j < n; j += ATTN_THREADS)
+            sc[h * ts + j] = expf_up(__fsub_rn(sc[h * ts + j], s_m[h]));
+        FOX_ATTN_MARK(4);
+      }
+    } else if (vact) {
+      // the weights of 4 positions per shared-memory load
+      const float* e = sc + ci * ch;
+      int j = 0;
+      for (; j + 4 <= cn; j += 4) {
+        float4 w[G];
 #pragma unroll
         for (int k = 0; k < G; ++k)
-          if (k < hpt) o[k] = __fmaf_rn(e[k * estep + j], v, o[k]);
+          if (k < hpt) w[k] = *reinterpret_cast<const float4*>(e + (hg + k * hgs) * ts + j);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const float v = staged_one<F16>(slot, j + jj, hd, d);
+#pragma unroll
+          for (int k = 0; k < G; ++k) {
+            if (k < hpt) {
+              const float x = jj == 0 ? w[k].x : jj == 1 ? w[k].y : jj == 2 ? w[k].z : w[k].w;
+              o[k] = __fmaf_rn(x, v, o[k]);
+              if (lsum) l[k] = __fadd_rn(l[k], x);
+            }
+          }
+        }
+      }
+      for (; j < cn; ++j) {
+        const float v = staged_one<F16>(slot, j, hd, d);
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+          if (k < hpt) {
+            const float x = e[(hg + k * hgs) * ts + j];
+            o[k] = __fmaf_rn(x, v, o[k]);
+            if (lsum) l[k] = __fadd_rn(l[k], x);
+          }
+        }
       }
     }
+    __syncthreads();  // slot c % ATTN_RING is refilled by the next iteration
   }
   FOX_ATTN_MARK(6);
-  if (sums) {
+  if (vact) {
 #pragma unroll
-    for (int k = 0; k < G; ++k)
-      if (k < hpt) m.part[(hg + k * hgs) * hd + d] = o[k];
+    for (int k = 0; k < G; ++k) {
+      if (k < hpt) {
+        const int h = hg + k * hgs;
+        m.part[h * hd + d] = o[k];
+        if (d == 0) s_l[h] = l[k];
+      }
+    }
   }
 }
 
@@ -365,7 +459,7 @@ FOX_DEV void attn_merge(const TileArgs& a, const TileSmem& m, int g, int nt) {
 // that writes q and position P - 1) the older rows of the first chunk are
 // staged before griddepcontrol.wait; q and the newest row are read after it.
 template <int DPL, bool F16, int G>
-__global__ void __launch_bounds__(ATTN_THREADS, 1) attention_tile_kernel(const AttnParams k) {
+__global__ void __launch_bounds__(ATTN_THREADS, DPL <= 4 ? 2 : 1) attention_tile_kernel(const AttnParams k) {
   extern __shared__ __align__(16) float tsm[];
   griddep_launch_dependents();  // the o projection may start streaming its weights
   FOX_ATTN_MARK(0);
@@ -382,7 +476,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1) attention_tile_kernel(const A
   const int T = attn_tile_len(a.P, a.nt), nt = (a.P + T - 1) / T;
   const TileSmem m = tile_smem(tsm, k.n_ctx, k.nt, G, k.hd, F16 ? 1 : 0, k.stage_rows);
   const bool live = t < nt;  // CTAs past the last tile only join the cluster's barriers
-  if (live) attn_tile_stage0<F16>(a, m.st, g, t);
+  if (live) attn_tile_stage0<F16>(a, m, g, t);
   griddep_wait();
   FOX_ATTN_MARK(9);
   if (live) attn_tile<DPL, F16, G>(a, m, g, t);

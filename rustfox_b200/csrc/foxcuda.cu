@@ -820,9 +820,15 @@ static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t 
 static int attn_nt_for(int sms, int n_kv_full) {
   return std::max(1, std::min(ATTN_TILE_MAX, sms / std::max(1, n_kv_full)));
 }
-// K/V rows per staged chunk of the tile attention: 64 KB of shared memory
-// for K and V together.
-static int attn_stage_rows(const AttnParams& ap, int) { return ap.kv_f16 ? 128 : 64; }
+// K/V rows per ring slot of the tile attention: the most (128, 64, 32 or
+// 16) for which the ring and the score rows fit a CTA's shared memory
+// (dynamic, below the 227 KB limit with room for the static arrays).
+constexpr size_t ATTN_SMEM_MAX = 220 * 1024;
+static int attn_stage_rows(const AttnParams& ap, int gqa) {
+  for (int ch = 128; ch > 16; ch >>= 1)
+    if (attn_tile_smem_bytes(ap.n_ctx, ap.nt, gqa, ap.hd, ap.kv_f16, ch) <= ATTN_SMEM_MAX) return ch;
+  return 16;
+}
 
 extern "C" int foxcuda_attn_tile_target(int device, uint32_t n_head_kv) {
   return attn_nt_for(sm_count(device), (int)n_head_kv);
