@@ -79,6 +79,9 @@ def parse():
     ap.add_argument("--contiguous", action="store_true",
                     help="with --batch: one contiguous cache per sequence instead of pages "
                          "from one shared pool")
+    ap.add_argument("--attention", action="store_true",
+                    help="time the tile attention on its own (foxcuda_attention, one sequence, fp16 "
+                         "caches) at 32768 positions and at the 4B and 27B decode shapes")
     ap.add_argument("--image", action="store_true",
                     help="time the model load: tensors uploaded and packed on the device, "
                          "against a device image opened from a file")
@@ -894,10 +897,70 @@ def run_image(args):
                 "counterpart to time"}), flush=True)
 
 
+def run_attention(args):
+    """The tile attention on its own through the C ABI (foxcuda_attention):
+    one sequence, fp16 K/V caches of N(0, 1) values, 32 query heads, head_dim
+    128, at (positions, KV heads) = (32768, 8), (576, 8) and (576, 16). Each
+    call cycles to another copy of the caches (together larger than L2).
+    CUDA-event time per call includes the call's own position copy and stream
+    synchronisation; the kernel alone is the ncu launch list of this command."""
+    import ctypes as C
+    import torch
+    import rustfox_b200 as rf
+    torch.cuda.set_device(0)
+    L = rf.lib()
+    p = C.c_void_p
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    hbm, src = measured_hbm_gbs()
+    res = []
+    for n_ctx, pos, nkv in [(32768, 32767, 8), (4096, 575, 8), (4096, 575, 16)]:
+        nh, hd = 32, 128
+        copies = 4 if n_ctx > 8192 else 16
+        ks = [torch.randn(nkv, n_ctx, hd, device="cuda", generator=gen).half() for _ in range(copies)]
+        vs = [torch.randn(nkv, n_ctx, hd, device="cuda", generator=gen).half() for _ in range(copies)]
+        q = torch.randn(nh * hd, device="cuda", generator=gen)
+        out = torch.empty(nh * hd, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def call(i):
+            st = L.foxcuda_attention(p(q.data_ptr()), p(ks[i % copies].data_ptr()), p(vs[i % copies].data_ptr()),
+                                     0, nh, nkv, hd, n_ctx, pos, 0, p(out.data_ptr()), p(stream))
+            if st != 0:
+                raise rf.FoxError(st, rf.api.last_error())
+        for i in range(max(3, args.warmup)):
+            call(i)
+        torch.cuda.synchronize()
+        ts = []
+        for i in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            call(i)
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        us = statistics.median(ts)
+        kv_bytes = 2 * nkv * (pos + 1) * hd * 2
+        res.append({"positions": pos + 1, "kv_heads": nkv, "us_per_call": us, "kv_bytes": kv_bytes,
+                    "gbs_per_call": kv_bytes / us / 1e3})
+        del ks, vs
+        torch.cuda.empty_cache()
+    print(json.dumps({
+        "metric": "tile attention per call", "unit": "us", "higher_is_better": False, "steps": args.steps,
+        "dtype": "f16 K/V, f32 arithmetic", "data": "synthetic (seeded N(0,1) caches and queries)",
+        "config": {"workload": "foxcuda_attention, one sequence, 32 query heads, head_dim 128",
+                   "l2": "caches cycled over copies larger than L2 together"},
+        "hbm_peak_gbs": hbm, "hbm_peak_source": src,
+        "note": "per-call event time includes the call's position copy and synchronisation; "
+                "kernel durations: ncu --metrics gpu__time_duration.sum on this command",
+        "results": res}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.attention:
+        run_attention(args)
     elif args.image:
         run_image(args)
     elif args.gemm:
