@@ -63,7 +63,7 @@ def test_parity_mode_picks_what_upstreams_cpu_picks(gguf):
 
 
 def test_fox_run_prints_the_same_text(gguf):
-    args = [CLI, "run", gguf, "-p", "the quick brown fox", "-n", "24", "--ctx", "96", "--temp", "0"]
+    args = [CLI, "run", gguf, "-p", "hello", "-n", "24", "--ctx", "96", "--temp", "0"]  # (the byte vocabulary has no space piece)
     out = {}
     for name, env in (("device", {"FOX_CUDA_PARITY": "1"}), ("cpu", {"FOX_CUDA": "0"})):
         r = subprocess.run(args, capture_output=True, text=True, env=dict(os.environ, **env), timeout=300)
