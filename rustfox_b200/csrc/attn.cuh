@@ -62,10 +62,13 @@ FOX_DEV const float* cluster_peer(const float* p, unsigned rank) {
 }
 
 constexpr int ATTN_THREADS = 256;  // threads of a tile CTA (8 warps)
-constexpr int ATTN_RING = 3;       // staged chunks per CTA: ATTN_RING - 1 in flight while one is read
+constexpr int ATTN_RING_MIN = 3;   // ring slots per CTA (nslot - 1 chunks in flight while one is read)
+constexpr int ATTN_RING_MAX = 4;
 
-FOX_DEV void cp_async_wait_ring() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(ATTN_RING - 1) : "memory");
+// Every commit group but the newest nslot - 1 has landed (this thread's copies).
+FOX_DEV void cp_async_wait_ring(int nslot) {
+  if (nslot >= 4) asm volatile("cp.async.wait_group 3;" ::: "memory");
+  else asm volatile("cp.async.wait_group 2;" ::: "memory");
 }
 
 // Where KV head g's positions of one sequence and layer live: the cache
@@ -177,24 +180,24 @@ FOX_DEV float dot8(const float (&kf)[8][DPL], int valid, const float* qh, int la
 //   q     G * hd     the group's query heads
 //   ml    64         per-head max [0, 32), sum [32, 64)
 //   part  G * hd     this tile's unnormalised outputs (read by the cluster)
-//   ring  ATTN_RING * ch * row bytes: staged chunks of K, then of V
+//   ring  nslot * ch * row bytes: staged chunks of K, then of V
 struct TileSmem {
   float* sc;
   float* q;
   float* ml;
   float* part;
   uint8_t* ring;
-  int ch, ts, slot;  // rows per chunk, score row stride, bytes per ring slot
+  int ch, ts, slot, nslot;  // rows per chunk, score row stride, bytes per ring slot, slots
 };
 
 __host__ __device__ inline int attn_score_stride(int n_ctx, int nt) { return (attn_tile_len(n_ctx, nt) + 3) & ~3; }
 
-inline size_t attn_tile_smem_bytes(int n_ctx, int nt, int gqa, int hd, int kv_f16, int ch) {
+inline size_t attn_tile_smem_bytes(int n_ctx, int nt, int gqa, int hd, int kv_f16, int ch, int nslot) {
   const size_t floats = (size_t)gqa * attn_score_stride(n_ctx, nt) + 2 * (size_t)gqa * hd + 64;
-  return floats * 4 + (size_t)ATTN_RING * ch * hd * (kv_f16 ? 2 : 4);
+  return floats * 4 + (size_t)nslot * ch * hd * (kv_f16 ? 2 : 4);
 }
 
-FOX_DEV TileSmem tile_smem(float* base, int n_ctx, int nt, int gqa, int hd, int kv_f16, int ch) {
+FOX_DEV TileSmem tile_smem(float* base, int n_ctx, int nt, int gqa, int hd, int kv_f16, int ch, int nslot) {
   TileSmem m;
   m.ts = attn_score_stride(n_ctx, nt);
   m.sc = base;
@@ -204,6 +207,7 @@ FOX_DEV TileSmem tile_smem(float* base, int n_ctx, int nt, int gqa, int hd, int 
   m.ring = reinterpret_cast<uint8_t*>(m.part + gqa * hd);
   m.ch = ch;
   m.slot = ch * hd * (kv_f16 ? 2 : 4);
+  m.nslot = nslot;
   return m;
 }
 
@@ -234,7 +238,7 @@ FOX_DEV TileGeom tile_geom(const TileArgs& a, int t, int ch) {
 }
 
 // Chunk c of the tile's staging order (K chunks 0..nk-1, then V chunks
-// 0..nk-1) into ring slot c % ATTN_RING, without position `skip`; one commit
+// 0..nk-1) into ring slot c % nslot, without position `skip`; one commit
 // group per call, empty past the last chunk.
 FOX_DEV void attn_issue(const TileSmem& m, const KvHead& kh, const KvHead& vh, const TileGeom& tg, int c,
                         int skip) {
@@ -243,12 +247,12 @@ FOX_DEV void attn_issue(const TileSmem& m, const KvHead& kh, const KvHead& vh, c
     const int r0 = tg.j0 + (isv ? c - tg.nk : c) * m.ch;
     KvHead src = kh;  // (a select of the base alone keeps both heads in registers)
     if (isv) src.base = vh.base;
-    stage_rows(m.ring + (uint32_t)(c % ATTN_RING) * m.slot, src, r0, min(tg.j0 + tg.n, r0 + m.ch), skip);
+    stage_rows(m.ring + (uint32_t)(c % m.nslot) * m.slot, src, r0, min(tg.j0 + tg.n, r0 + m.ch), skip);
   }
   cp_async_commit();
 }
 
-// The first ATTN_RING - 1 chunks of tile t of group g, without the newest
+// The first nslot - 1 chunks of tile t of group g, without the newest
 // position P - 1: everything they hold that earlier steps wrote, so they may
 // be issued before griddepcontrol.wait.
 template <bool F16>
@@ -256,12 +260,12 @@ FOX_DEV void attn_tile_stage0(const TileArgs& a, const TileSmem& m, int g, int t
   const int rb = a.hd * (F16 ? 2 : 4);
   const KvHead kh = a.head(a.kc, g, rb), vh = a.head(a.vc, g, rb);
   const TileGeom tg = tile_geom(a, t, m.ch);
-  for (int c = 0; c < ATTN_RING - 1; ++c) attn_issue(m, kh, vh, tg, c, a.P - 1);
+  for (int c = 0; c < m.nslot - 1; ++c) attn_issue(m, kh, vh, tg, c, a.P - 1);
 }
 
 // Tile t of KV group g (after attn_tile_stage0): every query head's max,
 // sum and unnormalised output into the CTA's shared memory (ml, part).
-// The chunks stream through the ring, ATTN_RING - 1 in flight: the K chunks
+// The chunks stream through the ring, nslot - 1 in flight: the K chunks
 // give the scores; after the last of them come the tile's max and the
 // weights (while the first V chunks are in flight); the V chunks give the
 // outputs and, in the same ascending order, the sums.
@@ -292,18 +296,18 @@ FOX_DEV void attn_tile(const TileArgs& a, const TileSmem& m, int g, int t) {
 #pragma unroll
   for (int k = 0; k < G; ++k) o[k] = l[k] = 0.0f;
   for (int c = 0; c < 2 * nk; ++c) {
-    attn_issue(m, kh, vh, tg, c + ATTN_RING - 1, -1);
-    cp_async_wait_ring();  // chunk c has landed (this thread's copies)
+    attn_issue(m, kh, vh, tg, c + m.nslot - 1, -1);
+    cp_async_wait_ring(m.nslot);  // chunk c has landed (this thread's copies)
     const bool isv = c >= nk;
     const int ci = isv ? c - nk : c;
     const int c0 = j0 + ci * ch, cn = min(ch, j0 + n - c0);
-    const uint8_t* slot = m.ring + (uint32_t)(c % ATTN_RING) * m.slot;
-    if (c < ATTN_RING - 1 && newest >= c0 && newest < c0 + cn) {
+    const uint8_t* slot = m.ring + (uint32_t)(c % m.nslot) * m.slot;
+    if (c < m.nslot - 1 && newest >= c0 && newest < c0 + cn) {
       // staged before the newest row was written: that row now
       KvHead h = kh;
       if (isv) h.base = vh.base;
       const unsigned* src = reinterpret_cast<const unsigned*>(h.row(newest));
-      unsigned* dst = reinterpret_cast<unsigned*>(m.ring + (uint32_t)(c % ATTN_RING) * m.slot +
+      unsigned* dst = reinterpret_cast<unsigned*>(m.ring + (uint32_t)(c % m.nslot) * m.slot +
                                                   (uint32_t)(newest - c0) * rb);
       for (int i = tid; i < (rb >> 2); i += ATTN_THREADS) dst[i] = __ldcg(src + i);
     }
@@ -391,7 +395,7 @@ FOX_DEV void attn_tile(const TileArgs& a, const TileSmem& m, int g, int t) {
         }
       }
     }
-    __syncthreads();  // slot c % ATTN_RING is refilled by the next iteration
+    __syncthreads();  // slot c % nslot is refilled by the next iteration
   }
   FOX_ATTN_MARK(6);
   if (vact) {
@@ -474,7 +478,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, DPL <= 4 ? 2 : 1) attention_tile
   a.P = (k.pos_list ? *k.pos_list[z] : *k.pos) + 1;
   a.scale = k.scale;
   const int T = attn_tile_len(a.P, a.nt), nt = (a.P + T - 1) / T;
-  const TileSmem m = tile_smem(tsm, k.n_ctx, k.nt, G, k.hd, F16 ? 1 : 0, k.stage_rows);
+  const TileSmem m = tile_smem(tsm, k.n_ctx, k.nt, G, k.hd, F16 ? 1 : 0, k.stage_rows, k.stage_slots);
   const bool live = t < nt;  // CTAs past the last tile only join the cluster's barriers
   if (live) attn_tile_stage0<F16>(a, m, g, t);
   griddep_wait();

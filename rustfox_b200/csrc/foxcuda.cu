@@ -820,14 +820,22 @@ static cudaError_t run_attention(const AttnParams& ap, bool exact, cudaStream_t 
 static int attn_nt_for(int sms, int n_kv_full) {
   return std::max(1, std::min(ATTN_TILE_MAX, sms / std::max(1, n_kv_full)));
 }
-// K/V rows per ring slot of the tile attention: the most (128, 64, 32 or
-// 16) for which the ring and the score rows fit a CTA's shared memory
-// (dynamic, below the 227 KB limit with room for the static arrays).
+// The tile attention's ring: rows per slot, the most (128, 64, 32 or 16)
+// for which three slots and the score rows fit a CTA's shared memory
+// (dynamic, below the 227 KB limit with room for the static arrays); and
+// four slots instead of three when the CTA holds an SM alone anyway (more
+// than half of it) and the fourth fits.
 constexpr size_t ATTN_SMEM_MAX = 220 * 1024;
-static int attn_stage_rows(const AttnParams& ap, int gqa) {
-  for (int ch = 128; ch > 16; ch >>= 1)
-    if (attn_tile_smem_bytes(ap.n_ctx, ap.nt, gqa, ap.hd, ap.kv_f16, ch) <= ATTN_SMEM_MAX) return ch;
-  return 16;
+constexpr size_t ATTN_SMEM_PAIR = 110 * 1024;  // two CTAs per SM below this
+static void attn_ring(AttnParams& ap, int gqa) {
+  int ch = 128;
+  while (ch > 16 && attn_tile_smem_bytes(ap.n_ctx, ap.nt, gqa, ap.hd, ap.kv_f16, ch, ATTN_RING_MIN) > ATTN_SMEM_MAX)
+    ch >>= 1;
+  ap.stage_rows = ch;
+  ap.stage_slots = ATTN_RING_MIN;
+  if (attn_tile_smem_bytes(ap.n_ctx, ap.nt, gqa, ap.hd, ap.kv_f16, ch, ATTN_RING_MIN) > ATTN_SMEM_PAIR &&
+      attn_tile_smem_bytes(ap.n_ctx, ap.nt, gqa, ap.hd, ap.kv_f16, ch, ATTN_RING_MAX) <= ATTN_SMEM_MAX)
+    ap.stage_slots = ATTN_RING_MAX;
 }
 
 extern "C" int foxcuda_attn_tile_target(int device, uint32_t n_head_kv) {
@@ -2238,8 +2246,8 @@ template <int DPL, bool F16, int G>
 static cudaError_t launch_tile_g(const AttnParams& ap_in, int n_seq, cudaStream_t s, bool pdl) {
   auto kern = attention_tile_kernel<DPL, F16, G>;
   AttnParams ap = ap_in;
-  ap.stage_rows = attn_stage_rows(ap, G);
-  const size_t sm = attn_tile_smem_bytes(ap.n_ctx, ap.nt, G, ap.hd, F16 ? 1 : 0, ap.stage_rows);
+  attn_ring(ap, G);
+  const size_t sm = attn_tile_smem_bytes(ap.n_ctx, ap.nt, G, ap.hd, F16 ? 1 : 0, ap.stage_rows, ap.stage_slots);
   static size_t marks[kMaxDevices] = {};
   cudaError_t e = opt_in_smem(kern, sm, marks);
   if (e != cudaSuccess) return e;

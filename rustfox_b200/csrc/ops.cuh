@@ -95,6 +95,7 @@ struct AttnParams {
   int kv_f16, n_ctx, hd, n_head, n_kv;
   int nt;                 // tile target of the tile attention (attn.cuh)
   int stage_rows;         // K/V rows per ring slot of the tile attention (set by its launch)
+  int stage_slots;        // ring slots of the tile attention (set by its launch)
   const int* pos;
   float* out;             // [n_head * hd]
   float scale;
