@@ -340,11 +340,10 @@ def test_sums_without_the_epoch_check_is_caught():
     """The model with a planted mistake: the completion takes whatever words
     are there instead of waiting for its epoch. The check above sees rows
     of another step (or none yet)."""
-    hits = 0
-    for seed in range(4):
-        bad, _ = _run_sums(3, 2, 3, rows=6, seed=30 + seed, trade=False, skip_epoch_check=True)
-        hits += bool(bad)
-    assert hits
+    # the interleavings come from OS threads: seeds until the first catch
+    # (a loaded host can run a few seeds without one)
+    assert any(_run_sums(3, 2, 3, rows=6, seed=30 + seed, trade=False, skip_epoch_check=True)[0]
+               for seed in range(40))
 
 
 def test_sums_dropping_a_prompt_tokens_completion_is_caught():
@@ -353,8 +352,5 @@ def test_sums_dropping_a_prompt_tokens_completion_is_caught():
     pushing the next token's o rows over those a slower rank still reads;
     the device completes it at the position advance for that reason. Seen
     as stale rows, a later epoch, or a wait that gives up."""
-    hits = 0
-    for seed in range(6):
-        bad, _ = _run_sums(8, 3, 6, rows=7, seed=100 + seed, trade=False, drop_prompt_fold=True)
-        hits += bool(bad)
-    assert hits
+    assert any(_run_sums(8, 3, 6, rows=7, seed=100 + seed, trade=False, drop_prompt_fold=True)[0]
+               for seed in range(40))
